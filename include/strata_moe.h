@@ -1,0 +1,141 @@
+/*
+ * strata_moe.h: C ABI of the B200 (sm_100a) mixture-of-experts hot path on GGUF quant blocks.
+ *
+ * Every entry point replaces one kernel-launching function of yibie/strata-mlx's Python modules
+ * `strata_mlx/blocks.py` and `strata_mlx/fused.py` (cited beside each declaration). The Python facade
+ * `strata_mlx_b200.blocks` / `strata_mlx_b200.fused` binds them with ctypes; any other host language binds
+ * the same symbols.
+ *
+ * Conventions
+ *   - Pointers are CUDA device pointers unless named `host_*`. Blocks are the GGUF file's raw bytes of a
+ *     stack (experts, rows, cols): row r of expert e starts at (e*rows + r) * row_bytes, with
+ *     row_bytes = cols / per_block * block_bytes (strata_mlx/blocks.py:296-297).
+ *   - `kind` is the GGML type id of the blocks (8 Q8_0, 10 Q2_K, 11 Q3_K, 12 Q4_K, 13 Q5_K, 14 Q6_K,
+ *     16 IQ2_XXS, 17 IQ2_XS, 18 IQ3_XXS, 20 IQ4_NL, 21 IQ3_S, 22 IQ2_S, 23 IQ4_XS, 29 IQ1_M, 42 Q2_0).
+ *   - `dtype` codes: SMOE_F32 = 0, SMOE_F16 = 1. Activations and results take the activations' type unless
+ *     a declaration says float32.
+ *   - `stream` is a cudaStream_t (0 = legacy default stream). Every call is asynchronous on it, allocates
+ *     nothing, synchronises nothing and so can be captured in a CUDA graph.
+ *   - Return value: 0 on success; > 0 an invalid argument (SMOE_E*), with a message from
+ *     smoe_last_error(); < 0 the negated cudaError_t of a failed launch.
+ */
+#ifndef STRATA_MOE_H
+#define STRATA_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SMOE_API __attribute__((visibility("default")))
+#else
+#define SMOE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { SMOE_F32 = 0, SMOE_F16 = 1 };
+enum {
+    SMOE_OK = 0,
+    SMOE_EKIND = 1,      /* block type not supported by this entry point */
+    SMOE_ESHAPE = 2,     /* a dimension does not divide into blocks / tiles, or is out of range */
+    SMOE_EDTYPE = 3,     /* activation type not supported */
+    SMOE_EARG = 4,       /* null pointer, misaligned pointer, or an inconsistent count */
+    SMOE_EWORKSPACE = 5, /* workspace missing or smaller than the *_workspace_size query asked for */
+    SMOE_ETIMEOUT = 6    /* a bounded device-side wait gave up (status read back by the host) */
+};
+
+/* Human-readable message of the last error returned on this host thread. */
+SMOE_API const char* smoe_last_error(void);
+
+/* Library version and the CUDA architecture it was built for (e.g. 1000 for sm_100a). */
+SMOE_API int smoe_version(void);
+SMOE_API int smoe_built_arch(void);
+
+/* Weights per block and bytes per block of a GGML type id (strata_mlx/blocks.py:36-38 BLOCK,
+ * strata_mlx/gguf.py:25-33 TYPES). Returns SMOE_EKIND for types without a decoder here. */
+SMOE_API int smoe_block_info(int kind, int* per_block, int* block_bytes);
+
+/* Every weight of `n_rows` rows of `cols` weights as float16/float32: out[r, c].
+ * Replaces `dequantize` / the `_DEQUANT` kernel (strata_mlx/blocks.py:261-270, 515-522). The float16
+ * result is the float32 weight rounded to nearest even once, bit-equal to gguf-py's dequantize. */
+SMOE_API int smoe_dequant(int kind, const uint8_t* blocks, int64_t n_rows, int64_t cols, void* out, int out_dtype,
+                 void* stream);
+
+/* out[p, r] = W[idx[p], r, :] . x[p / share, :] for p < pairs, r < rows; float32 sums.
+ * W is a stack (experts, rows, cols) of `kind` blocks. x and out are `dtype`.
+ * Replaces `BlockSwitchLinear.__call__` / the `_MATVEC` kernel (strata_mlx/blocks.py:196-220, 525-554):
+ * share = 1 gives a row of x to every pair (down), share = k one to each run of k pairs (gate, up).
+ * Indices >= experts are an error on the host side only if detected there; the kernel skips such pairs
+ * (their output rows are left as they were). */
+SMOE_API int smoe_matvec(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
+                const uint32_t* idx, int64_t pairs, int64_t share, const void* x, void* out, int dtype,
+                void* stream);
+
+/* The gate and up products of the same pairs in one launch: two smoe_matvec calls sharing idx and x
+ * (strata_mlx/blocks.py:971 `g, u = gate(x5, indices), up(x5, indices)`). The two stacks may differ in
+ * kind but have the same shape. */
+SMOE_API int smoe_matvec_gate_up(int gate_kind, const uint8_t* gate_blocks, int up_kind, const uint8_t* up_blocks,
+                        int64_t experts, int64_t rows, int64_t cols, const uint32_t* idx, int64_t pairs,
+                        int64_t share, const void* x, void* gate_out, void* up_out, int dtype, void* stream);
+
+/* out[p, :] = W[idx[p]] . swiglu(gate[p, :], up[p, :]) with swiglu formed as mlx-lm forms it in the
+ * activations' type (sigmoid in float32 rounded to the type, then two products in the type).
+ * Replaces `matvec_glu` / `_MATVEC_GLU` (strata_mlx/blocks.py:225-259, 939-955); unlike the reference it
+ * takes any pair count. gate/up are (pairs, cols), out (pairs, rows), all `dtype`. */
+SMOE_API int smoe_matvec_glu(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
+                    const uint32_t* idx, int64_t pairs, const void* gate, const void* up, void* out, int dtype,
+                    void* stream);
+
+/* h = swiglu(gate, up) elementwise over n values of `dtype`: mlx-lm's `swiglu` as restated at
+ * strata_mlx/blocks.py:222-237 (the unfused form `down(swiglu(g, u), indices)`, blocks.py:976). */
+SMOE_API int smoe_swiglu(const void* gate, const void* up, int64_t n, void* out, int dtype, void* stream);
+
+/* Router product: logits[t, e] = W[e, :] . x[t, :], W float16 (experts, hidden), x `x_dtype`
+ * (tokens, hidden), float32 sums and result. A token's sum does not depend on `tokens`.
+ * Replaces `WindowLinear.__call__` / `_MATVEC` of fused.py (strata_mlx/fused.py:334-390). */
+SMOE_API int smoe_router_logits(const uint16_t* weight, const void* x, int x_dtype, int64_t tokens, int64_t experts,
+                       int64_t hidden, float* logits, void* stream);
+
+/* idx[t, :] = the k largest of logits[t, :] (float32, n per row), largest first, ties to the lower index:
+ * `mx.argpartition(-logits, k - 1)[..., :k]`. Replaces `top_k` / `_TOPK` (strata_mlx/fused.py:400-436);
+ * any n <= 4096 and k <= 64, rows of any count. If `weights` is not null it also receives
+ * softmax(logits[t, idx[t, :]]) in float32 (strata_mlx/fused.py:491, `mx.softmax(..., precise=True)`). */
+SMOE_API int smoe_top_k(const float* logits, int64_t rows, int64_t n, int64_t k, uint32_t* idx, float* weights,
+               void* stream);
+
+/* The end of the MoE block: out[t, d] = half(sum_k y[t,k,d] w[t,k]) + half(half(sigmoid(g[t])) s[t,d]),
+ * the sum in float32 in MLX's col_reduce_small order (partials j = k mod 8, then in order), every product
+ * rounded, contraction off. y (tokens, k, d) `dtype`, w (tokens, k) float32, g (tokens) `dtype`,
+ * s (tokens, d) `dtype`. Replaces `moe_combine` / `_COMBINE` (strata_mlx/fused.py:448-481) for any token
+ * count and any d. */
+SMOE_API int smoe_combine(const void* y, const float* w, const void* g, const void* s, int64_t tokens, int64_t k,
+                 int64_t d, void* out, int dtype, void* stream);
+
+/* The dispatch permutation of `pairs` = tokens * k expert indices (int32, flat) into tiles of 16 slots,
+ * each tile one expert's: tile_expert[most] (experts for a tile nothing fills), token[most * 16] (0 in an
+ * unfilled slot), where[pairs] (the slot of each pair), most = pairs / 16 + min(experts, pairs).
+ * A pair's place within its expert follows its flat index. Replaces `tiles_of`
+ * (strata_mlx/blocks.py:657-681). Needs smoe_tiles_of_workspace_size() bytes of device workspace. */
+SMOE_API size_t smoe_tiles_of_workspace_size(int64_t pairs, int64_t experts);
+SMOE_API int smoe_tiles_of(const int32_t* indices, int64_t pairs, int64_t k, int64_t experts, uint32_t* tile_expert,
+                  uint32_t* token, uint32_t* where, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Whether smoe_tile_matmul takes a stack of such rows (strata_mlx/blocks.py:629-631 `tileable`). */
+SMOE_API int smoe_tileable(int kind, int64_t rows, int64_t cols);
+
+/* out[p, :] = W[tile_expert[p / 16]] . a[p, :] for p < p16 (a multiple of 16), the weights rounded to a's
+ * type (float16) before they multiply, float32 sums, out float32 (p16, rows). Tiles whose expert is
+ * >= experts are left out (their rows of out are not written). Grouped GEMM on the 5th-generation tensor
+ * cores (tcgen05, accumulators in TMEM). Replaces `tile_matmul` / `_TILES`
+ * (strata_mlx/blocks.py:583-654). Needs smoe_tile_matmul_workspace_size() bytes of device workspace. */
+SMOE_API size_t smoe_tile_matmul_workspace_size(int64_t p16);
+SMOE_API int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
+                     const void* a, int a_dtype, int64_t p16, const uint32_t* tile_expert, float* out,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* STRATA_MOE_H */

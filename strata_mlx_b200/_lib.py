@@ -1,0 +1,89 @@
+"""ctypes binding of libstrata_moe.so, the C ABI declared in include/strata_moe.h.
+
+The library is built in-tree (`python -m strata_mlx_b200._build`) and loaded from this package's directory.
+There is no fallback: if it is missing or fails to load, every entry point of the package raises.
+"""
+
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libstrata_moe.so")
+
+F32, F16 = 0, 1
+ETIMEOUT = 6
+
+_c = ctypes
+_p, _i, _i64, _sz = _c.c_void_p, _c.c_int, _c.c_int64, _c.c_size_t
+
+# name -> (restype, argtypes): the declarations of include/strata_moe.h
+SIGNATURES = {
+    "smoe_last_error": (_c.c_char_p, []),
+    "smoe_version": (_i, []),
+    "smoe_built_arch": (_i, []),
+    "smoe_block_info": (_i, [_i, _c.POINTER(_i), _c.POINTER(_i)]),
+    "smoe_dequant": (_i, [_i, _p, _i64, _i64, _p, _i, _p]),
+    "smoe_matvec": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _i, _p]),
+    "smoe_matvec_gate_up": (_i, [_i, _p, _i, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i, _p]),
+    "smoe_matvec_glu": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _i, _p]),
+    "smoe_swiglu": (_i, [_p, _p, _i64, _p, _i, _p]),
+    "smoe_router_logits": (_i, [_p, _p, _i, _i64, _i64, _i64, _p, _p]),
+    "smoe_top_k": (_i, [_p, _i64, _i64, _i64, _p, _p, _p]),
+    "smoe_combine": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
+    "smoe_tiles_of_workspace_size": (_sz, [_i64, _i64]),
+    "smoe_tiles_of": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _sz, _p]),
+    "smoe_tileable": (_i, [_i, _i64, _i64]),
+    "smoe_tile_matmul_workspace_size": (_sz, [_i64]),
+    "smoe_tile_matmul": (_i, [_i, _p, _i64, _i64, _i64, _p, _i, _i64, _p, _p, _p, _sz, _p]),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded library (loaded once). Raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m strata_mlx_b200._build` "
+                               "(there is no CPU fallback)")
+        handle = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype, fn.argtypes = res, args
+        _lib = handle
+    return _lib
+
+
+def call(name, *args):
+    """Call an entry point; a non-zero status raises ValueError (invalid argument) or RuntimeError (CUDA)."""
+    status = getattr(lib(), name)(*args)
+    if status != 0:
+        msg = lib().smoe_last_error().decode(errors="replace")
+        if status > 0:
+            raise ValueError(f"{name}: {msg}")
+        raise RuntimeError(f"{name}: {msg}")
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def dtype_code(dt) -> int:
+    if dt == torch.float16:
+        return F16
+    if dt == torch.float32:
+        return F32
+    raise ValueError(f"activations of {dt} are not supported (float16 or float32)")
+
+
+def require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("strata_mlx_b200 computes on CUDA tensors only (no CPU path)")

@@ -1,0 +1,323 @@
+"""Experts computed on the GGUF file's own blocks, on B200: the call surface of strata-mlx's `strata_mlx/blocks.py`.
+
+The blocks stay on the GPU as the file's bytes (a torch uint8 CUDA tensor) and hand-written sm_100a kernels
+(libstrata_moe.so, declared in include/strata_moe.h) read them:
+
+    matvec      out[pair, row] = W[expert of pair, row, :] . x          decoding, a pair at a time
+    matvec_glu  the same with x = swiglu(gate, up) formed in shared memory   the down product of a few pairs
+    tiles       the pairs of a chunk of a prompt sorted by expert into tiles of 16 (`tiles_of`), a tensor-core
+                grouped GEMM (tcgen05, accumulators in TMEM) per run of one expert's tiles (`tile_matmul`)
+    dequant     every weight of the stack as float16 or float32
+
+Names, signatures, tensor layouts, thresholds and the "None = path not taken" convention follow the
+reference (strata_mlx/blocks.py), so an engine written against it can import this module instead. Tensors
+are torch CUDA tensors; there is no CPU path and no fallback to another library's kernels.
+"""
+
+import math
+
+import torch
+
+from . import _lib
+
+# type -> (weights per block, bytes per block): the reference's BLOCK (strata_mlx/blocks.py:36-38) and the
+# K-types and Q8_0 the B200 build also reads on the GPU (strata_mlx/gguf.py:25-33)
+BLOCK = {"IQ4_NL": (32, 18), "IQ4_XS": (256, 136), "IQ3_S": (256, 110), "IQ3_XXS": (256, 98),
+         "IQ2_S": (256, 82), "IQ2_XS": (256, 74), "IQ2_XXS": (256, 66), "IQ1_M": (256, 56), "Q2_0": (64, 18),
+         "Q3_K": (256, 110), "Q8_0": (32, 34), "Q2_K": (256, 84), "Q4_K": (256, 144), "Q5_K": (256, 176),
+         "Q6_K": (256, 210)}
+# GGML type ids, the `kind` of the C ABI
+KIND_ID = {"Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14, "IQ2_XXS": 16, "IQ2_XS": 17,
+           "IQ3_XXS": 18, "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23, "IQ1_M": 29, "Q2_0": 42}
+
+# thresholds, module attributes as in the reference so that tests and engines can switch paths
+TILES_FROM = 1600  # (token, expert) pairs from which a prompt goes through tiles (strata_mlx/blocks.py:579)
+TOKENS_TILE, ROWS_TILE, COLS_TILE = 16, 64, 64  # strata_mlx/blocks.py:580
+BLOCK_GLU = True  # pairs unsorted, swiglu formed by the down kernel (strata_mlx/blocks.py:934)
+MATVEC_GLU_UPTO = 30  # pairs up to which down forms swiglu itself (strata_mlx/blocks.py:936)
+
+
+def _kind(kind: str) -> int:
+    if kind not in KIND_ID:
+        raise ValueError(f"{kind} blocks are not supported")
+    return KIND_ID[kind]
+
+
+def row_bytes(kind: str, cols: int) -> int:
+    per_block, block_bytes = BLOCK[kind]
+    if cols % per_block:
+        raise ValueError(f"{kind}: rows of {cols} weights do not end on a block of {per_block}")
+    return cols // per_block * block_bytes
+
+
+def dequantize(blocks: torch.Tensor, kind: str, shape: tuple, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """The weights of `blocks` (uint8, a tensor of `shape` as the file holds it) as floats
+    (strata_mlx/blocks.py:515-522). float16 results are bit-equal to gguf-py's weights rounded once."""
+    _lib.require_cuda(blocks)
+    *lead, rows, cols = shape
+    n = math.prod(lead) if lead else 1
+    if blocks.numel() != n * rows * row_bytes(kind, cols):
+        raise ValueError(f"{blocks.numel()} bytes do not hold a {kind} tensor of {tuple(shape)}")
+    out = torch.empty(tuple(shape), dtype=dtype, device=blocks.device)
+    _lib.call("smoe_dequant", _kind(kind), _lib.ptr(blocks), n * rows, cols, _lib.ptr(out),
+              _lib.dtype_code(dtype), _lib.stream())
+    return out
+
+
+def _threads_per_row(runs: int) -> int:
+    """As the reference (strata_mlx/blocks.py:303-308); kept for the `per_row` attribute only."""
+    p = 1
+    while p < 32 and runs % (2 * p) == 0 and runs // (2 * p) >= 4:
+        p *= 2
+    return p
+
+
+def _matvec(lin, x2, idx_flat, share, out_dtype):
+    pairs = idx_flat.numel()
+    out = torch.empty((pairs, lin.output_dims), dtype=out_dtype, device=x2.device)
+    if pairs:
+        _lib.call("smoe_matvec", _kind(lin.kind), _lib.ptr(lin.blocks), lin.num_experts, lin.output_dims,
+                  lin.input_dims, _lib.ptr(idx_flat), pairs, share, _lib.ptr(x2), _lib.ptr(out),
+                  _lib.dtype_code(out_dtype), _lib.stream())
+    return out
+
+
+def _flat_idx(indices: torch.Tensor) -> torch.Tensor:
+    flat = indices.reshape(-1)
+    if flat.dtype in (torch.int32, torch.uint32):
+        return flat.contiguous()
+    return flat.to(torch.int32).contiguous()
+
+
+class BlockSwitchLinear:
+    """A stack of linear layers kept as the file's blocks; called like mlx-lm's `QuantizedSwitchLinear`
+    (strata_mlx/blocks.py:525-558)."""
+
+    # From this many pairs on the reference unpacks the stack to floats for MLX's gather_mm; here the same
+    # threshold sends them through the dequant kernel and a float product, for parity of behaviour.
+    unpack_from = 5000
+
+    def __init__(self, blocks: torch.Tensor, kind: str, shape: tuple, per_row: int | None = None):
+        _kind(kind)
+        self.blocks, self.kind = blocks.reshape(-1), kind
+        self.num_experts, self.output_dims, self.input_dims = shape
+        if self.blocks.numel() != self.num_experts * self.output_dims * row_bytes(kind, self.input_dims):
+            raise ValueError(f"{self.blocks.numel()} bytes do not hold a {kind} stack of {tuple(shape)}")
+        self.per_row = per_row or _threads_per_row(self.input_dims // 32)
+
+    @property
+    def shape(self):
+        return (self.num_experts, self.output_dims, self.input_dims)
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor, sorted_indices: bool = False) -> torch.Tensor:
+        """x (..., 1, in), one row to each index or to each run of the last axis of `indices`."""
+        _lib.require_cuda(x, indices, self.blocks)
+        batch = tuple(x.shape[:-2])
+        ishape = tuple(indices.shape)
+        k = ishape[-1] if indices.dim() else 1
+        if batch == ishape:
+            share = 1
+        elif batch == (*ishape[:-1], 1):
+            share = k
+        else:
+            x, share = x.expand(*ishape, 1, self.input_dims), 1
+        pairs = indices.numel()
+        idx = _flat_idx(indices)
+        if pairs >= self.unpack_from:
+            out = self._as_floats(x.reshape(-1, self.input_dims), idx, share)
+        else:
+            out = _matvec(self, x.reshape(-1, self.input_dims).contiguous(), idx, share, x.dtype)
+        return out.reshape(*ishape, 1, self.output_dims)
+
+    def _as_floats(self, x2, idx, share):
+        w = dequantize(self.blocks, self.kind, self.shape, x2.dtype)
+        rows = x2[torch.arange(idx.numel(), device=x2.device) // share]
+        return torch.einsum("poi,pi->po", w[idx.to(torch.int64)].float(), rows.float()).to(x2.dtype)
+
+
+# ---- prompts: an expert's blocks a tile at a time, on the tensor cores
+
+def tileable(kind: str, rows: int, cols: int) -> bool:
+    """Whether `tile_matmul` takes a stack of such layers (strata_mlx/blocks.py:629-631)."""
+    return bool(_lib.lib().smoe_tileable(_kind(kind), rows, cols))
+
+
+def tile_matmul(blocks: torch.Tensor, kind: str, shape: tuple, a: torch.Tensor, tile_expert: torch.Tensor) -> torch.Tensor:
+    """out[p] = W[expert of p's tile] . a[p] for a stack `blocks` of `shape` (experts, rows, cols)
+    (strata_mlx/blocks.py:634-654).
+
+    a (P, cols) float16 or float32, P a multiple of TOKENS_TILE, every TOKENS_TILE rows for one expert;
+    tile_expert (P / TOKENS_TILE,) says which, or names no expert (the number of experts, or more) for a tile
+    to leave out: its rows of the result are then whatever was in memory. The weights are rounded to the type
+    of `a` before they multiply; sums are float32. Returns (P, rows) float32.
+    """
+    _lib.require_cuda(blocks, a, tile_expert)
+    experts, rows, cols = shape
+    p16 = a.shape[0]
+    if p16 % TOKENS_TILE or tile_expert.numel() * TOKENS_TILE != p16:
+        raise ValueError("a's rows must be TOKENS_TILE per entry of tile_expert")
+    a = a.contiguous()
+    te = tile_expert.reshape(-1).contiguous()
+    if te.dtype not in (torch.int32, torch.uint32):
+        te = te.to(torch.int32)
+    out = torch.empty((p16, rows), dtype=torch.float32, device=a.device)
+    ws = torch.empty(int(_lib.lib().smoe_tile_matmul_workspace_size(p16)), dtype=torch.uint8, device=a.device)
+    _lib.call("smoe_tile_matmul", _kind(kind), _lib.ptr(blocks), experts, rows, cols, _lib.ptr(a),
+              _lib.dtype_code(a.dtype), p16, _lib.ptr(te), _lib.ptr(out), _lib.ptr(ws), ws.numel(), _lib.stream())
+    return out
+
+
+def tiles_of(indices: torch.Tensor, experts: int) -> tuple:
+    """The pairs of `indices` (..., k) laid out in tiles of TOKENS_TILE, each tile one expert's
+    (strata_mlx/blocks.py:657-681).
+
+    -> (the expert of each tile, or `experts` for a tile nothing fills; the token of each slot; the slot of
+    each pair), uint32, worked out on the GPU in a number of tiles that depends only on the number of pairs.
+    """
+    _lib.require_cuda(indices)
+    k = indices.shape[-1]
+    flat = indices.reshape(-1)
+    flat = flat.view(torch.int32) if flat.dtype == torch.uint32 else flat.to(torch.int32)
+    flat = flat.contiguous()
+    pairs = flat.numel()
+    most = pairs // TOKENS_TILE + min(experts, pairs)
+    dev = indices.device
+    tile_expert = torch.empty(most, dtype=torch.uint32, device=dev)
+    token = torch.empty(most * TOKENS_TILE, dtype=torch.uint32, device=dev)
+    where = torch.empty(pairs, dtype=torch.uint32, device=dev)
+    if pairs:
+        ws = torch.empty(int(_lib.lib().smoe_tiles_of_workspace_size(pairs, experts)), dtype=torch.uint8, device=dev)
+        _lib.call("smoe_tiles_of", _lib.ptr(flat), pairs, k, experts, _lib.ptr(tile_expert), _lib.ptr(token),
+                  _lib.ptr(where), _lib.ptr(ws), ws.numel(), _lib.stream())
+    return tile_expert, token, where
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """mlx-lm's swiglu = silu(gate) * up in the inputs' type (sigmoid in float32 rounded to the type, then two
+    products in the type), as the reference relies on it (strata_mlx/blocks.py:222-237)."""
+    _lib.require_cuda(gate, up)
+    gate, up = gate.contiguous(), up.contiguous()
+    out = torch.empty_like(gate)
+    _lib.call("smoe_swiglu", _lib.ptr(gate), _lib.ptr(up), gate.numel(), _lib.ptr(out), _lib.dtype_code(gate.dtype),
+              _lib.stream())
+    return out
+
+
+def _as_int64(t):
+    return (t.view(torch.int32) if t.dtype == torch.uint32 else t).to(torch.int64)
+
+
+def _tiled_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.Tensor:
+    """The three products of a prompt's pairs through `tile_matmul`, the pairs in tiles (`tiles_of`)
+    (strata_mlx/blocks.py:684-694)."""
+    tiles, token, where = tiles_of(indices, gate.num_experts)
+    a = x.reshape(-1, x.shape[-1]).index_select(0, _as_int64(token))
+
+    def product(lin, a):
+        return tile_matmul(lin.blocks, lin.kind, lin.shape, a, tiles)
+
+    h = swiglu(product(gate, a), product(up, a)).to(x.dtype)
+    out = product(down, h).index_select(0, _as_int64(where)).to(x.dtype)
+    return out.reshape(*indices.shape, down.output_dims)
+
+
+def matvec_glu(lin, idx: torch.Tensor, gate: torch.Tensor, up: torch.Tensor):
+    """`lin(swiglu(gate, up), idx)` for a BlockSwitchLinear, one pair to each row of gate and up, (pairs, out)
+    (strata_mlx/blocks.py:939-955). None where the activations are of a type the kernel does not take."""
+    if gate.dtype not in (torch.float16, torch.float32) or up.dtype != gate.dtype:
+        return None
+    _lib.require_cuda(idx, gate, up, lin.blocks)
+    idx = _flat_idx(idx)
+    pairs = idx.numel()
+    gate = gate.reshape(pairs, -1).contiguous()
+    up = up.reshape(pairs, -1).contiguous()
+    out = torch.empty((pairs, lin.output_dims), dtype=gate.dtype, device=gate.device)
+    if pairs:
+        _lib.call("smoe_matvec_glu", _kind(lin.kind), _lib.ptr(lin.blocks), lin.num_experts, lin.output_dims,
+                  lin.input_dims, _lib.ptr(idx), pairs, _lib.ptr(gate), _lib.ptr(up), _lib.ptr(out),
+                  _lib.dtype_code(gate.dtype), _lib.stream())
+    return out
+
+
+def gate_up(gate, up, x2: torch.Tensor, idx_flat: torch.Tensor, share: int):
+    """The gate and up products of the same pairs in one launch (two BlockSwitchLinear calls of the
+    reference, strata_mlx/blocks.py:971). x2 (pairs / share, in) -> two (pairs, out)."""
+    pairs = idx_flat.numel()
+    g = torch.empty((pairs, gate.output_dims), dtype=x2.dtype, device=x2.device)
+    u = torch.empty_like(g)
+    if gate.kind != up.kind or gate.shape != up.shape:
+        return _matvec(gate, x2, idx_flat, share, x2.dtype), _matvec(up, x2, idx_flat, share, x2.dtype)
+    if pairs:
+        _lib.call("smoe_matvec_gate_up", _kind(gate.kind), _lib.ptr(gate.blocks), _kind(up.kind), _lib.ptr(up.blocks),
+                  gate.num_experts, gate.output_dims, gate.input_dims, _lib.ptr(idx_flat), pairs, share,
+                  _lib.ptr(x2), _lib.ptr(g), _lib.ptr(u), _lib.dtype_code(x2.dtype), _lib.stream())
+    return g, u
+
+
+def switch_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.Tensor:
+    """down(silu(gate(x)) * up(x)) through each token's experts: x (..., in), indices (..., experts per token)
+    -> (..., experts per token, out) (strata_mlx/blocks.py:958-986)."""
+    _lib.require_cuda(x, indices)
+    lins = (up, gate, down)
+    if (indices.numel() >= TILES_FROM and x.dtype in (torch.float16, torch.float32)
+            and all(tileable(lin.kind, lin.output_dims, lin.input_dims) for lin in lins)):
+        return _tiled_glu(x, indices, up, gate, down)
+    k = indices.shape[-1]
+    idx = _flat_idx(indices)
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    if idx.numel() != x2.shape[0] * k:
+        raise ValueError("indices must hold k experts for every token of x")
+    if idx.numel() >= min(lin.unpack_from for lin in lins):
+        g = gate._as_floats(x2, idx, k)
+        u = up._as_floats(x2, idx, k)
+        out = down._as_floats(swiglu(g, u), idx, 1)
+        return out.reshape(*indices.shape, down.output_dims)
+    g, u = gate_up(gate, up, x2, idx, k)
+    if BLOCK_GLU and idx.numel() <= MATVEC_GLU_UPTO:
+        out = matvec_glu(down, idx, g, u)
+    else:
+        out = _matvec(down, swiglu(g, u), idx, 1, x.dtype)
+    return out.reshape(*indices.shape, down.output_dims)
+
+
+class BlockSwitchGLU:
+    """A layer's routed experts, called like mlx-lm's `SwitchGLU` (strata_mlx/blocks.py:989-996)."""
+
+    def __init__(self, gate: BlockSwitchLinear, up: BlockSwitchLinear, down: BlockSwitchLinear):
+        self.gate_proj, self.up_proj, self.down_proj = gate, up, down
+
+    def __call__(self, x: torch.Tensor, indices: torch.Tensor) -> torch.Tensor:
+        return switch_glu(x, indices, self.up_proj, self.gate_proj, self.down_proj)
+
+
+class BlockLinear:
+    """One linear layer kept as the file's blocks (the shared expert's gate/up/down; the reference holds
+    these as MLX QuantizedLinear from `to_affine`, strata_mlx/load.py:253-256). x (..., in) -> (..., out)."""
+
+    def __init__(self, blocks: torch.Tensor, kind: str, shape: tuple):
+        self.stack = BlockSwitchLinear(blocks, kind, (1, *shape))
+        self.kind, self.output_dims, self.input_dims = kind, shape[0], shape[1]
+
+    @property
+    def blocks(self):
+        return self.stack.blocks
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        x2 = x.reshape(-1, self.input_dims).contiguous()
+        idx = torch.zeros(x2.shape[0], dtype=torch.int32, device=x.device)
+        return _matvec(self.stack, x2, idx, 1, x.dtype).reshape(*x.shape[:-1], self.output_dims)
+
+
+class BlockMLP:
+    """The shared expert: down(silu(gate(x)) * up(x)) on blocks (mlx-lm's MLP, strata_mlx/load.py:419-421),
+    gate and up in one launch and swiglu formed by the down kernel."""
+
+    def __init__(self, gate: BlockLinear, up: BlockLinear, down: BlockLinear):
+        self.gate_proj, self.up_proj, self.down_proj = gate, up, down
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        idx = torch.zeros(x2.shape[0], dtype=torch.int32, device=x.device)
+        g, u = gate_up(self.gate_proj.stack, self.up_proj.stack, x2, idx, 1)
+        out = matvec_glu(self.down_proj.stack, idx, g, u)
+        return out.reshape(*x.shape[:-1], self.down_proj.output_dims)

@@ -1,0 +1,107 @@
+// Shared helpers of the strata_moe CUDA library: status handling, float16 I/O, async copies.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/strata_moe.h"
+
+namespace smoe {
+
+// ---- host side: errors
+
+void set_error(const std::string& msg);  // defined in smoe_api.cu, thread-local message
+
+inline int fail(int code, const std::string& msg) {
+    set_error(msg);
+    return code;
+}
+
+inline int launch_status(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        set_error(std::string(what) + ": " + cudaGetErrorString(e));
+        return -static_cast<int>(e);
+    }
+    return SMOE_OK;
+}
+
+#define SMOE_REQUIRE(cond, code, msg) \
+    do {                              \
+        if (!(cond)) return ::smoe::fail((code), (msg)); \
+    } while (0)
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// ---- device side: loads of little-endian fields of a block (any alignment)
+
+__device__ __forceinline__ uint32_t u8(const uint8_t* p) { return p[0]; }
+__device__ __forceinline__ uint32_t u16le(const uint8_t* p) { return uint32_t(p[0]) | (uint32_t(p[1]) << 8); }
+__device__ __forceinline__ uint32_t u32le(const uint8_t* p) { return u16le(p) | (u16le(p + 2) << 16); }
+__device__ __forceinline__ float half_at(const uint8_t* p) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(u16le(p))));
+}
+
+// activation types: float32 or float16, converted to/from float32
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+template <typename T> __device__ __forceinline__ T from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float v) { return __float2half_rn(v); }
+
+// ---- async copies (sm_80+ cp.async; 16-byte granularity, zero-fill past `valid` bytes)
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src, int valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_addr(smem_dst)), "l"(gmem_src),
+                 "r"(valid));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+__device__ __forceinline__ void cp_async_wait_dyn(int n) {
+    // wait_group takes an immediate: dispatch the few depths used here
+    switch (n) {
+        case 0: cp_async_wait<0>(); break;
+        case 1: cp_async_wait<1>(); break;
+        case 2: cp_async_wait<2>(); break;
+        case 3: cp_async_wait<3>(); break;
+        case 4: cp_async_wait<4>(); break;
+        case 5: cp_async_wait<5>(); break;
+        case 6: cp_async_wait<6>(); break;
+        default: cp_async_wait<7>(); break;
+    }
+}
+
+// Copy bytes [src, src + n) of a blob that ends at `end` into smem starting at dst (16-byte aligned) with
+// 16-byte copies from the aligned address at or below src; the bytes land at dst + (src & 15). Lanes
+// `lane` of `width` share the work. Copies never read at or beyond `end`.
+__device__ __forceinline__ int stage_bytes(uint8_t* dst, const uint8_t* src, int64_t n, const uint8_t* end,
+                                           int lane, int width) {
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(src) & ~uintptr_t(15);
+    const int off = static_cast<int>(reinterpret_cast<uintptr_t>(src) - a0);
+    const int chunks = static_cast<int>((off + n + 15) >> 4);
+    const uintptr_t e = reinterpret_cast<uintptr_t>(end);
+    for (int c = lane; c < chunks; c += width) {
+        const uintptr_t g = a0 + 16 * uintptr_t(c);
+        int valid = e > g ? static_cast<int>(e - g < 16 ? e - g : 16) : 0;
+        cp_async16(dst + 16 * c, reinterpret_cast<const void*>(g), valid);
+    }
+    return off;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace smoe

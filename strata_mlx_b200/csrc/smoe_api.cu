@@ -1,0 +1,34 @@
+// Library-wide entry points: error messages, version, block table.
+#include <string>
+
+#include "blocks.cuh"
+
+namespace smoe {
+
+static thread_local std::string g_last_error;
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+}  // namespace smoe
+
+using namespace smoe;
+
+extern "C" const char* smoe_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int smoe_version(void) { return 1; }
+
+extern "C" int smoe_built_arch(void) {
+#ifdef SMOE_ARCH
+    return SMOE_ARCH;
+#else
+    return 0;
+#endif
+}
+
+extern "C" int smoe_block_info(int kind, int* per_block, int* block_bytes) {
+    int per = 0, bytes = 0;
+    if (!block_info(kind, per, bytes)) return fail(SMOE_EKIND, "block type " + std::to_string(kind) + " has no decoder");
+    if (per_block) *per_block = per;
+    if (block_bytes) *block_bytes = bytes;
+    return SMOE_OK;
+}

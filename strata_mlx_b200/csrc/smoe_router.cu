@@ -1,0 +1,240 @@
+// The router's product, its top-k choice with the softmax over the chosen, and the combine at the end of the
+// MoE block.
+#include <cfloat>
+
+#include "common.cuh"
+
+namespace smoe {
+
+// ---------------------------------------------------------------- router logits
+//
+// A CTA of 8 warps takes two expert rows and up to 8 tokens: four warps to a row, each reading every fourth
+// 16-byte chunk of the row (coalesced across the four), float32 fused multiply-adds, a shuffle tree, then
+// the four partials added in warp order. A token's sum is taken in the same order for any window size.
+
+constexpr int kRtTokens = 8;
+
+template <typename XT>
+__device__ __forceinline__ void load8(const XT* p, float* v);
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float* v) {
+    const uint4 q = *reinterpret_cast<const uint4*>(p);
+    const __half2* h = reinterpret_cast<const __half2*>(&q);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float* v) {
+    const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+
+template <typename XT>
+__global__ void __launch_bounds__(256) router_kernel(const __half* __restrict__ w, const XT* __restrict__ x,
+                                                     int64_t tokens, int64_t experts, int64_t hidden,
+                                                     float* __restrict__ logits) {
+    __shared__ float part[2][4][kRtTokens];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int local_row = warp >> 2, quarter = warp & 3;
+    const int64_t e = int64_t(blockIdx.x) * 2 + local_row;
+    const int64_t t0 = int64_t(blockIdx.y) * kRtTokens;
+    const int nt = static_cast<int>(min(int64_t(kRtTokens), tokens - t0));
+    float acc[kRtTokens];
+#pragma unroll
+    for (int t = 0; t < kRtTokens; ++t) acc[t] = 0.0f;
+    if (e < experts) {
+        const __half* row = w + e * hidden;
+        const int64_t chunks = hidden >> 3;
+        for (int64_t c = quarter * 32 + lane; c < chunks; c += 128) {
+            float wv[8];
+            load8<__half>(row + 8 * c, wv);
+#pragma unroll
+            for (int t = 0; t < kRtTokens; ++t) {
+                if (t < nt) {
+                    float xv[8];
+                    load8<XT>(x + (t0 + t) * hidden + 8 * c, xv);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[t] = fmaf(wv[j], xv[j], acc[t]);
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kRtTokens; ++t) acc[t] = warp_sum(acc[t]);
+    if (lane == 0) {
+#pragma unroll
+        for (int t = 0; t < kRtTokens; ++t) part[local_row][quarter][t] = acc[t];
+    }
+    __syncthreads();
+    if (threadIdx.x < 2 * kRtTokens) {
+        const int r = threadIdx.x / kRtTokens, t = threadIdx.x % kRtTokens;
+        const int64_t er = int64_t(blockIdx.x) * 2 + r;
+        if (er < experts && t < nt) {
+            float s = part[r][0][t];
+            s += part[r][1][t];
+            s += part[r][2][t];
+            s += part[r][3][t];
+            logits[(t0 + t) * experts + er] = s;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- top-k and softmax over the chosen
+//
+// A warp per row: its values in registers (NV per lane, -inf past n), k rounds of a (value, index)
+// arg-max over the warp, ties to the lower index, the winner struck out. Then the softmax of the chosen.
+
+__device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t bi) {
+    return v > bv || (v == bv && i < bi);
+}
+
+template <int NV>
+__global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ logits, int64_t rows, int n, int k,
+                                                   uint32_t* __restrict__ idx, float* __restrict__ weights) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t row = int64_t(blockIdx.x) * 4 + warp;
+    if (row >= rows) return;
+    const float* in = logits + row * n;
+    float v[NV];
+    bool live[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+        const int j = 32 * i + lane;
+        live[i] = j < n;
+        v[i] = live[i] ? in[j] : -INFINITY;
+    }
+    float top0 = 0.0f, sum = 0.0f, chosen = 0.0f;
+    for (int r = 0; r < k; ++r) {
+        float bv = -INFINITY;
+        uint32_t bi = 0xffffffffu;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+            const uint32_t j = 32u * i + lane;
+            if (live[i] && better(v[i], j, bv, bi)) {
+                bv = v[i];
+                bi = j;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) idx[row * k + r] = bi;
+        if (bi != 0xffffffffu && (bi & 31u) == uint32_t(lane)) {
+#pragma unroll
+            for (int i = 0; i < NV; ++i)
+                if (uint32_t(i) == (bi >> 5)) live[i] = false;
+        }
+        // softmax over the chosen, largest first: lane r keeps its own chosen logit
+        if (r == 0) top0 = bv;
+        if (lane == (r & 31) && r < 32) chosen = bv;
+    }
+    if (weights != nullptr) {
+        // exp(v - max) / sum in float32; k <= 32 here (checked on the host), one value a lane
+        const float ex = lane < k ? expf(chosen - top0) : 0.0f;
+        sum = warp_sum(lane < k ? ex : 0.0f);
+        if (lane < k) weights[row * k + lane] = ex / sum;
+    }
+}
+
+// ---------------------------------------------------------------- combine
+
+template <typename T> __device__ __forceinline__ T mul_t(T a, T b);
+template <> __device__ __forceinline__ __half mul_t<__half>(__half a, __half b) { return __hmul(a, b); }
+template <> __device__ __forceinline__ float mul_t<float>(float a, float b) { return __fmul_rn(a, b); }
+template <typename T> __device__ __forceinline__ T add_t(T a, T b);
+template <> __device__ __forceinline__ __half add_t<__half>(__half a, __half b) { return __hadd(a, b); }
+template <> __device__ __forceinline__ float add_t<float>(float a, float b) { return __fadd_rn(a, b); }
+
+template <typename T>
+__global__ void combine_kernel(const T* __restrict__ y, const float* __restrict__ w, const T* __restrict__ g,
+                               const T* __restrict__ s, int64_t tokens, int k, int64_t d, T* __restrict__ out) {
+    const int64_t t = blockIdx.y;
+    const float* wt = w + t * k;
+    const T gate = from_f32<T>(1.0f / (1.0f + expf(-to_f32(g[t]))));
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < d; i += int64_t(gridDim.x) * blockDim.x) {
+        const T* yt = y + (t * k) * d + i;
+        float acc = 0.0f;
+        for (int j = 0; j < 8 && j < k; ++j) {
+            float part = 0.0f;
+            for (int kk = j; kk < k; kk += 8) part = __fadd_rn(__fmul_rn(to_f32(yt[int64_t(kk) * d]), wt[kk]), part);
+            acc = j == 0 ? part : __fadd_rn(part, acc);
+        }
+        const T routed = from_f32<T>(acc);
+        const T shared = mul_t<T>(gate, s[t * d + i]);
+        out[t * d + i] = add_t<T>(routed, shared);
+    }
+}
+
+}  // namespace smoe
+
+using namespace smoe;
+
+extern "C" int smoe_router_logits(const uint16_t* weight, const void* x, int x_dtype, int64_t tokens, int64_t experts,
+                                  int64_t hidden, float* logits, void* stream) {
+    if (tokens == 0) return SMOE_OK;
+    SMOE_REQUIRE(weight && x && logits && tokens > 0 && experts > 0, SMOE_EARG, "null pointer or empty router");
+    SMOE_REQUIRE(hidden > 0 && hidden % 8 == 0, SMOE_ESHAPE, "router rows must hold a multiple of 8 values");
+    SMOE_REQUIRE((reinterpret_cast<uintptr_t>(weight) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
+                 SMOE_EARG, "router weight and activations must be 16-byte aligned");
+    SMOE_REQUIRE((tokens + kRtTokens - 1) / kRtTokens <= 65535, SMOE_ESHAPE, "too many tokens for one router call");
+    dim3 grid(static_cast<unsigned>((experts + 1) / 2), static_cast<unsigned>((tokens + kRtTokens - 1) / kRtTokens));
+    cudaStream_t st = as_stream(stream);
+    const __half* w = reinterpret_cast<const __half*>(weight);
+    if (x_dtype == SMOE_F16)
+        router_kernel<__half><<<grid, 256, 0, st>>>(w, static_cast<const __half*>(x), tokens, experts, hidden, logits);
+    else if (x_dtype == SMOE_F32)
+        router_kernel<float><<<grid, 256, 0, st>>>(w, static_cast<const float*>(x), tokens, experts, hidden, logits);
+    else
+        return fail(SMOE_EDTYPE, "router activations must be float16 or float32");
+    return launch_status("router_logits");
+}
+
+extern "C" int smoe_top_k(const float* logits, int64_t rows, int64_t n, int64_t k, uint32_t* idx, float* weights,
+                          void* stream) {
+    if (rows == 0) return SMOE_OK;
+    SMOE_REQUIRE(logits && idx && rows > 0, SMOE_EARG, "null pointer");
+    SMOE_REQUIRE(n > 0 && n <= 2048, SMOE_ESHAPE, "top_k takes rows of 1 to 2048 logits");
+    SMOE_REQUIRE(k >= 1 && k <= n && k <= 32, SMOE_ESHAPE, "top_k takes 1 <= k <= min(n, 32)");
+    const unsigned grid = static_cast<unsigned>((rows + 3) / 4);
+    cudaStream_t st = as_stream(stream);
+    const int nn = static_cast<int>(n), kk = static_cast<int>(k);
+    if (n <= 256)
+        topk_kernel<8><<<grid, 128, 0, st>>>(logits, rows, nn, kk, idx, weights);
+    else if (n <= 512)
+        topk_kernel<16><<<grid, 128, 0, st>>>(logits, rows, nn, kk, idx, weights);
+    else if (n <= 1024)
+        topk_kernel<32><<<grid, 128, 0, st>>>(logits, rows, nn, kk, idx, weights);
+    else
+        topk_kernel<64><<<grid, 128, 0, st>>>(logits, rows, nn, kk, idx, weights);
+    return launch_status("top_k");
+}
+
+extern "C" int smoe_combine(const void* y, const float* w, const void* g, const void* s, int64_t tokens, int64_t k,
+                            int64_t d, void* out, int dtype, void* stream) {
+    if (tokens == 0) return SMOE_OK;
+    SMOE_REQUIRE(y && w && g && s && out && tokens > 0 && k > 0 && d > 0, SMOE_EARG, "null pointer or empty shape");
+    SMOE_REQUIRE(tokens <= 65535, SMOE_ESHAPE, "too many tokens for one combine call");
+    dim3 grid(static_cast<unsigned>(std::min<int64_t>((d + 255) / 256, 64)), static_cast<unsigned>(tokens));
+    cudaStream_t st = as_stream(stream);
+    if (dtype == SMOE_F16)
+        combine_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(y), w, static_cast<const __half*>(g),
+                                                    static_cast<const __half*>(s), tokens, static_cast<int>(k), d,
+                                                    static_cast<__half*>(out));
+    else if (dtype == SMOE_F32)
+        combine_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(y), w, static_cast<const float*>(g),
+                                                   static_cast<const float*>(s), tokens, static_cast<int>(k), d,
+                                                   static_cast<float*>(out));
+    else
+        return fail(SMOE_EDTYPE, "combine takes float16 or float32 activations");
+    return launch_status("combine");
+}

@@ -1,0 +1,141 @@
+"""The MoE block's router, top-k choice and combine on B200: the MoE part of strata-mlx's `strata_mlx/fused.py`.
+
+    WindowLinear   float16 router weights times the activations, float32 sums and result
+    top_k          the k largest logits of each row, largest first, ties to the lower index
+    moe_combine    sum_k y_k w_k rounded to the type, plus sigmoid(g) * the shared expert, in MLX's order
+    SparseMoeBlock the model's MoE block as `_Routed.__call__` computes it (strata_mlx/fused.py:484-497)
+
+Names and conventions follow the reference; tensors are torch CUDA tensors and every product runs in the
+sm_100a kernels of libstrata_moe.so.
+"""
+
+import torch
+
+from . import _lib
+from .blocks import BlockMLP, BlockSwitchGLU
+
+ROUTER_TOPK = True  # strata_mlx/fused.py:420 (the kernel is the only top-k here; kept for engines that set it)
+ROUTER_AS_IS = True  # the router reads float16 activations as they are (strata_mlx/fused.py:421)
+COMBINE_UPTO = 16  # strata_mlx/fused.py:464: tokens the reference's kernel takes; this one takes any count
+
+
+class WindowLinear:
+    """A float16 linear layer without bias whose products come back in float32 (strata_mlx/fused.py:357-390).
+
+    Wraps a weight tensor (rows, cols) or an object with a `.weight`; any window of tokens goes through the
+    kernel, and a token's sum is taken in the same order whatever the window."""
+
+    upto, groups = 8, 16
+
+    def __init__(self, linear):
+        self.linear = linear
+        w = self.weight
+        self.rows, self.cols = w.shape
+
+    @property
+    def weight(self) -> torch.Tensor:
+        return self.linear if isinstance(self.linear, torch.Tensor) else self.linear.weight
+
+    def takes(self, x: torch.Tensor) -> bool:
+        return self.weight.dtype == torch.float16 and x.dtype in (torch.float16, torch.float32)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        w = self.weight
+        _lib.require_cuda(w, x)
+        if not self.takes(x):
+            raise ValueError("WindowLinear takes float16 weights and float16/float32 activations")
+        tokens = x.numel() // self.cols
+        x2 = x.reshape(tokens, self.cols).contiguous()
+        out = torch.empty((tokens, self.rows), dtype=torch.float32, device=x.device)
+        if tokens:
+            _lib.call("smoe_router_logits", _lib.ptr(w.contiguous()), _lib.ptr(x2), _lib.dtype_code(x.dtype), tokens,
+                      self.rows, self.cols, _lib.ptr(out), _lib.stream())
+        return out.reshape(*x.shape[:-1], self.rows)
+
+
+def _top_k(logits: torch.Tensor, k: int, with_weights: bool):
+    _lib.require_cuda(logits)
+    if logits.dtype != torch.float32:
+        raise ValueError("top_k takes float32 logits")
+    n = logits.shape[-1]
+    rows = logits.numel() // n
+    lg = logits.reshape(rows, n).contiguous()
+    idx = torch.empty((rows, k), dtype=torch.uint32, device=logits.device)
+    w = torch.empty((rows, k), dtype=torch.float32, device=logits.device) if with_weights else None
+    if rows:
+        _lib.call("smoe_top_k", _lib.ptr(lg), rows, n, k, _lib.ptr(idx), _lib.ptr(w), _lib.stream())
+    shape = (*logits.shape[:-1], k)
+    return idx.reshape(shape), (w.reshape(shape) if w is not None else None)
+
+
+def top_k(logits: torch.Tensor, k: int) -> torch.Tensor:
+    """The indices of the k largest logits (..., N) float32, as `mx.argpartition(-logits, k - 1)[..., :k]`:
+    largest first, ties to the lower index (strata_mlx/fused.py:424-436). uint32."""
+    return _top_k(logits, k, False)[0]
+
+
+def top_k_softmax(logits: torch.Tensor, k: int):
+    """`top_k` and `softmax(take_along_axis(logits, idx), precise=True)` in one launch
+    (strata_mlx/fused.py:490-491) -> (idx uint32, w float32)."""
+    return _top_k(logits, k, True)
+
+
+def moe_combine(y: torch.Tensor, w: torch.Tensor, g: torch.Tensor, s: torch.Tensor):
+    """y (..., K, D), w (..., K) float32, g (..., 1), s (..., D) -> (..., D) in y's type
+    (strata_mlx/fused.py:467-481). None where the types are not the kernel's."""
+    *lead, k, d = y.shape
+    if y.dtype not in (torch.float16, torch.float32) or w.dtype != torch.float32:
+        return None
+    if g.dtype != y.dtype or s.dtype != y.dtype:
+        return None
+    _lib.require_cuda(y, w, g, s)
+    rows = y.numel() // (k * d)
+    out = torch.empty((rows, d), dtype=y.dtype, device=y.device)
+    if rows:
+        _lib.call("smoe_combine", _lib.ptr(y.contiguous()), _lib.ptr(w.contiguous()), _lib.ptr(g.contiguous()),
+                  _lib.ptr(s.contiguous()), rows, k, d, _lib.ptr(out), _lib.dtype_code(y.dtype), _lib.stream())
+    return out.reshape(*lead, d)
+
+
+class SparseMoeBlock:
+    """The model's MoE block with the router's choice made by `top_k` and its end by `moe_combine`, computed
+    as `_Routed.__call__` computes it (strata_mlx/fused.py:484-497):
+
+        logits = gate(x) (float32); idx = top_k(logits, k); w = softmax(logits[idx]);
+        y = switch_mlp(x, idx); g = shared_expert_gate(x); s = shared_expert(x); out = moe_combine(y, w, g, s)
+
+    gate: WindowLinear or float16 weight (experts, hidden); switch_mlp: BlockSwitchGLU; shared_expert:
+    BlockMLP; shared_expert_gate: float16 weight (1, hidden)."""
+
+    def __init__(self, gate, switch_mlp: BlockSwitchGLU, shared_expert: BlockMLP, shared_expert_gate, top_k: int):
+        self.gate = gate if isinstance(gate, WindowLinear) else WindowLinear(gate)
+        self.switch_mlp, self.shared_expert = switch_mlp, shared_expert
+        self.shared_expert_gate = shared_expert_gate if isinstance(shared_expert_gate, WindowLinear) else WindowLinear(
+            shared_expert_gate)
+        self.top_k = top_k
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        logits = self.gate(x)
+        idx, w = top_k_softmax(logits, self.top_k)
+        y = self.switch_mlp(x, idx)
+        g = self.shared_expert_gate(x).to(x.dtype)
+        s = self.shared_expert(x)
+        out = moe_combine(y, w, g, s)
+        if out is None:
+            raise ValueError("the combine takes float16 or float32 activations")
+        return out
+
+
+_Routed = SparseMoeBlock
+
+
+def install_routers(layers) -> None:
+    """Make the routers of `layers` WindowLinear products (strata_mlx/fused.py:500-507): every `layer.mlp`
+    with a float16 `.gate` weight gets a WindowLinear gate."""
+    for layer in layers:
+        mlp = getattr(layer, "mlp", None)
+        if mlp is None:
+            continue
+        gate = getattr(mlp, "gate", None)
+        if gate is not None and not isinstance(gate, WindowLinear):
+            mlp.gate = WindowLinear(gate)
