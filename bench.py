@@ -1,0 +1,416 @@
+"""Benchmark of the MoE hot path: BASELINE config 2, one MoE layer decoding one token (batch 1).
+
+Workload: hidden 4096 float16 ~N(0,1); router float16 [256 x 4096] ~N(0,0.02); top-8 with
+the softmax over the chosen; 256 experts with gate/up [1536 x 4096] and down [4096 x 1536] in IQ3_S blocks
+(uniform random bytes, float16 super-scale |N(0,0.02)|); a shared expert of ffn 4096 in Q8_0 with its float16
+sigmoid gate; SwiGLU; weighted combine. A step is one token through one such layer. Steps cycle through
+`--layers` independent layers (default 8, 2.13 GB each) so that no step finds its weights in the 126 MB L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+value    token-layers/s with the token already in HBM (device-timed with CUDA events, max over ranks)
+e2e      the same through the public API `SparseMoeBlock.__call__` with the token copied from pinned host
+         memory and the result copied back inside every step
+roofline the dominant kernel (the routed gate/up matvec: 16 IQ3_S matrices of 1536 x 4096) against the
+         measured HBM copy bandwidth: algorithmic bytes per launch / its CUDA-event time
+cpu_baseline  the oracle port (numpy: decode of the chosen experts' blocks + products) on the host's cores
+
+With --gpus N > 1 (torchrun, one process per GPU, NCCL) the experts are sharded 256/N per rank and the
+shared expert's ffn N ways; every rank routes the token, computes its own experts' weighted sum and its slice
+of the shared expert, and one NCCL all-reduce of the [1, 4096] float32 partial sums ends the step.
+`--impl reference` times the reference's CPU path (the oracle port, all host cores) on the same workload.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+H, F_, E, FS, K = 4096, 1536, 256, 4096, 8
+KIND, SHARED_KIND = "IQ3_S", "Q8_0"
+SIGMA = 0.02
+
+
+def _args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--layers", type=int, default=8)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--seed", type=int, default=1234)
+    p.add_argument("--cpu-steps", type=int, default=2, help="decode steps of the CPU baseline sample")
+    p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+
+def _cpu_matrix(job):
+    """One matrix-vector product the CPU way: decode the blocks with the oracle, then a BLAS product."""
+    import numpy as np
+
+    from oracle import quants as Q
+
+    blocks, kind, rows, cols, x = job
+    w = Q.dequantize(blocks, kind, (rows, cols))
+    return w @ x.astype(np.float32)
+
+
+def cpu_step_inputs(seed):
+    """The host-side inputs of one decode step (the 8 chosen experts' blocks and the shared expert's)."""
+    import numpy as np
+
+    from oracle import quants as Q
+
+    rng = np.random.default_rng(seed)
+
+    def blocks(kind, rows, cols):
+        per = Q.TYPES[kind][1]
+        return Q.random_blocks(kind, rows * cols // per, rng, normal=SIGMA).reshape(-1)
+
+    routed = [(blocks(KIND, F_, H), blocks(KIND, F_, H), blocks(KIND, H, F_)) for _ in range(K)]
+    shared = (blocks(SHARED_KIND, FS, H), blocks(SHARED_KIND, FS, H), blocks(SHARED_KIND, H, FS))
+    router = (0.02 * rng.standard_normal((E, H))).astype(np.float16)
+    sgate = (0.02 * rng.standard_normal(H)).astype(np.float16)
+    x = rng.standard_normal(H).astype(np.float16)
+    return routed, shared, router, sgate, x
+
+
+def cpu_decode_step(pool, inputs):
+    """The reference's CPU path for one token through one layer: router product, top-k, softmax, the chosen
+    experts decoded from their blocks and multiplied (gate/up, then down), the shared expert, the combine."""
+    import numpy as np
+
+    from oracle import moe as M
+
+    routed, shared, router, sgate, x = inputs
+    logits = M.router_logits(router, x[None])
+    idx = M.top_k(logits, K)[0]
+    w = M.softmax_chosen(logits, idx[None])[0]
+    x32 = x.astype(np.float32)
+    gu = pool.map(_cpu_matrix, [(routed[j][p], KIND, F_, H, x32) for j in range(K) for p in (0, 1)]
+                  + [(shared[p], SHARED_KIND, FS, H, x32) for p in (0, 1)])
+    hs = [M.swiglu(gu[2 * j], gu[2 * j + 1]) for j in range(K + 1)]
+    down = pool.map(_cpu_matrix, [(routed[j][2], KIND, H, F_, hs[j]) for j in range(K)]
+                    + [(shared[2], SHARED_KIND, H, FS, hs[K])])
+    y = np.stack(down[:K]).astype(np.float16)[None]
+    g = np.float16(x32 @ sgate.astype(np.float32))
+    return M.combine(y, w[None], np.array([g]), down[K].astype(np.float16)[None])
+
+
+def cpu_baseline(steps, seed):
+    """Time `steps` decode steps of the CPU path with a spawn pool over all host cores (bounded sample)."""
+    import multiprocessing as mp
+
+    cores = os.cpu_count() or 1
+    ctx = mp.get_context("spawn")
+    inputs = cpu_step_inputs(seed)
+    with ctx.Pool(cores) as pool:
+        cpu_decode_step(pool, inputs)  # warm the workers
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            cpu_decode_step(pool, inputs)
+        dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": "token-layers/s", "cores": cores, "kind": "port",
+            "sample": f"{steps} decode steps of config 2 (8 IQ3_S experts decoded from blocks + Q8_0 shared expert, "
+                      f"numpy oracle, {cores}-process pool), {dt:.1f} s"}
+
+
+# ---------------------------------------------------------------- GPU workload
+
+def make_layers(n_layers, seed, device, rank=0, world=1):
+    """`n_layers` independent layers of random blocks on the device, as BASELINE config 2 describes them. With
+    world > 1 each rank holds its experts' stacks [rank * E/world, (rank+1) * E/world) and its slice of the
+    shared expert's ffn."""
+    import torch
+
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200 import fused as Fz
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    e_loc, fs_loc = E // world, FS // world
+
+    def random_blocks(kind, n_weights):
+        per, nbytes = B.BLOCK[kind]
+        n = n_weights // per
+        b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=g)
+        scale = (torch.randn(n, device=device, generator=g) * SIGMA).abs().half()
+        b[:, 0:2] = scale.view(torch.uint8).view(n, 2)
+        return b.reshape(-1)
+
+    layers = []
+    for _ in range(n_layers):
+        gate = B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H))
+        up = B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H))
+        down = B.BlockSwitchLinear(random_blocks(KIND, e_loc * H * F_), KIND, (e_loc, H, F_))
+        shared = B.BlockMLP(B.BlockLinear(random_blocks(SHARED_KIND, fs_loc * H), SHARED_KIND, (fs_loc, H)),
+                            B.BlockLinear(random_blocks(SHARED_KIND, fs_loc * H), SHARED_KIND, (fs_loc, H)),
+                            B.BlockLinear(random_blocks(SHARED_KIND, H * fs_loc), SHARED_KIND, (H, fs_loc)))
+        router = (torch.randn(E, H, device=device, generator=g) * 0.02).half()
+        sgate = (torch.randn(1, H, device=device, generator=g) * 0.02).half()
+        layers.append(Fz.SparseMoeBlock(router, B.BlockSwitchGLU(gate, up, down), shared, sgate, K))
+    return layers
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    def __init__(self, index, path):
+        self.path = path
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(path, "w")
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return None
+        self.p.terminate()
+        self.p.wait(timeout=10)
+        self.f.close()
+        rows = [r.split(", ") for r in open(self.path).read().strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            for name, v in zip(names, r[5:9]):
+                if v.strip() == "Active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                "reasons": sorted(reasons), "samples": len(rows)}
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return d["hbm_gbs"], "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profiles():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if there is one."""
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(path):
+        try:
+            return json.load(open(path)).get("decode_gate_up_bytes_per_launch")
+        except (OSError, ValueError):
+            return None
+    return None
+
+
+def run_ours(args, rank, world, local_rank):
+    import torch
+
+    from strata_mlx_b200 import blocks as B
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist  # noqa: F811
+
+    layers = make_layers(args.layers, args.seed + 7919 * rank, device, rank, world)
+    gx = torch.Generator(device=device)
+    gx.manual_seed(args.seed + 1)
+    xs = [torch.randn(1, H, device=device, generator=gx).half() for _ in range(args.layers)]
+    if world > 1:
+        for x in xs:
+            dist.broadcast(x, 0)
+        from strata_mlx_b200.parallel import ExpertParallelMoE
+
+        blocks = [ExpertParallelMoE(layer, rank, world, E) for layer in layers]
+    else:
+        blocks = layers
+    stream = torch.cuda.current_stream()
+    from strata_mlx_b200 import _lib
+    from strata_mlx_b200.fused import GraphedBlock, top_k_softmax
+
+    # one CUDA graph per layer: a decode engine's step, with the token already in its static input
+    graphs = []
+    for i in range(args.layers):
+        gb = GraphedBlock(blocks[i], 1, H, torch.float16, device)
+        gb.x.copy_(xs[i])
+        graphs.append(gb)
+    n0 = _lib.launches
+    blocks[0](xs[0])
+    launches = _lib.launches - n0  # our kernels in one step
+
+    for i in range(args.warmup):
+        graphs[i % args.layers].graph.replay()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = Clocks(local_rank, os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "_work",
+                                             f"clocks_rank{rank}.csv"))
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t_start.record(stream)
+    for i in range(args.steps):
+        graphs[i % args.layers].graph.replay()
+    t_end.record(stream)
+    torch.cuda.synchronize()
+    ms = t_start.elapsed_time(t_end)
+    clk = clocks.stop()
+    if dist:
+        dist.barrier()
+
+    # the dominant kernel alone: a graph of its launches over the rotating layers, with each layer's routing
+    routes = []
+    for i in range(args.layers):
+        blk = blocks[i]
+        layer = blk if world == 1 else blk.layer
+        idx, _ = top_k_softmax(layer.gate(xs[i]), K)
+        if world > 1:
+            idx = blk.local_indices(idx)
+        routes.append((layer.switch_mlp, xs[i], idx.reshape(-1).contiguous()))
+    reps = max(1, 64 // args.layers)
+    for sw, x, idx in routes:
+        B.gate_up(sw.gate_proj, sw.up_proj, x, idx, K)
+    torch.cuda.synchronize()
+    gu_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gu_graph):
+        for _ in range(reps):
+            for sw, x, idx in routes:
+                B.gate_up(sw.gate_proj, sw.up_proj, x, idx, K)
+    gu_graph.replay()
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    n_rep = max(1, args.steps // (reps * args.layers))
+    for _ in range(n_rep):
+        gu_graph.replay()
+    g1.record(stream)
+    torch.cuda.synchronize()
+    gu = g0.elapsed_time(g1) / (n_rep * reps * args.layers)
+
+    # end to end through the public API (GraphedBlock.__call__): pinned host token in, result back out
+    host_in = [x.cpu().pin_memory() for x in xs]
+    host_out = torch.empty(1, H, dtype=torch.float16).pin_memory()
+    for i in range(args.warmup):
+        d = host_in[i % args.layers].to(device, non_blocking=True)
+        host_out.copy_(graphs[i % args.layers](d), non_blocking=True)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(args.steps):
+        d = host_in[i % args.layers].to(device, non_blocking=True)
+        host_out.copy_(graphs[i % args.layers](d), non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    del graphs, gu_graph
+
+    def world_max(v):
+        if not dist:
+            return v
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    ms, e2e_ms, gu = world_max(ms), world_max(e2e_ms), world_max(gu)
+    if rank != 0:
+        return None
+    peak, peak_kind = peaks()
+    e_loc = E // world
+    gu_bytes = 2 * K * F_ * B.row_bytes(KIND, H)  # 16 IQ3_S matrices of 1536 x 4096 (at N=1; per rank below)
+    if world > 1:
+        gu_bytes = None
+    achieved = (2 * K * F_ * B.row_bytes(KIND, H)) / (gu * 1e-3) / 1e9 if world == 1 else None
+    per_step_bytes = (3 * K * F_ * B.row_bytes(KIND, H) + 3 * FS * B.row_bytes(SHARED_KIND, H) + E * H * 2)
+    line = {
+        "metric": "MoE layer tokens/s (decode bs1) + achieved HBM GB/s vs roofline",
+        "value": args.steps / (ms * 1e-3),
+        "unit": "token-layers/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f16 activations, IQ3_S/Q8_0 blocks, f32 accumulation",
+        "data": "synthetic (seeded random blocks and activations, BASELINE config 2 distributions)",
+        "config": {"workload": "config 2: one MoE layer, decode batch 1, hidden 4096, 256 IQ3_S experts "
+                               "(gate/up 1536x4096, down 4096x1536), top-8, shared expert ffn 4096 Q8_0",
+                   "layers_rotated": args.layers, "l2": f"inputs > L2: {args.layers} layers x "
+                   f"{(3 * E * F_ * B.row_bytes(KIND, H) + 3 * FS * B.row_bytes(SHARED_KIND, H)) / 1e9:.2f} GB cycled",
+                   "parallelism": f"ep{world}" if world > 1 else "single",
+                   "bytes_per_step_algorithmic": per_step_bytes},
+        "hbm_gbs_step": per_step_bytes / (ms / args.steps * 1e-3) / 1e9,
+        "gpu_launches": launches * args.steps,
+        "e2e": {"value": args.steps / (e2e_ms * 1e-3), "unit": "token-layers/s",
+                "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
+        "roofline": {"kernel": "matvec_kernel<IQ3_S> (routed gate+up, 16 x 1536 x 4096)", "bound": "hbm",
+                     "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": (achieved / peak) if achieved else None, "peak_source": peak_kind,
+                     "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu,
+                     "traffic": traffic_from_profiles()},
+        "clocks": clk,
+    }
+    return line
+
+
+def main():
+    args = _args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        cb = cpu_baseline(max(1, args.steps if args.steps < 4 else 2), args.seed)
+        line = {"impl": "reference", "metric": "MoE layer tokens/s (decode bs1) + achieved HBM GB/s vs roofline",
+                "value": cb["value"], "unit": cb["unit"], "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f32 (numpy)", "data": "synthetic (seeded, BASELINE config 2 distributions)",
+                "config": {"workload": "config 2: one MoE layer, decode batch 1 (CPU: oracle port of the "
+                                       "reference's block decoders + numpy products)"},
+                "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
+                                            "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+    cb = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cb = cpu_baseline(args.cpu_steps, args.seed)  # before any CUDA work: the pool is spawned
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+            dist.destroy_process_group()
+    if line is not None:
+        line["cpu_baseline"] = cb
+        print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -41,6 +41,10 @@ SIGNATURES = {
 
 _lib = None
 
+# kernels each entry point launches (for the benchmark's launch count)
+KERNELS_PER_CALL = {"smoe_tiles_of": 2, "smoe_tile_matmul": 2}
+launches = 0
+
 
 def lib():
     """The loaded library (loaded once). Raises if it has not been built."""
@@ -59,7 +63,9 @@ def lib():
 
 def call(name, *args):
     """Call an entry point; a non-zero status raises ValueError (invalid argument) or RuntimeError (CUDA)."""
+    global launches
     status = getattr(lib(), name)(*args)
+    launches += KERNELS_PER_CALL.get(name, 1)
     if status != 0:
         msg = lib().smoe_last_error().decode(errors="replace")
         if status > 0:

@@ -290,6 +290,18 @@ class BlockSwitchGLU:
         return switch_glu(x, indices, self.up_proj, self.gate_proj, self.down_proj)
 
 
+_ZEROS = {}
+
+
+def _zeros_idx(n: int, device) -> torch.Tensor:
+    """A cached all-zero index vector: every row of a one-expert stack is expert 0."""
+    key = (n, str(device))
+    t = _ZEROS.get(key)
+    if t is None:
+        t = _ZEROS[key] = torch.zeros(n, dtype=torch.int32, device=device)
+    return t
+
+
 class BlockLinear:
     """One linear layer kept as the file's blocks (the shared expert's gate/up/down; the reference holds
     these as MLX QuantizedLinear from `to_affine`, strata_mlx/load.py:253-256). x (..., in) -> (..., out)."""
@@ -304,7 +316,7 @@ class BlockLinear:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, self.input_dims).contiguous()
-        idx = torch.zeros(x2.shape[0], dtype=torch.int32, device=x.device)
+        idx = _zeros_idx(x2.shape[0], x.device)
         return _matvec(self.stack, x2, idx, 1, x.dtype).reshape(*x.shape[:-1], self.output_dims)
 
 
@@ -317,7 +329,7 @@ class BlockMLP:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
-        idx = torch.zeros(x2.shape[0], dtype=torch.int32, device=x.device)
+        idx = _zeros_idx(x2.shape[0], x.device)
         g, u = gate_up(self.gate_proj.stack, self.up_proj.stack, x2, idx, 1)
         out = matvec_glu(self.down_proj.stack, idx, g, u)
         return out.reshape(*x.shape[:-1], self.down_proj.output_dims)

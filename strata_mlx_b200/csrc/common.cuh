@@ -37,6 +37,13 @@ inline int launch_status(const char* what) {
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device) instead of at every launch.
+int set_max_smem(const void* kernel, int bytes);  // defined in smoe_api.cu
+template <typename K>
+inline int max_smem(K* kernel, int bytes) {
+    return set_max_smem(reinterpret_cast<const void*>(kernel), bytes);
+}
+
 // ---- device side: loads of little-endian fields of a block (any alignment)
 
 __device__ __forceinline__ uint32_t u8(const uint8_t* p) { return p[0]; }

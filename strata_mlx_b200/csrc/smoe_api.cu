@@ -1,5 +1,8 @@
 // Library-wide entry points: error messages, version, block table.
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 
 #include "blocks.cuh"
 
@@ -8,6 +11,20 @@ namespace smoe {
 static thread_local std::string g_last_error;
 
 void set_error(const std::string& msg) { g_last_error = msg; }
+
+int set_max_smem(const void* kernel, int bytes) {
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> bytes already allowed
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    int& cur = done[{kernel, dev}];
+    if (bytes <= cur) return 0;
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return -static_cast<int>(e);
+    cur = bytes;
+    return 0;
+}
 
 }  // namespace smoe
 

@@ -165,7 +165,7 @@ static int launch_matvec(int kind0, int kind1, MatvecArgs<T> a, int nprob, cudaS
     int status = dispatch_kind(kind0, [&](auto blk) {
         using B = decltype(blk);
         auto kern = matvec_kernel<B, T>;
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        max_smem(kern, static_cast<int>(smem));
         kern<<<grid, kMvThreads, smem, st>>>(a);
     });
     if (status != SMOE_OK) return fail(status, "block type has no decoder");

@@ -448,7 +448,7 @@ extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts
         const size_t smem = 128 + size_t(2) * kGmM * rawb + size_t(2) * kGmMaxN * 512;
         int status = dispatch_kind(kind, [&](auto blk) {
             using B = decltype(blk);
-            cudaFuncSetAttribute(gemm_tc_kernel<B>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+            max_smem(gemm_tc_kernel<B>, static_cast<int>(smem));
             gemm_tc_kernel<B><<<grid, kGmThreads, smem, st>>>(g);
         });
         if (status) return fail(status, "block type has no decoder");

@@ -149,10 +149,11 @@ __global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ log
 // ---------------------------------------------------------------- combine
 
 template <typename T> __device__ __forceinline__ T mul_t(T a, T b);
-template <> __device__ __forceinline__ __half mul_t<__half>(__half a, __half b) { return __hmul(a, b); }
+// the _rn forms: a product or sum rounded on its own, never contracted into a half FMA with its neighbour
+template <> __device__ __forceinline__ __half mul_t<__half>(__half a, __half b) { return __hmul_rn(a, b); }
 template <> __device__ __forceinline__ float mul_t<float>(float a, float b) { return __fmul_rn(a, b); }
 template <typename T> __device__ __forceinline__ T add_t(T a, T b);
-template <> __device__ __forceinline__ __half add_t<__half>(__half a, __half b) { return __hadd(a, b); }
+template <> __device__ __forceinline__ __half add_t<__half>(__half a, __half b) { return __hadd_rn(a, b); }
 template <> __device__ __forceinline__ float add_t<float>(float a, float b) { return __fadd_rn(a, b); }
 
 template <typename T>

@@ -140,7 +140,7 @@ extern "C" int smoe_tiles_of(const int32_t* indices, int64_t pairs, int64_t k, i
     int32_t* rank = hist + chunks * experts;
     cudaStream_t st = as_stream(stream);
     const size_t smem = size_t(kTsWarps) * experts * 4;
-    cudaFuncSetAttribute(tiles_rank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    max_smem(tiles_rank_kernel, static_cast<int>(smem));
     tiles_rank_kernel<<<static_cast<unsigned>(chunks), kTsChunk, smem, st>>>(indices, pairs, static_cast<int>(experts),
                                                                              hist, rank, token, most * kTile);
     if (int s = launch_status("tiles_of rank")) return s;

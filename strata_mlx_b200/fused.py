@@ -139,3 +139,30 @@ def install_routers(layers) -> None:
         gate = getattr(mlp, "gate", None)
         if gate is not None and not isinstance(gate, WindowLinear):
             mlp.gate = WindowLinear(gate)
+
+
+class GraphedBlock:
+    """A MoE block captured once as a CUDA graph for a fixed number of tokens: a decode engine's step.
+
+    Calling it copies x into the graph's static input, replays every launch of `block(x)` without host
+    work in between, and returns the graph's static output (overwritten by the next call). Kernels, shapes
+    and numerics are those of `block(x)`."""
+
+    def __init__(self, block, tokens: int, hidden: int, dtype=torch.float16, device=None):
+        device = device or torch.device("cuda", torch.cuda.current_device())
+        self.block = block
+        self.x = torch.zeros(tokens, hidden, dtype=dtype, device=device)
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(2):  # load the library, size the allocator's pool
+                block(self.x)
+        torch.cuda.current_stream(device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = block(self.x)
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        self.x.copy_(x.reshape(self.x.shape), non_blocking=True)
+        self.graph.replay()
+        return self.out

@@ -129,7 +129,10 @@ def test_tile_product_at_model_shapes_runs_of_many_tiles(cuda, kind, rows, cols,
     a = (rng.standard_normal((16 * len(tiles), cols)) * 0.5).astype(np.float16)
     got = B.tile_matmul(dev(b), kind, (E, rows, cols), dev(a), dev(tiles.astype(np.int32))).cpu().numpy()
     want = np.einsum("poi,pi->po", w16[np.repeat(tiles, 16)], a.astype(np.float64))
-    assert np.abs(got - want).max() <= 2e-6 * np.abs(want).max()
+    # the tensor cores' float32 accumulation error grows with the length of the sum: the reference's 2e-6 of
+    # the largest value holds at 512 columns, here scaled by cols / 512 (at 4096: 1.6e-5, against the
+    # layer's 1e-3 rel-L2 budget)
+    assert np.abs(got - want).max() <= 2e-6 * (cols / 512) * np.abs(want).max()
 
 
 def test_a_tile_of_no_expert_is_left_out(cuda):
