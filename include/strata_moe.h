@@ -122,6 +122,18 @@ SMOE_API size_t smoe_tiles_of_workspace_size(int64_t pairs, int64_t experts);
 SMOE_API int smoe_tiles_of(const int32_t* indices, int64_t pairs, int64_t k, int64_t experts, uint32_t* tile_expert,
                   uint32_t* token, uint32_t* where, void* workspace, size_t workspace_bytes, void* stream);
 
+/* smoe_tiles_of for callers that cannot allocate device memory (a host framework that owns every device
+ * allocation and gives a plugin only its inputs and outputs, or a loop that must not call cudaMalloc because it
+ * can synchronize the device). No counterpart in the reference: it is an addition of this library. Same
+ * arguments and results as smoe_tiles_of, without the workspace: its scratch is a fixed array of 1 MiB + 256
+ * bytes in the library's device image (held by every GPU that loads the library until the process exits),
+ * which limits it to smoe_tiles_of_workspace_size(pairs, experts) <= 1,048,832 bytes (131,072 pairs at 1,024
+ * experts; 209,664 at 256) and returns SMOE_ESHAPE beyond. It allocates nothing. The first call on a device looks up the array's
+ * device address (cudaGetSymbolAddress); make that first call before any stream capture. All calls share
+ * the array: calls that overlap on the GPU race on it. */
+SMOE_API int smoe_tiles_of_noalloc(const int32_t* indices, int64_t pairs, int64_t k, int64_t experts,
+                                   uint32_t* tile_expert, uint32_t* token, uint32_t* where, void* stream);
+
 /* Whether smoe_tile_matmul takes a stack of such rows (strata_mlx/blocks.py:629-631 `tileable`). */
 SMOE_API int smoe_tileable(int kind, int64_t rows, int64_t cols);
 

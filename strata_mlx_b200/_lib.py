@@ -34,6 +34,7 @@ SIGNATURES = {
     "smoe_combine": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
     "smoe_tiles_of_workspace_size": (_sz, [_i64, _i64]),
     "smoe_tiles_of": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _sz, _p]),
+    "smoe_tiles_of_noalloc": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
     "smoe_tileable": (_i, [_i, _i64, _i64]),
     "smoe_tile_matmul_workspace_size": (_sz, [_i64]),
     "smoe_tile_matmul": (_i, [_i, _p, _i64, _i64, _i64, _p, _i, _i64, _p, _p, _p, _sz, _p]),

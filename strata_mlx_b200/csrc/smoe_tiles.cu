@@ -6,6 +6,8 @@
 // the result is deterministic) and writes the chunk's histogram; it also clears `token`. The second gives
 // each expert its tiles (a scan of ceil(count / 16) over experts) and each pair its slot:
 // slot = 16 * first_tile[e] + (pairs of e in earlier chunks) + rank in chunk.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace smoe {
@@ -148,4 +150,79 @@ extern "C" int smoe_tiles_of(const int32_t* indices, int64_t pairs, int64_t k, i
                                                                            static_cast<int>(experts), hist, rank, most,
                                                                            tile_expert, token, where);
     return launch_status("tiles_of place");
+}
+
+// ---------------------------------------------------------------- the same permutation without a workspace
+//
+// Some callers cannot allocate device memory where they call this library: a host framework that owns every
+// device allocation and hands a plugin only its input and output buffers, or a serving loop that must not call
+// cudaMalloc because it can synchronize the whole device. For them smoe_tiles_of_noalloc runs the two kernels
+// above with their scratch (per-chunk histograms and per-pair ranks) in this fixed array instead of a caller's
+// workspace. The array is part of the library's device image: every GPU that loads the library holds its
+// 1 MiB (+ 256 bytes) until the process exits. All calls share it and it keeps what the last call left; nothing in it needs
+// to start at zero (each call writes every histogram entry and rank it later reads), but calls that overlap
+// on the GPU (on different streams, or from different host threads) race on it.
+
+namespace smoe {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t(1) << 20) + 256;  // 1 MiB of ranks and histograms, + alignment
+__device__ __align__(256) uint8_t g_tiles_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// The device address of g_tiles_scratch on the current device. In host code the array's name is only a
+// host-side handle, not a device address, so it is looked up once per device with cudaGetSymbolAddress.
+int scratch_on_current_device(void** addr) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    if (dev < 0 || dev >= kMaxDevices) return fail(SMOE_EARG, "device index beyond the no-alloc table");
+    std::lock_guard<std::mutex> lock(g_scratch_mu);
+    if (g_scratch_addr[dev] == nullptr) {
+        void* p = nullptr;
+        e = cudaGetSymbolAddress(&p, g_tiles_scratch);
+        if (e != cudaSuccess)
+            return fail(-static_cast<int>(e), std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+        g_scratch_addr[dev] = p;
+    }
+    *addr = g_scratch_addr[dev];
+    return SMOE_OK;
+}
+
+}  // namespace
+
+}  // namespace smoe
+
+extern "C" int smoe_tiles_of_noalloc(const int32_t* indices, int64_t pairs, int64_t k, int64_t experts,
+                                     uint32_t* tile_expert, uint32_t* token, uint32_t* where, void* stream) {
+    using namespace smoe;
+    if (pairs == 0) return SMOE_OK;
+    SMOE_REQUIRE(indices && tile_expert && token && where && pairs > 0 && k > 0, SMOE_EARG, "null pointer or no pairs");
+    SMOE_REQUIRE(experts > 0 && experts <= kTsMaxExperts, SMOE_ESHAPE, "tiles_of takes 1 to 1024 experts");
+    SMOE_REQUIRE(pairs % k == 0, SMOE_EARG, "pairs must be a multiple of k");
+    const size_t need = smoe_tiles_of_workspace_size(pairs, experts);
+    SMOE_REQUIRE(need <= kNoAllocScratchBytes, SMOE_ESHAPE,
+                 std::to_string(pairs) + " pairs over " + std::to_string(experts) + " experts need " +
+                     std::to_string(need) + " bytes of scratch, more than the " +
+                     std::to_string(kNoAllocScratchBytes) + " bytes of smoe_tiles_of_noalloc's fixed array; "
+                     "split the pairs or call smoe_tiles_of with a workspace");
+    void* scratch = nullptr;
+    if (int s = scratch_on_current_device(&scratch)) return s;
+    const int64_t chunks = (pairs + kTsChunk - 1) / kTsChunk;
+    const int64_t most = pairs / kTile + std::min(experts, pairs);
+    int32_t* hist = static_cast<int32_t*>(scratch);
+    int32_t* rank = hist + chunks * experts;
+    cudaStream_t st = as_stream(stream);
+    const size_t smem = size_t(kTsWarps) * experts * 4;
+    if (int s = max_smem(tiles_rank_kernel, static_cast<int>(smem))) return fail(s, "tiles_of: shared memory limit");
+    tiles_rank_kernel<<<static_cast<unsigned>(chunks), kTsChunk, smem, st>>>(indices, pairs, static_cast<int>(experts),
+                                                                             hist, rank, token, most * kTile);
+    if (int s = launch_status("tiles_of_noalloc rank")) return s;
+    tiles_place_kernel<<<static_cast<unsigned>(chunks), kTsChunk, 0, st>>>(indices, pairs, static_cast<int>(k),
+                                                                           static_cast<int>(experts), hist, rank, most,
+                                                                           tile_expert, token, where);
+    return launch_status("tiles_of_noalloc place");
 }
