@@ -164,10 +164,11 @@ extern "C" int smoe_tiles_of(const int32_t* indices, int64_t pairs, int64_t k, i
 // on the GPU (on different streams, or from different host threads) race on it.
 
 namespace smoe {
-namespace {
 
 constexpr size_t kNoAllocScratchBytes = (size_t(1) << 20) + 256;  // 1 MiB of ranks and histograms, + alignment
-__device__ __align__(256) uint8_t g_tiles_scratch[kNoAllocScratchBytes];
+static __device__ __align__(256) uint8_t g_tiles_scratch[kNoAllocScratchBytes];
+
+namespace {
 
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
