@@ -221,13 +221,23 @@ def _tiled_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.
     return out.reshape(*indices.shape, down.output_dims)
 
 
+# types whose float16 products run on the tensor-core decode kernel, with the columns of its stage
+MMA_MATVEC = {"IQ3_S": 256, "Q8_0": 128}
+
+
 def matvec_glu(lin, idx: torch.Tensor, gate: torch.Tensor, up: torch.Tensor):
     """`lin(swiglu(gate, up), idx)` for a BlockSwitchLinear, one pair to each row of gate and up, (pairs, out)
-    (strata_mlx/blocks.py:939-955). None where the activations are of a type the kernel does not take."""
+    (strata_mlx/blocks.py:939-955). None where the activations are of a type the kernel does not take.
+
+    For the types of the tensor-core decode kernel the SwiGLU is formed by its own small kernel first (the
+    same function, so the same bits) and the product runs there; the others form it inside the product."""
     if gate.dtype not in (torch.float16, torch.float32) or up.dtype != gate.dtype:
         return None
     _lib.require_cuda(idx, gate, up, lin.blocks)
     idx = _flat_idx(idx)
+    if gate.dtype == torch.float16 and lin.input_dims % MMA_MATVEC.get(lin.kind, 1 << 30) == 0:
+        h = swiglu(gate.reshape(idx.numel(), -1), up.reshape(idx.numel(), -1))
+        return _matvec(lin, h, idx, 1, gate.dtype)
     pairs = idx.numel()
     gate = gate.reshape(pairs, -1).contiguous()
     up = up.reshape(pairs, -1).contiguous()

@@ -86,10 +86,10 @@ __global__ void __launch_bounds__(kMvThreads) matvec_kernel(const MatvecArgs<T> 
     const int nr = static_cast<int>(max(int64_t(0), min(int64_t(a.rows_per_warp), a.rows - r0)));
 
     // 1. this warp's rows -> its slots (every lane commits one group per row, empty or not)
-    const uint8_t* base = a.blocks[prob] + (int64_t(e) * a.rows) * a.row_bytes;
+    const uint8_t* base = (prob ? a.blocks[1] : a.blocks[0]) + (int64_t(e) * a.rows) * a.row_bytes;
     uint8_t* my = slots + int64_t(warp) * a.rows_per_warp * a.stage;
     for (int i = 0; i < a.rows_per_warp; ++i) {
-        if (i < nr) stage_bytes(my + i * a.stage, base + (r0 + i) * a.row_bytes, a.row_bytes, a.end[prob], lane, 32);
+        if (i < nr) stage_bytes(my + i * a.stage, base + (r0 + i) * a.row_bytes, a.row_bytes, prob ? a.end[1] : a.end[0], lane, 32);
         cp_async_commit();
     }
 
@@ -106,7 +106,7 @@ __global__ void __launch_bounds__(kMvThreads) matvec_kernel(const MatvecArgs<T> 
 
     // 3. decode and reduce, a row at a time as its bytes land
     const int runs = static_cast<int>(a.cols >> 5);
-    T* out = a.out[prob] + p * a.rows;
+    T* out = (prob ? a.out[1] : a.out[0]) + p * a.rows;
     for (int i = 0; i < nr; ++i) {
         cp_async_wait_dyn(a.rows_per_warp - 1 - i);
         __syncwarp();
@@ -140,6 +140,11 @@ __global__ void swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u, 
 }
 
 // ---------------------------------------------------------------- host side
+
+// the tensor-core decode matvec (smoe_mv.cu): 0 launched, 1 not taken, else an error status
+int mv_mma_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
+               int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, __half* o0,
+               __half* o1, int nprob, cudaStream_t st);
 
 static int check_stack(int kind, int64_t experts, int64_t rows, int64_t cols, int& per, int& bytes) {
     if (!block_info(kind, per, bytes)) return fail(SMOE_EKIND, "block type " + std::to_string(kind) + " has no decoder");
@@ -199,6 +204,13 @@ static int matvec_common(int kind0, const uint8_t* b0, int kind1, const uint8_t*
     a.cols = cols;
     a.pairs = pairs;
     a.share = share;
+    if constexpr (sizeof(T) == 2) {
+        if (gate == nullptr) {
+            const int r = mv_mma_try(kind0, kind1, b0, a.blocks[1], experts, rows, cols, a.row_bytes, idx, pairs, share,
+                                     static_cast<const __half*>(x), a.out[0], a.out[1], nprob, st);
+            if (r != 1) return r;
+        }
+    }
     return launch_matvec<T>(kind0, kind1, a, nprob, st);
 }
 

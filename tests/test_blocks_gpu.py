@@ -88,6 +88,25 @@ def test_a_prompt_gets_the_same_products_a_pair_at_a_time_and_from_unpacked_weig
     assert np.abs(got[:, 0] - want).max() <= 1e-5 * scale
 
 
+@pytest.mark.parametrize("kind", ["IQ3_S", "Q8_0"])
+@pytest.mark.parametrize("rows, cols", [(40, 512), (1536, 4096), (4096, 1536), (16, 256)])
+@pytest.mark.parametrize("share", [1, 4])
+def test_float16_products_on_the_tensor_core_path(cuda, kind, rows, cols, share):
+    """The decode matvec of the hot path's types (mma.sync on exact float16 integers, float32 scales) against
+    the float64 product: the float16 result within 1e-3 of the largest value (its own rounding is 2^-11)."""
+    rng = np.random.default_rng(rows + cols + share)
+    E, pairs = 5, 8
+    b, w = stack(kind, rng, E, rows, cols, scale=(-0.05, 0.05))
+    layer = B.BlockSwitchLinear(dev(b), kind, (E, rows, cols))
+    idx = rng.integers(0, E, pairs // share * share).reshape(-1, share)
+    x = rng.standard_normal((pairs // share, cols)).astype(np.float16)
+    xs = x[:, None, None, :] if share > 1 else x[:, None, :]
+    got = layer(dev(xs if share > 1 else x.reshape(pairs // share, share, 1, cols)), dev(idx)).float().cpu().numpy()
+    want = np.einsum("pri,pi->pr", w[idx.reshape(-1)].astype(np.float64),
+                     x.astype(np.float64)[np.arange(idx.size) // share])
+    assert np.abs(got.reshape(idx.size, rows) - want).max() <= 1e-3 * np.abs(want).max()
+
+
 def test_half_precision_activations_come_back_as_half(cuda):
     """tests/test_blocks.py:63-70."""
     rng = np.random.default_rng(5)
