@@ -40,13 +40,14 @@ SIGMA = 0.02
 def _args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--steps", type=int, default=2000)
     p.add_argument("--warmup", type=int, default=20)
     p.add_argument("--layers", type=int, default=8)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--seed", type=int, default=1234)
     p.add_argument("--cpu-steps", type=int, default=2, help="decode steps of the CPU baseline sample")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
+    p.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
     return p.parse_args()
 
 
@@ -160,39 +161,130 @@ def make_layers(n_layers, seed, device, rank=0, world=1):
     return layers
 
 
-class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+def run_prefill(device, seed, steps=5, warmup=2):
+    """the same layer shapes in Q2_K (gate/up 1536 x 4096, down 4096 x 1536, 256 experts), a
+    prompt chunk of 1180 tokens ~N(0,1), router logits biased so expert load is Zipf-skewed (s = 1.1): the
+    router weight carries log p_e along a unit direction u that every token has a component 1 along. Times the
+    whole block (router, top-k, tiles_of, three tensor-core tile products, SwiGLU, the shared expert on the
+    tile product, combine) and the three routed tile products alone."""
+    import torch
 
-    def __init__(self, index, path):
-        self.path = path
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-             "clocks_event_reasons.sw_power_cap")
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200 import fused as Fz
+
+    T, kind = 1180, "Q2_K"
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def random_blocks(kd, n_weights):
+        per, nbytes = B.BLOCK[kd]
+        n = n_weights // per
+        b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=g)
+        for at in ((80, 82) if kd == "Q2_K" else (0,)):
+            b[:, at : at + 2] = (torch.randn(n, device=device, generator=g) * SIGMA).abs().half().view(torch.uint8).view(n, 2)
+        return b.reshape(-1)
+
+    gate = B.BlockSwitchLinear(random_blocks(kind, E * F_ * H), kind, (E, F_, H))
+    up = B.BlockSwitchLinear(random_blocks(kind, E * F_ * H), kind, (E, F_, H))
+    down = B.BlockSwitchLinear(random_blocks(kind, E * H * F_), kind, (E, H, F_))
+    shared = B.BlockMLP(B.BlockLinear(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+                        B.BlockLinear(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+                        B.BlockLinear(random_blocks(SHARED_KIND, H * FS), SHARED_KIND, (H, FS)))
+    rank = torch.empty(E, device=device)
+    rank[torch.randperm(E, device=device, generator=g)] = torch.arange(1, E + 1, device=device, dtype=torch.float32)
+    logp = -1.1 * torch.log(rank)
+    logp -= torch.logsumexp(logp, 0)
+    u = torch.randn(H, device=device, generator=g)
+    u /= u.norm()
+    router = (torch.randn(E, H, device=device, generator=g) * 0.02 + logp[:, None] * u[None, :]).half()
+    sgate = (torch.randn(1, H, device=device, generator=g) * 0.02).half()
+    block = Fz.SparseMoeBlock(router, B.BlockSwitchGLU(gate, up, down), shared, sgate, K)
+    x = torch.randn(T, H, device=device, generator=g)
+    x = (x - (x @ u)[:, None] * u[None, :] + u[None, :]).half()
+
+    for _ in range(warmup):
+        block(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        block(x)
+    e1.record()
+    torch.cuda.synchronize()
+    layer_ms = e0.elapsed_time(e1) / steps
+
+    # the routed tile products alone, on this chunk's tiles
+    idx = Fz.top_k(block.gate(x), K)
+    tiles, token, where = B.tiles_of(idx, E)
+    a = x.index_select(0, token.view(torch.int32).long())
+    hsz = torch.empty(a.shape[0], F_, dtype=torch.float16, device=device).normal_()
+    prods = [(gate, a), (up, a), (down, hsz)]
+    for lin, aa in prods:
+        B.tile_matmul(lin.blocks, lin.kind, lin.shape, aa, tiles)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(steps):
+        for lin, aa in prods:
+            B.tile_matmul(lin.blocks, lin.kind, lin.shape, aa, tiles)
+    e1.record()
+    torch.cuda.synchronize()
+    gemm_ms = e0.elapsed_time(e1) / steps
+    pairs = T * K
+    counts = torch.bincount(idx.view(torch.int32).reshape(-1).long(), minlength=E)
+    flops = 2.0 * pairs * 3 * F_ * H
+    return {"workload": "config 3: one MoE layer, prefill chunk of 1180 tokens, 256 Q2_K experts, top-8, Zipf s=1.1 "
+                        "routing, shared expert ffn 4096 Q8_0",
+            "layer_ms": layer_ms, "tokens_per_s": T / (layer_ms * 1e-3),
+            "routed_gemm_ms": gemm_ms, "routed_gemm_tflops": flops / (gemm_ms * 1e-3) / 1e12,
+            "routed_gflop": flops / 1e9, "experts_hit": int((counts > 0).sum().item()),
+            "max_pairs_per_expert": int(counts.max().item())}
+
+
+class Clocks:
+    """SM clocks and throttle reasons sampled with NVML every few milliseconds from a thread while the timed
+    region runs (reading counters only; nothing about the GPU is changed)."""
+
+    NAMES = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+
+    def __init__(self, index, path=None):
+        import threading
+
+        self.samples, self.stop_flag = [], threading.Event()
         try:
-            self.f = open(path, "w")
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.p = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            dev = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(index)).split(",")[index]) \
+                if "CUDA_VISIBLE_DEVICES" in os.environ else index
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(dev)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:  # noqa: BLE001 - no NVML: report no clock record
+            self.nv = None
+            return
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        while not self.stop_flag.is_set():
+            try:
+                mhz = self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+                reasons = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append((mhz, reasons))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(0.005)
 
     def stop(self):
-        if self.p is None:
+        if self.nv is None:
             return None
-        self.p.terminate()
-        self.p.wait(timeout=10)
-        self.f.close()
-        rows = [r.split(", ") for r in open(self.path).read().strip().splitlines() if r.count(",") >= 8]
-        if not rows:
+        self.stop_flag.set()
+        self.t.join(timeout=5)
+        if not self.samples:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in rows:
-            for name, v in zip(names, r[5:9]):
-                if v.strip() == "Active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
-                "reasons": sorted(reasons), "samples": len(rows)}
+        reasons = sorted(name for name, bit in self.NAMES.items() if any(r & bit for _, r in self.samples))
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": float(self.max_mhz),
+                "reasons": reasons, "samples": len(self.samples), "source": "NVML, 5 ms"}
 
 
 def peaks():
@@ -409,6 +501,18 @@ def main():
             dist.destroy_process_group()
     if line is not None:
         line["cpu_baseline"] = cb
+        if world == 1 and not args.no_prefill:
+            import torch
+
+            pf = run_prefill(torch.device("cuda", local_rank), args.seed + 99)
+            peak_tf = 1672.6
+            path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+            if os.path.exists(path):
+                peak_tf = json.load(open(path)).get("bf16_tflops", peak_tf)
+            pf["roofline"] = {"kernel": "gemm_tc_kernel<Q2_K> (three routed tile products)", "bound": "tensor",
+                              "achieved": pf["routed_gemm_tflops"], "peak": peak_tf, "unit": "TFLOP/s",
+                              "frac": pf["routed_gemm_tflops"] / peak_tf}
+            line["prefill"] = pf
         print(json.dumps(line))
 
 

@@ -113,6 +113,21 @@ SMOE_API int smoe_top_k(const float* logits, int64_t rows, int64_t n, int64_t k,
 SMOE_API int smoe_combine(const void* y, const float* w, const void* g, const void* s, int64_t tokens, int64_t k,
                  int64_t d, void* out, int dtype, void* stream);
 
+/* Expert parallelism (N ranks, each holding the experts [lo, lo + count) of every layer and a 1/N slice of the
+ * shared expert's ffn): the pieces around the one all-reduce of a decode step. No counterpart in the
+ * reference, which runs on one device (SURVEY: strata_mlx has no multi-device code); they split
+ * `_Routed.__call__` (strata_mlx/fused.py:487-497) at its combine.
+ *   smoe_localize:     lidx = idx - lo for this rank's experts, else `count` (a pair the kernels leave out).
+ *   smoe_partial_sums: sums[t, 0:d] = sum over this rank's pairs of y * w (MLX's order among them), float32;
+ *                      sums[t, d:2d] = float(s[t]) (this rank's slice of the shared expert) or 0 if s is null.
+ *   smoe_combine_sums: after the all-reduce of sums over ranks, out = half(routed) + half(half(sigmoid(g))
+ *                      half(shared)), the combine of strata_mlx/fused.py:448-462 on the summed partials. */
+SMOE_API int smoe_localize(const uint32_t* idx, int64_t n, int64_t lo, int64_t count, uint32_t* out, void* stream);
+SMOE_API int smoe_partial_sums(const void* y, const float* w, const uint32_t* lidx, int64_t experts, const void* s,
+                               int64_t tokens, int64_t k, int64_t d, float* sums, int dtype, void* stream);
+SMOE_API int smoe_combine_sums(const float* sums, const void* g, int64_t tokens, int64_t d, void* out, int dtype,
+                               void* stream);
+
 /* The dispatch permutation of `pairs` = tokens * k expert indices (int32, flat) into tiles of 16 slots,
  * each tile one expert's: tile_expert[most] (experts for a tile nothing fills), token[most * 16] (0 in an
  * unfilled slot), where[pairs] (the slot of each pair), most = pairs / 16 + min(experts, pairs).

@@ -166,3 +166,30 @@ def moe_block(x, router_w, k, experts, shared, shared_gate_w, dtype=np.float16, 
     s = dense_mlp(x, *shared, dtype=dtype)
     g = (x.astype(np.float64) @ np.asarray(shared_gate_w, dtype=np.float64).reshape(-1)).astype(dtype)
     return combine(y, w, g, s), idx, w, logits
+
+
+def partial_sums(y, w, lidx, experts, s):
+    """One rank's float32 partials of an expert-parallel combine: sum over its pairs (lidx < experts) of y w in
+    MLX's order, and its slice of the shared expert (float32). Returns (T, 2D) float32."""
+    T, K, D = y.shape
+    y32 = y.astype(np.float32)
+    w32 = np.asarray(w, dtype=np.float32)
+    mask = (np.asarray(lidx).reshape(T, K) < experts)
+    acc = np.zeros((T, D), dtype=np.float32)
+    for j in range(min(8, K)):
+        part = np.zeros((T, D), dtype=np.float32)
+        for k in range(j, K, 8):
+            term = (y32[:, k] * w32[:, k : k + 1]).astype(np.float32)
+            part = np.where(mask[:, k : k + 1], term + part, part).astype(np.float32)
+        acc = part if j == 0 else (part + acc).astype(np.float32)
+    shared = np.zeros((T, D), dtype=np.float32) if s is None else s.astype(np.float32)
+    return np.concatenate([acc, shared], axis=1)
+
+
+def combine_sums(sums, g, dtype=np.float16):
+    """The combine on summed partials: half(routed) + half(half(sigmoid(g)) half(shared)) (fused.py:448-462)."""
+    D = sums.shape[1] // 2
+    routed = sums[:, :D].astype(dtype)
+    gate = (np.float32(1) / (np.float32(1) + np.exp(-np.asarray(g, dtype=np.float32)))).astype(dtype)
+    shared = (gate.astype(np.float32)[:, None] * sums[:, D:].astype(dtype).astype(np.float32)).astype(dtype)
+    return (routed.astype(np.float32) + shared.astype(np.float32)).astype(dtype)

@@ -32,6 +32,9 @@ SIGNATURES = {
     "smoe_router_logits": (_i, [_p, _p, _i, _i64, _i64, _i64, _p, _p]),
     "smoe_top_k": (_i, [_p, _i64, _i64, _i64, _p, _p, _p]),
     "smoe_combine": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
+    "smoe_localize": (_i, [_p, _i64, _i64, _i64, _p, _p]),
+    "smoe_partial_sums": (_i, [_p, _p, _p, _i64, _p, _i64, _i64, _i64, _p, _i, _p]),
+    "smoe_combine_sums": (_i, [_p, _p, _i64, _i64, _p, _i, _p]),
     "smoe_tiles_of_workspace_size": (_sz, [_i64, _i64]),
     "smoe_tiles_of": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _sz, _p]),
     "smoe_tiles_of_noalloc": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),

@@ -312,9 +312,25 @@ def _zeros_idx(n: int, device) -> torch.Tensor:
     return t
 
 
+GEMM_FROM = 32  # tokens from which a one-expert layer goes through the tensor-core tile product
+
+
+def _dense_tiles(lin, x2: torch.Tensor) -> torch.Tensor:
+    """x2 (tokens, in) through a one-expert stack on the tile product: tokens padded to tiles of 16 of expert 0.
+    Returns (tokens, out) float32 (weights rounded to x's type, float32 sums, as `tile_matmul`)."""
+    tokens = x2.shape[0]
+    p16 = (tokens + TOKENS_TILE - 1) // TOKENS_TILE * TOKENS_TILE
+    a = x2 if p16 == tokens else torch.cat([x2, x2.new_zeros(p16 - tokens, x2.shape[1])])
+    te = torch.zeros(p16 // TOKENS_TILE, dtype=torch.int32, device=x2.device)
+    return tile_matmul(lin.blocks, lin.kind, lin.shape, a, te)[:tokens]
+
+
 class BlockLinear:
     """One linear layer kept as the file's blocks (the shared expert's gate/up/down; the reference holds
-    these as MLX QuantizedLinear from `to_affine`, strata_mlx/load.py:253-256). x (..., in) -> (..., out)."""
+    these as MLX QuantizedLinear from `to_affine`, strata_mlx/load.py:253-256). x (..., in) -> (..., out).
+
+    A few tokens go through the decode matvec; from GEMM_FROM tokens on (a prompt's chunk) the tensor-core tile
+    product reads the blocks once for all of them."""
 
     def __init__(self, blocks: torch.Tensor, kind: str, shape: tuple):
         self.stack = BlockSwitchLinear(blocks, kind, (1, *shape))
@@ -324,10 +340,18 @@ class BlockLinear:
     def blocks(self):
         return self.stack.blocks
 
+    def gemm(self, x2: torch.Tensor) -> bool:
+        return (x2.shape[0] >= GEMM_FROM and x2.dtype in (torch.float16, torch.float32)
+                and tileable(self.kind, self.output_dims, self.input_dims))
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, self.input_dims).contiguous()
-        idx = _zeros_idx(x2.shape[0], x.device)
-        return _matvec(self.stack, x2, idx, 1, x.dtype).reshape(*x.shape[:-1], self.output_dims)
+        if self.gemm(x2):
+            out = _dense_tiles(self.stack, x2).to(x.dtype)
+        else:
+            idx = _zeros_idx(x2.shape[0], x.device)
+            out = _matvec(self.stack, x2, idx, 1, x.dtype)
+        return out.reshape(*x.shape[:-1], self.output_dims)
 
 
 class BlockMLP:
@@ -339,6 +363,12 @@ class BlockMLP:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
+        if all(p.gemm(x2) for p in (self.gate_proj, self.up_proj, self.down_proj)):
+            # a prompt's chunk: the three products on the tensor cores, rounded to x's type as QuantizedLinear does
+            g = _dense_tiles(self.gate_proj.stack, x2).to(x.dtype)
+            u = _dense_tiles(self.up_proj.stack, x2).to(x.dtype)
+            out = _dense_tiles(self.down_proj.stack, swiglu(g, u)).to(x.dtype)
+            return out.reshape(*x.shape[:-1], self.down_proj.output_dims)
         idx = _zeros_idx(x2.shape[0], x.device)
         g, u = gate_up(self.gate_proj.stack, self.up_proj.stack, x2, idx, 1)
         out = matvec_glu(self.down_proj.stack, idx, g, u)

@@ -176,9 +176,101 @@ __global__ void combine_kernel(const T* __restrict__ y, const float* __restrict_
     }
 }
 
+// ---------------------------------------------------------------- expert parallelism
+
+// lidx = idx - lo for experts of this rank's range [lo, lo + count), else count (a pair the kernels leave out)
+__global__ void localize_kernel(const uint32_t* __restrict__ idx, int64_t n, uint32_t lo, uint32_t count,
+                                uint32_t* __restrict__ out) {
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
+        const uint32_t e = idx[i];
+        out[i] = (e >= lo && e - lo < count) ? e - lo : count;
+    }
+}
+
+// sums[t, 0:d] = this rank's share of sum_k y_k w_k (pairs of its experts only, MLX's order among them);
+// sums[t, d:2d] = its slice of the shared expert's output (float32), or 0.
+template <typename T>
+__global__ void partial_sum_kernel(const T* __restrict__ y, const float* __restrict__ w, const uint32_t* __restrict__ lidx,
+                                   uint32_t experts, const T* __restrict__ s, int64_t tokens, int k, int64_t d,
+                                   float* __restrict__ sums) {
+    const int64_t t = blockIdx.y;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < d; i += int64_t(gridDim.x) * blockDim.x) {
+        float acc = 0.0f;
+        for (int j = 0; j < 8 && j < k; ++j) {
+            float part = 0.0f;
+            for (int kk = j; kk < k; kk += 8) {
+                if (lidx[t * k + kk] < experts)
+                    part = __fadd_rn(__fmul_rn(to_f32(y[(t * k + kk) * d + i]), w[t * k + kk]), part);
+            }
+            acc = j == 0 ? part : __fadd_rn(part, acc);
+        }
+        sums[t * 2 * d + i] = acc;
+        sums[t * 2 * d + d + i] = s ? to_f32(s[t * d + i]) : 0.0f;
+    }
+}
+
+// The combine from all ranks' summed partials: out = half(routed) + half(half(sigmoid(g)) half(shared)).
+template <typename T>
+__global__ void combine_sums_kernel(const float* __restrict__ sums, const T* __restrict__ g, int64_t tokens, int64_t d,
+                                    T* __restrict__ out) {
+    const int64_t t = blockIdx.y;
+    const T gate = from_f32<T>(1.0f / (1.0f + expf(-to_f32(g[t]))));
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < d; i += int64_t(gridDim.x) * blockDim.x) {
+        const T routed = from_f32<T>(sums[t * 2 * d + i]);
+        const T shared = mul_t<T>(gate, from_f32<T>(sums[t * 2 * d + d + i]));
+        out[t * d + i] = add_t<T>(routed, shared);
+    }
+}
+
 }  // namespace smoe
 
 using namespace smoe;
+
+extern "C" int smoe_localize(const uint32_t* idx, int64_t n, int64_t lo, int64_t count, uint32_t* out, void* stream) {
+    if (n == 0) return SMOE_OK;
+    SMOE_REQUIRE(idx && out && n > 0 && lo >= 0 && count > 0 && lo + count <= 0xffffffffLL, SMOE_EARG,
+                 "localize: bad arguments");
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 1024));
+    localize_kernel<<<grid, 256, 0, as_stream(stream)>>>(idx, n, static_cast<uint32_t>(lo), static_cast<uint32_t>(count), out);
+    return launch_status("localize");
+}
+
+extern "C" int smoe_partial_sums(const void* y, const float* w, const uint32_t* lidx, int64_t experts, const void* s,
+                                 int64_t tokens, int64_t k, int64_t d, float* sums, int dtype, void* stream) {
+    if (tokens == 0) return SMOE_OK;
+    SMOE_REQUIRE(y && w && lidx && sums && tokens > 0 && k > 0 && d > 0 && experts > 0, SMOE_EARG,
+                 "partial_sums: bad arguments");
+    SMOE_REQUIRE(tokens <= 65535, SMOE_ESHAPE, "too many tokens for one call");
+    dim3 grid(static_cast<unsigned>(std::min<int64_t>((d + 255) / 256, 64)), static_cast<unsigned>(tokens));
+    cudaStream_t st = as_stream(stream);
+    if (dtype == SMOE_F16)
+        partial_sum_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(y), w, lidx, static_cast<uint32_t>(experts),
+                                                        static_cast<const __half*>(s), tokens, static_cast<int>(k), d, sums);
+    else if (dtype == SMOE_F32)
+        partial_sum_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(y), w, lidx, static_cast<uint32_t>(experts),
+                                                       static_cast<const float*>(s), tokens, static_cast<int>(k), d, sums);
+    else
+        return fail(SMOE_EDTYPE, "partial_sums takes float16 or float32 activations");
+    return launch_status("partial_sums");
+}
+
+extern "C" int smoe_combine_sums(const float* sums, const void* g, int64_t tokens, int64_t d, void* out, int dtype,
+                                 void* stream) {
+    if (tokens == 0) return SMOE_OK;
+    SMOE_REQUIRE(sums && g && out && tokens > 0 && d > 0, SMOE_EARG, "combine_sums: bad arguments");
+    SMOE_REQUIRE(tokens <= 65535, SMOE_ESHAPE, "too many tokens for one call");
+    dim3 grid(static_cast<unsigned>(std::min<int64_t>((d + 255) / 256, 64)), static_cast<unsigned>(tokens));
+    cudaStream_t st = as_stream(stream);
+    if (dtype == SMOE_F16)
+        combine_sums_kernel<__half><<<grid, 256, 0, st>>>(sums, static_cast<const __half*>(g), tokens, d,
+                                                         static_cast<__half*>(out));
+    else if (dtype == SMOE_F32)
+        combine_sums_kernel<float><<<grid, 256, 0, st>>>(sums, static_cast<const float*>(g), tokens, d,
+                                                        static_cast<float*>(out));
+    else
+        return fail(SMOE_EDTYPE, "combine_sums takes float16 or float32 activations");
+    return launch_status("combine_sums");
+}
 
 extern "C" int smoe_router_logits(const uint16_t* weight, const void* x, int x_dtype, int64_t tokens, int64_t experts,
                                   int64_t hidden, float* logits, void* stream) {

@@ -118,6 +118,22 @@ def test_the_moe_block_is_the_oracles(cuda, tokens, kinds):
     assert rel_l2(got, want) <= 1e-3
 
 
+def test_a_prompt_chunk_through_tiles_and_the_shared_gemm_is_the_oracles(cuda):
+    """Enough pairs for the routed tiles (TILES_FROM) and tokens for the shared expert's tile product."""
+    from strata_mlx_b200 import blocks as Bm
+
+    rng = np.random.default_rng(9)
+    H, F_, E, Fs, k, tokens = 512, 256, 16, 512, 4, 450
+    routed, shared, router, sgate = make_layer(rng, H, F_, E, Fs, ("Q2_K", "Q2_K", "Q2_K"), "Q8_0")
+    block = build_block(routed, shared, router, sgate, k)
+    assert tokens * k >= Bm.TILES_FROM and tokens >= Bm.GEMM_FROM
+    x = rng.standard_normal((tokens, H)).astype(np.float16)
+    got = block(dev(x)).cpu().numpy()
+    logits = block.gate(dev(x)).cpu().numpy()
+    want, idx, w, _ = M.moe_block(x, router, k, routed, shared, sgate, logits=logits)
+    assert rel_l2(got, want) <= 1e-3
+
+
 def test_the_decode_layer_at_baseline_shapes_is_the_oracles(cuda):
     """hidden 4096, 256 experts of IQ3_S (gate/up 1536 x 4096, down 4096 x 1536), top-8,
     shared expert ffn 4096 in Q8_0, batch 1."""
