@@ -48,6 +48,7 @@ def _args():
     p.add_argument("--cpu-steps", type=int, default=2, help="decode steps of the CPU baseline sample")
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     p.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
+    p.add_argument("--only-prefill", action="store_true", help="only the config-3 prefill measurement (profiling)")
     return p.parse_args()
 
 
@@ -478,6 +479,12 @@ def main():
                 "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                                             "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
+        return
+    if args.only_prefill:
+        import torch
+
+        print(json.dumps({"prefill": run_prefill(torch.device("cuda", local_rank), args.seed + 99, steps=args.steps,
+                                                 warmup=args.warmup)}))
         return
     cb = None
     if rank == 0 and world == 1 and not args.no_cpu:

@@ -6,29 +6,44 @@
 // run of up to 8 tiles (128 tokens) of one expert is the N side, so a weight row is decoded once for every
 // token of that expert in the run.
 //
-// Per CTA (persistent over jobs = (run of tiles, block of 128 rows)):
-//   warps 0-7  loaders + decoders: cp.async the raw block bytes of a 256-column stage of the 128 rows and the
-//              run's activations (canonical K-major core-matrix layout, no swizzle) into a double buffer; then
-//              each thread decodes 128 weights of one row (its TMEM lane) and stores them as float16 pairs
-//              into a TMEM A slot (3 slots); after the last stage they read the float32 accumulators back
-//              (tcgen05.ld) and write out.
+// Per CTA (persistent over jobs = (run of tiles, block of 128 rows)), warp-specialized, every hand-off an
+// mbarrier:
+//   warp 9     raw producer: per 256-column stage, the 16-byte aligned cover of each of the 128 rows' block
+//              bytes by tiled TMA over the stack seen as groups of q rows (q = 16 / gcd(row bytes, 16), one
+//              copy per residue class of rows) into a ring of raw slots (rows an odd number of 16-byte chunks
+//              apart).
+//   warp 10    activation producer: the run's rows of the stage by TMA (boxes of 128/64/32/16 rows x 64
+//              columns, 128-byte swizzle) into a ring of activation slots.
+//   warps 0-7  decoders: each thread reads its row's stage from shared memory, decodes 128 weights (half the
+//              stage) to float16 pairs and stores them into its TMEM lane of an A slot (3 slots); after a
+//              job's last stage they read the float32 accumulators back (tcgen05.ld) and write out.
 //   warp 8     one thread issues tcgen05.mma kind::f16 with A from TMEM and B from shared memory, 16 MMAs of
-//              K = 16 per stage, and tcgen05.commit releases the A slot, the activation buffer and, after a
+//              K = 16 per stage, and tcgen05.commit releases the A slot, the activation slot and, after a
 //              job's last stage, the accumulator.
 // Every wait is bounded; a CTA whose wait gives up records SMOE_ETIMEOUT in the workspace status word and
 // leaves its remaining jobs.
+#include <cuda.h>
+
+#include <mutex>
+#include <type_traits>
+
 #include "blocks.cuh"
+#include "gemm_dec.cuh"
 #include "tc05.cuh"
 
 namespace smoe {
 
 constexpr int kGmDecoders = 8;                 // decoder warps
-constexpr int kGmThreads = 32 * (kGmDecoders + 1);
+constexpr int kGmThreads = 32 * (kGmDecoders + 3);  // + the MMA warp and two producer warps
 constexpr int kGmM = 128;                      // weight rows per job
 constexpr int kGmKStage = 256;                 // columns per pipeline stage
 constexpr int kGmMaxTiles = 8;                 // tiles of 16 tokens per job -> N <= 128
 constexpr int kGmMaxN = 16 * kGmMaxTiles;
 constexpr int kGmASlots = 3;
+constexpr int kGmMaxRaw = 4;                   // raw block stage slots in shared memory
+constexpr int kGmMaxB = 3;                     // activation stage slots in shared memory
+constexpr int kGmAtomBytes = kGmMaxN * 128;    // one 64-column K atom of up to 128 activation rows (128-byte swizzle)
+constexpr int kGmBSlotBytes = (kGmKStage / 64) * kGmAtomBytes;
 constexpr uint32_t kGmTmemCols = 512;          // D: [0,128), A slots: 128 + 128 i
 constexpr uint32_t kWaitLimit = 1u << 22;      // polls of try_wait before a wait gives up
 
@@ -142,31 +157,101 @@ struct GemmArgs {
     int stage_bytes;  // raw bytes of one row's 256-column stage
     int rawb;         // smem stride of a row's raw stage (>= stage_bytes + 15, an odd multiple of 16)
     int mblocks;
+    int nb, nr;          // activation and raw stage slots
+    int q;               // rows per 16-byte aligned group of rows (16 / gcd(row_bytes, 16)): raw TMA copies per stage
+    int region_bytes;    // bytes of the raw rows of one residue class (128 / q rows) in a raw slot
 };
 
+// The tensor maps of one launch: the stack's bytes as 32-bit words in groups of q rows, and the activations
+// in boxes of 16, 32, 64 and 128 rows x 64 columns (128-byte swizzle).
+struct alignas(64) GemmMaps {
+    CUtensorMap w;
+    CUtensorMap a[4];
+};
+
+template <class D>
+struct D_lut {
+    static constexpr bool value = D::kLut;
+};
+template <>
+struct D_lut<void> {
+    static constexpr bool value = false;
+};
+
+
 struct GemmSmem {
-    uint64_t afull[kGmASlots], afree[kGmASlots], bfree[2], dfull, dfree, drain;
+    uint64_t rawfull[kGmMaxRaw], rawfree[kGmMaxRaw], bfull[kGmMaxB], bfree[kGmMaxB];
+    uint64_t afull[kGmASlots], afree[kGmASlots], dfull, dfree, drain;
     uint32_t tmem_base;
     int abort;
 };
 
-template <class B>
-__global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    GemmSmem& S = *reinterpret_cast<GemmSmem*>(smem);
-    uint8_t* raw = smem + 128;                                            // 2 x 128 rows x rawb
-    uint8_t* bbuf = raw + 2 * kGmM * g.rawb;                              // 2 x (kGmMaxN x 256) float16
+// Shared memory: [B slots: nb x 64 KB, 1024-aligned][IQ3_S codebook][raw slots: nr x 128 rows x rawb][mc][GemmSmem]
+// (with room for rounding the q residue classes' regions up to 128 bytes and for reads a little past the
+// last row)
+__host__ __device__ constexpr size_t gemm_raw_slot_bytes(int rawb) { return size_t(kGmM) * rawb + 2048; }
+
+// Offset of residue class j's rows in a raw slot. A tiled TMA copy writes to a 128-byte aligned address, so
+// the regions start on 128 bytes; within a class, rows are an odd number of 16-byte chunks apart (8
+// consecutive rows of one class read their 16-byte chunks on 8 different bank groups; rows of different
+// classes may share one when q > 1).
+__host__ __device__ constexpr int raw_region(int j, int region_bytes) { return j * ((region_bytes + 127) & ~127); }
+__host__ __device__ constexpr size_t gemm_smem_bytes(int nb, int nr, int rawb, bool lut) {
+    return size_t(nb) * kGmBSlotBytes + (lut ? 512 * kGmLutRep * 4 : 0) + size_t(nr) * gemm_raw_slot_bytes(rawb) +
+           128 + ((sizeof(GemmSmem) + 127) & ~size_t(127));
+}
+
+template <class D, int H>
+__device__ __forceinline__ void decode_half(const uint8_t* row, int off, uint32_t tbase, const uint32_t* lut,
+                                            const uint32_t* mc) {
+    D::template decode<H>(row, off, tbase, lut, mc);
+}
+
+// B: the block type (run decoder) for the generic path; D: a specialized decoder (gemm_dec.cuh) or void
+template <class B, class D>
+__global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g, const __grid_constant__ GemmMaps maps) {
+    constexpr bool kT = !std::is_void<D>::value;
+    constexpr bool kLut = kT && D_lut<D>::value;
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int nb = g.nb, nr = g.nr;
+    const size_t raw_slot = gemm_raw_slot_bytes(g.rawb);
+    uint8_t* bslots = smem;
+    uint32_t* lut = reinterpret_cast<uint32_t*>(smem + size_t(nb) * kGmBSlotBytes);
+    uint8_t* raw = smem + size_t(nb) * kGmBSlotBytes + (kLut ? 512 * kGmLutRep * 4 : 0);
+    uint32_t* mc = reinterpret_cast<uint32_t*>(raw + size_t(nr) * raw_slot);                     // 16 x (m, c)
+    GemmSmem& S = *reinterpret_cast<GemmSmem*>(reinterpret_cast<uint8_t*>(mc) + 128);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int njobs = g.hdr->count * g.mblocks;
     const int nk = static_cast<int>(g.cols / kGmKStage);
 
+    // the 128-byte swizzle of the TMA writes and of the B descriptors needs 1024-byte aligned slots
+    if (smem_addr(smem) & 1023u) {
+        if (threadIdx.x == 0) atomicExch(g.status, SMOE_EARG);
+        return;
+    }
+    if constexpr (kLut) {
+        for (int i = threadIdx.x; i < 512 * kGmLutRep; i += kGmThreads) lut[i] = __ldg(&kIq3sGrid[i / kGmLutRep]);
+    }
+    if (threadIdx.x < 16) {
+        const float mv = float(1 + 2 * threadIdx.x);
+        const uint32_t mb = __half_as_ushort(__float2half_rn(mv));
+        const uint32_t cb = __half_as_ushort(__float2half_rn(-1024.0f * mv));
+        mc[2 * threadIdx.x] = mb | (mb << 16);
+        mc[2 * threadIdx.x + 1] = cb | (cb << 16);
+    }
     if (threadIdx.x == 0) {
+        for (int i = 0; i < nr; ++i) {
+            tc::mbar_init(&S.rawfull[i], 1);
+            tc::mbar_init(&S.rawfree[i], kGmDecoders);
+        }
+        for (int i = 0; i < nb; ++i) {
+            tc::mbar_init(&S.bfull[i], 1);
+            tc::mbar_init(&S.bfree[i], 1);
+        }
         for (int i = 0; i < kGmASlots; ++i) {
             tc::mbar_init(&S.afull[i], kGmDecoders);
             tc::mbar_init(&S.afree[i], 1);
         }
-        tc::mbar_init(&S.bfree[0], 1);
-        tc::mbar_init(&S.bfree[1], 1);
         tc::mbar_init(&S.dfull, 1);
         tc::mbar_init(&S.dfree, kGmDecoders);
         tc::mbar_init(&S.drain, 1);
@@ -181,126 +266,184 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = S.tmem_base;
+    auto give_up = [&]() {
+        if (lane == 0) {
+            S.abort = 1;
+            atomicExch(g.status, SMOE_ETIMEOUT);
+        }
+    };
+    // every role walks the same sequence of (job, stage); slot i of a ring of n is reused every n stages
+    struct Ring {
+        int slot = 0;
+        uint32_t phase = 0;
+        __device__ void next(int n) {
+            if (++slot == n) {
+                slot = 0;
+                phase ^= 1;
+            }
+        }
+    };
 
-    if (warp == kGmDecoders) {
+    if (warp == kGmDecoders + 1) {
+        // ---------------- raw producer: the 16-byte aligned cover of each row's stage bytes, by TMA over the
+        // stack seen as rows of q rows (a multiple of 16 bytes), one copy per residue class of rows
+        Ring rr;
+        uint32_t gs = 0;
+        bool ok = true;
+        for (int job = blockIdx.x; job < njobs && ok; job += gridDim.x) {
+            const TileRun run = g.runs[job / g.mblocks];
+            const int64_t row0 = int64_t(job % g.mblocks) * kGmM;
+            const int64_t y0 = (int64_t(run.expert) * g.rows + row0) / g.q;
+            for (int s = 0; s < nk; ++s, ++gs, rr.next(nr)) {
+                if (gs >= uint32_t(nr)) {
+                    ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.rawfree[rr.slot], rr.phase ^ 1, kWaitLimit));
+                    if (!ok) break;
+                }
+                // q tiled copies, one per residue class of rows: rows j, j + q, ... of the job's 128
+                if (lane == 0) tc::mbar_arrive_expect_tx(&S.rawfull[rr.slot], static_cast<uint32_t>(kGmM * g.rawb));
+                __syncwarp();
+                if (lane < g.q) {
+                    const int64_t x = ((int64_t(lane) * g.row_bytes + int64_t(s) * g.stage_bytes) & ~int64_t(15)) >> 2;
+                    const uint32_t dst = smem_addr(raw + size_t(rr.slot) * raw_slot + raw_region(lane, g.region_bytes));
+                    if (dst & 127u) atomicExch(g.status, SMOE_EARG);  // a tiled copy's destination is 128-byte aligned
+                    else tc::tma_load_2d(dst, &maps.w, static_cast<int>(x), static_cast<int>(y0), &S.rawfull[rr.slot]);
+                }
+            }
+        }
+        // no bulk copy may still be writing this CTA's shared memory when it exits
+        for (uint32_t i = 0; i < uint32_t(nr) && i < gs; ++i) {
+            const uint32_t st = gs - 1 - i;
+            tc::mbar_wait(&S.rawfull[st % nr], (st / nr) & 1, kWaitLimit);
+        }
+        if (!ok) give_up();
+    } else if (warp == kGmDecoders + 2) {
+        // ---------------- activation producer: the run's rows of the stage's 256 columns by TMA into the
+        // 128-byte swizzle layout (row i of atom q at q * kGmAtomBytes + 128 i)
+        Ring br;
+        uint32_t gs = 0;
+        bool ok = true;
+        for (int job = blockIdx.x; job < njobs && ok; job += gridDim.x) {
+            const TileRun run = g.runs[job / g.mblocks];
+            for (int s = 0; s < nk; ++s, ++gs, br.next(nb)) {
+                if (gs >= uint32_t(nb)) {
+                    ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.bfree[br.slot], br.phase ^ 1, kWaitLimit));
+                    if (!ok) break;
+                }
+                if (lane == 0) {
+                    const uint32_t bdst = smem_addr(bslots + size_t(br.slot) * kGmBSlotBytes);
+                    tc::mbar_arrive_expect_tx(&S.bfull[br.slot], static_cast<uint32_t>(run.tiles) * 16u * kGmKStage * 2u);
+                    // the run's tiles as boxes of 128, 64, 32 and 16 rows (its bits), for each 64-column atom
+                    int done = 0;
+                    for (int b = 3; b >= 0; --b) {
+                        if (!((run.tiles >> b) & 1)) continue;
+                        for (int q = 0; q < kGmKStage / 64; ++q)
+                            tc::tma_load_2d(bdst + q * kGmAtomBytes + done * 128, &maps.a[b], s * kGmKStage + 64 * q,
+                                            run.first_tile * 16 + done, &S.bfull[br.slot]);
+                        done += 16 << b;
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        for (uint32_t i = 0; i < uint32_t(nb) && i < gs; ++i) {
+            const uint32_t st = gs - 1 - i;
+            tc::mbar_wait(&S.bfull[st % nb], (st / nb) & 1, kWaitLimit);
+        }
+        if (!ok) give_up();
+    } else if (warp == kGmDecoders) {
         // ---------------- MMA issuer (lane 0 issues; the warp waits together and agrees on every outcome)
-        uint32_t gstage = 0, jobs = 0;
+        Ring br;
+        uint32_t gs = 0, jobs = 0;
         bool ok = true;
         for (int job = blockIdx.x; job < njobs && ok; job += gridDim.x, ++jobs) {
             const TileRun run = g.runs[job / g.mblocks];
-            const int n = 16 * run.tiles;
-            const uint32_t idesc = tc::idesc_f16_f32(kGmM, n);
-            const uint32_t lbo = static_cast<uint32_t>(n) * 16u;
+            const uint32_t idesc = tc::idesc_f16_f32(kGmM, 16 * run.tiles);
             if (jobs > 0) ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.dfree, (jobs - 1) & 1, kWaitLimit));
             if (!ok) break;
             tc::fence_after_sync();
-            for (int s = 0; s < nk; ++s, ++gstage) {
-                const uint32_t as = gstage % kGmASlots, bs = gstage & 1;
-                ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.afull[as], (gstage / kGmASlots) & 1, kWaitLimit));
+            for (int s = 0; s < nk; ++s, ++gs, br.next(nb)) {
+                const uint32_t as = gs % kGmASlots;
+                ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.afull[as], (gs / kGmASlots) & 1, kWaitLimit) &&
+                                                 tc::mbar_wait(&S.bfull[br.slot], br.phase, kWaitLimit));
                 if (!ok) break;
                 tc::fence_after_sync();
                 if (lane == 0) {
-                    const uint32_t bbase = static_cast<uint32_t>(__cvta_generic_to_shared(bbuf + bs * (kGmMaxN * 512)));
-#pragma unroll 4
-                    for (int j = 0; j < kGmKStage / 16; ++j) {
-                        const uint64_t bd = tc::smem_desc(bbase + 2u * j * lbo, lbo, 128);
-                        tc::mma_f16_ts(tmem, tmem + 128u + 128u * as + 8u * j, bd, idesc, (s > 0 || j > 0) ? 1u : 0u);
+                    const uint32_t bbase = smem_addr(bslots + size_t(br.slot) * kGmBSlotBytes);
+#pragma unroll
+                    for (int k = 0; k < kGmKStage / 16; ++k) {
+                        const uint64_t bd = tc::smem_desc_sw128(bbase + (k >> 2) * kGmAtomBytes + (k & 3) * 32);
+                        tc::mma_f16_ts(tmem, tmem + 128u + 128u * as + 8u * k, bd, idesc, (s > 0 || k > 0) ? 1u : 0u);
                     }
                     tc::mma_commit(&S.afree[as]);
-                    tc::mma_commit(&S.bfree[bs]);
+                    tc::mma_commit(&S.bfree[br.slot]);
                     if (s == nk - 1) tc::mma_commit(&S.dfull);
                 }
                 __syncwarp();
             }
         }
-        if (!ok && lane == 0) {
-            S.abort = 1;
-            atomicExch(g.status, SMOE_ETIMEOUT);
-        }
+        if (!ok) give_up();
     } else {
-        // ---------------- loaders, decoders, epilogue (256 threads). Every wait's outcome is and-reduced over
-        // the 256 threads by the named barrier that follows it, so they leave a job together or not at all.
-        const int t = threadIdx.x;             // 0..255
+        // ---------------- decoders and epilogue (8 warps, each on its own: warp w decodes the 128 weights
+        // [128 h, 128 h + 128) of each stage for rows 32 (w % 4) .. + 31, h = w / 4)
         const int m = 32 * (warp & 3) + lane;  // TMEM lane = weight row within the block
-        const int h = warp >> 2;               // which 128 columns of a stage this thread decodes
-        uint32_t gstage = 0, jobs = 0;
+        const int h = warp >> 2;
+        const uint32_t* lut_lane = lut + (lane % kGmLutRep);
+        Ring rr;
+        uint32_t gs = 0, jobs = 0;
         bool ok = true;
         for (int job = blockIdx.x; job < njobs && ok; job += gridDim.x, ++jobs) {
-            const int ri = job / g.mblocks, mb = job % g.mblocks;
-            const TileRun run = g.runs[ri];
-            const int n = 16 * run.tiles;
-            const int64_t row0 = int64_t(mb) * kGmM;
+            const TileRun run = g.runs[job / g.mblocks];
+            const int64_t row0 = int64_t(job % g.mblocks) * kGmM;
             const int mrows = static_cast<int>(min(int64_t(kGmM), g.rows - row0));
-            const uint8_t* wbase = g.blocks + (int64_t(run.expert) * g.rows + row0) * g.row_bytes;
-            const __half* abase = g.a + int64_t(run.first_tile) * 16 * g.cols;
-
-            auto issue = [&](uint32_t gs, int s) {
-                const int slot = gs & 1;
-                uint8_t* rdst = raw + slot * (kGmM * g.rawb);
-                // raw bytes: the 16-byte chunks covering each row's stage
-                for (int r = t >> 3; r < mrows; r += 32) {
-                    const uint8_t* src = wbase + r * g.row_bytes + int64_t(s) * g.stage_bytes;
-                    stage_bytes(rdst + r * g.rawb, src, g.stage_bytes, g.end, t & 7, 8);
-                }
-                // activations: n rows x 256 columns -> chunk (row i, k-chunk c) at c * (n * 16) + i * 16
-                uint8_t* bdst = bbuf + slot * (kGmMaxN * 512);
-                for (int q = t; q < n * 32; q += 256) {
-                    const int i = q >> 5, c = q & 31;
-                    cp_async16(bdst + c * (n * 16) + i * 16, abase + int64_t(i) * g.cols + int64_t(s) * kGmKStage + 8 * c, 16);
-                }
-            };
-            auto wait_bfree = [&](uint32_t gs) -> bool {
-                return gs < 2 || tc::mbar_wait(&S.bfree[gs & 1], ((gs - 2) >> 1) & 1, kWaitLimit);
-            };
-
-            ok = tc::bar_and(1, 256, wait_bfree(gstage));
-            if (!ok) break;
-            issue(gstage, 0);
-            cp_async_commit();
-            for (int s = 0; s < nk; ++s, ++gstage) {
-                // (this barrier also means everyone is done decoding the stage whose buffers are refilled next)
-                const bool more = s + 1 < nk;
-                ok = tc::bar_and(1, 256, more ? wait_bfree(gstage + 1) : true);
-                if (!ok) break;
-                if (more) issue(gstage + 1, s + 1);
-                cp_async_commit();
-                cp_async_wait<1>();
-                tc::fence_proxy_async_smem();
-                const uint32_t as = gstage % kGmASlots;
-                ok = tc::bar_and(1, 256, gstage < kGmASlots ||
-                                             tc::mbar_wait(&S.afree[as], ((gstage - kGmASlots) / kGmASlots) & 1, kWaitLimit));
+            const uint8_t* wrow = g.blocks + ((int64_t(run.expert) * g.rows + row0) + m) * g.row_bytes;
+            const int row_off = raw_region(m % g.q, g.region_bytes) + (m / g.q) * g.rawb;
+            for (int s = 0; s < nk; ++s, ++gs, rr.next(nr)) {
+                const uint32_t as = gs % kGmASlots;
+                ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.rawfull[rr.slot], rr.phase, kWaitLimit) &&
+                                                 (gs < kGmASlots ||
+                                                  tc::mbar_wait(&S.afree[as], ((gs - kGmASlots) / kGmASlots) & 1, kWaitLimit)));
                 if (!ok) break;
                 tc::fence_after_sync();
-                // decode 4 runs (128 weights) of row m into TMEM lane m, columns 128 + 128 as + 64 h + 16 i
-                const uint8_t* rsrc = raw + (gstage & 1) * (kGmM * g.rawb) + m * g.rawb;
-                const int off = static_cast<int>((reinterpret_cast<uintptr_t>(wbase + int64_t(m) * g.row_bytes +
-                                                                              int64_t(s) * g.stage_bytes)) & 15);
+                // decode 128 weights of row m into TMEM lane m, columns 128 + 128 as + 64 h (+ 16 per 32 weights)
                 const uint32_t tbase = tmem + (uint32_t(32 * (warp & 3)) << 16) + 128u + 128u * as + 64u * h;
-#pragma unroll 1
-                for (int i = 0; i < 4; ++i) {
-                    uint32_t v[16];
-                    if (m < mrows) {
-                        float w[32];
-                        B::run(rsrc + off, 4 * h + i, w);
-#pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = tc::pack_half2(w[2 * j], w[2 * j + 1]);
+                const int off = static_cast<int>(reinterpret_cast<uintptr_t>(wrow + int64_t(s) * g.stage_bytes) & 15);
+                const uint8_t* rrow = raw + size_t(rr.slot) * raw_slot + row_off;
+                if (m < mrows) {
+                    if constexpr (kT) {
+                        if (h == 0) decode_half<D, 0>(rrow, off, tbase, lut_lane, mc);
+                        else decode_half<D, 1>(rrow, off, tbase, lut_lane, mc);
                     } else {
+#pragma unroll 1
+                        for (int i = 0; i < 4; ++i) {
+                            float w[32];
+                            B::run(rrow + off, 4 * h + i, w);
+                            uint32_t v[16];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) v[j] = 0u;
+                            for (int j = 0; j < 16; ++j) v[j] = tc::pack_half2(w[2 * j], w[2 * j + 1]);
+                            tc::tmem_st16(tbase + 16u * i, v);
+                        }
                     }
-                    tc::tmem_st16(tbase + 16u * i, v);
+                } else {
+                    uint32_t v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) v[j] = 0u;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) tc::tmem_st16(tbase + 16u * i, v);
                 }
                 tc::tmem_wait_st();
                 tc::fence_before_sync();
                 __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&S.afull[as]);
+                if (lane == 0) {
+                    tc::mbar_arrive(&S.afull[as]);
+                    tc::mbar_arrive(&S.rawfree[rr.slot]);
+                }
             }
             if (!ok) break;
-            // epilogue: accumulators of rows m, tokens [n/2 * h, n/2 * (h+1))
-            ok = tc::bar_and(1, 256, tc::mbar_wait(&S.dfull, jobs & 1, kWaitLimit));
+            // epilogue: accumulators of rows m, tokens [n/2 h, n/2 (h + 1))
+            ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.dfull, jobs & 1, kWaitLimit));
             if (!ok) break;
             tc::fence_after_sync();
-            const int half_n = n >> 1;
+            const int half_n = 8 * run.tiles;
             float* obase = g.out + int64_t(run.first_tile) * 16 * g.rows + row0 + m;
             for (int c0 = h * half_n; c0 < (h + 1) * half_n; c0 += 8) {
                 uint32_t v[8];
@@ -315,11 +458,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&S.dfree);
         }
-        cp_async_wait<0>();
-        if (!ok && t == 0) {
-            S.abort = 1;
-            atomicExch(g.status, SMOE_ETIMEOUT);
-        }
+        if (!ok) give_up();
     }
     tc::fence_before_sync();
     __syncthreads();
@@ -401,6 +540,55 @@ extern "C" size_t smoe_tile_matmul_workspace_size(int64_t p16) {
 }
 
 static int g_num_sms = 0;
+constexpr int kGmSmemLimit = 227 * 1024;  // opt-in dynamic shared memory per block on sm_100
+
+// The launch's tensor maps (GemmMaps). cuTensorMapEncodeTiled is reached through the runtime's driver entry
+// point (no link against libcuda).
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encoder() {
+    static std::once_flag once;
+    static EncodeTiledFn encode = nullptr;
+    std::call_once(once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            encode = reinterpret_cast<EncodeTiledFn>(fn);
+    });
+    return encode;
+}
+
+static int encode_maps(GemmMaps* maps, const uint8_t* blocks, int64_t total_rows, int64_t row_bytes, int q, int rawb,
+                       const void* a, int64_t p16, int64_t cols) {
+    EncodeTiledFn encode = encoder();
+    if (!encode) return fail(SMOE_EARG, "tile_matmul: cuTensorMapEncodeTiled is not available");
+    const cuuint32_t estr[2] = {1, 1};
+    {
+        // the stack as [total_rows / q][q * row_bytes / 4] words; a box is 128 / q groups x the stage's cover
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(q * row_bytes / 4), static_cast<cuuint64_t>(total_rows / q)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(q * row_bytes)};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(rawb / 4), static_cast<cuuint32_t>(kGmM / q)};
+        const CUresult r = encode(&maps->w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(blocks), dims,
+                                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(SMOE_EARG, "tile_matmul: block tensor map rejected (" + std::to_string(int(r)) + ")");
+    }
+    for (int b = 0; b < 4; ++b) {
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(p16)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
+        const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(16 << b)};
+        const CUresult r = encode(&maps->a[b], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a), dims, strides,
+                                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (r != CUDA_SUCCESS)
+            return fail(SMOE_EARG, "tile_matmul: activation tensor map rejected (" + std::to_string(int(r)) + ")");
+    }
+    return SMOE_OK;
+}
 
 extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
                                 const void* a, int a_dtype, int64_t p16, const uint32_t* tile_expert, float* out,
@@ -412,6 +600,7 @@ extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts
     SMOE_REQUIRE(blocks && a && tile_expert && out && p16 > 0 && experts > 0, SMOE_EARG, "null pointer or empty stack");
     SMOE_REQUIRE(p16 % 16 == 0, SMOE_ESHAPE, "a's rows must be a multiple of 16");
     SMOE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0, SMOE_EARG, "a must be 16-byte aligned");
+    SMOE_REQUIRE((reinterpret_cast<uintptr_t>(blocks) & 15) == 0, SMOE_EARG, "blocks must be 16-byte aligned");
     cudaStream_t st = as_stream(stream);
     const int64_t ntiles = p16 / 16;
     const int64_t row_bytes = cols / per * bytes;
@@ -434,6 +623,24 @@ extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts
         if ((rawb / 16) % 2 == 0) rawb += 16;  // an odd number of 16-byte chunks: rows fall on different banks
         g.rawb = rawb;
         g.mblocks = static_cast<int>((rows + kGmM - 1) / kGmM);
+        const bool lut = kind == GdIQ3S::kKind;
+        // the most raw slots (latency of the weights' DRAM reads), then the most activation slots that fit
+        g.nr = kGmMaxRaw;
+        g.nb = 0;
+        for (int nb = kGmMaxB; nb >= 2 && !g.nb; --nb)
+            if (gemm_smem_bytes(nb, g.nr, rawb, lut) <= size_t(kGmSmemLimit)) g.nb = nb;
+        while (!g.nb && g.nr > 2) {
+            --g.nr;
+            if (gemm_smem_bytes(2, g.nr, rawb, lut) <= size_t(kGmSmemLimit)) g.nb = 2;
+        }
+        SMOE_REQUIRE(g.nb, SMOE_EKIND, "tile_matmul: stage does not fit in shared memory");
+        const size_t smem = gemm_smem_bytes(g.nb, g.nr, rawb, lut);
+        int gcd = 16;
+        while (row_bytes % gcd) gcd >>= 1;
+        g.q = 16 / gcd;
+        g.region_bytes = (kGmM / g.q) * rawb;
+        GemmMaps maps;
+        if (int e = encode_maps(&maps, blocks, experts * rows, row_bytes, g.q, rawb, a, p16, cols)) return e;
         gemm_plan_kernel<<<1, 1024, 0, st>>>(tile_expert, ntiles, experts, static_cast<GemmPlanHeader*>(workspace),
                                              const_cast<TileRun*>(g.runs));
         if (int s = launch_status("tile_matmul plan")) return s;
@@ -445,13 +652,16 @@ extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts
         }
         const int64_t max_jobs = ntiles * g.mblocks;
         const unsigned grid = static_cast<unsigned>(std::min<int64_t>(max_jobs, g_num_sms));
-        const size_t smem = 128 + size_t(2) * kGmM * rawb + size_t(2) * kGmMaxN * 512;
-        int status = dispatch_kind(kind, [&](auto blk) {
-            using B = decltype(blk);
-            max_smem(gemm_tc_kernel<B>, static_cast<int>(smem));
-            gemm_tc_kernel<B><<<grid, kGmThreads, smem, st>>>(g);
-        });
-        if (status) return fail(status, "block type has no decoder");
+        int status = SMOE_OK;
+        auto launch = [&](auto kern) {
+            if (int e = max_smem(kern, static_cast<int>(smem))) status = fail(e, "tile_matmul: shared memory limit");
+            else kern<<<grid, kGmThreads, smem, st>>>(g, maps);
+        };
+        if (kind == GdQ2K::kKind) launch(gemm_tc_kernel<Q2_K, GdQ2K>);
+        else if (kind == GdIQ3S::kKind) launch(gemm_tc_kernel<IQ3_S, GdIQ3S>);
+        else if (kind == GdQ8_0::kKind) launch(gemm_tc_kernel<Q8_0, GdQ8_0>);
+        else status = dispatch_kind(kind, [&](auto blk) { launch(gemm_tc_kernel<decltype(blk), void>); });
+        if (status) return status;
         return launch_status("tile_matmul");
     }
     SMOE_REQUIRE(a_dtype == SMOE_F16 || a_dtype == SMOE_F32, SMOE_EDTYPE, "a must be float16 or float32");

@@ -40,6 +40,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
     return false;
 }
 
+// Arrive once on `bar` and raise its expected transaction count by `bytes` (bulk copies complete against it).
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(bar))),
+                 "r"(bytes)
+                 : "memory");
+}
+
+// Arrive once on `bar` when every cp.async this thread issued before has landed (counted in the init count).
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+                 : "memory");
+}
+
+// 2-D tiled TMA load of this GPU's global memory into this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst_smem, const void* tmap, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+            dst_smem),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y),
+        "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+        : "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
 }
@@ -136,6 +161,15 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n) {
 __device__ __forceinline__ uint64_t smem_desc(uint32_t smem_addr, uint32_t lbo, uint32_t sbo) {
     return uint64_t((smem_addr >> 4) & 0x3fff) | (uint64_t((lbo >> 4) & 0x3fff) << 16) |
            (uint64_t((sbo >> 4) & 0x3fff) << 32) | (uint64_t(1) << 46);
+}
+
+// Shared-memory descriptor of a K-major operand in the 128-byte swizzle layout that TMA writes with
+// CU_TENSOR_MAP_SWIZZLE_128B: rows of 128 bytes (64 float16 of K), 8-row groups 1024 bytes apart, the atom
+// 1024-byte aligned; a K step of 16 inside the atom advances the start address by 32 bytes. Version 1,
+// layout type 2 (128-byte swizzle), leading byte offset unused (1).
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
+    return uint64_t((smem_addr >> 4) & 0x3fff) | (uint64_t(1) << 16) | (uint64_t(1024 >> 4) << 32) |
+           (uint64_t(1) << 46) | (uint64_t(2) << 61);
 }
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
