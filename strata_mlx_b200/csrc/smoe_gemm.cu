@@ -8,16 +8,16 @@
 //
 // Per CTA (persistent over jobs = (run of tiles, block of 128 rows)), warp-specialized, every hand-off an
 // mbarrier:
-//   warp 9     raw producer: per 256-column stage, the 16-byte aligned cover of each of the 128 rows' block
+//   warp 17    raw producer: per 256-column stage, the 16-byte aligned cover of each of the 128 rows' block
 //              bytes by tiled TMA over the stack seen as groups of q rows (q = 16 / gcd(row bytes, 16), one
 //              copy per residue class of rows) into a ring of raw slots (rows an odd number of 16-byte chunks
 //              apart).
-//   warp 10    activation producer: the run's rows of the stage by TMA (boxes of 128/64/32/16 rows x 64
+//   warp 18    activation producer: the run's rows of the stage by TMA (boxes of 128/64/32/16 rows x 64
 //              columns, 128-byte swizzle) into a ring of activation slots.
-//   warps 0-7  decoders: each thread reads its row's stage from shared memory, decodes 128 weights (half the
-//              stage) to float16 pairs and stores them into its TMEM lane of an A slot (3 slots); after a
-//              job's last stage they read the float32 accumulators back (tcgen05.ld) and write out.
-//   warp 8     one thread issues tcgen05.mma kind::f16 with A from TMEM and B from shared memory, 16 MMAs of
+//   warps 0-15 decoders: each thread reads its row's stage from shared memory, decodes 64 weights (a quarter
+//              of the stage) to float16 pairs and stores them into its TMEM lane of an A slot (3 slots); after
+//              a job's last stage they read the float32 accumulators back (tcgen05.ld) and write out.
+//   warp 16    one thread issues tcgen05.mma kind::f16 with A from TMEM and B from shared memory, 16 MMAs of
 //              K = 16 per stage, and tcgen05.commit releases the A slot, the activation slot and, after a
 //              job's last stage, the accumulator.
 // Every wait is bounded; a CTA whose wait gives up records SMOE_ETIMEOUT in the workspace status word and
@@ -26,6 +26,7 @@
 
 #include <mutex>
 #include <type_traits>
+#include <utility>
 
 #include "blocks.cuh"
 #include "gemm_dec.cuh"
@@ -33,7 +34,7 @@
 
 namespace smoe {
 
-constexpr int kGmDecoders = 8;                 // decoder warps
+constexpr int kGmDecoders = 16;                // decoder warps: 4 per TMEM lane quarter, each a quarter of a stage
 constexpr int kGmThreads = 32 * (kGmDecoders + 3);  // + the MMA warp and two producer warps
 constexpr int kGmM = 128;                      // weight rows per job
 constexpr int kGmKStage = 256;                 // columns per pipeline stage
@@ -201,10 +202,23 @@ __host__ __device__ constexpr size_t gemm_smem_bytes(int nb, int nr, int rawb, b
            128 + ((sizeof(GemmSmem) + 127) & ~size_t(127));
 }
 
-template <class D, int H>
-__device__ __forceinline__ void decode_half(const uint8_t* row, int off, uint32_t tbase, const uint32_t* lut,
+// Decode quarter Q of a stage of the row staged at `row`, whose bytes start `off` bytes into it (a multiple of
+// the type's offset step): false if `off` is none the type can have.
+template <class D, int Q>
+__device__ __forceinline__ bool decode_part(int off, const uint8_t* row, uint32_t (&out)[32], const uint32_t* lut,
                                             const uint32_t* mc) {
-    D::template decode<H>(row, off, tbase, lut, mc);
+    const uint32_t* base = reinterpret_cast<const uint32_t*>(row + (off & ~3));
+    if ((off & 3) == 0) {
+        D::template decode<Q, 0>(BlockWords<0>{base}, out, lut, mc);
+        return true;
+    }
+    if constexpr (D::kOffStep == 2) {
+        if ((off & 3) == 2) {
+            D::template decode<Q, 2>(BlockWords<2>{base}, out, lut, mc);
+            return true;
+        }
+    }
+    return false;
 }
 
 // B: the block type (run decoder) for the generic path; D: a specialized decoder (gemm_dec.cuh) or void
@@ -351,7 +365,8 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
         }
         if (!ok) give_up();
     } else if (warp == kGmDecoders) {
-        // ---------------- MMA issuer (lane 0 issues; the warp waits together and agrees on every outcome)
+        // ---------------- MMA issuer (the converged warp issues, one elected lane; it waits together and agrees on
+        // every outcome)
         Ring br;
         uint32_t gs = 0, jobs = 0;
         bool ok = true;
@@ -367,26 +382,30 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
                                                  tc::mbar_wait(&S.bfull[br.slot], br.phase, kWaitLimit));
                 if (!ok) break;
                 tc::fence_after_sync();
-                if (lane == 0) {
-                    const uint32_t bbase = smem_addr(bslots + size_t(br.slot) * kGmBSlotBytes);
+                const uint64_t bd0 = tc::smem_desc_sw128(smem_addr(bslots + size_t(br.slot) * kGmBSlotBytes));
 #pragma unroll
-                    for (int k = 0; k < kGmKStage / 16; ++k) {
-                        const uint64_t bd = tc::smem_desc_sw128(bbase + (k >> 2) * kGmAtomBytes + (k & 3) * 32);
-                        tc::mma_f16_ts(tmem, tmem + 128u + 128u * as + 8u * k, bd, idesc, (s > 0 || k > 0) ? 1u : 0u);
-                    }
-                    tc::mma_commit(&S.afree[as]);
-                    tc::mma_commit(&S.bfree[br.slot]);
-                    if (s == nk - 1) tc::mma_commit(&S.dfull);
-                }
+                for (int k = 0; k < kGmKStage / 16; ++k)
+                    tc::mma_f16_ts_warp(tmem, tmem + 128u + 128u * as + 8u * k,
+                                        bd0 + uint64_t(((k >> 2) * kGmAtomBytes + (k & 3) * 32) >> 4), idesc,
+                                        (s > 0 || k > 0) ? 1u : 0u);
+                tc::mma_commit_warp(&S.afree[as]);
+                tc::mma_commit_warp(&S.bfree[br.slot]);
+                if (s == nk - 1) tc::mma_commit_warp(&S.dfull);
                 __syncwarp();
             }
         }
         if (!ok) give_up();
     } else {
-        // ---------------- decoders and epilogue (8 warps, each on its own: warp w decodes the 128 weights
-        // [128 h, 128 h + 128) of each stage for rows 32 (w % 4) .. + 31, h = w / 4)
-        const int m = 32 * (warp & 3) + lane;  // TMEM lane = weight row within the block
-        const int h = warp >> 2;
+        // ---------------- decoders and epilogue (16 warps, each on its own: warp w decodes the 64 weights
+        // [64 qq, 64 qq + 64) of each stage for TMEM lanes 32 (w % 4) .. + 31, qq = w / 4). TMEM lane L holds
+        // weight row m = q (L % (128 / q)) + L / (128 / q) of the block: the rows of one residue class mod q
+        // are 128 / q consecutive lanes, so (for q <= 4) a warp's rows share their byte offset in the stage
+        // and read consecutive rows of one region of the raw slot.
+        const int L = 32 * (warp & 3) + lane;
+        const int per_class = kGmM / g.q;
+        const int m = g.q * (L % per_class) + L / per_class;
+        const int row_off = raw_region(L / per_class, g.region_bytes) + (L % per_class) * g.rawb;
+        const int qq = warp >> 2;              // which 64 columns of a stage this warp decodes
         const uint32_t* lut_lane = lut + (lane % kGmLutRep);
         Ring rr;
         uint32_t gs = 0, jobs = 0;
@@ -396,7 +415,6 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
             const int64_t row0 = int64_t(job % g.mblocks) * kGmM;
             const int mrows = static_cast<int>(min(int64_t(kGmM), g.rows - row0));
             const uint8_t* wrow = g.blocks + ((int64_t(run.expert) * g.rows + row0) + m) * g.row_bytes;
-            const int row_off = raw_region(m % g.q, g.region_bytes) + (m / g.q) * g.rawb;
             for (int s = 0; s < nk; ++s, ++gs, rr.next(nr)) {
                 const uint32_t as = gs % kGmASlots;
                 ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.rawfull[rr.slot], rr.phase, kWaitLimit) &&
@@ -404,31 +422,37 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
                                                   tc::mbar_wait(&S.afree[as], ((gs - kGmASlots) / kGmASlots) & 1, kWaitLimit)));
                 if (!ok) break;
                 tc::fence_after_sync();
-                // decode 128 weights of row m into TMEM lane m, columns 128 + 128 as + 64 h (+ 16 per 32 weights)
-                const uint32_t tbase = tmem + (uint32_t(32 * (warp & 3)) << 16) + 128u + 128u * as + 64u * h;
+                // decode 64 weights of row m into TMEM lane L, columns 128 + 128 as + 32 qq (+ 16 per 32 weights)
+                const uint32_t tbase = tmem + (uint32_t(32 * (warp & 3)) << 16) + 128u + 128u * as + 32u * qq;
                 const int off = static_cast<int>(reinterpret_cast<uintptr_t>(wrow + int64_t(s) * g.stage_bytes) & 15);
                 const uint8_t* rrow = raw + size_t(rr.slot) * raw_slot + row_off;
-                if (m < mrows) {
-                    if constexpr (kT) {
-                        if (h == 0) decode_half<D, 0>(rrow, off, tbase, lut_lane, mc);
-                        else decode_half<D, 1>(rrow, off, tbase, lut_lane, mc);
-                    } else {
-#pragma unroll 1
-                        for (int i = 0; i < 4; ++i) {
-                            float w[32];
-                            B::run(rrow + off, 4 * h + i, w);
-                            uint32_t v[16];
-#pragma unroll
-                            for (int j = 0; j < 16; ++j) v[j] = tc::pack_half2(w[2 * j], w[2 * j + 1]);
-                            tc::tmem_st16(tbase + 16u * i, v);
-                        }
+                // every lane decodes (rows past the block's end decode bytes that were staged all the same and
+                // only reach accumulator rows the epilogue does not write); the warp converges before the
+                // .sync.aligned TMEM stores
+                if constexpr (kT) {
+                    uint32_t v[32];
+                    bool done;
+                    switch (qq) {
+                        case 0: done = decode_part<D, 0>(off, rrow, v, lut_lane, mc); break;
+                        case 1: done = decode_part<D, 1>(off, rrow, v, lut_lane, mc); break;
+                        case 2: done = decode_part<D, 2>(off, rrow, v, lut_lane, mc); break;
+                        default: done = decode_part<D, 3>(off, rrow, v, lut_lane, mc); break;
                     }
+                    if (!done) atomicExch(g.status, SMOE_EARG);  // an offset the block type cannot have
+                    __syncwarp();
+                    tc::tmem_st16(tbase, *reinterpret_cast<const uint32_t(*)[16]>(v));
+                    tc::tmem_st16(tbase + 16u, *reinterpret_cast<const uint32_t(*)[16]>(v + 16));
                 } else {
-                    uint32_t v[16];
+#pragma unroll 1
+                    for (int i = 0; i < 2; ++i) {
+                        float w[32];
+                        B::run(rrow + off, 2 * qq + i, w);
+                        uint32_t v[16];
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) v[j] = 0u;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) tc::tmem_st16(tbase + 16u * i, v);
+                        for (int j = 0; j < 16; ++j) v[j] = tc::pack_half2(w[2 * j], w[2 * j + 1]);
+                        __syncwarp();
+                        tc::tmem_st16(tbase + 16u * i, v);
+                    }
                 }
                 tc::tmem_wait_st();
                 tc::fence_before_sync();
@@ -439,13 +463,12 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
                 }
             }
             if (!ok) break;
-            // epilogue: accumulators of rows m, tokens [n/2 h, n/2 (h + 1))
+            // epilogue: accumulators of rows m, tokens 8 qq + 32 i .. + 7
             ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.dfull, jobs & 1, kWaitLimit));
             if (!ok) break;
             tc::fence_after_sync();
-            const int half_n = 8 * run.tiles;
             float* obase = g.out + int64_t(run.first_tile) * 16 * g.rows + row0 + m;
-            for (int c0 = h * half_n; c0 < (h + 1) * half_n; c0 += 8) {
+            for (int c0 = 8 * qq; c0 < 16 * run.tiles; c0 += 32) {
                 uint32_t v[8];
                 tc::tmem_ld8(tmem + (uint32_t(32 * (warp & 3)) << 16) + uint32_t(c0), v);
                 tc::tmem_wait_ld();
@@ -466,7 +489,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
     if (warp == kGmDecoders) {
         if (S.abort) {
             // let any MMA still in flight finish before the TMEM it writes is released (bounded wait)
-            if (lane == 0) tc::mma_commit(&S.drain);
+            tc::mma_commit_warp(&S.drain);
             __syncwarp();
             tc::mbar_wait(&S.drain, 0, kWaitLimit);
         }

@@ -32,11 +32,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for the phase of `parity` to complete, at most `limit` polls (each poll itself waits a bounded,
-// hardware-defined time). Returns false when it gave up.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+constexpr uint64_t kWaitNs = 1000000000ull;  // a wait gives up after one second
+
+// try_wait that may suspend the thread until the phase completes, for at most `hint_ns`
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar))), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for the phase of `parity` to complete, at most `limit` polls (each suspends the thread until the phase
+// completes or 1 ms passes) and at most kWaitNs in all. Returns false when it gave up.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t limit) {
-    for (uint32_t i = 0; i < limit; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 0; i < limit; ++i) {
+        if (mbar_try_wait_hint(bar, parity, 1000000u)) return true;
+        if (globaltimer_ns() - t0 > kWaitNs) return false;
+    }
     return false;
 }
 
@@ -139,11 +164,34 @@ __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uin
         : "memory");
 }
 
+// The same, called by a whole converged warp: one elected lane issues. A warp-uniform issue keeps the MMA
+// operands in the uniform datapath, which sustains one MMA per tensor-pipe slot (a branch on one lane does not).
+__device__ __forceinline__ void mma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p, e;\n\t.reg .b32 r;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive once on `bar` when every MMA this thread issued before has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
                      static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
                  : "memory");
+}
+
+// The same, called by the whole converged warp that issued with mma_f16_ts_warp (the same lane is elected).
+__device__ __forceinline__ void mma_commit_warp(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .pred e;\n\t.reg .b32 r;\n\t"
+        "elect.sync r|e, 0xffffffff;\n\t"
+        "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(
+            static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+        : "memory");
 }
 
 // Instruction descriptor, kind::f16: D float32, A and B float16, both K-major, M x N.
