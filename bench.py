@@ -451,7 +451,7 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": launches * args.steps,
         "e2e": {"value": args.steps / (e2e_ms * 1e-3), "unit": "token-layers/s",
                 "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
-        "roofline": {"kernel": "mv_mma_kernel<MmIQ3S> (routed gate+up, 16 x 1536 x 4096 IQ3_S)", "bound": "hbm",
+        "roofline": {"kernel": "mv8_kernel<M8IQ3S> (routed gate+up, 16 x 1536 x 4096 IQ3_S)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None, "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu,

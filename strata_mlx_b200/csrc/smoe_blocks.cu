@@ -141,7 +141,11 @@ __global__ void swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u, 
 
 // ---------------------------------------------------------------- host side
 
-// the tensor-core decode matvec (smoe_mv.cu): 0 launched, 1 not taken, else an error status
+// the int8 tensor-core decode matvec (smoe_mv8.cu): 0 launched, 1 not taken, else an error status
+int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
+            int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, __half* o0,
+            __half* o1, int nprob, cudaStream_t st);
+// the float16 tensor-core decode matvec (smoe_mv.cu), for what the int8 one does not take
 int mv_mma_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
                int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, __half* o0,
                __half* o1, int nprob, cudaStream_t st);
@@ -206,6 +210,9 @@ static int matvec_common(int kind0, const uint8_t* b0, int kind1, const uint8_t*
     a.share = share;
     if constexpr (sizeof(T) == 2) {
         if (gate == nullptr) {
+            const int r8 = mv8_try(kind0, kind1, b0, a.blocks[1], experts, rows, cols, a.row_bytes, idx, pairs, share,
+                                   static_cast<const __half*>(x), a.out[0], a.out[1], nprob, st);
+            if (r8 != 1) return r8;
             const int r = mv_mma_try(kind0, kind1, b0, a.blocks[1], experts, rows, cols, a.row_bytes, idx, pairs, share,
                                      static_cast<const __half*>(x), a.out[0], a.out[1], nprob, st);
             if (r != 1) return r;

@@ -1,0 +1,441 @@
+// Decode matvec on the int8 tensor cores for the types of the decode hot path (IQ3_S routed experts, Q8_0
+// shared expert): out[p, r] = W[idx[p], r, :] . x[p / share, :] with float16 activations.
+//
+// Every product is exact integer arithmetic until one float32 scaling per block:
+//   - the activations are split, per row and 256-column block, into two int8 vectors: x = s (hi + lo / 128)
+//     with s = max|x| / 127 over the block (|error| <= s / 256, far below float16's own rounding of the
+//     weights); each CTA does this for the rows it needs, into shared memory, while its first weight stages
+//     load;
+//   - the weights enter the MMA as int8: Q8_0 codes as stored, IQ3_S as grid value x sign from a codebook
+//     indexed by (9-bit grid index, 4 sign bits) of 8192 words (32 KB in shared memory), so expanding four
+//     weights is one lookup;
+//   - mma.sync m16n8k32 s8 takes one 32-weight run per MMA: column 0 of B holds hi, column 1 holds lo, so one
+//     MMA gives both sums of a run; 128 hi + lo times the run's integer sub-scale (1 + 2 s for IQ3_S) adds into
+//     an int32 total per row and block (|total| < 2^31 for any weights), scaled once by d s / 128 (IQ3_S), or
+//     run by run by d s / 128 (Q8_0).
+// Layout (B200, one persistent CTA of 16 warps per SM): a job = (problem, pair, tile of 16 weight rows) is
+// taken by a team of 4, 8 or 16 warps that split its 256- (IQ3_S) or 128-column (Q8_0) stages; the team adds
+// its partial sums in shared memory in a fixed order. A tile holds rows c, c + q, c + 2q, ... of one residue
+// class c mod q (q = 16 / gcd(row bytes, 16)), so its 16 rows' bytes sit at one offset within 16 bytes: every
+// warp loads its stages with one tiled TMA copy each (the stack seen as groups of q rows), rows an odd number
+// of 16-byte chunks apart, through a ring of shared-memory slots, and reads every field at a warp-uniform
+// offset.
+#include <cuda.h>
+
+#include <mutex>
+#include <utility>
+
+#include "blocks.cuh"
+#include "tc05.cuh"
+
+namespace smoe {
+
+constexpr int kM8Warps = 16;
+constexpr int kM8Threads = 32 * kM8Warps;
+constexpr int kM8MaxSlots = 4;
+constexpr int kM8XBlock = 256;                   // columns per activation scale
+constexpr uint32_t kM8WaitLimit = 1u << 22;
+
+__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                       uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ uint32_t lds_u16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
+__device__ __forceinline__ uint32_t lds_u8(const uint8_t* p) { return *p; }
+__device__ __forceinline__ float h2f(uint32_t bits) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits & 0xffffu)));
+}
+
+// ---------------------------------------------------------------- IQ3_S
+// (110 bytes: d 0, qs 2..65, qh 66..73, signs 74..105, scales 106..109.) In run r, lane tig of a row's quad
+// takes groups 2 tig and 2 tig + 1 (weights 8 tig .. 8 tig + 7 of the run): K 4 tig .. 4 tig + 3 of the MMA is
+// group 2 tig, K 16 + 4 tig .. is group 2 tig + 1, the same permutation for the activations.
+struct M8IQ3S {
+    static constexpr int kKind = 21, kStageCols = 256, kStageBytes = 110, kRS = 144, kRuns = 8;
+    static constexpr bool kLut = true;
+    // one stage (= one block) of rows gid (j = 0) and gid + 8 (j = 1): partial sums of the two rows
+    __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t* lut,
+                                 const uint8_t* xh, const uint8_t* xl, float xs, float (&total)[2]) {
+        const uint8_t* rb[2] = {r0, r1};
+        uint32_t sc[2], qh[2][2];
+        float d[2];
+        int t[2] = {0, 0};
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            d[j] = h2f(lds_u16(rb[j]));
+            sc[j] = lds_u16(rb[j] + 106) | (lds_u16(rb[j] + 108) << 16);
+            // qh bits of groups 2 tig, 2 tig + 1 of run r at bits 8 (r % 4), 8 (r % 4) + 1 of word r / 4
+            qh[j][0] = (lds_u16(rb[j] + 66) | (lds_u16(rb[j] + 68) << 16)) >> (2 * tig);
+            qh[j][1] = (lds_u16(rb[j] + 70) | (lds_u16(rb[j] + 72) << 16)) >> (2 * tig);
+        }
+        const uint8_t* xsrc = gid == 0 ? xh : xl;
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+            uint32_t a[2][2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint32_t q2 = lds_u16(rb[j] + 2 + 8 * r + 2 * tig);  // qs bytes of the two groups
+                const uint32_t sb = lds_u8(rb[j] + 74 + 4 * r + tig);      // their sign nibbles
+                const uint32_t h = (qh[j][r >> 2] >> (8 * (r & 3))) & 3u;
+                // both codebook indices in one word: qs | qh << 8 | signs << 9 in each half
+                const uint32_t z = __byte_perm(q2, 0u, 0x4140) | ((h * 0x00800100u) & 0x01000100u) |
+                                   ((sb * 0x00200200u) & 0x1E001E00u);
+                a[j][0] = lut[z & 0xffffu];
+                a[j][1] = lut[z >> 16];
+            }
+            uint2 b = make_uint2(0u, 0u);
+            if (gid < 2) b = *reinterpret_cast<const uint2*>(xsrc + 32 * r + 8 * tig);
+            int acc[4];
+            mma_s8(acc, a[0][0], a[1][0], a[0][1], a[1][1], b.x, b.y);
+            // (lanes with tig > 0 hold columns 2..7: zeros)
+            const int m0 = static_cast<int>(((sc[0] >> (4 * r)) & 15u) * 2u + 1u);
+            const int m1 = static_cast<int>(((sc[1] >> (4 * r)) & 15u) * 2u + 1u);
+            t[0] += m0 * (acc[0] * 128 + acc[1]);
+            t[1] += m1 * (acc[2] * 128 + acc[3]);
+        }
+        const float k = xs * (1.0f / 128.0f);
+        total[0] = fmaf(d[0] * k, static_cast<float>(t[0]), total[0]);
+        total[1] = fmaf(d[1] * k, static_cast<float>(t[1]), total[1]);
+    }
+};
+
+// ---------------------------------------------------------------- Q8_0
+// (34 bytes: d 0, qs 2..33.) A stage is four runs; in run r lane tig takes codes 8 tig .. 8 tig + 7.
+struct M8Q8_0 {
+    static constexpr int kKind = 8, kStageCols = 128, kStageBytes = 136, kRS = 176, kRuns = 4;
+    static constexpr bool kLut = false;
+    __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t*,
+                                 const uint8_t* xh, const uint8_t* xl, float xs, float (&total)[2]) {
+        const uint8_t* rb[2] = {r0, r1};
+        const uint8_t* xsrc = gid == 0 ? xh : xl;
+        const float k = xs * (1.0f / 128.0f);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            uint32_t a[2][2];
+            float d[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint8_t* p = rb[j] + 34 * r + 2 + 8 * tig;
+                const uint32_t* w = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
+                const uint32_t sh = 8u * static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 3u);
+                const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+                a[j][0] = __funnelshift_r(w0, w1, sh);
+                a[j][1] = __funnelshift_r(w1, w2, sh);
+                d[j] = h2f(lds_u16(rb[j] + 34 * r));
+            }
+            uint2 b = make_uint2(0u, 0u);
+            if (gid < 2) b = *reinterpret_cast<const uint2*>(xsrc + 32 * r + 8 * tig);
+            int acc[4];
+            mma_s8(acc, a[0][0], a[1][0], a[0][1], a[1][1], b.x, b.y);
+            total[0] = fmaf(d[0] * k, static_cast<float>(acc[0] * 128 + acc[1]), total[0]);
+            total[1] = fmaf(d[1] * k, static_cast<float>(acc[2] * 128 + acc[3]), total[1]);
+        }
+    }
+};
+
+struct M8Args {
+    const uint32_t* idx;
+    const __half* x;
+    __half* out[2];
+    int64_t experts, rows, cols, row_bytes, pairs, share;
+    int q, lq;      // rows per 16-byte aligned group of rows (a power of two) and its log2
+    int tiles;      // tiles of 16 rows (of one residue class) per pair
+    int jobs;       // nprob * pairs * tiles
+    int team;       // warps per job: 4, 8 or 16
+    int xrows;      // activation rows (pairs / share)
+    int nslots;     // ring slots per warp
+};
+struct alignas(64) M8Maps {
+    CUtensorMap w[2];
+};
+
+template <class D>
+__global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, const __grid_constant__ M8Maps maps) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    constexpr int kSlot = 16 * D::kRS;
+    const int ns = a.nslots;
+    uint8_t* ring = sm;                                                         // [warp][slot] 16 rows x kRS
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * kSlot);  // [warp][slot]
+    float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);       // [16 warps][16 rows]
+    uint32_t* lut = reinterpret_cast<uint32_t*>(red + kM8Warps * 16);            // 8192 words (IQ3_S)
+    const int xblocks = static_cast<int>(a.cols / kM8XBlock);
+    float* xscale = reinterpret_cast<float*>(lut + (D::kLut ? 8192 : 0));        // [xrows][xblocks]
+    int8_t* xhi = reinterpret_cast<int8_t*>(xscale + ((a.xrows * xblocks + 3) & ~3));  // [xrows][cols]
+    int8_t* xlo = xhi + size_t(a.xrows) * a.cols;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gid = lane >> 2, tig = lane & 3;
+    if (smem_addr(sm) & 127u) return;  // a tiled copy's destination is 128-byte aligned (the launch gives that)
+    const int team = a.team, teams = kM8Warps / team;
+    const int tid_team = warp / team, kq = warp % team;
+    const int S = static_cast<int>(a.cols / D::kStageCols);
+    const int my_stages = S > kq ? (S - kq + team - 1) / team : 0;
+    const int nteams = gridDim.x * teams;
+    const int q0 = blockIdx.x * teams + tid_team;
+    const int my_jobs = q0 < a.jobs ? (a.jobs - q0 + nteams - 1) / nteams : 0;
+    const int items = my_jobs * my_stages;
+    const int per_prob = static_cast<int>(a.pairs) * a.tiles;  // < 2^30 (the host checks)
+    uint8_t* my_ring = ring + size_t(warp) * ns * kSlot;
+    uint64_t* my_bars = bars + warp * kM8MaxSlots;
+
+    if (lane == 0) {
+        for (int i = 0; i < ns; ++i) tc::mbar_init(&my_bars[i], 1);
+        tc::fence_barrier_init();
+    }
+    __syncwarp();
+
+    // a job's place (worked out once per job, 32-bit): problem, pair, expert, the tile's residue class and
+    // block of 16 q rows, the first row of its TMA box, the activation row
+    struct Where {
+        int prob, cls, blk, xr, pair;
+        uint32_t e;
+        int y;
+    };
+    auto locate = [&](int job) {
+        const int j = q0 + job * nteams;
+        Where w;
+        w.prob = j / per_prob;
+        const int rest = j - w.prob * per_prob;
+        w.pair = rest / a.tiles;
+        const int tile = rest - w.pair * a.tiles;
+        w.cls = tile & (a.q - 1);
+        w.blk = tile >> a.lq;
+        w.e = a.idx[w.pair];
+        w.y = static_cast<int>((int64_t(w.e < a.experts ? w.e : 0) * a.rows) >> a.lq) + 16 * w.blk;
+        w.xr = w.pair / static_cast<int>(a.share);
+        return w;
+    };
+    // the copy cursor (lane 0): the next item to copy and its job, stage and slot
+    int pre_job = 0, pre_k = 0, pre_slot = 0, pre_s = kq;
+    Where pre_w = my_jobs > 0 ? locate(0) : Where{};
+    // lane 0 starts the TMA copy of the cursor's item into its slot and moves the cursor on; a pair naming no
+    // expert copies nothing and completes the slot's phase with a plain arrive, so every item takes one phase
+    auto issue = [&]() {
+        if (pre_w.e >= a.experts) {
+            tc::mbar_arrive(&my_bars[pre_slot]);
+        } else {
+            const int xb = (pre_w.cls * static_cast<int>(a.row_bytes) + pre_s * D::kStageBytes) & ~15;
+            tc::fence_proxy_async_smem();
+            tc::mbar_arrive_expect_tx(&my_bars[pre_slot], static_cast<uint32_t>(kSlot));
+            tc::tma_load_2d(smem_addr(my_ring + pre_slot * kSlot), pre_w.prob ? &maps.w[1] : &maps.w[0], xb >> 2,
+                            pre_w.y, &my_bars[pre_slot]);
+        }
+        if (++pre_slot == ns) pre_slot = 0;
+        pre_s += team;
+        if (++pre_k == my_stages) {
+            pre_k = 0;
+            pre_s = kq;
+            if (++pre_job < my_jobs) pre_w = locate(pre_job);
+        }
+    };
+    if (lane == 0)
+        for (int i = 0; i < ns - 1 && i < items; ++i) issue();
+
+    if constexpr (D::kLut) {
+        // grid value x sign: entry (g, s) of the 9-bit grid index g and the 4 sign bits s
+        for (int i = threadIdx.x; i < 8192; i += kM8Threads) {
+            const uint32_t g = __ldg(&kIq3sGrid[i & 511]), sg = static_cast<uint32_t>(i) >> 9;
+            uint32_t v = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int u = static_cast<int>((g >> (8 * b)) & 255u);
+                v |= (static_cast<uint32_t>((sg >> b) & 1u ? -u : u) & 255u) << (8 * b);
+            }
+            lut[i] = v;
+        }
+    }
+    // the activations, split per 256-column block into int8 hi and lo: a warp per block, 8 values a lane
+    for (int blk = warp; blk < a.xrows * xblocks; blk += kM8Warps) {
+        const int xr = blk / xblocks, b = blk % xblocks;
+        const int64_t c0 = int64_t(b) * kM8XBlock + 8 * lane;
+        const uint4 raw = *reinterpret_cast<const uint4*>(a.x + int64_t(xr) * a.cols + c0);
+        float v[8];
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h2[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float s = amax / 127.0f, inv = amax > 0.f ? 127.0f / amax : 0.f;
+        uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float hf = fminf(fmaxf(rintf(v[i] * inv), -127.f), 127.f);
+            const float lf = fminf(fmaxf(rintf((v[i] - hf * s) * (128.0f * inv)), -127.f), 127.f);
+            hw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(hf)) & 255u) << (8 * (i & 3));
+            lw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(lf)) & 255u) << (8 * (i & 3));
+        }
+        *reinterpret_cast<uint2*>(xhi + int64_t(xr) * a.cols + c0) = make_uint2(hw[0], hw[1]);
+        *reinterpret_cast<uint2*>(xlo + int64_t(xr) * a.cols + c0) = make_uint2(lw[0], lw[1]);
+        if (lane == 0) xscale[blk] = s;
+    }
+    __syncthreads();
+
+    // a wait that gives up (it should not) leaves the warp's remaining stages undone but keeps it in step
+    // with its team's barriers
+    bool ok = true;
+    float total[2] = {0.f, 0.f};
+    int it = 0, slot = 0;
+    uint32_t phase = 0;
+    for (int job = 0; job < my_jobs; ++job) {
+        const Where w = locate(job);
+        const uint8_t* xh = reinterpret_cast<const uint8_t*>(xhi) + int64_t(w.xr) * a.cols;
+        const uint8_t* xl = reinterpret_cast<const uint8_t*>(xlo) + int64_t(w.xr) * a.cols;
+        const float* xsc = xscale + w.xr * xblocks;
+        int s = kq;
+        for (int k = 0; k < my_stages; ++k, ++it, s += team) {
+            // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
+            if (it + ns - 1 < items) {
+                __syncwarp();
+                if (lane == 0) issue();
+            }
+            const int cur = slot;
+            if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, kM8WaitLimit));
+            if (++slot == ns) {
+                slot = 0;
+                phase ^= 1;
+            }
+            if (!ok || w.e >= a.experts) continue;
+            const int off = (w.cls * static_cast<int>(a.row_bytes) + s * D::kStageBytes) & 15;
+            const uint8_t* st = my_ring + cur * kSlot + off;
+            const int xc = s * D::kStageCols;
+            D::stage(st + gid * D::kRS, st + (gid + 8) * D::kRS, tig, gid, lut, xh + xc, xl + xc,
+                     xsc[xc / kM8XBlock], total);
+        }
+        // the team's partial sums of this job's 16 rows, added in warp order
+        float* rq = red + (tid_team * team) * 16;
+        if (tig == 0) {
+            rq[kq * 16 + gid] = total[0];
+            rq[kq * 16 + gid + 8] = total[1];
+        }
+        total[0] = total[1] = 0.f;
+        asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid_team), "r"(32 * team) : "memory");
+        if (kq == 0 && lane < 16) {
+            const int64_t row = int64_t(w.blk) * 16 * a.q + w.cls + int64_t(a.q) * lane;
+            if (w.e < a.experts && row < a.rows) {
+                float v = rq[lane];
+                for (int i = 1; i < team; ++i) v += rq[16 * i + lane];
+                (w.prob ? a.out[1] : a.out[0])[int64_t(w.pair) * a.rows + row] = __float2half_rn(v);
+            }
+        }
+        asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid_team), "r"(32 * team) : "memory");
+    }
+    // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
+    // a wait gave up)
+    if (!ok && lane == 0)
+        for (int i = 0; i < items; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
+    __syncwarp();
+}
+
+typedef CUresult (*M8EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static M8EncodeFn m8_encoder() {
+    static std::once_flag once;
+    static M8EncodeFn fn = nullptr;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<M8EncodeFn>(p);
+    });
+    return fn;
+}
+
+static int g_m8_sms = 0;
+
+// Launch the int8 tensor-core decode matvec when it takes the problem: 0 launched, 1 not taken, else an error.
+int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
+            int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, __half* o0,
+            __half* o1, int nprob, cudaStream_t st) {
+    if (kind0 != kind1) return 1;
+    auto go = [&](auto dec) -> int {
+        using D = decltype(dec);
+        if (cols % kM8XBlock || cols % D::kStageCols) return 1;
+        if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(b0) & 15) ||
+            (reinterpret_cast<uintptr_t>(b1) & 15))
+            return 1;
+        int gcd = 16;
+        while (row_bytes % gcd) gcd >>= 1;
+        const int q = 16 / gcd;
+        if (rows % q) return 1;
+        const int64_t xrows = (pairs + share - 1) / share;
+        const int xblocks = static_cast<int>(cols / kM8XBlock);
+        const size_t xbytes = size_t(((xrows * xblocks + 3) & ~int64_t(3)) * 4) + size_t(xrows * cols * 2);
+        const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + (D::kLut ? 8192 * 4 : 0) + xbytes;
+        const size_t slot = size_t(kM8Warps) * 16 * D::kRS;
+        int ns = kM8MaxSlots;
+        while (ns > 2 && fixed + ns * slot > size_t(227 * 1024)) --ns;
+        if (fixed + ns * slot > size_t(227 * 1024)) return 1;
+        M8EncodeFn encode = m8_encoder();
+        if (!encode) return 1;
+        M8Maps maps;
+        const uint8_t* bl[2] = {b0, b1};
+        for (int p = 0; p < 2; ++p) {
+            const cuuint64_t dims[2] = {static_cast<cuuint64_t>(q * row_bytes / 4),
+                                        static_cast<cuuint64_t>(experts * rows / q)};
+            const cuuint64_t strides[1] = {static_cast<cuuint64_t>(q * row_bytes)};
+            const cuuint32_t box[2] = {static_cast<cuuint32_t>(D::kRS / 4), 16};
+            const cuuint32_t estr[2] = {1, 1};
+            if (encode(&maps.w[p], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(bl[p]), dims, strides, box,
+                       estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+                return 1;
+        }
+        M8Args a{};
+        a.idx = idx;
+        a.x = x;
+        a.out[0] = o0;
+        a.out[1] = o1;
+        a.experts = experts;
+        a.rows = rows;
+        a.cols = cols;
+        a.row_bytes = row_bytes;
+        a.pairs = pairs;
+        a.share = share;
+        a.q = q;
+        a.lq = q == 1 ? 0 : q == 2 ? 1 : q == 4 ? 2 : q == 8 ? 3 : 4;
+        a.tiles = static_cast<int>((rows + 16 * q - 1) / (16 * q)) * q;
+        const int64_t jobs = int64_t(nprob) * pairs * a.tiles;
+        if (jobs > (int64_t(1) << 30) || xrows > (int64_t(1) << 20) || experts * rows / q >= (int64_t(1) << 31) ||
+            q * row_bytes >= (int64_t(1) << 27))
+            return 1;
+        a.jobs = static_cast<int>(jobs);
+        a.xrows = static_cast<int>(xrows);
+        a.nslots = ns;
+        if (g_m8_sms == 0) {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&g_m8_sms, cudaDevAttrMultiProcessorCount, dev);
+            if (g_m8_sms <= 0) g_m8_sms = 148;
+        }
+        const int S = static_cast<int>(cols / D::kStageCols);
+        int team = 4;
+        while (team < 16 && jobs * team < int64_t(g_m8_sms) * kM8Warps && 2 * team <= S) team *= 2;
+        a.team = team;
+        const int teams = kM8Warps / team;
+        const int64_t want = (jobs + teams - 1) / teams;
+        const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, g_m8_sms)));
+        const size_t smem = fixed + ns * slot;
+        if (int s = max_smem(mv8_kernel<D>, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
+        mv8_kernel<D><<<grid, kM8Threads, smem, st>>>(a, maps);
+        return launch_status("matvec (int8 tensor cores)");
+    };
+    if (kind0 == M8IQ3S::kKind) return go(M8IQ3S{});
+    if (kind0 == M8Q8_0::kKind) return go(M8Q8_0{});
+    return 1;
+}
+
+}  // namespace smoe
