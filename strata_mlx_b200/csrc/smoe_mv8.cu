@@ -14,12 +14,12 @@
 //     an int32 total per row and block (|total| < 2^31 for any weights), scaled once by d s / 128 (IQ3_S), or
 //     run by run by d s / 128 (Q8_0).
 // Layout (B200, one persistent CTA of 16 warps per SM): a job = (problem, pair, tile of 16 weight rows) is
-// taken by a team of 4, 8 or 16 warps that split its 256- (IQ3_S) or 128-column (Q8_0) stages; the team adds
-// its partial sums in shared memory in a fixed order. A tile holds rows c, c + q, c + 2q, ... of one residue
-// class c mod q (q = 16 / gcd(row bytes, 16)), so its 16 rows' bytes sit at one offset within 16 bytes: every
-// warp loads its stages with one tiled TMA copy each (the stack seen as groups of q rows), rows an odd number
-// of 16-byte chunks apart, through a ring of shared-memory slots, and reads every field at a warp-uniform
-// offset.
+// taken by a team of 1 to 16 warps (the size that gives the shortest longest warp) that split its 256-
+// (IQ3_S) or 128-column (Q8_0) stages; the team adds its partial sums in shared memory in a fixed order.
+// A tile holds rows c, c + q, c + 2q, ... of one residue class c mod q (q = 16 / gcd(row bytes, 16)), so its
+// 16 rows' bytes sit at one offset within 16 bytes: every warp loads its stages with one tiled TMA copy each
+// (the stack seen as groups of q rows), rows an odd number of 16-byte chunks apart, through a ring of
+// shared-memory slots, and reads every field at a warp-uniform offset.
 #include <cuda.h>
 
 #include <mutex>
@@ -61,13 +61,16 @@ struct M8IQ3S {
     __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t* lut,
                                  const uint8_t* xh, const uint8_t* xl, float xs, float (&total)[2]) {
         const uint8_t* rb[2] = {r0, r1};
-        uint32_t sc[2], qh[2][2];
+        uint32_t m[2][2], qh[2][2];
         float d[2];
         int t[2] = {0, 0};
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
             d[j] = h2f(lds_u16(rb[j]));
-            sc[j] = lds_u16(rb[j] + 106) | (lds_u16(rb[j] + 108) << 16);
+            // the runs' odd sub-scales 1 + 2 s as bytes: runs 0, 2, 4, 6 in m[j][0], runs 1, 3, 5, 7 in m[j][1]
+            const uint32_t sc = lds_u16(rb[j] + 106) | (lds_u16(rb[j] + 108) << 16);
+            m[j][0] = ((sc & 0x0F0F0F0Fu) << 1) | 0x01010101u;
+            m[j][1] = ((sc >> 3) & 0x1E1E1E1Eu) | 0x01010101u;
             // qh bits of groups 2 tig, 2 tig + 1 of run r at bits 8 (r % 4), 8 (r % 4) + 1 of word r / 4
             qh[j][0] = (lds_u16(rb[j] + 66) | (lds_u16(rb[j] + 68) << 16)) >> (2 * tig);
             qh[j][1] = (lds_u16(rb[j] + 70) | (lds_u16(rb[j] + 72) << 16)) >> (2 * tig);
@@ -80,7 +83,8 @@ struct M8IQ3S {
             for (int j = 0; j < 2; ++j) {
                 const uint32_t q2 = lds_u16(rb[j] + 2 + 8 * r + 2 * tig);  // qs bytes of the two groups
                 const uint32_t sb = lds_u8(rb[j] + 74 + 4 * r + tig);      // their sign nibbles
-                const uint32_t h = (qh[j][r >> 2] >> (8 * (r & 3))) & 3u;
+                // byte r % 4 of the shifted qh word: bits 0, 1 are the groups' (the rest never reach the index)
+                const uint32_t h = __byte_perm(qh[j][r >> 2], 0u, 0x4440 + (r & 3));
                 // both codebook indices in one word: qs | qh << 8 | signs << 9 in each half
                 const uint32_t z = __byte_perm(q2, 0u, 0x4140) | ((h * 0x00800100u) & 0x01000100u) |
                                    ((sb * 0x00200200u) & 0x1E001E00u);
@@ -92,8 +96,8 @@ struct M8IQ3S {
             int acc[4];
             mma_s8(acc, a[0][0], a[1][0], a[0][1], a[1][1], b.x, b.y);
             // (lanes with tig > 0 hold columns 2..7: zeros)
-            const int m0 = static_cast<int>(((sc[0] >> (4 * r)) & 15u) * 2u + 1u);
-            const int m1 = static_cast<int>(((sc[1] >> (4 * r)) & 15u) * 2u + 1u);
+            const int m0 = static_cast<int>(__byte_perm(m[0][r & 1], 0u, 0x4440 + (r >> 1)));
+            const int m1 = static_cast<int>(__byte_perm(m[1][r & 1], 0u, 0x4440 + (r >> 1)));
             t[0] += m0 * (acc[0] * 128 + acc[1]);
             t[1] += m1 * (acc[2] * 128 + acc[3]);
         }
@@ -145,10 +149,19 @@ struct M8Args {
     int q, lq;      // rows per 16-byte aligned group of rows (a power of two) and its log2
     int tiles;      // tiles of 16 rows (of one residue class) per pair
     int jobs;       // nprob * pairs * tiles
-    int team;       // warps per job: 4, 8 or 16
+    int team;       // warps per job: 1, 2, 4, 8 or 16
     int xrows;      // activation rows (pairs / share)
     int nslots;     // ring slots per warp
 };
+// a job's place (worked out once per job, 32-bit): problem, pair, expert, the tile's residue class and block
+// of 16 q rows, the first row of its TMA box, the activation row
+struct alignas(8) M8Where {
+    int prob, cls, blk, xr, pair;
+    uint32_t e;
+    int y, pad;
+};
+constexpr int kM8WhereBytes = kM8Warps * 4 * int(sizeof(M8Where));
+
 struct alignas(64) M8Maps {
     CUtensorMap w[2];
 };
@@ -161,7 +174,8 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
     uint8_t* ring = sm;                                                         // [warp][slot] 16 rows x kRS
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * kSlot);  // [warp][slot]
     float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);       // [16 warps][16 rows]
-    uint32_t* lut = reinterpret_cast<uint32_t*>(red + kM8Warps * 16);            // 8192 words (IQ3_S)
+    M8Where* where_ring = reinterpret_cast<M8Where*>(red + kM8Warps * 16);       // [16 warps][4]
+    uint32_t* lut = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(where_ring) + kM8WhereBytes);  // 8192 words
     const int xblocks = static_cast<int>(a.cols / kM8XBlock);
     float* xscale = reinterpret_cast<float*>(lut + (D::kLut ? 8192 : 0));        // [xrows][xblocks]
     int8_t* xhi = reinterpret_cast<int8_t*>(xscale + ((a.xrows * xblocks + 3) & ~3));  // [xrows][cols]
@@ -188,13 +202,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
     }
     __syncwarp();
 
-    // a job's place (worked out once per job, 32-bit): problem, pair, expert, the tile's residue class and
-    // block of 16 q rows, the first row of its TMA box, the activation row
-    struct Where {
-        int prob, cls, blk, xr, pair;
-        uint32_t e;
-        int y;
-    };
+    using Where = M8Where;
     auto locate = [&](int job) {
         const int j = q0 + job * nteams;
         Where w;
@@ -209,9 +217,16 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
         w.xr = w.pair / static_cast<int>(a.share);
         return w;
     };
-    // the copy cursor (lane 0): the next item to copy and its job, stage and slot
+    // the copy cursor (lane 0): the next item to copy and its job, stage and slot. The cursor works out each
+    // job's place (its expert index is a global load) and leaves it in the warp's ring of 4 places, where the
+    // warp picks it up when it starts the job: the cursor runs at most 3 items, so at most 3 jobs, ahead.
+    Where* my_where = where_ring + warp * 4;
     int pre_job = 0, pre_k = 0, pre_slot = 0, pre_s = kq;
-    Where pre_w = my_jobs > 0 ? locate(0) : Where{};
+    Where pre_w{};
+    if (lane == 0 && my_jobs > 0 && my_stages > 0) {
+        pre_w = locate(0);
+        my_where[0] = pre_w;
+    }
     // lane 0 starts the TMA copy of the cursor's item into its slot and moves the cursor on; a pair naming no
     // expert copies nothing and completes the slot's phase with a plain arrive, so every item takes one phase
     auto issue = [&]() {
@@ -229,7 +244,10 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
         if (++pre_k == my_stages) {
             pre_k = 0;
             pre_s = kq;
-            if (++pre_job < my_jobs) pre_w = locate(pre_job);
+            if (++pre_job < my_jobs) {
+                pre_w = locate(pre_job);
+                my_where[pre_job & 3] = pre_w;
+            }
         }
     };
     if (lane == 0)
@@ -281,6 +299,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
     }
     __syncthreads();
 
+    // a team of one warp needs no named barrier (there are 16, barrier 0 is __syncthreads')
+    auto team_sync = [&]() {
+        if (team == 1) __syncwarp();
+        else asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid_team), "r"(32 * team) : "memory");
+    };
     // a wait that gives up (it should not) leaves the warp's remaining stages undone but keeps it in step
     // with its team's barriers
     bool ok = true;
@@ -288,7 +311,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
     int it = 0, slot = 0;
     uint32_t phase = 0;
     for (int job = 0; job < my_jobs; ++job) {
-        const Where w = locate(job);
+        const Where w = my_stages > 0 ? my_where[job & 3] : locate(job);
         const uint8_t* xh = reinterpret_cast<const uint8_t*>(xhi) + int64_t(w.xr) * a.cols;
         const uint8_t* xl = reinterpret_cast<const uint8_t*>(xlo) + int64_t(w.xr) * a.cols;
         const float* xsc = xscale + w.xr * xblocks;
@@ -319,7 +342,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
             rq[kq * 16 + gid + 8] = total[1];
         }
         total[0] = total[1] = 0.f;
-        asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid_team), "r"(32 * team) : "memory");
+        team_sync();
         if (kq == 0 && lane < 16) {
             const int64_t row = int64_t(w.blk) * 16 * a.q + w.cls + int64_t(a.q) * lane;
             if (w.e < a.experts && row < a.rows) {
@@ -328,7 +351,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
                 (w.prob ? a.out[1] : a.out[0])[int64_t(w.pair) * a.rows + row] = __float2half_rn(v);
             }
         }
-        asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid_team), "r"(32 * team) : "memory");
+        team_sync();
     }
     // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
     // a wait gave up)
@@ -374,7 +397,8 @@ int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t 
         const int64_t xrows = (pairs + share - 1) / share;
         const int xblocks = static_cast<int>(cols / kM8XBlock);
         const size_t xbytes = size_t(((xrows * xblocks + 3) & ~int64_t(3)) * 4) + size_t(xrows * cols * 2);
-        const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + (D::kLut ? 8192 * 4 : 0) + xbytes;
+        const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + kM8WhereBytes +
+                             (D::kLut ? 8192 * 4 : 0) + xbytes;
         const size_t slot = size_t(kM8Warps) * 16 * D::kRS;
         int ns = kM8MaxSlots;
         while (ns > 2 && fixed + ns * slot > size_t(227 * 1024)) --ns;
@@ -421,9 +445,19 @@ int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t 
             cudaDeviceGetAttribute(&g_m8_sms, cudaDevAttrMultiProcessorCount, dev);
             if (g_m8_sms <= 0) g_m8_sms = 148;
         }
-        const int S = static_cast<int>(cols / D::kStageCols);
-        int team = 4;
-        while (team < 16 && jobs * team < int64_t(g_m8_sms) * kM8Warps && 2 * team <= S) team *= 2;
+        // the team size with the shortest longest warp: (jobs of the busiest team) x (stages of its busiest warp,
+        // plus about 3/4 of a stage for the team's reduction when the team has more than one warp), in quarters
+        const int64_t S = cols / D::kStageCols;
+        int team = 1;
+        int64_t best = -1;
+        for (int t = 1; t <= kM8Warps; t *= 2) {
+            const int64_t nteams = int64_t(g_m8_sms) * (kM8Warps / t);
+            const int64_t span = (jobs + nteams - 1) / nteams * (4 * ((S + t - 1) / t) + (t > 1 ? 3 : 0));
+            if (best < 0 || span < best) {
+                best = span;
+                team = t;
+            }
+        }
         a.team = team;
         const int teams = kM8Warps / team;
         const int64_t want = (jobs + teams - 1) / teams;
