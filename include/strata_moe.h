@@ -100,10 +100,22 @@ SMOE_API int smoe_router_logits(const uint16_t* weight, const void* x, int x_dty
 
 /* idx[t, :] = the k largest of logits[t, :] (float32, n per row), largest first, ties to the lower index:
  * `mx.argpartition(-logits, k - 1)[..., :k]`. Replaces `top_k` / `_TOPK` (strata_mlx/fused.py:400-436);
- * any n <= 4096 and k <= 64, rows of any count. If `weights` is not null it also receives
+ * any n <= 2048 and k <= 32, rows of any count. If `weights` is not null it also receives
  * softmax(logits[t, idx[t, :]]) in float32 (strata_mlx/fused.py:491, `mx.softmax(..., precise=True)`). */
 SMOE_API int smoe_top_k(const float* logits, int64_t rows, int64_t n, int64_t k, uint32_t* idx, float* weights,
                void* stream);
+
+/* The start of the MoE block in one launch: smoe_router_logits into `logits` (tokens, experts), then
+ * smoe_top_k with weights into idx / weights (tokens, k), and, when `gate_weight` (1, hidden, float16) is
+ * given, the shared expert's gate value gate_out[t] = (gate_weight . x[t]) rounded to x's type: the first
+ * three lines of `_Routed.__call__` (strata_mlx/fused.py:487-491, `shared_expert_gate(x).to(x.dtype)`) with the
+ * same sums and choice as the separate calls. experts <= 2048, k <= 32. `counters`: smoe_route_counters(tokens)
+ * bytes of device memory, zero before the first call; every call leaves them zero. Calls that share counters
+ * must not overlap on the GPU. No single reference counterpart: it fuses the three. */
+SMOE_API size_t smoe_route_counters(int64_t tokens);
+SMOE_API int smoe_route(const uint16_t* weight, const uint16_t* gate_weight, const void* x, int x_dtype,
+                        int64_t tokens, int64_t experts, int64_t hidden, int64_t k, float* logits, uint32_t* idx,
+                        float* weights, void* gate_out, uint32_t* counters, void* stream);
 
 /* The end of the MoE block: out[t, d] = half(sum_k y[t,k,d] w[t,k]) + half(half(sigmoid(g[t])) s[t,d]),
  * the sum in float32 in MLX's col_reduce_small order (partials j = k mod 8, then in order), every product

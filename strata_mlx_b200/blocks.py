@@ -223,22 +223,30 @@ def _tiled_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.
 
 # types whose float16 products run on the tensor-core decode kernel, with the columns of its stage
 MMA_MATVEC = {"IQ3_S": 256, "Q8_0": 128}
+# the int8 tensor-core decode kernel forms the SwiGLU of down's input itself when the activations (as int8
+# pairs) fit in its shared memory: types, the columns it splits the activations by, the bytes it may hold
+FUSED_GLU = ("IQ3_S", "Q8_0")
+FUSED_GLU_COLS, FUSED_GLU_BYTES = 256, 64 << 10
 
 
 def matvec_glu(lin, idx: torch.Tensor, gate: torch.Tensor, up: torch.Tensor):
     """`lin(swiglu(gate, up), idx)` for a BlockSwitchLinear, one pair to each row of gate and up, (pairs, out)
     (strata_mlx/blocks.py:939-955). None where the activations are of a type the kernel does not take.
 
-    For the types of the tensor-core decode kernel the SwiGLU is formed by its own small kernel first (the
-    same function, so the same bits) and the product runs there; the others form it inside the product."""
+    The SwiGLU is the same function (so the same bits) everywhere: the int8 tensor-core decode kernel forms
+    it while it splits the activations (as the reference's _MATVEC_GLU forms it in the matvec,
+    strata_mlx/blocks.py:222-224); for a product it does not take whose type has the float16 tensor-core
+    kernel, a small kernel forms it first; the CUDA-core kernel forms it inside the product."""
     if gate.dtype not in (torch.float16, torch.float32) or up.dtype != gate.dtype:
         return None
     _lib.require_cuda(idx, gate, up, lin.blocks)
     idx = _flat_idx(idx)
-    if gate.dtype == torch.float16 and lin.input_dims % MMA_MATVEC.get(lin.kind, 1 << 30) == 0:
-        h = swiglu(gate.reshape(idx.numel(), -1), up.reshape(idx.numel(), -1))
-        return _matvec(lin, h, idx, 1, gate.dtype)
     pairs = idx.numel()
+    fused = (gate.dtype == torch.float16 and lin.kind in FUSED_GLU and lin.input_dims % FUSED_GLU_COLS == 0
+             and pairs * lin.input_dims * 2 <= FUSED_GLU_BYTES)
+    if not fused and gate.dtype == torch.float16 and lin.input_dims % MMA_MATVEC.get(lin.kind, 1 << 30) == 0:
+        h = swiglu(gate.reshape(pairs, -1), up.reshape(pairs, -1))
+        return _matvec(lin, h, idx, 1, gate.dtype)
     gate = gate.reshape(pairs, -1).contiguous()
     up = up.reshape(pairs, -1).contiguous()
     out = torch.empty((pairs, lin.output_dims), dtype=gate.dtype, device=gate.device)

@@ -111,4 +111,20 @@ __device__ __forceinline__ float warp_sum(float v) {
     return v;
 }
 
+__device__ __forceinline__ float sigmoid_branch(float g) {
+    // MLX's form: 1 / (1 + exp(|g|)) taken on the side that cannot overflow
+    const float y = 1.0f / (1.0f + expf(fabsf(g)));
+    return g < 0.0f ? y : 1.0f - y;
+}
+
+// silu(gate) * up in the activations' type T, as mlx-lm's swiglu works it out (strata_mlx/blocks.py:222-224):
+// sigmoid in float32 rounded to T, then two products in T
+template <typename T>
+__device__ __forceinline__ T swiglu_one(T g, T u) {
+    const float gf = to_f32(g);
+    const T sig = from_f32<T>(sigmoid_branch(gf));
+    const T a = from_f32<T>(__fmul_rn(gf, to_f32(sig)));
+    return from_f32<T>(__fmul_rn(to_f32(a), to_f32(u)));
+}
+
 }  // namespace smoe

@@ -55,21 +55,6 @@ struct MatvecArgs {
     int stage;          // bytes of one row slot (row_bytes + 16, rounded to 16)
 };
 
-__device__ __forceinline__ float sigmoid_branch(float g) {
-    // MLX's form: 1 / (1 + exp(|g|)) taken on the side that cannot overflow
-    const float y = 1.0f / (1.0f + expf(fabsf(g)));
-    return g < 0.0f ? y : 1.0f - y;
-}
-
-// silu(gate) * up in the activations' type T: sigmoid in float32 rounded to T, then two products in T
-template <typename T>
-__device__ __forceinline__ T swiglu_one(T g, T u) {
-    const float gf = to_f32(g);
-    const T sig = from_f32<T>(sigmoid_branch(gf));
-    const T a = from_f32<T>(__fmul_rn(gf, to_f32(sig)));
-    return from_f32<T>(__fmul_rn(to_f32(a), to_f32(u)));
-}
-
 template <class B, typename T>
 __global__ void __launch_bounds__(kMvThreads) matvec_kernel(const MatvecArgs<T> a) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -143,8 +128,8 @@ __global__ void swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u, 
 
 // the int8 tensor-core decode matvec (smoe_mv8.cu): 0 launched, 1 not taken, else an error status
 int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
-            int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, __half* o0,
-            __half* o1, int nprob, cudaStream_t st);
+            int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, const __half* gate,
+            const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st);
 // the float16 tensor-core decode matvec (smoe_mv.cu), for what the int8 one does not take
 int mv_mma_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
                int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, __half* o0,
@@ -209,10 +194,11 @@ static int matvec_common(int kind0, const uint8_t* b0, int kind1, const uint8_t*
     a.pairs = pairs;
     a.share = share;
     if constexpr (sizeof(T) == 2) {
+        const int r8 = mv8_try(kind0, kind1, b0, a.blocks[1], experts, rows, cols, a.row_bytes, idx, pairs, share,
+                               static_cast<const __half*>(x), static_cast<const __half*>(gate),
+                               static_cast<const __half*>(up), a.out[0], a.out[1], nprob, st);
+        if (r8 != 1) return r8;
         if (gate == nullptr) {
-            const int r8 = mv8_try(kind0, kind1, b0, a.blocks[1], experts, rows, cols, a.row_bytes, idx, pairs, share,
-                                   static_cast<const __half*>(x), a.out[0], a.out[1], nprob, st);
-            if (r8 != 1) return r8;
             const int r = mv_mma_try(kind0, kind1, b0, a.blocks[1], experts, rows, cols, a.row_bytes, idx, pairs, share,
                                      static_cast<const __half*>(x), a.out[0], a.out[1], nprob, st);
             if (r != 1) return r;

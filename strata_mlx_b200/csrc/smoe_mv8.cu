@@ -144,6 +144,7 @@ struct M8Q8_0 {
 struct M8Args {
     const uint32_t* idx;
     const __half* x;
+    const __half *gate, *up;  // when gate is set, the activations are swiglu(gate, up) (down's input)
     __half* out[2];
     int64_t experts, rows, cols, row_bytes, pairs, share;
     int q, lq;      // rows per 16-byte aligned group of rows (a power of two) and its log2
@@ -160,7 +161,8 @@ struct alignas(8) M8Where {
     uint32_t e;
     int y, pad;
 };
-constexpr int kM8WhereBytes = kM8Warps * 4 * int(sizeof(M8Where));
+constexpr int kM8MaskRows = 1024;  // activation rows a CTA can mark as needed
+constexpr int kM8WhereBytes = kM8Warps * 4 * int(sizeof(M8Where)) + kM8MaskRows / 8;
 
 struct alignas(64) M8Maps {
     CUtensorMap w[2];
@@ -254,30 +256,49 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
         for (int i = 0; i < ns - 1 && i < items; ++i) issue();
 
     if constexpr (D::kLut) {
-        // grid value x sign: entry (g, s) of the 9-bit grid index g and the 4 sign bits s
-        for (int i = threadIdx.x; i < 8192; i += kM8Threads) {
-            const uint32_t g = __ldg(&kIq3sGrid[i & 511]), sg = static_cast<uint32_t>(i) >> 9;
-            uint32_t v = 0;
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const int u = static_cast<int>((g >> (8 * b)) & 255u);
-                v |= (static_cast<uint32_t>((sg >> b) & 1u ? -u : u) & 255u) << (8 * b);
+        // grid value x sign, entry g | s << 9 (built from gguf-py's grid with the rest of the tables): 32 KB
+        // copied in 16-byte pieces
+        const uint4* src = reinterpret_cast<const uint4*>(kIq3sSigned);
+        uint4* dst = reinterpret_cast<uint4*>(lut);
+        for (int i = threadIdx.x; i < 8192 / 4; i += kM8Threads) dst[i] = __ldg(src + i);
+    }
+    // the activation rows this CTA's jobs read (all of them when there are more than kM8MaskRows)
+    uint32_t* need = reinterpret_cast<uint32_t*>(where_ring + kM8Warps * 4);  // kM8MaskRows bits
+    const bool masked = a.xrows <= kM8MaskRows;
+    if (masked) {
+        for (int i = threadIdx.x; i < kM8MaskRows / 32; i += kM8Threads) need[i] = 0u;
+        __syncthreads();
+        if (lane == 0 && my_stages > 0)
+            for (int job = 0; job < my_jobs; ++job) {
+                const int xr = locate(job).xr;
+                atomicOr(&need[xr >> 5], 1u << (xr & 31));
             }
-            lut[i] = v;
-        }
+        __syncthreads();
     }
     // the activations, split per 256-column block into int8 hi and lo: a warp per block, 8 values a lane
     for (int blk = warp; blk < a.xrows * xblocks; blk += kM8Warps) {
         const int xr = blk / xblocks, b = blk % xblocks;
+        if (masked && !((need[xr >> 5] >> (xr & 31)) & 1u)) continue;
         const int64_t c0 = int64_t(b) * kM8XBlock + 8 * lane;
-        const uint4 raw = *reinterpret_cast<const uint4*>(a.x + int64_t(xr) * a.cols + c0);
         float v[8];
-        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+        if (a.gate) {
+            // the SwiGLU of the gate and up products, the same function (so the same float16 bits) as the
+            // separate kernel
+            const uint4 gr = *reinterpret_cast<const uint4*>(a.gate + int64_t(xr) * a.cols + c0);
+            const uint4 ur = *reinterpret_cast<const uint4*>(a.up + int64_t(xr) * a.cols + c0);
+            const __half* gh = reinterpret_cast<const __half*>(&gr);
+            const __half* uh = reinterpret_cast<const __half*>(&ur);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const float2 f = __half22float2(h2[i]);
-            v[2 * i] = f.x;
-            v[2 * i + 1] = f.y;
+            for (int i = 0; i < 8; ++i) v[i] = __half2float(swiglu_one(gh[i], uh[i]));
+        } else {
+            const uint4 raw = *reinterpret_cast<const uint4*>(a.x + int64_t(xr) * a.cols + c0);
+            const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float2 f = __half22float2(h2[i]);
+                v[2 * i] = f.x;
+                v[2 * i + 1] = f.y;
+            }
         }
         float amax = 0.f;
 #pragma unroll
@@ -380,15 +401,18 @@ static M8EncodeFn m8_encoder() {
 static int g_m8_sms = 0;
 
 // Launch the int8 tensor-core decode matvec when it takes the problem: 0 launched, 1 not taken, else an error.
+// x, or (gate, up) whose SwiGLU is the activations.
 int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
-            int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, __half* o0,
-            __half* o1, int nprob, cudaStream_t st) {
+            int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, const __half* gate,
+            const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st) {
     if (kind0 != kind1) return 1;
     auto go = [&](auto dec) -> int {
         using D = decltype(dec);
         if (cols % kM8XBlock || cols % D::kStageCols) return 1;
-        if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(b0) & 15) ||
-            (reinterpret_cast<uintptr_t>(b1) & 15))
+        if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(gate) & 15) ||
+            (reinterpret_cast<uintptr_t>(up) & 15) || (reinterpret_cast<uintptr_t>(b0) & 15) ||
+            (reinterpret_cast<uintptr_t>(b1) & 15) || (gate != nullptr) != (up != nullptr) ||
+            (gate == nullptr) == (x == nullptr))
             return 1;
         int gcd = 16;
         while (row_bytes % gcd) gcd >>= 1;
@@ -421,6 +445,8 @@ int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t 
         M8Args a{};
         a.idx = idx;
         a.x = x;
+        a.gate = gate;
+        a.up = up;
         a.out[0] = o0;
         a.out[1] = o1;
         a.experts = experts;

@@ -33,6 +33,40 @@ __device__ __forceinline__ void load8<float>(const float* p, float* v) {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+// acc[t] += this lane's share of row . x[t0 + t] for the CTA's layout (four warps to a row, every fourth
+// 16-byte chunk); four chunks of the row in flight at once (hidden 4096: all of this lane's), then their
+// products in chunk order
+template <typename XT>
+__device__ __forceinline__ void router_rows(const __half* __restrict__ row, bool live, const XT* __restrict__ x,
+                                            int64_t hidden, int64_t t0, int nt, float (&acc)[kRtTokens]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int quarter = warp & 3;
+#pragma unroll
+    for (int t = 0; t < kRtTokens; ++t) acc[t] = 0.0f;
+    if (!live) return;
+    const int64_t chunks = hidden >> 3;
+    for (int64_t c0 = quarter * 32 + lane; c0 < chunks; c0 += 4 * 128) {
+        float wv[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+            if (c0 + 128 * u < chunks) load8<__half>(row + 8 * (c0 + 128 * u), wv[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t c = c0 + 128 * u;
+            if (c >= chunks) break;
+#pragma unroll
+            for (int t = 0; t < kRtTokens; ++t) {
+                if (t < nt) {
+                    float xv[8];
+                    load8<XT>(x + (t0 + t) * hidden + 8 * c, xv);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[t] = fmaf(wv[u][j], xv[j], acc[t]);
+                }
+            }
+        }
+    }
+}
+
 template <typename XT>
 __global__ void __launch_bounds__(256) router_kernel(const __half* __restrict__ w, const XT* __restrict__ x,
                                                      int64_t tokens, int64_t experts, int64_t hidden,
@@ -44,25 +78,7 @@ __global__ void __launch_bounds__(256) router_kernel(const __half* __restrict__ 
     const int64_t t0 = int64_t(blockIdx.y) * kRtTokens;
     const int nt = static_cast<int>(min(int64_t(kRtTokens), tokens - t0));
     float acc[kRtTokens];
-#pragma unroll
-    for (int t = 0; t < kRtTokens; ++t) acc[t] = 0.0f;
-    if (e < experts) {
-        const __half* row = w + e * hidden;
-        const int64_t chunks = hidden >> 3;
-        for (int64_t c = quarter * 32 + lane; c < chunks; c += 128) {
-            float wv[8];
-            load8<__half>(row + 8 * c, wv);
-#pragma unroll
-            for (int t = 0; t < kRtTokens; ++t) {
-                if (t < nt) {
-                    float xv[8];
-                    load8<XT>(x + (t0 + t) * hidden + 8 * c, xv);
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) acc[t] = fmaf(wv[j], xv[j], acc[t]);
-                }
-            }
-        }
-    }
+    router_rows(w + e * hidden, e < experts, x, hidden, t0, nt, acc);
 #pragma unroll
     for (int t = 0; t < kRtTokens; ++t) acc[t] = warp_sum(acc[t]);
     if (lane == 0) {
@@ -92,20 +108,17 @@ __device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t b
     return v > bv || (v == bv && i < bi);
 }
 
-template <int NV>
-__global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ logits, int64_t rows, int n, int k,
-                                                   uint32_t* __restrict__ idx, float* __restrict__ weights) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t row = int64_t(blockIdx.x) * 4 + warp;
-    if (row >= rows) return;
-    const float* in = logits + row * n;
+// One row's top-k and softmax by one warp; `load` reads logit j of the row.
+template <int NV, class Load>
+__device__ __forceinline__ void topk_row(Load load, int n, int k, uint32_t* __restrict__ idx, float* __restrict__ weights) {
+    const int lane = threadIdx.x & 31;
     float v[NV];
     bool live[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         const int j = 32 * i + lane;
         live[i] = j < n;
-        v[i] = live[i] ? in[j] : -INFINITY;
+        v[i] = live[i] ? load(j) : -INFINITY;
     }
     float top0 = 0.0f, sum = 0.0f, chosen = 0.0f;
     for (int r = 0; r < k; ++r) {
@@ -128,7 +141,7 @@ __global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ log
                 bi = oi;
             }
         }
-        if (lane == 0) idx[row * k + r] = bi;
+        if (lane == 0) idx[r] = bi;
         if (bi != 0xffffffffu && (bi & 31u) == uint32_t(lane)) {
 #pragma unroll
             for (int i = 0; i < NV; ++i)
@@ -142,8 +155,77 @@ __global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ log
         // exp(v - max) / sum in float32; k <= 32 here (checked on the host), one value a lane
         const float ex = lane < k ? expf(chosen - top0) : 0.0f;
         sum = warp_sum(lane < k ? ex : 0.0f);
-        if (lane < k) weights[row * k + lane] = ex / sum;
+        if (lane < k) weights[lane] = ex / sum;
     }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(128) topk_kernel(const float* __restrict__ logits, int64_t rows, int n, int k,
+                                                   uint32_t* __restrict__ idx, float* __restrict__ weights) {
+    const int warp = threadIdx.x >> 5;
+    const int64_t row = int64_t(blockIdx.x) * 4 + warp;
+    if (row >= rows) return;
+    const float* in = logits + row * n;
+    topk_row<NV>([&](int j) { return in[j]; }, n, k, idx + row * k, weights ? weights + row * k : nullptr);
+}
+
+// ---------------------------------------------------------------- router, top-k, softmax and shared gate in
+// one launch
+//
+// The router kernel's CTAs over the expert rows (the same sums in the same order as router_kernel), plus one
+// more row when the shared expert's gate row is given: its sum, rounded to the activations' type, is the
+// block's gate value (`shared_expert_gate(x).to(x.dtype)`). Every CTA then counts itself done on its token
+// group's counter; the last one (which sees all the group's logits after the fence) runs top_k_softmax for
+// the group's tokens, a warp per token, and sets the counter back to zero for the next launch.
+
+template <typename XT, int NV>
+__global__ void __launch_bounds__(256) route_kernel(const __half* __restrict__ w, const __half* __restrict__ gw,
+                                                    const XT* __restrict__ x, int64_t tokens, int64_t experts,
+                                                    int64_t hidden, int k, float* __restrict__ logits,
+                                                    uint32_t* __restrict__ idx, float* __restrict__ weights,
+                                                    XT* __restrict__ gate_out, uint32_t* __restrict__ counters) {
+    __shared__ float part[2][4][kRtTokens];
+    __shared__ bool last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int local_row = warp >> 2, quarter = warp & 3;
+    const int64_t e = int64_t(blockIdx.x) * 2 + local_row;
+    const int64_t t0 = int64_t(blockIdx.y) * kRtTokens;
+    const int nt = static_cast<int>(min(int64_t(kRtTokens), tokens - t0));
+    const int64_t rows = experts + (gw != nullptr ? 1 : 0);
+    float acc[kRtTokens];
+    router_rows(e < experts ? w + e * hidden : gw, e < rows, x, hidden, t0, nt, acc);
+#pragma unroll
+    for (int t = 0; t < kRtTokens; ++t) acc[t] = warp_sum(acc[t]);
+    if (lane == 0) {
+#pragma unroll
+        for (int t = 0; t < kRtTokens; ++t) part[local_row][quarter][t] = acc[t];
+    }
+    __syncthreads();
+    if (threadIdx.x < 2 * kRtTokens) {
+        const int r = threadIdx.x / kRtTokens, t = threadIdx.x % kRtTokens;
+        const int64_t er = int64_t(blockIdx.x) * 2 + r;
+        if (er < rows && t < nt) {
+            float s = part[r][0][t];
+            s += part[r][1][t];
+            s += part[r][2][t];
+            s += part[r][3][t];
+            if (er < experts) logits[(t0 + t) * experts + er] = s;
+            else gate_out[t0 + t] = from_f32<XT>(s);
+        }
+    }
+    // the last CTA of this token group to finish takes the group's top-k
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(&counters[blockIdx.y], 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (warp < nt) {
+        const float* in = logits + (t0 + warp) * experts;
+        topk_row<NV>([&](int j) { return __ldcg(in + j); }, static_cast<int>(experts), k, idx + (t0 + warp) * k,
+                     weights + (t0 + warp) * k);
+    }
+    if (threadIdx.x == 0) counters[blockIdx.y] = 0u;
 }
 
 // ---------------------------------------------------------------- combine
@@ -165,10 +247,23 @@ __global__ void combine_kernel(const T* __restrict__ y, const float* __restrict_
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < d; i += int64_t(gridDim.x) * blockDim.x) {
         const T* yt = y + (t * k) * d + i;
         float acc = 0.0f;
-        for (int j = 0; j < 8 && j < k; ++j) {
-            float part = 0.0f;
-            for (int kk = j; kk < k; kk += 8) part = __fadd_rn(__fmul_rn(to_f32(yt[int64_t(kk) * d]), wt[kk]), part);
-            acc = j == 0 ? part : __fadd_rn(part, acc);
+        if (k == 8) {
+            // (the common case, its eight loads in flight together; the same sums in the same order)
+            float v[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = to_f32(yt[int64_t(j) * d]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float part = __fadd_rn(__fmul_rn(v[j], wt[j]), 0.0f);
+                acc = j == 0 ? part : __fadd_rn(part, acc);
+            }
+        } else {
+            for (int j = 0; j < 8 && j < k; ++j) {
+                float part = 0.0f;
+                for (int kk = j; kk < k; kk += 8)
+                    part = __fadd_rn(__fmul_rn(to_f32(yt[int64_t(kk) * d]), wt[kk]), part);
+                acc = j == 0 ? part : __fadd_rn(part, acc);
+            }
         }
         const T routed = from_f32<T>(acc);
         const T shared = mul_t<T>(gate, s[t * d + i]);
@@ -310,6 +405,50 @@ extern "C" int smoe_top_k(const float* logits, int64_t rows, int64_t n, int64_t 
     else
         topk_kernel<64><<<grid, 128, 0, st>>>(logits, rows, nn, kk, idx, weights);
     return launch_status("top_k");
+}
+
+extern "C" size_t smoe_route_counters(int64_t tokens) {
+    return static_cast<size_t>(tokens > 0 ? (tokens + kRtTokens - 1) / kRtTokens : 1) * sizeof(uint32_t);
+}
+
+extern "C" int smoe_route(const uint16_t* weight, const uint16_t* gate_weight, const void* x, int x_dtype,
+                          int64_t tokens, int64_t experts, int64_t hidden, int64_t k, float* logits, uint32_t* idx,
+                          float* weights, void* gate_out, uint32_t* counters, void* stream) {
+    if (tokens == 0) return SMOE_OK;
+    SMOE_REQUIRE(weight && x && logits && idx && weights && counters && tokens > 0 && experts > 0, SMOE_EARG,
+                 "null pointer or empty router");
+    SMOE_REQUIRE((gate_weight == nullptr) == (gate_out == nullptr), SMOE_EARG,
+                 "the shared gate's weight and output come together");
+    SMOE_REQUIRE(hidden > 0 && hidden % 8 == 0, SMOE_ESHAPE, "router rows must hold a multiple of 8 values");
+    SMOE_REQUIRE((reinterpret_cast<uintptr_t>(weight) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(gate_weight) & 15) == 0,
+                 SMOE_EARG, "router weights and activations must be 16-byte aligned");
+    SMOE_REQUIRE(experts <= 2048, SMOE_ESHAPE, "route takes rows of 1 to 2048 logits");
+    SMOE_REQUIRE(k >= 1 && k <= experts && k <= 32, SMOE_ESHAPE, "route takes 1 <= k <= min(experts, 32)");
+    SMOE_REQUIRE((tokens + kRtTokens - 1) / kRtTokens <= 65535, SMOE_ESHAPE, "too many tokens for one route call");
+    const int64_t rows = experts + (gate_weight ? 1 : 0);
+    dim3 grid(static_cast<unsigned>((rows + 1) / 2), static_cast<unsigned>((tokens + kRtTokens - 1) / kRtTokens));
+    cudaStream_t st = as_stream(stream);
+    const __half* w = reinterpret_cast<const __half*>(weight);
+    const __half* gw = reinterpret_cast<const __half*>(gate_weight);
+    const int kk = static_cast<int>(k);
+    auto go = [&](auto xt) {
+        using XT = decltype(xt);
+        const XT* xp = static_cast<const XT*>(x);
+        XT* go_ = static_cast<XT*>(gate_out);
+        if (experts <= 256)
+            route_kernel<XT, 8><<<grid, 256, 0, st>>>(w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+        else if (experts <= 512)
+            route_kernel<XT, 16><<<grid, 256, 0, st>>>(w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+        else if (experts <= 1024)
+            route_kernel<XT, 32><<<grid, 256, 0, st>>>(w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+        else
+            route_kernel<XT, 64><<<grid, 256, 0, st>>>(w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+    };
+    if (x_dtype == SMOE_F16) go(__half{});
+    else if (x_dtype == SMOE_F32) go(float{});
+    else return fail(SMOE_EDTYPE, "router activations must be float16 or float32");
+    return launch_status("route");
 }
 
 extern "C" int smoe_combine(const void* y, const float* w, const void* g, const void* s, int64_t tokens, int64_t k,

@@ -80,6 +80,40 @@ def top_k_softmax(logits: torch.Tensor, k: int):
     return _top_k(logits, k, True)
 
 
+_COUNTERS = {}
+
+
+def route(gate: "WindowLinear", shared_gate, x: torch.Tensor, k: int):
+    """The start of the MoE block in one launch: (idx, w, g) = (top_k_softmax(gate(x), k),
+    shared_gate(x).to(x.dtype)) with the same sums and choice as those calls (strata_mlx/fused.py:487-491).
+    shared_gate: a WindowLinear of one row, or None (g is then None). None where the kernel does not take x."""
+    if not gate.takes(x) or gate.rows > 2048 or not 1 <= k <= min(gate.rows, 32):
+        return None
+    if shared_gate is not None and (not shared_gate.takes(x) or shared_gate.rows != 1 or shared_gate.cols != gate.cols):
+        return None
+    _lib.require_cuda(gate.weight, x)
+    tokens = x.numel() // gate.cols
+    x2 = x.reshape(tokens, gate.cols).contiguous()
+    dev = x.device
+    logits = torch.empty((tokens, gate.rows), dtype=torch.float32, device=dev)
+    idx = torch.empty((tokens, k), dtype=torch.uint32, device=dev)
+    w = torch.empty((tokens, k), dtype=torch.float32, device=dev)
+    g = torch.empty((tokens,), dtype=x.dtype, device=dev) if shared_gate is not None else None
+    nbytes = int(_lib.lib().smoe_route_counters(tokens))
+    key = (str(dev), nbytes)
+    counters = _COUNTERS.get(key)
+    if counters is None:
+        counters = _COUNTERS[key] = torch.zeros(nbytes // 4, dtype=torch.int32, device=dev)
+    if tokens:
+        _lib.call("smoe_route", _lib.ptr(gate.weight.contiguous()),
+                  _lib.ptr(shared_gate.weight.contiguous()) if shared_gate is not None else None, _lib.ptr(x2),
+                  _lib.dtype_code(x.dtype), tokens, gate.rows, gate.cols, k, _lib.ptr(logits), _lib.ptr(idx),
+                  _lib.ptr(w), _lib.ptr(g) if g is not None else None, _lib.ptr(counters), _lib.stream())
+    lead = x.shape[:-1]
+    return (idx.reshape(*lead, k), w.reshape(*lead, k),
+            g.reshape(*lead, 1) if g is not None else None)
+
+
 def moe_combine(y: torch.Tensor, w: torch.Tensor, g: torch.Tensor, s: torch.Tensor):
     """y (..., K, D), w (..., K) float32, g (..., 1), s (..., D) -> (..., D) in y's type
     (strata_mlx/fused.py:467-481). None where the types are not the kernel's."""
@@ -115,10 +149,14 @@ class SparseMoeBlock:
         self.top_k = top_k
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        logits = self.gate(x)
-        idx, w = top_k_softmax(logits, self.top_k)
+        r = route(self.gate, self.shared_expert_gate, x, self.top_k)
+        if r is not None:
+            idx, w, g = r
+        else:
+            logits = self.gate(x)
+            idx, w = top_k_softmax(logits, self.top_k)
+            g = self.shared_expert_gate(x).to(x.dtype)
         y = self.switch_mlp(x, idx)
-        g = self.shared_expert_gate(x).to(x.dtype)
         s = self.shared_expert(x)
         out = moe_combine(y, w, g, s)
         if out is None:

@@ -66,6 +66,11 @@ def test_invalid_arguments_are_rejected_on_the_host(lib):
     assert lib.smoe_tiles_of(ctypes.c_void_p(16), 32, 2, 8, ctypes.c_void_p(16), ctypes.c_void_p(16),
                              ctypes.c_void_p(16), None, 0, None) == 5  # SMOE_EWORKSPACE
     assert lib.smoe_top_k(ctypes.c_void_p(16), 1, 4096, 8, ctypes.c_void_p(16), None, None) == 2
+    v = ctypes.c_void_p(16)
+    assert lib.smoe_route(v, None, v, 1, 1, 256, 512, 8, v, v, v, None, None, None) == 4  # no counters
+    assert lib.smoe_route(v, v, v, 1, 1, 256, 512, 8, v, v, v, None, v, None) == 4  # gate weight, no output
+    assert lib.smoe_route(v, None, v, 1, 1, 4096, 512, 8, v, v, v, None, v, None) == 2  # too many experts
+    assert lib.smoe_route_counters(20) == 12
     with pytest.raises(ValueError):
         _lib.call("smoe_dequant", 21, None, 4, 100, None, 1, None)
 

@@ -44,6 +44,28 @@ def test_a_router_product_in_float32_from_float16_weights(cuda, tokens):
         assert torch.equal(alone, got)
 
 
+@pytest.mark.parametrize("tokens", [1, 5, 8, 9, 20])
+@pytest.mark.parametrize("experts, k", [(256, 8), (60, 4), (1024, 16)])
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+@pytest.mark.parametrize("with_gate", [True, False])
+def test_route_in_one_launch_is_the_three_calls(cuda, tokens, experts, k, dtype, with_gate):
+    """The fused start of the block (router, top-k with softmax, shared gate) gives the bits of the separate
+    calls (strata_mlx/fused.py:487-491), call after call (its counters come back to zero)."""
+    rng = np.random.default_rng(tokens * 7 + experts + k)
+    w = dev((0.02 * rng.standard_normal((experts, 512))).astype(np.float16))
+    gw = dev((0.02 * rng.standard_normal((1, 512))).astype(np.float16))
+    router, sgate = F.WindowLinear(w), F.WindowLinear(gw)
+    for trial in range(3):
+        x = dev(rng.standard_normal((tokens, 512)).astype(dtype))
+        idx, wt, g = F.route(router, sgate if with_gate else None, x, k)
+        want_idx, want_w = F.top_k_softmax(router(x), k)
+        assert torch.equal(idx, want_idx) and torch.equal(wt, want_w)
+        if with_gate:
+            assert torch.equal(g, sgate(x).to(x.dtype))
+        else:
+            assert g is None
+
+
 @pytest.mark.parametrize("tokens", [1, 3, 8, 40])
 @pytest.mark.parametrize("ties", [False, True])
 @pytest.mark.parametrize("n, k", [(512, 10), (256, 8), (100, 3)])
