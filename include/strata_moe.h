@@ -88,6 +88,25 @@ SMOE_API int smoe_matvec_glu(int kind, const uint8_t* blocks, int64_t experts, i
                     const uint32_t* idx, int64_t pairs, const void* gate, const void* up, void* out, int dtype,
                     void* stream);
 
+/* Several products of the decode path in one launch (the routed experts' gate and up with the shared
+ * expert's gate and up; or the two down products): each problem is an smoe_matvec (x set, gate and up null)
+ * or an smoe_matvec_glu (x null, gate and up set; share is then 1). Problems that name the same activations
+ * read them once. All n problems are done when the call returns to the stream, in one int8 tensor-core launch
+ * when it takes all of them (float16 activations, IQ3_S / Q8_0, n <= 4), else one launch per problem.
+ * No single reference counterpart: it batches the calls of `_Routed.__call__` (strata_mlx/fused.py:492-494)
+ * that do not depend on one another. */
+typedef struct SmoeMatvec {
+    int kind;
+    const uint8_t* blocks;
+    int64_t experts, rows, cols;
+    const uint32_t* idx;
+    int64_t pairs, share;
+    const void *x, *gate, *up;
+    void* out;
+    int dtype;
+} SmoeMatvec;
+SMOE_API int smoe_matvec_batch(int n, const SmoeMatvec* problems, void* stream);
+
 /* h = swiglu(gate, up) elementwise over n values of `dtype`: mlx-lm's `swiglu` as restated at
  * strata_mlx/blocks.py:222-237 (the unfused form `down(swiglu(g, u), indices)`, blocks.py:976). */
 SMOE_API int smoe_swiglu(const void* gate, const void* up, int64_t n, void* out, int dtype, void* stream);

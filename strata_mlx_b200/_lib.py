@@ -18,6 +18,15 @@ ETIMEOUT = 6
 _c = ctypes
 _p, _i, _i64, _sz = _c.c_void_p, _c.c_int, _c.c_int64, _c.c_size_t
 
+
+
+class SmoeMatvec(ctypes.Structure):
+    """`SmoeMatvec` of include/strata_moe.h: one problem of smoe_matvec_batch."""
+
+    _fields_ = [("kind", _i), ("blocks", _p), ("experts", _i64), ("rows", _i64), ("cols", _i64), ("idx", _p),
+                ("pairs", _i64), ("share", _i64), ("x", _p), ("gate", _p), ("up", _p), ("out", _p), ("dtype", _i)]
+
+
 # name -> (restype, argtypes): the declarations of include/strata_moe.h
 SIGNATURES = {
     "smoe_last_error": (_c.c_char_p, []),
@@ -28,6 +37,7 @@ SIGNATURES = {
     "smoe_matvec": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _i, _p]),
     "smoe_matvec_gate_up": (_i, [_i, _p, _i, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i, _p]),
     "smoe_matvec_glu": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _i, _p]),
+    "smoe_matvec_batch": (_i, [_i, _c.POINTER(SmoeMatvec), _p]),
     "smoe_swiglu": (_i, [_p, _p, _i64, _p, _i, _p]),
     "smoe_router_logits": (_i, [_p, _p, _i, _i64, _i64, _i64, _p, _p]),
     "smoe_top_k": (_i, [_p, _i64, _i64, _i64, _p, _p, _p]),

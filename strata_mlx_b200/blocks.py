@@ -298,6 +298,54 @@ def switch_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.
     return out.reshape(*indices.shape, down.output_dims)
 
 
+def _problem(lin, idx, pairs, share, out, x=None, gate=None, up=None):
+    return _lib.SmoeMatvec(_kind(lin.kind), lin.blocks.data_ptr(), lin.num_experts, lin.output_dims, lin.input_dims,
+                           idx.data_ptr(), pairs, share, x.data_ptr() if x is not None else None,
+                           gate.data_ptr() if gate is not None else None, up.data_ptr() if up is not None else None,
+                           out.data_ptr(), _lib.dtype_code(out.dtype))
+
+
+def matvec_batch(problems) -> None:
+    """Run several products in one smoe_matvec_batch call (each an smoe_matvec or smoe_matvec_glu problem)."""
+    arr = (_lib.SmoeMatvec * len(problems))(*problems)
+    _lib.call("smoe_matvec_batch", len(problems), arr, _lib.stream())
+
+
+def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor):
+    """(switch_mlp(x, indices), shared(x)) for a step that runs both on the decode matvec, with the routed and
+    the shared expert's gate and up products in one launch (the same products, within the kernel's rounding,
+    as the separate calls), then the two down products. None where either would take another path (a
+    prompt's tiles, unpacked floats, a SwiGLU the down product does not take, activations of another type)."""
+    lins = (switch_mlp.gate_proj, switch_mlp.up_proj, switch_mlp.down_proj)
+    slins = (shared.gate_proj, shared.up_proj, shared.down_proj)
+    if x.dtype != torch.float16 or indices.numel() >= TILES_FROM or not BLOCK_GLU:
+        return None
+    k = indices.shape[-1]
+    idx = _flat_idx(indices)
+    x2 = x.reshape(-1, x.shape[-1]).contiguous()
+    tokens, pairs = x2.shape[0], idx.numel()
+    if (pairs != tokens * k or pairs > MATVEC_GLU_UPTO or pairs >= min(lin.unpack_from for lin in lins)
+            or any(lin.gemm(x2) for lin in slins)):
+        return None
+    _lib.require_cuda(x, indices, *(lin.blocks for lin in lins), *(lin.blocks for lin in slins))
+    dev, dt = x.device, x.dtype
+    gate, up, down = lins
+    sg, su, sd = (lin.stack for lin in slins)
+    zeros = _zeros_idx(tokens, dev)
+    g = torch.empty((pairs, gate.output_dims), dtype=dt, device=dev)
+    u = torch.empty((pairs, up.output_dims), dtype=dt, device=dev)
+    gs = torch.empty((tokens, sg.output_dims), dtype=dt, device=dev)
+    us = torch.empty((tokens, su.output_dims), dtype=dt, device=dev)
+    if pairs:
+        matvec_batch([_problem(gate, idx, pairs, k, g, x=x2), _problem(up, idx, pairs, k, u, x=x2),
+                      _problem(sg, zeros, tokens, 1, gs, x=x2), _problem(su, zeros, tokens, 1, us, x=x2)])
+    # the two down products stay separate launches: in one launch the shared expert's long rows (4096 columns)
+    # are the slowest warps' work and the pair is slower than the two alone
+    y = matvec_glu(down, idx, g, u)
+    s = matvec_glu(sd, zeros, gs, us)
+    return y.reshape(*indices.shape, down.output_dims), s.reshape(*x.shape[:-1], sd.output_dims)
+
+
 class BlockSwitchGLU:
     """A layer's routed experts, called like mlx-lm's `SwitchGLU` (strata_mlx/blocks.py:989-996)."""
 

@@ -1,0 +1,30 @@
+// The int8 tensor-core decode matvec (smoe_mv8.cu) as the entry points of smoe_blocks.cu call it.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace smoe {
+
+// One matvec problem: out[p, r] = W[idx[p], r, :] . a[p / share, :], a = x, or the SwiGLU of (gate, up).
+struct M8Spec {
+    int kind;
+    const uint8_t* blocks;
+    int64_t experts, rows, cols, row_bytes;
+    const uint32_t* idx;
+    int64_t pairs, share;
+    const __half *x, *gate, *up;
+    __half* out;
+};
+
+// n <= 4 problems in one launch: 0 launched, 1 not taken (the caller runs them another way), else an error.
+int mv8_batch(int n, const M8Spec* specs, cudaStream_t st);
+
+// the gate / up problems (nprob 1 or 2) of one stack pair: 0 launched, 1 not taken, else an error
+int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
+            int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, const __half* gate,
+            const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st);
+
+}  // namespace smoe

@@ -6,6 +6,7 @@
 // shared-memory slots with 16-byte cp.async copies (coalesced, all issued up front so every warp has several
 // KB in flight), then its lanes decode runs of 32 weights in registers and reduce with warp shuffles.
 #include "blocks.cuh"
+#include "mv8.cuh"
 
 namespace smoe {
 
@@ -126,10 +127,6 @@ __global__ void swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u, 
 
 // ---------------------------------------------------------------- host side
 
-// the int8 tensor-core decode matvec (smoe_mv8.cu): 0 launched, 1 not taken, else an error status
-int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
-            int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, const __half* gate,
-            const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st);
 // the float16 tensor-core decode matvec (smoe_mv.cu), for what the int8 one does not take
 int mv_mma_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
                int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, __half* o0,
@@ -245,6 +242,51 @@ extern "C" int smoe_matvec(int kind, const uint8_t* blocks, int64_t experts, int
         return matvec_common<float>(kind, blocks, kind, nullptr, experts, rows, cols, idx, pairs, share, x, nullptr,
                                     nullptr, out, nullptr, 1, as_stream(stream));
     return fail(SMOE_EDTYPE, "activations must be float16 or float32");
+}
+
+extern "C" int smoe_matvec_batch(int n, const SmoeMatvec* pr, void* stream) {
+    SMOE_REQUIRE(n >= 0 && n <= 64, SMOE_EARG, "a batch holds 0 to 64 problems");
+    if (n == 0) return SMOE_OK;
+    SMOE_REQUIRE(pr != nullptr, SMOE_EARG, "null problem list");
+    // every problem checked as its own entry point checks it, before any launch
+    M8Spec spec[4];
+    int m = 0;
+    bool one_launch = n <= 4;
+    for (int i = 0; i < n; ++i) {
+        const SmoeMatvec& p = pr[i];
+        int per, bytes;
+        if (int s = check_stack(p.kind, p.experts, p.rows, p.cols, per, bytes)) return s;
+        SMOE_REQUIRE(p.pairs >= 0, SMOE_EARG, "negative pair count");
+        SMOE_REQUIRE((p.x != nullptr) != (p.gate != nullptr && p.up != nullptr), SMOE_EARG,
+                     "a problem has x, or gate and up");
+        SMOE_REQUIRE(p.dtype == SMOE_F16 || p.dtype == SMOE_F32, SMOE_EDTYPE, "activations must be float16 or float32");
+        if (p.pairs == 0) continue;
+        SMOE_REQUIRE(p.blocks && p.idx && p.out, SMOE_EARG, "null pointer");
+        SMOE_REQUIRE(p.x == nullptr || p.share >= 1, SMOE_EARG, "share must be >= 1");
+        if (p.dtype != SMOE_F16) one_launch = false;
+        if (one_launch)
+            spec[m++] = M8Spec{p.kind, p.blocks, p.experts, p.rows, p.cols, p.cols / per * bytes, p.idx, p.pairs,
+                               p.x ? p.share : 1, static_cast<const __half*>(p.x), static_cast<const __half*>(p.gate),
+                               static_cast<const __half*>(p.up), static_cast<__half*>(p.out)};
+    }
+    cudaStream_t st = as_stream(stream);
+    if (one_launch && m > 0) {
+        const M8Spec& a = spec[0];
+        const int r = m == 1 ? mv8_try(a.kind, a.kind, a.blocks, a.blocks, a.experts, a.rows, a.cols, a.row_bytes, a.idx,
+                                       a.pairs, a.share, a.x, a.gate, a.up, a.out, a.out, 1, st)
+                             : mv8_batch(m, spec, st);
+        if (r != 1) return r;
+    }
+    for (int i = 0; i < n; ++i) {
+        const SmoeMatvec& p = pr[i];
+        if (p.pairs == 0) continue;
+        const int r = p.x ? smoe_matvec(p.kind, p.blocks, p.experts, p.rows, p.cols, p.idx, p.pairs, p.share, p.x,
+                                        p.out, p.dtype, stream)
+                          : smoe_matvec_glu(p.kind, p.blocks, p.experts, p.rows, p.cols, p.idx, p.pairs, p.gate,
+                                            p.up, p.out, p.dtype, stream);
+        if (r) return r;
+    }
+    return SMOE_OK;
 }
 
 extern "C" int smoe_matvec_gate_up(int gate_kind, const uint8_t* gate_blocks, int up_kind, const uint8_t* up_blocks,

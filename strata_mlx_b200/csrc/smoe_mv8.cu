@@ -22,10 +22,13 @@
 // shared-memory slots, and reads every field at a warp-uniform offset.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 #include "blocks.cuh"
+#include "mv8.cuh"
 #include "tc05.cuh"
 
 namespace smoe {
@@ -141,6 +144,10 @@ struct M8Q8_0 {
     }
 };
 
+// ---------------------------------------------------------------- one stack (or a gate / up pair)
+// The kernel the single entry points use: its geometry (stage, row stride) is the block type's, known at
+// compile time.
+
 struct M8Args {
     const uint32_t* idx;
     const __half* x;
@@ -156,28 +163,28 @@ struct M8Args {
 };
 // a job's place (worked out once per job, 32-bit): problem, pair, expert, the tile's residue class and block
 // of 16 q rows, the first row of its TMA box, the activation row
-struct alignas(8) M8Where {
+struct alignas(8) M8WhereS {
     int prob, cls, blk, xr, pair;
     uint32_t e;
     int y, pad;
 };
-constexpr int kM8MaskRows = 1024;  // activation rows a CTA can mark as needed
-constexpr int kM8WhereBytes = kM8Warps * 4 * int(sizeof(M8Where)) + kM8MaskRows / 8;
+constexpr int kM8SMaskRows = 1024;  // activation rows a CTA can mark as needed
+constexpr int kM8WhereSBytes = kM8Warps * 4 * int(sizeof(M8WhereS)) + kM8SMaskRows / 8;
 
-struct alignas(64) M8Maps {
+struct alignas(64) M8Maps2 {
     CUtensorMap w[2];
 };
 
 template <class D>
-__global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, const __grid_constant__ M8Maps maps) {
+__global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, const __grid_constant__ M8Maps2 maps) {
     extern __shared__ __align__(128) uint8_t sm[];
     constexpr int kSlot = 16 * D::kRS;
     const int ns = a.nslots;
     uint8_t* ring = sm;                                                         // [warp][slot] 16 rows x kRS
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * kSlot);  // [warp][slot]
     float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);       // [16 warps][16 rows]
-    M8Where* where_ring = reinterpret_cast<M8Where*>(red + kM8Warps * 16);       // [16 warps][4]
-    uint32_t* lut = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(where_ring) + kM8WhereBytes);  // 8192 words
+    M8WhereS* where_ring = reinterpret_cast<M8WhereS*>(red + kM8Warps * 16);       // [16 warps][4]
+    uint32_t* lut = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(where_ring) + kM8WhereSBytes);  // 8192 words
     const int xblocks = static_cast<int>(a.cols / kM8XBlock);
     float* xscale = reinterpret_cast<float*>(lut + (D::kLut ? 8192 : 0));        // [xrows][xblocks]
     int8_t* xhi = reinterpret_cast<int8_t*>(xscale + ((a.xrows * xblocks + 3) & ~3));  // [xrows][cols]
@@ -204,7 +211,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
     }
     __syncwarp();
 
-    using Where = M8Where;
+    using Where = M8WhereS;
     auto locate = [&](int job) {
         const int j = q0 + job * nteams;
         Where w;
@@ -262,11 +269,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
         uint4* dst = reinterpret_cast<uint4*>(lut);
         for (int i = threadIdx.x; i < 8192 / 4; i += kM8Threads) dst[i] = __ldg(src + i);
     }
-    // the activation rows this CTA's jobs read (all of them when there are more than kM8MaskRows)
-    uint32_t* need = reinterpret_cast<uint32_t*>(where_ring + kM8Warps * 4);  // kM8MaskRows bits
-    const bool masked = a.xrows <= kM8MaskRows;
+    // the activation rows this CTA's jobs read (all of them when there are more than kM8SMaskRows)
+    uint32_t* need = reinterpret_cast<uint32_t*>(where_ring + kM8Warps * 4);  // kM8SMaskRows bits
+    const bool masked = a.xrows <= kM8SMaskRows;
     if (masked) {
-        for (int i = threadIdx.x; i < kM8MaskRows / 32; i += kM8Threads) need[i] = 0u;
+        for (int i = threadIdx.x; i < kM8SMaskRows / 32; i += kM8Threads) need[i] = 0u;
         __syncthreads();
         if (lane == 0 && my_stages > 0)
             for (int job = 0; job < my_jobs; ++job) {
@@ -381,6 +388,282 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const M8Args a, cons
     __syncwarp();
 }
 
+// ---------------------------------------------------------------- several stacks in one launch
+// The same work for up to four problems of either type (the decode step's routed and shared gate / up
+// products): a job's problem, its type and geometry are read per job.
+
+// One stack's products in a launch: its pairs (expert idx[p], activation row p / share of source xs) times
+// its row tiles. Two stacks that share pairs and activations (gate and up) are two problems.
+struct M8Prob {
+    const uint32_t* idx;
+    __half* out;
+    int64_t rows, row_bytes;
+    uint32_t experts;
+    int kind;                     // 21 IQ3_S, 8 Q8_0
+    int stage_cols, stage_bytes;  // a stage of one row
+    int rs;                       // its rows' stride in a ring slot (an odd number of 16-byte chunks)
+    int q, lq;                    // rows per 16-byte aligned group of rows (a power of two) and its log2
+    int tiles, stages;            // tiles of 16 rows (of one residue class) per pair, stages per row
+    int job0, jobs;               // its jobs in the launch: [job0, job0 + jobs)
+    int pairs, share, xs;         // pairs, pairs per activation row, activation source
+    int idx0;                     // its first pair in the shared-memory copy of the expert indices
+};
+// An activation source: rows of `cols` float16, or the SwiGLU of two such (down's input).
+struct M8X {
+    const __half *x, *gate, *up;
+    int rows, cols;
+    int row0;    // its first row among all sources' rows
+    int scale0;  // its first block scale
+    int64_t byte0;  // its hi values' offset in the split area (its lo values follow rows x cols later)
+};
+constexpr int kM8MaxProbs = 4, kM8MaxX = 4;
+constexpr int kM8MaxRows = 1024;  // activation rows of all sources, and pairs of all problems
+struct M8Launch {
+    M8Prob p[kM8MaxProbs];
+    M8X x[kM8MaxX];
+    int nprob, nx, jobs, team, nslots, slot_bytes, lut, pairs, scales;
+    int64_t xbytes;
+};
+struct alignas(64) M8Maps {
+    CUtensorMap w[kM8MaxProbs];
+};
+// a job's place: problem, pair, expert, the tile's residue class and block of 16 q rows, the first row of its
+// TMA box, the activation row (among all sources')
+struct M8Where {
+    int prob, cls, blk, xr, pair, y;
+    uint32_t e;
+};
+
+__global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constant__ M8Launch L,
+                                                            const __grid_constant__ M8Maps maps) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int ns = L.nslots, slot_bytes = L.slot_bytes;
+    uint8_t* ring = sm;                                                                   // [warp][slot]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * slot_bytes);  // [warp][slot]
+    float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);                 // [16 warps][16 rows]
+    uint32_t* sidx = reinterpret_cast<uint32_t*>(red + kM8Warps * 16);                    // [kM8MaxRows]
+    uint32_t* need = sidx + kM8MaxRows;                                                   // kM8MaxRows bits
+    uint32_t* lut = need + kM8MaxRows / 32;                                               // 8192 words (IQ3_S)
+    float* xscale = reinterpret_cast<float*>(lut + (L.lut ? 8192 : 0));
+    int8_t* xsplit = reinterpret_cast<int8_t*>(xscale + ((L.scales + 3) & ~3));
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gid = lane >> 2, tig = lane & 3;
+    if (smem_addr(sm) & 127u) return;  // a tiled copy's destination is 128-byte aligned (the launch gives that)
+    const int team = L.team, teams = kM8Warps / team;
+    const int tid_team = warp / team, kq = warp % team;
+    const int nteams = gridDim.x * teams;
+    const int q0 = blockIdx.x * teams + tid_team;
+    const int my_jobs = q0 < L.jobs ? (L.jobs - q0 + nteams - 1) / nteams : 0;
+    uint8_t* my_ring = ring + size_t(warp) * ns * slot_bytes;
+    uint64_t* my_bars = bars + warp * kM8MaxSlots;
+
+    // the expert indices of every problem's pairs, once, in shared memory (a job's place needs no global load)
+    for (int pr = 0; pr < L.nprob; ++pr)
+        for (int i = threadIdx.x; i < L.p[pr].pairs; i += kM8Threads) sidx[L.p[pr].idx0 + i] = L.p[pr].idx[i];
+    if (lane == 0) {
+        for (int i = 0; i < ns; ++i) tc::mbar_init(&my_bars[i], 1);
+        tc::fence_barrier_init();
+    }
+    for (int i = threadIdx.x; i < kM8MaxRows / 32; i += kM8Threads) need[i] = 0u;
+    __syncthreads();
+
+    auto locate = [&](int job) {
+        const int j = q0 + job * nteams;
+        M8Where w;
+        w.prob = 0;
+#pragma unroll
+        for (int pr = 1; pr < kM8MaxProbs; ++pr)
+            if (pr < L.nprob && j >= L.p[pr].job0) w.prob = pr;
+        const M8Prob& P = L.p[w.prob];
+        const int rest = j - P.job0;
+        w.pair = rest / P.tiles;
+        const int tile = rest - w.pair * P.tiles;
+        w.cls = tile & (P.q - 1);
+        w.blk = tile >> P.lq;
+        w.e = sidx[P.idx0 + w.pair];
+        w.y = static_cast<int>((int64_t(w.e < P.experts ? w.e : 0) * P.rows) >> P.lq) + 16 * w.blk;
+        w.xr = L.x[P.xs].row0 + w.pair / P.share;
+        return w;
+    };
+    auto stages_of = [&](int prob) {
+        const int S = L.p[prob].stages;
+        return S > kq ? (S - kq + team - 1) / team : 0;
+    };
+
+    // the copy cursor (lane 0): the next item (a job's stage) to copy, its slot; it skips jobs in which this
+    // warp has no stage
+    int pre_job = 0, pre_k = 0, pre_slot = 0, pre_s = kq;
+    M8Where pre_w{};
+    int pre_n = 0;
+    auto seek = [&]() {  // from pre_job on, the first job with a stage for this warp
+        for (; pre_job < my_jobs; ++pre_job) {
+            pre_w = locate(pre_job);
+            pre_n = stages_of(pre_w.prob);
+            if (pre_n > 0) break;
+        }
+    };
+    // lane 0 starts the TMA copy of the cursor's item into its slot and moves the cursor on; a pair naming no
+    // expert copies nothing and completes the slot's phase with a plain arrive, so every item takes one phase
+    auto issue = [&]() {
+        if (pre_job >= my_jobs) return;
+        const M8Prob& P = L.p[pre_w.prob];
+        if (pre_w.e >= P.experts) {
+            tc::mbar_arrive(&my_bars[pre_slot]);
+        } else {
+            const int xb = (pre_w.cls * static_cast<int>(P.row_bytes) + pre_s * P.stage_bytes) & ~15;
+            tc::fence_proxy_async_smem();
+            tc::mbar_arrive_expect_tx(&my_bars[pre_slot], static_cast<uint32_t>(16 * P.rs));
+            tc::tma_load_2d(smem_addr(my_ring + pre_slot * slot_bytes), &maps.w[pre_w.prob], xb >> 2, pre_w.y,
+                            &my_bars[pre_slot]);
+        }
+        if (++pre_slot == ns) pre_slot = 0;
+        pre_s += team;
+        if (++pre_k == pre_n) {
+            pre_k = 0;
+            pre_s = kq;
+            ++pre_job;
+            seek();
+        }
+    };
+    if (lane == 0) {
+        seek();
+        for (int i = 0; i < ns - 1; ++i) issue();
+    }
+
+    if (L.lut) {
+        // grid value x sign, entry g | s << 9 (built from gguf-py's grid with the rest of the tables): 32 KB
+        // copied in 16-byte pieces
+        const uint4* src = reinterpret_cast<const uint4*>(kIq3sSigned);
+        uint4* dst = reinterpret_cast<uint4*>(lut);
+        for (int i = threadIdx.x; i < 8192 / 4; i += kM8Threads) dst[i] = __ldg(src + i);
+    }
+    // the activation rows this CTA's jobs read
+    if (lane == 0)
+        for (int job = 0; job < my_jobs; ++job) {
+            const int xr = locate(job).xr;
+            atomicOr(&need[xr >> 5], 1u << (xr & 31));
+        }
+    __syncthreads();
+    // the activations, split per 256-column block into int8 hi and lo: a warp per block, 8 values a lane
+    for (int src = 0; src < L.nx; ++src) {
+        const M8X& X = L.x[src];
+        const int xblocks = X.cols / kM8XBlock;
+        for (int blk = warp; blk < X.rows * xblocks; blk += kM8Warps) {
+            const int xr = blk / xblocks, b = blk - xr * xblocks;
+            const int grow = X.row0 + xr;
+            if (!((need[grow >> 5] >> (grow & 31)) & 1u)) continue;
+            const int64_t c0 = int64_t(b) * kM8XBlock + 8 * lane;
+            float v[8];
+            if (X.gate) {
+                // the SwiGLU of the gate and up products, the same function (so the same float16 bits) as the
+                // separate kernel
+                const uint4 gr = *reinterpret_cast<const uint4*>(X.gate + int64_t(xr) * X.cols + c0);
+                const uint4 ur = *reinterpret_cast<const uint4*>(X.up + int64_t(xr) * X.cols + c0);
+                const __half* gh = reinterpret_cast<const __half*>(&gr);
+                const __half* uh = reinterpret_cast<const __half*>(&ur);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = __half2float(swiglu_one(gh[i], uh[i]));
+            } else {
+                const uint4 raw = *reinterpret_cast<const uint4*>(X.x + int64_t(xr) * X.cols + c0);
+                const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float2 f = __half22float2(h2[i]);
+                    v[2 * i] = f.x;
+                    v[2 * i + 1] = f.y;
+                }
+            }
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float sc = amax / 127.0f, inv = amax > 0.f ? 127.0f / amax : 0.f;
+            uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float hf = fminf(fmaxf(rintf(v[i] * inv), -127.f), 127.f);
+                const float lf = fminf(fmaxf(rintf((v[i] - hf * sc) * (128.0f * inv)), -127.f), 127.f);
+                hw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(hf)) & 255u) << (8 * (i & 3));
+                lw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(lf)) & 255u) << (8 * (i & 3));
+            }
+            int8_t* hi = xsplit + X.byte0 + int64_t(xr) * X.cols + c0;
+            *reinterpret_cast<uint2*>(hi) = make_uint2(hw[0], hw[1]);
+            *reinterpret_cast<uint2*>(hi + int64_t(X.rows) * X.cols) = make_uint2(lw[0], lw[1]);
+            if (lane == 0) xscale[X.scale0 + blk] = sc;
+        }
+    }
+    __syncthreads();
+
+    // a team of one warp needs no named barrier (there are 16, barrier 0 is __syncthreads')
+    auto team_sync = [&]() {
+        if (team == 1) __syncwarp();
+        else asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid_team), "r"(32 * team) : "memory");
+    };
+    // a wait that gives up (it should not) leaves the warp's remaining stages undone but keeps it in step
+    // with its team's barriers
+    bool ok = true;
+    float total[2] = {0.f, 0.f};
+    int slot = 0, waited = 0;
+    uint32_t phase = 0;
+    for (int job = 0; job < my_jobs; ++job) {
+        const M8Where w = locate(job);
+        const M8Prob& P = L.p[w.prob];
+        const M8X& X = L.x[P.xs];
+        const int lx = w.xr - X.row0;
+        const uint8_t* xh = reinterpret_cast<const uint8_t*>(xsplit) + X.byte0 + int64_t(lx) * X.cols;
+        const uint8_t* xl = xh + int64_t(X.rows) * X.cols;
+        const float* xsc = xscale + X.scale0 + lx * (X.cols / kM8XBlock);
+        const int n = stages_of(w.prob);
+        int s = kq;
+        for (int k = 0; k < n; ++k, s += team) {
+            // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
+            __syncwarp();
+            if (lane == 0) issue();
+            const int cur = slot;
+            if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, kM8WaitLimit));
+            ++waited;
+            if (++slot == ns) {
+                slot = 0;
+                phase ^= 1;
+            }
+            if (!ok || w.e >= P.experts) continue;
+            const int off = (w.cls * static_cast<int>(P.row_bytes) + s * P.stage_bytes) & 15;
+            const uint8_t* st = my_ring + cur * slot_bytes + off;
+            const int xc = s * P.stage_cols;
+            if (P.kind == M8IQ3S::kKind)
+                M8IQ3S::stage(st + gid * M8IQ3S::kRS, st + (gid + 8) * M8IQ3S::kRS, tig, gid, lut, xh + xc, xl + xc,
+                              xsc[xc / kM8XBlock], total);
+            else
+                M8Q8_0::stage(st + gid * M8Q8_0::kRS, st + (gid + 8) * M8Q8_0::kRS, tig, gid, lut, xh + xc, xl + xc,
+                              xsc[xc / kM8XBlock], total);
+        }
+        // the team's partial sums of this job's 16 rows, added in warp order
+        float* rq = red + (tid_team * team) * 16;
+        if (tig == 0) {
+            rq[kq * 16 + gid] = total[0];
+            rq[kq * 16 + gid + 8] = total[1];
+        }
+        total[0] = total[1] = 0.f;
+        team_sync();
+        if (kq == 0 && lane < 16) {
+            const int64_t row = int64_t(w.blk) * 16 * P.q + w.cls + int64_t(P.q) * lane;
+            if (w.e < P.experts && row < P.rows) {
+                float v = rq[lane];
+                for (int i = 1; i < team; ++i) v += rq[16 * i + lane];
+                P.out[int64_t(w.pair) * P.rows + row] = __float2half_rn(v);
+            }
+        }
+        team_sync();
+    }
+    // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
+    // a wait gave up)
+    if (!ok && lane == 0)
+        for (int i = 0; i < waited + ns; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
+    __syncwarp();
+}
+
 typedef CUresult (*M8EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -402,7 +685,7 @@ static int g_m8_sms = 0;
 
 // Launch the int8 tensor-core decode matvec when it takes the problem: 0 launched, 1 not taken, else an error.
 // x, or (gate, up) whose SwiGLU is the activations.
-int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
+int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
             int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, const __half* gate,
             const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st) {
     if (kind0 != kind1) return 1;
@@ -421,7 +704,7 @@ int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t 
         const int64_t xrows = (pairs + share - 1) / share;
         const int xblocks = static_cast<int>(cols / kM8XBlock);
         const size_t xbytes = size_t(((xrows * xblocks + 3) & ~int64_t(3)) * 4) + size_t(xrows * cols * 2);
-        const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + kM8WhereBytes +
+        const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + kM8WhereSBytes +
                              (D::kLut ? 8192 * 4 : 0) + xbytes;
         const size_t slot = size_t(kM8Warps) * 16 * D::kRS;
         int ns = kM8MaxSlots;
@@ -429,7 +712,7 @@ int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t 
         if (fixed + ns * slot > size_t(227 * 1024)) return 1;
         M8EncodeFn encode = m8_encoder();
         if (!encode) return 1;
-        M8Maps maps;
+        M8Maps2 maps;
         const uint8_t* bl[2] = {b0, b1};
         for (int p = 0; p < 2; ++p) {
             const cuuint64_t dims[2] = {static_cast<cuuint64_t>(q * row_bytes / 4),
@@ -489,13 +772,176 @@ int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t 
         const int64_t want = (jobs + teams - 1) / teams;
         const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, g_m8_sms)));
         const size_t smem = fixed + ns * slot;
-        if (int s = max_smem(mv8_kernel<D>, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
-        mv8_kernel<D><<<grid, kM8Threads, smem, st>>>(a, maps);
+        if (int s = max_smem(mv8s_kernel<D>, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
+        mv8s_kernel<D><<<grid, kM8Threads, smem, st>>>(a, maps);
         return launch_status("matvec (int8 tensor cores)");
     };
     if (kind0 == M8IQ3S::kKind) return go(M8IQ3S{});
     if (kind0 == M8Q8_0::kKind) return go(M8Q8_0{});
     return 1;
+}
+
+
+// Launch several matvec problems as one int8 tensor-core kernel: 0 launched, 1 not taken (the caller runs
+// them another way), else an error status. Problems with the same activation pointers share one source.
+int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
+    if (n < 1 || n > kM8MaxProbs) return 1;
+    // the problems in order of falling cost per job (bytes of a 16-row tile), so that the round-robin of jobs
+    // over teams hands the big jobs out first
+    M8Spec specs[kM8MaxProbs];
+    for (int i = 0; i < n; ++i) specs[i] = specs_in[i];
+    auto job_bytes = [](const M8Spec& sp) { return sp.row_bytes * 16; };
+    for (int i = 1; i < n; ++i)
+        for (int j = i; j > 0 && job_bytes(specs[j]) > job_bytes(specs[j - 1]); --j) std::swap(specs[j], specs[j - 1]);
+    M8EncodeFn encode = m8_encoder();
+    if (!encode) return 1;
+    M8Launch L{};
+    M8Maps maps;
+    int jobs = 0, pairs = 0, rows = 0, scales = 0;
+    int64_t xbytes = 0;
+    bool lut = false;
+    int max_rs = 0;
+    for (int i = 0; i < n; ++i) {
+        const M8Spec& sp = specs[i];
+        int stage_cols, stage_bytes, rs;
+        if (sp.kind == M8IQ3S::kKind) {
+            stage_cols = M8IQ3S::kStageCols, stage_bytes = M8IQ3S::kStageBytes, rs = M8IQ3S::kRS;
+            lut = true;
+        } else if (sp.kind == M8Q8_0::kKind) {
+            stage_cols = M8Q8_0::kStageCols, stage_bytes = M8Q8_0::kStageBytes, rs = M8Q8_0::kRS;
+        } else {
+            return 1;
+        }
+        if (sp.cols % kM8XBlock || sp.cols % stage_cols || sp.pairs <= 0 || sp.share < 1) return 1;
+        const __half* xp = sp.x ? sp.x : sp.gate;
+        if ((reinterpret_cast<uintptr_t>(sp.x) & 15) || (reinterpret_cast<uintptr_t>(sp.gate) & 15) ||
+            (reinterpret_cast<uintptr_t>(sp.up) & 15) || (reinterpret_cast<uintptr_t>(sp.blocks) & 15) ||
+            (sp.gate != nullptr) != (sp.up != nullptr) || (sp.gate == nullptr) == (sp.x == nullptr))
+            return 1;
+        int gcd = 16;
+        while (sp.row_bytes % gcd) gcd >>= 1;
+        const int q = 16 / gcd;
+        if (sp.rows % q || sp.experts * sp.rows / q >= (int64_t(1) << 31) || q * sp.row_bytes >= (int64_t(1) << 27))
+            return 1;
+        // the activation source: an earlier problem's if it names the same activations
+        int xs = -1;
+        for (int j = 0; j < L.nx; ++j)
+            if (L.x[j].x == sp.x && L.x[j].gate == sp.gate && L.x[j].up == sp.up && L.x[j].cols == sp.cols)
+                xs = j;
+        const int64_t xrows = (sp.pairs + sp.share - 1) / sp.share;
+        if (xs < 0) {
+            if (L.nx == kM8MaxX) return 1;
+            xs = L.nx++;
+            M8X& X = L.x[xs];
+            X.x = sp.x;
+            X.gate = sp.gate;
+            X.up = sp.up;
+            X.rows = static_cast<int>(xrows);
+            X.cols = static_cast<int>(sp.cols);
+            X.row0 = rows;
+            X.scale0 = scales;
+            X.byte0 = xbytes;
+            rows += X.rows;
+            scales += X.rows * static_cast<int>(sp.cols / kM8XBlock);
+            xbytes += 2 * xrows * sp.cols;
+        } else if (L.x[xs].rows < xrows) {
+            return 1;
+        }
+        (void)xp;
+        M8Prob& P = L.p[i];
+        P.idx = sp.idx;
+        P.out = sp.out;
+        P.rows = sp.rows;
+        P.row_bytes = sp.row_bytes;
+        P.experts = static_cast<uint32_t>(sp.experts);
+        P.kind = sp.kind;
+        P.stage_cols = stage_cols;
+        P.stage_bytes = stage_bytes;
+        P.rs = rs;
+        P.q = q;
+        P.lq = q == 1 ? 0 : q == 2 ? 1 : q == 4 ? 2 : q == 8 ? 3 : 4;
+        P.tiles = static_cast<int>((sp.rows + 16 * q - 1) / (16 * q)) * q;
+        P.stages = static_cast<int>(sp.cols / stage_cols);
+        P.pairs = static_cast<int>(sp.pairs);
+        P.share = static_cast<int>(sp.share);
+        P.xs = xs;
+        P.idx0 = pairs;
+        P.job0 = jobs;
+        const int64_t pj = int64_t(P.pairs) * P.tiles;
+        if (pj + jobs > (int64_t(1) << 30)) return 1;
+        P.jobs = static_cast<int>(pj);
+        jobs += P.jobs;
+        pairs += P.pairs;
+        max_rs = std::max(max_rs, rs);
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(q * sp.row_bytes / 4),
+                                    static_cast<cuuint64_t>(sp.experts * sp.rows / q)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(q * sp.row_bytes)};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(rs / 4), 16};
+        const cuuint32_t estr[2] = {1, 1};
+        if (encode(&maps.w[i], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(sp.blocks), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return 1;
+    }
+    if (rows > kM8MaxRows || pairs > kM8MaxRows) return 1;
+    L.nprob = n;
+    L.jobs = jobs;
+    L.pairs = pairs;
+    L.scales = scales;
+    L.xbytes = xbytes;
+    L.lut = lut ? 1 : 0;
+    L.slot_bytes = 16 * max_rs;
+    const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + kM8MaxRows * 4 + kM8MaxRows / 8 +
+                         (lut ? 8192 * 4 : 0) + size_t((scales + 3) & ~3) * 4 + size_t(xbytes);
+    const size_t slot = size_t(kM8Warps) * L.slot_bytes;
+    int ns = kM8MaxSlots;
+    while (ns > 2 && fixed + ns * slot > size_t(227 * 1024)) --ns;
+    if (fixed + ns * slot > size_t(227 * 1024)) return 1;
+    L.nslots = ns;
+    if (g_m8_sms == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_m8_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_m8_sms <= 0) g_m8_sms = 148;
+    }
+    // the team size with the least work on the busiest warp: jobs go round-robin over the teams in problem
+    // order; a warp's share of a job is its stages' bytes, plus about 3/4 of a stage for the team's reduction
+    // when the team has more than one warp
+    int team = 1;
+    int64_t best = -1;
+    std::vector<int64_t> load;
+    for (int t = 1; t <= kM8Warps; t *= 2) {
+        const int64_t nteams = int64_t(g_m8_sms) * (kM8Warps / t);
+        load.assign(static_cast<size_t>(std::min<int64_t>(nteams, jobs)), 0);
+        int64_t j = 0;
+        for (int i = 0; i < n; ++i) {
+            const M8Prob& P = L.p[i];
+            const int64_t sb = int64_t(16) * P.stage_bytes;
+            const int64_t w = (P.stages + t - 1) / t * sb * 4 + (t > 1 ? 3 * sb : 0);
+            for (int64_t k = 0; k < P.jobs; ++k, ++j) load[static_cast<size_t>(j % nteams)] += w;
+        }
+        const int64_t span = *std::max_element(load.begin(), load.end());
+        if (best < 0 || span < best) {
+            best = span;
+            team = t;
+        }
+    }
+    L.team = team;
+    const int teams = kM8Warps / team;
+    const int64_t want = (jobs + teams - 1) / teams;
+    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, g_m8_sms)));
+    const size_t smem = fixed + ns * slot;
+    if (int s = max_smem(mv8_kernel, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
+    mv8_kernel<<<grid, kM8Threads, smem, st>>>(L, maps);
+    return launch_status("matvec (int8 tensor cores)");
+}
+
+// One or two problems (gate and up) of the existing entry points: the single-stack kernel.
+int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
+            int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, const __half* gate,
+            const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st) {
+    return mv8s_try(kind0, kind1, b0, b1, experts, rows, cols, row_bytes, idx, pairs, share, x, gate, up, o0, o1, nprob,
+                    st);
 }
 
 }  // namespace smoe

@@ -12,7 +12,7 @@ sm_100a kernels of libstrata_moe.so.
 import torch
 
 from . import _lib
-from .blocks import BlockMLP, BlockSwitchGLU
+from .blocks import BlockMLP, BlockSwitchGLU, decode_products
 
 ROUTER_TOPK = True  # strata_mlx/fused.py:420 (the kernel is the only top-k here; kept for engines that set it)
 ROUTER_AS_IS = True  # the router reads float16 activations as they are (strata_mlx/fused.py:421)
@@ -156,8 +156,10 @@ class SparseMoeBlock:
             logits = self.gate(x)
             idx, w = top_k_softmax(logits, self.top_k)
             g = self.shared_expert_gate(x).to(x.dtype)
-        y = self.switch_mlp(x, idx)
-        s = self.shared_expert(x)
+        ys = None
+        if isinstance(self.switch_mlp, BlockSwitchGLU) and isinstance(self.shared_expert, BlockMLP):
+            ys = decode_products(self.switch_mlp, self.shared_expert, x, idx)
+        y, s = ys if ys is not None else (self.switch_mlp(x, idx), self.shared_expert(x))
         out = moe_combine(y, w, g, s)
         if out is None:
             raise ValueError("the combine takes float16 or float32 activations")

@@ -266,3 +266,40 @@ def test_a_prompts_three_products_go_through_tiles(cuda, monkeypatch):
     scale = np.abs(want).max()
     assert np.abs(a_pair[0] - want).max() <= 5e-3 * scale
     assert np.abs(in_tiles[0] - want).max() <= 5e-3 * scale
+
+
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+def test_a_batch_of_products_gives_the_separate_products(cuda, dtype):
+    """smoe_matvec_batch: the routed experts' gate and up with a one-expert stack's gate and up on the same
+    activations, then two downs forming their SwiGLU, against the calls one at a time (the same bits when the
+    batch runs them one at a time, float32; within 1e-3 of the largest value in the one int8 launch, float16,
+    whose teams may add their partial sums in another grouping)."""
+    rng = np.random.default_rng(3)
+    E, F_, H, K, T = 16, 256, 512, 4, 2
+    gate = B.BlockSwitchLinear(dev(stack("IQ3_S", rng, E, F_, H)[0]), "IQ3_S", (E, F_, H))
+    up = B.BlockSwitchLinear(dev(stack("IQ3_S", rng, E, F_, H)[0]), "IQ3_S", (E, F_, H))
+    down = B.BlockSwitchLinear(dev(stack("IQ3_S", rng, E, H, F_)[0]), "IQ3_S", (E, H, F_))
+    sg = B.BlockSwitchLinear(dev(stack("Q8_0", rng, 1, 512, H)[0]), "Q8_0", (1, 512, H))
+    sd = B.BlockSwitchLinear(dev(stack("Q8_0", rng, 1, H, 512)[0]), "Q8_0", (1, H, 512))
+    x = dev(rng.standard_normal((T, H)).astype(dtype))
+    idx = dev(rng.choice(E, (T, K), replace=True).astype(np.int32)).reshape(-1)
+    zeros = B._zeros_idx(T, x.device)
+    tt = x.dtype
+    g, u = torch.empty((T * K, F_), dtype=tt, device="cuda"), torch.empty((T * K, F_), dtype=tt, device="cuda")
+    gs = torch.empty((T, 512), dtype=tt, device="cuda")
+    B.matvec_batch([B._problem(gate, idx, T * K, K, g, x=x), B._problem(up, idx, T * K, K, u, x=x),
+                    B._problem(sg, zeros, T, 1, gs, x=x)])
+    y = torch.empty((T * K, H), dtype=tt, device="cuda")
+    s = torch.empty((T, H), dtype=tt, device="cuda")
+    B.matvec_batch([B._problem(down, idx, T * K, 1, y, gate=g, up=u), B._problem(sd, zeros, T, 1, s, gate=gs, up=gs)])
+    want_g = B._matvec(gate, x, idx, K, tt)
+    want_u = B._matvec(up, x, idx, K, tt)
+    want_gs = B._matvec(sg, x, zeros, 1, tt)
+    want_y = B.matvec_glu(down, idx, want_g, want_u)
+    want_s = B.matvec_glu(sd, zeros, want_gs, want_gs)
+    for got, want in ((g, want_g), (u, want_u), (gs, want_gs), (y, want_y), (s, want_s)):
+        if dtype == np.float32:
+            assert torch.equal(got, want)
+        else:
+            tol = 1e-3 * want.float().abs().max().item()
+            assert (got.float() - want.float()).abs().max().item() <= tol
