@@ -197,9 +197,13 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     const int tid_team = warp / team, kq = warp % team;
     const int S = static_cast<int>(a.cols / D::kStageCols);
     const int my_stages = S > kq ? (S - kq + team - 1) / team : 0;
-    const int nteams = gridDim.x * teams;
-    const int q0 = blockIdx.x * teams + tid_team;
-    const int my_jobs = q0 < a.jobs ? (a.jobs - q0 + nteams - 1) / nteams : 0;
+    // CTA b takes the jobs [b J / G, (b + 1) J / G) (neighbouring tiles, so few activation rows); its team i
+    // takes every teams-th of them from the i-th on
+    const int cj0 = static_cast<int>(int64_t(blockIdx.x) * a.jobs / gridDim.x);
+    const int cj1 = static_cast<int>(int64_t(blockIdx.x + 1) * a.jobs / gridDim.x);
+    const int nteams = teams;
+    const int q0 = cj0 + tid_team;
+    const int my_jobs = q0 < cj1 ? (cj1 - q0 + teams - 1) / teams : 0;
     const int items = my_jobs * my_stages;
     const int per_prob = static_cast<int>(a.pairs) * a.tiles;  // < 2^30 (the host checks)
     uint8_t* my_ring = ring + size_t(warp) * ns * kSlot;
@@ -452,8 +456,9 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     if (smem_addr(sm) & 127u) return;  // a tiled copy's destination is 128-byte aligned (the launch gives that)
     const int team = L.team, teams = kM8Warps / team;
     const int tid_team = warp / team, kq = warp % team;
+    // jobs go round-robin over all the launch's teams, CTA-fastest (every SM gets a share of every problem)
     const int nteams = gridDim.x * teams;
-    const int q0 = blockIdx.x * teams + tid_team;
+    const int q0 = tid_team * gridDim.x + blockIdx.x;
     const int my_jobs = q0 < L.jobs ? (L.jobs - q0 + nteams - 1) / nteams : 0;
     uint8_t* my_ring = ring + size_t(warp) * ns * slot_bytes;
     uint64_t* my_bars = bars + warp * kM8MaxSlots;
@@ -754,23 +759,24 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
             cudaDeviceGetAttribute(&g_m8_sms, cudaDevAttrMultiProcessorCount, dev);
             if (g_m8_sms <= 0) g_m8_sms = 148;
         }
-        // the team size with the shortest longest warp: (jobs of the busiest team) x (stages of its busiest warp,
-        // plus about 3/4 of a stage for the team's reduction when the team has more than one warp), in quarters
+        // the team size with the least work on the busiest warp, in quarters of a stage: CTA b takes the jobs
+        // [b J / G, (b + 1) J / G), its teams share them round-robin; a warp does its share of each job's
+        // stages plus about 3/4 of a stage for the team's reduction when the team has more than one warp
         const int64_t S = cols / D::kStageCols;
+        const int64_t G = std::min<int64_t>(g_m8_sms, jobs);
         int team = 1;
         int64_t best = -1;
         for (int t = 1; t <= kM8Warps; t *= 2) {
-            const int64_t nteams = int64_t(g_m8_sms) * (kM8Warps / t);
-            const int64_t span = (jobs + nteams - 1) / nteams * (4 * ((S + t - 1) / t) + (t > 1 ? 3 : 0));
+            const int64_t teams = kM8Warps / t;
+            const int64_t most = ((jobs + G - 1) / G + teams - 1) / teams;  // jobs of the busiest team
+            const int64_t span = most * (4 * ((S + t - 1) / t) + (t > 1 ? 3 : 0));
             if (best < 0 || span < best) {
                 best = span;
                 team = t;
             }
         }
         a.team = team;
-        const int teams = kM8Warps / team;
-        const int64_t want = (jobs + teams - 1) / teams;
-        const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, g_m8_sms)));
+        const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
         const size_t smem = fixed + ns * slot;
         if (int s = max_smem(mv8s_kernel<D>, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
         mv8s_kernel<D><<<grid, kM8Threads, smem, st>>>(a, maps);
@@ -904,14 +910,15 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
         cudaDeviceGetAttribute(&g_m8_sms, cudaDevAttrMultiProcessorCount, dev);
         if (g_m8_sms <= 0) g_m8_sms = 148;
     }
-    // the team size with the least work on the busiest warp: jobs go round-robin over the teams in problem
-    // order; a warp's share of a job is its stages' bytes, plus about 3/4 of a stage for the team's reduction
-    // when the team has more than one warp
+    // the team size with the least work on the busiest warp: jobs go round-robin over all teams (CTA-fastest)
+    // in problem order; a warp's share of a job is its stages' bytes, plus about 3/4 of a stage for the team's
+    // reduction when the team has more than one warp
+    const int64_t G = std::min<int64_t>(g_m8_sms, jobs);
     int team = 1;
     int64_t best = -1;
     std::vector<int64_t> load;
     for (int t = 1; t <= kM8Warps; t *= 2) {
-        const int64_t nteams = int64_t(g_m8_sms) * (kM8Warps / t);
+        const int64_t nteams = G * (kM8Warps / t);
         load.assign(static_cast<size_t>(std::min<int64_t>(nteams, jobs)), 0);
         int64_t j = 0;
         for (int i = 0; i < n; ++i) {
@@ -927,9 +934,7 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
         }
     }
     L.team = team;
-    const int teams = kM8Warps / team;
-    const int64_t want = (jobs + teams - 1) / teams;
-    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, g_m8_sms)));
+    const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
     const size_t smem = fixed + ns * slot;
     if (int s = max_smem(mv8_kernel, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
     mv8_kernel<<<grid, kM8Threads, smem, st>>>(L, maps);
