@@ -107,6 +107,16 @@ typedef struct SmoeMatvec {
 } SmoeMatvec;
 SMOE_API int smoe_matvec_batch(int n, const SmoeMatvec* problems, void* stream);
 
+/* The shared expert's down product with the end of the MoE block as its epilogue: for t < tokens,
+ * out[t, r] = half(sum_j y[t,j,r] w[t,j]) + half(half(sigmoid(g[t])) half(W . swiglu(gate[t], up[t]))[r]),
+ * exactly smoe_matvec_glu into s followed by smoe_combine(y, w, g, s) (the same functions, so the same bits for
+ * the same product). W is one expert's stack (1, rows, cols), idx `tokens` zeros; float16 activations, IQ3_S
+ * or Q8_0 blocks with cols a multiple of 256 (SMOE_ESHAPE otherwise). No single reference counterpart: it
+ * fuses `shared_expert(x)` (strata_mlx/load.py:419-421) with `moe_combine` (strata_mlx/fused.py:448-481). */
+SMOE_API int smoe_matvec_glu_combine(int kind, const uint8_t* blocks, int64_t rows, int64_t cols, const uint32_t* idx,
+                                     int64_t tokens, const void* gate, const void* up, const void* y, const float* w,
+                                     const void* g, int64_t k, void* out, int dtype, void* stream);
+
 /* h = swiglu(gate, up) elementwise over n values of `dtype`: mlx-lm's `swiglu` as restated at
  * strata_mlx/blocks.py:222-237 (the unfused form `down(swiglu(g, u), indices)`, blocks.py:976). */
 SMOE_API int smoe_swiglu(const void* gate, const void* up, int64_t n, void* out, int dtype, void* stream);

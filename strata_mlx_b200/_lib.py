@@ -38,6 +38,7 @@ SIGNATURES = {
     "smoe_matvec_gate_up": (_i, [_i, _p, _i, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i, _p]),
     "smoe_matvec_glu": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _i, _p]),
     "smoe_matvec_batch": (_i, [_i, _c.POINTER(SmoeMatvec), _p]),
+    "smoe_matvec_glu_combine": (_i, [_i, _p, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i, _p]),
     "smoe_swiglu": (_i, [_p, _p, _i64, _p, _i, _p]),
     "smoe_router_logits": (_i, [_p, _p, _i, _i64, _i64, _i64, _p, _p]),
     "smoe_top_k": (_i, [_p, _i64, _i64, _i64, _p, _p, _p]),

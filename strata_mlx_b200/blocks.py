@@ -311,11 +311,13 @@ def matvec_batch(problems) -> None:
     _lib.call("smoe_matvec_batch", len(problems), arr, _lib.stream())
 
 
-def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor):
+def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, w=None, g=None):
     """(switch_mlp(x, indices), shared(x)) for a step that runs both on the decode matvec, with the routed and
     the shared expert's gate and up products in one launch (the same products, within the kernel's rounding,
-    as the separate calls), then the two down products. None where either would take another path (a
-    prompt's tiles, unpacked floats, a SwiGLU the down product does not take, activations of another type)."""
+    as the separate calls), then the two down products. With the combine's w (..., k) float32 and g (..., 1),
+    the shared down product also forms the block's output, `moe_combine(y, w, g, shared(x))` (same bits), and
+    the result is (None, out). None where either would take another path (a prompt's tiles, unpacked floats, a
+    SwiGLU the down product does not take, activations of another type)."""
     lins = (switch_mlp.gate_proj, switch_mlp.up_proj, switch_mlp.down_proj)
     slins = (shared.gate_proj, shared.up_proj, shared.down_proj)
     if x.dtype != torch.float16 or indices.numel() >= TILES_FROM or not BLOCK_GLU:
@@ -332,16 +334,26 @@ def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor):
     gate, up, down = lins
     sg, su, sd = (lin.stack for lin in slins)
     zeros = _zeros_idx(tokens, dev)
-    g = torch.empty((pairs, gate.output_dims), dtype=dt, device=dev)
-    u = torch.empty((pairs, up.output_dims), dtype=dt, device=dev)
+    g_r = torch.empty((pairs, gate.output_dims), dtype=dt, device=dev)
+    u_r = torch.empty((pairs, up.output_dims), dtype=dt, device=dev)
     gs = torch.empty((tokens, sg.output_dims), dtype=dt, device=dev)
     us = torch.empty((tokens, su.output_dims), dtype=dt, device=dev)
     if pairs:
-        matvec_batch([_problem(gate, idx, pairs, k, g, x=x2), _problem(up, idx, pairs, k, u, x=x2),
+        matvec_batch([_problem(gate, idx, pairs, k, g_r, x=x2), _problem(up, idx, pairs, k, u_r, x=x2),
                       _problem(sg, zeros, tokens, 1, gs, x=x2), _problem(su, zeros, tokens, 1, us, x=x2)])
     # the two down products stay separate launches: in one launch the shared expert's long rows (4096 columns)
     # are the slowest warps' work and the pair is slower than the two alone
-    y = matvec_glu(down, idx, g, u)
+    y = matvec_glu(down, idx, g_r, u_r)
+    fused = (w is not None and g is not None and sd.kind in FUSED_GLU and sd.input_dims % FUSED_GLU_COLS == 0
+             and tokens * sd.input_dims * 2 <= FUSED_GLU_BYTES and w.dtype == torch.float32 and g.dtype == dt
+             and sd.output_dims == down.output_dims)
+    if fused:
+        out = torch.empty((tokens, sd.output_dims), dtype=dt, device=dev)
+        if tokens:
+            _lib.call("smoe_matvec_glu_combine", _kind(sd.kind), _lib.ptr(sd.blocks), sd.output_dims, sd.input_dims,
+                      _lib.ptr(zeros), tokens, _lib.ptr(gs), _lib.ptr(us), _lib.ptr(y), _lib.ptr(w.contiguous()),
+                      _lib.ptr(g.contiguous()), k, _lib.ptr(out), _lib.dtype_code(dt), _lib.stream())
+        return None, out.reshape(*x.shape[:-1], sd.output_dims)
     s = matvec_glu(sd, zeros, gs, us)
     return y.reshape(*indices.shape, down.output_dims), s.reshape(*x.shape[:-1], sd.output_dims)
 

@@ -127,4 +127,41 @@ __device__ __forceinline__ T swiglu_one(T g, T u) {
     return from_f32<T>(__fmul_rn(to_f32(a), to_f32(u)));
 }
 
+template <typename T> __device__ __forceinline__ T mul_t(T a, T b);
+// the _rn forms: a product or sum rounded on its own, never contracted into a half FMA with its neighbour
+template <> __device__ __forceinline__ __half mul_t<__half>(__half a, __half b) { return __hmul_rn(a, b); }
+template <> __device__ __forceinline__ float mul_t<float>(float a, float b) { return __fmul_rn(a, b); }
+template <typename T> __device__ __forceinline__ T add_t(T a, T b);
+template <> __device__ __forceinline__ __half add_t<__half>(__half a, __half b) { return __hadd_rn(a, b); }
+template <> __device__ __forceinline__ float add_t<float>(float a, float b) { return __fadd_rn(a, b); }
+
+// One element of the MoE block's end (strata_mlx/fused.py:448-462): half(sum_j y_j w_j) + half(half(sigmoid(g))
+// s), the sum in float32 in MLX's col_reduce_small order (partials j = k mod 8, then in order), every product
+// and sum rounded on its own. y points at expert 0's value, the experts' values `stride` apart.
+template <typename T>
+__device__ __forceinline__ T combine_one(const T* __restrict__ y, int64_t stride, const float* __restrict__ w, int k,
+                                         T g, T s) {
+    const T gate = from_f32<T>(1.0f / (1.0f + expf(-to_f32(g))));
+    float acc = 0.0f;
+    if (k == 8) {
+        // (the common case, its eight loads in flight together; the same sums in the same order)
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = to_f32(y[int64_t(j) * stride]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float part = __fadd_rn(__fmul_rn(v[j], w[j]), 0.0f);
+            acc = j == 0 ? part : __fadd_rn(part, acc);
+        }
+    } else {
+        for (int j = 0; j < 8 && j < k; ++j) {
+            float part = 0.0f;
+            for (int kk = j; kk < k; kk += 8) part = __fadd_rn(__fmul_rn(to_f32(y[int64_t(kk) * stride]), w[kk]), part);
+            acc = j == 0 ? part : __fadd_rn(part, acc);
+        }
+    }
+    const T routed = from_f32<T>(acc);
+    return add_t<T>(routed, mul_t<T>(gate, s));
+}
+
 }  // namespace smoe

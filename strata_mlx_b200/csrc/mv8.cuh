@@ -27,4 +27,10 @@ int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t 
             int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, const __half* gate,
             const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st);
 
+// the shared expert's down product with the block's combine as its epilogue: 0 launched, 1 not taken, else an
+// error (out[t, r] = the combine of y (tokens, k, rows), w (tokens, k), g (tokens) and the product)
+int mv8_glu_combine(int kind, const uint8_t* blocks, int64_t rows, int64_t cols, int64_t row_bytes,
+                    const uint32_t* idx, int64_t tokens, const __half* gate, const __half* up, const __half* y,
+                    const float* w, const __half* g, int k, __half* out, cudaStream_t st);
+
 }  // namespace smoe

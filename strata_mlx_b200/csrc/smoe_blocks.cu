@@ -289,6 +289,25 @@ extern "C" int smoe_matvec_batch(int n, const SmoeMatvec* pr, void* stream) {
     return SMOE_OK;
 }
 
+extern "C" int smoe_matvec_glu_combine(int kind, const uint8_t* blocks, int64_t rows, int64_t cols,
+                                       const uint32_t* idx, int64_t tokens, const void* gate, const void* up,
+                                       const void* y, const float* w, const void* g, int64_t k, void* out, int dtype,
+                                       void* stream) {
+    int per, bytes;
+    if (int s = check_stack(kind, 1, rows, cols, per, bytes)) return s;
+    if (tokens == 0) return SMOE_OK;
+    SMOE_REQUIRE(tokens > 0 && blocks && idx && gate && up && y && w && g && out, SMOE_EARG, "null pointer");
+    SMOE_REQUIRE(k >= 1 && k <= 64, SMOE_ESHAPE, "1 <= k <= 64");
+    SMOE_REQUIRE(dtype == SMOE_F16, SMOE_EDTYPE, "the fused combine takes float16 activations");
+    const int r = mv8_glu_combine(kind, blocks, rows, cols, cols / per * bytes, idx, tokens,
+                                  static_cast<const __half*>(gate), static_cast<const __half*>(up),
+                                  static_cast<const __half*>(y), w, static_cast<const __half*>(g), static_cast<int>(k),
+                                  static_cast<__half*>(out), as_stream(stream));
+    if (r == 1) return fail(SMOE_ESHAPE, "the fused combine does not take this stack (IQ3_S or Q8_0, columns a "
+                                         "multiple of 256, activations within its shared memory)");
+    return r;
+}
+
 extern "C" int smoe_matvec_gate_up(int gate_kind, const uint8_t* gate_blocks, int up_kind, const uint8_t* up_blocks,
                                    int64_t experts, int64_t rows, int64_t cols, const uint32_t* idx, int64_t pairs,
                                    int64_t share, const void* x, void* gate_out, void* up_out, int dtype, void* stream) {

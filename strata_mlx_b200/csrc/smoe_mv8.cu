@@ -160,6 +160,13 @@ struct M8Args {
     int team;       // warps per job: 1, 2, 4, 8 or 16
     int xrows;      // activation rows (pairs / share)
     int nslots;     // ring slots per warp
+    // when cy is set, the product is the shared expert's down and out[0] receives the block's combine instead:
+    // out[t, r] = half(sum_j cy[t, j, r] cw[t, j]) + half(half(sigmoid(cg[t])) half(product[t, r])) (pair t is
+    // token t)
+    const __half* cy;
+    const float* cw;
+    const __half* cg;
+    int ck;
 };
 // a job's place (worked out once per job, 32-bit): problem, pair, expert, the tile's residue class and block
 // of 16 q rows, the first row of its TMA box, the activation row
@@ -380,7 +387,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
             if (w.e < a.experts && row < a.rows) {
                 float v = rq[lane];
                 for (int i = 1; i < team; ++i) v += rq[16 * i + lane];
-                (w.prob ? a.out[1] : a.out[0])[int64_t(w.pair) * a.rows + row] = __float2half_rn(v);
+                const __half prod = __float2half_rn(v);
+                __half* o = (w.prob ? a.out[1] : a.out[0]) + int64_t(w.pair) * a.rows + row;
+                if (a.cy == nullptr) *o = prod;
+                else *o = combine_one(a.cy + int64_t(w.pair) * a.ck * a.rows + row, a.rows, a.cw + int64_t(w.pair) * a.ck,
+                                      a.ck, a.cg[w.pair], prod);
             }
         }
         team_sync();
@@ -692,7 +703,8 @@ static int g_m8_sms = 0;
 // x, or (gate, up) whose SwiGLU is the activations.
 int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
             int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, const __half* gate,
-            const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st) {
+            const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st, const __half* cy = nullptr,
+            const float* cw = nullptr, const __half* cg = nullptr, int ck = 0) {
     if (kind0 != kind1) return 1;
     auto go = [&](auto dec) -> int {
         using D = decltype(dec);
@@ -753,6 +765,10 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         a.jobs = static_cast<int>(jobs);
         a.xrows = static_cast<int>(xrows);
         a.nslots = ns;
+        a.cy = cy;
+        a.cw = cw;
+        a.cg = cg;
+        a.ck = ck;
         if (g_m8_sms == 0) {
             int dev = 0;
             cudaGetDevice(&dev);
@@ -939,6 +955,14 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
     if (int s = max_smem(mv8_kernel, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
     mv8_kernel<<<grid, kM8Threads, smem, st>>>(L, maps);
     return launch_status("matvec (int8 tensor cores)");
+}
+
+// The shared expert's down product (one expert, pair t = token t) with the block's combine as its epilogue.
+int mv8_glu_combine(int kind, const uint8_t* blocks, int64_t rows, int64_t cols, int64_t row_bytes,
+                    const uint32_t* idx, int64_t tokens, const __half* gate, const __half* up, const __half* y,
+                    const float* w, const __half* g, int k, __half* out, cudaStream_t st) {
+    return mv8s_try(kind, kind, blocks, blocks, 1, rows, cols, row_bytes, idx, tokens, 1, nullptr, gate, up, out, out, 1,
+                    st, y, w, g, k);
 }
 
 // One or two problems (gate and up) of the existing entry points: the single-stack kernel.

@@ -230,45 +230,12 @@ __global__ void __launch_bounds__(256) route_kernel(const __half* __restrict__ w
 
 // ---------------------------------------------------------------- combine
 
-template <typename T> __device__ __forceinline__ T mul_t(T a, T b);
-// the _rn forms: a product or sum rounded on its own, never contracted into a half FMA with its neighbour
-template <> __device__ __forceinline__ __half mul_t<__half>(__half a, __half b) { return __hmul_rn(a, b); }
-template <> __device__ __forceinline__ float mul_t<float>(float a, float b) { return __fmul_rn(a, b); }
-template <typename T> __device__ __forceinline__ T add_t(T a, T b);
-template <> __device__ __forceinline__ __half add_t<__half>(__half a, __half b) { return __hadd_rn(a, b); }
-template <> __device__ __forceinline__ float add_t<float>(float a, float b) { return __fadd_rn(a, b); }
-
 template <typename T>
 __global__ void combine_kernel(const T* __restrict__ y, const float* __restrict__ w, const T* __restrict__ g,
                                const T* __restrict__ s, int64_t tokens, int k, int64_t d, T* __restrict__ out) {
     const int64_t t = blockIdx.y;
-    const float* wt = w + t * k;
-    const T gate = from_f32<T>(1.0f / (1.0f + expf(-to_f32(g[t]))));
-    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < d; i += int64_t(gridDim.x) * blockDim.x) {
-        const T* yt = y + (t * k) * d + i;
-        float acc = 0.0f;
-        if (k == 8) {
-            // (the common case, its eight loads in flight together; the same sums in the same order)
-            float v[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = to_f32(yt[int64_t(j) * d]);
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const float part = __fadd_rn(__fmul_rn(v[j], wt[j]), 0.0f);
-                acc = j == 0 ? part : __fadd_rn(part, acc);
-            }
-        } else {
-            for (int j = 0; j < 8 && j < k; ++j) {
-                float part = 0.0f;
-                for (int kk = j; kk < k; kk += 8)
-                    part = __fadd_rn(__fmul_rn(to_f32(yt[int64_t(kk) * d]), wt[kk]), part);
-                acc = j == 0 ? part : __fadd_rn(part, acc);
-            }
-        }
-        const T routed = from_f32<T>(acc);
-        const T shared = mul_t<T>(gate, s[t * d + i]);
-        out[t * d + i] = add_t<T>(routed, shared);
-    }
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < d; i += int64_t(gridDim.x) * blockDim.x)
+        out[t * d + i] = combine_one(y + (t * k) * d + i, d, w + t * k, k, g[t], s[t * d + i]);
 }
 
 // ---------------------------------------------------------------- expert parallelism

@@ -158,7 +158,9 @@ class SparseMoeBlock:
             g = self.shared_expert_gate(x).to(x.dtype)
         ys = None
         if isinstance(self.switch_mlp, BlockSwitchGLU) and isinstance(self.shared_expert, BlockMLP):
-            ys = decode_products(self.switch_mlp, self.shared_expert, x, idx)
+            ys = decode_products(self.switch_mlp, self.shared_expert, x, idx, w, g)
+        if ys is not None and ys[0] is None:
+            return ys[1]  # the shared expert's down product formed the combine
         y, s = ys if ys is not None else (self.switch_mlp(x, idx), self.shared_expert(x))
         out = moe_combine(y, w, g, s)
         if out is None:

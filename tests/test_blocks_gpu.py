@@ -303,3 +303,27 @@ def test_a_batch_of_products_gives_the_separate_products(cuda, dtype):
         else:
             tol = 1e-3 * want.float().abs().max().item()
             assert (got.float() - want.float()).abs().max().item() <= tol
+
+
+@pytest.mark.parametrize("tokens", [1, 3])
+def test_the_shared_down_product_with_the_combine_is_the_two_calls(cuda, tokens):
+    """smoe_matvec_glu_combine: the shared expert's down product with the block's end as its epilogue gives the
+    bits of smoe_matvec_glu then smoe_combine (strata_mlx/fused.py:448-481)."""
+    from strata_mlx_b200 import _lib
+    from strata_mlx_b200 import fused as F
+
+    rng = np.random.default_rng(tokens)
+    H, FS, K = 512, 512, 8
+    sd = B.BlockSwitchLinear(dev(stack("Q8_0", rng, 1, H, FS)[0]), "Q8_0", (1, H, FS))
+    gs = dev(rng.standard_normal((tokens, FS)).astype(np.float16))
+    us = dev(rng.standard_normal((tokens, FS)).astype(np.float16))
+    y = dev(rng.standard_normal((tokens, K, H)).astype(np.float16))
+    w = torch.softmax(dev(rng.standard_normal((tokens, K)).astype(np.float32)), -1)
+    g = dev(rng.standard_normal((tokens, 1)).astype(np.float16))
+    zeros = B._zeros_idx(tokens, y.device)
+    out = torch.empty((tokens, H), dtype=torch.float16, device="cuda")
+    _lib.call("smoe_matvec_glu_combine", B._kind("Q8_0"), _lib.ptr(sd.blocks), H, FS, _lib.ptr(zeros), tokens,
+              _lib.ptr(gs), _lib.ptr(us), _lib.ptr(y), _lib.ptr(w), _lib.ptr(g), K, _lib.ptr(out), 1, _lib.stream())
+    s = B.matvec_glu(sd, zeros, gs, us)
+    want = F.moe_combine(y, w, g, s)
+    assert torch.equal(out, want)
