@@ -11,8 +11,9 @@ sigmoid gate; SwiGLU; weighted combine. A step is one token through one such lay
 value    token-layers/s with the token already in HBM (device-timed with CUDA events, max over ranks)
 e2e      the same through the public API `SparseMoeBlock.__call__` with the token copied from pinned host
          memory and the result copied back inside every step
-roofline the dominant kernel (the routed gate/up matvec: 16 IQ3_S matrices of 1536 x 4096) against the
-         measured HBM copy bandwidth: algorithmic bytes per launch / its CUDA-event time
+roofline the dominant kernel (the step's batched gate/up: 16 IQ3_S matrices of 1536 x 4096 and the shared
+         expert's two Q8_0 4096 x 4096 in one launch) against the measured HBM copy bandwidth: algorithmic
+         bytes per launch / its CUDA-event time
 cpu_baseline  the oracle port (numpy: decode of the chosen experts' blocks + products) on the host's cores
 
 With --gpus N > 1 (torchrun, one process per GPU, NCCL) the experts are sharded 256/N per rank and the
@@ -363,7 +364,9 @@ def run_ours(args, rank, world, local_rank):
     if dist:
         dist.barrier()
 
-    # the dominant kernel alone: a graph of its launches over the rotating layers, with each layer's routing
+    # the dominant kernel alone: a graph of its launches over the rotating layers, with each layer's routing.
+    # On one GPU that is the step's batched gate/up launch (routed experts and shared expert in one int8
+    # tensor-core kernel); on several, each rank's routed gate/up.
     routes = []
     for i in range(args.layers):
         blk = blocks[i]
@@ -371,16 +374,31 @@ def run_ours(args, rank, world, local_rank):
         idx, _ = top_k_softmax(layer.gate(xs[i]), K)
         if world > 1:
             idx = blk.local_indices(idx)
-        routes.append((layer.switch_mlp, xs[i], idx.reshape(-1).contiguous()))
+        fi = idx.reshape(-1).contiguous()
+        sw, sh = layer.switch_mlp, layer.shared_expert
+        outs = [torch.empty((K, F_), dtype=torch.float16, device=device) for _ in range(2)]
+        souts = [torch.empty((1, sh.gate_proj.output_dims), dtype=torch.float16, device=device) for _ in range(2)]
+        z = B._zeros_idx(1, device)
+        probs = [B._problem(sw.gate_proj, fi, K, K, outs[0], x=xs[i]), B._problem(sw.up_proj, fi, K, K, outs[1], x=xs[i]),
+                 B._problem(sh.gate_proj.stack, z, 1, 1, souts[0], x=xs[i]),
+                 B._problem(sh.up_proj.stack, z, 1, 1, souts[1], x=xs[i])]
+        routes.append((sw, xs[i], fi, probs, outs + souts))
     reps = max(1, 64 // args.layers)
-    for sw, x, idx in routes:
-        B.gate_up(sw.gate_proj, sw.up_proj, x, idx, K)
+
+    def dominant(sw, x, idx, probs):
+        if world == 1:
+            B.matvec_batch(probs)
+        else:
+            B.gate_up(sw.gate_proj, sw.up_proj, x, idx, K)
+
+    for sw, x, idx, probs, _ in routes:
+        dominant(sw, x, idx, probs)
     torch.cuda.synchronize()
     gu_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gu_graph):
         for _ in range(reps):
-            for sw, x, idx in routes:
-                B.gate_up(sw.gate_proj, sw.up_proj, x, idx, K)
+            for sw, x, idx, probs, _ in routes:
+                dominant(sw, x, idx, probs)
     gu_graph.replay()
     torch.cuda.synchronize()
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -423,10 +441,9 @@ def run_ours(args, rank, world, local_rank):
         return None
     peak, peak_kind = peaks()
     e_loc = E // world
-    gu_bytes = 2 * K * F_ * B.row_bytes(KIND, H)  # 16 IQ3_S matrices of 1536 x 4096 (at N=1; per rank below)
-    if world > 1:
-        gu_bytes = None
-    achieved = (2 * K * F_ * B.row_bytes(KIND, H)) / (gu * 1e-3) / 1e9 if world == 1 else None
+    # 16 IQ3_S matrices of 1536 x 4096 and the shared expert's two Q8_0 4096 x 4096 (one GPU)
+    gu_bytes = 2 * K * F_ * B.row_bytes(KIND, H) + 2 * FS * B.row_bytes(SHARED_KIND, H) if world == 1 else None
+    achieved = gu_bytes / (gu * 1e-3) / 1e9 if world == 1 else None
     per_step_bytes = (3 * K * F_ * B.row_bytes(KIND, H) + 3 * FS * B.row_bytes(SHARED_KIND, H) + E * H * 2)
     line = {
         "metric": "MoE layer tokens/s (decode bs1) + achieved HBM GB/s vs roofline",
@@ -451,7 +468,8 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": launches * args.steps,
         "e2e": {"value": args.steps / (e2e_ms * 1e-3), "unit": "token-layers/s",
                 "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
-        "roofline": {"kernel": "mv8_kernel<M8IQ3S> (routed gate+up, 16 x 1536 x 4096 IQ3_S)", "bound": "hbm",
+        "roofline": {"kernel": "mv8_kernel (batched gate+up: 16 x 1536 x 4096 IQ3_S + 2 x 4096 x 4096 Q8_0)"
+                               if world == 1 else "mv8s_kernel<M8IQ3S> (routed gate+up)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": (achieved / peak) if achieved else None, "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu,
