@@ -6,9 +6,9 @@
 //     with s = max|x| / 127 over the block (|error| <= s / 256, far below float16's own rounding of the
 //     weights); each CTA does this for the rows it needs, into shared memory, while its first weight stages
 //     load;
-//   - the weights enter the MMA as int8: Q8_0 codes as stored, IQ3_S as grid value x sign from a codebook
-//     indexed by (9-bit grid index, 4 sign bits) of 8192 words (32 KB in shared memory), so expanding four
-//     weights is one lookup;
+//   - the weights enter the MMA as int8: Q8_0 codes as stored, IQ3_S as the grid word of a group's 9-bit
+//     index (16 copies of the 512-word grid in shared memory, 32 KB, so lookups rarely share a bank) with the
+//     group's signs applied by xor;
 //   - mma.sync m16n8k32 s8 takes one 32-weight run per MMA: column 0 of B holds hi, column 1 holds lo, so one
 //     MMA gives both sums of a run; 128 hi + lo times the run's integer sub-scale (1 + 2 s for IQ3_S) adds into
 //     an int32 total per row and block (|total| < 2^31 for any weights), scaled once by d s / 128 (IQ3_S), or
@@ -57,58 +57,116 @@ __device__ __forceinline__ float h2f(uint32_t bits) {
 // (110 bytes: d 0, qs 2..65, qh 66..73, signs 74..105, scales 106..109.) In run r, lane tig of a row's quad
 // takes groups 2 tig and 2 tig + 1 (weights 8 tig .. 8 tig + 7 of the run): K 4 tig .. 4 tig + 3 of the MMA is
 // group 2 tig, K 16 + 4 tig .. is group 2 tig + 1, the same permutation for the activations.
+//
+// A group's four weights are the grid word of its 9-bit index (qs byte | qh bit << 8) with the group's four
+// signs applied. The grid (512 words) sits in shared memory 16 times over, word i * 16 + lane % 16, so a
+// warp's 32 random lookups meet at most two to a bank. Every grid value is odd, so negating a byte is xor with
+// 0xFE: four sign bits become four 0x00 / 0xFF bytes by one multiply (each bit to the top of its byte) and a
+// sign-replicating byte permute.
+
+template <int O>
+__device__ __forceinline__ uint32_t ld_s16(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u16 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(O));
+    return v;
+}
+template <int O>
+__device__ __forceinline__ uint32_t ld_s8(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u8 %0, [%1+%2];" : "=r"(v) : "r"(a), "n"(O));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_s32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+// prmt.b32 in its default mode: a selector nibble with bit 3 set replicates the top bit of the chosen byte
+__device__ __forceinline__ uint32_t prmt_sr(uint32_t a, uint32_t c) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, 0, %2;" : "=r"(d) : "r"(a), "r"(c));
+    return d;
+}
+constexpr int kM8GridRep = 16;  // copies of the IQ3_S grid in shared memory
+
 struct M8IQ3S {
     static constexpr int kKind = 21, kStageCols = 256, kStageBytes = 110, kRS = 144, kRuns = 8;
     static constexpr bool kLut = true;
+    // run R of the stage: the two rows' groups (bq / bs: the lane's qs / sign bytes), lutl = this lane's grid copy
+    template <int R>
+    __device__ static __forceinline__ void run(const uint32_t (&bq)[2], const uint32_t (&bs)[2], const uint32_t (&qh)[2][2],
+                                               const uint32_t (&m)[2][2], uint32_t lutl, const uint8_t* xsrc, int tig,
+                                               int gid, int (&t)[2]) {
+        uint32_t a[2][2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint32_t q2 = ld_s16<2 + 8 * R>(bq[j]);  // qs bytes of the two groups
+            const uint32_t sb = ld_s8<74 + 4 * R>(bs[j]);   // their sign nibbles
+            // byte R % 4 of the shifted qh word: bits 0, 1 are the groups' (the rest never reach the index)
+            const uint32_t h = __byte_perm(qh[j][R >> 2], 0u, 0x4440 + (R & 3));
+            // both grid indices in one word: qs | qh << 8 in each half
+            const uint32_t z = __byte_perm(q2, 0u, 0x4140) | ((h * 0x00800100u) & 0x01000100u);
+            const uint32_t ga = ld_s32(lutl + ((z & 0x1ffu) << 6));
+            const uint32_t gb = ld_s32(lutl + ((z >> 16) << 6));
+            const uint32_t ma = prmt_sr((sb & 0x0Fu) * 0x10204080u, 0xBA98u);
+            const uint32_t mb = prmt_sr((sb & 0xF0u) * 0x01020408u, 0xBA98u);
+            a[j][0] = ga ^ (ma & 0xFEFEFEFEu);
+            a[j][1] = gb ^ (mb & 0xFEFEFEFEu);
+        }
+        uint2 b = make_uint2(0u, 0u);
+        if (gid < 2) b = *reinterpret_cast<const uint2*>(xsrc + 32 * R + 8 * tig);
+        int acc[4];
+        mma_s8(acc, a[0][0], a[1][0], a[0][1], a[1][1], b.x, b.y);
+        // (lanes with tig > 0 hold columns 2..7: zeros)
+        const int m0 = static_cast<int>(__byte_perm(m[0][R & 1], 0u, 0x4440 + (R >> 1)));
+        const int m1 = static_cast<int>(__byte_perm(m[1][R & 1], 0u, 0x4440 + (R >> 1)));
+        t[0] += m0 * (acc[0] * 128 + acc[1]);
+        t[1] += m1 * (acc[2] * 128 + acc[3]);
+    }
     // one stage (= one block) of rows gid (j = 0) and gid + 8 (j = 1): partial sums of the two rows
     __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t* lut,
                                  const uint8_t* xh, const uint8_t* xl, float xs, float (&total)[2]) {
-        const uint8_t* rb[2] = {r0, r1};
-        uint32_t m[2][2], qh[2][2];
+        const uint32_t rb[2] = {smem_addr(r0), smem_addr(r1)};
+        const uint32_t lutl = smem_addr(lut) + 4u * static_cast<uint32_t>((4 * gid + tig) & (kM8GridRep - 1));
+        uint32_t m[2][2], qh[2][2], bq[2], bs[2];
         float d[2];
         int t[2] = {0, 0};
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
-            d[j] = h2f(lds_u16(rb[j]));
+            d[j] = h2f(ld_s16<0>(rb[j]));
             // the runs' odd sub-scales 1 + 2 s as bytes: runs 0, 2, 4, 6 in m[j][0], runs 1, 3, 5, 7 in m[j][1]
-            const uint32_t sc = lds_u16(rb[j] + 106) | (lds_u16(rb[j] + 108) << 16);
+            const uint32_t sc = ld_s16<106>(rb[j]) | (ld_s16<108>(rb[j]) << 16);
             m[j][0] = ((sc & 0x0F0F0F0Fu) << 1) | 0x01010101u;
             m[j][1] = ((sc >> 3) & 0x1E1E1E1Eu) | 0x01010101u;
             // qh bits of groups 2 tig, 2 tig + 1 of run r at bits 8 (r % 4), 8 (r % 4) + 1 of word r / 4
-            qh[j][0] = (lds_u16(rb[j] + 66) | (lds_u16(rb[j] + 68) << 16)) >> (2 * tig);
-            qh[j][1] = (lds_u16(rb[j] + 70) | (lds_u16(rb[j] + 72) << 16)) >> (2 * tig);
+            qh[j][0] = (ld_s16<66>(rb[j]) | (ld_s16<68>(rb[j]) << 16)) >> (2 * tig);
+            qh[j][1] = (ld_s16<70>(rb[j]) | (ld_s16<72>(rb[j]) << 16)) >> (2 * tig);
+            bq[j] = rb[j] + 2u * tig;
+            bs[j] = rb[j] + tig;
         }
         const uint8_t* xsrc = gid == 0 ? xh : xl;
-#pragma unroll
-        for (int r = 0; r < 8; ++r) {
-            uint32_t a[2][2];
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const uint32_t q2 = lds_u16(rb[j] + 2 + 8 * r + 2 * tig);  // qs bytes of the two groups
-                const uint32_t sb = lds_u8(rb[j] + 74 + 4 * r + tig);      // their sign nibbles
-                // byte r % 4 of the shifted qh word: bits 0, 1 are the groups' (the rest never reach the index)
-                const uint32_t h = __byte_perm(qh[j][r >> 2], 0u, 0x4440 + (r & 3));
-                // both codebook indices in one word: qs | qh << 8 | signs << 9 in each half
-                const uint32_t z = __byte_perm(q2, 0u, 0x4140) | ((h * 0x00800100u) & 0x01000100u) |
-                                   ((sb * 0x00200200u) & 0x1E001E00u);
-                a[j][0] = lut[z & 0xffffu];
-                a[j][1] = lut[z >> 16];
-            }
-            uint2 b = make_uint2(0u, 0u);
-            if (gid < 2) b = *reinterpret_cast<const uint2*>(xsrc + 32 * r + 8 * tig);
-            int acc[4];
-            mma_s8(acc, a[0][0], a[1][0], a[0][1], a[1][1], b.x, b.y);
-            // (lanes with tig > 0 hold columns 2..7: zeros)
-            const int m0 = static_cast<int>(__byte_perm(m[0][r & 1], 0u, 0x4440 + (r >> 1)));
-            const int m1 = static_cast<int>(__byte_perm(m[1][r & 1], 0u, 0x4440 + (r >> 1)));
-            t[0] += m0 * (acc[0] * 128 + acc[1]);
-            t[1] += m1 * (acc[2] * 128 + acc[3]);
-        }
+        run<0>(bq, bs, qh, m, lutl, xsrc, tig, gid, t);
+        run<1>(bq, bs, qh, m, lutl, xsrc, tig, gid, t);
+        run<2>(bq, bs, qh, m, lutl, xsrc, tig, gid, t);
+        run<3>(bq, bs, qh, m, lutl, xsrc, tig, gid, t);
+        run<4>(bq, bs, qh, m, lutl, xsrc, tig, gid, t);
+        run<5>(bq, bs, qh, m, lutl, xsrc, tig, gid, t);
+        run<6>(bq, bs, qh, m, lutl, xsrc, tig, gid, t);
+        run<7>(bq, bs, qh, m, lutl, xsrc, tig, gid, t);
         const float k = xs * (1.0f / 128.0f);
         total[0] = fmaf(d[0] * k, static_cast<float>(t[0]), total[0]);
         total[1] = fmaf(d[1] * k, static_cast<float>(t[1]), total[1]);
     }
 };
+
+// the IQ3_S grid (entries 0..511 of the sign-folded table built from gguf-py's grid: sign bits 0), 16 times
+// over: 32 KB
+__device__ __forceinline__ void m8_fill_grid(uint32_t* lut) {
+    for (int i = threadIdx.x; i < 512 * kM8GridRep / 4; i += blockDim.x) {
+        const uint32_t g = __ldg(kIq3sSigned + (4 * i) / kM8GridRep);
+        reinterpret_cast<uint4*>(lut)[i] = make_uint4(g, g, g, g);
+    }
+}
 
 // ---------------------------------------------------------------- Q8_0
 // (34 bytes: d 0, qs 2..33.) A stage is four runs; in run r lane tig takes codes 8 tig .. 8 tig + 7.
@@ -191,7 +249,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * kSlot);  // [warp][slot]
     float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);       // [16 warps][16 rows]
     M8WhereS* where_ring = reinterpret_cast<M8WhereS*>(red + kM8Warps * 16);       // [16 warps][4]
-    uint32_t* lut = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(where_ring) + kM8WhereSBytes);  // 8192 words
+    uint32_t* lut = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(where_ring) + kM8WhereSBytes);  // 512 x 16 words
     const int xblocks = static_cast<int>(a.cols / kM8XBlock);
     float* xscale = reinterpret_cast<float*>(lut + (D::kLut ? 8192 : 0));        // [xrows][xblocks]
     int8_t* xhi = reinterpret_cast<int8_t*>(xscale + ((a.xrows * xblocks + 3) & ~3));  // [xrows][cols]
@@ -273,13 +331,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     if (lane == 0)
         for (int i = 0; i < ns - 1 && i < items; ++i) issue();
 
-    if constexpr (D::kLut) {
-        // grid value x sign, entry g | s << 9 (built from gguf-py's grid with the rest of the tables): 32 KB
-        // copied in 16-byte pieces
-        const uint4* src = reinterpret_cast<const uint4*>(kIq3sSigned);
-        uint4* dst = reinterpret_cast<uint4*>(lut);
-        for (int i = threadIdx.x; i < 8192 / 4; i += kM8Threads) dst[i] = __ldg(src + i);
-    }
+    if constexpr (D::kLut) m8_fill_grid(lut);
     // the activation rows this CTA's jobs read (all of them when there are more than kM8SMaskRows)
     uint32_t* need = reinterpret_cast<uint32_t*>(where_ring + kM8Warps * 4);  // kM8SMaskRows bits
     const bool masked = a.xrows <= kM8SMaskRows;
@@ -458,7 +510,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);                 // [16 warps][16 rows]
     uint32_t* sidx = reinterpret_cast<uint32_t*>(red + kM8Warps * 16);                    // [kM8MaxRows]
     uint32_t* need = sidx + kM8MaxRows;                                                   // kM8MaxRows bits
-    uint32_t* lut = need + kM8MaxRows / 32;                                               // 8192 words (IQ3_S)
+    uint32_t* lut = need + kM8MaxRows / 32;                                               // 512 x 16 words (IQ3_S)
     float* xscale = reinterpret_cast<float*>(lut + (L.lut ? 8192 : 0));
     int8_t* xsplit = reinterpret_cast<int8_t*>(xscale + ((L.scales + 3) & ~3));
 
@@ -547,13 +599,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
         for (int i = 0; i < ns - 1; ++i) issue();
     }
 
-    if (L.lut) {
-        // grid value x sign, entry g | s << 9 (built from gguf-py's grid with the rest of the tables): 32 KB
-        // copied in 16-byte pieces
-        const uint4* src = reinterpret_cast<const uint4*>(kIq3sSigned);
-        uint4* dst = reinterpret_cast<uint4*>(lut);
-        for (int i = threadIdx.x; i < 8192 / 4; i += kM8Threads) dst[i] = __ldg(src + i);
-    }
+    if (L.lut) m8_fill_grid(lut);
     // the activation rows this CTA's jobs read
     if (lane == 0)
         for (int job = 0; job < my_jobs; ++job) {
@@ -835,7 +881,6 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
             return 1;
         }
         if (sp.cols % kM8XBlock || sp.cols % stage_cols || sp.pairs <= 0 || sp.share < 1) return 1;
-        const __half* xp = sp.x ? sp.x : sp.gate;
         if ((reinterpret_cast<uintptr_t>(sp.x) & 15) || (reinterpret_cast<uintptr_t>(sp.gate) & 15) ||
             (reinterpret_cast<uintptr_t>(sp.up) & 15) || (reinterpret_cast<uintptr_t>(sp.blocks) & 15) ||
             (sp.gate != nullptr) != (sp.up != nullptr) || (sp.gate == nullptr) == (sp.x == nullptr))
@@ -869,7 +914,6 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
         } else if (L.x[xs].rows < xrows) {
             return 1;
         }
-        (void)xp;
         M8Prob& P = L.p[i];
         P.idx = sp.idx;
         P.out = sp.out;
