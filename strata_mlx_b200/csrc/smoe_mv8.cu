@@ -14,8 +14,9 @@
 //     an int32 total per row and block (|total| < 2^31 for any weights), scaled once by d s / 128 (IQ3_S), or
 //     run by run by d s / 128 (Q8_0).
 // Layout (B200, one persistent CTA of 16 warps per SM): a job = (problem, pair, tile of 16 weight rows) is
-// taken by a team of 1 to 16 warps (the size that gives the shortest longest warp) that split its 256-
-// (IQ3_S) or 128-column (Q8_0) stages; the team adds its partial sums in shared memory in a fixed order.
+// taken by a team of 1 to 16 warps (the size that gives the shortest longest warp) that split its 512-
+// (IQ3_S: two blocks) or 128-column (Q8_0) stages; the team adds its partial sums in shared memory in a fixed
+// order.
 // A tile holds rows c, c + q, c + 2q, ... of one residue class c mod q (q = 16 / gcd(row bytes, 16)), so its
 // 16 rows' bytes sit at one offset within 16 bytes: every warp loads its stages with one tiled TMA copy each
 // (the stack seen as groups of q rows), rows an odd number of 16-byte chunks apart, through a ring of
@@ -89,8 +90,11 @@ __device__ __forceinline__ uint32_t prmt_sr(uint32_t a, uint32_t c) {
 }
 constexpr int kM8GridRep = 16;  // copies of the IQ3_S grid in shared memory
 
+// NB blocks a stage: two (512 columns, 16 rows of 220 bytes in 240-byte rows of the ring slot) where the
+// width allows, else one (110 bytes in 144)
+template <int NB>
 struct M8IQ3S {
-    static constexpr int kKind = 21, kStageCols = 256, kStageBytes = 110, kRS = 144, kRuns = 8;
+    static constexpr int kKind = 21, kStageCols = 256 * NB, kStageBytes = 110 * NB, kRS = NB == 2 ? 240 : 144;
     static constexpr bool kLut = true;
     // run R of the stage: the two rows' groups (bq / bs: the lane's qs / sign bytes), lutl = this lane's grid copy
     template <int R>
@@ -123,9 +127,10 @@ struct M8IQ3S {
         t[0] += m0 * (acc[0] * 128 + acc[1]);
         t[1] += m1 * (acc[2] * 128 + acc[3]);
     }
-    // one stage (= one block) of rows gid (j = 0) and gid + 8 (j = 1): partial sums of the two rows
-    __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t* lut,
-                                 const uint8_t* xh, const uint8_t* xl, float xs, float (&total)[2]) {
+    // one block of rows gid (j = 0) and gid + 8 (j = 1): partial sums of the two rows
+    __device__ static __forceinline__ void block(const uint8_t* r0, const uint8_t* r1, int tig, int gid,
+                                                 const uint32_t* lut, const uint8_t* xh, const uint8_t* xl, float xs,
+                                                 float (&total)[2]) {
         const uint32_t rb[2] = {smem_addr(r0), smem_addr(r1)};
         const uint32_t lutl = smem_addr(lut) + 4u * static_cast<uint32_t>((4 * gid + tig) & (kM8GridRep - 1));
         uint32_t m[2][2], qh[2][2], bq[2], bs[2];
@@ -157,6 +162,12 @@ struct M8IQ3S {
         total[0] = fmaf(d[0] * k, static_cast<float>(t[0]), total[0]);
         total[1] = fmaf(d[1] * k, static_cast<float>(t[1]), total[1]);
     }
+    // one stage: NB blocks, each with its own activation scale (xs[0], xs[1])
+    __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t* lut,
+                                 const uint8_t* xh, const uint8_t* xl, const float* xs, float (&total)[2]) {
+        block(r0, r1, tig, gid, lut, xh, xl, xs[0], total);
+        if constexpr (NB == 2) block(r0 + 110, r1 + 110, tig, gid, lut, xh + 256, xl + 256, xs[1], total);
+    }
 };
 
 // the IQ3_S grid (entries 0..511 of the sign-folded table built from gguf-py's grid: sign bits 0), 16 times
@@ -171,13 +182,13 @@ __device__ __forceinline__ void m8_fill_grid(uint32_t* lut) {
 // ---------------------------------------------------------------- Q8_0
 // (34 bytes: d 0, qs 2..33.) A stage is four runs; in run r lane tig takes codes 8 tig .. 8 tig + 7.
 struct M8Q8_0 {
-    static constexpr int kKind = 8, kStageCols = 128, kStageBytes = 136, kRS = 176, kRuns = 4;
+    static constexpr int kKind = 8, kStageCols = 128, kStageBytes = 136, kRS = 176;
     static constexpr bool kLut = false;
     __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t*,
-                                 const uint8_t* xh, const uint8_t* xl, float xs, float (&total)[2]) {
+                                 const uint8_t* xh, const uint8_t* xl, const float* xs, float (&total)[2]) {
         const uint8_t* rb[2] = {r0, r1};
         const uint8_t* xsrc = gid == 0 ? xh : xl;
-        const float k = xs * (1.0f / 128.0f);
+        const float k = xs[0] * (1.0f / 128.0f);  // (a stage lies within one 256-column scale block)
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
             uint32_t a[2][2];
@@ -424,7 +435,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
             const uint8_t* st = my_ring + cur * kSlot + off;
             const int xc = s * D::kStageCols;
             D::stage(st + gid * D::kRS, st + (gid + 8) * D::kRS, tig, gid, lut, xh + xc, xl + xc,
-                     xsc[xc / kM8XBlock], total);
+                     xsc + xc / kM8XBlock, total);
         }
         // the team's partial sums of this job's 16 rows, added in warp order
         float* rq = red + (tid_team * team) * 16;
@@ -694,12 +705,12 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
             const int off = (w.cls * static_cast<int>(P.row_bytes) + s * P.stage_bytes) & 15;
             const uint8_t* st = my_ring + cur * slot_bytes + off;
             const int xc = s * P.stage_cols;
-            if (P.kind == M8IQ3S::kKind)
-                M8IQ3S::stage(st + gid * M8IQ3S::kRS, st + (gid + 8) * M8IQ3S::kRS, tig, gid, lut, xh + xc, xl + xc,
-                              xsc[xc / kM8XBlock], total);
+            if (P.kind == M8IQ3S<2>::kKind)
+                M8IQ3S<2>::stage(st + gid * M8IQ3S<2>::kRS, st + (gid + 8) * M8IQ3S<2>::kRS, tig, gid, lut, xh + xc, xl + xc,
+                              xsc + xc / kM8XBlock, total);
             else
                 M8Q8_0::stage(st + gid * M8Q8_0::kRS, st + (gid + 8) * M8Q8_0::kRS, tig, gid, lut, xh + xc, xl + xc,
-                              xsc[xc / kM8XBlock], total);
+                              xsc + xc / kM8XBlock, total);
         }
         // the team's partial sums of this job's 16 rows, added in warp order
         float* rq = red + (tid_team * team) * 16;
@@ -844,7 +855,7 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         mv8s_kernel<D><<<grid, kM8Threads, smem, st>>>(a, maps);
         return launch_status("matvec (int8 tensor cores)");
     };
-    if (kind0 == M8IQ3S::kKind) return go(M8IQ3S{});
+    if (kind0 == M8IQ3S<2>::kKind) return cols % M8IQ3S<2>::kStageCols ? go(M8IQ3S<1>{}) : go(M8IQ3S<2>{});
     if (kind0 == M8Q8_0::kKind) return go(M8Q8_0{});
     return 1;
 }
@@ -872,8 +883,8 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
     for (int i = 0; i < n; ++i) {
         const M8Spec& sp = specs[i];
         int stage_cols, stage_bytes, rs;
-        if (sp.kind == M8IQ3S::kKind) {
-            stage_cols = M8IQ3S::kStageCols, stage_bytes = M8IQ3S::kStageBytes, rs = M8IQ3S::kRS;
+        if (sp.kind == M8IQ3S<2>::kKind) {  // (widths of an odd number of 256 columns go problem by problem)
+            stage_cols = M8IQ3S<2>::kStageCols, stage_bytes = M8IQ3S<2>::kStageBytes, rs = M8IQ3S<2>::kRS;
             lut = true;
         } else if (sp.kind == M8Q8_0::kKind) {
             stage_cols = M8Q8_0::kStageCols, stage_bytes = M8Q8_0::kStageBytes, rs = M8Q8_0::kRS;
