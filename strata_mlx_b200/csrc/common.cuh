@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/strata_moe.h"
 
@@ -42,6 +43,33 @@ int set_max_smem(const void* kernel, int bytes);  // defined in smoe_api.cu
 template <typename K>
 inline int max_smem(K* kernel, int bytes) {
     return set_max_smem(reinterpret_cast<const void*>(kernel), bytes);
+}
+
+// ---- programmatic dependent launch
+//
+// A kernel launched with launch_pdl may start while the kernel before it in the stream is still running (its
+// CTAs are placed as that kernel's CTAs finish). Before pdl_wait() it may only set up its own shared memory and
+// read data no kernel writes (weights, codebooks); pdl_wait() returns once the kernel before it has completed
+// and its writes are visible. After the wait (at the end of its main work) the kernel calls pdl_release(),
+// letting the next kernel start placing CTAs: every kernel before this one has then completed. Launched
+// without the attribute, pdl_wait() returns at once.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // ---- device side: loads of little-endian fields of a block (any alignment)

@@ -290,6 +290,9 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         tc::fence_barrier_init();
     }
     __syncwarp();
+    // the codebook fills while the kernel before this one finishes; expert indices and activations wait for it
+    if constexpr (D::kLut) m8_fill_grid(lut);
+    pdl_wait();
 
     using Where = M8WhereS;
     auto locate = [&](int job) {
@@ -342,7 +345,6 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     if (lane == 0)
         for (int i = 0; i < ns - 1 && i < items; ++i) issue();
 
-    if constexpr (D::kLut) m8_fill_grid(lut);
     // the activation rows this CTA's jobs read (all of them when there are more than kM8SMaskRows)
     uint32_t* need = reinterpret_cast<uint32_t*>(where_ring + kM8Warps * 4);  // kM8SMaskRows bits
     const bool masked = a.xrows <= kM8SMaskRows;
@@ -459,6 +461,9 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         }
         team_sync();
     }
+    // the next kernel may start placing its CTAs (releasing right after the wait instead measured slower: the
+    // waiting CTAs of the next kernel crowd the running ones)
+    pdl_release();
     // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
     // a wait gave up)
     if (!ok && lane == 0)
@@ -537,14 +542,18 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     uint8_t* my_ring = ring + size_t(warp) * ns * slot_bytes;
     uint64_t* my_bars = bars + warp * kM8MaxSlots;
 
-    // the expert indices of every problem's pairs, once, in shared memory (a job's place needs no global load)
-    for (int pr = 0; pr < L.nprob; ++pr)
-        for (int i = threadIdx.x; i < L.p[pr].pairs; i += kM8Threads) sidx[L.p[pr].idx0 + i] = L.p[pr].idx[i];
+    // barriers and the codebook are set up while the kernel before this one finishes; expert indices and
+    // activations wait for it
     if (lane == 0) {
         for (int i = 0; i < ns; ++i) tc::mbar_init(&my_bars[i], 1);
         tc::fence_barrier_init();
     }
     for (int i = threadIdx.x; i < kM8MaxRows / 32; i += kM8Threads) need[i] = 0u;
+    if (L.lut) m8_fill_grid(lut);
+    pdl_wait();
+    // the expert indices of every problem's pairs, once, in shared memory (a job's place needs no global load)
+    for (int pr = 0; pr < L.nprob; ++pr)
+        for (int i = threadIdx.x; i < L.p[pr].pairs; i += kM8Threads) sidx[L.p[pr].idx0 + i] = L.p[pr].idx[i];
     __syncthreads();
 
     auto locate = [&](int job) {
@@ -610,7 +619,6 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
         for (int i = 0; i < ns - 1; ++i) issue();
     }
 
-    if (L.lut) m8_fill_grid(lut);
     // the activation rows this CTA's jobs read
     if (lane == 0)
         for (int job = 0; job < my_jobs; ++job) {
@@ -730,6 +738,9 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
         }
         team_sync();
     }
+    // the next kernel may start placing its CTAs (releasing right after the wait instead measured slower: the
+    // waiting CTAs of the next kernel crowd the running ones)
+    pdl_release();
     // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
     // a wait gave up)
     if (!ok && lane == 0)
@@ -852,7 +863,7 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
         const size_t smem = fixed + ns * slot;
         if (int s = max_smem(mv8s_kernel<D>, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
-        mv8s_kernel<D><<<grid, kM8Threads, smem, st>>>(a, maps);
+        launch_pdl(mv8s_kernel<D>, dim3(grid), dim3(kM8Threads), smem, st, a, maps);
         return launch_status("matvec (int8 tensor cores)");
     };
     if (kind0 == M8IQ3S<2>::kKind) return cols % M8IQ3S<2>::kStageCols ? go(M8IQ3S<1>{}) : go(M8IQ3S<2>{});
@@ -1008,7 +1019,7 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
     const size_t smem = fixed + ns * slot;
     if (int s = max_smem(mv8_kernel, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
-    mv8_kernel<<<grid, kM8Threads, smem, st>>>(L, maps);
+    launch_pdl(mv8_kernel, dim3(grid), dim3(kM8Threads), smem, st, L, maps);
     return launch_status("matvec (int8 tensor cores)");
 }
 

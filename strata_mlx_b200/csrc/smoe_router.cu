@@ -33,12 +33,25 @@ __device__ __forceinline__ void load8<float>(const float* p, float* v) {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
 
+// The lane's first chunks of its row (router_rows' first round), loaded ahead: weights no kernel writes, so a
+// launch may load them before it waits for the kernel before it.
+__device__ __forceinline__ void router_first(const __half* __restrict__ row, bool live, int64_t hidden,
+                                             float (&wv)[4][8]) {
+    const int quarter = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;
+    const int64_t chunks = hidden >> 3, c0 = quarter * 32 + lane;
+    if (!live) return;
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+        if (c0 + 128 * u < chunks) load8<__half>(row + 8 * (c0 + 128 * u), wv[u]);
+}
+
 // acc[t] += this lane's share of row . x[t0 + t] for the CTA's layout (four warps to a row, every fourth
 // 16-byte chunk); four chunks of the row in flight at once (hidden 4096: all of this lane's), then their
-// products in chunk order
+// products in chunk order. wv holds the first round's chunks (router_first).
 template <typename XT>
 __device__ __forceinline__ void router_rows(const __half* __restrict__ row, bool live, const XT* __restrict__ x,
-                                            int64_t hidden, int64_t t0, int nt, float (&acc)[kRtTokens]) {
+                                            int64_t hidden, int64_t t0, int nt, float (&acc)[kRtTokens],
+                                            float (&wv)[4][8]) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int quarter = warp & 3;
 #pragma unroll
@@ -46,10 +59,11 @@ __device__ __forceinline__ void router_rows(const __half* __restrict__ row, bool
     if (!live) return;
     const int64_t chunks = hidden >> 3;
     for (int64_t c0 = quarter * 32 + lane; c0 < chunks; c0 += 4 * 128) {
-        float wv[4][8];
+        if (c0 >= 4 * 128) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-            if (c0 + 128 * u < chunks) load8<__half>(row + 8 * (c0 + 128 * u), wv[u]);
+            for (int u = 0; u < 4; ++u)
+                if (c0 + 128 * u < chunks) load8<__half>(row + 8 * (c0 + 128 * u), wv[u]);
+        }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const int64_t c = c0 + 128 * u;
@@ -77,8 +91,9 @@ __global__ void __launch_bounds__(256) router_kernel(const __half* __restrict__ 
     const int64_t e = int64_t(blockIdx.x) * 2 + local_row;
     const int64_t t0 = int64_t(blockIdx.y) * kRtTokens;
     const int nt = static_cast<int>(min(int64_t(kRtTokens), tokens - t0));
-    float acc[kRtTokens];
-    router_rows(w + e * hidden, e < experts, x, hidden, t0, nt, acc);
+    float acc[kRtTokens], wv[4][8];
+    router_first(w + e * hidden, e < experts, hidden, wv);
+    router_rows(w + e * hidden, e < experts, x, hidden, t0, nt, acc, wv);
 #pragma unroll
     for (int t = 0; t < kRtTokens; ++t) acc[t] = warp_sum(acc[t]);
     if (lane == 0) {
@@ -192,8 +207,13 @@ __global__ void __launch_bounds__(256) route_kernel(const __half* __restrict__ w
     const int64_t t0 = int64_t(blockIdx.y) * kRtTokens;
     const int nt = static_cast<int>(min(int64_t(kRtTokens), tokens - t0));
     const int64_t rows = experts + (gw != nullptr ? 1 : 0);
-    float acc[kRtTokens];
-    router_rows(e < experts ? w + e * hidden : gw, e < rows, x, hidden, t0, nt, acc);
+    const __half* row = e < experts ? w + e * hidden : gw;
+    float acc[kRtTokens], wv[4][8];
+    // the router's weights load while the kernel before this one finishes; x, the outputs and the counters wait
+    router_first(row, e < rows, hidden, wv);
+    pdl_wait();
+    pdl_release();
+    router_rows(row, e < rows, x, hidden, t0, nt, acc, wv);
 #pragma unroll
     for (int t = 0; t < kRtTokens; ++t) acc[t] = warp_sum(acc[t]);
     if (lane == 0) {
@@ -404,13 +424,13 @@ extern "C" int smoe_route(const uint16_t* weight, const uint16_t* gate_weight, c
         const XT* xp = static_cast<const XT*>(x);
         XT* go_ = static_cast<XT*>(gate_out);
         if (experts <= 256)
-            route_kernel<XT, 8><<<grid, 256, 0, st>>>(w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(route_kernel<XT, 8>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
         else if (experts <= 512)
-            route_kernel<XT, 16><<<grid, 256, 0, st>>>(w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(route_kernel<XT, 16>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
         else if (experts <= 1024)
-            route_kernel<XT, 32><<<grid, 256, 0, st>>>(w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(route_kernel<XT, 32>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
         else
-            route_kernel<XT, 64><<<grid, 256, 0, st>>>(w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(route_kernel<XT, 64>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
     };
     if (x_dtype == SMOE_F16) go(__half{});
     else if (x_dtype == SMOE_F32) go(float{});
