@@ -49,16 +49,41 @@ inline int max_smem(K* kernel, int bytes) {
 //
 // A kernel launched with launch_pdl may start while the kernel before it in the stream is still running (its
 // CTAs are placed as that kernel's CTAs finish). Before pdl_wait() it may only set up its own shared memory and
-// read data no kernel writes (weights, codebooks); pdl_wait() returns once the kernel before it has completed
-// and its writes are visible. After the wait (at the end of its main work) the kernel calls pdl_release(),
-// letting the next kernel start placing CTAs: every kernel before this one has then completed. Launched
-// without the attribute, pdl_wait() returns at once.
+// read data that the launch before it does not write; pdl_wait() returns once that launch has completed and
+// its writes are visible. Every kernel launched here calls pdl_release() only after its own pdl_wait(), so when
+// a launch starts, every launch before the one just ahead of it has completed: data older than the previous
+// launch (weights, codebooks, the router's choice two launches back) may be read before the wait, which
+// pdl_early() tells the host. Outputs are written only after the wait. Launched without the attribute, or
+// behind a kernel that never releases (any other library's), a kernel starts after its predecessor completed
+// and pdl_wait() returns at once.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
+// The device memory one launch writes.
+struct Writes {
+    static constexpr int kMax = 6;
+    const void* p[kMax] = {};
+    size_t n[kMax] = {};
+    int count = 0;
+    Writes& add(const void* ptr, size_t bytes) {
+        if (ptr != nullptr && bytes > 0 && count < kMax) {
+            p[count] = ptr;
+            n[count] = bytes;
+            ++count;
+        }
+        return *this;
+    }
+};
+// Record what the launch just made on `st` with launch_pdl writes (the next launch on `st` may overlap it).
+void pdl_note(cudaStream_t st, const Writes& w);  // defined in smoe_api.cu
+// Whether the next launch on `st` may read [p, p + n) before its pdl_wait(): the last launch_pdl launch on
+// `st` does not write it. (A record older than the stream's true last launch errs safe: that launch is then
+// another kernel, which the next launch waits for in full.)
+bool pdl_early(cudaStream_t st, const void* p, size_t n);  // defined in smoe_api.cu
+
 template <typename... KArgs, typename... Args>
-inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                              Args&&... args) {
+inline cudaError_t launch_pdl(const Writes& writes, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -69,7 +94,9 @@ inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+    pdl_note(st, writes);
+    return e;
 }
 
 // ---- device side: loads of little-endian fields of a block (any alignment)

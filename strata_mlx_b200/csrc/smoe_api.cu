@@ -26,6 +26,33 @@ int set_max_smem(const void* kernel, int bytes) {
     return 0;
 }
 
+namespace {
+struct PdlRecord {
+    Writes w;
+};
+std::mutex g_pdl_mu;
+std::map<cudaStream_t, PdlRecord> g_pdl;  // stream -> what its last launch_pdl launch writes
+}  // namespace
+
+void pdl_note(cudaStream_t st, const Writes& w) {
+    std::lock_guard<std::mutex> lock(g_pdl_mu);
+    g_pdl[st].w = w;
+}
+
+bool pdl_early(cudaStream_t st, const void* p, size_t n) {
+    if (p == nullptr || n == 0) return true;
+    std::lock_guard<std::mutex> lock(g_pdl_mu);
+    auto it = g_pdl.find(st);
+    if (it == g_pdl.end()) return true;
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(p), a1 = a0 + n;
+    const Writes& w = it->second.w;
+    for (int i = 0; i < w.count; ++i) {
+        const uintptr_t b0 = reinterpret_cast<uintptr_t>(w.p[i]), b1 = b0 + w.n[i];
+        if (a0 < b1 && b0 < a1) return false;
+    }
+    return true;
+}
+
 }  // namespace smoe
 
 using namespace smoe;

@@ -236,6 +236,9 @@ struct M8Args {
     const float* cw;
     const __half* cg;
     int ck;
+    // bit 0: idx, bit 1: the activations may be read before pdl_wait (the launch just before this one does not
+    // write them), so the first weight copies and the activation split overlap that launch's end
+    int early;
 };
 // a job's place (worked out once per job, 32-bit): problem, pair, expert, the tile's residue class and block
 // of 16 q rows, the first row of its TMA box, the activation row
@@ -290,9 +293,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         tc::fence_barrier_init();
     }
     __syncwarp();
-    // the codebook fills while the kernel before this one finishes; expert indices and activations wait for it
+    // the codebook fills while the kernel before this one finishes; so do the first weight copies and the
+    // activation split when their inputs are older than that kernel (a.early); the rest waits for it
     if constexpr (D::kLut) m8_fill_grid(lut);
-    pdl_wait();
+    const bool early_idx = a.early & 1, early_x = (a.early >> 1) & 1;
+    if (!early_idx) pdl_wait();
 
     using Where = M8WhereS;
     auto locate = [&](int job) {
@@ -345,7 +350,8 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     if (lane == 0)
         for (int i = 0; i < ns - 1 && i < items; ++i) issue();
 
-    // the activation rows this CTA's jobs read (all of them when there are more than kM8SMaskRows)
+    // the activation rows this CTA's jobs read (all of them when there are more than kM8SMaskRows): a job's row
+    // is its pair's, pair / share, known without the expert index
     uint32_t* need = reinterpret_cast<uint32_t*>(where_ring + kM8Warps * 4);  // kM8SMaskRows bits
     const bool masked = a.xrows <= kM8SMaskRows;
     if (masked) {
@@ -353,11 +359,14 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         __syncthreads();
         if (lane == 0 && my_stages > 0)
             for (int job = 0; job < my_jobs; ++job) {
-                const int xr = locate(job).xr;
+                const int j = q0 + job * nteams;
+                const int pair = (j - (j / per_prob) * per_prob) / a.tiles;
+                const int xr = pair / static_cast<int>(a.share);
                 atomicOr(&need[xr >> 5], 1u << (xr & 31));
             }
         __syncthreads();
     }
+    if (early_idx && !early_x) pdl_wait();
     // the activations, split per 256-column block into int8 hi and lo: a warp per block, 8 values a lane
     for (int blk = warp; blk < a.xrows * xblocks; blk += kM8Warps) {
         const int xr = blk / xblocks, b = blk % xblocks;
@@ -401,6 +410,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         *reinterpret_cast<uint2*>(xlo + int64_t(xr) * a.cols + c0) = make_uint2(lw[0], lw[1]);
         if (lane == 0) xscale[blk] = s;
     }
+    if (early_idx && early_x) pdl_wait();  // (every path has waited once from here on: outputs, the combine)
     __syncthreads();
 
     // a team of one warp needs no named barrier (there are 16, barrier 0 is __syncthreads')
@@ -863,7 +873,13 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
         const size_t smem = fixed + ns * slot;
         if (int s = max_smem(mv8s_kernel<D>, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
-        launch_pdl(mv8s_kernel<D>, dim3(grid), dim3(kM8Threads), smem, st, a, maps);
+        const size_t xb = size_t(xrows) * cols * sizeof(__half);
+        a.early = (pdl_early(st, idx, size_t(pairs) * 4) ? 1 : 0) |
+                  ((x ? pdl_early(st, x, xb) : pdl_early(st, gate, xb) && pdl_early(st, up, xb)) ? 2 : 0);
+        Writes wr;
+        wr.add(o0, size_t(pairs) * rows * sizeof(__half));
+        if (nprob == 2 && o1 != o0) wr.add(o1, size_t(pairs) * rows * sizeof(__half));
+        launch_pdl(wr, mv8s_kernel<D>, dim3(grid), dim3(kM8Threads), smem, st, a, maps);
         return launch_status("matvec (int8 tensor cores)");
     };
     if (kind0 == M8IQ3S<2>::kKind) return cols % M8IQ3S<2>::kStageCols ? go(M8IQ3S<1>{}) : go(M8IQ3S<2>{});
@@ -1019,7 +1035,9 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
     const size_t smem = fixed + ns * slot;
     if (int s = max_smem(mv8_kernel, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
-    launch_pdl(mv8_kernel, dim3(grid), dim3(kM8Threads), smem, st, L, maps);
+    Writes wr;
+    for (int i = 0; i < n; ++i) wr.add(L.p[i].out, size_t(L.p[i].pairs) * L.p[i].rows * sizeof(__half));
+    launch_pdl(wr, mv8_kernel, dim3(grid), dim3(kM8Threads), smem, st, L, maps);
     return launch_status("matvec (int8 tensor cores)");
 }
 

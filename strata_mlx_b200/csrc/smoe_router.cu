@@ -423,14 +423,17 @@ extern "C" int smoe_route(const uint16_t* weight, const uint16_t* gate_weight, c
         using XT = decltype(xt);
         const XT* xp = static_cast<const XT*>(x);
         XT* go_ = static_cast<XT*>(gate_out);
+        Writes wr;
+        wr.add(logits, size_t(tokens) * experts * 4).add(idx, size_t(tokens) * k * 4).add(weights, size_t(tokens) * k * 4);
+        wr.add(gate_out, size_t(tokens) * sizeof(XT)).add(counters, smoe_route_counters(tokens));
         if (experts <= 256)
-            launch_pdl(route_kernel<XT, 8>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(wr, route_kernel<XT, 8>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
         else if (experts <= 512)
-            launch_pdl(route_kernel<XT, 16>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(wr, route_kernel<XT, 16>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
         else if (experts <= 1024)
-            launch_pdl(route_kernel<XT, 32>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(wr, route_kernel<XT, 32>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
         else
-            launch_pdl(route_kernel<XT, 64>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(wr, route_kernel<XT, 64>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
     };
     if (x_dtype == SMOE_F16) go(__half{});
     else if (x_dtype == SMOE_F32) go(float{});
