@@ -492,14 +492,14 @@ struct M8Prob {
     __half* out;
     int64_t rows, row_bytes;
     uint32_t experts;
-    int kind;                     // 21 IQ3_S, 8 Q8_0
+    int kind;                     // 21 IQ3_S (two-block stages), 8 Q8_0
     int stage_cols, stage_bytes;  // a stage of one row
     int rs;                       // its rows' stride in a ring slot (an odd number of 16-byte chunks)
     int q, lq;                    // rows per 16-byte aligned group of rows (a power of two) and its log2
     int tiles, stages;            // tiles of 16 rows (of one residue class) per pair, stages per row
     int job0, jobs;               // its jobs in the launch: [job0, job0 + jobs)
     int pairs, share, xs;         // pairs, pairs per activation row, activation source
-    int idx0;                     // its first pair in the shared-memory copy of the expert indices
+    int early;                    // idx may be read before pdl_wait (the launch ahead does not write it)
 };
 // An activation source: rows of `cols` float16, or the SwiGLU of two such (down's input).
 struct M8X {
@@ -508,25 +508,67 @@ struct M8X {
     int row0;    // its first row among all sources' rows
     int scale0;  // its first block scale
     int64_t byte0;  // its hi values' offset in the split area (its lo values follow rows x cols later)
+    int early;      // may be read before pdl_wait
 };
 constexpr int kM8MaxProbs = 4, kM8MaxX = 4;
-constexpr int kM8MaxRows = 1024;  // activation rows of all sources, and pairs of all problems
+constexpr int kM8MaxRows = 1024;   // activation rows of all sources
+constexpr int kM8MaxWarpJobs = 32;  // jobs of one warp (one per lane of its job table)
 struct M8Launch {
     M8Prob p[kM8MaxProbs];
     M8X x[kM8MaxX];
-    int nprob, nx, jobs, team, nslots, slot_bytes, lut, pairs, scales;
+    int nprob, nx, jobs, team, nslots, slot_bytes, lut, scales;
     int64_t xbytes;
 };
 struct alignas(64) M8Maps {
     CUtensorMap w[kM8MaxProbs];
 };
-// a job's place: problem, pair, expert, the tile's residue class and block of 16 q rows, the first row of its
-// TMA box, the activation row (among all sources')
-struct M8Where {
-    int prob, cls, blk, xr, pair, y;
-    uint32_t e;
-};
 
+// One 256-column block of an activation row split into int8 hi and lo and its scale, by one warp (8 values a
+// lane): v = s (hi + lo / 128), s = max|v| / 127. With gate set, v = swiglu(gate, up) (the same function, so
+// the same float16 bits, as the separate SwiGLU kernel).
+__device__ __forceinline__ void m8_split(const __half* x, const __half* gate, const __half* up, int64_t at,
+                                         int8_t* hi, int8_t* lo, float* scale, int lane) {
+    float v[8];
+    if (gate) {
+        const uint4 gr = *reinterpret_cast<const uint4*>(gate + at);
+        const uint4 ur = *reinterpret_cast<const uint4*>(up + at);
+        const __half* gh = reinterpret_cast<const __half*>(&gr);
+        const __half* uh = reinterpret_cast<const __half*>(&ur);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = __half2float(swiglu_one(gh[i], uh[i]));
+    } else {
+        const uint4 raw = *reinterpret_cast<const uint4*>(x + at);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h2[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
+        }
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float s = amax / 127.0f, inv = amax > 0.f ? 127.0f / amax : 0.f;
+    uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float hf = fminf(fmaxf(rintf(v[i] * inv), -127.f), 127.f);
+        const float lf = fminf(fmaxf(rintf((v[i] - hf * s) * (128.0f * inv)), -127.f), 127.f);
+        hw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(hf)) & 255u) << (8 * (i & 3));
+        lw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(lf)) & 255u) << (8 * (i & 3));
+    }
+    *reinterpret_cast<uint2*>(hi) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(lo) = make_uint2(lw[0], lw[1]);
+    if (lane == 0) *scale = s;
+}
+
+// Layout: jobs go round-robin over all the launch's teams, CTA-fastest (every SM gets a share of every
+// problem, the costliest problems first). A warp's jobs (at most 32) are worked out once, lane l holding its
+// l-th job's place in registers; the copy cursor and the consumer read them with a shuffle per job, and every
+// per-stage step is warp-uniform arithmetic (lane 0 alone issues the copy).
 __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constant__ M8Launch L,
                                                             const __grid_constant__ M8Maps maps) {
     extern __shared__ __align__(128) uint8_t sm[];
@@ -534,8 +576,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     uint8_t* ring = sm;                                                                   // [warp][slot]
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * slot_bytes);  // [warp][slot]
     float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);                 // [16 warps][16 rows]
-    uint32_t* sidx = reinterpret_cast<uint32_t*>(red + kM8Warps * 16);                    // [kM8MaxRows]
-    uint32_t* need = sidx + kM8MaxRows;                                                   // kM8MaxRows bits
+    uint32_t* need = reinterpret_cast<uint32_t*>(red + kM8Warps * 16);                    // kM8MaxRows bits
     uint32_t* lut = need + kM8MaxRows / 32;                                               // 512 x 16 words (IQ3_S)
     float* xscale = reinterpret_cast<float*>(lut + (L.lut ? 8192 : 0));
     int8_t* xsplit = reinterpret_cast<int8_t*>(xscale + ((L.scales + 3) & ~3));
@@ -545,147 +586,118 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     if (smem_addr(sm) & 127u) return;  // a tiled copy's destination is 128-byte aligned (the launch gives that)
     const int team = L.team, teams = kM8Warps / team;
     const int tid_team = warp / team, kq = warp % team;
-    // jobs go round-robin over all the launch's teams, CTA-fastest (every SM gets a share of every problem)
     const int nteams = gridDim.x * teams;
     const int q0 = tid_team * gridDim.x + blockIdx.x;
-    const int my_jobs = q0 < L.jobs ? (L.jobs - q0 + nteams - 1) / nteams : 0;
+    const int my_jobs = q0 < L.jobs ? min((L.jobs - q0 + nteams - 1) / nteams, kM8MaxWarpJobs) : 0;
     uint8_t* my_ring = ring + size_t(warp) * ns * slot_bytes;
     uint64_t* my_bars = bars + warp * kM8MaxSlots;
 
-    // barriers and the codebook are set up while the kernel before this one finishes; expert indices and
-    // activations wait for it
+    // barriers and the codebook are set up while the kernel before this one finishes
     if (lane == 0) {
         for (int i = 0; i < ns; ++i) tc::mbar_init(&my_bars[i], 1);
         tc::fence_barrier_init();
     }
     for (int i = threadIdx.x; i < kM8MaxRows / 32; i += kM8Threads) need[i] = 0u;
     if (L.lut) m8_fill_grid(lut);
-    pdl_wait();
-    // the expert indices of every problem's pairs, once, in shared memory (a job's place needs no global load)
-    for (int pr = 0; pr < L.nprob; ++pr)
-        for (int i = threadIdx.x; i < L.p[pr].pairs; i += kM8Threads) sidx[L.p[pr].idx0 + i] = L.p[pr].idx[i];
-    __syncthreads();
 
-    auto locate = [&](int job) {
-        const int j = q0 + job * nteams;
-        M8Where w;
-        w.prob = 0;
+    // lane l's job: problem, pair, tile (residue class and block), activation row; then its expert and the
+    // first row of its TMA box, once the indices may be read
+    int j_prob = 0, j_pair = 0, j_cls = 0, j_blk = 0, j_xr = 0, j_y = 0, j_valid = 0;
+    const bool has = lane < my_jobs;
+    if (has) {
+        const int j = q0 + lane * nteams;
 #pragma unroll
         for (int pr = 1; pr < kM8MaxProbs; ++pr)
-            if (pr < L.nprob && j >= L.p[pr].job0) w.prob = pr;
-        const M8Prob& P = L.p[w.prob];
+            if (pr < L.nprob && j >= L.p[pr].job0) j_prob = pr;
+        const M8Prob& P = L.p[j_prob];
         const int rest = j - P.job0;
-        w.pair = rest / P.tiles;
-        const int tile = rest - w.pair * P.tiles;
-        w.cls = tile & (P.q - 1);
-        w.blk = tile >> P.lq;
-        w.e = sidx[P.idx0 + w.pair];
-        w.y = static_cast<int>((int64_t(w.e < P.experts ? w.e : 0) * P.rows) >> P.lq) + 16 * w.blk;
-        w.xr = L.x[P.xs].row0 + w.pair / P.share;
-        return w;
+        j_pair = rest / P.tiles;
+        const int tile = rest - j_pair * P.tiles;
+        j_cls = tile & (P.q - 1);
+        j_blk = tile >> P.lq;
+        j_xr = L.x[P.xs].row0 + j_pair / P.share;
+    }
+    auto place = [&](bool now) {  // the expert of lane l's job, for the jobs whose indices may be read now
+        if (has && now) {
+            const M8Prob& P = L.p[j_prob];
+            const uint32_t e = __ldg(P.idx + j_pair);
+            j_valid = e < P.experts ? 1 : 0;
+            j_y = static_cast<int>((int64_t(j_valid ? e : 0) * P.rows) >> P.lq) + 16 * j_blk;
+        }
     };
+    place(has && L.p[j_prob].early);
+    if (has) atomicOr(&need[j_xr >> 5], 1u << (j_xr & 31));
+    __syncthreads();
+
+    // the copy cursor (warp-uniform): the next item's job, its stage index k of n, slot, byte position in the
+    // row, box row; lane 0 issues
+    int i_job = 0, i_k = 0, i_n = 0, i_slot = 0, i_pos = 0, i_step = 0, i_y = 0, i_map = 0, i_valid = 0, i_bytes = 0;
+    int issued = 0;
     auto stages_of = [&](int prob) {
         const int S = L.p[prob].stages;
         return S > kq ? (S - kq + team - 1) / team : 0;
     };
-
-    // the copy cursor (lane 0): the next item (a job's stage) to copy, its slot; it skips jobs in which this
-    // warp has no stage
-    int pre_job = 0, pre_k = 0, pre_slot = 0, pre_s = kq;
-    M8Where pre_w{};
-    int pre_n = 0;
-    auto seek = [&]() {  // from pre_job on, the first job with a stage for this warp
-        for (; pre_job < my_jobs; ++pre_job) {
-            pre_w = locate(pre_job);
-            pre_n = stages_of(pre_w.prob);
-            if (pre_n > 0) break;
+    // move the cursor to job `job` or the first after it with a stage for this warp
+    auto seek = [&](int job) {
+        for (i_job = job; i_job < my_jobs; ++i_job) {
+            const int pr = __shfl_sync(0xffffffffu, j_prob, i_job);
+            i_n = stages_of(pr);
+            if (i_n == 0) continue;
+            const M8Prob& P = L.p[pr];
+            i_map = pr;
+            i_k = 0;
+            i_pos = __shfl_sync(0xffffffffu, j_cls, i_job) * static_cast<int>(P.row_bytes) + kq * P.stage_bytes;
+            i_step = team * P.stage_bytes;
+            i_y = __shfl_sync(0xffffffffu, j_y, i_job);
+            i_valid = __shfl_sync(0xffffffffu, j_valid, i_job);
+            i_bytes = 16 * P.rs;
+            return;
         }
     };
-    // lane 0 starts the TMA copy of the cursor's item into its slot and moves the cursor on; a pair naming no
-    // expert copies nothing and completes the slot's phase with a plain arrive, so every item takes one phase
+    // issue the cursor's item (a pair naming no expert copies nothing and completes the slot's phase with a
+    // plain arrive, so every item takes one phase) and move on
     auto issue = [&]() {
-        if (pre_job >= my_jobs) return;
-        const M8Prob& P = L.p[pre_w.prob];
-        if (pre_w.e >= P.experts) {
-            tc::mbar_arrive(&my_bars[pre_slot]);
-        } else {
-            const int xb = (pre_w.cls * static_cast<int>(P.row_bytes) + pre_s * P.stage_bytes) & ~15;
-            tc::fence_proxy_async_smem();
-            tc::mbar_arrive_expect_tx(&my_bars[pre_slot], static_cast<uint32_t>(16 * P.rs));
-            tc::tma_load_2d(smem_addr(my_ring + pre_slot * slot_bytes), &maps.w[pre_w.prob], xb >> 2, pre_w.y,
-                            &my_bars[pre_slot]);
+        if (lane == 0) {
+            if (i_valid) {
+                tc::mbar_arrive_expect_tx(&my_bars[i_slot], static_cast<uint32_t>(i_bytes));
+                tc::tma_load_2d(smem_addr(my_ring + i_slot * slot_bytes), &maps.w[i_map], (i_pos & ~15) >> 2, i_y,
+                                &my_bars[i_slot]);
+            } else {
+                tc::mbar_arrive(&my_bars[i_slot]);
+            }
         }
-        if (++pre_slot == ns) pre_slot = 0;
-        pre_s += team;
-        if (++pre_k == pre_n) {
-            pre_k = 0;
-            pre_s = kq;
-            ++pre_job;
-            seek();
+        ++issued;
+        if (++i_slot == ns) i_slot = 0;
+        i_pos += i_step;
+        if (++i_k == i_n) seek(i_job + 1);
+    };
+    // the early problems' first copies go out before the wait; the cursor stops at a job whose indices wait
+    seek(0);
+    while (i_job < my_jobs && issued < ns - 1 && L.p[i_map].early) issue();
+
+    // the activation blocks of the rows this CTA's jobs read, early sources first
+    auto split = [&](bool early_pass) {
+        for (int src = 0; src < L.nx; ++src) {
+            const M8X& X = L.x[src];
+            if ((X.early != 0) != early_pass) continue;
+            const int xblocks = X.cols / kM8XBlock;
+            for (int blk = warp; blk < X.rows * xblocks; blk += kM8Warps) {
+                const int xr = blk / xblocks, b = blk - xr * xblocks;
+                const int grow = X.row0 + xr;
+                if (!((need[grow >> 5] >> (grow & 31)) & 1u)) continue;
+                const int64_t at = int64_t(xr) * X.cols + int64_t(b) * kM8XBlock + 8 * lane;
+                int8_t* hi = xsplit + X.byte0 + at;
+                m8_split(X.x, X.gate, X.up, at, hi, hi + int64_t(X.rows) * X.cols, xscale + X.scale0 + blk, lane);
+            }
         }
     };
-    if (lane == 0) {
-        seek();
-        for (int i = 0; i < ns - 1; ++i) issue();
-    }
-
-    // the activation rows this CTA's jobs read
-    if (lane == 0)
-        for (int job = 0; job < my_jobs; ++job) {
-            const int xr = locate(job).xr;
-            atomicOr(&need[xr >> 5], 1u << (xr & 31));
-        }
+    split(true);
+    pdl_wait();
+    place(has && !L.p[j_prob].early);
+    if (i_job < my_jobs && !L.p[i_map].early) seek(i_job);  // (re-read the place: its expert is known now)
+    split(false);
     __syncthreads();
-    // the activations, split per 256-column block into int8 hi and lo: a warp per block, 8 values a lane
-    for (int src = 0; src < L.nx; ++src) {
-        const M8X& X = L.x[src];
-        const int xblocks = X.cols / kM8XBlock;
-        for (int blk = warp; blk < X.rows * xblocks; blk += kM8Warps) {
-            const int xr = blk / xblocks, b = blk - xr * xblocks;
-            const int grow = X.row0 + xr;
-            if (!((need[grow >> 5] >> (grow & 31)) & 1u)) continue;
-            const int64_t c0 = int64_t(b) * kM8XBlock + 8 * lane;
-            float v[8];
-            if (X.gate) {
-                // the SwiGLU of the gate and up products, the same function (so the same float16 bits) as the
-                // separate kernel
-                const uint4 gr = *reinterpret_cast<const uint4*>(X.gate + int64_t(xr) * X.cols + c0);
-                const uint4 ur = *reinterpret_cast<const uint4*>(X.up + int64_t(xr) * X.cols + c0);
-                const __half* gh = reinterpret_cast<const __half*>(&gr);
-                const __half* uh = reinterpret_cast<const __half*>(&ur);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) v[i] = __half2float(swiglu_one(gh[i], uh[i]));
-            } else {
-                const uint4 raw = *reinterpret_cast<const uint4*>(X.x + int64_t(xr) * X.cols + c0);
-                const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const float2 f = __half22float2(h2[i]);
-                    v[2 * i] = f.x;
-                    v[2 * i + 1] = f.y;
-                }
-            }
-            float amax = 0.f;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const float sc = amax / 127.0f, inv = amax > 0.f ? 127.0f / amax : 0.f;
-            uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float hf = fminf(fmaxf(rintf(v[i] * inv), -127.f), 127.f);
-                const float lf = fminf(fmaxf(rintf((v[i] - hf * sc) * (128.0f * inv)), -127.f), 127.f);
-                hw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(hf)) & 255u) << (8 * (i & 3));
-                lw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(lf)) & 255u) << (8 * (i & 3));
-            }
-            int8_t* hi = xsplit + X.byte0 + int64_t(xr) * X.cols + c0;
-            *reinterpret_cast<uint2*>(hi) = make_uint2(hw[0], hw[1]);
-            *reinterpret_cast<uint2*>(hi + int64_t(X.rows) * X.cols) = make_uint2(lw[0], lw[1]);
-            if (lane == 0) xscale[X.scale0 + blk] = sc;
-        }
-    }
-    __syncthreads();
+    while (i_job < my_jobs && issued < ns - 1) issue();
 
     // a team of one warp needs no named barrier (there are 16, barrier 0 is __syncthreads')
     auto team_sync = [&]() {
@@ -696,36 +708,43 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     // with its team's barriers
     bool ok = true;
     float total[2] = {0.f, 0.f};
-    int slot = 0, waited = 0;
+    int slot = 0, consumed = 0;
     uint32_t phase = 0;
     for (int job = 0; job < my_jobs; ++job) {
-        const M8Where w = locate(job);
-        const M8Prob& P = L.p[w.prob];
+        const int pr = __shfl_sync(0xffffffffu, j_prob, job);
+        const int pair = __shfl_sync(0xffffffffu, j_pair, job);
+        const int cls = __shfl_sync(0xffffffffu, j_cls, job);
+        const int blk = __shfl_sync(0xffffffffu, j_blk, job);
+        const int xr = __shfl_sync(0xffffffffu, j_xr, job);
+        const int valid = __shfl_sync(0xffffffffu, j_valid, job);
+        const M8Prob& P = L.p[pr];
         const M8X& X = L.x[P.xs];
-        const int lx = w.xr - X.row0;
+        const int lx = xr - X.row0;
         const uint8_t* xh = reinterpret_cast<const uint8_t*>(xsplit) + X.byte0 + int64_t(lx) * X.cols;
         const uint8_t* xl = xh + int64_t(X.rows) * X.cols;
         const float* xsc = xscale + X.scale0 + lx * (X.cols / kM8XBlock);
-        const int n = stages_of(w.prob);
-        int s = kq;
-        for (int k = 0; k < n; ++k, s += team) {
+        const int n = stages_of(pr);
+        const bool iq3 = P.kind == M8IQ3S<2>::kKind;
+        int pos = cls * static_cast<int>(P.row_bytes) + kq * P.stage_bytes;
+        const int step = team * P.stage_bytes;
+        int xc = kq * P.stage_cols;
+        const int xstep = team * P.stage_cols;
+        for (int k = 0; k < n; ++k, pos += step, xc += xstep) {
             // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
             __syncwarp();
-            if (lane == 0) issue();
+            if (i_job < my_jobs) issue();
             const int cur = slot;
             if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, kM8WaitLimit));
-            ++waited;
+            ++consumed;
             if (++slot == ns) {
                 slot = 0;
                 phase ^= 1;
             }
-            if (!ok || w.e >= P.experts) continue;
-            const int off = (w.cls * static_cast<int>(P.row_bytes) + s * P.stage_bytes) & 15;
-            const uint8_t* st = my_ring + cur * slot_bytes + off;
-            const int xc = s * P.stage_cols;
-            if (P.kind == M8IQ3S<2>::kKind)
-                M8IQ3S<2>::stage(st + gid * M8IQ3S<2>::kRS, st + (gid + 8) * M8IQ3S<2>::kRS, tig, gid, lut, xh + xc, xl + xc,
-                              xsc + xc / kM8XBlock, total);
+            if (!ok || !valid) continue;
+            const uint8_t* st = my_ring + cur * slot_bytes + (pos & 15);
+            if (iq3)
+                M8IQ3S<2>::stage(st + gid * M8IQ3S<2>::kRS, st + (gid + 8) * M8IQ3S<2>::kRS, tig, gid, lut, xh + xc,
+                                 xl + xc, xsc + xc / kM8XBlock, total);
             else
                 M8Q8_0::stage(st + gid * M8Q8_0::kRS, st + (gid + 8) * M8Q8_0::kRS, tig, gid, lut, xh + xc, xl + xc,
                               xsc + xc / kM8XBlock, total);
@@ -739,11 +758,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
         total[0] = total[1] = 0.f;
         team_sync();
         if (kq == 0 && lane < 16) {
-            const int64_t row = int64_t(w.blk) * 16 * P.q + w.cls + int64_t(P.q) * lane;
-            if (w.e < P.experts && row < P.rows) {
+            const int64_t row = int64_t(blk) * 16 * P.q + cls + int64_t(P.q) * lane;
+            if (valid && row < P.rows) {
                 float v = rq[lane];
                 for (int i = 1; i < team; ++i) v += rq[16 * i + lane];
-                P.out[int64_t(w.pair) * P.rows + row] = __float2half_rn(v);
+                P.out[int64_t(pair) * P.rows + row] = __float2half_rn(v);
             }
         }
         team_sync();
@@ -754,7 +773,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
     // a wait gave up)
     if (!ok && lane == 0)
-        for (int i = 0; i < waited + ns; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
+        for (int i = consumed; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
     __syncwarp();
 }
 
@@ -903,7 +922,7 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
     if (!encode) return 1;
     M8Launch L{};
     M8Maps maps;
-    int jobs = 0, pairs = 0, rows = 0, scales = 0;
+    int jobs = 0, rows = 0, scales = 0;
     int64_t xbytes = 0;
     bool lut = false;
     int max_rs = 0;
@@ -946,6 +965,8 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
             X.row0 = rows;
             X.scale0 = scales;
             X.byte0 = xbytes;
+            const size_t xb = size_t(xrows) * sp.cols * sizeof(__half);
+            X.early = (sp.x ? pdl_early(st, sp.x, xb) : pdl_early(st, sp.gate, xb) && pdl_early(st, sp.up, xb)) ? 1 : 0;
             rows += X.rows;
             scales += X.rows * static_cast<int>(sp.cols / kM8XBlock);
             xbytes += 2 * xrows * sp.cols;
@@ -969,13 +990,12 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
         P.pairs = static_cast<int>(sp.pairs);
         P.share = static_cast<int>(sp.share);
         P.xs = xs;
-        P.idx0 = pairs;
+        P.early = pdl_early(st, sp.idx, size_t(sp.pairs) * 4) ? 1 : 0;
         P.job0 = jobs;
         const int64_t pj = int64_t(P.pairs) * P.tiles;
         if (pj + jobs > (int64_t(1) << 30)) return 1;
         P.jobs = static_cast<int>(pj);
         jobs += P.jobs;
-        pairs += P.pairs;
         max_rs = std::max(max_rs, rs);
         const cuuint64_t dims[2] = {static_cast<cuuint64_t>(q * sp.row_bytes / 4),
                                     static_cast<cuuint64_t>(sp.experts * sp.rows / q)};
@@ -987,15 +1007,14 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return 1;
     }
-    if (rows > kM8MaxRows || pairs > kM8MaxRows) return 1;
+    if (rows > kM8MaxRows) return 1;
     L.nprob = n;
     L.jobs = jobs;
-    L.pairs = pairs;
     L.scales = scales;
     L.xbytes = xbytes;
     L.lut = lut ? 1 : 0;
     L.slot_bytes = 16 * max_rs;
-    const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + kM8MaxRows * 4 + kM8MaxRows / 8 +
+    const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + kM8MaxRows / 8 +
                          (lut ? 8192 * 4 : 0) + size_t((scales + 3) & ~3) * 4 + size_t(xbytes);
     const size_t slot = size_t(kM8Warps) * L.slot_bytes;
     int ns = kM8MaxSlots;
@@ -1032,6 +1051,8 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
         }
     }
     L.team = team;
+    // a warp keeps at most 32 jobs (one per lane of its job table)
+    if (jobs > int64_t(kM8MaxWarpJobs) * G * (kM8Warps / team)) return 1;
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
     const size_t smem = fixed + ns * slot;
     if (int s = max_smem(mv8_kernel, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
