@@ -203,6 +203,41 @@ SMOE_API int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts, 
                      const void* a, int a_dtype, int64_t p16, const uint32_t* tile_expert, float* out,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* One MoE block's decode step for one float16 token in a single persistent launch: smoe_route (with the
+ * shared gate), the four gate / up products of smoe_matvec_batch, the routed down product of smoe_matvec_glu
+ * and smoe_matvec_glu_combine, as `_Routed.__call__` (strata_mlx/fused.py:487-497) runs them for one token.
+ * Routed experts IQ3_S (gate / up (experts, ffn, hidden), down (experts, hidden, ffn)), the shared expert
+ * Q8_0 (gate / up (1, sffn, hidden), down (1, hidden, sffn)); hidden and ffn multiples of 512, sffn of 256,
+ * experts <= 256, k <= 32 (SMOE_EKIND / SMOE_ESHAPE otherwise). Outputs: logits [experts] float32, idx and
+ * weights [k], gate_out (1 float16), out [hidden] float16 -- the same choice, and products within the int8
+ * split's rounding of the separate calls. `scratch`: smoe_decode_layer_scratch() bytes of device memory,
+ * zero before the first call and then left to the library (the launches count their grid barriers in it);
+ * calls sharing a scratch must not overlap on the GPU. One CTA per SM, all resident together (a cooperative
+ * launch); every wait on another CTA gives up after a second, leaving a flag that
+ * smoe_decode_layer_status() reads (1: some wait gave up, the outputs are not valid). No single reference
+ * counterpart: it fuses the four calls above. */
+typedef struct SmoeDecodeLayer {
+    const uint16_t* router;      /* [experts][hidden] float16 */
+    const uint16_t* shared_gate; /* [hidden] float16, the shared expert's gate row */
+    int64_t experts, hidden, k;
+    int kind;                    /* 21 (IQ3_S) */
+    const uint8_t *gate, *up, *down;
+    int64_t ffn;
+    int shared_kind;             /* 8 (Q8_0) */
+    const uint8_t *sgate, *sup, *sdown;
+    int64_t sffn;
+    float* logits;
+    uint32_t* idx;
+    float* weights;
+    void* gate_out;
+    void* out;
+    void* scratch;
+} SmoeDecodeLayer;
+SMOE_API size_t smoe_decode_layer_scratch(int64_t hidden, int64_t k, int64_t ffn, int64_t sffn);
+SMOE_API int smoe_decode_layer(const SmoeDecodeLayer* layer, const void* x, void* stream);
+SMOE_API int smoe_decode_layer_status(const void* scratch, int64_t hidden, int64_t k, int64_t ffn, int64_t sffn,
+                                      int* failed);
+
 #ifdef __cplusplus
 }
 #endif

@@ -27,6 +27,15 @@ class SmoeMatvec(ctypes.Structure):
                 ("pairs", _i64), ("share", _i64), ("x", _p), ("gate", _p), ("up", _p), ("out", _p), ("dtype", _i)]
 
 
+class SmoeDecodeLayer(ctypes.Structure):
+    """`SmoeDecodeLayer` of include/strata_moe.h: one MoE block for smoe_decode_layer."""
+
+    _fields_ = [("router", _p), ("shared_gate", _p), ("experts", _i64), ("hidden", _i64), ("k", _i64), ("kind", _i),
+                ("gate", _p), ("up", _p), ("down", _p), ("ffn", _i64), ("shared_kind", _i), ("sgate", _p),
+                ("sup", _p), ("sdown", _p), ("sffn", _i64), ("logits", _p), ("idx", _p), ("weights", _p),
+                ("gate_out", _p), ("out", _p), ("scratch", _p)]
+
+
 # name -> (restype, argtypes): the declarations of include/strata_moe.h
 SIGNATURES = {
     "smoe_last_error": (_c.c_char_p, []),
@@ -39,6 +48,9 @@ SIGNATURES = {
     "smoe_matvec_glu": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _i, _p]),
     "smoe_matvec_batch": (_i, [_i, _c.POINTER(SmoeMatvec), _p]),
     "smoe_matvec_glu_combine": (_i, [_i, _p, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i, _p]),
+    "smoe_decode_layer_scratch": (_sz, [_i64, _i64, _i64, _i64]),
+    "smoe_decode_layer": (_i, [_c.POINTER(SmoeDecodeLayer), _p, _p]),
+    "smoe_decode_layer_status": (_i, [_p, _i64, _i64, _i64, _i64, _c.POINTER(_i)]),
     "smoe_swiglu": (_i, [_p, _p, _i64, _p, _i, _p]),
     "smoe_router_logits": (_i, [_p, _p, _i, _i64, _i64, _i64, _p, _p]),
     "smoe_top_k": (_i, [_p, _i64, _i64, _i64, _p, _p, _p]),

@@ -189,9 +189,31 @@ struct M8Q8_0 {
     }
 };
 
+// Eight values a lane of one 256-column block (a warp) split into int8 hi and lo and the block's scale:
+// v = s (hi + lo / 128), s = max|v| / 127.
+__device__ __forceinline__ void m8_split_values(const float (&v)[8], int8_t* hi, int8_t* lo, float* scale, int lane) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float s = amax / 127.0f, inv = amax > 0.f ? 127.0f / amax : 0.f;
+    uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float hf = fminf(fmaxf(rintf(v[i] * inv), -127.f), 127.f);
+        const float lf = fminf(fmaxf(rintf((v[i] - hf * s) * (128.0f * inv)), -127.f), 127.f);
+        hw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(hf)) & 255u) << (8 * (i & 3));
+        lw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(lf)) & 255u) << (8 * (i & 3));
+    }
+    *reinterpret_cast<uint2*>(hi) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(lo) = make_uint2(lw[0], lw[1]);
+    if (lane == 0) *scale = s;
+}
+
 // One 256-column block of an activation row split into int8 hi and lo and its scale, by one warp (8 values a
-// lane): v = s (hi + lo / 128), s = max|v| / 127. With gate set, v = swiglu(gate, up) (the same function, so
-// the same float16 bits, as the separate SwiGLU kernel).
+// lane, from element `at`). With gate set, v = swiglu(gate, up) (the same function, so the same float16 bits,
+// as the separate SwiGLU kernel).
 __device__ __forceinline__ void m8_split(const __half* x, const __half* gate, const __half* up, int64_t at,
                                          int8_t* hi, int8_t* lo, float* scale, int lane) {
     float v[8];
@@ -212,23 +234,7 @@ __device__ __forceinline__ void m8_split(const __half* x, const __half* gate, co
             v[2 * i + 1] = f.y;
         }
     }
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float s = amax / 127.0f, inv = amax > 0.f ? 127.0f / amax : 0.f;
-    uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        const float hf = fminf(fmaxf(rintf(v[i] * inv), -127.f), 127.f);
-        const float lf = fminf(fmaxf(rintf((v[i] - hf * s) * (128.0f * inv)), -127.f), 127.f);
-        hw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(hf)) & 255u) << (8 * (i & 3));
-        lw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(lf)) & 255u) << (8 * (i & 3));
-    }
-    *reinterpret_cast<uint2*>(hi) = make_uint2(hw[0], hw[1]);
-    *reinterpret_cast<uint2*>(lo) = make_uint2(lw[0], lw[1]);
-    if (lane == 0) *scale = s;
+    m8_split_values(v, hi, lo, scale, lane);
 }
 
 }  // namespace smoe

@@ -1,0 +1,630 @@
+// The MoE block's decode step for one token in one persistent launch: the router with its top-k and the
+// softmax over the chosen and the shared expert's gate, the routed experts' and the shared expert's gate / up
+// products, their down products, and the block's combine -- the work of smoe_route, smoe_matvec_batch,
+// smoe_matvec_glu and smoe_matvec_glu_combine, without the four launches' prologues and pipeline drains.
+//
+// B200 layout: one CTA of 16 warps per SM, all co-resident (a cooperative launch). The phases whose inputs are
+// other CTAs' outputs are separated by grid barriers (an atomic counter in global memory, every wait bounded):
+//   A  every CTA: its router rows' weights in flight, codebook, the token's int8 split, the shared expert's
+//      first weight copies (they need no routing);
+//   B  router rows -> logits (global), the shared gate row -> gate value;            barrier 1
+//   C  every CTA takes the top-k of the logits itself (the same choice everywhere), so the routed experts'
+//      copies start at once; CTA 0 writes idx and weights;
+//   D  gate / up tiles of the four stacks (jobs round-robin over all teams, CTA-fastest, costliest first),
+//      products to global;                                                          barrier 2
+//   E  down tiles: the routed down on the first CTAs, the shared down on the rest (contiguous job ranges, so
+//      a CTA splits one or two SwiGLU rows), products to global;                     barrier 3
+//   F  the combine of every output row, by row ranges.
+// Each warp's copy cursor runs through its phase-D items and on into its phase-E items: the down weights
+// stream in while the gate / up products finish and while the CTAs wait at barrier 2. Stage decoders, the
+// activation split and the combine are the matvec kernels' own (mv8_dev.cuh, common.cuh), so every product is
+// the same integer arithmetic.
+#include <algorithm>
+#include <vector>
+
+#include "mv8_dev.cuh"
+#include "router_dev.cuh"
+
+namespace smoe {
+
+constexpr int kLyRep = 8;        // copies of the IQ3_S grid (16 KB; the ring needs the rest)
+constexpr int kLyMaxK = 32;      // routed experts a token takes
+constexpr int kLyMaxExperts = 256;
+constexpr int kLyTopkNV = kLyMaxExperts / 32;
+
+// One stack of a phase: a job is a tile of 16 weight rows (one residue class mod q) of one pair.
+struct LyStack {
+    __half* out;             // [pairs][rows]
+    int64_t rows, row_bytes;
+    int kind;                // 21 IQ3_S (two-block stages) or 8 Q8_0
+    int stage_cols, stage_bytes, rs, q, lq, tiles, stages;
+    int routed;              // expert idx[pair] (pairs = k), or the one expert (pairs = 1)
+    int pairs;
+    int job0, jobs;          // its jobs within the phase
+    int map;                 // its tensor map
+    int src;                 // its activation source within the phase
+};
+// Activation rows of a phase, split into int8 hi / lo: the token (phase D) or swiglu(gate, up) rows (E).
+struct LySource {
+    const __half *x, *gate, *up;
+    int rows, cols;          // rows: the token's 1, or the k routed pairs' (a CTA splits the ones it needs)
+};
+struct LyArgs {
+    const __half* router;    // [experts][hidden]
+    const __half* sgate;     // [hidden]
+    const __half* x;         // [hidden]
+    int experts, hidden, k;
+    float* logits;
+    uint32_t* idx;
+    float* weights;
+    __half* gate_out;
+    __half* out;             // [hidden]
+    __half *y, *s;           // routed down products [k][hidden], the shared down product [hidden]
+    unsigned long long* bar; // grid barrier arrivals (never reset: launches count on from a multiple of 3 G)
+    int* err;                // set when a wait gave up
+    LyStack d[4];            // gate / up stacks, costliest first
+    LyStack e[2];            // routed down, shared down
+    LySource src_d, src_e[2];
+    int nd, jobs_d, team_d;
+    int gr;                  // CTAs of the routed down; the rest take the shared down
+    int team_e[2];
+    int nslots, slot_bytes, split_bytes;
+};
+struct alignas(64) LyMaps {
+    CUtensorMap w[6];
+};
+
+__device__ __forceinline__ unsigned long long ld_acquire(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Every CTA arrives, then waits (thread 0, bounded) until all G have: `target` arrivals in all. Returns false
+// when the wait gave up (the error flag is then set).
+__device__ __forceinline__ bool grid_sync(unsigned long long* bar, unsigned long long target, int* err, int* flag) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(bar, 1ull);
+        bool ok = true;
+        if (ld_acquire(bar) < target) {
+            const uint64_t t0 = tc::globaltimer_ns();
+            while (ld_acquire(bar) < target) {
+                if (tc::globaltimer_ns() - t0 > tc::kWaitNs) {
+                    ok = false;
+                    atomicExch(err, 1);
+                    break;
+                }
+                __nanosleep(64);
+            }
+        }
+        __threadfence();
+        *flag = ok ? 1 : 0;
+    }
+    __syncthreads();
+    return *flag != 0;
+}
+
+__device__ __forceinline__ uint4 ldcg16(const __half* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+
+// m8_split for a SwiGLU row written by other CTAs before a barrier (read from L2)
+__device__ __forceinline__ void ly_split_glu(const __half* gate, const __half* up, int64_t at, int8_t* hi, int8_t* lo,
+                                             float* scale, int lane) {
+    float v[8];
+    const uint4 gr = ldcg16(gate + at), ur = ldcg16(up + at);
+    const __half* gh = reinterpret_cast<const __half*>(&gr);
+    const __half* uh = reinterpret_cast<const __half*>(&ur);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __half2float(swiglu_one(gh[i], uh[i]));
+    m8_split_values(v, hi, lo, scale, lane);
+}
+
+__global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __grid_constant__ LyArgs A,
+                                                                     const __grid_constant__ LyMaps M) {
+    extern __shared__ __align__(128) uint8_t sm[];
+    const int ns = A.nslots, slot_bytes = A.slot_bytes;
+    uint8_t* ring = sm;                                                                    // [warp][slot]
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * slot_bytes);  // [warp][slot]
+    float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);                  // [16 warps][16 rows]
+    float* part = red + kM8Warps * 16;                                                     // [4 rows][4 quarters]
+    uint32_t* sidx = reinterpret_cast<uint32_t*>(part + 16);                               // [k]
+    float* sw = reinterpret_cast<float*>(sidx + kLyMaxK);                                  // [k]
+    int* flag = reinterpret_cast<int*>(sw + kLyMaxK);                                      // barrier result
+    uint32_t* lut = reinterpret_cast<uint32_t*>(flag + 32);                                // 512 x kLyRep words
+    float* xscale = reinterpret_cast<float*>(lut + 512 * kLyRep);                          // [128]
+    int8_t* xsplit = reinterpret_cast<int8_t*>(xscale + 128);                              // split_bytes
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gid = lane >> 2, tig = lane & 3;
+    if (smem_addr(sm) & 127u) return;  // a tiled copy's destination is 128-byte aligned (the launch gives that)
+    const int G = gridDim.x, b = blockIdx.x;
+    const int H = A.hidden, E = A.experts, K = A.k;
+
+    // ---- A: router weights in flight first (4 warps to a row, rows b, b + G, ... of the experts + shared gate)
+    const int router_rows_n = E + (A.sgate != nullptr ? 1 : 0);
+    const int my_row = b + G * (warp >> 2);
+    const bool row_live = my_row < router_rows_n;
+    const __half* row_ptr = my_row < E ? A.router + int64_t(my_row) * H : A.sgate;
+    float wv[4][8], acc[kRtTokens];
+    router_first(row_ptr, row_live, H, wv);
+
+    // the arrival count this launch starts from: a multiple of 3 G (early arrivals at barrier 1 are fewer
+    // than G)
+    __shared__ unsigned long long base_s;
+    if (threadIdx.x == 0) {
+        const unsigned long long v0 = ld_acquire(A.bar);
+        base_s = v0 - v0 % (3ull * G);
+    }
+    if (lane == 0) {
+        for (int i = 0; i < ns; ++i) tc::mbar_init(&bars[warp * kM8MaxSlots + i], 1);
+        tc::fence_barrier_init();
+    }
+    m8_fill_grid<kLyRep>(lut);
+    // the token split into int8 hi / lo per 256-column block (phase D's only source row)
+    for (int blk = warp; blk < H / kM8XBlock; blk += kM8Warps) {
+        const int64_t at = int64_t(blk) * kM8XBlock + 8 * lane;
+        m8_split(A.x, nullptr, nullptr, at, xsplit + at, xsplit + H + at, xscale + blk, lane);
+    }
+
+    // ---- the copy cursor over this warp's items: phase D jobs, then phase E jobs
+    uint8_t* my_ring = ring + size_t(warp) * ns * slot_bytes;
+    uint64_t* my_bars = bars + warp * kM8MaxSlots;
+    // phase D: CTA-fastest round-robin over all teams
+    const int team_d = A.team_d, tid_d = warp / team_d, kq_d = warp % team_d;
+    const int nteams_d = G * (kM8Warps / team_d);
+    const int q0_d = tid_d * G + b;
+    const int jobs_d = q0_d < A.jobs_d ? min((A.jobs_d - q0_d + nteams_d - 1) / nteams_d, 32) : 0;
+    // phase E: CTAs [0, gr) take the routed down's jobs, the rest the shared down's, in contiguous ranges
+    const int eg = b < A.gr ? 0 : 1;
+    const int gsz = eg == 0 ? A.gr : G - A.gr, gb = eg == 0 ? b : b - A.gr;
+    const LyStack& SE = A.e[eg];
+    const int team_e = A.team_e[eg], tid_e = warp / team_e, kq_e = warp % team_e;
+    const int cj0 = static_cast<int>(int64_t(gb) * SE.jobs / gsz), cj1 = static_cast<int>(int64_t(gb + 1) * SE.jobs / gsz);
+    const int q0_e = cj0 + tid_e, teams_e = kM8Warps / team_e;
+    const int jobs_e = q0_e < cj1 ? min((cj1 - q0_e + teams_e - 1) / teams_e, 32) : 0;
+
+    // lane l's phase-D and phase-E jobs: meta = stack | cls << 2 | valid << 6 | pair << 7 | blk << 13, and
+    // the first row of its TMA box
+    auto job_meta = [&](const LyStack& S, int stack, int rest) {
+        const int pair = rest / S.tiles, tile = rest - pair * S.tiles;
+        return stack | ((tile & (S.q - 1)) << 2) | (pair << 7) | ((tile >> S.lq) << 13);
+    };
+    int md = 0, yd = 0, me = 0, ye = 0;
+    if (lane < jobs_d) {
+        const int j = q0_d + lane * nteams_d;
+        int st = 0;
+#pragma unroll
+        for (int i = 1; i < 4; ++i)
+            if (i < A.nd && j >= A.d[i].job0) st = i;
+        md = job_meta(A.d[st], st, j - A.d[st].job0);
+    }
+    if (lane < jobs_e) me = job_meta(SE, eg, q0_e + lane * teams_e);
+    // the box row of a job once its expert is known (stacks with one expert: expert 0)
+    auto place = [&](const LyStack& S, int meta, uint32_t e, int& valid_meta) {
+        const int ok = e < uint32_t(S.routed ? E : 1) ? 1 : 0;
+        valid_meta = meta | (ok << 6);
+        return static_cast<int>((int64_t(ok ? e : 0) * S.rows) >> S.lq) + 16 * (meta >> 13);
+    };
+    if (lane < jobs_d && !A.d[md & 3].routed) yd = place(A.d[md & 3], md, 0, md);
+
+    int c_phase = 0, c_job = 0, c_k = 0, c_n = 0, c_slot = 0, c_pos = 0, c_step = 0, c_y = 0, c_map = 0,
+        c_valid = 0, c_bytes = 0, issued = 0;
+    auto stages_for = [&](const LyStack& S, int kq, int team) {
+        return S.stages > kq ? (S.stages - kq + team - 1) / team : 0;
+    };
+    // move the cursor to (phase, job) or the first job after it with a stage for this warp
+    auto seek = [&](int phase, int job) {
+        c_phase = phase;
+        for (;;) {
+            const int njobs = c_phase == 0 ? jobs_d : jobs_e;
+            if (job >= njobs) {
+                if (c_phase == 0) {
+                    c_phase = 1;
+                    job = 0;
+                    continue;
+                }
+                c_phase = 2;  // done
+                return;
+            }
+            const int meta = __shfl_sync(0xffffffffu, c_phase == 0 ? md : me, job);
+            const LyStack& S = c_phase == 0 ? A.d[meta & 3] : A.e[meta & 3];
+            const int kq = c_phase == 0 ? kq_d : kq_e, team = c_phase == 0 ? team_d : team_e;
+            c_n = stages_for(S, kq, team);
+            if (c_n == 0) {
+                ++job;
+                continue;
+            }
+            c_job = job;
+            c_k = 0;
+            c_map = S.map;
+            c_pos = ((meta >> 2) & 15) * static_cast<int>(S.row_bytes) + kq * S.stage_bytes;
+            c_step = team * S.stage_bytes;
+            c_y = __shfl_sync(0xffffffffu, c_phase == 0 ? yd : ye, job);
+            c_valid = (meta >> 6) & 1;
+            c_bytes = 16 * S.rs;
+            return;
+        }
+    };
+    auto issue = [&]() {
+        if (lane == 0) {
+            if (c_valid) {
+                tc::mbar_arrive_expect_tx(&my_bars[c_slot], static_cast<uint32_t>(c_bytes));
+                tc::tma_load_2d(smem_addr(my_ring + c_slot * slot_bytes), &M.w[c_map], (c_pos & ~15) >> 2, c_y,
+                                &my_bars[c_slot]);
+            } else {
+                tc::mbar_arrive(&my_bars[c_slot]);
+            }
+        }
+        ++issued;
+        if (++c_slot == ns) c_slot = 0;
+        c_pos += c_step;
+        if (++c_k == c_n) seek(c_phase, c_job + 1);
+    };
+    // the shared expert's first copies go out now (no routing needed); the cursor stops at a routed job
+    seek(0, 0);
+    auto ready = [&]() {  // the cursor's job has its place
+        if (c_phase == 2) return false;
+        const int meta = __shfl_sync(0xffffffffu, c_phase == 0 ? md : me, c_job);
+        return c_phase == 0 && !A.d[meta & 3].routed;
+    };
+    while (issued < ns - 1 && ready()) issue();
+
+    // ---- B: router rows -> logits, the shared gate row -> the gate value
+    if (row_live) {
+        router_rows(row_ptr, true, A.x, H, 0, 1, acc, wv);
+        acc[0] = warp_sum(acc[0]);
+    } else {
+        acc[0] = 0.f;
+    }
+    if (lane == 0) part[(warp >> 2) * 4 + (warp & 3)] = acc[0];
+    __syncthreads();
+    if (threadIdx.x < 4) {
+        const int r = b + G * threadIdx.x;
+        if (r < router_rows_n) {
+            float s = part[threadIdx.x * 4 + 0];
+            s += part[threadIdx.x * 4 + 1];
+            s += part[threadIdx.x * 4 + 2];
+            s += part[threadIdx.x * 4 + 3];
+            if (r < E) A.logits[r] = s;
+            else *A.gate_out = __float2half_rn(s);
+        }
+    }
+    const unsigned long long base = base_s;
+    bool ok = grid_sync(A.bar, base + G, A.err, flag);
+
+    // ---- C: the top-k of the logits, in every CTA
+    if (warp == 0) {
+        topk_row<kLyTopkNV>([&](int j) { return __ldcg(A.logits + j); }, E, K, sidx, sw);
+        if (b == 0 && lane < K) {
+            A.idx[lane] = sidx[lane];
+            A.weights[lane] = sw[lane];
+        }
+    }
+    __syncthreads();
+    if (lane < jobs_d && A.d[md & 3].routed) yd = place(A.d[md & 3], md, sidx[(md >> 7) & 63], md);
+    if (lane < jobs_e) ye = place(SE, me, SE.routed ? sidx[(me >> 7) & 63] : 0u, me);
+    // re-read the cursor's job when none of its items went out yet (it waited for its place)
+    if (c_phase < 2 && c_k == 0) seek(c_phase, c_job);
+    while (c_phase < 2 && issued < ns - 1) issue();
+
+    // ---- D and E: the stages of this warp's jobs
+    float total[2] = {0.f, 0.f};
+    int slot = 0, consumed = 0;
+    uint32_t phase = 0;
+    auto run_jobs = [&](int P) {
+        const int njobs = P == 0 ? jobs_d : jobs_e;
+        const int team = P == 0 ? team_d : team_e, kq = P == 0 ? kq_d : kq_e, tid = P == 0 ? tid_d : tid_e;
+        for (int job = 0; job < njobs; ++job) {
+            const int meta = __shfl_sync(0xffffffffu, P == 0 ? md : me, job);
+            const LyStack& S = P == 0 ? A.d[meta & 3] : A.e[meta & 3];
+            const int cls = (meta >> 2) & 15, valid = (meta >> 6) & 1, pair = (meta >> 7) & 63, blk = meta >> 13;
+            // the job's activation row in the split area: the token (D), or the pair's slot (E: the first or
+            // second routed pair of this CTA's range, or the shared row)
+            const int cols = static_cast<int>(S.stages) * S.stage_cols;
+            const int lrow = P == 0 ? 0 : (S.routed ? pair - (cj0 / S.tiles) : 0);
+            const uint8_t* xh = reinterpret_cast<const uint8_t*>(xsplit) + int64_t(lrow) * cols;
+            const uint8_t* xl = xh + (P == 0 ? H : A.split_bytes / 2);
+            const float* xsc = xscale + lrow * (cols / kM8XBlock);
+            const int n = stages_for(S, kq, team);
+            const bool iq3 = S.kind == M8IQ3S<2>::kKind;
+            int pos = cls * static_cast<int>(S.row_bytes) + kq * S.stage_bytes;
+            const int step = team * S.stage_bytes;
+            int xc = kq * S.stage_cols;
+            const int xstep = team * S.stage_cols;
+            for (int k = 0; k < n; ++k, pos += step, xc += xstep) {
+                __syncwarp();
+                if (c_phase < 2) issue();
+                const int cur = slot;
+                if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, kM8WaitLimit));
+                ++consumed;
+                if (++slot == ns) {
+                    slot = 0;
+                    phase ^= 1;
+                }
+                if (!ok || !valid) continue;
+                const uint8_t* st = my_ring + cur * slot_bytes + (pos & 15);
+                if (iq3)
+                    M8IQ3S<2, kLyRep>::stage(st + gid * M8IQ3S<2>::kRS, st + (gid + 8) * M8IQ3S<2>::kRS, tig, gid, lut,
+                                             xh + xc, xl + xc, xsc + xc / kM8XBlock, total);
+                else
+                    M8Q8_0::stage(st + gid * M8Q8_0::kRS, st + (gid + 8) * M8Q8_0::kRS, tig, gid, lut, xh + xc,
+                                  xl + xc, xsc + xc / kM8XBlock, total);
+            }
+            // the team's partial sums of the job's 16 rows, added in warp order
+            float* rq = red + (tid * team) * 16;
+            if (tig == 0) {
+                rq[kq * 16 + gid] = total[0];
+                rq[kq * 16 + gid + 8] = total[1];
+            }
+            total[0] = total[1] = 0.f;
+            if (team == 1) __syncwarp();
+            else asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid), "r"(32 * team) : "memory");
+            if (kq == 0 && lane < 16) {
+                const int64_t row = int64_t(blk) * 16 * S.q + cls + int64_t(S.q) * lane;
+                if (valid && row < S.rows) {
+                    float v = rq[lane];
+                    for (int i = 1; i < team; ++i) v += rq[16 * i + lane];
+                    S.out[int64_t(pair) * S.rows + row] = __float2half_rn(v);
+                }
+            }
+            if (team == 1) __syncwarp();
+            else asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid), "r"(32 * team) : "memory");
+        }
+    };
+    run_jobs(0);
+    ok = grid_sync(A.bar, base + 2ull * G, A.err, flag) && ok;
+
+    // ---- E: the split of this CTA's SwiGLU rows (one or two routed pairs, or the shared row), then its jobs
+    {
+        const LySource& X = A.src_e[eg];
+        const int xblocks = X.cols / kM8XBlock;
+        const int p0 = SE.routed ? cj0 / SE.tiles : 0;
+        const int p1 = SE.routed ? min((cj1 - 1) / SE.tiles, X.rows - 1) : 0;
+        const int nrows = cj1 > cj0 ? p1 - p0 + 1 : 0;
+        for (int blk = warp; blk < nrows * xblocks; blk += kM8Warps) {
+            const int lr = blk / xblocks, c = blk - lr * xblocks;
+            const int64_t at = int64_t(p0 + lr) * X.cols + int64_t(c) * kM8XBlock + 8 * lane;
+            const int64_t lat = int64_t(lr) * X.cols + int64_t(c) * kM8XBlock + 8 * lane;
+            ly_split_glu(X.gate, X.up, at, xsplit + lat, xsplit + A.split_bytes / 2 + lat, xscale + blk, lane);
+        }
+        __syncthreads();
+    }
+    run_jobs(1);
+    ok = grid_sync(A.bar, base + 3ull * G, A.err, flag) && ok;
+
+    // ---- F: the combine, rows [b H / G, (b + 1) H / G)
+    if (ok) {
+        const __half g = __ldcg(A.gate_out);
+        const int r0 = static_cast<int>(int64_t(b) * H / G), r1 = static_cast<int>(int64_t(b + 1) * H / G);
+        for (int r = r0 + threadIdx.x; r < r1; r += kM8Threads) {
+            const __half sv = __ldcg(A.s + r);
+            // combine_one reads the k experts' values at y + j * stride; they were written by other CTAs
+            __half yv[kLyMaxK];
+            for (int j = 0; j < K; ++j) yv[j] = __ldcg(A.y + int64_t(j) * H + r);
+            A.out[r] = combine_one(yv, 1, sw, K, g, sv);
+        }
+    }
+    // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
+    // a wait gave up)
+    if (!ok && lane == 0)
+        for (int i = consumed; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
+    __syncwarp();
+}
+
+}  // namespace smoe
+
+using namespace smoe;
+
+extern "C" size_t smoe_decode_layer_scratch(int64_t hidden, int64_t k, int64_t ffn, int64_t sffn) {
+    // g_r, u_r [k][ffn]; gs, us [sffn]; y [k][hidden]; s [hidden] (float16), then the barrier counter and flag
+    const size_t halves = size_t(2 * k * ffn + 2 * sffn + k * hidden + hidden);
+    return ((halves * 2 + 255) & ~size_t(255)) + 256;
+}
+
+namespace {
+typedef CUresult (*LyEncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                               const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                               CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+LyEncodeFn ly_encoder() {
+    static LyEncodeFn fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            return reinterpret_cast<LyEncodeFn>(p);
+        return static_cast<LyEncodeFn>(nullptr);
+    }();
+    return fn;
+}
+}  // namespace
+
+extern "C" int smoe_decode_layer(const SmoeDecodeLayer* L, const void* x, void* stream) {
+    SMOE_REQUIRE(L && x, SMOE_EARG, "decode_layer: null argument");
+    const int64_t H = L->hidden, E = L->experts, K = L->k, F = L->ffn, FS = L->sffn;
+    SMOE_REQUIRE(L->router && L->shared_gate && L->gate && L->up && L->down && L->sgate && L->sup && L->sdown && L->logits && L->idx &&
+                     L->weights && L->gate_out && L->out && L->scratch,
+                 SMOE_EARG, "decode_layer: null pointer");
+    SMOE_REQUIRE(L->kind == 21 && L->shared_kind == 8, SMOE_EKIND,
+                 "decode_layer takes IQ3_S routed experts and a Q8_0 shared expert");
+    SMOE_REQUIRE(E >= 1 && E <= kLyMaxExperts && K >= 1 && K <= std::min<int64_t>(E, kLyMaxK), SMOE_ESHAPE,
+                 "decode_layer: 1 <= k <= experts <= 256, k <= 32");
+    SMOE_REQUIRE(H % 512 == 0 && F % 512 == 0 && FS % 256 == 0 && H <= 16384 && F <= 16384 && FS <= 16384,
+                 SMOE_ESHAPE, "decode_layer: hidden and ffn multiples of 512, shared ffn of 256");
+    const void* ptrs[] = {L->router, L->shared_gate, x, L->gate, L->up, L->down, L->sgate, L->sup, L->sdown,
+                          L->scratch};
+    for (const void* p : ptrs)
+        SMOE_REQUIRE((reinterpret_cast<uintptr_t>(p) & 15) == 0, SMOE_EARG, "decode_layer: 16-byte aligned inputs");
+    LyEncodeFn encode = ly_encoder();
+    SMOE_REQUIRE(encode != nullptr, SMOE_EARG, "decode_layer: no tensor-map encoder");
+    cudaStream_t st = as_stream(stream);
+    int dev = 0, sms = 0, coop = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev);
+    SMOE_REQUIRE(sms > 1 && coop, SMOE_EARG, "decode_layer: needs cooperative launches");
+    const int G = sms;
+
+    LyArgs A{};
+    A.router = reinterpret_cast<const __half*>(L->router);
+    A.sgate = reinterpret_cast<const __half*>(L->shared_gate);
+    A.x = static_cast<const __half*>(x);
+    A.experts = static_cast<int>(E);
+    A.hidden = static_cast<int>(H);
+    A.k = static_cast<int>(K);
+    A.logits = L->logits;
+    A.idx = L->idx;
+    A.weights = L->weights;
+    A.gate_out = static_cast<__half*>(L->gate_out);
+    A.out = static_cast<__half*>(L->out);
+    __half* scr = static_cast<__half*>(L->scratch);
+    __half* g_r = scr;
+    __half* u_r = g_r + K * F;
+    __half* gs = u_r + K * F;
+    __half* us = gs + FS;
+    A.y = us + FS;
+    A.s = A.y + K * H;
+    const size_t halves = size_t(2 * K * F + 2 * FS + K * H + H);
+    uint8_t* tail = reinterpret_cast<uint8_t*>(L->scratch) + ((halves * 2 + 255) & ~size_t(255));
+    A.bar = reinterpret_cast<unsigned long long*>(tail);
+    A.err = reinterpret_cast<int*>(tail + 64);
+
+    // the six stacks: geometry, TMA maps (raw rows seen as [rows / q][q row_bytes / 4] words)
+    LyMaps maps;
+    auto stack = [&](LyStack& S, int map, int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
+                     int routed, int pairs, __half* out) -> bool {
+        const int64_t per = kind == 21 ? 256 : 32, bb = kind == 21 ? 110 : 34;
+        S.row_bytes = cols / per * bb;
+        S.kind = kind;
+        S.stage_cols = kind == 21 ? M8IQ3S<2>::kStageCols : M8Q8_0::kStageCols;
+        S.stage_bytes = kind == 21 ? M8IQ3S<2>::kStageBytes : M8Q8_0::kStageBytes;
+        S.rs = kind == 21 ? M8IQ3S<2>::kRS : M8Q8_0::kRS;
+        int gcd = 16;
+        while (S.row_bytes % gcd) gcd >>= 1;
+        S.q = 16 / gcd;
+        S.lq = S.q == 1 ? 0 : S.q == 2 ? 1 : S.q == 4 ? 2 : S.q == 8 ? 3 : 4;
+        if (rows % S.q || experts * rows / S.q >= (int64_t(1) << 31)) return false;
+        S.rows = rows;
+        S.tiles = static_cast<int>((rows + 16 * S.q - 1) / (16 * S.q)) * S.q;
+        S.stages = static_cast<int>(cols / S.stage_cols);
+        S.routed = routed;
+        S.pairs = pairs;
+        S.jobs = pairs * S.tiles;
+        S.map = map;
+        S.out = out;
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(S.q * S.row_bytes / 4),
+                                    static_cast<cuuint64_t>(experts * rows / S.q)};
+        const cuuint64_t strides[1] = {static_cast<cuuint64_t>(S.q * S.row_bytes)};
+        const cuuint32_t box[2] = {static_cast<cuuint32_t>(S.rs / 4), 16};
+        const cuuint32_t estr[2] = {1, 1};
+        return encode(&maps.w[map], CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint8_t*>(blocks), dims, strides,
+                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    // phase D, costliest jobs first: the shared expert's rows (Q8_0 of hidden columns) before the routed
+    const int kk = static_cast<int>(K);
+    bool good = stack(A.d[0], 0, 8, L->sgate, 1, FS, H, 0, 1, gs) && stack(A.d[1], 1, 8, L->sup, 1, FS, H, 0, 1, us) &&
+                stack(A.d[2], 2, 21, L->gate, E, F, H, 1, kk, g_r) && stack(A.d[3], 3, 21, L->up, E, F, H, 1, kk, u_r) &&
+                stack(A.e[0], 4, 21, L->down, E, H, F, 1, kk, A.y) && stack(A.e[1], 5, 8, L->sdown, 1, H, FS, 0, 1, A.s);
+    SMOE_REQUIRE(good, SMOE_ESHAPE, "decode_layer: stack geometry");
+    A.nd = 4;
+    int jobs = 0;
+    for (int i = 0; i < 4; ++i) {
+        A.d[i].job0 = jobs;
+        jobs += A.d[i].jobs;
+    }
+    A.jobs_d = jobs;
+    A.e[0].job0 = A.e[1].job0 = 0;
+    A.src_d = LySource{A.x, nullptr, nullptr, 1, static_cast<int>(H)};
+    A.src_e[0] = LySource{nullptr, g_r, u_r, kk, static_cast<int>(F)};
+    A.src_e[1] = LySource{nullptr, gs, us, 1, static_cast<int>(FS)};
+
+    // phase D's team size: the least work on the busiest warp (jobs round-robin over all teams, CTA-fastest)
+    {
+        int64_t best = -1;
+        std::vector<int64_t> load;
+        for (int t = 1; t <= kM8Warps; t *= 2) {
+            const int64_t nteams = int64_t(G) * (kM8Warps / t);
+            if (jobs > 32 * nteams) continue;
+            load.assign(static_cast<size_t>(std::min<int64_t>(nteams, jobs)), 0);
+            int64_t j = 0;
+            for (int i = 0; i < 4; ++i) {
+                const LyStack& S = A.d[i];
+                const int64_t sb = int64_t(16) * S.stage_bytes * (S.kind == 21 ? 5 : 2);  // decode cost per byte
+                const int64_t w = (S.stages + t - 1) / t * sb + (t > 1 ? sb / 2 : 0);
+                for (int64_t q = 0; q < S.jobs; ++q, ++j) load[static_cast<size_t>(j % nteams)] += w;
+            }
+            const int64_t span = *std::max_element(load.begin(), load.end());
+            if (best < 0 || span < best) {
+                best = span;
+                A.team_d = t;
+            }
+        }
+        SMOE_REQUIRE(best >= 0, SMOE_ESHAPE, "decode_layer: too many jobs");
+    }
+    // phase E: CTAs in proportion to the two down stacks' decode cost, then each group's team size
+    {
+        const double cr = double(A.e[0].jobs) * A.e[0].stages * A.e[0].stage_bytes * 5;
+        const double cs = double(A.e[1].jobs) * A.e[1].stages * A.e[1].stage_bytes * 2;
+        A.gr = std::min(G - 1, std::max(1, static_cast<int>(G * cr / (cr + cs) + 0.5)));
+        for (int g = 0; g < 2; ++g) {
+            const LyStack& S = A.e[g];
+            const int gsz = g == 0 ? A.gr : G - A.gr;
+            const int64_t per = (S.jobs + gsz - 1) / gsz;  // jobs of the busiest CTA
+            int64_t best = -1;
+            for (int t = 1; t <= kM8Warps; t *= 2) {
+                const int64_t teams = kM8Warps / t;
+                const int64_t most = (per + teams - 1) / teams;
+                if (most > 32) continue;
+                const int64_t span = most * (4 * ((S.stages + t - 1) / t) + (t > 1 ? 3 : 0));
+                if (best < 0 || span < best) {
+                    best = span;
+                    A.team_e[g] = t;
+                }
+            }
+            SMOE_REQUIRE(best >= 0, SMOE_ESHAPE, "decode_layer: too many down jobs");
+            // a routed CTA's range must span at most two pairs (its split holds two rows)
+            if (g == 0) SMOE_REQUIRE(per <= S.tiles, SMOE_ESHAPE, "decode_layer: too few CTAs for the routed down");
+        }
+    }
+    // shared memory: the split area holds the token (D) or a CTA's SwiGLU rows (E: two routed rows, or the
+    // shared one)
+    const int64_t split_d = 2 * H, split_e = std::max<int64_t>(2 * 2 * F, 2 * FS);
+    A.split_bytes = static_cast<int>((std::max(split_d, split_e) + 127) & ~int64_t(127));
+    A.slot_bytes = 16 * std::max(M8IQ3S<2>::kRS, M8Q8_0::kRS);
+    const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + 16 * 4 + kLyMaxK * 8 + 32 * 4 +
+                         512 * kLyRep * 4 + 128 * 4 + size_t(A.split_bytes);
+    const size_t slot = size_t(kM8Warps) * A.slot_bytes;
+    int ns = kM8MaxSlots;
+    while (ns > 2 && fixed + ns * slot > size_t(227 * 1024 - 256)) --ns;
+    SMOE_REQUIRE(fixed + ns * slot <= size_t(227 * 1024 - 256), SMOE_ESHAPE, "decode_layer: shared memory");
+    A.nslots = ns;
+    const size_t smem = fixed + ns * slot;
+    if (int s = max_smem(decode_layer_kernel, static_cast<int>(smem)))
+        return fail(s, "decode_layer: shared memory limit");
+
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(G);
+    cfg.blockDim = dim3(kM8Threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, decode_layer_kernel, A, maps);
+    return launch_status("decode_layer");
+}
+
+extern "C" int smoe_decode_layer_status(const void* scratch, int64_t hidden, int64_t k, int64_t ffn, int64_t sffn,
+                                        int* failed) {
+    SMOE_REQUIRE(scratch && failed, SMOE_EARG, "decode_layer_status: null argument");
+    const size_t halves = size_t(2 * k * ffn + 2 * sffn + k * hidden + hidden);
+    const uint8_t* tail = static_cast<const uint8_t*>(scratch) + ((halves * 2 + 255) & ~size_t(255));
+    int v = 0;
+    cudaError_t e = cudaMemcpy(&v, tail + 64, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail(-static_cast<int>(e), "decode_layer_status: copy");
+    *failed = v;
+    return SMOE_OK;
+}

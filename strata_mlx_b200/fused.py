@@ -9,6 +9,8 @@ Names and conventions follow the reference; tensors are torch CUDA tensors and e
 sm_100a kernels of libstrata_moe.so.
 """
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -82,6 +84,67 @@ def top_k_softmax(logits: torch.Tensor, k: int):
 
 _COUNTERS = {}
 
+LAYER_KERNEL = True  # one launch per one-token step where the layer's types and shapes allow (smoe_decode_layer)
+_LAYER_SCRATCH = {}
+
+
+def decode_layer(block: "SparseMoeBlock", x: torch.Tensor):
+    """block(x) for one float16 token in a single persistent launch (smoe_decode_layer: router, top-k, the
+    shared gate, the gate / up and down products of the routed and the shared expert, the combine), or None
+    where the kernel does not apply: another type than IQ3_S routed / Q8_0 shared stacks, other shapes, more
+    than one token."""
+    if not LAYER_KERNEL or x.dtype != torch.float16 or x.numel() != block.gate.cols or not x.is_cuda:
+        return None
+    sw, sh = block.switch_mlp, block.shared_expert
+    if not isinstance(sw, BlockSwitchGLU) or not isinstance(sh, BlockMLP):
+        return None
+    g, u, d = sw.gate_proj, sw.up_proj, sw.down_proj
+    sg, su, sd = sh.gate_proj.stack, sh.up_proj.stack, sh.down_proj.stack
+    if any(lin.kind != "IQ3_S" for lin in (g, u, d)) or any(lin.kind != "Q8_0" for lin in (sg, su, sd)):
+        return None
+    router, sgw = block.gate.weight, block.shared_expert_gate.weight
+    experts, hidden, k = block.gate.rows, block.gate.cols, block.top_k
+    ffn, sffn = g.output_dims, sg.output_dims
+    if (g.shape != (experts, ffn, hidden) or u.shape != g.shape or d.shape != (experts, hidden, ffn)
+            or sg.shape != (1, sffn, hidden) or su.shape != sg.shape or sd.shape != (1, hidden, sffn)):
+        return None
+    if (router.dtype != torch.float16 or sgw.dtype != torch.float16 or sgw.numel() != hidden
+            or hidden % 512 or ffn % 512 or sffn % 256 or experts > 256 or not 1 <= k <= min(experts, 32)):
+        return None
+    if k >= min(lin.unpack_from for lin in (g, u, d)):
+        return None
+    dev = x.device
+    key = (str(dev), hidden, k, ffn, sffn)
+    scratch = _LAYER_SCRATCH.get(key)
+    if scratch is None:
+        nbytes = int(_lib.lib().smoe_decode_layer_scratch(hidden, k, ffn, sffn))
+        scratch = _LAYER_SCRATCH[key] = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+    logits = torch.empty(experts, dtype=torch.float32, device=dev)
+    idx = torch.empty(k, dtype=torch.uint32, device=dev)
+    w = torch.empty(k, dtype=torch.float32, device=dev)
+    gate_out = torch.empty(1, dtype=x.dtype, device=dev)
+    out = torch.empty(hidden, dtype=x.dtype, device=dev)
+    spec = _lib.SmoeDecodeLayer(
+        _lib.ptr(router.contiguous()), _lib.ptr(sgw.contiguous()), experts, hidden, k, 21, _lib.ptr(g.blocks),
+        _lib.ptr(u.blocks), _lib.ptr(d.blocks), ffn, 8, _lib.ptr(sg.blocks), _lib.ptr(su.blocks), _lib.ptr(sd.blocks),
+        sffn, _lib.ptr(logits), _lib.ptr(idx), _lib.ptr(w), _lib.ptr(gate_out), _lib.ptr(out), _lib.ptr(scratch))
+    _lib.call("smoe_decode_layer", ctypes.byref(spec), _lib.ptr(x.contiguous()), _lib.stream())
+    return out.reshape(x.shape)
+
+
+def decode_layer_failed(x: torch.Tensor, block: "SparseMoeBlock") -> bool:
+    """Whether a wait of the one-launch decode step gave up since the scratch was made (its outputs are then
+    not valid). Reads the flag back from the device."""
+    g, sg = block.switch_mlp.gate_proj, block.shared_expert.gate_proj.stack
+    key = (str(x.device), block.gate.cols, block.top_k, g.output_dims, sg.output_dims)
+    scratch = _LAYER_SCRATCH.get(key)
+    if scratch is None:
+        return False
+    flag = ctypes.c_int(0)
+    _lib.call("smoe_decode_layer_status", _lib.ptr(scratch), block.gate.cols, block.top_k, g.output_dims,
+              sg.output_dims, ctypes.byref(flag))
+    return flag.value != 0
+
 
 def route(gate: "WindowLinear", shared_gate, x: torch.Tensor, k: int):
     """The start of the MoE block in one launch: (idx, w, g) = (top_k_softmax(gate(x), k),
@@ -149,6 +212,9 @@ class SparseMoeBlock:
         self.top_k = top_k
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        out = decode_layer(self, x)
+        if out is not None:
+            return out
         r = route(self.gate, self.shared_expert_gate, x, self.top_k)
         if r is not None:
             idx, w, g = r
