@@ -93,44 +93,64 @@ __device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t b
 }
 
 // One row's top-k and softmax by one warp; `load` reads logit j of the row.
+// Order-preserving 32-bit key of a logit: larger keys for larger values, equal keys for equal values (-0 as +0),
+// 0 for NaN (never chosen: `better` takes no NaN) -- every other key is above 0 (-inf's is 0x007FFFFF).
+__device__ __forceinline__ uint32_t topk_key(float v) {
+    if (v != v) return 0u;
+    const uint32_t u = v == 0.0f ? 0u : __float_as_uint(v);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// One row's top-k and softmax by one warp; `load` reads logit j of the row. Lane l holds logits l, l + 32, ...;
+// each round the warp takes the largest key among the lanes' own best (a max reduction), the lowest index
+// among the lanes holding it (a min reduction: ties to the lower index), and the winning lane alone looks for
+// its next best. The same choice as rounds of `better` over all live values: the largest value, the lowest
+// index among equal ones, never a NaN; 0xffffffff (and -inf) once nothing is left.
 template <int NV, class Load>
 __device__ __forceinline__ void topk_row(Load load, int n, int k, uint32_t* __restrict__ idx, float* __restrict__ weights) {
     const int lane = threadIdx.x & 31;
     float v[NV];
-    bool live[NV];
+    uint32_t key[NV];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
         const int j = 32 * i + lane;
-        live[i] = j < n;
-        v[i] = live[i] ? load(j) : -INFINITY;
+        v[i] = j < n ? load(j) : -INFINITY;
+        key[i] = j < n ? topk_key(v[i]) : 0u;
     }
+    // this lane's best: its largest key, the first such (the lowest index)
+    uint32_t hk = 0u;
+    int hi = 0;
+    auto rescan = [&]() {
+        hk = 0u;
+        hi = 0;
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+            if (key[i] > hk) {
+                hk = key[i];
+                hi = i;
+            }
+    };
+    rescan();
     float top0 = 0.0f, sum = 0.0f, chosen = 0.0f;
     for (int r = 0; r < k; ++r) {
+        const uint32_t m = __reduce_max_sync(0xffffffffu, hk);
         float bv = -INFINITY;
         uint32_t bi = 0xffffffffu;
+        if (m != 0u) {
+            bi = __reduce_min_sync(0xffffffffu, hk == m ? uint32_t(32 * hi + lane) : 0xffffffffu);
+            float mine = 0.0f;
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            const uint32_t j = 32u * i + lane;
-            if (live[i] && better(v[i], j, bv, bi)) {
-                bv = v[i];
-                bi = j;
-            }
-        }
+            for (int i = 0; i < NV; ++i)
+                if (i == hi) mine = v[i];
+            bv = __shfl_sync(0xffffffffu, mine, bi & 31u);
+            if ((bi & 31u) == uint32_t(lane)) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (better(ov, oi, bv, bi)) {
-                bv = ov;
-                bi = oi;
+                for (int i = 0; i < NV; ++i)
+                    if (uint32_t(i) == (bi >> 5)) key[i] = 0u;
+                rescan();
             }
         }
         if (lane == 0) idx[r] = bi;
-        if (bi != 0xffffffffu && (bi & 31u) == uint32_t(lane)) {
-#pragma unroll
-            for (int i = 0; i < NV; ++i)
-                if (uint32_t(i) == (bi >> 5)) live[i] = false;
-        }
         // softmax over the chosen, largest first: lane r keeps its own chosen logit
         if (r == 0) top0 = bv;
         if (lane == (r & 31) && r < 32) chosen = bv;
