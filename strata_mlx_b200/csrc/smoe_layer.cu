@@ -20,7 +20,6 @@
 // activation split and the combine are the matvec kernels' own (mv8_dev.cuh, common.cuh), so every product is
 // the same integer arithmetic.
 #include <algorithm>
-#include <vector>
 
 #include "mv8_dev.cuh"
 #include "router_dev.cuh"
@@ -65,9 +64,8 @@ struct LyArgs {
     LyStack d[4];            // gate / up stacks, costliest first
     LyStack e[2];            // routed down, shared down
     LySource src_d, src_e[2];
-    int nd, jobs_d, team_d;
+    int nd, jobs_d;
     int gr;                  // CTAs of the routed down; the rest take the shared down
-    int team_e[2];
     int nslots, slot_bytes, split_bytes;
 };
 struct alignas(64) LyMaps {
@@ -120,14 +118,18 @@ __device__ __forceinline__ void ly_split_glu(const __half* gate, const __half* u
     m8_split_values(v, hi, lo, scale, lane);
 }
 
+constexpr int kLySlots = 16;  // jobs whose partial sums a CTA holds at once (a ring of job slots)
+
 __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __grid_constant__ LyArgs A,
                                                                      const __grid_constant__ LyMaps M) {
     extern __shared__ __align__(128) uint8_t sm[];
     const int ns = A.nslots, slot_bytes = A.slot_bytes;
     uint8_t* ring = sm;                                                                    // [warp][slot]
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * slot_bytes);  // [warp][slot]
-    float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);                  // [16 warps][16 rows]
-    float* part = red + kM8Warps * 16;                                                     // [4 rows][4 quarters]
+    float* partial = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);              // [job slot][warp][16]
+    int* cnt = reinterpret_cast<int*>(partial + kLySlots * kM8Warps * 16);                 // [job slot] arrivals
+    int* tag = cnt + kLySlots;                                                             // [job slot] its job
+    float* part = reinterpret_cast<float*>(tag + kLySlots);                                // [4 rows][4 quarters]
     uint32_t* sidx = reinterpret_cast<uint32_t*>(part + 16);                               // [k]
     float* sw = reinterpret_cast<float*>(sidx + kLyMaxK);                                  // [k]
     int* flag = reinterpret_cast<int*>(sw + kLyMaxK);                                      // barrier result
@@ -141,13 +143,20 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
     const int G = gridDim.x, b = blockIdx.x;
     const int H = A.hidden, E = A.experts, K = A.k;
 
-    // ---- A: router weights in flight first (4 warps to a row, rows b, b + G, ... of the experts + shared gate)
+    // ---- A: the global loads first (router weights, the token's split block, the codebook), their uses later
     const int router_rows_n = E + (A.sgate != nullptr ? 1 : 0);
     const int my_row = b + G * (warp >> 2);
     const bool row_live = my_row < router_rows_n;
     const __half* row_ptr = my_row < E ? A.router + int64_t(my_row) * H : A.sgate;
     float wv[4][8], acc[kRtTokens];
     router_first(row_ptr, row_live, H, wv);
+    const int xblocks_d = H / kM8XBlock;
+    uint4 xr0 = make_uint4(0u, 0u, 0u, 0u);
+    if (warp < xblocks_d) xr0 = *reinterpret_cast<const uint4*>(A.x + int64_t(warp) * kM8XBlock + 8 * lane);
+    uint32_t g0 = 0u, g1 = 0u;
+    const int li0 = threadIdx.x, li1 = threadIdx.x + kM8Threads;  // 1024 groups of 4 words: 512 x kLyRep / 4
+    g0 = __ldg(kIq3sSigned + (4 * li0) / kLyRep);
+    g1 = __ldg(kIq3sSigned + (4 * li1) / kLyRep);
 
     // the arrival count this launch starts from: a multiple of 3 G (early arrivals at barrier 1 are fewer
     // than G)
@@ -160,97 +169,113 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
         for (int i = 0; i < ns; ++i) tc::mbar_init(&bars[warp * kM8MaxSlots + i], 1);
         tc::fence_barrier_init();
     }
-    m8_fill_grid<kLyRep>(lut);
-    // the token split into int8 hi / lo per 256-column block (phase D's only source row)
-    for (int blk = warp; blk < H / kM8XBlock; blk += kM8Warps) {
-        const int64_t at = int64_t(blk) * kM8XBlock + 8 * lane;
-        m8_split(A.x, nullptr, nullptr, at, xsplit + at, xsplit + H + at, xscale + blk, lane);
+    if (threadIdx.x < kLySlots) {
+        cnt[threadIdx.x] = 0;
+        tag[threadIdx.x] = threadIdx.x;
     }
 
-    // ---- the copy cursor over this warp's items: phase D jobs, then phase E jobs
-    uint8_t* my_ring = ring + size_t(warp) * ns * slot_bytes;
-    uint64_t* my_bars = bars + warp * kM8MaxSlots;
-    // phase D: CTA-fastest round-robin over all teams
-    const int team_d = A.team_d, tid_d = warp / team_d, kq_d = warp % team_d;
-    const int nteams_d = G * (kM8Warps / team_d);
-    const int q0_d = tid_d * G + b;
-    const int jobs_d = q0_d < A.jobs_d ? min((A.jobs_d - q0_d + nteams_d - 1) / nteams_d, 32) : 0;
-    // phase E: CTAs [0, gr) take the routed down's jobs, the rest the shared down's, in contiguous ranges
-    const int eg = b < A.gr ? 0 : 1;
-    const int gsz = eg == 0 ? A.gr : G - A.gr, gb = eg == 0 ? b : b - A.gr;
-    const LyStack& SE = A.e[eg];
-    const int team_e = A.team_e[eg], tid_e = warp / team_e, kq_e = warp % team_e;
-    const int cj0 = static_cast<int>(int64_t(gb) * SE.jobs / gsz), cj1 = static_cast<int>(int64_t(gb + 1) * SE.jobs / gsz);
-    const int q0_e = cj0 + tid_e, teams_e = kM8Warps / team_e;
-    const int jobs_e = q0_e < cj1 ? min((cj1 - q0_e + teams_e - 1) / teams_e, 32) : 0;
-
-    // lane l's phase-D and phase-E jobs: meta = stack | cls << 2 | valid << 6 | pair << 7 | blk << 13, and
-    // the first row of its TMA box
+    // ---- this CTA's jobs, lane i of every warp holding job i: phase D round-robin over the CTAs (CTA-fastest,
+    // costliest stacks first), phase E a contiguous range of one down stack. meta = stack | cls << 2 |
+    // valid << 6 | pair << 7 | blk << 13; y = the first row of its TMA box; u0 = its first unit (stage) among
+    // the CTA's. Units go round-robin over the 16 warps; a warp's units of one job are consecutive.
     auto job_meta = [&](const LyStack& S, int stack, int rest) {
         const int pair = rest / S.tiles, tile = rest - pair * S.tiles;
         return stack | ((tile & (S.q - 1)) << 2) | (pair << 7) | ((tile >> S.lq) << 13);
     };
-    int md = 0, yd = 0, me = 0, ye = 0;
-    if (lane < jobs_d) {
-        const int j = q0_d + lane * nteams_d;
-        int st = 0;
-#pragma unroll
-        for (int i = 1; i < 4; ++i)
-            if (i < A.nd && j >= A.d[i].job0) st = i;
-        md = job_meta(A.d[st], st, j - A.d[st].job0);
-    }
-    if (lane < jobs_e) me = job_meta(SE, eg, q0_e + lane * teams_e);
-    // the box row of a job once its expert is known (stacks with one expert: expert 0)
     auto place = [&](const LyStack& S, int meta, uint32_t e, int& valid_meta) {
         const int ok = e < uint32_t(S.routed ? E : 1) ? 1 : 0;
         valid_meta = meta | (ok << 6);
         return static_cast<int>((int64_t(ok ? e : 0) * S.rows) >> S.lq) + 16 * (meta >> 13);
     };
-    if (lane < jobs_d && !A.d[md & 3].routed) yd = place(A.d[md & 3], md, 0, md);
+    const int nj_d = b < A.jobs_d ? min((A.jobs_d - b + G - 1) / G, 32) : 0;
+    int md = 0, yd = 0, sd = 0, ud = 0;
+    if (lane < nj_d) {
+        const int j = b + lane * G;
+        int st = 0;
+#pragma unroll
+        for (int i = 1; i < 4; ++i)
+            if (i < A.nd && j >= A.d[i].job0) st = i;
+        md = job_meta(A.d[st], st, j - A.d[st].job0);
+        sd = A.d[st].stages;
+        if (!A.d[st].routed) yd = place(A.d[st], md, 0u, md);
+    }
+    // ud: exclusive prefix sum of the jobs' stage counts
+    ud = sd;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, ud, o);
+        if (lane >= o) ud += v;
+    }
+    const int units_d = __shfl_sync(0xffffffffu, ud, 31);
+    ud -= sd;
+    const int eg = b < A.gr ? 0 : 1;
+    const int gsz = eg == 0 ? A.gr : G - A.gr, gb = eg == 0 ? b : b - A.gr;
+    const LyStack& SE = A.e[eg];
+    const int cj0 = static_cast<int>(int64_t(gb) * SE.jobs / gsz), cj1 = static_cast<int>(int64_t(gb + 1) * SE.jobs / gsz);
+    const int nj_e = min(cj1 - cj0, 32);
+    const int units_e = nj_e * SE.stages;
+    int me = 0, ye = 0;
+    if (lane < nj_e) me = job_meta(SE, eg, cj0 + lane);
 
-    int c_phase = 0, c_job = 0, c_k = 0, c_n = 0, c_slot = 0, c_pos = 0, c_step = 0, c_y = 0, c_map = 0,
-        c_valid = 0, c_bytes = 0, issued = 0;
-    auto stages_for = [&](const LyStack& S, int kq, int team) {
-        return S.stages > kq ? (S.stages - kq + team - 1) / team : 0;
-    };
-    // move the cursor to (phase, job) or the first job after it with a stage for this warp
-    auto seek = [&](int phase, int job) {
-        c_phase = phase;
-        for (;;) {
-            const int njobs = c_phase == 0 ? jobs_d : jobs_e;
-            if (job >= njobs) {
-                if (c_phase == 0) {
-                    c_phase = 1;
-                    job = 0;
-                    continue;
-                }
-                c_phase = 2;  // done
-                return;
-            }
-            const int meta = __shfl_sync(0xffffffffu, c_phase == 0 ? md : me, job);
-            const LyStack& S = c_phase == 0 ? A.d[meta & 3] : A.e[meta & 3];
-            const int kq = c_phase == 0 ? kq_d : kq_e, team = c_phase == 0 ? team_d : team_e;
-            c_n = stages_for(S, kq, team);
-            if (c_n == 0) {
-                ++job;
-                continue;
-            }
-            c_job = job;
-            c_k = 0;
-            c_map = S.map;
-            c_pos = ((meta >> 2) & 15) * static_cast<int>(S.row_bytes) + kq * S.stage_bytes;
-            c_step = team * S.stage_bytes;
-            c_y = __shfl_sync(0xffffffffu, c_phase == 0 ? yd : ye, job);
-            c_valid = (meta >> 6) & 1;
-            c_bytes = 16 * S.rs;
-            return;
+    // ---- the token's split and the codebook, now that their loads are in
+    if (warp < xblocks_d) {
+        const __half2* h2 = reinterpret_cast<const __half2*>(&xr0);
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(h2[i]);
+            v[2 * i] = f.x;
+            v[2 * i + 1] = f.y;
         }
+        const int at = warp * kM8XBlock + 8 * lane;
+        m8_split_values(v, xsplit + at, xsplit + H + at, xscale + warp, lane);
+    }
+    for (int blk = warp + kM8Warps; blk < xblocks_d; blk += kM8Warps) {  // (hidden above 4096)
+        const int64_t at = int64_t(blk) * kM8XBlock + 8 * lane;
+        m8_split(A.x, nullptr, nullptr, at, xsplit + at, xsplit + H + at, xscale + blk, lane);
+    }
+    reinterpret_cast<uint4*>(lut)[li0] = make_uint4(g0, g0, g0, g0);
+    reinterpret_cast<uint4*>(lut)[li1] = make_uint4(g1, g1, g1, g1);
+    __syncthreads();
+
+    // ---- the copy cursor over this warp's units: phase D's, then phase E's
+    uint8_t* my_ring = ring + size_t(warp) * ns * slot_bytes;
+    uint64_t* my_bars = bars + warp * kM8MaxSlots;
+    int c_unit = warp, c_slot = 0, issued = 0;  // c_unit: D units below units_d, then E units (offset units_d)
+    // the job of unit u of phase P: the last job whose first unit is at or below u
+    auto job_of_d = [&](int u) {
+        const uint32_t m = __ballot_sync(0xffffffffu, lane < nj_d && ud <= u);
+        return 31 - __clz(m);
+    };
+    // whether the cursor's unit has its place (phase D's routed jobs wait for the choice)
+    bool placed = false;
+    auto cursor_ready = [&]() {
+        if (c_unit >= units_d + units_e) return false;
+        if (placed || c_unit >= units_d) return placed;
+        const int i = job_of_d(c_unit);
+        return !A.d[__shfl_sync(0xffffffffu, md, i) & 3].routed;
     };
     auto issue = [&]() {
+        int meta, y, s;
+        const LyStack* S;
+        if (c_unit < units_d) {
+            const int i = job_of_d(c_unit);
+            meta = __shfl_sync(0xffffffffu, md, i);
+            y = __shfl_sync(0xffffffffu, yd, i);
+            s = c_unit - __shfl_sync(0xffffffffu, ud, i);
+            S = &A.d[meta & 3];
+        } else {
+            const int u = c_unit - units_d, i = u / SE.stages;
+            meta = __shfl_sync(0xffffffffu, me, i);
+            y = __shfl_sync(0xffffffffu, ye, i);
+            s = u - i * SE.stages;
+            S = &SE;
+        }
         if (lane == 0) {
-            if (c_valid) {
-                tc::mbar_arrive_expect_tx(&my_bars[c_slot], static_cast<uint32_t>(c_bytes));
-                tc::tma_load_2d(smem_addr(my_ring + c_slot * slot_bytes), &M.w[c_map], (c_pos & ~15) >> 2, c_y,
+            if ((meta >> 6) & 1) {
+                const int pos = ((meta >> 2) & 15) * static_cast<int>(S->row_bytes) + s * S->stage_bytes;
+                tc::mbar_arrive_expect_tx(&my_bars[c_slot], static_cast<uint32_t>(16 * S->rs));
+                tc::tma_load_2d(smem_addr(my_ring + c_slot * slot_bytes), &M.w[S->map], (pos & ~15) >> 2, y,
                                 &my_bars[c_slot]);
             } else {
                 tc::mbar_arrive(&my_bars[c_slot]);
@@ -258,17 +283,15 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
         }
         ++issued;
         if (++c_slot == ns) c_slot = 0;
-        c_pos += c_step;
-        if (++c_k == c_n) seek(c_phase, c_job + 1);
+        // the next unit of this warp: 16 on, from the last D unit to the first E unit
+        const int nx = c_unit + kM8Warps;
+        c_unit = c_unit < units_d && nx >= units_d ? units_d + warp : nx;
+        if (c_unit >= units_d + units_e) c_unit = units_d + units_e;  // done
     };
-    // the shared expert's first copies go out now (no routing needed); the cursor stops at a routed job
-    seek(0, 0);
-    auto ready = [&]() {  // the cursor's job has its place
-        if (c_phase == 2) return false;
-        const int meta = __shfl_sync(0xffffffffu, c_phase == 0 ? md : me, c_job);
-        return c_phase == 0 && !A.d[meta & 3].routed;
-    };
-    while (issued < ns - 1 && ready()) issue();
+    if (units_d <= warp) c_unit = units_d + warp;  // (no D unit for this warp)
+    if (c_unit >= units_d + units_e) c_unit = units_d + units_e;
+    // the shared expert's first copies go out now (they need no routing)
+    while (issued < ns - 1 && cursor_ready()) issue();
 
     // ---- B: router rows -> logits, the shared gate row -> the gate value
     if (row_live) {
@@ -296,87 +319,135 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
     // ---- C: the top-k of the logits, in every CTA
     if (warp == 0) {
         topk_row<kLyTopkNV>([&](int j) { return __ldcg(A.logits + j); }, E, K, sidx, sw);
+        __syncwarp();
         if (b == 0 && lane < K) {
             A.idx[lane] = sidx[lane];
             A.weights[lane] = sw[lane];
         }
     }
     __syncthreads();
-    if (lane < jobs_d && A.d[md & 3].routed) yd = place(A.d[md & 3], md, sidx[(md >> 7) & 63], md);
-    if (lane < jobs_e) ye = place(SE, me, SE.routed ? sidx[(me >> 7) & 63] : 0u, me);
-    // re-read the cursor's job when none of its items went out yet (it waited for its place)
-    if (c_phase < 2 && c_k == 0) seek(c_phase, c_job);
-    while (c_phase < 2 && issued < ns - 1) issue();
+    if (lane < nj_d && A.d[md & 3].routed) yd = place(A.d[md & 3], md, sidx[(md >> 7) & 63], md);
+    if (lane < nj_e) ye = place(SE, me, SE.routed ? sidx[(me >> 7) & 63] : 0u, me);
+    placed = true;
+    while (issued < ns - 1 && cursor_ready()) issue();
 
-    // ---- D and E: the stages of this warp's jobs
+    // ---- D and E: this warp's units; per job, its partial sums go to the job's slot, and the last warp of
+    // the job to arrive adds them in warp order and writes the 16 rows
     float total[2] = {0.f, 0.f};
     int slot = 0, consumed = 0;
     uint32_t phase = 0;
-    auto run_jobs = [&](int P) {
-        const int njobs = P == 0 ? jobs_d : jobs_e;
-        const int team = P == 0 ? team_d : team_e, kq = P == 0 ? kq_d : kq_e, tid = P == 0 ? tid_d : tid_e;
-        for (int job = 0; job < njobs; ++job) {
-            const int meta = __shfl_sync(0xffffffffu, P == 0 ? md : me, job);
-            const LyStack& S = P == 0 ? A.d[meta & 3] : A.e[meta & 3];
-            const int cls = (meta >> 2) & 15, valid = (meta >> 6) & 1, pair = (meta >> 7) & 63, blk = meta >> 13;
-            // the job's activation row in the split area: the token (D), or the pair's slot (E: the first or
+    auto flush = [&](int job, const LyStack& S, int meta, int u0, int nst) {
+        const int js = job & (kLySlots - 1);
+        // the slot's previous job (job - kLySlots) must have been added up (bounded wait; it should not wait)
+        if (lane == 0) {
+            const volatile int* t = tag + js;
+            if (*t != job) {
+                const uint64_t t0 = tc::globaltimer_ns();
+                while (*t != job && tc::globaltimer_ns() - t0 < tc::kWaitNs) __nanosleep(32);
+            }
+        }
+        __syncwarp();
+        float* pw = partial + (js * kM8Warps + warp) * 16;
+        if (tig == 0) {
+            pw[gid] = total[0];
+            pw[gid + 8] = total[1];
+        }
+        total[0] = total[1] = 0.f;
+        __syncwarp();
+        int last = 0;
+        if (lane == 0) {
+            __threadfence_block();
+            last = atomicAdd(cnt + js, 1) == min(nst, kM8Warps) - 1;
+            __threadfence_block();
+        }
+        last = __shfl_sync(0xffffffffu, last, 0);
+        if (!last) return;
+        const int cls = (meta >> 2) & 15, valid = (meta >> 6) & 1, pair = (meta >> 7) & 63, blk = meta >> 13;
+        if (lane < 16) {
+            float v = 0.f;
+            bool first = true;
+            for (int w = 0; w < kM8Warps; ++w) {
+                if (((w - u0) & (kM8Warps - 1)) >= nst) continue;  // warp w had no unit of this job
+                const float pv = partial[(js * kM8Warps + w) * 16 + lane];
+                v = first ? pv : v + pv;
+                first = false;
+            }
+            const int64_t row = int64_t(blk) * 16 * S.q + cls + int64_t(S.q) * lane;
+            if (valid && row < S.rows) S.out[int64_t(pair) * S.rows + row] = __float2half_rn(v);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            cnt[js] = 0;
+            __threadfence_block();
+            *reinterpret_cast<volatile int*>(tag + js) = job + kLySlots;
+        }
+    };
+    auto run_units = [&](int P) {
+        const int units = P == 0 ? units_d : units_e;
+        int cur = -1, cur_meta = 0, cur_u0 = 0, cur_n = 0;
+        const LyStack* CS = nullptr;
+        for (int u = warp; u < units; u += kM8Warps) {
+            int i, meta, s;
+            const LyStack* S;
+            int u0, nst;
+            if (P == 0) {
+                i = job_of_d(u);
+                meta = __shfl_sync(0xffffffffu, md, i);
+                u0 = __shfl_sync(0xffffffffu, ud, i);
+                S = &A.d[meta & 3];
+                nst = S->stages;
+            } else {
+                i = u / SE.stages;
+                meta = __shfl_sync(0xffffffffu, me, i);
+                u0 = i * SE.stages;
+                S = &SE;
+                nst = SE.stages;
+            }
+            s = u - u0;
+            if (i != cur) {
+                if (cur >= 0) flush(cur, *CS, cur_meta, cur_u0, cur_n);
+                cur = i;
+                cur_meta = meta;
+                cur_u0 = u0;
+                cur_n = nst;
+                CS = S;
+            }
+            // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
+            __syncwarp();
+            if (c_unit < units_d + units_e) issue();
+            const int cs = slot;
+            if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cs], phase, kM8WaitLimit));
+            ++consumed;
+            if (++slot == ns) {
+                slot = 0;
+                phase ^= 1;
+            }
+            if (!ok || !((meta >> 6) & 1)) continue;
+            // the unit's activation row in the split area: the token (D), or the pair's row (E: the first or
             // second routed pair of this CTA's range, or the shared row)
-            const int cols = static_cast<int>(S.stages) * S.stage_cols;
-            const int lrow = P == 0 ? 0 : (S.routed ? pair - (cj0 / S.tiles) : 0);
+            const int cols = S->stages * S->stage_cols;
+            const int lrow = P == 0 ? 0 : (S->routed ? ((meta >> 7) & 63) - cj0 / S->tiles : 0);
             const uint8_t* xh = reinterpret_cast<const uint8_t*>(xsplit) + int64_t(lrow) * cols;
             const uint8_t* xl = xh + (P == 0 ? H : A.split_bytes / 2);
             const float* xsc = xscale + lrow * (cols / kM8XBlock);
-            const int n = stages_for(S, kq, team);
-            const bool iq3 = S.kind == M8IQ3S<2>::kKind;
-            int pos = cls * static_cast<int>(S.row_bytes) + kq * S.stage_bytes;
-            const int step = team * S.stage_bytes;
-            int xc = kq * S.stage_cols;
-            const int xstep = team * S.stage_cols;
-            for (int k = 0; k < n; ++k, pos += step, xc += xstep) {
-                __syncwarp();
-                if (c_phase < 2) issue();
-                const int cur = slot;
-                if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, kM8WaitLimit));
-                ++consumed;
-                if (++slot == ns) {
-                    slot = 0;
-                    phase ^= 1;
-                }
-                if (!ok || !valid) continue;
-                const uint8_t* st = my_ring + cur * slot_bytes + (pos & 15);
-                if (iq3)
-                    M8IQ3S<2, kLyRep>::stage(st + gid * M8IQ3S<2>::kRS, st + (gid + 8) * M8IQ3S<2>::kRS, tig, gid, lut,
-                                             xh + xc, xl + xc, xsc + xc / kM8XBlock, total);
-                else
-                    M8Q8_0::stage(st + gid * M8Q8_0::kRS, st + (gid + 8) * M8Q8_0::kRS, tig, gid, lut, xh + xc,
-                                  xl + xc, xsc + xc / kM8XBlock, total);
-            }
-            // the team's partial sums of the job's 16 rows, added in warp order
-            float* rq = red + (tid * team) * 16;
-            if (tig == 0) {
-                rq[kq * 16 + gid] = total[0];
-                rq[kq * 16 + gid + 8] = total[1];
-            }
-            total[0] = total[1] = 0.f;
-            if (team == 1) __syncwarp();
-            else asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid), "r"(32 * team) : "memory");
-            if (kq == 0 && lane < 16) {
-                const int64_t row = int64_t(blk) * 16 * S.q + cls + int64_t(S.q) * lane;
-                if (valid && row < S.rows) {
-                    float v = rq[lane];
-                    for (int i = 1; i < team; ++i) v += rq[16 * i + lane];
-                    S.out[int64_t(pair) * S.rows + row] = __float2half_rn(v);
-                }
-            }
-            if (team == 1) __syncwarp();
-            else asm volatile("bar.sync %0, %1;\n" ::"r"(1 + tid), "r"(32 * team) : "memory");
+            const int pos = ((meta >> 2) & 15) * static_cast<int>(S->row_bytes) + s * S->stage_bytes;
+            const int xc = s * S->stage_cols;
+            const uint8_t* st = my_ring + cs * slot_bytes + (pos & 15);
+            if (S->kind == M8IQ3S<2>::kKind)
+                M8IQ3S<2, kLyRep>::stage(st + gid * M8IQ3S<2>::kRS, st + (gid + 8) * M8IQ3S<2>::kRS, tig, gid, lut,
+                                         xh + xc, xl + xc, xsc + xc / kM8XBlock, total);
+            else
+                M8Q8_0::stage(st + gid * M8Q8_0::kRS, st + (gid + 8) * M8Q8_0::kRS, tig, gid, lut, xh + xc, xl + xc,
+                              xsc + xc / kM8XBlock, total);
         }
+        if (cur >= 0) flush(cur, *CS, cur_meta, cur_u0, cur_n);
     };
-    run_jobs(0);
+    run_units(0);
     ok = grid_sync(A.bar, base + 2ull * G, A.err, flag) && ok;
 
-    // ---- E: the split of this CTA's SwiGLU rows (one or two routed pairs, or the shared row), then its jobs
+    // ---- E: the split of this CTA's SwiGLU rows (one or two routed pairs, or the shared row), then its units
     {
+        if (threadIdx.x < kLySlots) tag[threadIdx.x] = threadIdx.x;  // (every phase-D job was added up)
         const LySource& X = A.src_e[eg];
         const int xblocks = X.cols / kM8XBlock;
         const int p0 = SE.routed ? cj0 / SE.tiles : 0;
@@ -390,7 +461,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
         }
         __syncthreads();
     }
-    run_jobs(1);
+    run_units(1);
     ok = grid_sync(A.bar, base + 3ull * G, A.err, flag) && ok;
 
     // ---- F: the combine, rows [b H / G, (b + 1) H / G)
@@ -539,30 +610,9 @@ extern "C" int smoe_decode_layer(const SmoeDecodeLayer* L, const void* x, void* 
     A.src_e[0] = LySource{nullptr, g_r, u_r, kk, static_cast<int>(F)};
     A.src_e[1] = LySource{nullptr, gs, us, 1, static_cast<int>(FS)};
 
-    // phase D's team size: the least work on the busiest warp (jobs round-robin over all teams, CTA-fastest)
-    {
-        int64_t best = -1;
-        std::vector<int64_t> load;
-        for (int t = 1; t <= kM8Warps; t *= 2) {
-            const int64_t nteams = int64_t(G) * (kM8Warps / t);
-            if (jobs > 32 * nteams) continue;
-            load.assign(static_cast<size_t>(std::min<int64_t>(nteams, jobs)), 0);
-            int64_t j = 0;
-            for (int i = 0; i < 4; ++i) {
-                const LyStack& S = A.d[i];
-                const int64_t sb = int64_t(16) * S.stage_bytes * (S.kind == 21 ? 5 : 2);  // decode cost per byte
-                const int64_t w = (S.stages + t - 1) / t * sb + (t > 1 ? sb / 2 : 0);
-                for (int64_t q = 0; q < S.jobs; ++q, ++j) load[static_cast<size_t>(j % nteams)] += w;
-            }
-            const int64_t span = *std::max_element(load.begin(), load.end());
-            if (best < 0 || span < best) {
-                best = span;
-                A.team_d = t;
-            }
-        }
-        SMOE_REQUIRE(best >= 0, SMOE_ESHAPE, "decode_layer: too many jobs");
-    }
-    // phase E: CTAs in proportion to the two down stacks' decode cost, then each group's team size
+    // phase D: jobs round-robin over the CTAs, at most 32 a CTA
+    SMOE_REQUIRE(jobs <= 32 * int64_t(G), SMOE_ESHAPE, "decode_layer: too many gate / up jobs");
+    // phase E: CTAs in proportion to the two down stacks' decode cost (an IQ3_S byte about 2.5 times a Q8_0 one)
     {
         const double cr = double(A.e[0].jobs) * A.e[0].stages * A.e[0].stage_bytes * 5;
         const double cs = double(A.e[1].jobs) * A.e[1].stages * A.e[1].stage_bytes * 2;
@@ -571,18 +621,7 @@ extern "C" int smoe_decode_layer(const SmoeDecodeLayer* L, const void* x, void* 
             const LyStack& S = A.e[g];
             const int gsz = g == 0 ? A.gr : G - A.gr;
             const int64_t per = (S.jobs + gsz - 1) / gsz;  // jobs of the busiest CTA
-            int64_t best = -1;
-            for (int t = 1; t <= kM8Warps; t *= 2) {
-                const int64_t teams = kM8Warps / t;
-                const int64_t most = (per + teams - 1) / teams;
-                if (most > 32) continue;
-                const int64_t span = most * (4 * ((S.stages + t - 1) / t) + (t > 1 ? 3 : 0));
-                if (best < 0 || span < best) {
-                    best = span;
-                    A.team_e[g] = t;
-                }
-            }
-            SMOE_REQUIRE(best >= 0, SMOE_ESHAPE, "decode_layer: too many down jobs");
+            SMOE_REQUIRE(per <= 32, SMOE_ESHAPE, "decode_layer: too many down jobs");
             // a routed CTA's range must span at most two pairs (its split holds two rows)
             if (g == 0) SMOE_REQUIRE(per <= S.tiles, SMOE_ESHAPE, "decode_layer: too few CTAs for the routed down");
         }
@@ -592,8 +631,8 @@ extern "C" int smoe_decode_layer(const SmoeDecodeLayer* L, const void* x, void* 
     const int64_t split_d = 2 * H, split_e = std::max<int64_t>(2 * 2 * F, 2 * FS);
     A.split_bytes = static_cast<int>((std::max(split_d, split_e) + 127) & ~int64_t(127));
     A.slot_bytes = 16 * std::max(M8IQ3S<2>::kRS, M8Q8_0::kRS);
-    const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + 16 * 4 + kLyMaxK * 8 + 32 * 4 +
-                         512 * kLyRep * 4 + 128 * 4 + size_t(A.split_bytes);
+    const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + size_t(kLySlots) * kM8Warps * 16 * 4 + 2 * kLySlots * 4 +
+                         16 * 4 + kLyMaxK * 8 + 32 * 4 + 512 * kLyRep * 4 + 128 * 4 + size_t(A.split_bytes);
     const size_t slot = size_t(kM8Warps) * A.slot_bytes;
     int ns = kM8MaxSlots;
     while (ns > 2 && fixed + ns * slot > size_t(227 * 1024 - 256)) --ns;
