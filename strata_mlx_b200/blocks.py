@@ -227,6 +227,7 @@ MMA_MATVEC = {"IQ3_S": 256, "Q8_0": 128}
 # pairs) fit in its shared memory: types, the columns it splits the activations by, the bytes it may hold
 FUSED_GLU = ("IQ3_S", "Q8_0")
 FUSED_GLU_COLS, FUSED_GLU_BYTES = 256, 64 << 10
+BATCHED_DOWN = False  # decode_products: the routed and the shared down product in one launch
 
 
 def matvec_glu(lin, idx: torch.Tensor, gate: torch.Tensor, up: torch.Tensor):
@@ -341,8 +342,14 @@ def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, 
     if pairs:
         matvec_batch([_problem(gate, idx, pairs, k, g_r, x=x2), _problem(up, idx, pairs, k, u_r, x=x2),
                       _problem(sg, zeros, tokens, 1, gs, x=x2), _problem(su, zeros, tokens, 1, us, x=x2)])
-    # the two down products stay separate launches: in one launch the shared expert's long rows (4096 columns)
-    # are the slowest warps' work and the pair is slower than the two alone
+    if BATCHED_DOWN and sd.kind in FUSED_GLU and down.kind in FUSED_GLU:
+        # both down products in one launch (the shared expert's Q8_0 rows and the routed experts' in the same
+        # CTAs, so the SMs stream one while they decode the other); the combine is its own launch
+        y = torch.empty((pairs, down.output_dims), dtype=dt, device=dev)
+        s = torch.empty((tokens, sd.output_dims), dtype=dt, device=dev)
+        if pairs:
+            matvec_batch([_problem(down, idx, pairs, 1, y, gate=g_r, up=u_r), _problem(sd, zeros, tokens, 1, s, gate=gs, up=us)])
+        return y.reshape(*indices.shape, down.output_dims), s.reshape(*x.shape[:-1], sd.output_dims)
     y = matvec_glu(down, idx, g_r, u_r)
     fused = (w is not None and g is not None and sd.kind in FUSED_GLU and sd.input_dims % FUSED_GLU_COLS == 0
              and tokens * sd.input_dims * 2 <= FUSED_GLU_BYTES and w.dtype == torch.float32 and g.dtype == dt

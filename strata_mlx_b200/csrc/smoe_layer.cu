@@ -65,7 +65,6 @@ struct LyArgs {
     LyStack e[2];            // routed down, shared down
     LySource src_d, src_e[2];
     int nd, jobs_d;
-    int gr;                  // CTAs of the routed down; the rest take the shared down
     int nslots, slot_bytes, split_bytes;
 };
 struct alignas(64) LyMaps {
@@ -94,7 +93,6 @@ __device__ __forceinline__ bool grid_sync(unsigned long long* bar, unsigned long
                     atomicExch(err, 1);
                     break;
                 }
-                __nanosleep(64);
             }
         }
         __threadfence();
@@ -118,7 +116,8 @@ __device__ __forceinline__ void ly_split_glu(const __half* gate, const __half* u
     m8_split_values(v, hi, lo, scale, lane);
 }
 
-constexpr int kLySlots = 16;  // jobs whose partial sums a CTA holds at once (a ring of job slots)
+// A CTA's jobs of a phase, each with a slot for its warps' partial sums (the host keeps every CTA within it)
+constexpr int kLySlots = 17;
 
 __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __grid_constant__ LyArgs A,
                                                                      const __grid_constant__ LyMaps M) {
@@ -127,15 +126,14 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
     uint8_t* ring = sm;                                                                    // [warp][slot]
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * slot_bytes);  // [warp][slot]
     float* partial = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);              // [job slot][warp][16]
-    int* cnt = reinterpret_cast<int*>(partial + kLySlots * kM8Warps * 16);                 // [job slot] arrivals
-    int* tag = cnt + kLySlots;                                                             // [job slot] its job
-    float* part = reinterpret_cast<float*>(tag + kLySlots);                                // [4 rows][4 quarters]
+    int* cnt = reinterpret_cast<int*>(partial + kLySlots * kM8Warps * 16);                 // [job slot] units in
+    float* part = reinterpret_cast<float*>(cnt + 32);                                      // [4 rows][4 quarters]
     uint32_t* sidx = reinterpret_cast<uint32_t*>(part + 16);                               // [k]
     float* sw = reinterpret_cast<float*>(sidx + kLyMaxK);                                  // [k]
     int* flag = reinterpret_cast<int*>(sw + kLyMaxK);                                      // barrier result
     uint32_t* lut = reinterpret_cast<uint32_t*>(flag + 32);                                // 512 x kLyRep words
-    float* xscale = reinterpret_cast<float*>(lut + 512 * kLyRep);                          // [128]
-    int8_t* xsplit = reinterpret_cast<int8_t*>(xscale + 128);                              // split_bytes
+    float* xscale = reinterpret_cast<float*>(lut + 512 * kLyRep);                          // [64]
+    int8_t* xsplit = reinterpret_cast<int8_t*>(xscale + 64);                               // split_bytes
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
@@ -169,15 +167,15 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
         for (int i = 0; i < ns; ++i) tc::mbar_init(&bars[warp * kM8MaxSlots + i], 1);
         tc::fence_barrier_init();
     }
-    if (threadIdx.x < kLySlots) {
-        cnt[threadIdx.x] = 0;
-        tag[threadIdx.x] = threadIdx.x;
-    }
+    if (threadIdx.x < kLySlots) cnt[threadIdx.x] = 0;
+    for (int i = threadIdx.x; i < kLySlots * kM8Warps * 16; i += kM8Threads) partial[i] = 0.f;
 
-    // ---- this CTA's jobs, lane i of every warp holding job i: phase D round-robin over the CTAs (CTA-fastest,
-    // costliest stacks first), phase E a contiguous range of one down stack. meta = stack | cls << 2 |
-    // valid << 6 | pair << 7 | blk << 13; y = the first row of its TMA box; u0 = its first unit (stage) among
-    // the CTA's. Units go round-robin over the 16 warps; a warp's units of one job are consecutive.
+    // ---- this CTA's jobs. A phase's jobs are of two stacks: the compute-heavy one (kind A: IQ3_S, SA stages a
+    // job) and the bandwidth-heavy one (kind B: Q8_0, SB stages); lane i of every warp holds the CTA's job i
+    // (its A jobs first, then its B jobs): meta = stack | cls << 2 | valid << 6 | pair << 7 | blk << 13, and y,
+    // the first row of its TMA box. The CTA's units (stages) of both kinds are merged in proportion (unit p is
+    // of kind A when floor((p + 1) NA / N) > floor(p NA / N)), so every SM decodes and streams at once, and
+    // dealt round-robin to the 16 warps.
     auto job_meta = [&](const LyStack& S, int stack, int rest) {
         const int pair = rest / S.tiles, tile = rest - pair * S.tiles;
         return stack | ((tile & (S.q - 1)) << 2) | (pair << 7) | ((tile >> S.lq) << 13);
@@ -187,35 +185,40 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
         valid_meta = meta | (ok << 6);
         return static_cast<int>((int64_t(ok ? e : 0) * S.rows) >> S.lq) + 16 * (meta >> 13);
     };
-    const int nj_d = b < A.jobs_d ? min((A.jobs_d - b + G - 1) / G, 32) : 0;
-    int md = 0, yd = 0, sd = 0, ud = 0;
+    // phase D: the jobs of all four stacks round-robin over the CTAs; stacks 0, 1 (the shared expert, B) take
+    // the first jobs, so a CTA's B jobs come first in its round-robin list: reorder to A first
+    const int nj_d = b < A.jobs_d ? min((A.jobs_d - b + G - 1) / G, kLySlots) : 0;
+    const int jb_d = b < A.d[2].job0 ? min((A.d[2].job0 - b + G - 1) / G, nj_d) : 0;  // B jobs of this CTA
+    const int ja_d = nj_d - jb_d;
+    int md = 0, yd = 0;
     if (lane < nj_d) {
-        const int j = b + lane * G;
+        const int li = lane < ja_d ? jb_d + lane : lane - ja_d;  // round-robin index of lane's job
+        const int j = b + li * G;
         int st = 0;
 #pragma unroll
         for (int i = 1; i < 4; ++i)
             if (i < A.nd && j >= A.d[i].job0) st = i;
         md = job_meta(A.d[st], st, j - A.d[st].job0);
-        sd = A.d[st].stages;
         if (!A.d[st].routed) yd = place(A.d[st], md, 0u, md);
     }
-    // ud: exclusive prefix sum of the jobs' stage counts
-    ud = sd;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, ud, o);
-        if (lane >= o) ud += v;
-    }
-    const int units_d = __shfl_sync(0xffffffffu, ud, 31);
-    ud -= sd;
-    const int eg = b < A.gr ? 0 : 1;
-    const int gsz = eg == 0 ? A.gr : G - A.gr, gb = eg == 0 ? b : b - A.gr;
-    const LyStack& SE = A.e[eg];
-    const int cj0 = static_cast<int>(int64_t(gb) * SE.jobs / gsz), cj1 = static_cast<int>(int64_t(gb + 1) * SE.jobs / gsz);
-    const int nj_e = min(cj1 - cj0, 32);
-    const int units_e = nj_e * SE.stages;
+    const int sa_d = A.d[2].stages, sb_d = A.d[0].stages;
+    // phase E: this CTA's tiles of one routed pair (the CTAs split the pairs evenly, then a pair's tiles), and
+    // its share of the shared down's jobs
+    const LyStack& ER = A.e[0];
+    const LyStack& ES = A.e[1];
+    const int npair = ER.pairs;
+    const int epair = static_cast<int>(int64_t(b) * npair / G);
+    const int pc0 = static_cast<int>((int64_t(epair) * G + npair - 1) / npair);
+    const int pc1 = static_cast<int>((int64_t(epair + 1) * G + npair - 1) / npair);
+    const int rt0 = static_cast<int>(int64_t(b - pc0) * ER.tiles / (pc1 - pc0));
+    const int rt1 = static_cast<int>(int64_t(b - pc0 + 1) * ER.tiles / (pc1 - pc0));
+    const int ja_e = min(rt1 - rt0, kLySlots);
+    const int sj0 = static_cast<int>(int64_t(b) * ES.jobs / G), sj1 = static_cast<int>(int64_t(b + 1) * ES.jobs / G);
+    const int jb_e = min(sj1 - sj0, kLySlots - ja_e);
     int me = 0, ye = 0;
-    if (lane < nj_e) me = job_meta(SE, eg, cj0 + lane);
+    if (lane < ja_e) me = job_meta(ER, 0, epair * ER.tiles + rt0 + lane);
+    else if (lane < ja_e + jb_e) me = job_meta(ES, 1, sj0 + lane - ja_e);
+    const int sa_e = ER.stages, sb_e = ES.stages;
 
     // ---- the token's split and the codebook, now that their loads are in
     if (warp < xblocks_d) {
@@ -228,54 +231,98 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
             v[2 * i + 1] = f.y;
         }
         const int at = warp * kM8XBlock + 8 * lane;
-        m8_split_values(v, xsplit + at, xsplit + H + at, xscale + warp, lane);
+        m8_split_values(v, xsplit + at, xsplit + A.split_bytes / 2 + at, xscale + warp, lane);
     }
     for (int blk = warp + kM8Warps; blk < xblocks_d; blk += kM8Warps) {  // (hidden above 4096)
         const int64_t at = int64_t(blk) * kM8XBlock + 8 * lane;
-        m8_split(A.x, nullptr, nullptr, at, xsplit + at, xsplit + H + at, xscale + blk, lane);
+        m8_split(A.x, nullptr, nullptr, at, xsplit + at, xsplit + A.split_bytes / 2 + at, xscale + blk, lane);
     }
     reinterpret_cast<uint4*>(lut)[li0] = make_uint4(g0, g0, g0, g0);
     reinterpret_cast<uint4*>(lut)[li1] = make_uint4(g1, g1, g1, g1);
     __syncthreads();
 
+    // ---- units: phase P's merged sequence of NA A units and NB B units; position p -> (job, stage)
+    const int na_d = ja_d * sa_d, nb_d = jb_d * sb_d, n_d = na_d + nb_d;
+    const int na_e = ja_e * sa_e, nb_e = jb_e * sb_e, n_e = na_e + nb_e;
+    // A warp walks positions p = warp, warp + 16, ...: a = floor(p NA / N) A units lie before p, r the
+    // remainder; p is an A unit when r + NA >= N. Jobs from unit indices by multiplying with 2^16 / stages
+    // rounded up (exact below 2048 units).
+    struct Unit {
+        int job, stage, kind;  // job: the CTA's job index (its lane); kind 0 = A, 1 = B
+    };
+    struct UnitWalk {
+        int p, a, r;
+    };
+    auto walk_start = [&](int P, int p0) {
+        const int na = P == 0 ? na_d : na_e, n = P == 0 ? n_d : n_e;
+        UnitWalk w;
+        w.p = p0;
+        w.a = n > 0 ? p0 * na / n : 0;
+        w.r = n > 0 ? p0 * na - w.a * n : 0;
+        return w;
+    };
+    const int q16_d = n_d > 0 ? kM8Warps * na_d / n_d : 0, r16_d = n_d > 0 ? kM8Warps * na_d - q16_d * n_d : 0;
+    const int q16_e = n_e > 0 ? kM8Warps * na_e / n_e : 0, r16_e = n_e > 0 ? kM8Warps * na_e - q16_e * n_e : 0;
+    const int ma_d = (65536 + sa_d - 1) / sa_d, mb_d = (65536 + sb_d - 1) / sb_d;
+    const int ma_e = (65536 + sa_e - 1) / sa_e, mb_e = (65536 + sb_e - 1) / sb_e;
+    auto walk_unit = [&](int P, const UnitWalk& w) {
+        const int na = P == 0 ? na_d : na_e, n = P == 0 ? n_d : n_e;
+        Unit u;
+        if (w.r + na >= n) {
+            const int sa = P == 0 ? sa_d : sa_e;
+            u.kind = 0;
+            u.job = (w.a * (P == 0 ? ma_d : ma_e)) >> 16;
+            u.stage = w.a - u.job * sa;
+        } else {
+            const int sb = P == 0 ? sb_d : sb_e, ja = P == 0 ? ja_d : ja_e, q = w.p - w.a;
+            const int jb = (q * (P == 0 ? mb_d : mb_e)) >> 16;
+            u.kind = 1;
+            u.job = ja + jb;
+            u.stage = q - jb * sb;
+        }
+        return u;
+    };
+    auto walk_next = [&](int P, UnitWalk& w) {
+        const int n = P == 0 ? n_d : n_e;
+        w.p += kM8Warps;
+        w.a += P == 0 ? q16_d : q16_e;
+        w.r += P == 0 ? r16_d : r16_e;
+        if (w.r >= n) {
+            w.r -= n;
+            ++w.a;
+        }
+    };
+
     // ---- the copy cursor over this warp's units: phase D's, then phase E's
     uint8_t* my_ring = ring + size_t(warp) * ns * slot_bytes;
     uint64_t* my_bars = bars + warp * kM8MaxSlots;
-    int c_unit = warp, c_slot = 0, issued = 0;  // c_unit: D units below units_d, then E units (offset units_d)
-    // the job of unit u of phase P: the last job whose first unit is at or below u
-    auto job_of_d = [&](int u) {
-        const uint32_t m = __ballot_sync(0xffffffffu, lane < nj_d && ud <= u);
-        return 31 - __clz(m);
+    int c_phase = 0, c_slot = 0, issued = 0;
+    UnitWalk cw = walk_start(0, warp);
+    auto c_norm = [&]() {  // to the next phase when this one is done
+        if (c_phase == 0 && cw.p >= n_d) {
+            c_phase = 1;
+            cw = walk_start(1, warp);
+        }
+        if (c_phase == 1 && cw.p >= n_e) c_phase = 2;
     };
-    // whether the cursor's unit has its place (phase D's routed jobs wait for the choice)
+    c_norm();
     bool placed = false;
-    auto cursor_ready = [&]() {
-        if (c_unit >= units_d + units_e) return false;
-        if (placed || c_unit >= units_d) return placed;
-        const int i = job_of_d(c_unit);
-        return !A.d[__shfl_sync(0xffffffffu, md, i) & 3].routed;
+    auto cursor_ready = [&]() {  // the cursor's unit has its place (phase D's routed jobs wait for the choice)
+        if (c_phase == 2) return false;
+        if (placed) return true;
+        if (c_phase == 1) return false;
+        return walk_unit(0, cw).kind == 1;  // the shared expert's units need no routing
     };
     auto issue = [&]() {
-        int meta, y, s;
-        const LyStack* S;
-        if (c_unit < units_d) {
-            const int i = job_of_d(c_unit);
-            meta = __shfl_sync(0xffffffffu, md, i);
-            y = __shfl_sync(0xffffffffu, yd, i);
-            s = c_unit - __shfl_sync(0xffffffffu, ud, i);
-            S = &A.d[meta & 3];
-        } else {
-            const int u = c_unit - units_d, i = u / SE.stages;
-            meta = __shfl_sync(0xffffffffu, me, i);
-            y = __shfl_sync(0xffffffffu, ye, i);
-            s = u - i * SE.stages;
-            S = &SE;
-        }
+        const Unit u = walk_unit(c_phase, cw);
+        const int meta = __shfl_sync(0xffffffffu, c_phase == 0 ? md : me, u.job);
+        const int y = __shfl_sync(0xffffffffu, c_phase == 0 ? yd : ye, u.job);
+        const LyStack& S = c_phase == 0 ? A.d[meta & 3] : A.e[meta & 3];
         if (lane == 0) {
             if ((meta >> 6) & 1) {
-                const int pos = ((meta >> 2) & 15) * static_cast<int>(S->row_bytes) + s * S->stage_bytes;
-                tc::mbar_arrive_expect_tx(&my_bars[c_slot], static_cast<uint32_t>(16 * S->rs));
-                tc::tma_load_2d(smem_addr(my_ring + c_slot * slot_bytes), &M.w[S->map], (pos & ~15) >> 2, y,
+                const int pos = ((meta >> 2) & 15) * static_cast<int>(S.row_bytes) + u.stage * S.stage_bytes;
+                tc::mbar_arrive_expect_tx(&my_bars[c_slot], static_cast<uint32_t>(16 * S.rs));
+                tc::tma_load_2d(smem_addr(my_ring + c_slot * slot_bytes), &M.w[S.map], (pos & ~15) >> 2, y,
                                 &my_bars[c_slot]);
             } else {
                 tc::mbar_arrive(&my_bars[c_slot]);
@@ -283,13 +330,9 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
         }
         ++issued;
         if (++c_slot == ns) c_slot = 0;
-        // the next unit of this warp: 16 on, from the last D unit to the first E unit
-        const int nx = c_unit + kM8Warps;
-        c_unit = c_unit < units_d && nx >= units_d ? units_d + warp : nx;
-        if (c_unit >= units_d + units_e) c_unit = units_d + units_e;  // done
+        walk_next(c_phase, cw);
+        c_norm();
     };
-    if (units_d <= warp) c_unit = units_d + warp;  // (no D unit for this warp)
-    if (c_unit >= units_d + units_e) c_unit = units_d + units_e;
     // the shared expert's first copies go out now (they need no routing)
     while (issued < ns - 1 && cursor_ready()) issue();
 
@@ -327,94 +370,67 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
     }
     __syncthreads();
     if (lane < nj_d && A.d[md & 3].routed) yd = place(A.d[md & 3], md, sidx[(md >> 7) & 63], md);
-    if (lane < nj_e) ye = place(SE, me, SE.routed ? sidx[(me >> 7) & 63] : 0u, me);
+    if (lane < ja_e) ye = place(ER, me, sidx[(me >> 7) & 63], me);
+    else if (lane < ja_e + jb_e) ye = place(ES, me, 0u, me);
     placed = true;
     while (issued < ns - 1 && cursor_ready()) issue();
 
-    // ---- D and E: this warp's units; per job, its partial sums go to the job's slot, and the last warp of
-    // the job to arrive adds them in warp order and writes the 16 rows
-    float total[2] = {0.f, 0.f};
+    // ---- D and E: this warp's units. A warp adds up each job's units it has (two jobs open at a time: one
+    // of each kind); its partial sums then go to the job's slot, and the warp whose units complete the job adds
+    // the 16 warps' slots in warp order (zero where a warp had none) and writes the 16 rows.
+    float tot[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    int open_job[2] = {-1, -1}, open_units[2] = {0, 0};
     int slot = 0, consumed = 0;
     uint32_t phase = 0;
-    auto flush = [&](int job, const LyStack& S, int meta, int u0, int nst) {
-        const int js = job & (kLySlots - 1);
-        // the slot's previous job (job - kLySlots) must have been added up (bounded wait; it should not wait)
-        if (lane == 0) {
-            const volatile int* t = tag + js;
-            if (*t != job) {
-                const uint64_t t0 = tc::globaltimer_ns();
-                while (*t != job && tc::globaltimer_ns() - t0 < tc::kWaitNs) __nanosleep(32);
-            }
-        }
-        __syncwarp();
+    auto flush = [&](int P, int kind) {
+        const int job = open_job[kind];
+        if (job < 0) return;
+        const int js = job;
+        const int meta = __shfl_sync(0xffffffffu, P == 0 ? md : me, job);
+        const LyStack& S = P == 0 ? A.d[meta & 3] : A.e[meta & 3];
         float* pw = partial + (js * kM8Warps + warp) * 16;
         if (tig == 0) {
-            pw[gid] = total[0];
-            pw[gid + 8] = total[1];
+            pw[gid] = tot[kind][0];
+            pw[gid + 8] = tot[kind][1];
         }
-        total[0] = total[1] = 0.f;
+        tot[kind][0] = tot[kind][1] = 0.f;
         __syncwarp();
         int last = 0;
         if (lane == 0) {
             __threadfence_block();
-            last = atomicAdd(cnt + js, 1) == min(nst, kM8Warps) - 1;
+            last = atomicAdd(cnt + js, open_units[kind]) + open_units[kind] == S.stages;
             __threadfence_block();
         }
+        open_job[kind] = -1;
+        open_units[kind] = 0;
         last = __shfl_sync(0xffffffffu, last, 0);
         if (!last) return;
         const int cls = (meta >> 2) & 15, valid = (meta >> 6) & 1, pair = (meta >> 7) & 63, blk = meta >> 13;
+        float* pj = partial + js * kM8Warps * 16;
         if (lane < 16) {
-            float v = 0.f;
-            bool first = true;
-            for (int w = 0; w < kM8Warps; ++w) {
-                if (((w - u0) & (kM8Warps - 1)) >= nst) continue;  // warp w had no unit of this job
-                const float pv = partial[(js * kM8Warps + w) * 16 + lane];
-                v = first ? pv : v + pv;
-                first = false;
-            }
+            float v = pj[lane];
+            for (int w = 1; w < kM8Warps; ++w) v += pj[w * 16 + lane];
             const int64_t row = int64_t(blk) * 16 * S.q + cls + int64_t(S.q) * lane;
             if (valid && row < S.rows) S.out[int64_t(pair) * S.rows + row] = __float2half_rn(v);
         }
         __syncwarp();
-        if (lane == 0) {
-            cnt[js] = 0;
-            __threadfence_block();
-            *reinterpret_cast<volatile int*>(tag + js) = job + kLySlots;
-        }
+        // the slot back to zero for the next phase
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pj[i * 32 + lane] = 0.f;
+        if (lane == 0) cnt[js] = 0;
     };
     auto run_units = [&](int P) {
-        const int units = P == 0 ? units_d : units_e;
-        int cur = -1, cur_meta = 0, cur_u0 = 0, cur_n = 0;
-        const LyStack* CS = nullptr;
-        for (int u = warp; u < units; u += kM8Warps) {
-            int i, meta, s;
-            const LyStack* S;
-            int u0, nst;
-            if (P == 0) {
-                i = job_of_d(u);
-                meta = __shfl_sync(0xffffffffu, md, i);
-                u0 = __shfl_sync(0xffffffffu, ud, i);
-                S = &A.d[meta & 3];
-                nst = S->stages;
-            } else {
-                i = u / SE.stages;
-                meta = __shfl_sync(0xffffffffu, me, i);
-                u0 = i * SE.stages;
-                S = &SE;
-                nst = SE.stages;
+        const int n = P == 0 ? n_d : n_e;
+        for (UnitWalk w = walk_start(P, warp); w.p < n; walk_next(P, w)) {
+            const Unit u = walk_unit(P, w);
+            if (u.job != open_job[u.kind]) {
+                flush(P, u.kind);
+                open_job[u.kind] = u.job;
             }
-            s = u - u0;
-            if (i != cur) {
-                if (cur >= 0) flush(cur, *CS, cur_meta, cur_u0, cur_n);
-                cur = i;
-                cur_meta = meta;
-                cur_u0 = u0;
-                cur_n = nst;
-                CS = S;
-            }
+            ++open_units[u.kind];
             // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
             __syncwarp();
-            if (c_unit < units_d + units_e) issue();
+            if (cursor_ready()) issue();
             const int cs = slot;
             if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cs], phase, kM8WaitLimit));
             ++consumed;
@@ -422,42 +438,45 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
                 slot = 0;
                 phase ^= 1;
             }
+            const int meta = __shfl_sync(0xffffffffu, P == 0 ? md : me, u.job);
             if (!ok || !((meta >> 6) & 1)) continue;
-            // the unit's activation row in the split area: the token (D), or the pair's row (E: the first or
-            // second routed pair of this CTA's range, or the shared row)
-            const int cols = S->stages * S->stage_cols;
-            const int lrow = P == 0 ? 0 : (S->routed ? ((meta >> 7) & 63) - cj0 / S->tiles : 0);
-            const uint8_t* xh = reinterpret_cast<const uint8_t*>(xsplit) + int64_t(lrow) * cols;
-            const uint8_t* xl = xh + (P == 0 ? H : A.split_bytes / 2);
-            const float* xsc = xscale + lrow * (cols / kM8XBlock);
-            const int pos = ((meta >> 2) & 15) * static_cast<int>(S->row_bytes) + s * S->stage_bytes;
-            const int xc = s * S->stage_cols;
+            const LyStack& S = P == 0 ? A.d[meta & 3] : A.e[meta & 3];
+            // the unit's activation row in the split area: the token (D); in E the CTA's routed pair's row, or
+            // the shared row after it
+            const int xoff = P == 0 ? 0 : (u.kind == 0 ? 0 : ER.stages * ER.stage_cols);
+            const int soff = P == 0 ? 0 : (u.kind == 0 ? 0 : ER.stages * ER.stage_cols / kM8XBlock);
+            const uint8_t* xh = reinterpret_cast<const uint8_t*>(xsplit) + xoff;
+            const uint8_t* xl = xh + A.split_bytes / 2;
+            const float* xsc = xscale + soff;
+            const int pos = ((meta >> 2) & 15) * static_cast<int>(S.row_bytes) + u.stage * S.stage_bytes;
+            const int xc = u.stage * S.stage_cols;
             const uint8_t* st = my_ring + cs * slot_bytes + (pos & 15);
-            if (S->kind == M8IQ3S<2>::kKind)
+            if (S.kind == M8IQ3S<2>::kKind)
                 M8IQ3S<2, kLyRep>::stage(st + gid * M8IQ3S<2>::kRS, st + (gid + 8) * M8IQ3S<2>::kRS, tig, gid, lut,
-                                         xh + xc, xl + xc, xsc + xc / kM8XBlock, total);
+                                         xh + xc, xl + xc, xsc + xc / kM8XBlock, tot[u.kind]);
             else
                 M8Q8_0::stage(st + gid * M8Q8_0::kRS, st + (gid + 8) * M8Q8_0::kRS, tig, gid, lut, xh + xc, xl + xc,
-                              xsc + xc / kM8XBlock, total);
+                              xsc + xc / kM8XBlock, tot[u.kind]);
         }
-        if (cur >= 0) flush(cur, *CS, cur_meta, cur_u0, cur_n);
+        flush(P, 0);
+        flush(P, 1);
     };
     run_units(0);
     ok = grid_sync(A.bar, base + 2ull * G, A.err, flag) && ok;
 
-    // ---- E: the split of this CTA's SwiGLU rows (one or two routed pairs, or the shared row), then its units
+    // ---- E: the split of this CTA's SwiGLU rows (its routed pair's, then the shared one), then its units
     {
-        if (threadIdx.x < kLySlots) tag[threadIdx.x] = threadIdx.x;  // (every phase-D job was added up)
-        const LySource& X = A.src_e[eg];
-        const int xblocks = X.cols / kM8XBlock;
-        const int p0 = SE.routed ? cj0 / SE.tiles : 0;
-        const int p1 = SE.routed ? min((cj1 - 1) / SE.tiles, X.rows - 1) : 0;
-        const int nrows = cj1 > cj0 ? p1 - p0 + 1 : 0;
-        for (int blk = warp; blk < nrows * xblocks; blk += kM8Warps) {
-            const int lr = blk / xblocks, c = blk - lr * xblocks;
-            const int64_t at = int64_t(p0 + lr) * X.cols + int64_t(c) * kM8XBlock + 8 * lane;
-            const int64_t lat = int64_t(lr) * X.cols + int64_t(c) * kM8XBlock + 8 * lane;
-            ly_split_glu(X.gate, X.up, at, xsplit + lat, xsplit + A.split_bytes / 2 + lat, xscale + blk, lane);
+        const int xb_r = ER.stages * ER.stage_cols / kM8XBlock;  // blocks of a routed row
+        const int xb_s = ES.stages * ES.stage_cols / kM8XBlock;
+        const int nr = ja_e > 0 ? xb_r : 0, nsb = jb_e > 0 ? xb_s : 0;
+        for (int blk = warp; blk < nr + nsb; blk += kM8Warps) {
+            const bool routed = blk < nr;
+            const LySource& X = A.src_e[routed ? 0 : 1];
+            const int c = routed ? blk : blk - nr;
+            const int64_t at = int64_t(routed ? epair : 0) * X.cols + int64_t(c) * kM8XBlock + 8 * lane;
+            const int lat = (routed ? 0 : xb_r * kM8XBlock) + c * kM8XBlock + 8 * lane;
+            ly_split_glu(X.gate, X.up, at, xsplit + lat, xsplit + A.split_bytes / 2 + lat,
+                         xscale + (routed ? c : xb_r + c), lane);
         }
         __syncthreads();
     }
@@ -610,29 +629,24 @@ extern "C" int smoe_decode_layer(const SmoeDecodeLayer* L, const void* x, void* 
     A.src_e[0] = LySource{nullptr, g_r, u_r, kk, static_cast<int>(F)};
     A.src_e[1] = LySource{nullptr, gs, us, 1, static_cast<int>(FS)};
 
-    // phase D: jobs round-robin over the CTAs, at most 32 a CTA
-    SMOE_REQUIRE(jobs <= 32 * int64_t(G), SMOE_ESHAPE, "decode_layer: too many gate / up jobs");
-    // phase E: CTAs in proportion to the two down stacks' decode cost (an IQ3_S byte about 2.5 times a Q8_0 one)
-    {
-        const double cr = double(A.e[0].jobs) * A.e[0].stages * A.e[0].stage_bytes * 5;
-        const double cs = double(A.e[1].jobs) * A.e[1].stages * A.e[1].stage_bytes * 2;
-        A.gr = std::min(G - 1, std::max(1, static_cast<int>(G * cr / (cr + cs) + 0.5)));
-        for (int g = 0; g < 2; ++g) {
-            const LyStack& S = A.e[g];
-            const int gsz = g == 0 ? A.gr : G - A.gr;
-            const int64_t per = (S.jobs + gsz - 1) / gsz;  // jobs of the busiest CTA
-            SMOE_REQUIRE(per <= 32, SMOE_ESHAPE, "decode_layer: too many down jobs");
-            // a routed CTA's range must span at most two pairs (its split holds two rows)
-            if (g == 0) SMOE_REQUIRE(per <= S.tiles, SMOE_ESHAPE, "decode_layer: too few CTAs for the routed down");
-        }
+    // every CTA's jobs of a phase within its kLySlots partial-sum slots: phase D round-robin; phase E its tiles
+    // of one routed pair (the CTAs split the pairs evenly) and its share of the shared down's jobs
+    SMOE_REQUIRE(jobs <= int64_t(kLySlots) * G, SMOE_ESHAPE, "decode_layer: too many gate / up jobs");
+    SMOE_REQUIRE(G >= K, SMOE_ESHAPE, "decode_layer: fewer SMs than routed experts");
+    for (int b = 0; b < G; ++b) {
+        const int p = static_cast<int>(int64_t(b) * K / G);
+        const int c0 = static_cast<int>((int64_t(p) * G + K - 1) / K), c1 = static_cast<int>((int64_t(p + 1) * G + K - 1) / K);
+        const int64_t rt = int64_t(b - c0 + 1) * A.e[0].tiles / (c1 - c0) - int64_t(b - c0) * A.e[0].tiles / (c1 - c0);
+        const int64_t st_ = int64_t(b + 1) * A.e[1].jobs / G - int64_t(b) * A.e[1].jobs / G;
+        SMOE_REQUIRE(rt + st_ <= kLySlots, SMOE_ESHAPE, "decode_layer: too many down jobs for a CTA");
     }
-    // shared memory: the split area holds the token (D) or a CTA's SwiGLU rows (E: two routed rows, or the
+    SMOE_REQUIRE((F + FS) / 256 <= 64 && H / 256 <= 64, SMOE_ESHAPE, "decode_layer: activation scales");
+    // shared memory: the split area holds the token (D) or a CTA's SwiGLU rows (E: its routed pair's and the
     // shared one)
-    const int64_t split_d = 2 * H, split_e = std::max<int64_t>(2 * 2 * F, 2 * FS);
-    A.split_bytes = static_cast<int>((std::max(split_d, split_e) + 127) & ~int64_t(127));
+    A.split_bytes = static_cast<int>((2 * std::max<int64_t>(H, F + FS) + 127) & ~int64_t(127));
     A.slot_bytes = 16 * std::max(M8IQ3S<2>::kRS, M8Q8_0::kRS);
-    const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + size_t(kLySlots) * kM8Warps * 16 * 4 + 2 * kLySlots * 4 +
-                         16 * 4 + kLyMaxK * 8 + 32 * 4 + 512 * kLyRep * 4 + 128 * 4 + size_t(A.split_bytes);
+    const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + size_t(kLySlots) * kM8Warps * 16 * 4 + 32 * 4 + 16 * 4 +
+                         kLyMaxK * 8 + 32 * 4 + 512 * kLyRep * 4 + 64 * 4 + size_t(A.split_bytes);
     const size_t slot = size_t(kM8Warps) * A.slot_bytes;
     int ns = kM8MaxSlots;
     while (ns > 2 && fixed + ns * slot > size_t(227 * 1024 - 256)) --ns;

@@ -81,8 +81,9 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     uint8_t* ring = sm;                                                         // [warp][slot] 16 rows x kRS
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * kSlot);  // [warp][slot]
     float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);       // [16 warps][16 rows]
-    M8WhereS* where_ring = reinterpret_cast<M8WhereS*>(red + kM8Warps * 16);       // [16 warps][4]
-    uint32_t* lut = reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(where_ring) + kM8WhereSBytes);  // 512 x 16 words
+    uint8_t* spare = reinterpret_cast<uint8_t*>(red + kM8Warps * 16);           // kM8WhereSBytes
+    uint32_t* need = reinterpret_cast<uint32_t*>(spare + kM8WhereSBytes - kM8SMaskRows / 8);  // kM8SMaskRows bits
+    uint32_t* lut = reinterpret_cast<uint32_t*>(spare + kM8WhereSBytes);        // 512 x 16 words
     const int xblocks = static_cast<int>(a.cols / kM8XBlock);
     float* xscale = reinterpret_cast<float*>(lut + (D::kLut ? 8192 : 0));        // [xrows][xblocks]
     int8_t* xhi = reinterpret_cast<int8_t*>(xscale + ((a.xrows * xblocks + 3) & ~3));  // [xrows][cols]
@@ -96,13 +97,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     const int S = static_cast<int>(a.cols / D::kStageCols);
     const int my_stages = S > kq ? (S - kq + team - 1) / team : 0;
     // CTA b takes the jobs [b J / G, (b + 1) J / G) (neighbouring tiles, so few activation rows); its team i
-    // takes every teams-th of them from the i-th on
+    // takes every teams-th of them from the i-th on (at most 32: one per lane of the warp's job table)
     const int cj0 = static_cast<int>(int64_t(blockIdx.x) * a.jobs / gridDim.x);
     const int cj1 = static_cast<int>(int64_t(blockIdx.x + 1) * a.jobs / gridDim.x);
-    const int nteams = teams;
     const int q0 = cj0 + tid_team;
-    const int my_jobs = q0 < cj1 ? (cj1 - q0 + teams - 1) / teams : 0;
-    const int items = my_jobs * my_stages;
+    const int my_jobs = q0 < cj1 ? min((cj1 - q0 + teams - 1) / teams, 32) : 0;
     const int per_prob = static_cast<int>(a.pairs) * a.tiles;  // < 2^30 (the host checks)
     uint8_t* my_ring = ring + size_t(warp) * ns * kSlot;
     uint64_t* my_bars = bars + warp * kM8MaxSlots;
@@ -111,125 +110,93 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         for (int i = 0; i < ns; ++i) tc::mbar_init(&my_bars[i], 1);
         tc::fence_barrier_init();
     }
-    __syncwarp();
+    const bool masked = a.xrows <= kM8SMaskRows;
+    for (int i = threadIdx.x; i < kM8SMaskRows / 32; i += kM8Threads) need[i] = 0u;
     // the codebook fills while the kernel before this one finishes; so do the first weight copies and the
     // activation split when their inputs are older than that kernel (a.early); the rest waits for it
     if constexpr (D::kLut) m8_fill_grid(lut);
     const bool early_idx = a.early & 1, early_x = (a.early >> 1) & 1;
-    if (!early_idx) pdl_wait();
 
-    using Where = M8WhereS;
-    auto locate = [&](int job) {
-        const int j = q0 + job * nteams;
-        Where w;
-        w.prob = j / per_prob;
-        const int rest = j - w.prob * per_prob;
-        w.pair = rest / a.tiles;
-        const int tile = rest - w.pair * a.tiles;
-        w.cls = tile & (a.q - 1);
-        w.blk = tile >> a.lq;
-        w.e = a.idx[w.pair];
-        w.y = static_cast<int>((int64_t(w.e < a.experts ? w.e : 0) * a.rows) >> a.lq) + 16 * w.blk;
-        w.xr = w.pair / static_cast<int>(a.share);
-        return w;
-    };
-    // the copy cursor (lane 0): the next item to copy and its job, stage and slot. The cursor works out each
-    // job's place (its expert index is a global load) and leaves it in the warp's ring of 4 places, where the
-    // warp picks it up when it starts the job: the cursor runs at most 3 items, so at most 3 jobs, ahead.
-    Where* my_where = where_ring + warp * 4;
-    int pre_job = 0, pre_k = 0, pre_slot = 0, pre_s = kq;
-    Where pre_w{};
-    if (lane == 0 && my_jobs > 0 && my_stages > 0) {
-        pre_w = locate(0);
-        my_where[0] = pre_w;
+    // lane l's job (the warp's l-th): problem, pair, tile (residue class and block); its expert and the first
+    // row of its TMA box once the indices may be read. A job's activation row is its pair's / share.
+    int j_prob = 0, j_pair = 0, j_cls = 0, j_blk = 0, j_y = 0, j_valid = 0;
+    const bool has = lane < my_jobs;
+    if (has) {
+        const int j = q0 + lane * teams;
+        j_prob = j / per_prob;
+        const int rest = j - j_prob * per_prob;
+        j_pair = rest / a.tiles;
+        const int tile = rest - j_pair * a.tiles;
+        j_cls = tile & (a.q - 1);
+        j_blk = tile >> a.lq;
     }
-    // lane 0 starts the TMA copy of the cursor's item into its slot and moves the cursor on; a pair naming no
-    // expert copies nothing and completes the slot's phase with a plain arrive, so every item takes one phase
+    auto place = [&]() {
+        if (has) {
+            const uint32_t e = __ldg(a.idx + j_pair);
+            j_valid = e < a.experts ? 1 : 0;
+            j_y = static_cast<int>((int64_t(j_valid ? e : 0) * a.rows) >> a.lq) + 16 * j_blk;
+        }
+    };
+    __syncthreads();
+    if (masked && has && my_stages > 0) {
+        const int xr = j_pair / static_cast<int>(a.share);
+        atomicOr(&need[xr >> 5], 1u << (xr & 31));
+    }
+    __syncthreads();
+
+    // the copy cursor (warp-uniform): the next item's job, stage, slot, byte position in the row
+    int i_job = 0, i_k = 0, i_slot = 0, i_pos = 0, i_y = 0, i_map = 0, i_valid = 0, issued = 0;
+    auto seek = [&](int job) {
+        i_job = job;
+        i_k = 0;
+        if (job >= my_jobs || my_stages == 0) {
+            i_job = my_jobs;
+            return;
+        }
+        i_map = __shfl_sync(0xffffffffu, j_prob, job);
+        i_pos = __shfl_sync(0xffffffffu, j_cls, job) * static_cast<int>(a.row_bytes) + kq * D::kStageBytes;
+        i_y = __shfl_sync(0xffffffffu, j_y, job);
+        i_valid = __shfl_sync(0xffffffffu, j_valid, job);
+    };
+    // issue the cursor's item (a pair naming no expert copies nothing and completes the slot's phase with a
+    // plain arrive, so every item takes one phase) and move on
     auto issue = [&]() {
-        if (pre_w.e >= a.experts) {
-            tc::mbar_arrive(&my_bars[pre_slot]);
-        } else {
-            const int xb = (pre_w.cls * static_cast<int>(a.row_bytes) + pre_s * D::kStageBytes) & ~15;
-            tc::fence_proxy_async_smem();
-            tc::mbar_arrive_expect_tx(&my_bars[pre_slot], static_cast<uint32_t>(kSlot));
-            tc::tma_load_2d(smem_addr(my_ring + pre_slot * kSlot), pre_w.prob ? &maps.w[1] : &maps.w[0], xb >> 2,
-                            pre_w.y, &my_bars[pre_slot]);
-        }
-        if (++pre_slot == ns) pre_slot = 0;
-        pre_s += team;
-        if (++pre_k == my_stages) {
-            pre_k = 0;
-            pre_s = kq;
-            if (++pre_job < my_jobs) {
-                pre_w = locate(pre_job);
-                my_where[pre_job & 3] = pre_w;
+        if (lane == 0) {
+            if (i_valid) {
+                tc::mbar_arrive_expect_tx(&my_bars[i_slot], static_cast<uint32_t>(kSlot));
+                tc::tma_load_2d(smem_addr(my_ring + i_slot * kSlot), &maps.w[i_map], (i_pos & ~15) >> 2, i_y,
+                                &my_bars[i_slot]);
+            } else {
+                tc::mbar_arrive(&my_bars[i_slot]);
             }
+        }
+        ++issued;
+        if (++i_slot == ns) i_slot = 0;
+        i_pos += team * D::kStageBytes;
+        if (++i_k == my_stages) seek(i_job + 1);
+    };
+    // the activations, split per 256-column block into int8 hi and lo: a warp per block, 8 values a lane
+    auto split = [&]() {
+        for (int blk = warp; blk < a.xrows * xblocks; blk += kM8Warps) {
+            const int xr = blk / xblocks, b = blk % xblocks;
+            if (masked && !((need[xr >> 5] >> (xr & 31)) & 1u)) continue;
+            const int64_t at = int64_t(xr) * a.cols + int64_t(b) * kM8XBlock + 8 * lane;
+            m8_split(a.x, a.gate, a.up, at, xhi + at, xlo + at, xscale + blk, lane);
         }
     };
-    if (lane == 0)
-        for (int i = 0; i < ns - 1 && i < items; ++i) issue();
-
-    // the activation rows this CTA's jobs read (all of them when there are more than kM8SMaskRows): a job's row
-    // is its pair's, pair / share, known without the expert index
-    uint32_t* need = reinterpret_cast<uint32_t*>(where_ring + kM8Warps * 4);  // kM8SMaskRows bits
-    const bool masked = a.xrows <= kM8SMaskRows;
-    if (masked) {
-        for (int i = threadIdx.x; i < kM8SMaskRows / 32; i += kM8Threads) need[i] = 0u;
-        __syncthreads();
-        if (lane == 0 && my_stages > 0)
-            for (int job = 0; job < my_jobs; ++job) {
-                const int j = q0 + job * nteams;
-                const int pair = (j - (j / per_prob) * per_prob) / a.tiles;
-                const int xr = pair / static_cast<int>(a.share);
-                atomicOr(&need[xr >> 5], 1u << (xr & 31));
-            }
-        __syncthreads();
+    if (early_idx) {
+        place();
+        seek(0);
+        while (i_job < my_jobs && issued < ns - 1) issue();
     }
-    if (early_idx && !early_x) pdl_wait();
-    // the activations, split per 256-column block into int8 hi and lo: a warp per block, 8 values a lane
-    for (int blk = warp; blk < a.xrows * xblocks; blk += kM8Warps) {
-        const int xr = blk / xblocks, b = blk % xblocks;
-        if (masked && !((need[xr >> 5] >> (xr & 31)) & 1u)) continue;
-        const int64_t c0 = int64_t(b) * kM8XBlock + 8 * lane;
-        float v[8];
-        if (a.gate) {
-            // the SwiGLU of the gate and up products, the same function (so the same float16 bits) as the
-            // separate kernel
-            const uint4 gr = *reinterpret_cast<const uint4*>(a.gate + int64_t(xr) * a.cols + c0);
-            const uint4 ur = *reinterpret_cast<const uint4*>(a.up + int64_t(xr) * a.cols + c0);
-            const __half* gh = reinterpret_cast<const __half*>(&gr);
-            const __half* uh = reinterpret_cast<const __half*>(&ur);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __half2float(swiglu_one(gh[i], uh[i]));
-        } else {
-            const uint4 raw = *reinterpret_cast<const uint4*>(a.x + int64_t(xr) * a.cols + c0);
-            const __half2* h2 = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 f = __half22float2(h2[i]);
-                v[2 * i] = f.x;
-                v[2 * i + 1] = f.y;
-            }
-        }
-        float amax = 0.f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        const float s = amax / 127.0f, inv = amax > 0.f ? 127.0f / amax : 0.f;
-        uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float hf = fminf(fmaxf(rintf(v[i] * inv), -127.f), 127.f);
-            const float lf = fminf(fmaxf(rintf((v[i] - hf * s) * (128.0f * inv)), -127.f), 127.f);
-            hw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(hf)) & 255u) << (8 * (i & 3));
-            lw[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(lf)) & 255u) << (8 * (i & 3));
-        }
-        *reinterpret_cast<uint2*>(xhi + int64_t(xr) * a.cols + c0) = make_uint2(hw[0], hw[1]);
-        *reinterpret_cast<uint2*>(xlo + int64_t(xr) * a.cols + c0) = make_uint2(lw[0], lw[1]);
-        if (lane == 0) xscale[blk] = s;
+    if (early_x) split();
+    pdl_wait();  // (from here on every input may be read and outputs written)
+    if (!early_idx) {
+        place();
+        seek(0);
+        while (i_job < my_jobs && issued < ns - 1) issue();
     }
-    if (early_idx && early_x) pdl_wait();  // (every path has waited once from here on: outputs, the combine)
+    if (!early_x) split();
     __syncthreads();
 
     // a team of one warp needs no named barrier (there are 16, barrier 0 is __syncthreads')
@@ -241,30 +208,33 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     // with its team's barriers
     bool ok = true;
     float total[2] = {0.f, 0.f};
-    int it = 0, slot = 0;
+    int slot = 0, consumed = 0;
     uint32_t phase = 0;
     for (int job = 0; job < my_jobs; ++job) {
-        const Where w = my_stages > 0 ? my_where[job & 3] : locate(job);
-        const uint8_t* xh = reinterpret_cast<const uint8_t*>(xhi) + int64_t(w.xr) * a.cols;
-        const uint8_t* xl = reinterpret_cast<const uint8_t*>(xlo) + int64_t(w.xr) * a.cols;
-        const float* xsc = xscale + w.xr * xblocks;
-        int s = kq;
-        for (int k = 0; k < my_stages; ++k, ++it, s += team) {
+        const int prob = __shfl_sync(0xffffffffu, j_prob, job);
+        const int pair = __shfl_sync(0xffffffffu, j_pair, job);
+        const int cls = __shfl_sync(0xffffffffu, j_cls, job);
+        const int blk = __shfl_sync(0xffffffffu, j_blk, job);
+        const int valid = __shfl_sync(0xffffffffu, j_valid, job);
+        const int xr = pair / static_cast<int>(a.share);
+        const uint8_t* xh = reinterpret_cast<const uint8_t*>(xhi) + int64_t(xr) * a.cols;
+        const uint8_t* xl = reinterpret_cast<const uint8_t*>(xlo) + int64_t(xr) * a.cols;
+        const float* xsc = xscale + xr * xblocks;
+        int pos = cls * static_cast<int>(a.row_bytes) + kq * D::kStageBytes;
+        int xc = kq * D::kStageCols;
+        for (int k = 0; k < my_stages; ++k, pos += team * D::kStageBytes, xc += team * D::kStageCols) {
             // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
-            if (it + ns - 1 < items) {
-                __syncwarp();
-                if (lane == 0) issue();
-            }
+            __syncwarp();
+            if (i_job < my_jobs) issue();
             const int cur = slot;
             if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, kM8WaitLimit));
+            ++consumed;
             if (++slot == ns) {
                 slot = 0;
                 phase ^= 1;
             }
-            if (!ok || w.e >= a.experts) continue;
-            const int off = (w.cls * static_cast<int>(a.row_bytes) + s * D::kStageBytes) & 15;
-            const uint8_t* st = my_ring + cur * kSlot + off;
-            const int xc = s * D::kStageCols;
+            if (!ok || !valid) continue;
+            const uint8_t* st = my_ring + cur * kSlot + (pos & 15);
             D::stage(st + gid * D::kRS, st + (gid + 8) * D::kRS, tig, gid, lut, xh + xc, xl + xc,
                      xsc + xc / kM8XBlock, total);
         }
@@ -277,15 +247,15 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         total[0] = total[1] = 0.f;
         team_sync();
         if (kq == 0 && lane < 16) {
-            const int64_t row = int64_t(w.blk) * 16 * a.q + w.cls + int64_t(a.q) * lane;
-            if (w.e < a.experts && row < a.rows) {
+            const int64_t row = int64_t(blk) * 16 * a.q + cls + int64_t(a.q) * lane;
+            if (valid && row < a.rows) {
                 float v = rq[lane];
                 for (int i = 1; i < team; ++i) v += rq[16 * i + lane];
                 const __half prod = __float2half_rn(v);
-                __half* o = (w.prob ? a.out[1] : a.out[0]) + int64_t(w.pair) * a.rows + row;
+                __half* o = (prob ? a.out[1] : a.out[0]) + int64_t(pair) * a.rows + row;
                 if (a.cy == nullptr) *o = prod;
-                else *o = combine_one(a.cy + int64_t(w.pair) * a.ck * a.rows + row, a.rows, a.cw + int64_t(w.pair) * a.ck,
-                                      a.ck, a.cg[w.pair], prod);
+                else *o = combine_one(a.cy + int64_t(pair) * a.ck * a.rows + row, a.rows, a.cw + int64_t(pair) * a.ck,
+                                      a.ck, a.cg[pair], prod);
             }
         }
         team_sync();
@@ -296,7 +266,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
     // a wait gave up)
     if (!ok && lane == 0)
-        for (int i = 0; i < items; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
+        for (int i = consumed; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
     __syncwarp();
 }
 
@@ -659,12 +629,14 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         for (int t = 1; t <= kM8Warps; t *= 2) {
             const int64_t teams = kM8Warps / t;
             const int64_t most = ((jobs + G - 1) / G + teams - 1) / teams;  // jobs of the busiest team
+            if (most > 32) continue;  // (a warp's job table holds 32)
             const int64_t span = most * (4 * ((S + t - 1) / t) + (t > 1 ? 3 : 0));
             if (best < 0 || span < best) {
                 best = span;
                 team = t;
             }
         }
+        if (best < 0) return 1;
         a.team = team;
         const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
         const size_t smem = fixed + ns * slot;

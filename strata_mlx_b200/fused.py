@@ -84,7 +84,7 @@ def top_k_softmax(logits: torch.Tensor, k: int):
 
 _COUNTERS = {}
 
-LAYER_KERNEL = True  # one launch per one-token step where the layer's types and shapes allow (smoe_decode_layer)
+LAYER_KERNEL = False  # one launch per one-token step (smoe_decode_layer) where the types and shapes allow it
 _LAYER_SCRATCH = {}
 
 

@@ -19,6 +19,12 @@ from strata_mlx_b200 import fused as F  # noqa: E402
 from test_moe_gpu import build_block, dev, make_layer, rel_l2  # noqa: E402
 
 
+@pytest.fixture(autouse=True)
+def layer_kernel_on(monkeypatch):
+    """These tests run SparseMoeBlock through the one-launch step (off by default)."""
+    monkeypatch.setattr(F, "LAYER_KERNEL", True)
+
+
 def four_launches(block, x, monkeypatch):
     """block(x) through route / batched gate-up / down / down+combine, and the route's outputs."""
     with monkeypatch.context() as m:
