@@ -37,8 +37,8 @@ __device__ __forceinline__ float h2f(uint32_t bits) {
 // A group's four weights are the grid word of its 9-bit index (qs byte | qh bit << 8) with the group's four
 // signs applied. The grid (512 words) sits in shared memory REP times over, word i * REP + lane % REP, so a
 // warp's 32 random lookups meet at most 32 / REP to a bank. Every grid value is odd, so negating a byte is xor with
-// 0xFE: four sign bits become four 0x00 / 0xFF bytes by one multiply (each bit to the top of its byte) and a
-// sign-replicating byte permute.
+// 0xFE: a sign byte's bits (two groups') become 0x00 / 0xFF bytes by one multiply per group (each bit to
+// the top of a byte) and a sign-replicating byte permute.
 
 template <int O>
 __device__ __forceinline__ uint32_t ld_s16(uint32_t a) {
@@ -87,8 +87,10 @@ struct M8IQ3S {
             const uint32_t z = __byte_perm(q2, 0u, 0x4140) | ((h * 0x00800100u) & 0x01000100u);
             const uint32_t ga = ld_s32(lutl + (z & 0x1ffu) * (4 * REP));
             const uint32_t gb = ld_s32(lutl + (z >> 16) * (4 * REP));
-            const uint32_t ma = prmt_sr((sb & 0x0Fu) * 0x10204080u, 0xBA98u);
-            const uint32_t mb = prmt_sr((sb & 0xF0u) * 0x01020408u, 0xBA98u);
+            // sign masks: each of the byte's 8 bits moved to the top of a byte by one multiply (copies of sb at
+            // 9-bit strides never overlap), bytes reordered and their top bits replicated by one permute
+            const uint32_t ma = prmt_sr(sb * 0x80402010u, 0x89ABu);  // bits 0..3 (group 2 tig)
+            const uint32_t mb = prmt_sr(sb * 0x08040201u, 0x89ABu);  // bits 4..7 (group 2 tig + 1)
             a[j][0] = ga ^ (ma & 0xFEFEFEFEu);
             a[j][1] = gb ^ (mb & 0xFEFEFEFEu);
         }
