@@ -91,8 +91,11 @@ SMOE_API int smoe_matvec_glu(int kind, const uint8_t* blocks, int64_t experts, i
 /* Several products of the decode path in one launch (the routed experts' gate and up with the shared
  * expert's gate and up; or the two down products): each problem is an smoe_matvec (x set, gate and up null)
  * or an smoe_matvec_glu (x null, gate and up set; share is then 1). Problems that name the same activations
- * read them once. All n problems are done when the call returns to the stream, in one int8 tensor-core launch
- * when it takes all of them (float16 activations, IQ3_S / Q8_0, n <= 4), else one launch per problem.
+ * read them once. All problems are done when the call returns to the stream, in one int8 tensor-core launch
+ * when it takes all of them (float16 activations, IQ3_S / Q8_0, at most 4), else one launch per problem.
+ * A problem with out, x, gate and up all null is not computed: it names weights a later launch reads (the
+ * blocks of experts idx[0 .. pairs) of its stack), which the one launch fetches into L2 while it streams its
+ * own (at most two such; a hint, dropped when the batch is not one launch).
  * No single reference counterpart: it batches the calls of `_Routed.__call__` (strata_mlx/fused.py:492-494)
  * that do not depend on one another. */
 typedef struct SmoeMatvec {

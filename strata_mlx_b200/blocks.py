@@ -228,6 +228,7 @@ MMA_MATVEC = {"IQ3_S": 256, "Q8_0": 128}
 FUSED_GLU = ("IQ3_S", "Q8_0")
 FUSED_GLU_COLS, FUSED_GLU_BYTES = 256, 64 << 10
 BATCHED_DOWN = False  # decode_products: the routed and the shared down product in one launch
+PREFETCH_DOWN = False  # decode_products: the down stacks' experts fetched into L2 by the gate/up launch (measured slower)
 
 
 def matvec_glu(lin, idx: torch.Tensor, gate: torch.Tensor, up: torch.Tensor):
@@ -300,10 +301,12 @@ def switch_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.
 
 
 def _problem(lin, idx, pairs, share, out, x=None, gate=None, up=None):
+    """One smoe_matvec_batch problem; out None names lin's experts idx[:pairs] for an L2 prefetch."""
     return _lib.SmoeMatvec(_kind(lin.kind), lin.blocks.data_ptr(), lin.num_experts, lin.output_dims, lin.input_dims,
                            idx.data_ptr(), pairs, share, x.data_ptr() if x is not None else None,
                            gate.data_ptr() if gate is not None else None, up.data_ptr() if up is not None else None,
-                           out.data_ptr(), _lib.dtype_code(out.dtype))
+                           out.data_ptr() if out is not None else None,
+                           _lib.dtype_code(out.dtype if out is not None else torch.float16))
 
 
 def matvec_batch(problems) -> None:
@@ -340,8 +343,10 @@ def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, 
     gs = torch.empty((tokens, sg.output_dims), dtype=dt, device=dev)
     us = torch.empty((tokens, su.output_dims), dtype=dt, device=dev)
     if pairs:
+        # with the two down stacks' weights fetched into L2 meanwhile (the gate/up launch is compute-bound)
+        ahead = [_problem(down, idx, pairs, 1, None), _problem(sd, zeros, tokens, 1, None)] if PREFETCH_DOWN else []
         matvec_batch([_problem(gate, idx, pairs, k, g_r, x=x2), _problem(up, idx, pairs, k, u_r, x=x2),
-                      _problem(sg, zeros, tokens, 1, gs, x=x2), _problem(su, zeros, tokens, 1, us, x=x2)])
+                      _problem(sg, zeros, tokens, 1, gs, x=x2), _problem(su, zeros, tokens, 1, us, x=x2)] + ahead)
     if BATCHED_DOWN and sd.kind in FUSED_GLU and down.kind in FUSED_GLU:
         # both down products in one launch (the shared expert's Q8_0 rows and the routed experts' in the same
         # CTAs, so the SMs stream one while they decode the other); the combine is its own launch

@@ -19,8 +19,19 @@ struct M8Spec {
     __half* out;
 };
 
-// n <= 4 problems in one launch: 0 launched, 1 not taken (the caller runs them another way), else an error.
-int mv8_batch(int n, const M8Spec* specs, cudaStream_t st);
+// A later launch's weights to fetch into L2 meanwhile: the blocks of experts idx[0 .. pairs) of a stack whose
+// experts are expert_bytes apart.
+struct M8Pref {
+    const uint8_t* blocks;
+    int64_t expert_bytes;
+    const uint32_t* idx;
+    int pairs;
+    uint32_t experts;
+};
+
+// n <= 4 problems in one launch (and up to two stacks' weights fetched into L2 for later launches): 0 launched,
+// 1 not taken (the caller runs them another way), else an error.
+int mv8_batch(int n, const M8Spec* specs, cudaStream_t st, int npf = 0, const M8Pref* pf = nullptr);
 
 // the gate / up problems (nprob 1 or 2) of one stack pair: 0 launched, 1 not taken, else an error
 int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,

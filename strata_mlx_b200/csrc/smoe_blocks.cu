@@ -250,12 +250,23 @@ extern "C" int smoe_matvec_batch(int n, const SmoeMatvec* pr, void* stream) {
     SMOE_REQUIRE(pr != nullptr, SMOE_EARG, "null problem list");
     // every problem checked as its own entry point checks it, before any launch
     M8Spec spec[4];
-    int m = 0;
-    bool one_launch = n <= 4;
+    M8Pref pref[2];
+    int m = 0, npf = 0, ncomp = 0;
+    for (int i = 0; i < n; ++i) ncomp += pr[i].out != nullptr ? 1 : 0;
+    bool one_launch = ncomp <= 4;
     for (int i = 0; i < n; ++i) {
         const SmoeMatvec& p = pr[i];
         int per, bytes;
         if (int s = check_stack(p.kind, p.experts, p.rows, p.cols, per, bytes)) return s;
+        if (p.out == nullptr) {
+            // a prefetch: the experts' blocks named by idx, fetched into L2 for a later launch
+            SMOE_REQUIRE(p.x == nullptr && p.gate == nullptr && p.up == nullptr, SMOE_EARG,
+                         "a problem without out has no activations (it names weights to fetch ahead)");
+            if (p.pairs > 0 && p.blocks && p.idx && npf < 2 && p.pairs < (int64_t(1) << 30))
+                pref[npf++] = M8Pref{p.blocks, p.rows * (p.cols / per * bytes), p.idx, static_cast<int>(p.pairs),
+                                     static_cast<uint32_t>(std::min<int64_t>(p.experts, 0xffffffffLL))};
+            continue;
+        }
         SMOE_REQUIRE(p.pairs >= 0, SMOE_EARG, "negative pair count");
         SMOE_REQUIRE((p.x != nullptr) != (p.gate != nullptr && p.up != nullptr), SMOE_EARG,
                      "a problem has x, or gate and up");
@@ -272,14 +283,15 @@ extern "C" int smoe_matvec_batch(int n, const SmoeMatvec* pr, void* stream) {
     cudaStream_t st = as_stream(stream);
     if (one_launch && m > 0) {
         const M8Spec& a = spec[0];
-        const int r = m == 1 ? mv8_try(a.kind, a.kind, a.blocks, a.blocks, a.experts, a.rows, a.cols, a.row_bytes, a.idx,
-                                       a.pairs, a.share, a.x, a.gate, a.up, a.out, a.out, 1, st)
-                             : mv8_batch(m, spec, st);
+        const int r = m == 1 && npf == 0
+                          ? mv8_try(a.kind, a.kind, a.blocks, a.blocks, a.experts, a.rows, a.cols, a.row_bytes, a.idx,
+                                    a.pairs, a.share, a.x, a.gate, a.up, a.out, a.out, 1, st)
+                          : mv8_batch(m, spec, st, npf, pref);
         if (r != 1) return r;
     }
     for (int i = 0; i < n; ++i) {
         const SmoeMatvec& p = pr[i];
-        if (p.pairs == 0) continue;
+        if (p.pairs == 0 || p.out == nullptr) continue;
         const int r = p.x ? smoe_matvec(p.kind, p.blocks, p.experts, p.rows, p.cols, p.idx, p.pairs, p.share, p.x,
                                         p.out, p.dtype, stream)
                           : smoe_matvec_glu(p.kind, p.blocks, p.experts, p.rows, p.cols, p.idx, p.pairs, p.gate,

@@ -302,9 +302,12 @@ struct M8X {
 constexpr int kM8MaxProbs = 4, kM8MaxX = 4;
 constexpr int kM8MaxRows = 1024;   // activation rows of all sources
 constexpr int kM8MaxWarpJobs = 32;  // jobs of one warp (one per lane of its job table)
+constexpr int kM8MaxPref = 2;
 struct M8Launch {
     M8Prob p[kM8MaxProbs];
     M8X x[kM8MaxX];
+    M8Pref pf[kM8MaxPref];  // later launches' weights fetched into L2 while this one streams its own
+    int npf;
     int nprob, nx, jobs, team, nslots, slot_bytes, lut, scales;
     int64_t xbytes;
 };
@@ -514,6 +517,24 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
         }
         team_sync();
     }
+    // this CTA's slice of every expert the later launches read, into L2 (evict-last), once its own weights
+    // are in (the launch's tail leaves HBM idle)
+    if (warp == 0) {
+        const uint64_t keep = tc::policy_evict_last();
+        for (int f = 0; f < L.npf; ++f) {
+            const M8Pref& Pf = L.pf[f];
+            const int64_t eb = Pf.expert_bytes;
+            const int64_t s0 = (int64_t(blockIdx.x) * eb / gridDim.x) & ~int64_t(15);
+            const int64_t s1 = (int64_t(blockIdx.x + 1) * eb / gridDim.x) & ~int64_t(15);
+            for (int i = lane; i < Pf.pairs; i += 32) {
+                const uint32_t e = __ldg(Pf.idx + i);
+                if (e >= Pf.experts) continue;
+                const uint8_t* base = Pf.blocks + int64_t(e) * eb;
+                for (int64_t o = s0; o < s1; o += 65536)
+                    tc::prefetch_l2_bulk(base + o, static_cast<uint32_t>(min(int64_t(65536), s1 - o)), keep);
+            }
+        }
+    }
     // the next kernel may start placing its CTAs (releasing right after the wait instead measured slower: the
     // waiting CTAs of the next kernel crowd the running ones)
     pdl_release();
@@ -658,8 +679,8 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
 
 // Launch several matvec problems as one int8 tensor-core kernel: 0 launched, 1 not taken (the caller runs
 // them another way), else an error status. Problems with the same activation pointers share one source.
-int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
-    if (n < 1 || n > kM8MaxProbs) return 1;
+int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st, int npf, const M8Pref* pf) {
+    if (n < 1 || n > kM8MaxProbs || npf < 0 || npf > kM8MaxPref) return 1;
     // the problems in order of falling cost per job (bytes of a 16-row tile), so that the round-robin of jobs
     // over teams hands the big jobs out first
     M8Spec specs[kM8MaxProbs];
@@ -758,6 +779,11 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st) {
     }
     if (rows > kM8MaxRows) return 1;
     L.nprob = n;
+    L.npf = 0;
+    for (int i = 0; i < npf; ++i)
+        if (pf[i].blocks && pf[i].idx && pf[i].pairs > 0 && pf[i].expert_bytes % 16 == 0 &&
+            (reinterpret_cast<uintptr_t>(pf[i].blocks) & 15) == 0)
+            L.pf[L.npf++] = pf[i];
     L.jobs = jobs;
     L.scales = scales;
     L.xbytes = xbytes;

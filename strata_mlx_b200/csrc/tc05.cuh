@@ -90,6 +90,36 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst_smem, const void* tmap,
         : "memory");
 }
 
+// L2 eviction policies (createpolicy): evict_first for data read once (streamed weights), evict_last for data
+// fetched ahead of the launch that reads it
+__device__ __forceinline__ uint64_t policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// tma_load_2d with an L2 cache policy
+__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst_smem, const void* tmap, int x, int y, uint64_t* bar,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, %3}], "
+        "[%4], %5;\n" ::"r"(dst_smem),
+        "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar))),
+        "l"(policy)
+        : "memory");
+}
+
+// Fetch [src, src + bytes) of global memory into L2 (no destination; 16-byte aligned, a multiple of 16 bytes)
+__device__ __forceinline__ void prefetch_l2_bulk(const void* src, uint32_t bytes, uint64_t policy) {
+    asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;\n" ::"l"(src), "r"(bytes), "l"(policy)
+                 : "memory");
+}
+
 __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
 }
