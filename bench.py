@@ -1,6 +1,6 @@
-"""Benchmark of the MoE hot path: BASELINE config 2, one MoE layer decoding one token (batch 1).
+"""Benchmark of the MoE hot path: the headline configuration 2, one MoE layer decoding one token (batch 1).
 
-Workload: hidden 4096 float16 ~N(0,1); router float16 [256 x 4096] ~N(0,0.02); top-8 with
+Workload (the benchmark's configs[1]): hidden 4096 float16 ~N(0,1); router float16 [256 x 4096] ~N(0,0.02); top-8 with
 the softmax over the chosen; 256 experts with gate/up [1536 x 4096] and down [4096 x 1536] in IQ3_S blocks
 (uniform random bytes, float16 super-scale |N(0,0.02)|); a shared expert of ffn 4096 in Q8_0 with its float16
 sigmoid gate; SwiGLU; weighted combine. A step is one token through one such layer. Steps cycle through
@@ -132,7 +132,7 @@ def cpu_baseline(steps, seed):
 # ---------------------------------------------------------------- GPU workload
 
 def make_layers(n_layers, seed, device, rank=0, world=1):
-    """`n_layers` independent layers of random blocks on the device, as BASELINE config 2 describes them. With
+    """`n_layers` independent layers of random blocks on the device, as configuration 2 of the benchmark describes them. With
     world > 1 each rank holds its experts' stacks [rank * E/world, (rank+1) * E/world) and its slice of the
     shared expert's ffn."""
     import torch
@@ -166,12 +166,16 @@ def make_layers(n_layers, seed, device, rank=0, world=1):
     return layers
 
 
-def run_prefill(device, seed, steps=5, warmup=2):
-    """the same layer shapes in Q2_K (gate/up 1536 x 4096, down 4096 x 1536, 256 experts), a
+def run_prefill(device, seed, steps=5, warmup=2, rank=0, world=1):
+    """Configuration 3 of the benchmark: the same layer shapes in Q2_K (gate/up 1536 x 4096, down 4096 x 1536, 256 experts), a
     prompt chunk of 1180 tokens ~N(0,1), router logits biased so expert load is Zipf-skewed (s = 1.1): the
     router weight carries log p_e along a unit direction u that every token has a component 1 along. Times the
     whole block (router, top-k, tiles_of, three tensor-core tile products, SwiGLU, the shared expert on the
-    tile product, combine) and the three routed tile products alone."""
+    tile product, combine) and the three routed tile products alone.
+
+    With world > 1 every rank makes the same layer and chunk, keeps its experts (E / world) and the whole
+    shared expert, and takes a contiguous share of the tokens; the block is `ExpertParallelPrompt` (all-to-all
+    dispatch and return over NCCL), timed on every rank with CUDA events, the maximum over ranks reported."""
     import torch
 
     from strata_mlx_b200 import blocks as B
@@ -206,6 +210,8 @@ def run_prefill(device, seed, steps=5, warmup=2):
     block = Fz.SparseMoeBlock(router, B.BlockSwitchGLU(gate, up, down), shared, sgate, K)
     x = torch.randn(T, H, device=device, generator=g)
     x = (x - (x @ u)[:, None] * u[None, :] + u[None, :]).half()
+    if world > 1:
+        return _prefill_ep(block, x, steps, warmup, rank, world)
 
     for _ in range(warmup):
         block(x)
@@ -243,6 +249,45 @@ def run_prefill(device, seed, steps=5, warmup=2):
             "routed_gemm_ms": gemm_ms, "routed_gemm_tflops": flops / (gemm_ms * 1e-3) / 1e12,
             "routed_gflop": flops / 1e9, "experts_hit": int((counts > 0).sum().item()),
             "max_pairs_per_expert": int(counts.max().item())}
+
+
+def _prefill_ep(block, x, steps, warmup, rank, world):
+    """Configuration 3 over `world` ranks: rank r's experts and tokens [r T / world, (r+1) T / world)."""
+    import torch
+    import torch.distributed as dist
+
+    from strata_mlx_b200 import parallel as P
+
+    T = x.shape[0]
+    sw = block.switch_mlp
+    stacks = [(lin.blocks, lin.kind, lin.shape) for lin in (sw.gate_proj, sw.up_proj, sw.down_proj)]
+    sh = block.shared_expert
+    shared = [(lin.blocks, lin.kind, lin.shape) for lin in (sh.gate_proj, sh.up_proj, sh.down_proj)]
+    part = P.shard_layer(block.gate.weight, *stacks, shared, block.shared_expert_gate.weight, K, rank, world,
+                         whole_shared=True)
+    ep = P.ExpertParallelPrompt(part, rank, world, E)
+    xr = x[rank * T // world : (rank + 1) * T // world].contiguous()
+    for _ in range(warmup):
+        ep(xr)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        ep(xr)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / steps], device=x.device)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    received = torch.tensor([ep.received], device=x.device)
+    per_rank = [torch.zeros_like(received) for _ in range(world)]
+    dist.all_gather(per_rank, received)
+    layer_ms = float(ms.item())
+    return {"workload": f"config 3 over {world} GPUs: one MoE layer, prefill chunk of 1180 tokens split over the "
+                        "ranks, 256 Q2_K experts sharded E/N, top-8, Zipf s=1.1 routing, the shared expert ffn 4096 "
+                        "Q8_0 on every rank; all-to-all dispatch and return over NCCL",
+            "layer_ms": layer_ms, "tokens_per_s": T / (layer_ms * 1e-3),
+            "pairs_per_rank": [int(t.item()) for t in per_rank]}
 
 
 class Clocks:
@@ -521,6 +566,12 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         line = run_ours(args, rank, world, local_rank)
+        if world > 1 and not args.no_prefill:
+            import torch
+
+            pf = run_prefill(torch.device("cuda", local_rank), args.seed + 99, rank=rank, world=world)
+            if line is not None:
+                line["prefill"] = pf
     finally:
         if world > 1:
             import torch.distributed as dist

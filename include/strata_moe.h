@@ -159,7 +159,7 @@ SMOE_API int smoe_combine(const void* y, const float* w, const void* g, const vo
 
 /* Expert parallelism (N ranks, each holding the experts [lo, lo + count) of every layer and a 1/N slice of the
  * shared expert's ffn): the pieces around the one all-reduce of a decode step. No counterpart in the
- * reference, which runs on one device (SURVEY: strata_mlx has no multi-device code); they split
+ * reference, which runs on one device (strata_mlx has no multi-device code); they split
  * `_Routed.__call__` (strata_mlx/fused.py:487-497) at its combine.
  *   smoe_localize:     lidx = idx - lo for this rank's experts, else `count` (a pair the kernels leave out).
  *   smoe_partial_sums: sums[t, 0:d] = sum over this rank's pairs of y * w (MLX's order among them), float32;
@@ -171,6 +171,24 @@ SMOE_API int smoe_partial_sums(const void* y, const float* w, const uint32_t* li
                                int64_t tokens, int64_t k, int64_t d, float* sums, int dtype, void* stream);
 SMOE_API int smoe_combine_sums(const float* sums, const void* g, int64_t tokens, int64_t d, void* out, int dtype,
                                void* stream);
+
+/* Expert parallelism for a prompt chunk (each rank holds its own tokens; rank r owns experts [r E/N, (r+1) E/N)):
+ * the two ends of the all-to-all exchanges that carry the pairs to their experts' ranks and the outputs back.
+ * Like the decode pieces above, no counterpart in the reference; together they split `_Routed.__call__`
+ * (strata_mlx/fused.py:487-497) between the top-k and the combine.
+ *   smoe_ep_dispatch:  from idx (pairs = tokens * k expert indices, flat), counts[ranks] = the pairs per
+ *                      destination rank (idx / (experts / ranks)); where[pairs] = each pair's place in the send
+ *                      order (destinations in rank order, one destination's pairs in pair order; -1 for an
+ *                      index not below `experts`, which is not sent); send_expert[place] = the expert in its
+ *                      owner's numbering; send_x[place] = the pair's token row of x (tokens, hidden) `dtype`.
+ *                      send_expert and send_x hold `pairs` entries / rows; the first sum(counts) are written.
+ *   smoe_combine_rows: smoe_combine with the experts' outputs read at y[where[t * k + j]] (the rows returned
+ *                      by the exchange, in the send order) instead of y[t, j]; a pair with where -1 adds 0. */
+SMOE_API int smoe_ep_dispatch(const uint32_t* idx, int64_t pairs, int64_t k, int64_t experts, int64_t ranks,
+                              const void* x, int64_t hidden, int dtype, int32_t* counts, int32_t* where,
+                              uint32_t* send_expert, void* send_x, void* stream);
+SMOE_API int smoe_combine_rows(const void* y, const int32_t* where, const float* w, const void* g, const void* s,
+                               int64_t tokens, int64_t k, int64_t d, void* out, int dtype, void* stream);
 
 /* The dispatch permutation of `pairs` = tokens * k expert indices (int32, flat) into tiles of 16 slots,
  * each tile one expert's: tile_expert[most] (experts for a tile nothing fills), token[most * 16] (0 in an

@@ -193,3 +193,32 @@ def combine_sums(sums, g, dtype=np.float16):
     gate = (np.float32(1) / (np.float32(1) + np.exp(-np.asarray(g, dtype=np.float32)))).astype(dtype)
     shared = (gate.astype(np.float32)[:, None] * sums[:, D:].astype(dtype).astype(np.float32)).astype(dtype)
     return (routed.astype(np.float32) + shared.astype(np.float32)).astype(dtype)
+
+
+def ep_plan(idx, experts, ranks):
+    """The send side of a prompt chunk's expert-parallel exchange. No counterpart in the reference (one device);
+    it splits `_Routed.__call__` (strata_mlx/fused.py:487-497) between top-k and `switch_mlp`: each pair goes to
+    the rank owning its expert (idx // (experts / ranks)); destinations in rank order, one destination's pairs in
+    pair order. Returns (counts[ranks] int32, where[pairs] int32 (-1: index out of range, not sent),
+    send_expert[sent] uint32 (the expert in its owner's numbering), order[sent] (the pair of each place))."""
+    flat = np.asarray(idx).reshape(-1).astype(np.int64)
+    per = experts // ranks
+    dest = np.where(flat < experts, flat // per, ranks)
+    order = np.argsort(dest, kind="stable")
+    order = order[dest[order] < ranks]
+    counts = np.bincount(dest[dest < ranks], minlength=ranks).astype(np.int32)
+    where = np.full(flat.size, -1, dtype=np.int32)
+    where[order] = np.arange(order.size, dtype=np.int32)
+    send_expert = (flat[order] - dest[order] * per).astype(np.uint32)
+    return counts, where, send_expert, order
+
+
+def combine_rows(y_rows, where, w, g, s):
+    """`combine` with pair (t, j)'s expert output at y_rows[where[t k + j]] (0 for where -1)."""
+    T, K = np.asarray(w).shape
+    wh = np.asarray(where).reshape(T, K)
+    yr = np.asarray(y_rows)
+    if yr.shape[0] == 0:
+        return combine(np.zeros((T, K, s.shape[-1]), dtype=yr.dtype), w, g, s)
+    y = np.where((wh >= 0)[..., None], yr[np.maximum(wh, 0)], 0).astype(yr.dtype)
+    return combine(y, w, g, s)

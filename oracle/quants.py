@@ -278,7 +278,7 @@ def random_blocks(kind: str, n_blocks: int, rng: np.random.Generator, scale=(-0.
     """Uniform random block bytes with the float16 scale fields overwritten (tests/test_gguf.py:17-30).
 
     `scale` draws the scales uniformly from an interval; `normal=sigma` draws |N(0, sigma)| instead (the
-    benchmark blocks of SURVEY-style configs: a positive super-scale around sigma).
+    benchmark's blocks: a positive super-scale around sigma).
     """
     _, _, block_bytes = TYPES[kind]
     b = rng.integers(0, 256, (n_blocks, block_bytes), dtype=np.uint8)

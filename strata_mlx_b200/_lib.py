@@ -60,6 +60,8 @@ SIGNATURES = {
     "smoe_localize": (_i, [_p, _i64, _i64, _i64, _p, _p]),
     "smoe_partial_sums": (_i, [_p, _p, _p, _i64, _p, _i64, _i64, _i64, _p, _i, _p]),
     "smoe_combine_sums": (_i, [_p, _p, _i64, _i64, _p, _i, _p]),
+    "smoe_ep_dispatch": (_i, [_p, _i64, _i64, _i64, _i64, _p, _i64, _i, _p, _p, _p, _p, _p]),
+    "smoe_combine_rows": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
     "smoe_tiles_of_workspace_size": (_sz, [_i64, _i64]),
     "smoe_tiles_of": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _sz, _p]),
     "smoe_tiles_of_noalloc": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),

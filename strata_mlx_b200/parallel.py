@@ -1,6 +1,6 @@
 """Expert parallelism across the GPUs of one node: one process per GPU, NCCL over NVLink / NVSwitch.
 
-The reference runs on one device; SURVEY's multi-GPU plan splits its MoE block (`_Routed.__call__`,
+The reference runs on one device; the multi-GPU plan here splits its MoE block (`_Routed.__call__`,
 strata_mlx/fused.py:487-497) at the combine:
 
     rank r of N holds experts [r E/N, (r+1) E/N) of every stack and rows / columns [r F/N, (r+1) F/N) of the
@@ -10,7 +10,15 @@ strata_mlx/fused.py:487-497) at the combine:
     applies the combine's rounding to the summed partials.
 
 The sums are taken in a fixed order on each rank and NCCL's reduction across ranks, so the result depends on
-N at the level of float32 rounding (within the 1e-3 rel-L2 budget), not on timing. No TMA multicast anywhere.
+N at the level of float32 rounding (within the 1e-3 rel-L2 budget), not on timing.
+
+A prompt chunk splits by tokens as well (`ExpertParallelPrompt`): each rank routes its own tokens, sends every
+pair's token row to the rank of its expert (an all-to-all of the counts, then of the rows and the experts'
+local numbers), runs the grouped products over what it received, sends the outputs back by the reverse
+all-to-all, and combines at the tokens' home with the whole shared expert. A pair's output is computed by the
+same kernels from the same row as on one device, and the combine reads the outputs in the same order, so the
+result differs from one device's only where the receiving rank's pair count chooses another product path.
+No TMA multicast anywhere.
 """
 
 import torch
@@ -55,14 +63,19 @@ def slice_cols(blocks: torch.Tensor, kind: str, shape: tuple, c0: int, c1: int) 
     return blocks.reshape(rows, rb)[:, c0 // per * nbytes : c1 // per * nbytes].contiguous().reshape(-1)
 
 
-def shard_layer(router, gate, up, down, shared, shared_gate, top_k: int, rank: int, world: int) -> SparseMoeBlock:
+def shard_layer(router, gate, up, down, shared, shared_gate, top_k: int, rank: int, world: int,
+                whole_shared: bool = False) -> SparseMoeBlock:
     """`rank`'s part of a MoE layer: its experts of the routed stacks (each a (blocks, kind, shape)) and its
-    slice of the shared expert's ffn (gate/up rows, down columns); router and shared gate replicated."""
+    slice of the shared expert's ffn (gate/up rows, down columns), or with `whole_shared` the whole shared
+    expert (a prompt chunk's ranks each run it on their own tokens); router and shared gate replicated."""
     def local_stack(b, kd, s):
         lb, ls = shard_stack(b, kd, s, rank, world)
         return BlockSwitchLinear(lb, kd, ls)
 
     sw = BlockSwitchGLU(local_stack(*gate), local_stack(*up), local_stack(*down))
+    if whole_shared:
+        return SparseMoeBlock(router, sw, BlockMLP(*(BlockLinear(b, kd, s) for b, kd, s in shared)), shared_gate,
+                              top_k)
     (gb, gk, (fs, hid)), (ub, uk, _), (db, dk, _) = shared
     lo, n = expert_range(rank, world, fs)
     sh = BlockMLP(BlockLinear(slice_rows(gb, gk, (fs, hid), lo, lo + n), gk, (n, hid)),
@@ -113,5 +126,93 @@ class ExpertParallelMoE:
         return out.reshape(*lead, hidden)
 
 
-__all__ = ["ExpertParallelMoE", "expert_range", "shard_stack", "shard_layer", "slice_cols", "slice_rows",
-           "WindowLinear"]
+def exchange_counts(counts: torch.Tensor, group=None) -> torch.Tensor:
+    """All-to-all of one int32 per rank: element r of the result is what rank r has for this one."""
+    out = torch.empty_like(counts)
+    dist.all_to_all_single(out, counts, group=group)
+    return out
+
+
+def exchange_rows(rows: torch.Tensor, send: list, recv: list, group=None) -> torch.Tensor:
+    """All-to-all of rows: the first send[r] rows of `rows` (after those for ranks before r) go to rank r,
+    and the result holds recv[r] rows from each rank r, in rank order. Integer rows travel as int32."""
+    out = torch.empty((sum(recv),) + tuple(rows.shape[1:]), dtype=rows.dtype, device=rows.device)
+    src = rows[: sum(send)]
+    if rows.dtype == torch.uint32:
+        src, out = src.view(torch.int32), out.view(torch.int32)
+    dist.all_to_all_single(out, src.contiguous(), recv, send, group=group)
+    return out.view(rows.dtype) if rows.dtype == torch.uint32 else out
+
+
+def dispatch(idx: torch.Tensor, x: torch.Tensor, experts: int, world: int):
+    """The send side of a prompt chunk's exchange (`smoe_ep_dispatch`): per-rank pair counts (int32, world),
+    each pair's place in the send order (int32, -1 if not sent), the expert of each place in its owner's
+    numbering (uint32) and the token row of each place. idx (tokens, k) uint32, x (tokens, hidden)."""
+    tokens, k = idx.shape
+    hidden = x.shape[-1]
+    pairs = tokens * k
+    counts = torch.empty(world, dtype=torch.int32, device=x.device)
+    where = torch.empty(pairs, dtype=torch.int32, device=x.device)
+    send_expert = torch.empty(pairs, dtype=torch.uint32, device=x.device)
+    send_x = torch.empty((pairs, hidden), dtype=x.dtype, device=x.device)
+    _lib.call("smoe_ep_dispatch", _lib.ptr(idx.contiguous()), pairs, k, experts, world, _lib.ptr(x), hidden,
+              _lib.dtype_code(x.dtype), _lib.ptr(counts), _lib.ptr(where), _lib.ptr(send_expert), _lib.ptr(send_x),
+              _lib.stream())
+    return counts, where, send_expert, send_x
+
+
+def combine_rows(y: torch.Tensor, where: torch.Tensor, w: torch.Tensor, g: torch.Tensor, s: torch.Tensor):
+    """The block's combine with each pair's expert output at row where[t k + j] of y (`smoe_combine_rows`)."""
+    tokens, k = w.shape
+    hidden = s.shape[-1]
+    out = torch.empty((tokens, hidden), dtype=s.dtype, device=s.device)
+    _lib.call("smoe_combine_rows", _lib.ptr(y), _lib.ptr(where), _lib.ptr(w.contiguous()),
+              _lib.ptr(g.contiguous()), _lib.ptr(s.contiguous()), tokens, k, hidden, _lib.ptr(out),
+              _lib.dtype_code(s.dtype), _lib.stream())
+    return out
+
+
+class ExpertParallelPrompt:
+    """A prompt chunk through a MoE block whose experts are spread over the ranks of `group`, each rank holding
+    its own tokens: call it on every rank with that rank's tokens (any count, 0 included).
+
+    `layer` is this rank's part with the whole shared expert (`shard_layer(..., whole_shared=True)`). Per call:
+    the router and top-k of the rank's tokens, `smoe_ep_dispatch`, the all-to-all of the counts (the one host
+    synchronisation: NCCL needs the split sizes), of the token rows and of the experts' numbers, the grouped
+    products of the received pairs (`switch_glu`, one pair per row), the reverse all-to-all of the outputs and
+    the combine at home (`smoe_combine_rows`). `received` is the pair count the last call computed here."""
+
+    def __init__(self, layer: SparseMoeBlock, rank: int, world: int, experts: int, group=None):
+        self.layer, self.rank, self.world, self.group = layer, rank, world, group
+        self.experts = experts
+        expert_range(rank, world, experts)
+        self.received = 0
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        layer = self.layer
+        lead, hidden = x.shape[:-1], x.shape[-1]
+        x2 = x.reshape(-1, hidden).contiguous()
+        k = layer.top_k
+        idx, w = top_k_softmax(layer.gate(x2), k)
+        counts, where, send_expert, send_x = dispatch(idx, x2, self.experts, self.world)
+        if self.world > 1:
+            recv_counts = exchange_counts(counts, self.group)
+            send, recv = counts.tolist(), recv_counts.tolist()
+            rows = exchange_rows(send_x, send, recv, self.group)
+            local = exchange_rows(send_expert, send, recv, self.group)
+        else:
+            send = recv = counts.tolist()
+            rows, local = send_x[: send[0]], send_expert[: send[0]]
+        self.received = rows.shape[0]
+        if self.received:
+            y = layer.switch_mlp(rows, local.reshape(-1, 1)).reshape(-1, hidden)
+        else:
+            y = rows
+        back = exchange_rows(y, recv, send, self.group) if self.world > 1 else y
+        s = layer.shared_expert(x2)
+        g = layer.shared_expert_gate(x2).to(x.dtype)
+        return combine_rows(back, where, w, g, s).reshape(*lead, hidden)
+
+
+__all__ = ["ExpertParallelMoE", "ExpertParallelPrompt", "combine_rows", "dispatch", "exchange_counts",
+           "exchange_rows", "expert_range", "shard_stack", "shard_layer", "slice_cols", "slice_rows", "WindowLinear"]

@@ -107,7 +107,7 @@ def test_a_graph_of_one_launch_steps_replays_the_same(cuda):
 
 
 def test_the_one_launch_step_at_baseline_shapes_is_the_oracles(cuda):
-    """BASELINE config 2 (hidden 4096, 256 IQ3_S experts of ffn 1536, top-8, Q8_0 shared expert of 4096)."""
+    """Benchmark configuration 2 (hidden 4096, 256 IQ3_S experts of ffn 1536, top-8, Q8_0 shared expert of 4096)."""
     rng = np.random.default_rng(12)
     H, F_, E, Fs, k = 4096, 1536, 256, 4096, 8
     routed, shared, router, sgate = make_layer(rng, H, F_, E, Fs, ("IQ3_S",) * 3, "Q8_0")

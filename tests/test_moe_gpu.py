@@ -3,7 +3,7 @@
 Mirrors the reference's tests/test_fused.py (cited per test). Bars: router logits within 1e-5 of the largest
 (float64 oracle) and the same bits for a token alone as inside a window; top-k indices exactly those of a
 stable arg-sort of the kernel's own logits; the combine bit-equal to the oracle's restatement of MLX's order;
-the MoE block's output within rel-L2 1e-3 of the oracle (tolerance of BASELINE's north star), its expert
+the MoE block's output within rel-L2 1e-3 of the oracle (the path's stated tolerance), its expert
 indices exact.
 """
 
@@ -157,7 +157,7 @@ def test_a_prompt_chunk_through_tiles_and_the_shared_gemm_is_the_oracles(cuda):
 
 
 def test_the_decode_layer_at_baseline_shapes_is_the_oracles(cuda):
-    """hidden 4096, 256 experts of IQ3_S (gate/up 1536 x 4096, down 4096 x 1536), top-8,
+    """Benchmark configuration 2: hidden 4096, 256 experts of IQ3_S (gate/up 1536 x 4096, down 4096 x 1536), top-8,
     shared expert ffn 4096 in Q8_0, batch 1."""
     rng = np.random.default_rng(2)
     H, F_, E, Fs, k = 4096, 1536, 256, 4096, 8

@@ -111,3 +111,75 @@ def test_two_ranks_over_gloo_give_the_single_block():
         assert p.exitcode == 0
     errs = sorted(q.get() for _ in range(2))
     assert all(e <= 1e-3 for _, e in errs), errs
+
+
+def test_the_send_plan_keeps_pair_order_within_each_destination():
+    """oracle ep_plan against a direct statement: destinations in rank order, pairs in order within each."""
+    rng = np.random.default_rng(11)
+    idx = rng.integers(0, 66, size=(37, 8))  # 64 experts; 64 and 65 are out of range and stay home
+    counts, where, send_expert, order = M.ep_plan(idx, 64, 4)
+    flat = idx.reshape(-1)
+    want = [i for r in range(4) for i in range(flat.size) if flat[i] < 64 and flat[i] // 16 == r]
+    np.testing.assert_array_equal(order, want)
+    np.testing.assert_array_equal(counts, [sum(1 for i in want if flat[i] // 16 == r) for r in range(4)])
+    assert all(where[i] == -1 for i in range(flat.size) if flat[i] >= 64)
+    np.testing.assert_array_equal(where[order], np.arange(len(want)))
+    np.testing.assert_array_equal(send_expert, flat[order] % 16)
+
+
+def _prompt_rank(rank, world, port, seed, split, q):
+    """One rank of a prompt chunk: its tokens routed, the pairs sent by the product's exchange helpers, the
+    received pairs' products and the combine done by the oracle."""
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        routed, shared, router, sgate, _ = layer(seed)
+        rng = np.random.default_rng(seed + 1)
+        x_all = rng.standard_normal((sum(split), H)).astype(np.float16)
+        x = x_all[sum(split[:rank]) : sum(split[: rank + 1])]
+        local = []
+        for b, kind, shape in routed:
+            lb, ls = P.shard_stack(torch.from_numpy(b), kind, shape, rank, world)
+            local.append((lb.numpy(), kind, ls))
+        logits = M.router_logits(router, x)
+        idx = M.top_k(logits, K)
+        w = M.softmax_chosen(logits, idx)
+        counts, where, send_expert, order = M.ep_plan(idx, E, world)
+        send_x = x[order // K]
+        recv_counts = P.exchange_counts(torch.from_numpy(counts))
+        send, recv = counts.tolist(), recv_counts.tolist()
+        rows = P.exchange_rows(torch.from_numpy(send_x), send, recv).numpy()
+        experts = P.exchange_rows(torch.from_numpy(send_expert), send, recv).numpy()
+        y = np.zeros((rows.shape[0], H), dtype=np.float16)
+        for i in range(rows.shape[0]):
+            y[i] = M.switch_glu(rows[i : i + 1], experts[i : i + 1].reshape(1, 1).astype(np.int64), *local)[0, 0]
+        back = P.exchange_rows(torch.from_numpy(y), recv, send).numpy()
+        s = M.dense_mlp(x, *shared)
+        g = (x.astype(np.float64) @ sgate.astype(np.float64).reshape(-1)).astype(np.float16)
+        out = M.combine_rows(back, where, w, g, s)
+        if x.shape[0]:
+            want, *_ = M.moe_block(x, router, K, routed, shared, sgate)
+            err = np.linalg.norm(out.astype(np.float64) - want) / np.linalg.norm(want.astype(np.float64))
+        else:
+            err = 0.0
+        q.put((rank, float(err), int(rows.shape[0])))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("split", [(4, 3), (5, 0)])
+def test_a_prompt_chunk_over_two_gloo_ranks_gives_each_ranks_tokens_the_single_block(split):
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    procs = [ctx.Process(target=_prompt_rank, args=(r, 2, port, 6, split, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    got = sorted(q.get() for _ in range(2))
+    assert all(e <= 1e-3 for _, e, _ in got), got
+    assert sum(n for *_, n in got) == sum(split) * K  # every pair computed once, somewhere
