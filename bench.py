@@ -50,6 +50,10 @@ def _args():
     p.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline (profiling runs)")
     p.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
     p.add_argument("--only-prefill", action="store_true", help="only the config-3 prefill measurement (profiling)")
+    p.add_argument("--no-verify", action="store_true", help="skip the config-4 verify-pass measurement")
+    p.add_argument("--only-verify", action="store_true", help="only the config-4 verify-pass measurement")
+    p.add_argument("--only-matvec", metavar="KIND", help="profiling: the CUDA-core matvec of config 4's down "
+                   "product (40 pairs of 5 tokens, 64 experts of 4096 x 1536 KIND blocks), a few launches")
     return p.parse_args()
 
 
@@ -249,6 +253,110 @@ def run_prefill(device, seed, steps=5, warmup=2, rank=0, world=1):
             "routed_gemm_ms": gemm_ms, "routed_gemm_tflops": flops / (gemm_ms * 1e-3) / 1e12,
             "routed_gflop": flops / 1e9, "experts_hit": int((counts > 0).sum().item()),
             "max_pairs_per_expert": int(counts.max().item())}
+
+
+VERIFY_TYPES = ("Q8_0", "Q4_K", "Q5_K", "Q6_K", "Q2_K", "Q3_K", "IQ3_S", "IQ3_XXS", "IQ4_XS")
+# the float16 scale fields of each type's block (byte offsets), overwritten with |N(0, SIGMA)|
+SCALE_AT = {"Q8_0": (0,), "Q4_K": (0, 2), "Q5_K": (0, 2), "Q6_K": (208,), "Q2_K": (80, 82), "Q3_K": (108,),
+            "IQ3_S": (0,), "IQ3_XXS": (0,), "IQ4_XS": (0,)}
+
+
+def run_verify(device, seed, steps=50, warmup=5, n_layers=8, tokens=5):
+    """Configuration 4 of the benchmark, a speculative verify pass: 5 tokens (1 accepted + 4 drafted) through 8
+    MoE layers of 256 experts, top-8, whose routed tensors cycle through the nine block types (layer l's
+    gate/up/down have VERIFY_TYPES[(3 l + j) % 9]), each with the Q8_0 shared expert of ffn 4096. Every layer is
+    one CUDA graph (`GraphedBlock`); a step replays the 8 in order. Every layer takes the same window (the
+    layers are random, so a chained window would overflow float16 and route by inf): the routing stays that
+    of N(0,1) tokens. The layers hold 22 GB, so a step reads its experts from HBM. `bytes` counts each layer's
+    distinct chosen experts' three stacks, the shared expert and the router, once per step."""
+    import torch
+
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200 import fused as Fz
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def random_blocks(kind, n_weights):
+        per, nbytes = B.BLOCK[kind]
+        n = n_weights // per
+        b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=g)
+        for at in SCALE_AT[kind]:
+            b[:, at : at + 2] = (torch.randn(n, device=device, generator=g) * SIGMA).abs().half().view(torch.uint8).view(n, 2)
+        return b.reshape(-1)
+
+    x = torch.randn(tokens, H, device=device, generator=g).half()
+    graphs, total_bytes = [], 0
+    for layer in range(n_layers):
+        kinds = [VERIFY_TYPES[(3 * layer + j) % 9] for j in range(3)]
+        gate = B.BlockSwitchLinear(random_blocks(kinds[0], E * F_ * H), kinds[0], (E, F_, H))
+        up = B.BlockSwitchLinear(random_blocks(kinds[1], E * F_ * H), kinds[1], (E, F_, H))
+        down = B.BlockSwitchLinear(random_blocks(kinds[2], E * H * F_), kinds[2], (E, H, F_))
+        shared = B.BlockMLP(B.BlockLinear(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+                            B.BlockLinear(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+                            B.BlockLinear(random_blocks(SHARED_KIND, H * FS), SHARED_KIND, (H, FS)))
+        router = (torch.randn(E, H, device=device, generator=g) * 0.02).half()
+        sgate = (torch.randn(1, H, device=device, generator=g) * 0.02).half()
+        block = Fz.SparseMoeBlock(router, B.BlockSwitchGLU(gate, up, down), shared, sgate, K)
+        hit = int(torch.unique(Fz.top_k(block.gate(x), K).view(torch.int32)).numel())
+        per_expert = F_ * B.row_bytes(kinds[0], H) + F_ * B.row_bytes(kinds[1], H) + H * B.row_bytes(kinds[2], F_)
+        total_bytes += hit * per_expert + 3 * FS * B.row_bytes(SHARED_KIND, H) + (E + 1) * H * 2
+        graphs.append(Fz.GraphedBlock(block, tokens, H, torch.float16, device))
+    for _ in range(warmup):
+        for gb in graphs:
+            gb(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        for gb in graphs:
+            gb(x)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    peak = 6462.0
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        peak = json.load(open(path)).get("hbm_gbs", peak)
+    gbs = total_bytes / (ms * 1e-3) / 1e9
+    return {"workload": f"config 4: verify pass of {tokens} tokens through {n_layers} MoE layers cycling the nine "
+                        "block types, 256 experts top-8, shared expert ffn 4096 Q8_0, one CUDA graph per layer",
+            "ms_per_pass": ms, "tokens_per_s": tokens / (ms * 1e-3),
+            "token_layers_per_s": tokens * n_layers / (ms * 1e-3), "bytes_per_pass": total_bytes,
+            "achieved_gbs": gbs, "hbm_peak_gbs": peak, "frac": gbs / peak}
+
+
+def run_matvec(kind, seed, steps=3, warmup=3, experts=64, tokens=5):
+    """One product of config 4's shape on the CUDA-core decode matvec (a type the tensor-core kernels do not
+    take): `tokens` x top-8 pairs through a stack of `experts` (4096 x 1536) of `kind`, 283 MB for Q5_K (more
+    than L2), small enough for a profiler's replays."""
+    import torch
+
+    from strata_mlx_b200 import blocks as B
+
+    device = torch.device("cuda", 0)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    per, nbytes = B.BLOCK[kind]
+    n = experts * H * F_ // per
+    b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=g)
+    for at in SCALE_AT[kind]:
+        b[:, at : at + 2] = (torch.randn(n, device=device, generator=g) * SIGMA).abs().half().view(torch.uint8).view(n, 2)
+    lin = B.BlockSwitchLinear(b.reshape(-1), kind, (experts, H, F_))
+    x = torch.randn(tokens, 1, 1, F_, device=device, generator=g).half()  # one row shared by a token's 8 pairs
+    idx = torch.randperm(experts, device=device, generator=g)[: tokens * K].to(torch.int32).reshape(tokens, K)
+    for _ in range(warmup):
+        lin(x, idx)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        lin(x, idx)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / steps * 1e3
+    nbytes_read = tokens * K * H * B.row_bytes(kind, F_)
+    return {"kind": kind, "pairs": tokens * K, "us": us, "gbs": nbytes_read / (us * 1e-6) / 1e9}
 
 
 def _prefill_ep(block, x, steps, warmup, rank, world):
@@ -546,6 +654,15 @@ def main():
                                             "d2h_bytes_per_step": 0}}
         print(json.dumps(line))
         return
+    if args.only_matvec:
+        print(json.dumps({"matvec": run_matvec(args.only_matvec, args.seed + 299, steps=args.steps,
+                                               warmup=args.warmup)}))
+        return
+    if args.only_verify:
+        import torch
+
+        print(json.dumps({"verify": run_verify(torch.device("cuda", local_rank), args.seed + 199)}))
+        return
     if args.only_prefill:
         import torch
 
@@ -592,6 +709,10 @@ def main():
                               "achieved": pf["routed_gemm_tflops"], "peak": peak_tf, "unit": "TFLOP/s",
                               "frac": pf["routed_gemm_tflops"] / peak_tf}
             line["prefill"] = pf
+        if world == 1 and not args.no_verify:
+            import torch
+
+            line["verify"] = run_verify(torch.device("cuda", local_rank), args.seed + 199)
         print(json.dumps(line))
 
 

@@ -332,6 +332,231 @@ struct IQ1_M {
     }
 };
 
+// ---- Staged forms: `Staged<B>::run` writes the same floats as `B::run` (the same operations in the same order)
+// for a row held in shared memory with at least 4 bytes after its end that may be read (the matvec's row slots).
+// It reads the row four bytes at a time (two aligned words and a funnel shift, whatever the row's alignment)
+// and turns small integers into floats without a conversion instruction: a byte v placed in the mantissa of
+// 2^23 is the float 2^23 + v, and subtracting 2^23 + c gives v - c exactly (|v - c| < 2^23).
+
+__device__ __forceinline__ uint32_t word_at(const uint8_t* p) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~uintptr_t(3));
+    return __funnelshift_r(w[0], w[1], static_cast<uint32_t>(a & 3u) * 8u);
+}
+// byte j of w, less c, as a float (base = 2^23 + c)
+template <int J>
+__device__ __forceinline__ float byte_less(uint32_t w, float base) {
+    return __fsub_rn(__int_as_float(static_cast<int>(__byte_perm(w, 0x4B000000u, 0x7540u + J))), base);
+}
+constexpr float kF0 = 8388608.0f;  // 2^23
+
+template <class B>
+struct Staged {
+    __device__ static void run(const uint8_t* row, int n, float* w) { B::run(row, n, w); }
+};
+
+template <>
+struct Staged<Q8_0> {
+    __device__ static void run(const uint8_t* row, int n, float* w) {
+        const uint8_t* b = row + n * Q8_0::kBytes;
+        const float d = half_at(b);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const uint32_t u = word_at(b + 2 + 4 * i) ^ 0x80808080u;  // int8 q as q + 128
+            w[4 * i + 0] = mul_rn(d, byte_less<0>(u, kF0 + 128.0f));
+            w[4 * i + 1] = mul_rn(d, byte_less<1>(u, kF0 + 128.0f));
+            w[4 * i + 2] = mul_rn(d, byte_less<2>(u, kF0 + 128.0f));
+            w[4 * i + 3] = mul_rn(d, byte_less<3>(u, kF0 + 128.0f));
+        }
+    }
+};
+
+template <>
+struct Staged<Q2_K> {
+    __device__ static void run(const uint8_t* row, int n, float* w) {
+        const uint8_t* b = row + (n >> 3) * Q2_K::kBytes;
+        const int r = n & 7;
+        const uint8_t* q = b + 16 + 32 * (r >> 2);
+        const int shift = 2 * (r & 3);
+        const float d = half_at(b + 80), dmin = half_at(b + 82);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const uint32_t s = b[2 * r + h];
+            const float dl = mul_rn(d, float(s & 15)), ml = mul_rn(dmin, float(s >> 4));
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const uint32_t v = (word_at(q + 16 * h + 4 * i) >> shift) & 0x03030303u;
+                w[16 * h + 4 * i + 0] = sub_rn(mul_rn(dl, byte_less<0>(v, kF0)), ml);
+                w[16 * h + 4 * i + 1] = sub_rn(mul_rn(dl, byte_less<1>(v, kF0)), ml);
+                w[16 * h + 4 * i + 2] = sub_rn(mul_rn(dl, byte_less<2>(v, kF0)), ml);
+                w[16 * h + 4 * i + 3] = sub_rn(mul_rn(dl, byte_less<3>(v, kF0)), ml);
+            }
+        }
+    }
+};
+
+template <>
+struct Staged<Q3_K> {
+    __device__ static void run(const uint8_t* row, int n, float* w) {
+        const uint8_t* b = row + (n >> 3) * Q3_K::kBytes;
+        const int r = n & 7;
+        const uint8_t* q = b + 32 + 32 * (r >> 2);
+        const int shift = 2 * (r & 3);
+        const float d = half_at(b + 108);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float dl = mul_rn(d, Q3_K::scale(b + 96, 2 * r + h));
+#pragma unroll
+            for (int i = 16 * h; i < 16 * h + 16; i += 4) {
+                // q + 4 where bit r of hmask is set, q where it is clear; less 4
+                const uint32_t v = ((word_at(q + i) >> shift) & 0x03030303u) |
+                                   (((word_at(b + i) >> r) & 0x01010101u) << 2);
+                w[i + 0] = mul_rn(dl, byte_less<0>(v, kF0 + 4.0f));
+                w[i + 1] = mul_rn(dl, byte_less<1>(v, kF0 + 4.0f));
+                w[i + 2] = mul_rn(dl, byte_less<2>(v, kF0 + 4.0f));
+                w[i + 3] = mul_rn(dl, byte_less<3>(v, kF0 + 4.0f));
+            }
+        }
+    }
+};
+
+template <>
+struct Staged<Q4_K> {
+    __device__ static void run(const uint8_t* row, int n, float* w) {
+        const uint8_t* b = row + (n >> 3) * Q4_K::kBytes;
+        const int t = n & 7;
+        float sc, mn;
+        k4_scale_min(b + 4, t, sc, mn);
+        const float dl = mul_rn(half_at(b), sc), ml = mul_rn(half_at(b + 2), mn);
+        const uint8_t* q = b + 16 + 32 * (t >> 1);
+        const int shift = 4 * (t & 1);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const uint32_t v = (word_at(q + i) >> shift) & 0x0F0F0F0Fu;
+            w[i + 0] = sub_rn(mul_rn(dl, byte_less<0>(v, kF0)), ml);
+            w[i + 1] = sub_rn(mul_rn(dl, byte_less<1>(v, kF0)), ml);
+            w[i + 2] = sub_rn(mul_rn(dl, byte_less<2>(v, kF0)), ml);
+            w[i + 3] = sub_rn(mul_rn(dl, byte_less<3>(v, kF0)), ml);
+        }
+    }
+};
+
+template <>
+struct Staged<Q5_K> {
+    __device__ static void run(const uint8_t* row, int n, float* w) {
+        const uint8_t* b = row + (n >> 3) * Q5_K::kBytes;
+        const int t = n & 7;
+        float sc, mn;
+        k4_scale_min(b + 4, t, sc, mn);
+        const float dl = mul_rn(half_at(b), sc), ml = mul_rn(half_at(b + 2), mn);
+        const uint8_t* q = b + 48 + 32 * (t >> 1);
+        const int shift = 4 * (t & 1);
+#pragma unroll
+        for (int i = 0; i < 32; i += 4) {
+            const uint32_t v = ((word_at(q + i) >> shift) & 0x0F0F0F0Fu) | (((word_at(b + 16 + i) >> t) & 0x01010101u) << 4);
+            w[i + 0] = sub_rn(mul_rn(dl, byte_less<0>(v, kF0)), ml);
+            w[i + 1] = sub_rn(mul_rn(dl, byte_less<1>(v, kF0)), ml);
+            w[i + 2] = sub_rn(mul_rn(dl, byte_less<2>(v, kF0)), ml);
+            w[i + 3] = sub_rn(mul_rn(dl, byte_less<3>(v, kF0)), ml);
+        }
+    }
+};
+
+template <>
+struct Staged<Q6_K> {
+    __device__ static void run(const uint8_t* row, int n, float* w) {
+        const uint8_t* b = row + (n >> 3) * Q6_K::kBytes;
+        const int r = n & 7, h = r >> 2, s = r & 3;
+        const uint8_t* ql = b + 64 * h + 32 * (s & 1);
+        const uint8_t* qh = b + 128 + 32 * h;
+        const int lshift = 4 * (s >> 1), hshift = 2 * s;
+        const float d = half_at(b + 208);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const float dsc = mul_rn(d, float(int8_t(b[192 + 2 * r + half])));
+#pragma unroll
+            for (int i = 16 * half; i < 16 * half + 16; i += 4) {
+                const uint32_t v = ((word_at(ql + i) >> lshift) & 0x0F0F0F0Fu) |
+                                   (((word_at(qh + i) >> hshift) & 0x03030303u) << 4);  // q + 32
+                w[i + 0] = mul_rn(dsc, byte_less<0>(v, kF0 + 32.0f));
+                w[i + 1] = mul_rn(dsc, byte_less<1>(v, kF0 + 32.0f));
+                w[i + 2] = mul_rn(dsc, byte_less<2>(v, kF0 + 32.0f));
+                w[i + 3] = mul_rn(dsc, byte_less<3>(v, kF0 + 32.0f));
+            }
+        }
+    }
+};
+
+// four grid bytes times db, each negated where its sign bit is set
+__device__ __forceinline__ void grid4(uint32_t g, float db, uint32_t sign, float* w) {
+    const float v0 = mul_rn(db, byte_less<0>(g, kF0)), v1 = mul_rn(db, byte_less<1>(g, kF0));
+    const float v2 = mul_rn(db, byte_less<2>(g, kF0)), v3 = mul_rn(db, byte_less<3>(g, kF0));
+    w[0] = (sign & 1u) ? -v0 : v0;
+    w[1] = (sign & 2u) ? -v1 : v1;
+    w[2] = (sign & 4u) ? -v2 : v2;
+    w[3] = (sign & 8u) ? -v3 : v3;
+}
+
+template <>
+struct Staged<IQ3_XXS> {
+    __device__ static void run(const uint8_t* row, int n, float* w) {
+        const uint8_t* b = row + (n >> 3) * IQ3_XXS::kBytes;
+        const int ib = n & 7;
+        const uint32_t aux = word_at(b + 66 + 4 * ib);
+        const float db = mul_rn(mul_rn(half_at(b), 0.5f + float(aux >> 28)), 0.5f);
+        const uint32_t q0 = word_at(b + 2 + 8 * ib), q1 = word_at(b + 6 + 8 * ib);
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+            const uint32_t qb = ((l < 4 ? q0 : q1) >> (8 * (l & 3))) & 255u;
+            const uint32_t sign = uint32_t(__ldg(&kKsigns[(aux >> (7 * (l >> 1))) & 127])) >> (4 * (l & 1));
+            grid4(__ldg(&kIq3xxsGrid[qb]), db, sign, w + 4 * l);
+        }
+    }
+};
+
+template <>
+struct Staged<IQ3_S> {
+    __device__ static void run(const uint8_t* row, int n, float* w) {
+        const uint8_t* b = row + (n >> 3) * IQ3_S::kBytes;
+        const int ib = n & 7;
+        const float db = mul_rn(half_at(b), float(1 + 2 * ((b[106 + (ib >> 1)] >> (4 * (ib & 1))) & 15)));
+        const uint32_t high = b[66 + ib];
+        const uint32_t q0 = word_at(b + 2 + 8 * ib), q1 = word_at(b + 6 + 8 * ib);
+        const uint32_t signs = word_at(b + 74 + 4 * ib);
+#pragma unroll
+        for (int l = 0; l < 8; ++l) {
+            const uint32_t qb = ((l < 4 ? q0 : q1) >> (8 * (l & 3))) & 255u;
+            const uint32_t sign = signs >> (4 * l);
+            grid4(__ldg(&kIq3sGrid[qb | (((high >> l) & 1u) << 8)]), db, sign, w + 4 * l);
+        }
+    }
+};
+
+template <>
+struct Staged<IQ4_XS> {
+    __device__ static void run(const uint8_t* row, int n, float* w) {
+        const uint8_t* b = row + (n >> 3) * IQ4_XS::kBytes;
+        const int ib = n & 7;
+        const uint32_t ls = ((b[4 + (ib >> 1)] >> (4 * (ib & 1))) & 15u) | (((u16le(b + 2) >> (2 * ib)) & 3u) << 4);
+        const float dl = mul_rn(half_at(b), float(int(ls) - 32));
+        const uint8_t* q = b + 8 + 16 * ib;
+        // the codebook value k as the float (2^23 + k + 128) - (2^23 + 128)
+        const auto kv = [](uint32_t i) {
+            return __fsub_rn(__int_as_float(0x4B000000 | (int(__ldg(&kKvalues[i])) + 128)), kF0 + 128.0f);
+        };
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+            const uint32_t v = word_at(q + i);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const uint32_t byte = (v >> (8 * j)) & 255u;
+                w[i + j] = mul_rn(dl, kv(byte & 15u));
+                w[16 + i + j] = mul_rn(dl, kv(byte >> 4));
+            }
+        }
+    }
+};
+
 // Dispatch a GGML type id to a functor templated on the block struct. Returns SMOE_EKIND if unknown.
 template <typename F>
 inline int dispatch_kind(int kind, F&& f) {

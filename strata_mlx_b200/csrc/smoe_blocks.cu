@@ -79,14 +79,20 @@ __global__ void __launch_bounds__(kMvThreads) matvec_kernel(const MatvecArgs<T> 
         cp_async_commit();
     }
 
-    // 2. the pair's activations as float32
+    // 2. the pair's activations as float32. Run n's eight float4 chunks are stored permuted (chunk v at
+    // v ^ (n & 7)): the lanes of a warp each read their own run, 128 bytes apart, and without the permutation
+    // every 16-byte read of eight lanes would fall on the same four banks.
+    const auto at = [](int64_t c) {
+        const int64_t n = c >> 5;
+        return (n << 5) | ((((c >> 2) & 7) ^ (n & 7)) << 2) | (c & 3);
+    };
     if (a.gate != nullptr) {
         const T* g = a.gate + p * a.cols;
         const T* u = a.up + p * a.cols;
-        for (int64_t c = threadIdx.x; c < a.cols; c += kMvThreads) xs[c] = to_f32(swiglu_one(g[c], u[c]));
+        for (int64_t c = threadIdx.x; c < a.cols; c += kMvThreads) xs[at(c)] = to_f32(swiglu_one(g[c], u[c]));
     } else {
         const T* x = a.x + (p / a.share) * a.cols;
-        for (int64_t c = threadIdx.x; c < a.cols; c += kMvThreads) xs[c] = to_f32(x[c]);
+        for (int64_t c = threadIdx.x; c < a.cols; c += kMvThreads) xs[at(c)] = to_f32(x[c]);
     }
     __syncthreads();
 
@@ -101,12 +107,12 @@ __global__ void __launch_bounds__(kMvThreads) matvec_kernel(const MatvecArgs<T> 
         float acc = 0.0f;
         for (int n = lane; n < runs; n += 32) {
             float w[32];
-            B::run(row, n, w);
+            Staged<B>::run(row, n, w);
             const float4* xv = reinterpret_cast<const float4*>(xs + 32 * n);
             float s = 0.0f;
 #pragma unroll
             for (int v = 0; v < 8; ++v) {
-                const float4 xq = xv[v];
+                const float4 xq = xv[v ^ (n & 7)];
                 s = fmaf(w[4 * v], xq.x, s);
                 s = fmaf(w[4 * v + 1], xq.y, s);
                 s = fmaf(w[4 * v + 2], xq.z, s);
@@ -116,6 +122,276 @@ __global__ void __launch_bounds__(kMvThreads) matvec_kernel(const MatvecArgs<T> 
         }
         acc = warp_sum(acc);
         if (lane == 0) out[r0 + i] = from_f32<T>(acc);
+    }
+}
+
+// ---------------------------------------------------------------- matvec on int8 dot products
+//
+// The K-types with float16 activations. Every weight of a run is a small integer q times a float scale of its
+// 32 (or 16) weights, less a float minimum of them (gguf-py quants.py:404-552): w = dl q - ml. The pair's
+// activations are split once into two int8 vectors, x = s (hi + lo / 128) with s = max|x| / 127 (|x - that|
+// <= s / 256), so a run's sum is dl s (sum q hi + sum q lo / 128) - ml sum x: the integer sums exact in int32,
+// four products a dp4a, and the float work once per 16 or 32 weights. Results stay within 1e-3 of the largest
+// value of the float64 product, the bar of the tensor-core kernels.
+
+// the 32 activations of run n sit in two 16-byte chunks, the chunks of runs n and n + 4 in swapped order, so
+// that the 8 lanes of a quarter warp (runs n .. n + 7, 32 bytes apart) read 8 different bank groups
+__device__ __forceinline__ int x8_at(int c) {
+    const int n = c >> 5;
+    return (n << 5) | ((((c >> 4) & 1) ^ ((n >> 2) & 1)) << 4) | (c & 15);
+}
+
+// four bytes at byte position p of a row slot (any alignment; reads the aligned word after them too)
+__device__ __forceinline__ uint32_t slot_word(const uint32_t* sw, int p) {
+    return __funnelshift_r(sw[p >> 2], sw[(p >> 2) + 1], 8u * static_cast<uint32_t>(p & 3));
+}
+// eight consecutive words from byte position p
+__device__ __forceinline__ void slot_words8(const uint32_t* sw, int p, uint32_t (&w)[8]) {
+    const uint32_t sh = 8u * static_cast<uint32_t>(p & 3);
+    const uint32_t* a = sw + (p >> 2);
+    uint32_t r[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) r[i] = a[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = __funnelshift_r(r[i], r[i + 1], sh);
+}
+__device__ __forceinline__ float slot_half(const uint32_t* sw, int p) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(slot_word(sw, p) & 0xffffu)));
+}
+
+// s (H + L / 128): a sum of q x from the integer sums against hi and lo
+__device__ __forceinline__ float x8_sum(int hsum, int lsum, float s) {
+    return s * fmaf(float(lsum), 0.0078125f, float(hsum));
+}
+
+// Dot8<B>::run: run n of a row in a slot (sw: the slot's words, p: the byte position of the row's block), the
+// run's activations h / l (eight words of int8 each) and the sums of x over its two 16-column halves
+template <class B>
+struct Dot8 {
+    static constexpr bool kTaken = false;
+};
+
+template <>
+struct Dot8<Q4_K> {
+    static constexpr bool kTaken = true, kMins = true;
+    __device__ static float run(const uint32_t* sw, const uint8_t* b, int p, int n, const uint32_t (&h)[8],
+                                const uint32_t (&l)[8], const float* sx, float s) {
+        const int t = n & 7;
+        float sc, mn;
+        k4_scale_min(b + 4, t, sc, mn);
+        const float dl = mul_rn(slot_half(sw, p), sc), ml = mul_rn(slot_half(sw, p + 2), mn);
+        uint32_t q[8];
+        slot_words8(sw, p + 16 + 32 * (t >> 1), q);
+        const int shift = 4 * (t & 1);
+        int hs = 0, ls = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int v = static_cast<int>((q[i] >> shift) & 0x0F0F0F0Fu);
+            hs = __dp4a(v, static_cast<int>(h[i]), hs);
+            ls = __dp4a(v, static_cast<int>(l[i]), ls);
+        }
+        return fmaf(dl, x8_sum(hs, ls, s), -ml * (sx[0] + sx[1]));
+    }
+};
+
+template <>
+struct Dot8<Q5_K> {
+    static constexpr bool kTaken = true, kMins = true;
+    __device__ static float run(const uint32_t* sw, const uint8_t* b, int p, int n, const uint32_t (&h)[8],
+                                const uint32_t (&l)[8], const float* sx, float s) {
+        const int t = n & 7;
+        float sc, mn;
+        k4_scale_min(b + 4, t, sc, mn);
+        const float dl = mul_rn(slot_half(sw, p), sc), ml = mul_rn(slot_half(sw, p + 2), mn);
+        uint32_t q[8], qh[8];
+        slot_words8(sw, p + 48 + 32 * (t >> 1), q);
+        slot_words8(sw, p + 16, qh);
+        const int shift = 4 * (t & 1);
+        int hs = 0, ls = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int v = static_cast<int>(((q[i] >> shift) & 0x0F0F0F0Fu) | (((qh[i] >> t) & 0x01010101u) << 4));
+            hs = __dp4a(v, static_cast<int>(h[i]), hs);
+            ls = __dp4a(v, static_cast<int>(l[i]), ls);
+        }
+        return fmaf(dl, x8_sum(hs, ls, s), -ml * (sx[0] + sx[1]));
+    }
+};
+
+template <>
+struct Dot8<Q6_K> {
+    static constexpr bool kTaken = true, kMins = false;
+    __device__ static float run(const uint32_t* sw, const uint8_t* b, int p, int n, const uint32_t (&h)[8],
+                                const uint32_t (&l)[8], const float*, float s) {
+        const int r = n & 7, hh = r >> 2, sub = r & 3;
+        uint32_t ql[8], qh[8];
+        slot_words8(sw, p + 64 * hh + 32 * (sub & 1), ql);
+        slot_words8(sw, p + 128 + 32 * hh, qh);
+        const int lshift = 4 * (sub >> 1), hshift = 2 * sub;
+        const float d = slot_half(sw, p + 208);
+        float acc = 0.0f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const float dsc = mul_rn(d, float(int8_t(b[192 + 2 * r + half])));
+            int hs = 0, ls = 0;
+#pragma unroll
+            for (int i = 4 * half; i < 4 * half + 4; ++i) {
+                const uint32_t u = ((ql[i] >> lshift) & 0x0F0F0F0Fu) | (((qh[i] >> hshift) & 0x03030303u) << 4);
+                const int v = static_cast<int>(__vsub4(u, 0x20202020u));  // q - 32 in each byte
+                hs = __dp4a(v, static_cast<int>(h[i]), hs);
+                ls = __dp4a(v, static_cast<int>(l[i]), ls);
+            }
+            acc = fmaf(dsc, x8_sum(hs, ls, s), acc);
+        }
+        return acc;
+    }
+};
+
+template <>
+struct Dot8<Q2_K> {
+    static constexpr bool kTaken = true, kMins = true;
+    __device__ static float run(const uint32_t* sw, const uint8_t* b, int p, int n, const uint32_t (&h)[8],
+                                const uint32_t (&l)[8], const float* sx, float s) {
+        const int r = n & 7;
+        uint32_t q[8];
+        slot_words8(sw, p + 16 + 32 * (r >> 2), q);
+        const int shift = 2 * (r & 3);
+        const float d = slot_half(sw, p + 80), dmin = slot_half(sw, p + 82);
+        float acc = 0.0f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const uint32_t sc = b[2 * r + half];
+            const float dl = mul_rn(d, float(sc & 15)), ml = mul_rn(dmin, float(sc >> 4));
+            int hs = 0, ls = 0;
+#pragma unroll
+            for (int i = 4 * half; i < 4 * half + 4; ++i) {
+                const int v = static_cast<int>((q[i] >> shift) & 0x03030303u);
+                hs = __dp4a(v, static_cast<int>(h[i]), hs);
+                ls = __dp4a(v, static_cast<int>(l[i]), ls);
+            }
+            acc = fmaf(dl, x8_sum(hs, ls, s), fmaf(-ml, sx[half], acc));
+        }
+        return acc;
+    }
+};
+
+template <>
+struct Dot8<Q3_K> {
+    static constexpr bool kTaken = true, kMins = false;
+    __device__ static float run(const uint32_t* sw, const uint8_t* b, int p, int n, const uint32_t (&h)[8],
+                                const uint32_t (&l)[8], const float*, float s) {
+        const int r = n & 7;
+        uint32_t q[8], hm[8];
+        slot_words8(sw, p + 32 + 32 * (r >> 2), q);
+        slot_words8(sw, p, hm);
+        const int shift = 2 * (r & 3);
+        const float d = slot_half(sw, p + 108);
+        float acc = 0.0f;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const float dl = mul_rn(d, Q3_K::scale(b + 96, 2 * r + half));
+            int hs = 0, ls = 0;
+#pragma unroll
+            for (int i = 4 * half; i < 4 * half + 4; ++i) {
+                // q + 4 where bit r of hmask is set, q where it is clear; less 4
+                const uint32_t u = ((q[i] >> shift) & 0x03030303u) | (((hm[i] >> r) & 0x01010101u) << 2);
+                const int v = static_cast<int>(__vsub4(u, 0x04040404u));
+                hs = __dp4a(v, static_cast<int>(h[i]), hs);
+                ls = __dp4a(v, static_cast<int>(l[i]), ls);
+            }
+            acc = fmaf(dl, x8_sum(hs, ls, s), acc);
+        }
+        return acc;
+    }
+};
+
+template <class B>
+__global__ void __launch_bounds__(kMvThreads) matvec8_kernel(const MatvecArgs<__half> a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int64_t cols = a.cols;
+    int8_t* xh = reinterpret_cast<int8_t*>(smem);
+    int8_t* xl = xh + cols;
+    float* sx = reinterpret_cast<float*>(smem + 2 * cols);  // sum of x over each 16 columns
+    float* red = sx + cols / 16;                             // 8 warps' maxima, then s
+    uint8_t* slots = smem + ((2 * cols + (cols / 16) * 4 + 64 + 15) & ~int64_t(15));
+
+    const int prob = blockIdx.z;
+    const int64_t p = blockIdx.y;
+    const uint32_t e = a.idx[p];
+    if (e >= a.experts) return;  // a pair that names no expert is left out
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t rows_per_cta = int64_t(kMvWarps) * a.rows_per_warp;
+    const int64_t r0 = blockIdx.x * rows_per_cta + int64_t(warp) * a.rows_per_warp;
+    const int nr = static_cast<int>(max(int64_t(0), min(int64_t(a.rows_per_warp), a.rows - r0)));
+
+    // 1. this warp's rows -> its slots
+    const uint8_t* base = (prob ? a.blocks[1] : a.blocks[0]) + (int64_t(e) * a.rows) * a.row_bytes;
+    uint8_t* my = slots + int64_t(warp) * a.rows_per_warp * a.stage;
+    for (int i = 0; i < a.rows_per_warp; ++i) {
+        if (i < nr) stage_bytes(my + i * a.stage, base + (r0 + i) * a.row_bytes, a.row_bytes, prob ? a.end[1] : a.end[0], lane, 32);
+        cp_async_commit();
+    }
+
+    // 2. the pair's activations split into int8 hi / lo with one scale s = max|x| / 127
+    const __half* g = a.gate ? a.gate + p * cols : nullptr;
+    const __half* u = a.up ? a.up + p * cols : nullptr;
+    const __half* x = a.gate ? nullptr : a.x + (p / a.share) * cols;
+    const auto value = [&](int64_t c) { return __half2float(g ? swiglu_one(g[c], u[c]) : x[c]); };
+    uint32_t m = 0;  // max |x| as bits (non-negative floats order as integers; a NaN orders above inf)
+    for (int64_t c = threadIdx.x; c < cols; c += kMvThreads) m = max(m, __float_as_uint(fabsf(value(c))));
+    m = __reduce_max_sync(0xffffffffu, m);
+    if (lane == 0) reinterpret_cast<uint32_t*>(red)[warp] = m;
+    __syncthreads();
+    m = 0;
+#pragma unroll
+    for (int w = 0; w < kMvWarps; ++w) m = max(m, reinterpret_cast<uint32_t*>(red)[w]);
+    const float xmax = __uint_as_float(m);
+    const float s = xmax / 127.0f;  // (inf or NaN when x is: the products come out NaN)
+    const float inv = xmax > 0.0f ? 127.0f / xmax : 0.0f;
+    for (int64_t c = threadIdx.x; c < cols; c += kMvThreads) {
+        const float v = value(c) * inv;
+        const float hi = rintf(v);
+        const int at = x8_at(static_cast<int>(c));
+        xh[at] = static_cast<int8_t>(__float2int_rn(hi));
+        xl[at] = static_cast<int8_t>(__float2int_rn((v - hi) * 128.0f));
+    }
+    __syncthreads();
+    if constexpr (Dot8<B>::kMins) {
+        for (int64_t gi = threadIdx.x; gi < cols / 16; gi += kMvThreads) {
+            int hs = 0, ls = 0;
+            for (int j = 0; j < 16; ++j) {
+                const int at = x8_at(static_cast<int>(16 * gi + j));
+                hs += xh[at];
+                ls += xl[at];
+            }
+            sx[gi] = x8_sum(hs, ls, s);
+        }
+        __syncthreads();
+    }
+
+    // 3. decode and reduce, a row at a time as its bytes land
+    const int runs = static_cast<int>(cols >> 5);
+    __half* out = (prob ? a.out[1] : a.out[0]) + p * a.rows;
+    const uint4* xh4 = reinterpret_cast<const uint4*>(xh);
+    const uint4* xl4 = reinterpret_cast<const uint4*>(xl);
+    for (int i = 0; i < nr; ++i) {
+        cp_async_wait_dyn(a.rows_per_warp - 1 - i);
+        __syncwarp();
+        const int off = static_cast<int>(reinterpret_cast<uintptr_t>(base + (r0 + i) * a.row_bytes) & 15);
+        const uint8_t* slot = my + i * a.stage;
+        const uint32_t* sw = reinterpret_cast<const uint32_t*>(slot);
+        float acc = 0.0f;
+        for (int n = lane; n < runs; n += 32) {
+            const int swz = (n >> 2) & 1;
+            const uint4 h0 = xh4[2 * n + swz], h1 = xh4[2 * n + (swz ^ 1)];
+            const uint4 l0 = xl4[2 * n + swz], l1 = xl4[2 * n + (swz ^ 1)];
+            const uint32_t hw[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+            const uint32_t lw[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+            const int pos = off + (n >> 3) * B::kBytes;
+            acc += Dot8<B>::run(sw, slot + pos, pos, n, hw, lw, sx + 2 * n, s);
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) out[r0 + i] = __float2half_rn(acc);
     }
 }
 
@@ -147,7 +423,8 @@ static int launch_matvec(int kind0, int kind1, MatvecArgs<T> a, int nprob, cudaS
     a.stage = static_cast<int>((a.row_bytes + 16 + 15) & ~int64_t(15));
     // about 64 KB of rows in flight per CTA, at most 4 rows a warp
     int rpw = static_cast<int>(std::min<int64_t>(4, std::max<int64_t>(1, (64 << 10) / (int64_t(kMvWarps) * a.stage))));
-    int64_t smem = xs_bytes + int64_t(kMvWarps) * rpw * a.stage;
+    // (+16: the staged decoders read whole aligned words, up to 3 bytes past the end of a row's slot)
+    int64_t smem = xs_bytes + int64_t(kMvWarps) * rpw * a.stage + 16;
     SMOE_REQUIRE(smem <= 200 * 1024, SMOE_ESHAPE, "rows too long for the staged matvec");
     a.rows_per_warp = rpw;
     const int64_t rows_per_cta = int64_t(kMvWarps) * rpw;
@@ -155,6 +432,15 @@ static int launch_matvec(int kind0, int kind1, MatvecArgs<T> a, int nprob, cudaS
     SMOE_REQUIRE(a.pairs <= 65535, SMOE_ESHAPE, "more than 65535 pairs in one matvec call");
     int status = dispatch_kind(kind0, [&](auto blk) {
         using B = decltype(blk);
+        if constexpr (sizeof(T) == 2 && Dot8<B>::kTaken) {
+            // the int8 activations, the sums of x per 16 columns and 8 maxima take the float32 row's place
+            const int64_t xs8 = (2 * a.cols + (a.cols / 16) * 4 + 64 + 15) & ~int64_t(15);
+            const int64_t smem8 = smem - xs_bytes + xs8;
+            auto kern = matvec8_kernel<B>;
+            max_smem(kern, static_cast<int>(smem8));
+            kern<<<grid, kMvThreads, smem8, st>>>(a);
+            return;
+        }
         auto kern = matvec_kernel<B, T>;
         max_smem(kern, static_cast<int>(smem));
         kern<<<grid, kMvThreads, smem, st>>>(a);

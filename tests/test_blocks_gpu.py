@@ -107,6 +107,26 @@ def test_float16_products_on_the_tensor_core_path(cuda, kind, rows, cols, share)
     assert np.abs(got.reshape(idx.size, rows) - want).max() <= 1e-3 * np.abs(want).max()
 
 
+@pytest.mark.parametrize("kind", ["Q2_K", "Q3_K", "Q4_K", "Q5_K", "Q6_K"])
+@pytest.mark.parametrize("rows, cols", [(40, 512), (1536, 4096), (4096, 1536), (16, 256)])
+@pytest.mark.parametrize("share", [1, 8])
+def test_float16_products_of_the_k_types_on_int8_dot_products(cuda, kind, rows, cols, share):
+    """The K-types with float16 activations (the activations split into int8 hi / lo, integer dot products,
+    float scales and minimums per 16 or 32 weights) against the float64 product: within 1e-3 of the largest
+    value, the bar of the tensor-core kernels (the split keeps x to 1/256 of max|x| / 127)."""
+    rng = np.random.default_rng(rows + cols + share + len(kind))
+    E, pairs = 5, 8
+    b, w = stack(kind, rng, E, rows, cols, scale=(-0.05, 0.05))
+    layer = B.BlockSwitchLinear(dev(b), kind, (E, rows, cols))
+    idx = rng.integers(0, E, pairs // share * share).reshape(-1, share)
+    x = rng.standard_normal((pairs // share, cols)).astype(np.float16)
+    xs = x[:, None, None, :] if share > 1 else x[:, None, :]
+    got = layer(dev(xs if share > 1 else x.reshape(pairs // share, share, 1, cols)), dev(idx)).float().cpu().numpy()
+    want = np.einsum("pri,pi->pr", w[idx.reshape(-1)].astype(np.float64),
+                     x.astype(np.float64)[np.arange(idx.size) // share])
+    assert np.abs(got.reshape(idx.size, rows) - want).max() <= 1e-3 * np.abs(want).max()
+
+
 def test_half_precision_activations_come_back_as_half(cuda):
     """tests/test_blocks.py:63-70."""
     rng = np.random.default_rng(5)
@@ -196,7 +216,7 @@ def test_gate_and_up_in_one_launch_are_two_launches(cuda):
     assert torch.equal(g, gate(x5, idx).reshape(6, -1)) and torch.equal(u, up(x5, idx).reshape(6, -1))
 
 
-@pytest.mark.parametrize("kind", ["IQ3_S", "IQ2_XS", "IQ4_NL", "Q2_K", "Q8_0"])
+@pytest.mark.parametrize("kind", ["IQ3_S", "IQ2_XS", "IQ4_NL", "Q2_K", "Q5_K", "Q8_0"])
 @pytest.mark.parametrize("tokens", [1, 20])
 def test_down_taking_swiglu_itself_and_unsorted_pairs_give_the_same_bits(cuda, monkeypatch, kind, tokens):
     """tests/test_blocks.py:257-280: the BLOCK_GLU path (swiglu formed in down) == down(swiglu(g, u))."""
