@@ -51,6 +51,13 @@ def _args():
     p.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
     p.add_argument("--only-prefill", action="store_true", help="only the config-3 prefill measurement (profiling)")
     p.add_argument("--no-verify", action="store_true", help="skip the config-4 verify-pass measurement")
+    p.add_argument("--ep-prefill", action="store_true", help="with --gpus N > 1: config 3 over the N ranks "
+                   "(all-to-all dispatch); on one GPU config 3 always runs")
+    p.add_argument("--stack", action="store_true", help="with --gpus N > 1: config 5 (the 26-layer stack, "
+                   "experts sharded over the ranks); on one GPU it always runs unless --no-stack")
+    p.add_argument("--no-stack", action="store_true", help="skip the config-5 stack measurement")
+    p.add_argument("--only-stack", action="store_true", help="only the config-5 stack measurement")
+    p.add_argument("--stack-layers", type=int, default=26)
     p.add_argument("--only-verify", action="store_true", help="only the config-4 verify-pass measurement")
     p.add_argument("--only-matvec", metavar="KIND", help="profiling: the CUDA-core matvec of config 4's down "
                    "product (40 pairs of 5 tokens, 64 experts of 4096 x 1536 KIND blocks), a few launches")
@@ -324,6 +331,122 @@ def run_verify(device, seed, steps=50, warmup=5, n_layers=8, tokens=5):
             "ms_per_pass": ms, "tokens_per_s": tokens / (ms * 1e-3),
             "token_layers_per_s": tokens * n_layers / (ms * 1e-3), "bytes_per_pass": total_bytes,
             "achieved_gbs": gbs, "hbm_peak_gbs": peak, "frac": gbs / peak}
+
+
+def run_stack(args, rank, world, local_rank, prompt=32768, chunk=2048, decode_steps=20):
+    """Configuration 5 of the benchmark: the expert-parallel stack. `--stack-layers` (26) MoE layers of 256 IQ3_S
+    experts (2.08 GB of routed blocks a layer), experts sharded E / world per rank, the Q8_0 shared expert of ffn
+    4096, router N(0, 0.02); a prompt of 32,768 tokens in chunks of 2,048 (each rank takes its share of every
+    chunk: `ExpertParallelPrompt`, all-to-all dispatch and return; one GPU: `SparseMoeBlock`), then decoding at
+    batch 1 and 8 (each layer one CUDA graph; several GPUs: `ExpertParallelMoE`, one all-reduce a layer).
+    Every layer takes the same chunk / tokens (random layers chained would overflow float16). Times are CUDA
+    events, the maximum over ranks. Prefill tokens/s counts the prompt's tokens (all ranks); decode tokens/s
+    counts the batch's tokens through the whole stack."""
+    import torch
+
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200 import fused as Fz
+    from strata_mlx_b200 import parallel as P
+
+    device = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist  # noqa: F811
+    g = torch.Generator(device=device)
+    g.manual_seed(args.seed + 4099 + 7919 * rank)
+    e_loc = E // world
+
+    def random_blocks(kind, n_weights):
+        per, nbytes = B.BLOCK[kind]
+        n = n_weights // per
+        b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=g)
+        b[:, 0:2] = (torch.randn(n, device=device, generator=g) * SIGMA).abs().half().view(torch.uint8).view(n, 2)
+        return b.reshape(-1)
+
+    prompt_blocks, decode_blocks = [], []
+    for _ in range(args.stack_layers):
+        sw = B.BlockSwitchGLU(B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H)),
+                              B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H)),
+                              B.BlockSwitchLinear(random_blocks(KIND, e_loc * H * F_), KIND, (e_loc, H, F_)))
+        shared = [(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+                  (random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+                  (random_blocks(SHARED_KIND, H * FS), SHARED_KIND, (H, FS))]
+        router = (torch.randn(E, H, device=device, generator=g) * 0.02).half()
+        sgate = (torch.randn(1, H, device=device, generator=g) * 0.02).half()
+        if world > 1:  # every rank routes with the same router and gate
+            dist.broadcast(router, 0)
+            dist.broadcast(sgate, 0)
+        whole = B.BlockMLP(*(B.BlockLinear(b, k, s) for b, k, s in shared))
+        prompt_layer = Fz.SparseMoeBlock(router, sw, whole, sgate, K)
+        if world == 1:
+            prompt_blocks.append(prompt_layer)
+            decode_blocks.append(prompt_layer)
+            continue
+        lo, n = P.expert_range(rank, world, FS)
+        (gb, gk, gs), (ub, uk, us), (db, dk, ds) = shared
+        sliced = B.BlockMLP(B.BlockLinear(P.slice_rows(gb, gk, gs, lo, lo + n), gk, (n, H)),
+                            B.BlockLinear(P.slice_rows(ub, uk, us, lo, lo + n), uk, (n, H)),
+                            B.BlockLinear(P.slice_cols(db, dk, ds, lo, lo + n), dk, (H, n)))
+        prompt_blocks.append(P.ExpertParallelPrompt(prompt_layer, rank, world, E))
+        decode_blocks.append(P.ExpertParallelMoE(Fz.SparseMoeBlock(router, sw, sliced, sgate, K), rank, world, E))
+
+    gx = torch.Generator(device=device)
+    gx.manual_seed(args.seed + 5)
+    chunk_x = torch.randn(chunk, H, device=device, generator=gx).half()
+    mine = chunk_x[rank * chunk // world : (rank + 1) * chunk // world].contiguous()
+
+    def world_max(v):
+        t = torch.tensor([v], device=device)
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # prefill: every chunk through every layer
+    for blk in prompt_blocks[:2]:
+        blk(mine)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(prompt // chunk):
+        for blk in prompt_blocks:
+            blk(mine)
+    e1.record()
+    torch.cuda.synchronize()
+    prefill_ms = world_max(e0.elapsed_time(e1))
+    received = [blk.received for blk in prompt_blocks] if world > 1 else None
+
+    out = {"workload": f"config 5: {args.stack_layers} MoE layers x 256 IQ3_S experts sharded over {world} GPU(s), "
+                       f"shared expert ffn 4096 Q8_0; prefill {prompt} tokens in chunks of {chunk}, then decode at "
+                       "batch 1 and 8, one CUDA graph a layer",
+           "prefill_ms": prefill_ms, "prefill_tokens_per_s": prompt / (prefill_ms * 1e-3)}
+    if received is not None:
+        out["prefill_pairs_last_chunk_rank_layer0"] = received[0]
+    for batch in (1, 8):
+        xb = torch.randn(batch, H, device=device, generator=gx).half()
+        if dist:
+            dist.broadcast(xb, 0)
+        graphs = [Fz.GraphedBlock(blk, batch, H, torch.float16, device) for blk in decode_blocks]
+        for gb in graphs:
+            gb.x.copy_(xb)
+        for gb in graphs:
+            gb.graph.replay()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0.record()
+        for _ in range(decode_steps):
+            for gb in graphs:
+                gb.graph.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = world_max(e0.elapsed_time(e1) / decode_steps)
+        out[f"decode_bs{batch}_ms_per_token_step"] = ms
+        out[f"decode_bs{batch}_tokens_per_s"] = batch / (ms * 1e-3)
+        del graphs
+        torch.cuda.synchronize()
+    return out
 
 
 def run_matvec(kind, seed, steps=3, warmup=3, experts=64, tokens=5):
@@ -658,6 +781,9 @@ def main():
         print(json.dumps({"matvec": run_matvec(args.only_matvec, args.seed + 299, steps=args.steps,
                                                warmup=args.warmup)}))
         return
+    if args.only_stack and world == 1:
+        print(json.dumps({"stack": run_stack(args, 0, 1, local_rank)}))
+        return
     if args.only_verify:
         import torch
 
@@ -683,12 +809,16 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         line = run_ours(args, rank, world, local_rank)
-        if world > 1 and not args.no_prefill:
+        if world > 1 and args.ep_prefill and not args.no_prefill:
             import torch
 
             pf = run_prefill(torch.device("cuda", local_rank), args.seed + 99, rank=rank, world=world)
             if line is not None:
                 line["prefill"] = pf
+        if world > 1 and args.stack and not args.no_stack:
+            st = run_stack(args, rank, world, local_rank)
+            if line is not None:
+                line["stack"] = st
     finally:
         if world > 1:
             import torch.distributed as dist
@@ -713,6 +843,8 @@ def main():
             import torch
 
             line["verify"] = run_verify(torch.device("cuda", local_rank), args.seed + 199)
+        if world == 1 and not args.no_stack:
+            line["stack"] = run_stack(args, rank, world, local_rank)
         print(json.dumps(line))
 
 

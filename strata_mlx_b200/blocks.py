@@ -223,8 +223,8 @@ def _tiled_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.
 
 # types whose float16 products run on the tensor-core decode kernel, with the columns of its stage
 MMA_MATVEC = {"IQ3_S": 256, "Q8_0": 128}
-# the int8 tensor-core decode kernel forms the SwiGLU of down's input itself when the activations (as int8
-# pairs) fit in its shared memory: types, the columns it splits the activations by, the bytes it may hold
+# the int8 tensor-core decode kernel forms the SwiGLU of down's input itself: types, the columns it splits the
+# activations by, and the bytes of activations the shared down product with the combine may hold (one launch)
 FUSED_GLU = ("IQ3_S", "Q8_0")
 FUSED_GLU_COLS, FUSED_GLU_BYTES = 256, 64 << 10
 BATCHED_DOWN = False  # decode_products: the routed and the shared down product in one launch
@@ -244,8 +244,8 @@ def matvec_glu(lin, idx: torch.Tensor, gate: torch.Tensor, up: torch.Tensor):
     _lib.require_cuda(idx, gate, up, lin.blocks)
     idx = _flat_idx(idx)
     pairs = idx.numel()
-    fused = (gate.dtype == torch.float16 and lin.kind in FUSED_GLU and lin.input_dims % FUSED_GLU_COLS == 0
-             and pairs * lin.input_dims * 2 <= FUSED_GLU_BYTES)
+    # (the kernel takes the pairs in as many launches as their activations need)
+    fused = gate.dtype == torch.float16 and lin.kind in FUSED_GLU and lin.input_dims % FUSED_GLU_COLS == 0
     if not fused and gate.dtype == torch.float16 and lin.input_dims % MMA_MATVEC.get(lin.kind, 1 << 30) == 0:
         h = swiglu(gate.reshape(pairs, -1), up.reshape(pairs, -1))
         return _matvec(lin, h, idx, 1, gate.dtype)

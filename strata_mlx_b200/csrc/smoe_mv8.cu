@@ -845,12 +845,34 @@ int mv8_glu_combine(int kind, const uint8_t* blocks, int64_t rows, int64_t cols,
                     st, y, w, g, k);
 }
 
-// One or two problems (gate and up) of the existing entry points: the single-stack kernel.
+// One or two problems (gate and up) of the existing entry points: the single-stack kernel. Pairs whose
+// activations do not fit one launch's shared memory (or its warps' job tables) go in equal launches of a
+// multiple of `share` pairs each; every pair's result is the one a single launch would give.
 int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,
             int64_t row_bytes, const uint32_t* idx, int64_t pairs, int64_t share, const __half* x, const __half* gate,
             const __half* up, __half* o0, __half* o1, int nprob, cudaStream_t st) {
-    return mv8s_try(kind0, kind1, b0, b1, experts, rows, cols, row_bytes, idx, pairs, share, x, gate, up, o0, o1, nprob,
-                    st);
+    const auto part = [&](int64_t p0, int64_t n) {
+        const int64_t x0 = p0 / share * cols;
+        return mv8s_try(kind0, kind1, b0, b1, experts, rows, cols, row_bytes, idx + p0, n, share, x ? x + x0 : nullptr,
+                        gate ? gate + p0 * cols : nullptr, up ? up + p0 * cols : nullptr, o0 + p0 * rows,
+                        o1 + p0 * rows, nprob, st);
+    };
+    int r = part(0, pairs);
+    if (r != 1 || share < 1 || pairs <= share || pairs % share) return r;
+    for (int64_t parts = 2; parts <= 64; parts *= 2) {
+        const int64_t n = ((pairs / share + parts - 1) / parts) * share;  // pairs a launch
+        if (n >= pairs) continue;
+        r = part(0, n);
+        if (r == 1) continue;
+        if (r != 0) return r;
+        for (int64_t p0 = n; p0 < pairs; p0 += n) {
+            r = part(p0, std::min(n, pairs - p0));
+            if (r == 1) return fail(SMOE_ESHAPE, "matvec: a part of the pairs was not taken");
+            if (r != 0) return r;
+        }
+        return 0;
+    }
+    return 1;
 }
 
 }  // namespace smoe
