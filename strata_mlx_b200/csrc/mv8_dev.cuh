@@ -70,7 +70,7 @@ constexpr int kM8GridRep = 16;  // copies of the IQ3_S grid in shared memory (th
 template <int NB, int REP = kM8GridRep>
 struct M8IQ3S {
     static constexpr int kKind = 21, kStageCols = 256 * NB, kStageBytes = 110 * NB, kRS = NB == 2 ? 240 : 144;
-    static constexpr bool kLut = true;
+    static constexpr bool kLut = true, kTokens = false;
     // run R of the stage: the two rows' groups (bq / bs: the lane's qs / sign bytes), lutl = this lane's grid copy
     template <int R>
     __device__ static __forceinline__ void run(const uint32_t (&bq)[2], const uint32_t (&bs)[2], const uint32_t (&qh)[2][2],
@@ -161,7 +161,7 @@ __device__ __forceinline__ void m8_fill_grid(uint32_t* lut) {
 // (34 bytes: d 0, qs 2..33.) A stage is four runs; in run r lane tig takes codes 8 tig .. 8 tig + 7.
 struct M8Q8_0 {
     static constexpr int kKind = 8, kStageCols = 128, kStageBytes = 136, kRS = 176;
-    static constexpr bool kLut = false;
+    static constexpr bool kLut = false, kTokens = true;
     __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t*,
                                  const uint8_t* xh, const uint8_t* xl, const float* xs, float (&total)[2]) {
         const uint8_t* rb[2] = {r0, r1};
@@ -183,6 +183,38 @@ struct M8Q8_0 {
             }
             uint2 b = make_uint2(0u, 0u);
             if (gid < 2) b = *reinterpret_cast<const uint2*>(xsrc + 32 * r + 8 * tig);
+            int acc[4];
+            mma_s8(acc, a[0][0], a[1][0], a[0][1], a[1][1], b.x, b.y);
+            total[0] = fmaf(d[0] * k, static_cast<float>(acc[0] * 128 + acc[1]), total[0]);
+            total[1] = fmaf(d[1] * k, static_cast<float>(acc[2] * 128 + acc[3]), total[1]);
+        }
+    }
+    // The same stage for nt <= 4 tokens of one expert, their activation rows xstride bytes (and xsstride
+    // scales) apart: column 2t of B holds token t's hi, column 2t + 1 its lo, so lane tig of a quad receives
+    // token tig's two sums, and its total is token tig's (tig < nt). One pass over the weights for all nt.
+    __device__ static void stage_tokens(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint8_t* xh,
+                                        const uint8_t* xl, int64_t xstride, const float* xs, int xsstride, int nt,
+                                        float (&total)[2]) {
+        const uint8_t* rb[2] = {r0, r1};
+        const int t = gid >> 1;
+        const uint8_t* xsrc = ((gid & 1) ? xl : xh) + int64_t(t) * xstride;
+        const float k = tig < nt ? xs[tig * xsstride] * (1.0f / 128.0f) : 0.0f;
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            uint32_t a[2][2];
+            float d[2];
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const uint8_t* p = rb[j] + 34 * r + 2 + 8 * tig;
+                const uint32_t* w = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
+                const uint32_t sh = 8u * static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 3u);
+                const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+                a[j][0] = __funnelshift_r(w0, w1, sh);
+                a[j][1] = __funnelshift_r(w1, w2, sh);
+                d[j] = h2f(lds_u16(rb[j] + 34 * r));
+            }
+            uint2 b = make_uint2(0u, 0u);
+            if (t < nt) b = *reinterpret_cast<const uint2*>(xsrc + 32 * r + 8 * tig);
             int acc[4];
             mma_s8(acc, a[0][0], a[1][0], a[0][1], a[1][1], b.x, b.y);
             total[0] = fmaf(d[0] * k, static_cast<float>(acc[0] * 128 + acc[1]), total[0]);

@@ -58,6 +58,9 @@ struct M8Args {
     // bit 0: idx, bit 1: the activations may be read before pdl_wait (the launch just before this one does not
     // write them), so the first weight copies and the activation split overlap that launch's end
     int early;
+    // pairs a job takes: 1, or up to 4 for a one-expert stack whose pairs each have their own activation row
+    // (the shared expert over several tokens: the weights are read and expanded once for all of them)
+    int tok;
 };
 // a job's place (worked out once per job, 32-bit): problem, pair, expert, the tile's residue class and block
 // of 16 q rows, the first row of its TMA box, the activation row
@@ -80,8 +83,8 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     const int ns = a.nslots;
     uint8_t* ring = sm;                                                         // [warp][slot] 16 rows x kRS
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + size_t(kM8Warps) * ns * kSlot);  // [warp][slot]
-    float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);       // [16 warps][16 rows]
-    uint8_t* spare = reinterpret_cast<uint8_t*>(red + kM8Warps * 16);           // kM8WhereSBytes
+    float* red = reinterpret_cast<float*>(bars + kM8Warps * kM8MaxSlots);       // [16 warps][4 pairs][16 rows]
+    uint8_t* spare = reinterpret_cast<uint8_t*>(red + kM8Warps * 64);           // kM8WhereSBytes
     uint32_t* need = reinterpret_cast<uint32_t*>(spare + kM8WhereSBytes - kM8SMaskRows / 8);  // kM8SMaskRows bits
     uint32_t* lut = reinterpret_cast<uint32_t*>(spare + kM8WhereSBytes);        // 512 x 16 words
     const int xblocks = static_cast<int>(a.cols / kM8XBlock);
@@ -102,7 +105,9 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     const int cj1 = static_cast<int>(int64_t(blockIdx.x + 1) * a.jobs / gridDim.x);
     const int q0 = cj0 + tid_team;
     const int my_jobs = q0 < cj1 ? min((cj1 - q0 + teams - 1) / teams, 32) : 0;
-    const int per_prob = static_cast<int>(a.pairs) * a.tiles;  // < 2^30 (the host checks)
+    const int tok = a.tok;
+    const int units = static_cast<int>((a.pairs + tok - 1) / tok);  // a job's pairs: [unit tok, unit tok + tok)
+    const int per_prob = units * a.tiles;  // < 2^30 (the host checks)
     uint8_t* my_ring = ring + size_t(warp) * ns * kSlot;
     uint64_t* my_bars = bars + warp * kM8MaxSlots;
 
@@ -132,15 +137,22 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     }
     auto place = [&]() {
         if (has) {
-            const uint32_t e = __ldg(a.idx + j_pair);
+            const uint32_t e = __ldg(a.idx + int64_t(j_pair) * tok);
             j_valid = e < a.experts ? 1 : 0;
             j_y = static_cast<int>((int64_t(j_valid ? e : 0) * a.rows) >> a.lq) + 16 * j_blk;
         }
     };
     __syncthreads();
     if (masked && has && my_stages > 0) {
-        const int xr = j_pair / static_cast<int>(a.share);
-        atomicOr(&need[xr >> 5], 1u << (xr & 31));
+        if (tok == 1) {
+            const int xr = j_pair / static_cast<int>(a.share);
+            atomicOr(&need[xr >> 5], 1u << (xr & 31));
+        } else {
+            for (int t = 0; t < tok && j_pair * tok + t < a.xrows; ++t) {
+                const int xr = j_pair * tok + t;
+                atomicOr(&need[xr >> 5], 1u << (xr & 31));
+            }
+        }
     }
     __syncthreads();
 
@@ -216,7 +228,8 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         const int cls = __shfl_sync(0xffffffffu, j_cls, job);
         const int blk = __shfl_sync(0xffffffffu, j_blk, job);
         const int valid = __shfl_sync(0xffffffffu, j_valid, job);
-        const int xr = pair / static_cast<int>(a.share);
+        const int xr = tok == 1 ? pair / static_cast<int>(a.share) : pair * tok;
+        const int nt = tok == 1 ? 1 : min(tok, static_cast<int>(a.pairs) - pair * tok);
         const uint8_t* xh = reinterpret_cast<const uint8_t*>(xhi) + int64_t(xr) * a.cols;
         const uint8_t* xl = reinterpret_cast<const uint8_t*>(xlo) + int64_t(xr) * a.cols;
         const float* xsc = xscale + xr * xblocks;
@@ -235,27 +248,38 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
             }
             if (!ok || !valid) continue;
             const uint8_t* st = my_ring + cur * kSlot + (pos & 15);
+            if constexpr (D::kTokens) {
+                if (tok > 1) {
+                    D::stage_tokens(st + gid * D::kRS, st + (gid + 8) * D::kRS, tig, gid, xh + xc, xl + xc, a.cols,
+                                    xsc + xc / kM8XBlock, xblocks, nt, total);
+                    continue;
+                }
+            }
             D::stage(st + gid * D::kRS, st + (gid + 8) * D::kRS, tig, gid, lut, xh + xc, xl + xc,
                      xsc + xc / kM8XBlock, total);
         }
-        // the team's partial sums of this job's 16 rows, added in warp order
-        float* rq = red + (tid_team * team) * 16;
-        if (tig == 0) {
-            rq[kq * 16 + gid] = total[0];
-            rq[kq * 16 + gid + 8] = total[1];
+        // the team's partial sums of this job's 16 rows (for each of its pairs: lane tig holds pair tig's),
+        // added in warp order
+        float* rq = red + (tid_team * team) * 64;
+        if (tig < nt) {
+            rq[(kq * 4 + tig) * 16 + gid] = total[0];
+            rq[(kq * 4 + tig) * 16 + gid + 8] = total[1];
         }
         total[0] = total[1] = 0.f;
         team_sync();
         if (kq == 0 && lane < 16) {
             const int64_t row = int64_t(blk) * 16 * a.q + cls + int64_t(a.q) * lane;
             if (valid && row < a.rows) {
-                float v = rq[lane];
-                for (int i = 1; i < team; ++i) v += rq[16 * i + lane];
-                const __half prod = __float2half_rn(v);
-                __half* o = (prob ? a.out[1] : a.out[0]) + int64_t(pair) * a.rows + row;
-                if (a.cy == nullptr) *o = prod;
-                else *o = combine_one(a.cy + int64_t(pair) * a.ck * a.rows + row, a.rows, a.cw + int64_t(pair) * a.ck,
-                                      a.ck, a.cg[pair], prod);
+                for (int t = 0; t < nt; ++t) {
+                    float v = rq[t * 16 + lane];
+                    for (int i = 1; i < team; ++i) v += rq[(i * 4 + t) * 16 + lane];
+                    const __half prod = __float2half_rn(v);
+                    const int64_t pp = tok == 1 ? pair : int64_t(pair) * tok + t;
+                    __half* o = (prob ? a.out[1] : a.out[0]) + pp * a.rows + row;
+                    if (a.cy == nullptr) *o = prod;
+                    else *o = combine_one(a.cy + pp * a.ck * a.rows + row, a.rows, a.cw + pp * a.ck, a.ck, a.cg[pp],
+                                          prod);
+                }
             }
         }
         team_sync();
@@ -586,7 +610,7 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         const int64_t xrows = (pairs + share - 1) / share;
         const int xblocks = static_cast<int>(cols / kM8XBlock);
         const size_t xbytes = size_t(((xrows * xblocks + 3) & ~int64_t(3)) * 4) + size_t(xrows * cols * 2);
-        const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + kM8WhereSBytes +
+        const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 64 * 4 + kM8WhereSBytes +
                              (D::kLut ? 8192 * 4 : 0) + xbytes;
         const size_t slot = size_t(kM8Warps) * 16 * D::kRS;
         int ns = kM8MaxSlots;
@@ -623,7 +647,8 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         a.q = q;
         a.lq = q == 1 ? 0 : q == 2 ? 1 : q == 4 ? 2 : q == 8 ? 3 : 4;
         a.tiles = static_cast<int>((rows + 16 * q - 1) / (16 * q)) * q;
-        const int64_t jobs = int64_t(nprob) * pairs * a.tiles;
+        a.tok = D::kTokens && experts == 1 && share == 1 && pairs > 1 ? 4 : 1;
+        const int64_t jobs = int64_t(nprob) * ((pairs + a.tok - 1) / a.tok) * a.tiles;
         if (jobs > (int64_t(1) << 30) || xrows > (int64_t(1) << 20) || experts * rows / q >= (int64_t(1) << 31) ||
             q * row_bytes >= (int64_t(1) << 27))
             return 1;
