@@ -192,6 +192,12 @@ class ExpertParallelPrompt:
         layer = self.layer
         lead, hidden = x.shape[:-1], x.shape[-1]
         x2 = x.reshape(-1, hidden).contiguous()
+        if x2.shape[0] == 0:
+            # a rank with no tokens of this chunk still takes part in every exchange: it routes one zero token
+            # (its pairs are computed where they land and dropped here), so no exchange or product of this rank
+            # is empty
+            self(x2.new_zeros(1, hidden))
+            return x2.new_zeros(*lead, hidden)
         k = layer.top_k
         idx, w = top_k_softmax(layer.gate(x2), k)
         counts, where, send_expert, send_x = dispatch(idx, x2, self.experts, self.world)
