@@ -183,3 +183,89 @@ def test_a_prompt_chunk_over_two_gloo_ranks_gives_each_ranks_tokens_the_single_b
     got = sorted(q.get() for _ in range(2))
     assert all(e <= 1e-3 for _, e, _ in got), got
     assert sum(n for *_, n in got) == sum(split) * K  # every pair computed once, somewhere
+
+
+class _OracleLayer:
+    """A rank's layer whose products are the oracle's, on CPU tensors: stands in for the CUDA kernels so that
+    `ExpertParallelPrompt.__call__` itself (its exchanges, the empty-rank case) runs on gloo ranks."""
+
+    def __init__(self, router, local, shared, sgate, k):
+        self.router, self.local, self.shared, self.sgate, self.top_k = router, local, shared, sgate, k
+        self.gate = lambda x: torch.from_numpy(M.router_logits(self.router, x.numpy()).astype(np.float32))
+        self.shared_expert_gate = lambda x: torch.from_numpy(
+            (x.numpy().astype(np.float64) @ self.sgate.astype(np.float64).reshape(-1, 1)).astype(np.float16))
+        self.shared_expert = lambda x: torch.from_numpy(M.dense_mlp(x.numpy(), *self.shared))
+
+    def switch_mlp(self, rows, local):
+        e = local.view(torch.int32).numpy().astype(np.int64)
+        y = np.stack([M.switch_glu(rows[i : i + 1].numpy(), e[i : i + 1], *self.local)[0] for i in range(rows.shape[0])])
+        return torch.from_numpy(y)
+
+
+def _oracle_top_k_softmax(logits, k):
+    lg = logits.numpy()
+    idx = M.top_k(lg, k)
+    return torch.from_numpy(idx.astype(np.int64)).to(torch.int32).view(torch.uint32), torch.from_numpy(
+        M.softmax_chosen(lg, idx).astype(np.float32))
+
+
+def _oracle_dispatch(idx, x, experts, world):
+    pairs = idx.numel()
+    counts, where, send_expert, order = M.ep_plan(idx.view(torch.int32).numpy(), experts, world)
+    k = idx.shape[-1]
+    sx = np.zeros((pairs, x.shape[-1]), dtype=np.float16)
+    sx[: order.size] = x.numpy()[order // k]
+    se = np.zeros(pairs, dtype=np.int32)
+    se[: order.size] = send_expert.astype(np.int32)
+    return (torch.from_numpy(counts), torch.from_numpy(where), torch.from_numpy(se).view(torch.uint32),
+            torch.from_numpy(sx))
+
+
+def _oracle_combine_rows(y, where, w, g, s):
+    return torch.from_numpy(M.combine_rows(y.numpy(), where.numpy(), w.numpy(), g.numpy().reshape(-1), s.numpy()))
+
+
+def _class_rank(rank, world, port, seed, split, q):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        P.top_k_softmax, P.dispatch, P.combine_rows = _oracle_top_k_softmax, _oracle_dispatch, _oracle_combine_rows
+        routed, shared, router, sgate, _ = layer(seed)
+        rng = np.random.default_rng(seed + 1)
+        x_all = rng.standard_normal((sum(split), H)).astype(np.float16)
+        x = x_all[sum(split[:rank]) : sum(split[: rank + 1])]
+        local = []
+        for b, kind, shape in routed:
+            lb, ls = P.shard_stack(torch.from_numpy(b), kind, shape, rank, world)
+            local.append((lb.numpy(), kind, ls))
+        block = P.ExpertParallelPrompt(_OracleLayer(router, local, shared, sgate, K), rank, world, E)
+        got = block(torch.from_numpy(x)).numpy()
+        assert got.shape == x.shape
+        err = 0.0
+        if x.shape[0]:
+            want, *_ = M.moe_block(x, router, K, routed, shared, sgate)
+            err = float(np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want.astype(np.float64)))
+        q.put((rank, err, int(block.received)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("split", [(4, 3), (5, 0), (0, 6)])
+def test_the_prompt_class_over_two_gloo_ranks_with_oracle_products(split):
+    """`ExpertParallelPrompt.__call__` on two gloo ranks, its kernels replaced by the oracle: every rank's
+    tokens get the single block's output, a rank without tokens routes one zero token and returns none."""
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.SimpleQueue()
+    procs = [ctx.Process(target=_class_rank, args=(r, 2, port, 7, split, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+        assert p.exitcode == 0
+    got = sorted(q.get() for _ in range(2))
+    assert all(e <= 1e-3 for _, e, _ in got), got
+    # every pair computed once; the empty rank's zero token adds its K pairs
+    assert sum(n for *_, n in got) == sum(split) * K + K * sum(1 for t in split if t == 0)
