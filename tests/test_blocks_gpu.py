@@ -127,6 +127,27 @@ def test_float16_products_of_the_k_types_on_int8_dot_products(cuda, kind, rows, 
     assert np.abs(got.reshape(idx.size, rows) - want).max() <= 1e-3 * np.abs(want).max()
 
 
+@pytest.mark.parametrize("kind", ["IQ3_S", "Q8_0", "Q4_K", "Q6_K", "IQ4_XS"])
+def test_a_window_gives_each_token_its_bits_alone(cuda, kind):
+    """window_matvec (strata_mlx/blocks.py:449-470): a verify window's dense product within 1e-3 of the largest
+    value of the float64 product; each token the same bits as alone on the CUDA-core kernels, within 1e-3 of
+    its result alone on the int8 tensor-core kernel (IQ3_S, Q8_0), whose team of warps depends on the window."""
+    rng = np.random.default_rng(len(kind))
+    rows, cols = 256, 1024
+    b, w = stack(kind, rng, 1, rows, cols, scale=(-0.05, 0.05))
+    x = rng.standard_normal((5, cols)).astype(np.float16)
+    got = B.window_matvec(dev(b), kind, rows, cols, dev(x))
+    assert got.shape == (5, rows) and got.dtype == torch.float16
+    want = x.astype(np.float64) @ w[0].astype(np.float64).T
+    for t in range(5):
+        alone = B.window_matvec(dev(b), kind, rows, cols, dev(x[t : t + 1]))
+        if kind in ("IQ3_S", "Q8_0"):
+            assert (got[t : t + 1].float() - alone.float()).abs().max().item() <= 1e-3 * np.abs(want).max()
+        else:
+            assert torch.equal(got[t : t + 1], alone)
+    assert np.abs(got.float().cpu().numpy() - want).max() <= 1e-3 * np.abs(want).max()
+
+
 def test_half_precision_activations_come_back_as_half(cuda):
     """tests/test_blocks.py:63-70."""
     rng = np.random.default_rng(5)
