@@ -53,11 +53,11 @@ def row_bytes(kind: str, cols: int) -> int:
 def window_matvec(blocks: torch.Tensor, kind: str, rows: int, cols: int, x: torch.Tensor,
                   per_row: int | None = None) -> torch.Tensor:
     """out[t] = W . x[t] for one layer's blocks (rows, cols) and a window of tokens x (tokens, cols) ->
-    (tokens, rows) in x's type (strata_mlx/blocks.py:449-470): a verify pass's dense product. On the CUDA-core
+    (tokens, rows) in x's type (strata_mlx/blocks.py:349-396): a verify pass's dense product. On the CUDA-core
     kernels (the K-types, IQ3_XXS, IQ4_XS, the IQ2 / IQ1 types) a token gets the same bits as alone, whatever the
     window; on the int8 tensor-core kernel (IQ3_S, Q8_0) its integer sums are exact but the float32 partial sums
     of a row may be grouped over a different number of warps for another window, so a token's result can differ
-    from its result alone in the last bits (the reference keeps the bits, strata_mlx/blocks.py:481-483).
+    from its result alone in the last bits (the reference keeps the bits, strata_mlx/blocks.py:350, 485-486).
     `per_row` is the reference's threads-per-row hint and changes nothing here."""
     _lib.require_cuda(blocks, x)
     stack = BlockSwitchLinear(blocks, kind, (1, rows, cols))

@@ -129,7 +129,7 @@ def test_float16_products_of_the_k_types_on_int8_dot_products(cuda, kind, rows, 
 
 @pytest.mark.parametrize("kind", ["IQ3_S", "Q8_0", "Q4_K", "Q6_K", "IQ4_XS"])
 def test_a_window_gives_each_token_its_bits_alone(cuda, kind):
-    """window_matvec (strata_mlx/blocks.py:449-470): a verify window's dense product within 1e-3 of the largest
+    """window_matvec (strata_mlx/blocks.py:349-396): a verify window's dense product within 1e-3 of the largest
     value of the float64 product; each token the same bits as alone on the CUDA-core kernels, within 1e-3 of
     its result alone on the int8 tensor-core kernel (IQ3_S, Q8_0), whose team of warps depends on the window."""
     rng = np.random.default_rng(len(kind))
