@@ -1,7 +1,8 @@
 """Writes tests/golden/blocks.npz: block bytes of every type with the weights the reference's decoders give.
 
-Run once, in a container that has the reference checkout (its path is the first argument, default
-/root/reference) and gguf-py 0.19.0, the decoder version the reference pins (`uv.lock:135-136`):
+Run once, in a container that has the reference checkout (its path is the first argument, or the
+STRATA_MLX_REFERENCE environment variable) and gguf-py 0.19.0, the decoder version the reference pins
+(`uv.lock:135-136`):
 
     python tests/golden/make_golden.py [/path/to/strata-mlx]
 
@@ -92,4 +93,7 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("STRATA_MLX_REFERENCE")
+    if not ref:
+        sys.exit("usage: make_golden.py /path/to/strata-mlx (or set STRATA_MLX_REFERENCE)")
+    main(ref)
