@@ -245,4 +245,15 @@ def moe_layer(files: list, layer: int, top_k: int | None = None, device="cuda"):
     return SparseMoeBlock(router, switch, shared, sgate, int(top_k))
 
 
-__all__ = ["GGUF", "TYPES", "Tensor", "experts", "find", "float_matrix", "linear", "moe_layer", "shards", "to_device"]
+_EXPERT_LAYER = re.compile(r"^blk\.(\d+)\.ffn_gate_exps\.weight$")
+
+
+def moe_layers(files: list, top_k: int | None = None, device="cuda") -> dict:
+    """Every MoE layer of the model's files: layer index -> SparseMoeBlock (the layers whose routed experts'
+    gate stack is in the files), uploaded one layer at a time."""
+    found = sorted({int(m.group(1)) for f in files for name in f.tensors if (m := _EXPERT_LAYER.match(name))})
+    return {i: moe_layer(files, i, top_k, device) for i in found}
+
+
+__all__ = ["GGUF", "TYPES", "Tensor", "experts", "find", "float_matrix", "linear", "moe_layer", "moe_layers",
+           "shards", "to_device"]

@@ -121,6 +121,21 @@ def test_a_moe_layer_is_built_from_the_files_bytes(tmp_path):
     assert block.shared_expert_gate.weight.shape == (1, H)
 
 
+def test_every_moe_layer_of_split_files_is_found(tmp_path):
+    rng = np.random.default_rng(5)
+    tensors = layer_tensors(rng, 0)
+    tensors.update(layer_tensors(rng, 2, kinds=("Q2_K", "Q3_K", "IQ3_XXS")))
+    tensors["token_embd.weight"] = (rng.standard_normal((16, H)).astype(np.float16), None)
+    names = sorted(tensors)
+    write(tmp_path / "s-00001-of-00002.gguf", {n: tensors[n] for n in names[:5]})
+    write(tmp_path / "s-00002-of-00002.gguf", {n: tensors[n] for n in names[5:]})
+    layers = G.moe_layers(G.shards(str(tmp_path / "s-00001-of-00002.gguf")), device="cpu")
+    assert sorted(layers) == [0, 2]
+    assert layers[2].switch_mlp.up_proj.kind == "Q3_K" and layers[0].switch_mlp.down_proj.kind == "Q2_K"
+    np.testing.assert_array_equal(layers[2].switch_mlp.down_proj.blocks.numpy(),
+                                  tensors["blk.2.ffn_down_exps.weight"][0].reshape(-1))
+
+
 def test_what_is_not_a_gguf_file_or_not_a_block_type_is_refused(tmp_path):
     p = tmp_path / "no.gguf"
     p.write_bytes(b"GGML" + bytes(60))
