@@ -68,7 +68,11 @@ SMOE_API int smoe_dequant(int kind, const uint8_t* blocks, int64_t n_rows, int64
  * Replaces `BlockSwitchLinear.__call__` / the `_MATVEC` kernel (strata_mlx/blocks.py:196-220, 525-554):
  * share = 1 gives a row of x to every pair (down), share = k one to each run of k pairs (gate, up).
  * Indices >= experts are an error on the host side only if detected there; the kernel skips such pairs
- * (their output rows are left as they were). */
+ * (their output rows are left as they were). Kernels by type and dtype: IQ3_S and Q8_0 with float16 x on the
+ * int8 tensor cores (x split into int8 hi / lo; up to four pairs of a one-expert stack in one pass over its
+ * weights; pairs whose activations do not fit one launch in several), the K-types with float16 x on int8
+ * dot products on the CUDA cores, everything else (and float32 x) on float32 CUDA-core sums; the int8 forms
+ * stay within 1e-3 of the largest value of the exact product. */
 SMOE_API int smoe_matvec(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
                 const uint32_t* idx, int64_t pairs, int64_t share, const void* x, void* out, int dtype,
                 void* stream);
