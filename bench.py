@@ -15,10 +15,14 @@ roofline the dominant kernel (the step's batched gate/up: 16 IQ3_S matrices of 1
          expert's two Q8_0 4096 x 4096 in one launch) against the measured HBM copy bandwidth: algorithmic
          bytes per launch / its CUDA-event time
 cpu_baseline  the oracle port (numpy: decode of the chosen experts' blocks + products) on the host's cores
+prefill  configuration 3: a 1,180-token prompt chunk through a Q2_K layer, Zipf-routed, and its tile products
+verify   configuration 4: a 5-token verify pass through 8 layers cycling the nine block types
+stack    configuration 5: 26 IQ3_S layers, a 32,768-token prompt in 2,048-token chunks, decode at batch 1 and 8
 
 With --gpus N > 1 (torchrun, one process per GPU, NCCL) the experts are sharded 256/N per rank and the
 shared expert's ffn N ways; every rank routes the token, computes its own experts' weighted sum and its slice
-of the shared expert, and one NCCL all-reduce of the [1, 4096] float32 partial sums ends the step.
+of the shared expert, and one NCCL all-reduce of the [1, 4096] float32 partial sums ends the step;
+`--ep-prefill` and `--stack` add configurations 3 and 5 over the ranks (all-to-all dispatch of prompt pairs).
 `--impl reference` times the reference's CPU path (the oracle port, all host cores) on the same workload.
 """
 
