@@ -55,10 +55,6 @@ def _args():
     p.add_argument("--no-prefill", action="store_true", help="skip the config-3 prefill measurement")
     p.add_argument("--only-prefill", action="store_true", help="only the config-3 prefill measurement (profiling)")
     p.add_argument("--no-verify", action="store_true", help="skip the config-4 verify-pass measurement")
-    p.add_argument("--ep-prefill", action="store_true", help="with --gpus N > 1: config 3 over the N ranks "
-                   "(all-to-all dispatch); on one GPU config 3 always runs")
-    p.add_argument("--stack", action="store_true", help="with --gpus N > 1: config 5 (the 26-layer stack, "
-                   "experts sharded over the ranks); on one GPU it always runs unless --no-stack")
     p.add_argument("--no-stack", action="store_true", help="skip the config-5 stack measurement")
     p.add_argument("--only-stack", action="store_true", help="only the config-5 stack measurement")
     p.add_argument("--stack-layers", type=int, default=26)
@@ -126,59 +122,150 @@ def cpu_decode_step(pool, inputs):
     return M.combine(y, w[None], np.array([g]), down[K].astype(np.float16)[None])
 
 
-def cpu_baseline(steps, seed):
-    """Time `steps` decode steps of the CPU path with a spawn pool over all host cores (bounded sample)."""
+def cpu_baseline(steps, seed, warmup=1):
+    """Time `steps` decode steps of the CPU path with a spawn pool over all host cores (bounded sample), each
+    step decoding the chosen experts' blocks; then the same steps with the weights decoded beforehand."""
     import multiprocessing as mp
 
     cores = os.cpu_count() or 1
     ctx = mp.get_context("spawn")
     inputs = cpu_step_inputs(seed)
     with ctx.Pool(cores) as pool:
-        cpu_decode_step(pool, inputs)  # warm the workers
+        for _ in range(max(1, warmup)):
+            cpu_decode_step(pool, inputs)  # (the first also warms the workers)
         t0 = time.perf_counter()
         for _ in range(steps):
             cpu_decode_step(pool, inputs)
         dt = time.perf_counter() - t0
-    return {"value": steps / dt, "unit": "token-layers/s", "cores": cores, "kind": "port",
-            "sample": f"{steps} decode steps of config 2 (8 IQ3_S experts decoded from blocks + Q8_0 shared expert, "
-                      f"numpy oracle, {cores}-process pool), {dt:.1f} s"}
+    out = {"value": steps / dt, "unit": "token-layers/s", "cores": cores, "kind": "port",
+           "sample": f"{steps} decode steps of config 2 (8 IQ3_S experts decoded from blocks + Q8_0 shared expert, "
+                     f"numpy oracle, {cores}-process pool), {dt:.1f} s"}
+    out["product_only"] = cpu_product_only(inputs, max(steps, 3))
+    return out
+
+
+def cpu_product_only(inputs, steps):
+    """The CPU path with the weights decoded beforehand (float32 arrays of the 8 chosen experts and the shared
+    expert, made outside the timing): per step the router, top-k, softmax, the 27 matrix-vector products (numpy
+    BLAS with every host core), SwiGLU and the combine."""
+    import numpy as np
+
+    from oracle import moe as M
+    from oracle import quants as Q
+
+    routed, shared, router, sgate, x = inputs
+    wr = [[Q.dequantize(routed[j][p], KIND, (F_, H) if p < 2 else (H, F_)) for p in range(3)] for j in range(K)]
+    ws = [Q.dequantize(shared[p], SHARED_KIND, (FS, H) if p < 2 else (H, FS)) for p in range(3)]
+    cores = os.cpu_count() or 1
+
+    def step():
+        with np.errstate(invalid="ignore", over="ignore"):
+            logits = M.router_logits(router, x[None])
+            idx = M.top_k(logits, K)[0]
+            w = M.softmax_chosen(logits, idx[None])[0]
+            x32 = x.astype(np.float32)
+            hs = [M.swiglu(wr[j][0] @ x32, wr[j][1] @ x32) for j in range(K)]
+            y = np.stack([wr[j][2] @ hs[j] for j in range(K)]).astype(np.float16)[None]
+            s = ws[2] @ M.swiglu(ws[0] @ x32, ws[1] @ x32)
+            g = np.float16(x32 @ sgate.astype(np.float32))
+            return M.combine(y, w[None], np.array([g]), s.astype(np.float16)[None])
+
+    from threadpoolctl import threadpool_limits
+
+    with threadpool_limits(cores):
+        step()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            step()
+        dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": "token-layers/s", "threads": cores,
+            "sample": f"{steps} decode steps of config 2 with the 8 chosen experts' and the shared expert's weights "
+                      f"decoded to float32 beforehand (numpy BLAS), {dt:.2f} s"}
 
 
 # ---------------------------------------------------------------- GPU workload
 
-def make_layers(n_layers, seed, device, rank=0, world=1):
-    """`n_layers` independent layers of random blocks on the device, as configuration 2 of the benchmark describes them. With
-    world > 1 each rank holds its experts' stacks [rank * E/world, (rank+1) * E/world) and its slice of the
-    shared expert's ffn."""
+def make_layers(n_layers, seed, device, rank=0, world=1, sigma=SIGMA):
+    """`n_layers` independent layers of random blocks on the device, as configuration 2 of the benchmark describes
+    them. Every rank draws the same layers (the seed does not depend on the rank); with world > 1 each rank then
+    keeps its experts [rank E/world, (rank+1) E/world) of every stack and its slice of the shared expert's ffn,
+    so the ranks' parts add up to the one-GPU layer (the router and the shared gate whole on every rank)."""
     import torch
 
     from strata_mlx_b200 import blocks as B
     from strata_mlx_b200 import fused as Fz
+    from strata_mlx_b200 import parallel as P
 
     g = torch.Generator(device=device)
     g.manual_seed(seed)
-    e_loc, fs_loc = E // world, FS // world
 
     def random_blocks(kind, n_weights):
         per, nbytes = B.BLOCK[kind]
         n = n_weights // per
         b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=g)
-        scale = (torch.randn(n, device=device, generator=g) * SIGMA).abs().half()
+        scale = (torch.randn(n, device=device, generator=g) * sigma).abs().half()
         b[:, 0:2] = scale.view(torch.uint8).view(n, 2)
         return b.reshape(-1)
 
     layers = []
     for _ in range(n_layers):
-        gate = B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H))
-        up = B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H))
-        down = B.BlockSwitchLinear(random_blocks(KIND, e_loc * H * F_), KIND, (e_loc, H, F_))
-        shared = B.BlockMLP(B.BlockLinear(random_blocks(SHARED_KIND, fs_loc * H), SHARED_KIND, (fs_loc, H)),
-                            B.BlockLinear(random_blocks(SHARED_KIND, fs_loc * H), SHARED_KIND, (fs_loc, H)),
-                            B.BlockLinear(random_blocks(SHARED_KIND, H * fs_loc), SHARED_KIND, (H, fs_loc)))
+        stacks = [(random_blocks(KIND, E * F_ * H), KIND, (E, F_, H)), (random_blocks(KIND, E * F_ * H), KIND, (E, F_, H)),
+                  (random_blocks(KIND, E * H * F_), KIND, (E, H, F_))]
+        shared = [(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+                  (random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+                  (random_blocks(SHARED_KIND, H * FS), SHARED_KIND, (H, FS))]
         router = (torch.randn(E, H, device=device, generator=g) * 0.02).half()
         sgate = (torch.randn(1, H, device=device, generator=g) * 0.02).half()
-        layers.append(Fz.SparseMoeBlock(router, B.BlockSwitchGLU(gate, up, down), shared, sgate, K))
+        if world == 1:
+            layers.append(Fz.SparseMoeBlock(router, B.BlockSwitchGLU(*(B.BlockSwitchLinear(*st) for st in stacks)),
+                                            B.BlockMLP(*(B.BlockLinear(*sh) for sh in shared)), sgate, K))
+            continue
+        part = P.shard_layer(router, *stacks, shared, sgate, K, rank, world)
+        # own copies of this rank's bytes, so that the whole layer's are freed
+        for lin in (part.switch_mlp.gate_proj, part.switch_mlp.up_proj, part.switch_mlp.down_proj):
+            lin.blocks = lin.blocks.clone()
+        for lin in (part.shared_expert.gate_proj, part.shared_expert.up_proj, part.shared_expert.down_proj):
+            lin.stack.blocks = lin.stack.blocks.clone()
+        layers.append(part)
+        del stacks, shared
     return layers
+
+
+def parity_ep(device, seed, rank, world, exchange, tokens=1):
+    """rel-L2 of the expert-parallel block (this rank's part, through the exchange) against the same layer
+    whole on this GPU, at |N(0, 0.001)| super-scales (where every output is finite): configuration 2's shapes."""
+    import torch
+
+    from strata_mlx_b200 import blocks as B
+    from strata_mlx_b200 import fused as Fz
+    from strata_mlx_b200 import parallel as P
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def random_blocks(kind, n_weights):
+        per, nbytes = B.BLOCK[kind]
+        n = n_weights // per
+        b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=g)
+        b[:, 0:2] = (torch.randn(n, device=device, generator=g) * 0.001).abs().half().view(torch.uint8).view(n, 2)
+        return b.reshape(-1)
+
+    stacks = [(random_blocks(KIND, E * F_ * H), KIND, (E, F_, H)), (random_blocks(KIND, E * F_ * H), KIND, (E, F_, H)),
+              (random_blocks(KIND, E * H * F_), KIND, (E, H, F_))]
+    shared = [(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+              (random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
+              (random_blocks(SHARED_KIND, H * FS), SHARED_KIND, (H, FS))]
+    router = (torch.randn(E, H, device=device, generator=g) * 0.02).half()
+    sgate = (torch.randn(1, H, device=device, generator=g) * 0.02).half()
+    x = torch.randn(tokens, H, device=device, generator=g).half()
+    whole = Fz.SparseMoeBlock(router, B.BlockSwitchGLU(*(B.BlockSwitchLinear(*st) for st in stacks)),
+                              B.BlockMLP(*(B.BlockLinear(*sh) for sh in shared)), sgate, K)
+    want = whole(x).double()
+    ep = P.ExpertParallelMoE(P.shard_layer(router, *stacks, shared, sgate, K, rank, world), rank, world, E,
+                             exchange=exchange)
+    got = ep(x).double()
+    torch.cuda.synchronize()
+    return float((got - want).norm() / want.norm())
 
 
 def run_prefill(device, seed, steps=5, warmup=2, rank=0, world=1):
@@ -356,30 +443,32 @@ def run_stack(args, rank, world, local_rank, prompt=32768, chunk=2048, decode_st
     dist = None
     if world > 1:
         import torch.distributed as dist  # noqa: F811
+    # a rank's experts are its own draws (random either way); the shared expert, the router and the shared gate
+    # are the same draws on every rank
     g = torch.Generator(device=device)
     g.manual_seed(args.seed + 4099 + 7919 * rank)
+    gs = torch.Generator(device=device)
+    gs.manual_seed(args.seed + 4099)
     e_loc = E // world
 
-    def random_blocks(kind, n_weights):
+    def random_blocks(kind, n_weights, gen=g):
         per, nbytes = B.BLOCK[kind]
         n = n_weights // per
-        b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=g)
-        b[:, 0:2] = (torch.randn(n, device=device, generator=g) * SIGMA).abs().half().view(torch.uint8).view(n, 2)
+        b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=gen)
+        b[:, 0:2] = (torch.randn(n, device=device, generator=gen) * SIGMA).abs().half().view(torch.uint8).view(n, 2)
         return b.reshape(-1)
 
+    exchange = P.PeerExchange(rank, world, H, max_tokens=64, device=device) if world > 1 else None
     prompt_blocks, decode_blocks = [], []
     for _ in range(args.stack_layers):
         sw = B.BlockSwitchGLU(B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H)),
                               B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H)),
                               B.BlockSwitchLinear(random_blocks(KIND, e_loc * H * F_), KIND, (e_loc, H, F_)))
-        shared = [(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
-                  (random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
-                  (random_blocks(SHARED_KIND, H * FS), SHARED_KIND, (H, FS))]
-        router = (torch.randn(E, H, device=device, generator=g) * 0.02).half()
-        sgate = (torch.randn(1, H, device=device, generator=g) * 0.02).half()
-        if world > 1:  # every rank routes with the same router and gate
-            dist.broadcast(router, 0)
-            dist.broadcast(sgate, 0)
+        shared = [(random_blocks(SHARED_KIND, FS * H, gs), SHARED_KIND, (FS, H)),
+                  (random_blocks(SHARED_KIND, FS * H, gs), SHARED_KIND, (FS, H)),
+                  (random_blocks(SHARED_KIND, H * FS, gs), SHARED_KIND, (H, FS))]
+        router = (torch.randn(E, H, device=device, generator=gs) * 0.02).half()
+        sgate = (torch.randn(1, H, device=device, generator=gs) * 0.02).half()
         whole = B.BlockMLP(*(B.BlockLinear(b, k, s) for b, k, s in shared))
         prompt_layer = Fz.SparseMoeBlock(router, sw, whole, sgate, K)
         if world == 1:
@@ -392,7 +481,8 @@ def run_stack(args, rank, world, local_rank, prompt=32768, chunk=2048, decode_st
                             B.BlockLinear(P.slice_rows(ub, uk, us, lo, lo + n), uk, (n, H)),
                             B.BlockLinear(P.slice_cols(db, dk, ds, lo, lo + n), dk, (H, n)))
         prompt_blocks.append(P.ExpertParallelPrompt(prompt_layer, rank, world, E))
-        decode_blocks.append(P.ExpertParallelMoE(Fz.SparseMoeBlock(router, sw, sliced, sgate, K), rank, world, E))
+        decode_blocks.append(P.ExpertParallelMoE(Fz.SparseMoeBlock(router, sw, sliced, sgate, K), rank, world, E,
+                                                 exchange=exchange))
 
     gx = torch.Generator(device=device)
     gx.manual_seed(args.seed + 5)
@@ -419,14 +509,20 @@ def run_stack(args, rank, world, local_rank, prompt=32768, chunk=2048, decode_st
     e1.record()
     torch.cuda.synchronize()
     prefill_ms = world_max(e0.elapsed_time(e1))
-    received = [blk.received for blk in prompt_blocks] if world > 1 else None
+    received = None
+    if world > 1:  # each rank's pair count of the last chunk, per layer
+        mine_r = torch.tensor([blk.received for blk in prompt_blocks], device=device)
+        every = [torch.zeros_like(mine_r) for _ in range(world)]
+        dist.all_gather(every, mine_r)
+        received = [t.tolist() for t in every]
 
     out = {"workload": f"config 5: {args.stack_layers} MoE layers x 256 IQ3_S experts sharded over {world} GPU(s), "
                        f"shared expert ffn 4096 Q8_0; prefill {prompt} tokens in chunks of {chunk}, then decode at "
                        "batch 1 and 8, one CUDA graph a layer",
            "prefill_ms": prefill_ms, "prefill_tokens_per_s": prompt / (prefill_ms * 1e-3)}
     if received is not None:
-        out["prefill_pairs_last_chunk_rank_layer0"] = received[0]
+        out["prefill_pairs_per_rank_last_chunk_layer0"] = [r[0] for r in received]
+        out["prefill_pairs_per_rank_max_over_layers"] = [max(r) for r in received]
     for batch in (1, 8):
         xb = torch.randn(batch, H, device=device, generator=gx).half()
         if dist:
@@ -450,6 +546,11 @@ def run_stack(args, rank, world, local_rank, prompt=32768, chunk=2048, decode_st
         out[f"decode_bs{batch}_tokens_per_s"] = batch / (ms * 1e-3)
         del graphs
         torch.cuda.synchronize()
+    if exchange is not None:
+        if exchange.failed():
+            out["error"] = "a wait of the peer exchange gave up"
+        dist.barrier()
+        exchange.close()
     return out
 
 
@@ -531,7 +632,7 @@ class Clocks:
 
     NAMES = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
-    def __init__(self, index, path=None):
+    def __init__(self, index):
         import threading
 
         self.samples, self.stop_flag = [], threading.Event()
@@ -602,16 +703,18 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         import torch.distributed as dist  # noqa: F811
 
-    layers = make_layers(args.layers, args.seed + 7919 * rank, device, rank, world)
+    # every rank draws the same layers and keeps its part of each (world > 1)
+    layers = make_layers(args.layers, args.seed, device, rank, world)
     gx = torch.Generator(device=device)
     gx.manual_seed(args.seed + 1)
     xs = [torch.randn(1, H, device=device, generator=gx).half() for _ in range(args.layers)]
+    exchange, parity = None, None
     if world > 1:
-        for x in xs:
-            dist.broadcast(x, 0)
-        from strata_mlx_b200.parallel import ExpertParallelMoE
+        from strata_mlx_b200.parallel import ExpertParallelMoE, PeerExchange
 
-        blocks = [ExpertParallelMoE(layer, rank, world, E) for layer in layers]
+        exchange = PeerExchange(rank, world, H, max_tokens=64, device=device)
+        blocks = [ExpertParallelMoE(layer, rank, world, E, exchange=exchange) for layer in layers]
+        parity = parity_ep(device, args.seed + 17, rank, world, exchange)
     else:
         blocks = layers
     stream = torch.cuda.current_stream()
@@ -628,15 +731,20 @@ def run_ours(args, rank, world, local_rank):
     blocks[0](xs[0])
     launches = _lib.launches - n0  # our kernels in one step
 
+    def align():
+        """Line the ranks' timed regions up on the device: a barrier on the host, then a small all-reduce on the
+        timing stream whose end every rank reaches together."""
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+            torch.cuda.synchronize()
+            dist.all_reduce(torch.ones(1, device=device))
+
     for i in range(args.warmup):
         graphs[i % args.layers].graph.replay()
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
-    clocks = Clocks(local_rank, os.path.join(ROOT, "gpurun_out" if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else "_work",
-                                             f"clocks_rank{rank}.csv"))
+    clocks = Clocks(local_rank)
+    align()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
     t_start.record(stream)
     for i in range(args.steps):
         graphs[i % args.layers].graph.replay()
@@ -644,13 +752,13 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     ms = t_start.elapsed_time(t_end)
     clk = clocks.stop()
-    if dist:
-        dist.barrier()
+    if exchange is not None and exchange.failed():
+        raise RuntimeError("a wait of the peer exchange gave up during the timed steps")
 
-    # the dominant kernel alone: a graph of its launches over the rotating layers, with each layer's routing.
-    # On one GPU that is the step's batched gate/up launch (routed experts and shared expert in one int8
-    # tensor-core kernel); on several, each rank's routed gate/up.
-    routes = []
+    # the dominant kernel alone: a graph of its launches over the rotating layers, with each layer's routing: the
+    # step's batched gate/up launch (the routed experts' of this rank and the shared expert's, in one int8
+    # tensor-core kernel)
+    routes, gu_bytes = [], 0
     for i in range(args.layers):
         blk = blocks[i]
         layer = blk if world == 1 else blk.layer
@@ -659,29 +767,26 @@ def run_ours(args, rank, world, local_rank):
             idx = blk.local_indices(idx)
         fi = idx.reshape(-1).contiguous()
         sw, sh = layer.switch_mlp, layer.shared_expert
+        valid = int((fi.view(torch.int32) < sw.gate_proj.num_experts).sum().item())
+        gu_bytes += (2 * valid * F_ * B.row_bytes(KIND, H)
+                     + 2 * sh.gate_proj.output_dims * B.row_bytes(SHARED_KIND, H))
         outs = [torch.empty((K, F_), dtype=torch.float16, device=device) for _ in range(2)]
         souts = [torch.empty((1, sh.gate_proj.output_dims), dtype=torch.float16, device=device) for _ in range(2)]
         z = B._zeros_idx(1, device)
         probs = [B._problem(sw.gate_proj, fi, K, K, outs[0], x=xs[i]), B._problem(sw.up_proj, fi, K, K, outs[1], x=xs[i]),
                  B._problem(sh.gate_proj.stack, z, 1, 1, souts[0], x=xs[i]),
                  B._problem(sh.up_proj.stack, z, 1, 1, souts[1], x=xs[i])]
-        routes.append((sw, xs[i], fi, probs, outs + souts))
+        routes.append((probs, outs + souts, fi))
+    gu_bytes /= args.layers  # per launch, averaged over the layers' routings
     reps = max(1, 64 // args.layers)
-
-    def dominant(sw, x, idx, probs):
-        if world == 1:
-            B.matvec_batch(probs)
-        else:
-            B.gate_up(sw.gate_proj, sw.up_proj, x, idx, K)
-
-    for sw, x, idx, probs, _ in routes:
-        dominant(sw, x, idx, probs)
+    for probs, _, _ in routes:
+        B.matvec_batch(probs)
     torch.cuda.synchronize()
     gu_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gu_graph):
         for _ in range(reps):
-            for sw, x, idx, probs, _ in routes:
-                dominant(sw, x, idx, probs)
+            for probs, _, _ in routes:
+                B.matvec_batch(probs)
     gu_graph.replay()
     torch.cuda.synchronize()
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -699,9 +804,7 @@ def run_ours(args, rank, world, local_rank):
     for i in range(args.warmup):
         d = host_in[i % args.layers].to(device, non_blocking=True)
         host_out.copy_(graphs[i % args.layers](d), non_blocking=True)
-    torch.cuda.synchronize()
-    if dist:
-        dist.barrier()
+    align()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
@@ -711,6 +814,8 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
     del graphs, gu_graph
+    if exchange is not None and exchange.failed():
+        raise RuntimeError("a wait of the peer exchange gave up during the end-to-end steps")
 
     def world_max(v):
         if not dist:
@@ -719,15 +824,21 @@ def run_ours(args, rank, world, local_rank):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return t.item()
 
-    ms, e2e_ms, gu = world_max(ms), world_max(e2e_ms), world_max(gu)
+    ms, e2e_ms, gu, gu_bytes = world_max(ms), world_max(e2e_ms), world_max(gu), world_max(gu_bytes)
+    if parity is not None:
+        parity = world_max(parity)
+    if exchange is not None:
+        torch.cuda.synchronize()
+        dist.barrier()
+        exchange.close()
     if rank != 0:
         return None
     peak, peak_kind = peaks()
-    e_loc = E // world
-    # 16 IQ3_S matrices of 1536 x 4096 and the shared expert's two Q8_0 4096 x 4096 (one GPU)
-    gu_bytes = 2 * K * F_ * B.row_bytes(KIND, H) + 2 * FS * B.row_bytes(SHARED_KIND, H) if world == 1 else None
-    achieved = gu_bytes / (gu * 1e-3) / 1e9 if world == 1 else None
-    per_step_bytes = (3 * K * F_ * B.row_bytes(KIND, H) + 3 * FS * B.row_bytes(SHARED_KIND, H) + E * H * 2)
+    achieved = gu_bytes / (gu * 1e-3) / 1e9
+    # bytes a rank reads per step: its share of the routed experts (8 of 256 spread evenly), its slice of the
+    # shared expert, the whole router
+    per_step_bytes = (3 * K * F_ * B.row_bytes(KIND, H) + 3 * FS * B.row_bytes(SHARED_KIND, H)) / world + (E + 1) * H * 2
+    step_gbs = per_step_bytes / (ms / args.steps * 1e-3) / 1e9
     line = {
         "metric": "MoE layer tokens/s (decode bs1) + achieved HBM GB/s vs roofline",
         "value": args.steps / (ms * 1e-3),
@@ -741,25 +852,35 @@ def run_ours(args, rank, world, local_rank):
         "vs_baseline": None,
         "dtype": "f16 activations, IQ3_S/Q8_0 blocks, f32 accumulation",
         "data": "synthetic (seeded random blocks and activations, BASELINE config 2 distributions)",
-        "config": {"workload": "config 2: one MoE layer, decode batch 1, hidden 4096, 256 IQ3_S experts "
-                               "(gate/up 1536x4096, down 4096x1536), top-8, shared expert ffn 4096 Q8_0",
-                   "layers_rotated": args.layers, "l2": f"inputs > L2: {args.layers} layers x "
-                   f"{(3 * E * F_ * B.row_bytes(KIND, H) + 3 * FS * B.row_bytes(SHARED_KIND, H)) / 1e9:.2f} GB cycled",
-                   "parallelism": f"ep{world}" if world > 1 else "single",
-                   "bytes_per_step_algorithmic": per_step_bytes},
-        "hbm_gbs_step": per_step_bytes / (ms / args.steps * 1e-3) / 1e9,
+        "config": dict(CONFIG2),
+        "setup": {"layers_rotated": args.layers, "l2": f"inputs > L2: {args.layers} layers x "
+                  f"{(3 * E * F_ * B.row_bytes(KIND, H) + 3 * FS * B.row_bytes(SHARED_KIND, H)) / 1e9:.2f} GB cycled",
+                  "parallelism": f"ep{world}: experts {E // world} a rank, shared ffn {FS // world} a rank, one "
+                                 "exchange of partial sums over NVLink peer memory a step" if world > 1 else "single",
+                  "bytes_per_rank_per_step": per_step_bytes},
+        "hbm_gbs_step": step_gbs,
+        "step_roofline": {"bound": "hbm", "achieved": step_gbs, "peak": peak, "unit": "GB/s", "frac": step_gbs / peak,
+                          "bytes": "per rank per step: its share of the routed and shared bytes, the router"},
         "gpu_launches": launches * args.steps,
         "e2e": {"value": args.steps / (e2e_ms * 1e-3), "unit": "token-layers/s",
                 "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
-        "roofline": {"kernel": "mv8_kernel (batched gate+up: 16 x 1536 x 4096 IQ3_S + 2 x 4096 x 4096 Q8_0)"
-                               if world == 1 else "mv8s_kernel<M8IQ3S> (routed gate+up)", "bound": "hbm",
+        "roofline": {"kernel": "mv8_kernel (batched gate+up: this rank's IQ3_S 1536 x 4096 pairs + the Q8_0 shared "
+                               "expert's gate and up rows)", "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": (achieved / peak) if achieved else None, "peak_source": peak_kind,
+                     "frac": achieved / peak, "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu,
-                     "traffic": traffic_from_profiles()},
+                     "traffic": traffic_from_profiles() if world == 1 else None},
         "clocks": clk,
     }
+    if parity is not None:
+        line["parity_rel_l2"] = parity
+        line["parity"] = ("max over ranks of rel-L2(expert-parallel block, the same layer whole on one GPU), one "
+                          "token, super-scales |N(0, 0.001)|")
     return line
+
+
+CONFIG2 = {"workload": "config 2: one MoE layer, decode batch 1, hidden 4096, 256 IQ3_S experts (gate/up 1536x4096, "
+                       "down 4096x1536), top-8, shared expert ffn 4096 Q8_0"}
 
 
 def main():
@@ -770,15 +891,21 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return
-        cb = cpu_baseline(max(1, args.steps if args.steps < 4 else 2), args.seed)
+        # the reference's CPU path: each step a whole decode step (about a second on 16 cores); at most 40 steps
+        steps, warmup = min(args.steps, 40), min(args.warmup, 3)
+        cb = cpu_baseline(steps, args.seed, warmup=warmup)
         line = {"impl": "reference", "metric": "MoE layer tokens/s (decode bs1) + achieved HBM GB/s vs roofline",
-                "value": cb["value"], "unit": cb["unit"], "n_gpus": world, "steps": args.steps,
-                "warmup": args.warmup, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "f32 (numpy)", "data": "synthetic (seeded, BASELINE config 2 distributions)",
-                "config": {"workload": "config 2: one MoE layer, decode batch 1 (CPU: oracle port of the "
-                                       "reference's block decoders + numpy products)"},
+                "value": cb["value"], "unit": cb["unit"], "n_gpus": world, "steps": steps, "warmup": warmup,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f32 (numpy; blocks decoded by the oracle port of the reference's decoders)",
+                "data": "synthetic (seeded random blocks and activations, BASELINE config 2 distributions)",
+                "config": dict(CONFIG2),
+                "setup": {"cpu": f"oracle port of the reference's block decoders + numpy products, {cb['cores']} "
+                                 "processes"},
                 "cpu_baseline": cb, "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                                             "d2h_bytes_per_step": 0}}
+        if steps != args.steps:
+            line["sample"] = f"{steps} of the {args.steps} steps asked for (each a whole decode step on the CPU)"
         print(json.dumps(line))
         return
     if args.only_matvec:
@@ -813,13 +940,15 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         line = run_ours(args, rank, world, local_rank)
-        if world > 1 and args.ep_prefill and not args.no_prefill:
+        # several GPUs: configurations 3 and 5 over the ranks too (every rank takes the same steps, so an error
+        # is raised on every rank and ends the job)
+        if world > 1 and not args.no_prefill:
             import torch
 
             pf = run_prefill(torch.device("cuda", local_rank), args.seed + 99, rank=rank, world=world)
             if line is not None:
                 line["prefill"] = pf
-        if world > 1 and args.stack and not args.no_stack:
+        if world > 1 and not args.no_stack:
             st = run_stack(args, rank, world, local_rank)
             if line is not None:
                 line["stack"] = st

@@ -4,7 +4,7 @@
  * Every entry point replaces one kernel-launching function of yibie/strata-mlx's Python modules
  * `strata_mlx/blocks.py` and `strata_mlx/fused.py` (cited beside each declaration). The Python facade
  * `strata_mlx_b200.blocks` / `strata_mlx_b200.fused` binds them with ctypes; any other host language binds
- * the same symbols.
+ * the same symbols (plain C types only: pointers, sizes, int codes).
  *
  * Conventions
  *   - Pointers are CUDA device pointers unless named `host_*`. Blocks are the GGUF file's raw bytes of a
@@ -14,8 +14,10 @@
  *     16 IQ2_XXS, 17 IQ2_XS, 18 IQ3_XXS, 20 IQ4_NL, 21 IQ3_S, 22 IQ2_S, 23 IQ4_XS, 29 IQ1_M, 42 Q2_0).
  *   - `dtype` codes: SMOE_F32 = 0, SMOE_F16 = 1. Activations and results take the activations' type unless
  *     a declaration says float32.
- *   - `stream` is a cudaStream_t (0 = legacy default stream). Every call is asynchronous on it, allocates
- *     nothing, synchronises nothing and so can be captured in a CUDA graph.
+ *   - `stream` is a cudaStream_t (0 = legacy default stream). Every call that takes a stream is asynchronous
+ *     on it, allocates nothing, synchronises nothing and so can be captured in a CUDA graph. The calls without
+ *     a stream (the *_status reads, smoe_matvec_set_wait_limit, the exchange buffers' alloc / open / close /
+ *     free) synchronise or allocate and belong outside capture.
  *   - Return value: 0 on success; > 0 an invalid argument (SMOE_E*), with a message from
  *     smoe_last_error(); < 0 the negated cudaError_t of a failed launch.
  */
@@ -76,6 +78,17 @@ SMOE_API int smoe_dequant(int kind, const uint8_t* blocks, int64_t n_rows, int64
 SMOE_API int smoe_matvec(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
                 const uint32_t* idx, int64_t pairs, int64_t share, const void* x, void* out, int dtype,
                 void* stream);
+
+/* The int8 tensor-core decode kernels (the IQ3_S / Q8_0 paths of smoe_matvec, smoe_matvec_gate_up,
+ * smoe_matvec_glu, smoe_matvec_batch and smoe_matvec_glu_combine) bound every wait for a weight copy (about a
+ * second). A wait that gives up stops the warp's copies, records SMOE_ETIMEOUT in a status word on the device,
+ * and leaves that launch's outputs not valid. smoe_matvec_status synchronizes the current device and reads the
+ * word (0 or SMOE_ETIMEOUT); `clear` zeroes it. smoe_matvec_set_wait_limit sets the bound in polls on the
+ * current device (each poll suspends the waiting thread up to 1 ms; 0: one check, no wait; < 0: the default),
+ * for tests that make a wait run out; it synchronizes the device. No counterpart in the reference (its kernels
+ * have no device-side waits). */
+SMOE_API int smoe_matvec_status(int* status, int clear);
+SMOE_API int smoe_matvec_set_wait_limit(int64_t polls);
 
 /* The gate and up products of the same pairs in one launch: two smoe_matvec calls sharing idx and x
  * (strata_mlx/blocks.py:971 `g, u = gate(x5, indices), up(x5, indices)`). The two stacks may differ in
@@ -176,6 +189,51 @@ SMOE_API int smoe_partial_sums(const void* y, const float* w, const uint32_t* li
 SMOE_API int smoe_combine_sums(const float* sums, const void* g, int64_t tokens, int64_t d, void* out, int dtype,
                                void* stream);
 
+/* The decode step's one exchange over NVLink peer memory, fused with the end of the block: it replaces the
+ * smoe_partial_sums -> all-reduce -> smoe_combine_sums sequence above with one launch. No counterpart in the
+ * reference (one device only); it is the same split of `_Routed.__call__` (strata_mlx/fused.py:487-497) at its
+ * combine, with the same rounding points as smoe_combine_sums.
+ *   smoe_ep_exchange_bytes:  bytes of one rank's exchange buffer for `ranks` ranks, up to max_tokens tokens of
+ *                            d values (0 for sizes out of range: 1..16 ranks).
+ *   smoe_ep_exchange_alloc:  cudaMalloc (zeroed) on the current device, and its CUDA IPC handle (64 bytes) for
+ *                            the other ranks of the node; smoe_ep_exchange_free releases it.
+ *   smoe_ep_exchange_open:   map another rank's buffer from its handle; smoe_ep_exchange_close unmaps it.
+ *   smoe_ep_reduce_combine:  every rank calls it with the same shape, in the same order: rank r forms its float32
+ *                            partials (routed: its pairs' y w in MLX's order; shared: float(s)), stores them into
+ *                            every rank's buffer, waits for every rank's (bounded: about a second, or wait_polls
+ *                            polls when not 0), adds them in rank order and writes
+ *                            out = half(routed) + half(half(sigmoid(g)) half(shared)) -- the same bits on every
+ *                            rank. Calls that share buffers must be ordered on the GPU (one stream). Each launch
+ *                            counts itself in the buffer, so it can be captured in a CUDA graph and replayed.
+ *   smoe_ep_exchange_status: synchronizes the device and reads this rank's status word (SMOE_ETIMEOUT when a wait
+ *                            gave up; the outputs of that call were not written); `clear` zeroes it.
+ *   smoe_ep_reduce_combine_emulated: every rank's call in one cooperative launch on one GPU (ranks 2..8, each
+ *                            spec's peers naming the other specs' buffers): the exchange's arithmetic and order
+ *                            on a machine with one GPU (tests). */
+typedef struct SmoeEpReduce {
+    int rank, ranks;
+    void* peers[16];        /* every rank's exchange buffer as mapped here (peers[rank]: this rank's own) */
+    const void* y;          /* (tokens, k, d) this rank's experts' outputs; rows of other ranks' pairs are not read */
+    const float* w;         /* (tokens, k) */
+    const uint32_t* lidx;   /* (tokens, k) local expert of each pair (smoe_localize), >= experts for another rank's */
+    int64_t experts;        /* experts of this rank */
+    const void* s;          /* (tokens, d) this rank's slice of the shared expert, or null */
+    const void* g;          /* (tokens) the shared expert's gate value */
+    int64_t tokens, k, d;
+    int64_t capacity;       /* max_tokens x d of the buffers */
+    void* out;              /* (tokens, d) */
+    int dtype;
+    uint32_t wait_polls;    /* 0: the default bound */
+} SmoeEpReduce;
+SMOE_API size_t smoe_ep_exchange_bytes(int64_t ranks, int64_t max_tokens, int64_t d);
+SMOE_API int smoe_ep_exchange_alloc(size_t bytes, void** buffer, void* ipc_handle);
+SMOE_API int smoe_ep_exchange_open(const void* ipc_handle, void** peer_buffer);
+SMOE_API int smoe_ep_exchange_close(void* peer_buffer);
+SMOE_API int smoe_ep_exchange_free(void* buffer);
+SMOE_API int smoe_ep_exchange_status(void* buffer, int* failed, int clear);
+SMOE_API int smoe_ep_reduce_combine(const SmoeEpReduce* r, void* stream);
+SMOE_API int smoe_ep_reduce_combine_emulated(int ranks, const SmoeEpReduce* r, void* stream);
+
 /* Expert parallelism for a prompt chunk (each rank holds its own tokens; rank r owns experts [r E/N, (r+1) E/N)):
  * the two ends of the all-to-all exchanges that carry the pairs to their experts' ranks and the outputs back.
  * Like the decode pieces above, no counterpart in the reference; together they split `_Routed.__call__`
@@ -194,6 +252,64 @@ SMOE_API int smoe_ep_dispatch(const uint32_t* idx, int64_t pairs, int64_t k, int
 SMOE_API int smoe_combine_rows(const void* y, const int32_t* where, const float* w, const void* g, const void* s,
                                int64_t tokens, int64_t k, int64_t d, void* out, int dtype, void* stream);
 
+/* The hyper-connection around a block: the write of the block before it folded into the read of the residual
+ * streams (strata_mlx/fused.py:46-146 `_NORM`, `_DOWN`, `_UP`; `FusedResidual.__call__`, 280-323), for `tokens`
+ * tokens, hc streams of d values, a low rank of `rank`:
+ *   residual = before + out * inject_in (before (tokens, hc d), out (tokens, d), inject_in (tokens, hc)), in the
+ *              activations' type; normed = residual rsqrt(mean of its squares per stream + eps) norm, float32;
+ *   total_j  = (row j of down, or of inject_w, . normed) / hc; low = total sigmoid(total) (rows of down, float32),
+ *              inject = 2 sigmoid(total) (rows of inject_w, the activations' type), when inject_w is given;
+ *   mixed[c] = sum over streams s of normed[s d + c] sigmoid(up[s d + c] . low) / hc, the activations' type.
+ * Sums in float32 in an order fixed by the shapes, so a token gets the same bits alone as in a window. Weights
+ * and activations share `dtype` (float16 or float32); down (rank, hc d), up (hc d, rank), inject_w (hc, hc d)
+ * or null, norm (hc d), weights 16-byte aligned; d and rank multiples of 8, hc <= 8. Three launches;
+ * smoe_hyper_workspace_size() bytes of device workspace (normed and low). */
+typedef struct SmoeHyper {
+    const void* norm;
+    const void* down;
+    const void* up;
+    const void* inject_w;  /* or null: no inject output (the caller keeps inject_in) */
+    int64_t hc, d, rank;
+    float eps;
+    int dtype;
+} SmoeHyper;
+SMOE_API size_t smoe_hyper_workspace_size(int64_t tokens, int64_t hc, int64_t d, int64_t rank);
+SMOE_API int smoe_hyper_connection(const SmoeHyper* h, const void* before, const void* out, const void* inject_in,
+                                   int64_t tokens, void* mixed, void* residual, void* inject, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* A Q3_K tensor held as planes (strata_mlx/blocks.py:399-512): its blocks (rows, cols) rearranged once into
+ * hm (8 words a block: the high-bit mask), qs (16 words: the two-bit codes), sc (16 int8: the six-bit scales
+ * less 32) and dd (the float16 d), 114 bytes a block for the file's 110; the same weights.
+ *   smoe_q3k_planes:         the rearrangement (`q3k_planes`, blocks.py:403-414).
+ *   smoe_q3k_planes_window:  out[t, r] = W . x[t] for tokens x (tokens, cols) -> (tokens, rows) in x's type
+ *                            (`q3k_planes_window`, blocks.py:482-499); a token's bits do not depend on the window.
+ *   smoe_q3k_planes_dequant: every weight (d scale) value as the block decoder forms it, rounded once
+ *                            (`q3k_planes_dequantize`, blocks.py:502-512). */
+SMOE_API int smoe_q3k_planes(const uint8_t* blocks, int64_t rows, int64_t cols, uint32_t* hm, uint32_t* qs,
+                             int8_t* sc, uint16_t* dd, void* stream);
+SMOE_API int smoe_q3k_planes_window(const uint32_t* hm, const uint32_t* qs, const int8_t* sc, const uint16_t* dd,
+                                    int64_t rows, int64_t cols, const void* x, int64_t tokens, void* out, int dtype,
+                                    void* stream);
+SMOE_API int smoe_q3k_planes_dequant(const uint32_t* hm, const uint32_t* qs, const int8_t* sc, const uint16_t* dd,
+                                     int64_t rows, int64_t cols, void* out, int dtype, void* stream);
+
+/* A Q6_K tensor as ScaledLinear holds it (strata_mlx/dense.py:109-167): a weight is code * scale * d with codes
+ * int8 (rows, cols) (the six bits less 32), scales int8 (rows, cols / 16), d float16 (rows, cols / d_step).
+ *   smoe_q6k_parts:     the three parts from the file's blocks (`q6k_parts`, strata_mlx/gguf.py:150-165; d_step 256).
+ *   smoe_scaled_window: out[t, r] = sum over groups of 16 of (d scale) (codes . x[t]), float32 sums, for tokens
+ *                       x (tokens, cols) -> (tokens, rows) in x's type (`ScaledLinear.__call__`, dense.py:147-167);
+ *                       codes 16-byte aligned; a token's bits do not depend on the window.
+ *   smoe_scaled_floats: every weight (float(d) float(scale)) float(code) rounded once (`ScaledLinear.floats`,
+ *                       dense.py:128-145). */
+SMOE_API int smoe_q6k_parts(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* codes, int8_t* scales,
+                            uint16_t* d, void* stream);
+SMOE_API int smoe_scaled_window(const int8_t* codes, const int8_t* scales, const uint16_t* d, int64_t rows,
+                                int64_t cols, int64_t d_step, const void* x, int64_t tokens, void* out, int dtype,
+                                void* stream);
+SMOE_API int smoe_scaled_floats(const int8_t* codes, const int8_t* scales, const uint16_t* d, int64_t rows,
+                                int64_t cols, int64_t d_step, void* out, int dtype, void* stream);
+
 /* The dispatch permutation of `pairs` = tokens * k expert indices (int32, flat) into tiles of 16 slots,
  * each tile one expert's: tile_expert[most] (experts for a tile nothing fills), token[most * 16] (0 in an
  * unfilled slot), where[pairs] (the slot of each pair), most = pairs / 16 + min(experts, pairs).
@@ -210,8 +326,9 @@ SMOE_API int smoe_tiles_of(const int32_t* indices, int64_t pairs, int64_t k, int
  * bytes in the library's device image (held by every GPU that loads the library until the process exits),
  * which limits it to smoe_tiles_of_workspace_size(pairs, experts) <= 1,048,832 bytes (131,072 pairs at 1,024
  * experts; 209,664 at 256) and returns SMOE_ESHAPE beyond. It allocates nothing. The first call on a device looks up the array's
- * device address (cudaGetSymbolAddress); make that first call before any stream capture. All calls share
- * the array: calls that overlap on the GPU race on it. */
+ * device address (cudaGetSymbolAddress) and keeps it for the life of the process; make that first call before
+ * any stream capture, and make no call on a device after resetting it (the kept address is then stale). All
+ * calls share the array: calls that overlap on the GPU race on it. */
 SMOE_API int smoe_tiles_of_noalloc(const int32_t* indices, int64_t pairs, int64_t k, int64_t experts,
                                    uint32_t* tile_expert, uint32_t* token, uint32_t* where, void* stream);
 

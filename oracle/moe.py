@@ -195,6 +195,16 @@ def combine_sums(sums, g, dtype=np.float16):
     return (routed.astype(np.float32) + shared.astype(np.float32)).astype(dtype)
 
 
+def ep_reduce_combine(partials, g, dtype=np.float16):
+    """The end of an expert-parallel decode step over the peer exchange: the ranks' float32 partials (each
+    `partial_sums`' (T, 2D)) added in rank order, in float32, then `combine_sums`. No counterpart in the
+    reference (one device); it is the combine of strata_mlx/fused.py:448-462 split across ranks."""
+    total = np.asarray(partials[0], dtype=np.float32).copy()
+    for p in partials[1:]:
+        total = (total + np.asarray(p, dtype=np.float32)).astype(np.float32)
+    return combine_sums(total, g, dtype)
+
+
 def ep_plan(idx, experts, ranks):
     """The send side of a prompt chunk's expert-parallel exchange. No counterpart in the reference (one device);
     it splits `_Routed.__call__` (strata_mlx/fused.py:487-497) between top-k and `switch_mlp`: each pair goes to

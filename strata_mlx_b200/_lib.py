@@ -36,6 +36,21 @@ class SmoeDecodeLayer(ctypes.Structure):
                 ("gate_out", _p), ("out", _p), ("scratch", _p)]
 
 
+class SmoeEpReduce(ctypes.Structure):
+    """`SmoeEpReduce` of include/strata_moe.h: one rank's call of smoe_ep_reduce_combine."""
+
+    _fields_ = [("rank", _i), ("ranks", _i), ("peers", _p * 16), ("y", _p), ("w", _p), ("lidx", _p),
+                ("experts", _i64), ("s", _p), ("g", _p), ("tokens", _i64), ("k", _i64), ("d", _i64),
+                ("capacity", _i64), ("out", _p), ("dtype", _i), ("wait_polls", _c.c_uint32)]
+
+
+class SmoeHyper(ctypes.Structure):
+    """`SmoeHyper` of include/strata_moe.h: a hyper-connection's weights and sizes."""
+
+    _fields_ = [("norm", _p), ("down", _p), ("up", _p), ("inject_w", _p), ("hc", _i64), ("d", _i64), ("rank", _i64),
+                ("eps", _c.c_float), ("dtype", _i)]
+
+
 # name -> (restype, argtypes): the declarations of include/strata_moe.h
 SIGNATURES = {
     "smoe_last_error": (_c.c_char_p, []),
@@ -47,6 +62,8 @@ SIGNATURES = {
     "smoe_matvec_gate_up": (_i, [_i, _p, _i, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _p, _i, _p]),
     "smoe_matvec_glu": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _i, _p]),
     "smoe_matvec_batch": (_i, [_i, _c.POINTER(SmoeMatvec), _p]),
+    "smoe_matvec_status": (_i, [_c.POINTER(_i), _i]),
+    "smoe_matvec_set_wait_limit": (_i, [_i64]),
     "smoe_matvec_glu_combine": (_i, [_i, _p, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i, _p]),
     "smoe_decode_layer_scratch": (_sz, [_i64, _i64, _i64, _i64]),
     "smoe_decode_layer": (_i, [_c.POINTER(SmoeDecodeLayer), _p, _p]),
@@ -60,8 +77,24 @@ SIGNATURES = {
     "smoe_localize": (_i, [_p, _i64, _i64, _i64, _p, _p]),
     "smoe_partial_sums": (_i, [_p, _p, _p, _i64, _p, _i64, _i64, _i64, _p, _i, _p]),
     "smoe_combine_sums": (_i, [_p, _p, _i64, _i64, _p, _i, _p]),
+    "smoe_ep_exchange_bytes": (_sz, [_i64, _i64, _i64]),
+    "smoe_ep_exchange_alloc": (_i, [_sz, _c.POINTER(_p), _p]),
+    "smoe_ep_exchange_open": (_i, [_p, _c.POINTER(_p)]),
+    "smoe_ep_exchange_close": (_i, [_p]),
+    "smoe_ep_exchange_free": (_i, [_p]),
+    "smoe_ep_exchange_status": (_i, [_p, _c.POINTER(_i), _i]),
+    "smoe_ep_reduce_combine": (_i, [_c.POINTER(SmoeEpReduce), _p]),
+    "smoe_ep_reduce_combine_emulated": (_i, [_i, _c.POINTER(SmoeEpReduce), _p]),
     "smoe_ep_dispatch": (_i, [_p, _i64, _i64, _i64, _i64, _p, _i64, _i, _p, _p, _p, _p, _p]),
     "smoe_combine_rows": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
+    "smoe_hyper_workspace_size": (_sz, [_i64, _i64, _i64, _i64]),
+    "smoe_hyper_connection": (_i, [_c.POINTER(SmoeHyper), _p, _p, _p, _i64, _p, _p, _p, _p, _sz, _p]),
+    "smoe_q3k_planes": (_i, [_p, _i64, _i64, _p, _p, _p, _p, _p]),
+    "smoe_q3k_planes_window": (_i, [_p, _p, _p, _p, _i64, _i64, _p, _i64, _p, _i, _p]),
+    "smoe_q3k_planes_dequant": (_i, [_p, _p, _p, _p, _i64, _i64, _p, _i, _p]),
+    "smoe_q6k_parts": (_i, [_p, _i64, _i64, _p, _p, _p, _p]),
+    "smoe_scaled_window": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _i, _p]),
+    "smoe_scaled_floats": (_i, [_p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
     "smoe_tiles_of_workspace_size": (_sz, [_i64, _i64]),
     "smoe_tiles_of": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p, _sz, _p]),
     "smoe_tiles_of_noalloc": (_i, [_p, _i64, _i64, _i64, _p, _p, _p, _p]),
@@ -72,8 +105,11 @@ SIGNATURES = {
 
 _lib = None
 
-# kernels each entry point launches (for the benchmark's launch count)
-KERNELS_PER_CALL = {"smoe_tiles_of": 2, "smoe_tile_matmul": 2}
+# kernels each entry point launches (for the benchmark's launch count); 1 where not named
+KERNELS_PER_CALL = {"smoe_tiles_of": 2, "smoe_tiles_of_noalloc": 2, "smoe_tile_matmul": 2, "smoe_ep_dispatch": 2,
+                    "smoe_ep_exchange_alloc": 0, "smoe_ep_exchange_open": 0, "smoe_ep_exchange_close": 0,
+                    "smoe_ep_exchange_free": 0, "smoe_ep_exchange_status": 0, "smoe_decode_layer_status": 0,
+                    "smoe_matvec_status": 0, "smoe_matvec_set_wait_limit": 0, "smoe_hyper_connection": 3}
 launches = 0
 
 

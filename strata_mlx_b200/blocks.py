@@ -65,6 +65,50 @@ def window_matvec(blocks: torch.Tensor, kind: str, rows: int, cols: int, x: torc
     return _matvec(stack, x2, _zeros_idx(x2.shape[0], x.device), 1, x.dtype)
 
 
+# ---- Q3_K held as planes: the blocks rearranged once into aligned arrays of their parts (the same weights), so a
+# thread reads words where the file's 110-byte blocks give it bytes; 114 bytes a block (strata_mlx/blocks.py:399-401)
+Q3K_PLANE_BYTES = 114
+
+
+def q3k_planes(blocks: torch.Tensor, rows: int, cols: int) -> dict:
+    """A Q3_K tensor's blocks (rows, cols as the file has them) -> its planes {hm, qs, sc, dd}: the high-bit masks
+    (8 words a block), the two-bit codes (16 words), the scales less 32 (16 int8) and d (float16), made on the GPU
+    (strata_mlx/blocks.py:403-414)."""
+    _lib.require_cuda(blocks)
+    if cols % 256 or blocks.numel() != rows * row_bytes("Q3_K", cols):
+        raise ValueError(f"{blocks.numel()} bytes do not hold a Q3_K tensor of ({rows}, {cols})")
+    n = rows * (cols // 256)
+    dev = blocks.device
+    planes = {"hm": torch.empty(n * 8, dtype=torch.int32, device=dev), "qs": torch.empty(n * 16, dtype=torch.int32, device=dev),
+              "sc": torch.empty(n * 16, dtype=torch.int8, device=dev), "dd": torch.empty(n, dtype=torch.float16, device=dev)}
+    _lib.call("smoe_q3k_planes", _lib.ptr(blocks.reshape(-1).contiguous()), rows, cols, _lib.ptr(planes["hm"]),
+              _lib.ptr(planes["qs"]), _lib.ptr(planes["sc"]), _lib.ptr(planes["dd"]), _lib.stream())
+    return planes
+
+
+def q3k_planes_window(planes: dict, rows: int, cols: int, x: torch.Tensor) -> torch.Tensor:
+    """out[t] = W . x[t] for a Q3_K tensor held as planes, x (tokens, cols) -> (tokens, rows) in x's type
+    (strata_mlx/blocks.py:482-499). A warp a row, its lanes over the row's half blocks whatever the window, so a
+    token gets the same bits alone as in a window."""
+    _lib.require_cuda(x, *planes.values())
+    x2 = x.reshape(-1, cols).contiguous()
+    out = torch.empty((x2.shape[0], rows), dtype=x.dtype, device=x.device)
+    if x2.shape[0]:
+        _lib.call("smoe_q3k_planes_window", _lib.ptr(planes["hm"]), _lib.ptr(planes["qs"]), _lib.ptr(planes["sc"]),
+                  _lib.ptr(planes["dd"]), rows, cols, _lib.ptr(x2), x2.shape[0], _lib.ptr(out),
+                  _lib.dtype_code(x.dtype), _lib.stream())
+    return out
+
+
+def q3k_planes_dequantize(planes: dict, rows: int, cols: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """Every weight of a Q3_K tensor held as planes, (rows, cols): the block decoder's bits (blocks.py:502-512)."""
+    _lib.require_cuda(*planes.values())
+    out = torch.empty((rows, cols), dtype=dtype, device=planes["dd"].device)
+    _lib.call("smoe_q3k_planes_dequant", _lib.ptr(planes["hm"]), _lib.ptr(planes["qs"]), _lib.ptr(planes["sc"]),
+              _lib.ptr(planes["dd"]), rows, cols, _lib.ptr(out), _lib.dtype_code(dtype), _lib.stream())
+    return out
+
+
 def dequantize(blocks: torch.Tensor, kind: str, shape: tuple, dtype: torch.dtype = torch.float32) -> torch.Tensor:
     """The weights of `blocks` (uint8, a tensor of `shape` as the file holds it) as floats
     (strata_mlx/blocks.py:515-522). float16 results are bit-equal to gguf-py's weights rounded once."""
@@ -330,13 +374,15 @@ def matvec_batch(problems) -> None:
     _lib.call("smoe_matvec_batch", len(problems), arr, _lib.stream())
 
 
-def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, w=None, g=None):
+def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, w=None, g=None, batched_down=None):
     """(switch_mlp(x, indices), shared(x)) for a step that runs both on the decode matvec, with the routed and
     the shared expert's gate and up products in one launch (the same products, within the kernel's rounding,
     as the separate calls), then the two down products. With the combine's w (..., k) float32 and g (..., 1),
     the shared down product also forms the block's output, `moe_combine(y, w, g, shared(x))` (same bits), and
-    the result is (None, out). None where either would take another path (a prompt's tiles, unpacked floats, a
-    SwiGLU the down product does not take, activations of another type)."""
+    the result is (None, out). `batched_down` (default: the module's BATCHED_DOWN) puts both down products in
+    one launch and returns (y, s). None where either would take another path (a prompt's tiles, unpacked
+    floats, a SwiGLU the down product does not take, activations of another type). Indices at or past a stack's
+    expert count name pairs the products leave out (their rows are not written)."""
     lins = (switch_mlp.gate_proj, switch_mlp.up_proj, switch_mlp.down_proj)
     slins = (shared.gate_proj, shared.up_proj, shared.down_proj)
     if x.dtype != torch.float16 or indices.numel() >= TILES_FROM or not BLOCK_GLU:
@@ -362,7 +408,9 @@ def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, 
         ahead = [_problem(down, idx, pairs, 1, None), _problem(sd, zeros, tokens, 1, None)] if PREFETCH_DOWN else []
         matvec_batch([_problem(gate, idx, pairs, k, g_r, x=x2), _problem(up, idx, pairs, k, u_r, x=x2),
                       _problem(sg, zeros, tokens, 1, gs, x=x2), _problem(su, zeros, tokens, 1, us, x=x2)] + ahead)
-    if BATCHED_DOWN and sd.kind in FUSED_GLU and down.kind in FUSED_GLU:
+    if batched_down is None:
+        batched_down = BATCHED_DOWN
+    if batched_down and sd.kind in FUSED_GLU and down.kind in FUSED_GLU:
         # both down products in one launch (the shared expert's Q8_0 rows and the routed experts' in the same
         # CTAs, so the SMs stream one while they decode the other); the combine is its own launch
         y = torch.empty((pairs, down.output_dims), dtype=dt, device=dev)

@@ -1,0 +1,561 @@
+// The dense steps on either side of the MoE block in a decode pass:
+//
+//   hyper-connection  the read of the four residual streams before a block and the write of the block before it
+//                     (strata_mlx/fused.py:46-131, 280-323): norm, projection down, projection up and mix;
+//   Q3_K planes       a Q3_K tensor's blocks rearranged once into aligned planes, a window of tokens multiplied
+//                     on them, their weights as floats (strata_mlx/blocks.py:399-512);
+//   Q6_K parts        a Q6_K tensor as a signed byte a weight, a scale per 16 and d per 256 (ScaledLinear,
+//                     strata_mlx/dense.py:109-167; parts as strata_mlx/gguf.py:150-165 makes them), a window of
+//                     tokens multiplied on them, their weights as floats.
+//
+// Every product sums in float32 in an order fixed by the tensor's shape alone, so a token gets the same bits
+// alone as in a window (the reference's rule for these kernels, strata_mlx/fused.py:40, blocks.py:487-488).
+// All of them are small and bound by latency or by the bytes of the weights: one launch each, overlapped with
+// the launch before by programmatic dependent launch.
+#include <algorithm>
+
+#include "blocks.cuh"
+
+namespace smoe {
+namespace {
+
+constexpr int kDnThreads = 256;
+constexpr int kDnTok = 8;  // tokens a pass of the window products keeps in registers
+
+// ---- block reductions in a fixed order (xor tree in each warp, then the warps in order)
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    v = warp_sum(v);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float t = 0.0f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    return t;
+}
+
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<__half>(const __half* p, float (&v)[8]) {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(p));
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __half22float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+
+// ---------------------------------------------------------------- hyper-connection
+
+// One (stream, token) a CTA: h = before + out * inject_in; the residual h in T, normed = h rsqrt(mean h^2 + eps)
+// norm in float32 (strata_mlx/fused.py:63-90).
+template <typename T>
+__global__ void __launch_bounds__(kDnThreads) hc_norm_kernel(const T* __restrict__ before, const T* __restrict__ out,
+                                                             const T* __restrict__ inject_in, const T* __restrict__ norm,
+                                                             int hc, int d, float eps, T* __restrict__ residual,
+                                                             float* __restrict__ normed) {
+    __shared__ float red[kDnThreads / 32];
+    const int s = blockIdx.x, t = blockIdx.y;
+    const int64_t wide = int64_t(hc) * d;
+    pdl_wait();
+    const float back = to_f32(inject_in[int64_t(t) * hc + s]);
+    const T* b = before + int64_t(t) * wide + int64_t(s) * d;
+    const T* o = out + int64_t(t) * d;
+    float sq = 0.0f;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float h = fmaf(to_f32(o[i]), back, to_f32(b[i]));
+        sq = fmaf(h, h, sq);
+    }
+    const float total = block_sum(sq, red);
+    const float scale = rsqrtf(total / static_cast<float>(d) + eps);
+    T* res = residual + int64_t(t) * wide + int64_t(s) * d;
+    float* nrm = normed + int64_t(t) * wide + int64_t(s) * d;
+    const T* nw = norm + int64_t(s) * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float h = fmaf(to_f32(o[i]), back, to_f32(b[i]));
+        res[i] = from_f32<T>(h);
+        nrm[i] = h * scale * to_f32(nw[i]);
+    }
+    pdl_release();
+}
+
+// One row of `down` (or of the inject weight) a CTA, every token of the window: total = row . normed / hc; a
+// down row gives low = total sigmoid(total), an inject row inject = 2 sigmoid(total) in T
+// (strata_mlx/fused.py:92-119).
+template <typename T>
+__global__ void __launch_bounds__(kDnThreads) hc_down_kernel(const float* __restrict__ normed, const T* __restrict__ down,
+                                                             const T* __restrict__ inject_w, int rank, int hc,
+                                                             int64_t wide, int tokens, float* __restrict__ low,
+                                                             T* __restrict__ inject) {
+    __shared__ float red[kDnThreads / 32];
+    const int j = blockIdx.x;
+    const T* row = j < rank ? down + int64_t(j) * wide : inject_w + int64_t(j - rank) * wide;
+    pdl_wait();
+    for (int t0 = 0; t0 < tokens; t0 += kDnTok) {
+        const int nt = min(kDnTok, tokens - t0);
+        float acc[kDnTok];
+#pragma unroll
+        for (int tt = 0; tt < kDnTok; ++tt) acc[tt] = 0.0f;
+        for (int64_t i = int64_t(threadIdx.x) * 8; i < wide; i += int64_t(blockDim.x) * 8) {
+            float w[8];
+            load8(row + i, w);
+#pragma unroll
+            for (int tt = 0; tt < kDnTok; ++tt) {
+                if (tt < nt) {
+                    const float4* x = reinterpret_cast<const float4*>(normed + int64_t(t0 + tt) * wide + i);
+                    const float4 a = x[0], b = x[1];
+                    float v = acc[tt];
+                    v = fmaf(w[0], a.x, v), v = fmaf(w[1], a.y, v), v = fmaf(w[2], a.z, v), v = fmaf(w[3], a.w, v);
+                    v = fmaf(w[4], b.x, v), v = fmaf(w[5], b.y, v), v = fmaf(w[6], b.z, v), v = fmaf(w[7], b.w, v);
+                    acc[tt] = v;
+                }
+            }
+        }
+#pragma unroll
+        for (int tt = 0; tt < kDnTok; ++tt) {
+            if (tt < nt) {  // (uniform over the CTA)
+                const float total = block_sum(acc[tt], red) / static_cast<float>(hc);
+                if (threadIdx.x == 0) {
+                    const float gate = 1.0f / (1.0f + expf(-total));
+                    const int t = t0 + tt;
+                    if (j < rank) low[int64_t(t) * rank + j] = total * gate;
+                    else inject[int64_t(t) * hc + (j - rank)] = from_f32<T>(2.0f * gate);
+                }
+            }
+        }
+    }
+    pdl_release();
+}
+
+// 32 columns a CTA, each with its hc rows of `up` (hc x 32 threads): gate = up[s d + c] . low; the streams'
+// normed[s d + c] sigmoid(gate) mixed: mixed[c] = their sum / hc in T (strata_mlx/fused.py:121-146).
+template <typename T>
+__global__ void hc_up_kernel(const float* __restrict__ normed, const T* __restrict__ up, const float* __restrict__ low,
+                             int rank, int hc, int d, int tokens, T* __restrict__ mixed) {
+    extern __shared__ float sm[];
+    float* lows = sm;                          // [kDnTok][rank]
+    float* parts = sm + kDnTok * rank;         // [hc][32][kDnTok]
+    const int cc = threadIdx.x & 31, s = threadIdx.x >> 5;
+    const int c = blockIdx.x * 32 + cc;
+    const int64_t wide = int64_t(hc) * d;
+    const int64_t at = int64_t(s) * d + c;
+    pdl_wait();
+    for (int t0 = 0; t0 < tokens; t0 += kDnTok) {
+        const int nt = min(kDnTok, tokens - t0);
+        __syncthreads();
+        for (int i = threadIdx.x; i < nt * rank; i += blockDim.x) lows[i] = low[int64_t(t0) * rank + i];
+        __syncthreads();
+        if (c < d) {
+            float acc[kDnTok];
+#pragma unroll
+            for (int tt = 0; tt < kDnTok; ++tt) acc[tt] = 0.0f;
+            const T* row = up + at * rank;
+            for (int r = 0; r < rank; r += 8) {
+                float w[8];
+                load8(row + r, w);
+#pragma unroll
+                for (int tt = 0; tt < kDnTok; ++tt) {
+                    if (tt < nt) {
+                        const float* l = lows + tt * rank + r;
+                        float v = acc[tt];
+#pragma unroll
+                        for (int q = 0; q < 8; ++q) v = fmaf(w[q], l[q], v);
+                        acc[tt] = v;
+                    }
+                }
+            }
+#pragma unroll
+            for (int tt = 0; tt < kDnTok; ++tt)
+                if (tt < nt)
+                    parts[(s * 32 + cc) * kDnTok + tt] = normed[int64_t(t0 + tt) * wide + at] / (1.0f + expf(-acc[tt]));
+        }
+        __syncthreads();
+        if (s == 0 && c < d) {
+            for (int tt = 0; tt < nt; ++tt) {
+                float mix = 0.0f;
+                for (int k = 0; k < hc; ++k) mix += parts[(k * 32 + cc) * kDnTok + tt];
+                mixed[int64_t(t0 + tt) * d + c] = from_f32<T>(mix / static_cast<float>(hc));
+            }
+        }
+    }
+    pdl_release();
+}
+
+// ---------------------------------------------------------------- Q3_K planes
+
+// One block a thread: hm (32 bytes as 8 words), qs (64 bytes as 16 words), the 16 six-bit scales less 32 as
+// int8, d (strata_mlx/blocks.py:403-414).
+__global__ void q3k_planes_kernel(const uint8_t* __restrict__ blocks, int64_t n, uint32_t* __restrict__ hm,
+                                  uint32_t* __restrict__ qs, int8_t* __restrict__ sc, uint16_t* __restrict__ dd) {
+    for (int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; b < n; b += int64_t(gridDim.x) * blockDim.x) {
+        const uint8_t* p = blocks + b * Q3_K::kBytes;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) hm[b * 8 + w] = u32le(p + 4 * w);
+#pragma unroll
+        for (int w = 0; w < 16; ++w) qs[b * 16 + w] = u32le(p + 32 + 4 * w);
+#pragma unroll
+        for (int k = 0; k < 16; ++k) sc[b * 16 + k] = static_cast<int8_t>(Q3_K::scale(p + 96, k));
+        dd[b] = static_cast<uint16_t>(u16le(p + 108));
+    }
+}
+
+// weight i (0..31) of run rr of a half: two bits of the half's qs word, less 4 where the block's hmask bit is
+// clear (strata_mlx/blocks.py:420-424)
+__device__ __forceinline__ int q3k_value(uint32_t qw, uint32_t hw, int k, int j, int rr) {
+    return static_cast<int>((qw >> (8 * k + 2 * j)) & 3u) - (((hw >> (8 * k + rr)) & 1u) ? 0 : 4);
+}
+
+// A warp a row; lane l takes the halves (128 weights) l, l + 32, ... of the row; every token of the window per
+// pass (kDnTok at a time), sums in float32, the lanes added by an xor tree (strata_mlx/blocks.py:426-459).
+template <typename T>
+__global__ void q3k_window_kernel(const uint32_t* __restrict__ hm, const uint32_t* __restrict__ qs,
+                                  const int8_t* __restrict__ sc, const uint16_t* __restrict__ dd, int64_t rows, int cols,
+                                  const T* __restrict__ x, int tokens, T* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    pdl_wait();
+    if (r < rows) {
+        const int blocks = cols / 256;
+        for (int t0 = 0; t0 < tokens; t0 += kDnTok) {
+            const int nt = min(kDnTok, tokens - t0);
+            float sum[kDnTok];
+#pragma unroll
+            for (int tt = 0; tt < kDnTok; ++tt) sum[tt] = 0.0f;
+            for (int h = lane; h < 2 * blocks; h += 32) {
+                const int64_t blk = r * blocks + h / 2;
+                const int n = h & 1;
+                uint32_t hw[8], qw[8];
+#pragma unroll
+                for (int w = 0; w < 8; ++w) {
+                    hw[w] = __ldg(hm + blk * 8 + w);
+                    qw[w] = __ldg(qs + blk * 16 + 8 * n + w);
+                }
+                const float d = __half2float(__ushort_as_half(__ldg(dd + blk)));
+                const int64_t base = (h / 2) * 256 + 128 * n;
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int rr = 4 * n + j;
+                    const float s0 = d * float(sc[blk * 16 + 2 * rr]), s1 = d * float(sc[blk * 16 + 2 * rr + 1]);
+                    float a0[kDnTok], a1[kDnTok];
+#pragma unroll
+                    for (int tt = 0; tt < kDnTok; ++tt) a0[tt] = a1[tt] = 0.0f;
+#pragma unroll
+                    for (int w4 = 0; w4 < 8; ++w4) {
+                        float v[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) v[k] = float(q3k_value(qw[w4], hw[w4], k, j, rr));
+                        const int64_t xi = base + 32 * j + 4 * w4;
+#pragma unroll
+                        for (int tt = 0; tt < kDnTok; ++tt) {
+                            if (tt < nt) {
+                                const T* xr = x + int64_t(t0 + tt) * cols + xi;
+                                float p = 0.0f;
+#pragma unroll
+                                for (int k = 0; k < 4; ++k) p = fmaf(v[k], to_f32(xr[k]), p);
+                                if (w4 < 4) a0[tt] += p;
+                                else a1[tt] += p;
+                            }
+                        }
+                    }
+#pragma unroll
+                    for (int tt = 0; tt < kDnTok; ++tt) sum[tt] = fmaf(s0, a0[tt], fmaf(s1, a1[tt], sum[tt]));
+                }
+            }
+#pragma unroll
+            for (int tt = 0; tt < kDnTok; ++tt) {
+                const float total = warp_sum(sum[tt]);
+                if (lane == 0 && tt < nt) out[int64_t(t0 + tt) * rows + r] = from_f32<T>(total);
+            }
+        }
+    }
+    pdl_release();
+}
+
+// A thread a run of 32: d scale value as the block decoder gives it, (d * scale) * value
+// (strata_mlx/blocks.py:462-479)
+template <typename T>
+__global__ void q3k_planes_dequant_kernel(const uint32_t* __restrict__ hm, const uint32_t* __restrict__ qs,
+                                          const int8_t* __restrict__ sc, const uint16_t* __restrict__ dd, int64_t runs,
+                                          T* __restrict__ out) {
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < runs; i += int64_t(gridDim.x) * blockDim.x) {
+        const int rr = static_cast<int>(i & 7);
+        const int64_t blk = i >> 3;
+        const int n = rr >> 2, j = rr & 3;
+        const float d = __half2float(__ushort_as_half(dd[blk]));
+        const float s0 = mul_rn(d, float(sc[blk * 16 + 2 * rr])), s1 = mul_rn(d, float(sc[blk * 16 + 2 * rr + 1]));
+        T* o = out + blk * 256 + 32 * rr;
+        for (int w4 = 0; w4 < 8; ++w4) {
+            const uint32_t qw = qs[blk * 16 + 8 * n + w4], hw = hm[blk * 8 + w4];
+            for (int k = 0; k < 4; ++k)
+                o[4 * w4 + k] = from_f32<T>(mul_rn(w4 < 4 ? s0 : s1, float(q3k_value(qw, hw, k, j, rr))));
+        }
+    }
+}
+
+// ---------------------------------------------------------------- Q6_K parts (ScaledLinear)
+
+// One block a thread: codes (256 int8, the six bits less 32, in the weights' order), the 16 scales, d
+// (strata_mlx/gguf.py:150-165).
+__global__ void q6k_parts_kernel(const uint8_t* __restrict__ blocks, int64_t n, int8_t* __restrict__ codes,
+                                 int8_t* __restrict__ scales, uint16_t* __restrict__ d) {
+    for (int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; b < n; b += int64_t(gridDim.x) * blockDim.x) {
+        const uint8_t* p = blocks + b * Q6_K::kBytes;
+        int8_t* c = codes + b * 256;
+        for (int h = 0; h < 2; ++h)
+            for (int q = 0; q < 4; ++q)
+                for (int l = 0; l < 32; ++l) {
+                    const uint32_t lo = (uint32_t(p[64 * h + 32 * (q & 1) + l]) >> (4 * (q >> 1))) & 15u;
+                    const uint32_t hi = (uint32_t(p[128 + 32 * h + l]) >> (2 * q)) & 3u;
+                    c[128 * h + 32 * q + l] = static_cast<int8_t>(static_cast<int>(lo | (hi << 4)) - 32);
+                }
+        for (int k = 0; k < 16; ++k) scales[b * 16 + k] = static_cast<int8_t>(p[192 + k]);
+        d[b] = static_cast<uint16_t>(u16le(p + 208));
+    }
+}
+
+// A warp a row, lane l the groups of 16 weights l, l + 32, ...: per group s = d scale and s (codes . x); float32
+// (strata_mlx/dense.py:30-72)
+template <typename T>
+__global__ void scaled_window_kernel(const int8_t* __restrict__ codes, const int8_t* __restrict__ scales,
+                                     const uint16_t* __restrict__ dv, int64_t rows, int cols, int d_step,
+                                     const T* __restrict__ x, int tokens, T* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    pdl_wait();
+    if (r < rows) {
+        const int groups = cols / 16, per_d = cols / d_step;
+        for (int t0 = 0; t0 < tokens; t0 += kDnTok) {
+            const int nt = min(kDnTok, tokens - t0);
+            float sum[kDnTok];
+#pragma unroll
+            for (int tt = 0; tt < kDnTok; ++tt) sum[tt] = 0.0f;
+            for (int g = lane; g < groups; g += 32) {
+                const uint4 raw = __ldg(reinterpret_cast<const uint4*>(codes + r * cols) + g);
+                const int8_t* cv = reinterpret_cast<const int8_t*>(&raw);
+                const float s = __half2float(__ushort_as_half(__ldg(dv + r * per_d + (16 * g) / d_step))) *
+                                float(__ldg(scales + r * groups + g));
+#pragma unroll
+                for (int tt = 0; tt < kDnTok; ++tt) {
+                    if (tt < nt) {
+                        const T* xr = x + int64_t(t0 + tt) * cols + 16 * g;
+                        float a = 0.0f;
+#pragma unroll
+                        for (int v = 0; v < 16; ++v) a = fmaf(float(cv[v]), to_f32(xr[v]), a);
+                        sum[tt] = fmaf(s, a, sum[tt]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int tt = 0; tt < kDnTok; ++tt) {
+                const float total = warp_sum(sum[tt]);
+                if (lane == 0 && tt < nt) out[int64_t(t0 + tt) * rows + r] = from_f32<T>(total);
+            }
+        }
+    }
+    pdl_release();
+}
+
+// every weight: (float(d) * float(scale)) * float(code) rounded once to T (strata_mlx/dense.py:75-84)
+template <typename T>
+__global__ void scaled_floats_kernel(const int8_t* __restrict__ codes, const int8_t* __restrict__ scales,
+                                     const uint16_t* __restrict__ dv, int64_t rows, int cols, int d_step,
+                                     T* __restrict__ out) {
+    const int64_t groups = int64_t(rows) * (cols / 16);
+    for (int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; g < groups; g += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t r = g / (cols / 16), gc = g - r * (cols / 16);
+        const float s = mul_rn(__half2float(__ushort_as_half(dv[r * (cols / d_step) + (16 * gc) / d_step])),
+                               float(scales[g]));
+        const int8_t* c = codes + r * cols + 16 * gc;
+        T* o = out + r * cols + 16 * gc;
+        for (int i = 0; i < 16; ++i) o[i] = from_f32<T>(mul_rn(s, float(c[i])));
+    }
+}
+
+unsigned grid_of(int64_t items, int threads) {
+    return static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>((items + threads - 1) / threads, 148 * 16)));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace smoe
+
+using namespace smoe;
+
+// ---------------------------------------------------------------- hyper-connection entry points
+
+extern "C" size_t smoe_hyper_workspace_size(int64_t tokens, int64_t hc, int64_t d, int64_t rank) {
+    if (tokens < 0 || hc < 1 || d < 1 || rank < 1) return 0;
+    return size_t(((tokens * hc * d * 4 + 255) & ~int64_t(255)) + tokens * rank * 4);
+}
+
+extern "C" int smoe_hyper_connection(const SmoeHyper* h, const void* before, const void* out, const void* inject_in,
+                                     int64_t tokens, void* mixed, void* residual, void* inject, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    SMOE_REQUIRE(h, SMOE_EARG, "hyper_connection: null spec");
+    SMOE_REQUIRE(h->hc >= 1 && h->hc <= 8, SMOE_ESHAPE, "hyper_connection: 1 to 8 streams");
+    SMOE_REQUIRE(h->d >= 1 && h->d % 8 == 0 && h->rank >= 8 && h->rank % 8 == 0 && h->rank <= 1024, SMOE_ESHAPE,
+                 "hyper_connection: d and rank must be multiples of 8 (rank 8..1024)");
+    SMOE_REQUIRE(tokens >= 0 && tokens <= 65535, SMOE_ESHAPE, "hyper_connection: too many tokens");
+    SMOE_REQUIRE(h->dtype == SMOE_F16 || h->dtype == SMOE_F32, SMOE_EDTYPE, "hyper_connection: float16 or float32");
+    if (tokens == 0) return SMOE_OK;
+    SMOE_REQUIRE(before && out && inject_in && mixed && residual && h->norm && h->down && h->up, SMOE_EARG,
+                 "hyper_connection: null pointer");
+    SMOE_REQUIRE(!h->inject_w || inject, SMOE_EARG, "hyper_connection: an inject weight needs an inject output");
+    SMOE_REQUIRE(aligned16(h->down) && aligned16(h->up) && (!h->inject_w || aligned16(h->inject_w)), SMOE_EARG,
+                 "hyper_connection: weights must be 16-byte aligned");
+    SMOE_REQUIRE(workspace && workspace_bytes >= smoe_hyper_workspace_size(tokens, h->hc, h->d, h->rank),
+                 SMOE_EWORKSPACE, "hyper_connection: workspace too small");
+    const int hc = static_cast<int>(h->hc), d = static_cast<int>(h->d), rank = static_cast<int>(h->rank);
+    const int64_t wide = int64_t(hc) * d;
+    float* normed = static_cast<float*>(workspace);
+    float* low = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + ((tokens * wide * 4 + 255) & ~int64_t(255)));
+    const int n_inject = h->inject_w ? hc : 0;
+    cudaStream_t st = as_stream(stream);
+    const size_t esz = h->dtype == SMOE_F16 ? 2 : 4;
+    const size_t up_smem = size_t(kDnTok) * rank * 4 + size_t(hc) * 32 * kDnTok * 4;
+    auto go = [&](auto tag) -> int {
+        using T = decltype(tag);
+        cudaError_t e = launch_pdl(Writes().add(residual, tokens * wide * esz).add(normed, tokens * wide * 4),
+                                   hc_norm_kernel<T>, dim3(hc, static_cast<unsigned>(tokens)), dim3(kDnThreads), 0, st,
+                                   static_cast<const T*>(before), static_cast<const T*>(out),
+                                   static_cast<const T*>(inject_in), static_cast<const T*>(h->norm), hc, d, h->eps,
+                                   static_cast<T*>(residual), normed);
+        if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("hc_norm: ") + cudaGetErrorString(e));
+        e = launch_pdl(Writes().add(low, tokens * rank * 4).add(n_inject ? inject : nullptr, tokens * hc * esz),
+                       hc_down_kernel<T>, dim3(rank + n_inject), dim3(kDnThreads), 0, st, normed,
+                       static_cast<const T*>(h->down), static_cast<const T*>(h->inject_w), rank, hc, wide,
+                       static_cast<int>(tokens), low, static_cast<T*>(inject));
+        if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("hc_down: ") + cudaGetErrorString(e));
+        if (int s = max_smem(hc_up_kernel<T>, static_cast<int>(up_smem))) return fail(s, "hc_up: shared memory");
+        e = launch_pdl(Writes().add(mixed, tokens * d * esz), hc_up_kernel<T>, dim3((d + 31) / 32), dim3(32 * hc),
+                       up_smem, st, normed, static_cast<const T*>(h->up), low, rank, hc, d, static_cast<int>(tokens),
+                       static_cast<T*>(mixed));
+        if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("hc_up: ") + cudaGetErrorString(e));
+        return launch_status("hyper_connection");
+    };
+    return h->dtype == SMOE_F16 ? go(__half()) : go(float());
+}
+
+// ---------------------------------------------------------------- Q3_K planes entry points
+
+extern "C" int smoe_q3k_planes(const uint8_t* blocks, int64_t rows, int64_t cols, uint32_t* hm, uint32_t* qs,
+                               int8_t* sc, uint16_t* dd, void* stream) {
+    SMOE_REQUIRE(rows >= 0 && cols > 0 && cols % 256 == 0, SMOE_ESHAPE, "q3k_planes: rows of whole blocks");
+    const int64_t n = rows * (cols / 256);
+    if (n == 0) return SMOE_OK;
+    SMOE_REQUIRE(blocks && hm && qs && sc && dd, SMOE_EARG, "q3k_planes: null pointer");
+    q3k_planes_kernel<<<grid_of(n, 128), 128, 0, as_stream(stream)>>>(blocks, n, hm, qs, sc, dd);
+    return launch_status("q3k_planes");
+}
+
+extern "C" int smoe_q3k_planes_window(const uint32_t* hm, const uint32_t* qs, const int8_t* sc, const uint16_t* dd,
+                                      int64_t rows, int64_t cols, const void* x, int64_t tokens, void* out, int dtype,
+                                      void* stream) {
+    SMOE_REQUIRE(rows >= 1 && cols > 0 && cols % 256 == 0 && cols <= (1 << 24), SMOE_ESHAPE,
+                 "q3k_planes_window: rows of whole blocks");
+    if (tokens == 0) return SMOE_OK;
+    SMOE_REQUIRE(hm && qs && sc && dd && x && out && tokens > 0, SMOE_EARG, "q3k_planes_window: bad arguments");
+    const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
+    cudaStream_t st = as_stream(stream);
+    cudaError_t e;
+    if (dtype == SMOE_F16)
+        e = launch_pdl(Writes().add(out, tokens * rows * 2), q3k_window_kernel<__half>, dim3(grid), dim3(256), 0, st,
+                       hm, qs, sc, dd, rows, static_cast<int>(cols), static_cast<const __half*>(x),
+                       static_cast<int>(tokens), static_cast<__half*>(out));
+    else if (dtype == SMOE_F32)
+        e = launch_pdl(Writes().add(out, tokens * rows * 4), q3k_window_kernel<float>, dim3(grid), dim3(256), 0, st,
+                       hm, qs, sc, dd, rows, static_cast<int>(cols), static_cast<const float*>(x),
+                       static_cast<int>(tokens), static_cast<float*>(out));
+    else
+        return fail(SMOE_EDTYPE, "q3k_planes_window: float16 or float32 activations");
+    if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("q3k_planes_window: ") + cudaGetErrorString(e));
+    return launch_status("q3k_planes_window");
+}
+
+extern "C" int smoe_q3k_planes_dequant(const uint32_t* hm, const uint32_t* qs, const int8_t* sc, const uint16_t* dd,
+                                       int64_t rows, int64_t cols, void* out, int dtype, void* stream) {
+    SMOE_REQUIRE(rows >= 0 && cols > 0 && cols % 256 == 0, SMOE_ESHAPE, "q3k_planes_dequant: rows of whole blocks");
+    const int64_t runs = rows * cols / 32;
+    if (runs == 0) return SMOE_OK;
+    SMOE_REQUIRE(hm && qs && sc && dd && out, SMOE_EARG, "q3k_planes_dequant: null pointer");
+    cudaStream_t st = as_stream(stream);
+    if (dtype == SMOE_F16)
+        q3k_planes_dequant_kernel<__half><<<grid_of(runs, 256), 256, 0, st>>>(hm, qs, sc, dd, runs,
+                                                                              static_cast<__half*>(out));
+    else if (dtype == SMOE_F32)
+        q3k_planes_dequant_kernel<float><<<grid_of(runs, 256), 256, 0, st>>>(hm, qs, sc, dd, runs,
+                                                                             static_cast<float*>(out));
+    else
+        return fail(SMOE_EDTYPE, "q3k_planes_dequant: float16 or float32");
+    return launch_status("q3k_planes_dequant");
+}
+
+// ---------------------------------------------------------------- Q6_K parts entry points
+
+extern "C" int smoe_q6k_parts(const uint8_t* blocks, int64_t rows, int64_t cols, int8_t* codes, int8_t* scales,
+                              uint16_t* d, void* stream) {
+    SMOE_REQUIRE(rows >= 0 && cols > 0 && cols % 256 == 0, SMOE_ESHAPE, "q6k_parts: rows of whole blocks");
+    const int64_t n = rows * (cols / 256);
+    if (n == 0) return SMOE_OK;
+    SMOE_REQUIRE(blocks && codes && scales && d, SMOE_EARG, "q6k_parts: null pointer");
+    q6k_parts_kernel<<<grid_of(n, 128), 128, 0, as_stream(stream)>>>(blocks, n, codes, scales, d);
+    return launch_status("q6k_parts");
+}
+
+extern "C" int smoe_scaled_window(const int8_t* codes, const int8_t* scales, const uint16_t* d, int64_t rows,
+                                  int64_t cols, int64_t d_step, const void* x, int64_t tokens, void* out, int dtype,
+                                  void* stream) {
+    SMOE_REQUIRE(rows >= 1 && cols > 0 && cols % 16 == 0 && cols <= (1 << 24), SMOE_ESHAPE,
+                 "scaled_window: rows of whole groups of 16");
+    SMOE_REQUIRE(d_step >= 16 && d_step % 16 == 0 && cols % d_step == 0, SMOE_ESHAPE,
+                 "scaled_window: d must cover whole groups of 16 and divide the row");
+    if (tokens == 0) return SMOE_OK;
+    SMOE_REQUIRE(codes && scales && d && x && out && tokens > 0, SMOE_EARG, "scaled_window: bad arguments");
+    SMOE_REQUIRE(aligned16(codes), SMOE_EARG, "scaled_window: codes must be 16-byte aligned");
+    const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
+    cudaStream_t st = as_stream(stream);
+    cudaError_t e;
+    if (dtype == SMOE_F16)
+        e = launch_pdl(Writes().add(out, tokens * rows * 2), scaled_window_kernel<__half>, dim3(grid), dim3(256), 0,
+                       st, codes, scales, d, rows, static_cast<int>(cols), static_cast<int>(d_step),
+                       static_cast<const __half*>(x), static_cast<int>(tokens), static_cast<__half*>(out));
+    else if (dtype == SMOE_F32)
+        e = launch_pdl(Writes().add(out, tokens * rows * 4), scaled_window_kernel<float>, dim3(grid), dim3(256), 0,
+                       st, codes, scales, d, rows, static_cast<int>(cols), static_cast<int>(d_step),
+                       static_cast<const float*>(x), static_cast<int>(tokens), static_cast<float*>(out));
+    else
+        return fail(SMOE_EDTYPE, "scaled_window: float16 or float32 activations");
+    if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("scaled_window: ") + cudaGetErrorString(e));
+    return launch_status("scaled_window");
+}
+
+extern "C" int smoe_scaled_floats(const int8_t* codes, const int8_t* scales, const uint16_t* d, int64_t rows,
+                                  int64_t cols, int64_t d_step, void* out, int dtype, void* stream) {
+    SMOE_REQUIRE(rows >= 0 && cols > 0 && cols % 16 == 0 && d_step >= 16 && d_step % 16 == 0 && cols % d_step == 0,
+                 SMOE_ESHAPE, "scaled_floats: rows of whole groups of 16");
+    const int64_t groups = rows * (cols / 16);
+    if (groups == 0) return SMOE_OK;
+    SMOE_REQUIRE(codes && scales && d && out, SMOE_EARG, "scaled_floats: null pointer");
+    cudaStream_t st = as_stream(stream);
+    if (dtype == SMOE_F16)
+        scaled_floats_kernel<__half><<<grid_of(groups, 256), 256, 0, st>>>(codes, scales, d, rows, static_cast<int>(cols),
+                                                                           static_cast<int>(d_step),
+                                                                           static_cast<__half*>(out));
+    else if (dtype == SMOE_F32)
+        scaled_floats_kernel<float><<<grid_of(groups, 256), 256, 0, st>>>(codes, scales, d, rows, static_cast<int>(cols),
+                                                                          static_cast<int>(d_step),
+                                                                          static_cast<float*>(out));
+    else
+        return fail(SMOE_EDTYPE, "scaled_floats: float16 or float32");
+    return launch_status("scaled_floats");
+}

@@ -32,6 +32,16 @@
 #include "mv8_dev.cuh"
 
 namespace smoe {
+// A wait for a weight copy that gives up (it should not: each is bounded, about a second) records SMOE_ETIMEOUT
+// here; the launch's outputs are then not valid. smoe_matvec_status reads and clears it. g_mv8_polls is the
+// bound in polls (each suspends up to 1 ms), settable for tests.
+static __device__ int g_mv8_status = 0;
+static __device__ uint32_t g_mv8_polls = kM8WaitLimit;
+
+__device__ __forceinline__ void mv8_gave_up(int lane) {
+    if (lane == 0) atomicExch(&g_mv8_status, SMOE_ETIMEOUT);
+}
+
 // ---------------------------------------------------------------- one stack (or a gate / up pair)
 // The kernel the single entry points use: its geometry (stage, row stride) is the block type's, known at
 // compile time.
@@ -219,8 +229,9 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     // a wait that gives up (it should not) leaves the warp's remaining stages undone but keeps it in step
     // with its team's barriers
     bool ok = true;
+    const uint32_t polls = g_mv8_polls;
     float total[2] = {0.f, 0.f};
-    int slot = 0, consumed = 0;
+    int slot = 0, waited = 0;
     uint32_t phase = 0;
     for (int job = 0; job < my_jobs; ++job) {
         const int prob = __shfl_sync(0xffffffffu, j_prob, job);
@@ -238,10 +249,13 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         for (int k = 0; k < my_stages; ++k, pos += team * D::kStageBytes, xc += team * D::kStageCols) {
             // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
             __syncwarp();
-            if (i_job < my_jobs) issue();
+            if (ok && i_job < my_jobs) issue();  // (after a wait gave up, nothing more is copied)
             const int cur = slot;
-            if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, kM8WaitLimit));
-            ++consumed;
+            if (ok) {
+                ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, polls));
+                if (ok) ++waited;
+                else mv8_gave_up(lane);
+            }
             if (++slot == ns) {
                 slot = 0;
                 phase ^= 1;
@@ -287,10 +301,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     // the next kernel may start placing its CTAs (releasing right after the wait instead measured slower: the
     // waiting CTAs of the next kernel crowd the running ones)
     pdl_release();
-    // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
-    // a wait gave up)
+    // no copy may still be writing this CTA's shared memory when it exits: every item was waited for, unless a
+    // wait gave up; then the items from the one it gave up on are waited for here with the full bound (no item
+    // was issued after it)
     if (!ok && lane == 0)
-        for (int i = consumed; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
+        for (int i = waited; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, kM8WaitLimit);
     __syncwarp();
 }
 
@@ -481,8 +496,9 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     // a wait that gives up (it should not) leaves the warp's remaining stages undone but keeps it in step
     // with its team's barriers
     bool ok = true;
+    const uint32_t polls = g_mv8_polls;
     float total[2] = {0.f, 0.f};
-    int slot = 0, consumed = 0;
+    int slot = 0, waited = 0;
     uint32_t phase = 0;
     for (int job = 0; job < my_jobs; ++job) {
         const int pr = __shfl_sync(0xffffffffu, j_prob, job);
@@ -506,10 +522,13 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
         for (int k = 0; k < n; ++k, pos += step, xc += xstep) {
             // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
             __syncwarp();
-            if (i_job < my_jobs) issue();
+            if (ok && i_job < my_jobs) issue();  // (after a wait gave up, nothing more is copied)
             const int cur = slot;
-            if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, kM8WaitLimit));
-            ++consumed;
+            if (ok) {
+                ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, polls));
+                if (ok) ++waited;
+                else mv8_gave_up(lane);
+            }
             if (++slot == ns) {
                 slot = 0;
                 phase ^= 1;
@@ -562,10 +581,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     // the next kernel may start placing its CTAs (releasing right after the wait instead measured slower: the
     // waiting CTAs of the next kernel crowd the running ones)
     pdl_release();
-    // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
-    // a wait gave up)
+    // no copy may still be writing this CTA's shared memory when it exits: every item was waited for, unless a
+    // wait gave up; then the items from the one it gave up on are waited for here with the full bound (no item
+    // was issued after it)
     if (!ok && lane == 0)
-        for (int i = consumed; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
+        for (int i = waited; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, kM8WaitLimit);
     __syncwarp();
 }
 
@@ -901,3 +921,27 @@ int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t 
 }
 
 }  // namespace smoe
+
+using namespace smoe;
+
+extern "C" int smoe_matvec_status(int* status, int clear) {
+    SMOE_REQUIRE(status, SMOE_EARG, "matvec_status: null pointer");
+    int v = 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_mv8_status, sizeof(int));
+    if (e == cudaSuccess && clear) {
+        const int zero = 0;
+        e = cudaMemcpyToSymbol(g_mv8_status, &zero, sizeof(int));
+    }
+    if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("matvec_status: ") + cudaGetErrorString(e));
+    *status = v;
+    return SMOE_OK;
+}
+
+extern "C" int smoe_matvec_set_wait_limit(int64_t polls) {
+    const uint32_t v = polls < 0 ? kM8WaitLimit : static_cast<uint32_t>(std::min<int64_t>(polls, kM8WaitLimit));
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_mv8_polls, &v, sizeof(v));
+    if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("matvec_set_wait_limit: ") + cudaGetErrorString(e));
+    return SMOE_OK;
+}

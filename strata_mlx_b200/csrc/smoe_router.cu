@@ -128,10 +128,12 @@ __global__ void combine_kernel(const T* __restrict__ y, const float* __restrict_
 // lidx = idx - lo for experts of this rank's range [lo, lo + count), else count (a pair the kernels leave out)
 __global__ void localize_kernel(const uint32_t* __restrict__ idx, int64_t n, uint32_t lo, uint32_t count,
                                 uint32_t* __restrict__ out) {
+    pdl_wait();
     for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x) {
         const uint32_t e = idx[i];
         out[i] = (e >= lo && e - lo < count) ? e - lo : count;
     }
+    pdl_release();
 }
 
 // sums[t, 0:d] = this rank's share of sum_k y_k w_k (pairs of its experts only, MLX's order among them);
@@ -178,7 +180,10 @@ extern "C" int smoe_localize(const uint32_t* idx, int64_t n, int64_t lo, int64_t
     SMOE_REQUIRE(idx && out && n > 0 && lo >= 0 && count > 0 && lo + count <= 0xffffffffLL, SMOE_EARG,
                  "localize: bad arguments");
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 1024));
-    localize_kernel<<<grid, 256, 0, as_stream(stream)>>>(idx, n, static_cast<uint32_t>(lo), static_cast<uint32_t>(count), out);
+    const cudaError_t e = launch_pdl(Writes().add(out, size_t(n) * 4), localize_kernel, dim3(grid), dim3(256), 0,
+                                     as_stream(stream), idx, n, static_cast<uint32_t>(lo), static_cast<uint32_t>(count),
+                                     out);
+    if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("localize: ") + cudaGetErrorString(e));
     return launch_status("localize");
 }
 

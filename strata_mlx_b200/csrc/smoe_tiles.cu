@@ -142,7 +142,7 @@ extern "C" int smoe_tiles_of(const int32_t* indices, int64_t pairs, int64_t k, i
     int32_t* rank = hist + chunks * experts;
     cudaStream_t st = as_stream(stream);
     const size_t smem = size_t(kTsWarps) * experts * 4;
-    max_smem(tiles_rank_kernel, static_cast<int>(smem));
+    if (int s = max_smem(tiles_rank_kernel, static_cast<int>(smem))) return fail(s, "tiles_of: shared memory limit");
     tiles_rank_kernel<<<static_cast<unsigned>(chunks), kTsChunk, smem, st>>>(indices, pairs, static_cast<int>(experts),
                                                                              hist, rank, token, most * kTile);
     if (int s = launch_status("tiles_of rank")) return s;
@@ -175,7 +175,10 @@ std::mutex g_scratch_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
 // The device address of g_tiles_scratch on the current device. In host code the array's name is only a
-// host-side handle, not a device address, so it is looked up once per device with cudaGetSymbolAddress.
+// host-side handle, not a device address, so it is looked up once per device with cudaGetSymbolAddress and kept
+// for the life of the process: a device reset (cudaDeviceReset, or the primary context torn down and made again)
+// leaves the kept address stale, so a process that resets a device must not call smoe_tiles_of_noalloc on it
+// afterwards.
 int scratch_on_current_device(void** addr) {
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);

@@ -4,6 +4,7 @@
     top_k          the k largest logits of each row, largest first, ties to the lower index
     moe_combine    sum_k y_k w_k rounded to the type, plus sigmoid(g) * the shared expert, in MLX's order
     SparseMoeBlock the model's MoE block as `_Routed.__call__` computes it (strata_mlx/fused.py:484-497)
+    FusedResidual  the hyper-connection before and after every block: norm, low-rank gate, mix (fused.py:280-323)
 
 Names and conventions follow the reference; tensors are torch CUDA tensors and every product runs in the
 sm_100a kernels of libstrata_moe.so.
@@ -235,6 +236,47 @@ class SparseMoeBlock:
 
 
 _Routed = SparseMoeBlock
+
+
+class FusedResidual:
+    """A hyper-connection of the model (its `GatedResidual`) with the write of the block before it folded into its
+    read, on three sm_100a kernels (`smoe_hyper_connection`; strata_mlx/fused.py:280-323).
+
+    `gr` has the model's weights: `hc_norm.weight` (hc d), `input_mix_weight_down.weight` (rank, hc d),
+    `input_mix_weight_up.weight` (hc d, rank), `block_inject_weight` (None, or with `.weight` (hc, hc d)) and `hc`,
+    as torch CUDA tensors of the activations' type. Any window of tokens takes the same kernels, and a token gets
+    the same bits alone as in a window."""
+
+    def __init__(self, gr, eps: float = 1e-6):
+        self.norm = gr.hc_norm.weight
+        self.down, self.up = gr.input_mix_weight_down.weight, gr.input_mix_weight_up.weight
+        inj = getattr(gr, "block_inject_weight", None)
+        self.inject_w = inj.weight if inj is not None else None
+        self.rank, self.wide = self.down.shape
+        self.hc, self.eps = int(gr.hc), eps
+        _lib.require_cuda(self.norm, self.down, self.up, self.inject_w)
+
+    def __call__(self, before: torch.Tensor, out: torch.Tensor, inject_in: torch.Tensor):
+        """before (1, T, hc d), out (1, T, d), inject_in (1, T, hc): the residual is before + out * inject_in.
+
+        Returns (the block's input (1, T, d), the residual (1, T, hc d), inject for the block's output (1, T, hc))."""
+        _lib.require_cuda(before, out, inject_in)
+        T, d, dtype = before.shape[1], out.shape[2], before.dtype
+        if out.dtype != dtype or inject_in.dtype != dtype or self.down.dtype != dtype:
+            raise ValueError("FusedResidual takes weights and activations of one type (float16 or float32)")
+        dev = before.device
+        mixed = torch.empty((T, d), dtype=dtype, device=dev)
+        residual = torch.empty((T, self.wide), dtype=dtype, device=dev)
+        inject = torch.empty((T, self.hc), dtype=dtype, device=dev) if self.inject_w is not None else None
+        nbytes = int(_lib.lib().smoe_hyper_workspace_size(T, self.hc, d, self.rank))
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+        spec = _lib.SmoeHyper(self.norm.data_ptr(), self.down.data_ptr(), self.up.data_ptr(),
+                              self.inject_w.data_ptr() if self.inject_w is not None else None, self.hc, d, self.rank,
+                              self.eps, _lib.dtype_code(dtype))
+        _lib.call("smoe_hyper_connection", ctypes.byref(spec), _lib.ptr(before.reshape(T, -1).contiguous()),
+                  _lib.ptr(out.reshape(T, d).contiguous()), _lib.ptr(inject_in.reshape(T, self.hc).contiguous()), T,
+                  _lib.ptr(mixed), _lib.ptr(residual), _lib.ptr(inject), _lib.ptr(ws), ws.numel(), _lib.stream())
+        return mixed[None], residual[None], (inject[None] if inject is not None else inject_in)
 
 
 def install_routers(layers) -> None:

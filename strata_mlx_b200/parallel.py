@@ -21,12 +21,15 @@ result differs from one device's only where the receiving rank's pair count choo
 No TMA multicast anywhere.
 """
 
+import ctypes
+
 import torch
 import torch.distributed as dist
 
 from . import _lib
-from .blocks import BlockLinear, BlockMLP, BlockSwitchGLU, BlockSwitchLinear, gate_up, matvec_glu, row_bytes
-from .fused import SparseMoeBlock, WindowLinear, top_k_softmax
+from .blocks import (BlockLinear, BlockMLP, BlockSwitchGLU, BlockSwitchLinear, decode_products, gate_up, matvec_glu,
+                     row_bytes)
+from .fused import SparseMoeBlock, WindowLinear, route, top_k_softmax
 
 
 def expert_range(rank: int, world: int, experts: int):
@@ -84,16 +87,101 @@ def shard_layer(router, gate, up, down, shared, shared_gate, top_k: int, rank: i
     return SparseMoeBlock(router, sw, sh, shared_gate, top_k)
 
 
+class PeerExchange:
+    """The buffers of a decode step's one exchange over NVLink peer memory (`smoe_ep_reduce_combine`): one per
+    rank, `hidden` values of up to `max_tokens` tokens, mapped by every rank of the node through CUDA IPC
+    handles. Make it on every rank of `group` at the same point (the handles are all-gathered); the calls that
+    use it must be ordered on one stream per rank, and every rank must make the same calls in the same order.
+
+    `reduce_combine` is the end of an expert-parallel MoE block: each rank's partial sums go to every rank, are
+    added in rank order and rounded as the combine rounds them, so every rank gets the same bits. A wait that
+    gives up (a rank that never arrives) leaves the outputs unwritten and `failed()` true."""
+
+    HANDLE = 64
+
+    def __init__(self, rank: int, world: int, hidden: int, max_tokens: int = 64, group=None, device=None):
+        self.rank, self.world, self.hidden, self.max_tokens = rank, world, hidden, max_tokens
+        self.device = device or torch.device("cuda", torch.cuda.current_device())
+        nbytes = int(_lib.lib().smoe_ep_exchange_bytes(world, max_tokens, hidden))
+        if nbytes == 0:
+            raise ValueError(f"no exchange for {world} ranks of {max_tokens} x {hidden} values")
+        buf, handle = ctypes.c_void_p(), (ctypes.c_uint8 * self.HANDLE)()
+        with torch.cuda.device(self.device):
+            _lib.call("smoe_ep_exchange_alloc", nbytes, ctypes.byref(buf), handle)
+        self.buffer = buf.value
+        self.peers, self._opened = [], []
+        if world == 1:
+            self.peers = [self.buffer]
+            return
+        mine = torch.tensor(list(bytes(handle)), dtype=torch.uint8, device=self.device)
+        everyone = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(everyone, mine, group=group)
+        for r, h in enumerate(everyone):
+            if r == rank:
+                self.peers.append(self.buffer)
+                continue
+            hb = (ctypes.c_uint8 * self.HANDLE)(*h.cpu().tolist())
+            p = ctypes.c_void_p()
+            with torch.cuda.device(self.device):
+                _lib.call("smoe_ep_exchange_open", hb, ctypes.byref(p))
+            self.peers.append(p.value)
+            self._opened.append(p.value)
+
+    def spec(self, y, w, lidx, experts: int, s, g, out, wait_polls: int = 0) -> "_lib.SmoeEpReduce":
+        tokens, k = w.shape[0], w.shape[-1]
+        d = out.shape[-1]
+        return _lib.SmoeEpReduce(self.rank, self.world, (ctypes.c_void_p * 16)(*self.peers), y.data_ptr(),
+                                 w.data_ptr(), lidx.data_ptr(), experts, s.data_ptr() if s is not None else None,
+                                 g.data_ptr(), tokens, k, d, self.max_tokens * self.hidden, out.data_ptr(),
+                                 _lib.dtype_code(out.dtype), wait_polls)
+
+    def reduce_combine(self, y, w, lidx, experts: int, s, g, out, wait_polls: int = 0) -> torch.Tensor:
+        """out (tokens, hidden) = the block's end from every rank's y (tokens, k, hidden) of its experts, w
+        (tokens, k) float32, lidx (tokens, k) local experts (>= `experts` for another rank's), s (tokens, hidden)
+        its slice of the shared expert (or None) and g (tokens) the shared expert's gate value."""
+        _lib.require_cuda(y, w, lidx, g, out, s)
+        if out.shape[0] > self.max_tokens or out.shape[-1] != self.hidden:
+            raise ValueError(f"the exchange holds up to {self.max_tokens} tokens of {self.hidden}")
+        spec = self.spec(y, w, lidx, experts, s, g, out, wait_polls)
+        _lib.call("smoe_ep_reduce_combine", ctypes.byref(spec), _lib.stream())
+        return out
+
+    def failed(self, clear: bool = False) -> bool:
+        """Whether a wait of this rank's exchange gave up (synchronizes the device)."""
+        flag = ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            _lib.call("smoe_ep_exchange_status", ctypes.c_void_p(self.buffer), ctypes.byref(flag), int(clear))
+        return flag.value != 0
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after every rank is done with it: barrier first)."""
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                _lib.call("smoe_ep_exchange_close", ctypes.c_void_p(p))
+            self._opened = []
+            if self.buffer:
+                _lib.call("smoe_ep_exchange_free", ctypes.c_void_p(self.buffer))
+                self.buffer = None
+
+
 class ExpertParallelMoE:
     """A MoE block whose experts are spread over the ranks of `group`: call it on every rank with the same x.
 
     `layer` is this rank's part (`shard_layer`): the full router and shared-expert gate, the rank's experts,
-    its slice of the shared expert. Returns the whole block's output on every rank."""
+    its slice of the shared expert. Returns the whole block's output on every rank.
 
-    def __init__(self, layer: SparseMoeBlock, rank: int, world: int, experts: int, group=None):
+    With a `PeerExchange`, a decode step of float16 tokens is five launches overlapped by programmatic
+    dependent launch: `smoe_route` (router, top-k, softmax, shared gate), `smoe_localize`, the routed and shared
+    gate / up products in one launch, both down products in one launch, and `smoe_ep_reduce_combine` (the
+    exchange of the partial sums over peer memory with the combine). Without one (or for other activations),
+    the partial sums go through one all-reduce of the process group."""
+
+    def __init__(self, layer: SparseMoeBlock, rank: int, world: int, experts: int, group=None,
+                 exchange: "PeerExchange | None" = None):
         self.layer, self.rank, self.world, self.group = layer, rank, world, group
         self.lo, self.count = expert_range(rank, world, experts)
         self.experts = experts
+        self.exchange = exchange
 
     def local_indices(self, idx: torch.Tensor) -> torch.Tensor:
         """This rank's view of the chosen experts: idx - lo for its own, `count` (left out) for the others."""
@@ -102,10 +190,37 @@ class ExpertParallelMoE:
         _lib.call("smoe_localize", _lib.ptr(flat), flat.numel(), self.lo, self.count, _lib.ptr(out), _lib.stream())
         return out.reshape(idx.shape)
 
+    def _exchange_step(self, x2: torch.Tensor):
+        """The block through the peer exchange, or None where it does not apply."""
+        ex, layer = self.exchange, self.layer
+        tokens, hidden = x2.shape
+        if (ex is None or tokens == 0 or tokens > ex.max_tokens or hidden != ex.hidden
+                or x2.dtype not in (torch.float16, torch.float32)):
+            return None
+        k = layer.top_k
+        r = route(layer.gate, layer.shared_expert_gate, x2, k)
+        if r is None:
+            return None
+        idx, w, g = r
+        lidx = self.local_indices(idx)
+        sw, sh = layer.switch_mlp, layer.shared_expert
+        ys = None
+        if isinstance(sw, BlockSwitchGLU) and isinstance(sh, BlockMLP):
+            ys = decode_products(sw, sh, x2, lidx, batched_down=True)
+        if ys is None or ys[0] is None:
+            ys = (sw(x2, lidx), sh(x2))
+        y, s = ys
+        out = torch.empty((tokens, hidden), dtype=x2.dtype, device=x2.device)
+        return ex.reduce_combine(y.reshape(tokens, k, hidden), w, lidx, self.count, s.reshape(tokens, hidden),
+                                 g.reshape(tokens), out)
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         layer = self.layer
         lead, hidden = x.shape[:-1], x.shape[-1]
         x2 = x.reshape(-1, hidden).contiguous()
+        out = self._exchange_step(x2)
+        if out is not None:
+            return out.reshape(*lead, hidden)
         tokens, k = x2.shape[0], layer.top_k
         logits = layer.gate(x2)
         idx, w = top_k_softmax(logits, k)
@@ -220,5 +335,5 @@ class ExpertParallelPrompt:
         return combine_rows(back, where, w, g, s).reshape(*lead, hidden)
 
 
-__all__ = ["ExpertParallelMoE", "ExpertParallelPrompt", "combine_rows", "dispatch", "exchange_counts",
+__all__ = ["ExpertParallelMoE", "ExpertParallelPrompt", "PeerExchange", "combine_rows", "dispatch", "exchange_counts",
            "exchange_rows", "expert_range", "shard_stack", "shard_layer", "slice_cols", "slice_rows", "WindowLinear"]

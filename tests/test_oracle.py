@@ -107,3 +107,55 @@ def test_oracle_swiglu_rounds_in_the_activation_type():
     assert got.dtype == np.float16
     want = g.astype(np.float64) / (1 + np.exp(-g.astype(np.float64))) * u
     assert np.abs(got - want).max() <= 2e-3 * np.abs(want).max()
+
+
+# ---------------------------------------------------------------- the dense steps (oracle/dense.py)
+
+DENSE = os.path.join(os.path.dirname(__file__), "golden", "dense.npz")
+
+
+def test_oracle_q6k_parts_are_the_references():
+    """Against the reference's own q6k_parts (strata_mlx/gguf.py:150-165), run to make tests/golden/dense.npz."""
+    from oracle import dense as D
+
+    g = np.load(DENSE)
+    rows, cols = g["shape"]
+    codes, scales, d = D.q6k_parts(g["Q6_K/blocks"], rows, cols)
+    np.testing.assert_array_equal(codes, g["Q6_K/codes"])
+    np.testing.assert_array_equal(scales, g["Q6_K/scales"])
+    np.testing.assert_array_equal(d.view(np.uint16), g["Q6_K/d"])
+    # and their weights are the block decoder's, bit for bit
+    w = D.scaled_floats(codes, scales, d)
+    np.testing.assert_array_equal(w.view(np.uint32), Q.dequantize(g["Q6_K/blocks"], "Q6_K", (rows, cols)).view(np.uint32))
+
+
+def test_oracle_q3k_planes_are_the_references():
+    """Against the reference's own q3k_planes (strata_mlx/blocks.py:403-414), run to make tests/golden/dense.npz."""
+    from oracle import dense as D
+
+    g = np.load(DENSE)
+    rows, cols = g["shape"]
+    p = D.q3k_planes(g["Q3_K/blocks"], rows, cols)
+    for name in ("hm", "qs", "sc"):
+        np.testing.assert_array_equal(p[name], g[f"Q3_K/{name}"])
+    np.testing.assert_array_equal(p["dd"].view(np.uint16), g["Q3_K/dd"])
+    w = D.q3k_planes_weights(p, rows, cols)
+    np.testing.assert_array_equal(w.view(np.uint32), Q.dequantize(g["Q3_K/blocks"], "Q3_K", (rows, cols)).view(np.uint32))
+
+
+def test_oracle_hyper_connection_reads_before_plainly_when_nothing_was_written():
+    """strata_mlx's tests/test_fused.py:40-48 in the oracle: out = 0 and inject_in = 0 leave the residual `before`,
+    and the read is the hyper-connection of `before` alone."""
+    from oracle import dense as D
+
+    rng = np.random.default_rng(6)
+    hc, d, rank, T = 4, 96, 24, 2
+    before = rng.standard_normal((T, hc * d)).astype(np.float32)
+    norm = (1 + 0.2 * rng.standard_normal(hc * d)).astype(np.float32)
+    down = (0.1 * rng.standard_normal((rank, hc * d))).astype(np.float32)
+    up = (0.1 * rng.standard_normal((hc * d, rank))).astype(np.float32)
+    inj = (0.1 * rng.standard_normal((hc, hc * d))).astype(np.float32)
+    mixed, residual, inject = D.hyper_connection(before, np.zeros((T, d)), np.zeros((T, hc)), norm, down, up, inj, hc,
+                                                 dtype=np.float32)
+    np.testing.assert_array_equal(residual, before)
+    assert mixed.shape == (T, d) and inject.shape == (T, hc) and np.all((inject > 0) & (inject < 2))

@@ -32,40 +32,64 @@ def layer(seed):
     return routed, shared, router, sgate, x
 
 
-def run_rank(rank, world, device, seed):
+def run_rank(rank, world, device, seed, exchange=False, graph=False):
+    """rel-L2 of the expert-parallel block on this rank against the oracle's whole block (and, with the peer
+    exchange, the bits of every rank's output: a checksum the caller compares across ranks)."""
+    from strata_mlx_b200 import fused as F
     from strata_mlx_b200 import parallel as P
 
     routed, shared, router, sgate, x = layer(seed)
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(device)  # noqa: E731
     part = P.shard_layer(dev(router), *((dev(b), k, s) for b, k, s in routed),
                          [(dev(b), k, s) for b, k, s in shared], dev(sgate), K, rank, world)
-    block = P.ExpertParallelMoE(part, rank, world, E)
-    got = block(dev(x)).cpu().numpy()
+    ex = P.PeerExchange(rank, world, H, max_tokens=8, device=device) if exchange else None
+    block = P.ExpertParallelMoE(part, rank, world, E, exchange=ex)
+    if graph:
+        gb = F.GraphedBlock(block, x.shape[0], H, torch.float16, device)
+        for _ in range(3):
+            out = gb(dev(x))
+        got = out.cpu().numpy()
+        del gb
+    else:
+        got = block(dev(x)).cpu().numpy()
+    failed = ex.failed() if ex is not None else False
     logits = part.gate(dev(x)).cpu().numpy()
     want, *_ = M.moe_block(x, router, K, routed, shared, sgate, logits=logits)
-    return np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want.astype(np.float64))
+    err = float(np.linalg.norm(got.astype(np.float64) - want) / np.linalg.norm(want.astype(np.float64)))
+    if ex is not None:
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        ex.close()
+    return err, int(got.view(np.uint16).astype(np.int64).sum()), failed
 
 
 def test_one_rank_expert_parallel_block_is_the_oracles(cuda):
-    assert run_rank(0, 1, cuda, 4) <= 1e-3
+    assert run_rank(0, 1, cuda, 4)[0] <= 1e-3
 
 
-def _nccl_rank(rank, world, port, q):
+@pytest.mark.parametrize("graph", [False, True])
+def test_one_rank_peer_exchange_block_is_the_oracles(cuda, graph):
+    err, _, failed = run_rank(0, 1, cuda, 4, exchange=True, graph=graph)
+    assert err <= 1e-3 and not failed
+
+
+def _nccl_rank(rank, world, port, q, exchange=False, graph=False):
     import torch.distributed as dist
 
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                             device_id=torch.device("cuda", rank), timeout=datetime.timedelta(seconds=60))
     try:
-        q.put((rank, float(run_rank(rank, world, torch.device("cuda", rank), 5))))
+        q.put((rank,) + run_rank(rank, world, torch.device("cuda", rank), 5, exchange, graph))
         dist.barrier()
     finally:
         dist.destroy_process_group()
 
 
-def test_two_ranks_over_nccl_give_the_single_block(cuda):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+def _spawn(target, world, *args):
     import torch.multiprocessing as mp
 
     with socket.socket() as sk:
@@ -73,14 +97,31 @@ def test_two_ranks_over_nccl_give_the_single_block(cuda):
         port = sk.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.SimpleQueue()
-    procs = [ctx.Process(target=_nccl_rank, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=target, args=(r, world, port, q) + args) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
         p.join(timeout=300)
         assert p.exitcode == 0
-    errs = sorted(q.get() for _ in range(2))
-    assert all(e <= 1e-3 for _, e in errs), errs
+    return sorted(q.get() for _ in range(world))
+
+
+def test_two_ranks_over_nccl_give_the_single_block(cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    got = _spawn(_nccl_rank, 2)
+    assert all(e <= 1e-3 for _, e, _, _ in got), got
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_two_ranks_over_the_peer_exchange_give_the_single_block(cuda, graph):
+    """The decode step with its one exchange over NVLink peer memory: within rel-L2 1e-3 of the oracle on both
+    ranks, the same bits on both (the partials are added in rank order everywhere), no wait gave up."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    got = _spawn(_nccl_rank, 2, True, graph)
+    assert all(e <= 1e-3 and not failed for _, e, _, failed in got), got
+    assert got[0][2] == got[1][2], got
 
 
 # ---------------------------------------------------------------- a prompt chunk, tokens split over the ranks

@@ -68,3 +68,21 @@ def test_no_alloc_tiles_reject_what_does_not_fit_their_array(cuda):
             torch.empty(pairs, dtype=torch.int32, device="cuda")]
     with pytest.raises(ValueError, match="fixed array"):
         _lib.call("smoe_tiles_of_noalloc", _lib.ptr(idx), pairs, k, experts, *(_lib.ptr(o) for o in outs), _lib.stream())
+
+
+def test_no_alloc_tiles_at_the_array_limit_and_one_pair_past_it(cuda):
+    # 131,072 pairs over 1,024 experts: the histograms and ranks fill the 1 MiB array exactly
+    rng = np.random.default_rng(11)
+    pairs, k, experts = 131072, 8, 1024
+    need = int(_lib.lib().smoe_tiles_of_workspace_size(pairs, experts))
+    assert need == (1 << 20) + 256
+    idx = torch.from_numpy(rng.integers(0, experts, size=pairs).astype(np.int32)).cuda()
+    got = without_allocation(idx, k, experts)
+    want = with_workspace(idx, k, experts)
+    torch.cuda.synchronize()
+    for g, w in zip(got, want):
+        assert torch.equal(g, w)
+    # one pair more (k = 1) needs a chunk's histogram more: refused on the host
+    more = torch.zeros(pairs + 1, dtype=torch.int32, device="cuda")
+    with pytest.raises(ValueError, match="fixed array"):
+        without_allocation(more, 1, experts)
