@@ -140,7 +140,7 @@ def cpu_baseline(steps, seed, warmup=1):
     out = {"value": steps / dt, "unit": "token-layers/s", "cores": cores, "kind": "port",
            "sample": f"{steps} decode steps of config 2 (8 IQ3_S experts decoded from blocks + Q8_0 shared expert, "
                      f"numpy oracle, {cores}-process pool), {dt:.1f} s"}
-    out["product_only"] = cpu_product_only(inputs, max(steps, 3))
+    out["product_only"] = cpu_product_only(inputs, 50)
     return out
 
 
@@ -301,9 +301,9 @@ def run_prefill(device, seed, steps=5, warmup=2, rank=0, world=1):
     shared = B.BlockMLP(B.BlockLinear(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
                         B.BlockLinear(random_blocks(SHARED_KIND, FS * H), SHARED_KIND, (FS, H)),
                         B.BlockLinear(random_blocks(SHARED_KIND, H * FS), SHARED_KIND, (H, FS)))
-    rank = torch.empty(E, device=device)
-    rank[torch.randperm(E, device=device, generator=g)] = torch.arange(1, E + 1, device=device, dtype=torch.float32)
-    logp = -1.1 * torch.log(rank)
+    zipf = torch.empty(E, device=device)  # each expert's place in the Zipf order
+    zipf[torch.randperm(E, device=device, generator=g)] = torch.arange(1, E + 1, device=device, dtype=torch.float32)
+    logp = -1.1 * torch.log(zipf)
     logp -= torch.logsumexp(logp, 0)
     u = torch.randn(H, device=device, generator=g)
     u /= u.norm()
@@ -351,6 +351,64 @@ def run_prefill(device, seed, steps=5, warmup=2, rank=0, world=1):
             "routed_gemm_ms": gemm_ms, "routed_gemm_tflops": flops / (gemm_ms * 1e-3) / 1e12,
             "routed_gflop": flops / 1e9, "experts_hit": int((counts > 0).sum().item()),
             "max_pairs_per_expert": int(counts.max().item())}
+
+
+def run_config1(device, seed, steps=200, cpu_steps=3):
+    """Configuration 1 of the benchmark: one expert's matrix-vector product, W [1536 x 4096] in IQ3_S blocks
+    (2,703,360 bytes), x float16 [4096] ~N(0,1). The GPU takes W from a stack of 256 such experts (692 MB, more
+    than L2), a different expert each step, through `BlockSwitchLinear` (the int8 tensor-core decode matvec);
+    the CPU decodes the same blocks with the oracle port and multiplies with numpy (all host threads), and the
+    product alone with the weights decoded beforehand."""
+    import numpy as np
+    import torch
+
+    from oracle import quants as Q
+    from strata_mlx_b200 import blocks as B
+
+    experts, rows, cols = 256, F_, H
+    rng = np.random.default_rng(seed)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    per, nbytes = B.BLOCK[KIND]
+    n = experts * rows * cols // per
+    b = torch.randint(0, 256, (n, nbytes), dtype=torch.uint8, device=device, generator=g)
+    b[:, 0:2] = (torch.randn(n, device=device, generator=g) * SIGMA).abs().half().view(torch.uint8).view(n, 2)
+    lin = B.BlockSwitchLinear(b.reshape(-1), KIND, (experts, rows, cols))
+    x = torch.randn(1, 1, cols, device=device, generator=g).half()
+    idxs = [torch.tensor([[e]], dtype=torch.int32, device=device) for e in range(experts)]
+    for i in range(5):
+        lin(x, idxs[i])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        lin(x, idxs[(37 * i) % experts])
+    e1.record()
+    torch.cuda.synchronize()
+    gpu_us = e0.elapsed_time(e1) / steps * 1e3
+    mbytes = rows * B.row_bytes(KIND, cols)
+    # the CPU: one expert's blocks decoded and multiplied, then the product alone
+    blocks = b[: rows * cols // per].cpu().numpy().reshape(-1)
+    xc = x.reshape(-1).float().cpu().numpy()
+    Q.dequantize(blocks, KIND, (rows, cols))
+    t0 = time.perf_counter()
+    for _ in range(cpu_steps):
+        w = Q.dequantize(blocks, KIND, (rows, cols))
+        w @ xc
+    cpu_s = (time.perf_counter() - t0) / cpu_steps
+    from threadpoolctl import threadpool_limits
+
+    with threadpool_limits(os.cpu_count() or 1):
+        w @ xc
+        t0 = time.perf_counter()
+        for _ in range(50):
+            w @ xc
+        prod_s = (time.perf_counter() - t0) / 50
+    return {"workload": "config 1: one expert's matvec, W [1536 x 4096] IQ3_S blocks, x float16 [4096]",
+            "gpu_us_per_matvec": gpu_us, "gpu_gbs": mbytes / (gpu_us * 1e-6) / 1e9,
+            "gpu_note": "one launch per matvec (its latency included), a different expert of a 692 MB stack each",
+            "cpu_ms_decode_and_product": cpu_s * 1e3, "cpu_ms_product_only": prod_s * 1e3,
+            "cpu_threads": os.cpu_count(), "bytes_per_matvec": mbytes}
 
 
 VERIFY_TYPES = ("Q8_0", "Q4_K", "Q5_K", "Q6_K", "Q2_K", "Q3_K", "IQ3_S", "IQ3_XXS", "IQ4_XS")
@@ -447,8 +505,8 @@ def run_stack(args, rank, world, local_rank, prompt=32768, chunk=2048, decode_st
     # are the same draws on every rank
     g = torch.Generator(device=device)
     g.manual_seed(args.seed + 4099 + 7919 * rank)
-    gs = torch.Generator(device=device)
-    gs.manual_seed(args.seed + 4099)
+    g_same = torch.Generator(device=device)
+    g_same.manual_seed(args.seed + 4099)
     e_loc = E // world
 
     def random_blocks(kind, n_weights, gen=g):
@@ -464,11 +522,11 @@ def run_stack(args, rank, world, local_rank, prompt=32768, chunk=2048, decode_st
         sw = B.BlockSwitchGLU(B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H)),
                               B.BlockSwitchLinear(random_blocks(KIND, e_loc * F_ * H), KIND, (e_loc, F_, H)),
                               B.BlockSwitchLinear(random_blocks(KIND, e_loc * H * F_), KIND, (e_loc, H, F_)))
-        shared = [(random_blocks(SHARED_KIND, FS * H, gs), SHARED_KIND, (FS, H)),
-                  (random_blocks(SHARED_KIND, FS * H, gs), SHARED_KIND, (FS, H)),
-                  (random_blocks(SHARED_KIND, H * FS, gs), SHARED_KIND, (H, FS))]
-        router = (torch.randn(E, H, device=device, generator=gs) * 0.02).half()
-        sgate = (torch.randn(1, H, device=device, generator=gs) * 0.02).half()
+        shared = [(random_blocks(SHARED_KIND, FS * H, g_same), SHARED_KIND, (FS, H)),
+                  (random_blocks(SHARED_KIND, FS * H, g_same), SHARED_KIND, (FS, H)),
+                  (random_blocks(SHARED_KIND, H * FS, g_same), SHARED_KIND, (H, FS))]
+        router = (torch.randn(E, H, device=device, generator=g_same) * 0.02).half()
+        sgate = (torch.randn(1, H, device=device, generator=g_same) * 0.02).half()
         whole = B.BlockMLP(*(B.BlockLinear(b, k, s) for b, k, s in shared))
         prompt_layer = Fz.SparseMoeBlock(router, sw, whole, sgate, K)
         if world == 1:
@@ -598,7 +656,7 @@ def _prefill_ep(block, x, steps, warmup, rank, world):
     sw = block.switch_mlp
     stacks = [(lin.blocks, lin.kind, lin.shape) for lin in (sw.gate_proj, sw.up_proj, sw.down_proj)]
     sh = block.shared_expert
-    shared = [(lin.blocks, lin.kind, lin.shape) for lin in (sh.gate_proj, sh.up_proj, sh.down_proj)]
+    shared = [(lin.blocks, lin.kind, (lin.output_dims, lin.input_dims)) for lin in (sh.gate_proj, sh.up_proj, sh.down_proj)]
     part = P.shard_layer(block.gate.weight, *stacks, shared, block.shared_expert_gate.weight, K, rank, world,
                          whole_shared=True)
     ep = P.ExpertParallelPrompt(part, rank, world, E)
@@ -977,6 +1035,10 @@ def main():
         if world == 1 and not args.no_verify:
             import torch
 
+            try:
+                line["config1"] = run_config1(torch.device("cuda", local_rank), args.seed + 149)
+            except Exception as exc:  # noqa: BLE001
+                line["config1"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
             try:
                 line["verify"] = run_verify(torch.device("cuda", local_rank), args.seed + 199)
             except Exception as exc:  # noqa: BLE001

@@ -16,7 +16,7 @@
  *     a declaration says float32.
  *   - `stream` is a cudaStream_t (0 = legacy default stream). Every call that takes a stream is asynchronous
  *     on it, allocates nothing, synchronises nothing and so can be captured in a CUDA graph. The calls without
- *     a stream (the *_status reads, smoe_matvec_set_wait_limit, the exchange buffers' alloc / open / close /
+ *     a stream (the *_status reads, smoe_matvec_wait_test, the exchange buffers' alloc / open / close /
  *     free) synchronise or allocate and belong outside capture.
  *   - Return value: 0 on success; > 0 an invalid argument (SMOE_E*), with a message from
  *     smoe_last_error(); < 0 the negated cudaError_t of a failed launch.
@@ -83,12 +83,12 @@ SMOE_API int smoe_matvec(int kind, const uint8_t* blocks, int64_t experts, int64
  * smoe_matvec_glu, smoe_matvec_batch and smoe_matvec_glu_combine) bound every wait for a weight copy (about a
  * second). A wait that gives up stops the warp's copies, records SMOE_ETIMEOUT in a status word on the device,
  * and leaves that launch's outputs not valid. smoe_matvec_status synchronizes the current device and reads the
- * word (0 or SMOE_ETIMEOUT); `clear` zeroes it. smoe_matvec_set_wait_limit sets the bound in polls on the
- * current device (each poll suspends the waiting thread up to 1 ms; 0: one check, no wait; < 0: the default),
- * for tests that make a wait run out; it synchronizes the device. No counterpart in the reference (its kernels
- * have no device-side waits). */
+ * word (0 or SMOE_ETIMEOUT); `clear` zeroes it. smoe_matvec_wait_test is for tests that make a wait run out:
+ * it sets, on the current device, the bound in polls (each suspends the waiting thread up to 1 ms; < 0 restores
+ * the default) and, with `withhold`, has every warp leave its first weight copy unissued, so that the wait for it
+ * runs out; it synchronizes the device. No counterpart in the reference (its kernels have no device-side waits). */
 SMOE_API int smoe_matvec_status(int* status, int clear);
-SMOE_API int smoe_matvec_set_wait_limit(int64_t polls);
+SMOE_API int smoe_matvec_wait_test(int64_t polls, int withhold);
 
 /* The gate and up products of the same pairs in one launch: two smoe_matvec calls sharing idx and x
  * (strata_mlx/blocks.py:971 `g, u = gate(x5, indices), up(x5, indices)`). The two stacks may differ in

@@ -63,7 +63,7 @@ SIGNATURES = {
     "smoe_matvec_glu": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _i, _p]),
     "smoe_matvec_batch": (_i, [_i, _c.POINTER(SmoeMatvec), _p]),
     "smoe_matvec_status": (_i, [_c.POINTER(_i), _i]),
-    "smoe_matvec_set_wait_limit": (_i, [_i64]),
+    "smoe_matvec_wait_test": (_i, [_i64, _i]),
     "smoe_matvec_glu_combine": (_i, [_i, _p, _i64, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64, _p, _i, _p]),
     "smoe_decode_layer_scratch": (_sz, [_i64, _i64, _i64, _i64]),
     "smoe_decode_layer": (_i, [_c.POINTER(SmoeDecodeLayer), _p, _p]),
@@ -109,7 +109,7 @@ _lib = None
 KERNELS_PER_CALL = {"smoe_tiles_of": 2, "smoe_tiles_of_noalloc": 2, "smoe_tile_matmul": 2, "smoe_ep_dispatch": 2,
                     "smoe_ep_exchange_alloc": 0, "smoe_ep_exchange_open": 0, "smoe_ep_exchange_close": 0,
                     "smoe_ep_exchange_free": 0, "smoe_ep_exchange_status": 0, "smoe_decode_layer_status": 0,
-                    "smoe_matvec_status": 0, "smoe_matvec_set_wait_limit": 0, "smoe_hyper_connection": 3}
+                    "smoe_matvec_status": 0, "smoe_matvec_wait_test": 0, "smoe_hyper_connection": 3}
 launches = 0
 
 

@@ -1,13 +1,14 @@
-"""Experts computed on the GGUF file's own blocks, on B200: the call surface of strata-mlx's `strata_mlx/blocks.py`.
+"""Mixture-of-experts products read straight from GGUF quant blocks on B200, behind the Python interface of
+strata-mlx's `strata_mlx/blocks.py`.
 
-The blocks stay on the GPU as the file's bytes (a torch uint8 CUDA tensor) and hand-written sm_100a kernels
-(libstrata_moe.so, declared in include/strata_moe.h) read them:
+Each stack of experts lives on the GPU as one uint8 tensor holding the file's bytes unchanged; hand-written
+sm_100a kernels (libstrata_moe.so, C ABI in include/strata_moe.h) decode the blocks as they multiply:
 
-    matvec      out[pair, row] = W[expert of pair, row, :] . x          decoding, a pair at a time
-    matvec_glu  the same with x = swiglu(gate, up) formed in shared memory   the down product of a few pairs
-    tiles       the pairs of a chunk of a prompt sorted by expert into tiles of 16 (`tiles_of`), a tensor-core
-                grouped GEMM (tcgen05, accumulators in TMEM) per run of one expert's tiles (`tile_matmul`)
-    dequant     every weight of the stack as float16 or float32
+    matvec      decode steps: each (token, expert) pair's rows dotted with its activation row
+    matvec_glu  the down product of a few pairs, SwiGLU of (gate, up) formed while the activations are split
+    tiles       a prompt chunk: pairs grouped by expert into 16-slot tiles (`tiles_of`), then one tensor-core
+                grouped GEMM (tcgen05, accumulators in TMEM) per run of an expert's tiles (`tile_matmul`)
+    dequant     a stack's weights expanded to float16 or float32
 
 Names, signatures, tensor layouts, thresholds and the "None = path not taken" convention follow the
 reference (strata_mlx/blocks.py), so an engine written against it can import this module instead. Tensors
@@ -20,8 +21,9 @@ import torch
 
 from . import _lib
 
-# type -> (weights per block, bytes per block): the reference's BLOCK (strata_mlx/blocks.py:36-38) and the
-# K-types and Q8_0 the B200 build also reads on the GPU (strata_mlx/gguf.py:25-33)
+# GGML type name -> (weights a block holds, its size in bytes): the format constants of the reference's BLOCK
+# (strata_mlx/blocks.py:36-38), extended by the K-types and Q8_0 this build also decodes on the GPU
+# (strata_mlx/gguf.py:25-33)
 BLOCK = {"IQ4_NL": (32, 18), "IQ4_XS": (256, 136), "IQ3_S": (256, 110), "IQ3_XXS": (256, 98),
          "IQ2_S": (256, 82), "IQ2_XS": (256, 74), "IQ2_XXS": (256, 66), "IQ1_M": (256, 56), "Q2_0": (64, 18),
          "Q3_K": (256, 110), "Q8_0": (32, 34), "Q2_K": (256, 84), "Q4_K": (256, 144), "Q5_K": (256, 176),
@@ -31,7 +33,7 @@ KIND_ID = {"Q8_0": 8, "Q2_K": 10, "Q3_K": 11, "Q4_K": 12, "Q5_K": 13, "Q6_K": 14
            "IQ3_XXS": 18, "IQ4_NL": 20, "IQ3_S": 21, "IQ2_S": 22, "IQ4_XS": 23, "IQ1_M": 29, "Q2_0": 42}
 
 # thresholds, module attributes as in the reference so that tests and engines can switch paths
-TILES_FROM = 1600  # (token, expert) pairs from which a prompt goes through tiles (strata_mlx/blocks.py:579)
+TILES_FROM = 1600  # a call with at least this many (token, expert) pairs takes the tile path (strata_mlx/blocks.py:579)
 TOKENS_TILE, ROWS_TILE, COLS_TILE = 16, 64, 64  # strata_mlx/blocks.py:580
 BLOCK_GLU = True  # pairs unsorted, swiglu formed by the down kernel (strata_mlx/blocks.py:934)
 MATVEC_GLU_UPTO = 30  # pairs up to which down forms swiglu itself (strata_mlx/blocks.py:936)
@@ -46,14 +48,14 @@ def _kind(kind: str) -> int:
 def row_bytes(kind: str, cols: int) -> int:
     per_block, block_bytes = BLOCK[kind]
     if cols % per_block:
-        raise ValueError(f"{kind}: rows of {cols} weights do not end on a block of {per_block}")
+        raise ValueError(f"{kind}: {cols} columns is not a whole number of {per_block}-weight blocks")
     return cols // per_block * block_bytes
 
 
 def window_matvec(blocks: torch.Tensor, kind: str, rows: int, cols: int, x: torch.Tensor,
                   per_row: int | None = None) -> torch.Tensor:
-    """out[t] = W . x[t] for one layer's blocks (rows, cols) and a window of tokens x (tokens, cols) ->
-    (tokens, rows) in x's type (strata_mlx/blocks.py:349-396): a verify pass's dense product. On the CUDA-core
+    """The dense product of a verify window: every token of x (tokens, cols) times one layer's block matrix
+    (rows, cols), giving (tokens, rows) in x's type (strata_mlx/blocks.py:349-396). On the CUDA-core
     kernels (the K-types, IQ3_XXS, IQ4_XS, the IQ2 / IQ1 types) a token gets the same bits as alone, whatever the
     window; on the int8 tensor-core kernel (IQ3_S, Q8_0) its integer sums are exact but the float32 partial sums
     of a row may be grouped over a different number of warps for another window, so a token's result can differ
@@ -65,14 +67,14 @@ def window_matvec(blocks: torch.Tensor, kind: str, rows: int, cols: int, x: torc
     return _matvec(stack, x2, _zeros_idx(x2.shape[0], x.device), 1, x.dtype)
 
 
-# ---- Q3_K held as planes: the blocks rearranged once into aligned arrays of their parts (the same weights), so a
-# thread reads words where the file's 110-byte blocks give it bytes; 114 bytes a block (strata_mlx/blocks.py:399-401)
+# ---- Q3_K as planes: each field of the 110-byte blocks gathered into its own word-aligned array once, the
+# weights unchanged, so the kernels load whole words; 114 bytes per block (strata_mlx/blocks.py:399-401)
 Q3K_PLANE_BYTES = 114
 
 
 def q3k_planes(blocks: torch.Tensor, rows: int, cols: int) -> dict:
-    """A Q3_K tensor's blocks (rows, cols as the file has them) -> its planes {hm, qs, sc, dd}: the high-bit masks
-    (8 words a block), the two-bit codes (16 words), the scales less 32 (16 int8) and d (float16), made on the GPU
+    """Split a Q3_K matrix (rows, cols) into its planes on the GPU: {hm: high-bit masks, 8 words per block;
+    qs: two-bit codes, 16 words; sc: the sixteen 6-bit scales minus 32, as int8; dd: the float16 d}
     (strata_mlx/blocks.py:403-414)."""
     _lib.require_cuda(blocks)
     if cols % 256 or blocks.numel() != rows * row_bytes("Q3_K", cols):
@@ -87,9 +89,9 @@ def q3k_planes(blocks: torch.Tensor, rows: int, cols: int) -> dict:
 
 
 def q3k_planes_window(planes: dict, rows: int, cols: int, x: torch.Tensor) -> torch.Tensor:
-    """out[t] = W . x[t] for a Q3_K tensor held as planes, x (tokens, cols) -> (tokens, rows) in x's type
-    (strata_mlx/blocks.py:482-499). A warp a row, its lanes over the row's half blocks whatever the window, so a
-    token gets the same bits alone as in a window."""
+    """Multiply a window of tokens x (tokens, cols) by a Q3_K matrix kept as planes; (tokens, rows) in x's type
+    (strata_mlx/blocks.py:482-499). The split of a row's sum across lanes depends on the matrix's shape only, so
+    each token's result has the same bits whether it comes alone or with others."""
     _lib.require_cuda(x, *planes.values())
     x2 = x.reshape(-1, cols).contiguous()
     out = torch.empty((x2.shape[0], rows), dtype=x.dtype, device=x.device)
@@ -101,7 +103,8 @@ def q3k_planes_window(planes: dict, rows: int, cols: int, x: torch.Tensor) -> to
 
 
 def q3k_planes_dequantize(planes: dict, rows: int, cols: int, dtype: torch.dtype = torch.float32) -> torch.Tensor:
-    """Every weight of a Q3_K tensor held as planes, (rows, cols): the block decoder's bits (blocks.py:502-512)."""
+    """Expand a Q3_K matrix kept as planes to floats (rows, cols), with the same bits the block decoder gives
+    (blocks.py:502-512)."""
     _lib.require_cuda(*planes.values())
     out = torch.empty((rows, cols), dtype=dtype, device=planes["dd"].device)
     _lib.call("smoe_q3k_planes_dequant", _lib.ptr(planes["hm"]), _lib.ptr(planes["qs"]), _lib.ptr(planes["sc"]),
@@ -110,8 +113,8 @@ def q3k_planes_dequantize(planes: dict, rows: int, cols: int, dtype: torch.dtype
 
 
 def dequantize(blocks: torch.Tensor, kind: str, shape: tuple, dtype: torch.dtype = torch.float32) -> torch.Tensor:
-    """The weights of `blocks` (uint8, a tensor of `shape` as the file holds it) as floats
-    (strata_mlx/blocks.py:515-522). float16 results are bit-equal to gguf-py's weights rounded once."""
+    """Expand a block tensor to floats: `blocks` are the file's uint8 bytes of a tensor whose logical shape is
+    `shape` (strata_mlx/blocks.py:515-522). A float16 result is gguf-py's float32 weight rounded once."""
     _lib.require_cuda(blocks)
     *lead, rows, cols = shape
     n = math.prod(lead) if lead else 1
@@ -149,11 +152,13 @@ def _flat_idx(indices: torch.Tensor) -> torch.Tensor:
 
 
 class BlockSwitchLinear:
-    """A stack of linear layers kept as the file's blocks; called like mlx-lm's `QuantizedSwitchLinear`
-    (strata_mlx/blocks.py:525-558)."""
+    """One projection of every expert (experts, out, in), stored as the stack's GGUF bytes on the device; its call
+    takes what mlx-lm's `QuantizedSwitchLinear` takes (strata_mlx/blocks.py:525-558)."""
 
-    # From this many pairs on the reference unpacks the stack to floats for MLX's gather_mm; here the same
-    # threshold sends them through the dequant kernel and a float product, for parity of behaviour.
+    # From this many pairs on one call, the products go by expert: grouped into tiles for the tensor-core GEMM
+    # where the type and shape allow it (the reference unpacks the stack to floats for MLX's gather_mm there,
+    # strata_mlx/blocks.py:528-531); otherwise the decode matvec, which takes any pair count. Neither expands a
+    # whole stack.
     unpack_from = 5000
 
     def __init__(self, blocks: torch.Tensor, kind: str, shape: tuple, per_row: int | None = None):
@@ -169,7 +174,9 @@ class BlockSwitchLinear:
         return (self.num_experts, self.output_dims, self.input_dims)
 
     def __call__(self, x: torch.Tensor, indices: torch.Tensor, sorted_indices: bool = False) -> torch.Tensor:
-        """x (..., 1, in), one row to each index or to each run of the last axis of `indices`."""
+        """Each (token, expert) pair of `indices` times its activation row. x is (..., 1, in): either one row per
+        entry of `indices`, or one row that all entries along the last axis of `indices` share (a token's k
+        experts). Returns (*indices.shape, 1, out)."""
         _lib.require_cuda(x, indices, self.blocks)
         batch = tuple(x.shape[:-2])
         ishape = tuple(indices.shape)
@@ -183,32 +190,36 @@ class BlockSwitchLinear:
         pairs = indices.numel()
         idx = _flat_idx(indices)
         if pairs >= self.unpack_from:
-            out = self._as_floats(x.reshape(-1, self.input_dims), idx, share)
+            out = self._many_pairs(x.reshape(-1, self.input_dims).contiguous(), idx, share)
         else:
             out = _matvec(self, x.reshape(-1, self.input_dims).contiguous(), idx, share, x.dtype)
         return out.reshape(*ishape, 1, self.output_dims)
 
-    def _as_floats(self, x2, idx, share):
-        w = dequantize(self.blocks, self.kind, self.shape, x2.dtype)
-        rows = x2[torch.arange(idx.numel(), device=x2.device) // share]
-        return torch.einsum("poi,pi->po", w[idx.to(torch.int64)].float(), rows.float()).to(x2.dtype)
+    def _many_pairs(self, x2, idx, share):
+        """(pairs, out) for a large call: rows x2[p // share] through expert idx[p], by tiles of one expert on the
+        tensor cores where `tileable`, else the decode matvec."""
+        if x2.dtype in (torch.float16, torch.float32) and tileable(self.kind, self.output_dims, self.input_dims):
+            tiles, token, where = tiles_of(idx.reshape(-1, share), self.num_experts)
+            a = x2.index_select(0, _as_int64(token))
+            out = tile_matmul(self.blocks, self.kind, self.shape, a, tiles)
+            return out.index_select(0, _as_int64(where)).to(x2.dtype)
+        return _matvec(self, x2, idx, share, x2.dtype)
 
 
-# ---- prompts: an expert's blocks a tile at a time, on the tensor cores
+# ---- prompt chunks: pairs sorted into per-expert tiles, multiplied on the tensor cores
 
 def tileable(kind: str, rows: int, cols: int) -> bool:
-    """Whether `tile_matmul` takes a stack of such layers (strata_mlx/blocks.py:629-631)."""
+    """True when the tile GEMM handles matrices of this type and shape (strata_mlx/blocks.py:629-631)."""
     return bool(_lib.lib().smoe_tileable(_kind(kind), rows, cols))
 
 
 def tile_matmul(blocks: torch.Tensor, kind: str, shape: tuple, a: torch.Tensor, tile_expert: torch.Tensor) -> torch.Tensor:
-    """out[p] = W[expert of p's tile] . a[p] for a stack `blocks` of `shape` (experts, rows, cols)
-    (strata_mlx/blocks.py:634-654).
+    """Grouped GEMM over tiles: row p of the (P, rows) float32 result is a[p] times the matrix of the expert its
+    tile belongs to, for a stack `blocks` of `shape` (experts, rows, cols) (strata_mlx/blocks.py:634-654).
 
-    a (P, cols) float16 or float32, P a multiple of TOKENS_TILE, every TOKENS_TILE rows for one expert;
-    tile_expert (P / TOKENS_TILE,) says which, or names no expert (the number of experts, or more) for a tile
-    to leave out: its rows of the result are then whatever was in memory. The weights are rounded to the type
-    of `a` before they multiply; sums are float32. Returns (P, rows) float32.
+    `a` is (P, cols), float16 or float32, cut into tiles of TOKENS_TILE rows; tile_expert[i] is the expert of
+    tile i. An entry of `experts` or more marks a padding tile: it is skipped and its result rows are left
+    unwritten. Weights are rounded to a's type before the tensor cores multiply; accumulation is float32.
     """
     _lib.require_cuda(blocks, a, tile_expert)
     experts, rows, cols = shape
@@ -227,11 +238,12 @@ def tile_matmul(blocks: torch.Tensor, kind: str, shape: tuple, a: torch.Tensor, 
 
 
 def tiles_of(indices: torch.Tensor, experts: int) -> tuple:
-    """The pairs of `indices` (..., k) laid out in tiles of TOKENS_TILE, each tile one expert's
+    """Group the (token, expert) pairs of `indices` (..., k) by expert into tiles of TOKENS_TILE slots
     (strata_mlx/blocks.py:657-681).
 
-    -> (the expert of each tile, or `experts` for a tile nothing fills; the token of each slot; the slot of
-    each pair), uint32, worked out on the GPU in a number of tiles that depends only on the number of pairs.
+    Returns three uint32 tensors: tile_expert (each tile's expert; `experts` for tiles left empty), token (the
+    token in each slot) and where (each pair's slot). Computed on the GPU; the tile count is a bound fixed by
+    the pair count alone, so no host synchronisation is needed to size the outputs.
     """
     _lib.require_cuda(indices)
     k = indices.shape[-1]
@@ -267,8 +279,8 @@ def _as_int64(t):
 
 
 def _tiled_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.Tensor:
-    """The three products of a prompt's pairs through `tile_matmul`, the pairs in tiles (`tiles_of`)
-    (strata_mlx/blocks.py:684-694)."""
+    """A prompt chunk's SwiGLU experts on the tile path: tiles_of, gather of the token rows, gate and up tile
+    GEMMs, SwiGLU, the down tile GEMM, and the results read back in pair order (strata_mlx/blocks.py:684-694)."""
     tiles, token, where = tiles_of(indices, gate.num_experts)
     a = x.reshape(-1, x.shape[-1]).index_select(0, _as_int64(token))
 
@@ -291,8 +303,9 @@ PREFETCH_DOWN = False  # decode_products: the down stacks' experts fetched into 
 
 
 def matvec_glu(lin, idx: torch.Tensor, gate: torch.Tensor, up: torch.Tensor):
-    """`lin(swiglu(gate, up), idx)` for a BlockSwitchLinear, one pair to each row of gate and up, (pairs, out)
-    (strata_mlx/blocks.py:939-955). None where the activations are of a type the kernel does not take.
+    """The down projection of SwiGLU(gate, up): row p of gate and up (pairs, in) goes through expert idx[p] of
+    `lin`, giving (pairs, out) (strata_mlx/blocks.py:939-955). Returns None for activation types the kernels
+    do not take.
 
     The SwiGLU is the same function (so the same bits) everywhere: the int8 tensor-core decode kernel forms
     it while it splits the activations (as the reference's _MATVEC_GLU forms it in the matvec,
@@ -334,8 +347,9 @@ def gate_up(gate, up, x2: torch.Tensor, idx_flat: torch.Tensor, share: int):
 
 
 def switch_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.Tensor:
-    """down(silu(gate(x)) * up(x)) through each token's experts: x (..., in), indices (..., experts per token)
-    -> (..., experts per token, out) (strata_mlx/blocks.py:958-986)."""
+    """Each token's chosen experts as SwiGLU feed-forwards, down(silu(gate x) * up x): x (..., in) and
+    indices (..., k) give (..., k, out). Picks the tile path, the fused decode matvecs or the plain products by
+    pair count, type and shape (strata_mlx/blocks.py:958-986)."""
     _lib.require_cuda(x, indices)
     lins = (up, gate, down)
     if (indices.numel() >= TILES_FROM and x.dtype in (torch.float16, torch.float32)
@@ -347,9 +361,9 @@ def switch_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.
     if idx.numel() != x2.shape[0] * k:
         raise ValueError("indices must hold k experts for every token of x")
     if idx.numel() >= min(lin.unpack_from for lin in lins):
-        g = gate._as_floats(x2, idx, k)
-        u = up._as_floats(x2, idx, k)
-        out = down._as_floats(swiglu(g, u), idx, 1)
+        g = gate._many_pairs(x2, idx, k)
+        u = up._many_pairs(x2, idx, k)
+        out = down._many_pairs(swiglu(g, u), idx, 1)
         return out.reshape(*indices.shape, down.output_dims)
     g, u = gate_up(gate, up, x2, idx, k)
     if BLOCK_GLU and idx.numel() <= MATVEC_GLU_UPTO:
@@ -434,7 +448,8 @@ def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, 
 
 
 class BlockSwitchGLU:
-    """A layer's routed experts, called like mlx-lm's `SwitchGLU` (strata_mlx/blocks.py:989-996)."""
+    """The routed experts of one layer (gate, up and down stacks); calls like mlx-lm's `SwitchGLU`
+    (strata_mlx/blocks.py:989-996)."""
 
     def __init__(self, gate: BlockSwitchLinear, up: BlockSwitchLinear, down: BlockSwitchLinear):
         self.gate_proj, self.up_proj, self.down_proj = gate, up, down

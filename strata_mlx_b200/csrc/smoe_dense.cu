@@ -208,14 +208,35 @@ __global__ void q3k_planes_kernel(const uint8_t* __restrict__ blocks, int64_t n,
     }
 }
 
-// weight i (0..31) of run rr of a half: two bits of the half's qs word, less 4 where the block's hmask bit is
-// clear (strata_mlx/blocks.py:420-424)
-__device__ __forceinline__ int q3k_value(uint32_t qw, uint32_t hw, int k, int j, int rr) {
-    return static_cast<int>((qw >> (8 * k + 2 * j)) & 3u) - (((hw >> (8 * k + rr)) & 1u) ? 0 : 4);
+// Four weights of one run from one word of each plane, packed a byte each: byte k of the qs word holds the run's two
+// bits at 2 (rr % 4), byte k of the hm word its high bit at rr; q + 4 h is then 0..7 and the weight (before its
+// scale) q + 4 h - 4, as the block decoder has it (a clear high bit subtracts 4).
+__device__ __forceinline__ uint32_t q3k_codes4(uint32_t qw, uint32_t hw, int rr) {
+    return ((qw >> (2 * (rr & 3))) & 0x03030303u) | (((hw >> rr) & 0x01010101u) << 2);
+}
+// byte k of packed codes as the float (code - 4), exactly: the byte placed in the mantissa of 2^23
+__device__ __forceinline__ float q3k_value(uint32_t codes, int k) {
+    return __uint_as_float(__byte_perm(codes, 0x4B000000u, 0x7550u + k)) - 8388612.0f;
 }
 
-// A warp a row; lane l takes the halves (128 weights) l, l + 32, ... of the row; every token of the window per
-// pass (kDnTok at a time), sums in float32, the lanes added by an xor tree (strata_mlx/blocks.py:426-459).
+template <typename T>
+__device__ __forceinline__ float4 load4(const T* p);
+template <>
+__device__ __forceinline__ float4 load4<__half>(const __half* p) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+template <>
+__device__ __forceinline__ float4 load4<float>(const float* p) {
+    return *reinterpret_cast<const float4*>(p);
+}
+
+// A warp a row; lane l takes the half blocks (128 weights) l, l + 32, ... of the row. Per half: its 8 hm and 8
+// qs words and its 8 scales; per run (a 2-bit field of every qs byte) the words give four weights each; every
+// token of the window (kDnTok a pass) takes the run's two sub-blocks' sums, scaled once each. Lanes add by an xor
+// tree. The split of the row depends on its length only (strata_mlx/blocks.py:426-459).
 template <typename T>
 __global__ void q3k_window_kernel(const uint32_t* __restrict__ hm, const uint32_t* __restrict__ qs,
                                   const int8_t* __restrict__ sc, const uint16_t* __restrict__ dd, int64_t rows, int cols,
@@ -224,50 +245,53 @@ __global__ void q3k_window_kernel(const uint32_t* __restrict__ hm, const uint32_
     const int64_t r = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     pdl_wait();
     if (r < rows) {
-        const int blocks = cols / 256;
+        const int halves = cols / 128;
         for (int t0 = 0; t0 < tokens; t0 += kDnTok) {
             const int nt = min(kDnTok, tokens - t0);
             float sum[kDnTok];
 #pragma unroll
             for (int tt = 0; tt < kDnTok; ++tt) sum[tt] = 0.0f;
-            for (int h = lane; h < 2 * blocks; h += 32) {
-                const int64_t blk = r * blocks + h / 2;
+            for (int h = lane; h < halves; h += 32) {
+                const int64_t blk = r * (cols / 256) + (h >> 1);
                 const int n = h & 1;
                 uint32_t hw[8], qw[8];
-#pragma unroll
-                for (int w = 0; w < 8; ++w) {
-                    hw[w] = __ldg(hm + blk * 8 + w);
-                    qw[w] = __ldg(qs + blk * 16 + 8 * n + w);
-                }
+                const uint4* hp = reinterpret_cast<const uint4*>(hm + blk * 8);
+                const uint4* qp = reinterpret_cast<const uint4*>(qs + blk * 16 + 8 * n);
+                const uint4 h0 = __ldg(hp), h1 = __ldg(hp + 1), q0 = __ldg(qp), q1 = __ldg(qp + 1);
+                hw[0] = h0.x, hw[1] = h0.y, hw[2] = h0.z, hw[3] = h0.w, hw[4] = h1.x, hw[5] = h1.y, hw[6] = h1.z, hw[7] = h1.w;
+                qw[0] = q0.x, qw[1] = q0.y, qw[2] = q0.z, qw[3] = q0.w, qw[4] = q1.x, qw[5] = q1.y, qw[6] = q1.z, qw[7] = q1.w;
+                const uint2 scw = __ldg(reinterpret_cast<const uint2*>(sc + blk * 16 + 8 * n));
                 const float d = __half2float(__ushort_as_half(__ldg(dd + blk)));
-                const int64_t base = (h / 2) * 256 + 128 * n;
+                const T* xh = x + int64_t(t0) * cols + int64_t(h) * 128;
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int rr = 4 * n + j;
-                    const float s0 = d * float(sc[blk * 16 + 2 * rr]), s1 = d * float(sc[blk * 16 + 2 * rr + 1]);
-                    float a0[kDnTok], a1[kDnTok];
+                    float lo[kDnTok], hi[kDnTok];  // the run's first and second 16 weights
 #pragma unroll
-                    for (int tt = 0; tt < kDnTok; ++tt) a0[tt] = a1[tt] = 0.0f;
+                    for (int tt = 0; tt < kDnTok; ++tt) lo[tt] = hi[tt] = 0.0f;
 #pragma unroll
-                    for (int w4 = 0; w4 < 8; ++w4) {
-                        float v[4];
-#pragma unroll
-                        for (int k = 0; k < 4; ++k) v[k] = float(q3k_value(qw[w4], hw[w4], k, j, rr));
-                        const int64_t xi = base + 32 * j + 4 * w4;
+                    for (int w = 0; w < 8; ++w) {
+                        const uint32_t c = q3k_codes4(qw[w], hw[w], rr);
+                        const float v0 = q3k_value(c, 0), v1 = q3k_value(c, 1), v2 = q3k_value(c, 2), v3 = q3k_value(c, 3);
 #pragma unroll
                         for (int tt = 0; tt < kDnTok; ++tt) {
                             if (tt < nt) {
-                                const T* xr = x + int64_t(t0 + tt) * cols + xi;
-                                float p = 0.0f;
-#pragma unroll
-                                for (int k = 0; k < 4; ++k) p = fmaf(v[k], to_f32(xr[k]), p);
-                                if (w4 < 4) a0[tt] += p;
-                                else a1[tt] += p;
+                                const float4 xv = load4(xh + int64_t(tt) * cols + 32 * j + 4 * w);
+                                float p = v0 * xv.x;
+                                p = fmaf(v1, xv.y, p);
+                                p = fmaf(v2, xv.z, p);
+                                p = fmaf(v3, xv.w, p);
+                                if (w < 4) lo[tt] += p;
+                                else hi[tt] += p;
                             }
                         }
                     }
+                    // scales 2 rr, 2 rr + 1 are bytes 2 j, 2 j + 1 of this half's eight
+                    const uint32_t pair = (j < 2 ? scw.x : scw.y) >> (16 * (j & 1));
+                    const float s0 = d * float(static_cast<int8_t>(pair & 0xffu));
+                    const float s1 = d * float(static_cast<int8_t>((pair >> 8) & 0xffu));
 #pragma unroll
-                    for (int tt = 0; tt < kDnTok; ++tt) sum[tt] = fmaf(s0, a0[tt], fmaf(s1, a1[tt], sum[tt]));
+                    for (int tt = 0; tt < kDnTok; ++tt) sum[tt] = fmaf(s1, hi[tt], fmaf(s0, lo[tt], sum[tt]));
                 }
             }
 #pragma unroll
@@ -280,24 +304,36 @@ __global__ void q3k_window_kernel(const uint32_t* __restrict__ hm, const uint32_
     pdl_release();
 }
 
-// A thread a run of 32: d scale value as the block decoder gives it, (d * scale) * value
-// (strata_mlx/blocks.py:462-479)
+template <typename T>
+__device__ __forceinline__ void store4(T* p, float a, float b, float c, float e);
+template <>
+__device__ __forceinline__ void store4<float>(float* p, float a, float b, float c, float e) {
+    *reinterpret_cast<float4*>(p) = make_float4(a, b, c, e);
+}
+template <>
+__device__ __forceinline__ void store4<__half>(__half* p, float a, float b, float c, float e) {
+    const __half2 lo = __floats2half2_rn(a, b), hi = __floats2half2_rn(c, e);
+    uint2 v;
+    v.x = *reinterpret_cast<const uint32_t*>(&lo);
+    v.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(p) = v;
+}
+
+// A thread four weights: their codes from one qs and one hm word, (d scale) (code - 4) as the block decoder forms
+// each weight, rounded once; a vector store (strata_mlx/blocks.py:462-479)
 template <typename T>
 __global__ void q3k_planes_dequant_kernel(const uint32_t* __restrict__ hm, const uint32_t* __restrict__ qs,
-                                          const int8_t* __restrict__ sc, const uint16_t* __restrict__ dd, int64_t runs,
+                                          const int8_t* __restrict__ sc, const uint16_t* __restrict__ dd, int64_t quads,
                                           T* __restrict__ out) {
-    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < runs; i += int64_t(gridDim.x) * blockDim.x) {
-        const int rr = static_cast<int>(i & 7);
-        const int64_t blk = i >> 3;
-        const int n = rr >> 2, j = rr & 3;
-        const float d = __half2float(__ushort_as_half(dd[blk]));
-        const float s0 = mul_rn(d, float(sc[blk * 16 + 2 * rr])), s1 = mul_rn(d, float(sc[blk * 16 + 2 * rr + 1]));
-        T* o = out + blk * 256 + 32 * rr;
-        for (int w4 = 0; w4 < 8; ++w4) {
-            const uint32_t qw = qs[blk * 16 + 8 * n + w4], hw = hm[blk * 8 + w4];
-            for (int k = 0; k < 4; ++k)
-                o[4 * w4 + k] = from_f32<T>(mul_rn(w4 < 4 ? s0 : s1, float(q3k_value(qw, hw, k, j, rr))));
-        }
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < quads; i += int64_t(gridDim.x) * blockDim.x) {
+        const int64_t blk = i >> 6;
+        const int at = 4 * static_cast<int>(i & 63);  // the first weight's place in the block
+        const int n = at >> 7, j = (at >> 5) & 3, w = (at & 31) >> 2;
+        const int rr = 4 * n + j;
+        const uint32_t c = q3k_codes4(qs[blk * 16 + 8 * n + w], hm[blk * 8 + w], rr);
+        const float s = mul_rn(__half2float(__ushort_as_half(dd[blk])), float(sc[blk * 16 + 2 * rr + (w >> 2)]));
+        store4<T>(out + blk * 256 + at, mul_rn(s, q3k_value(c, 0)), mul_rn(s, q3k_value(c, 1)), mul_rn(s, q3k_value(c, 2)),
+                  mul_rn(s, q3k_value(c, 3)));
     }
 }
 
@@ -465,6 +501,8 @@ extern "C" int smoe_q3k_planes_window(const uint32_t* hm, const uint32_t* qs, co
                  "q3k_planes_window: rows of whole blocks");
     if (tokens == 0) return SMOE_OK;
     SMOE_REQUIRE(hm && qs && sc && dd && x && out && tokens > 0, SMOE_EARG, "q3k_planes_window: bad arguments");
+    SMOE_REQUIRE(aligned16(x) && aligned16(hm) && aligned16(qs) && (reinterpret_cast<uintptr_t>(sc) & 7) == 0,
+                 SMOE_EARG, "q3k_planes_window: activations and planes must be 16-byte aligned (sc 8-byte)");
     const unsigned grid = static_cast<unsigned>((rows * 32 + 255) / 256);
     cudaStream_t st = as_stream(stream);
     cudaError_t e;
@@ -485,16 +523,17 @@ extern "C" int smoe_q3k_planes_window(const uint32_t* hm, const uint32_t* qs, co
 extern "C" int smoe_q3k_planes_dequant(const uint32_t* hm, const uint32_t* qs, const int8_t* sc, const uint16_t* dd,
                                        int64_t rows, int64_t cols, void* out, int dtype, void* stream) {
     SMOE_REQUIRE(rows >= 0 && cols > 0 && cols % 256 == 0, SMOE_ESHAPE, "q3k_planes_dequant: rows of whole blocks");
-    const int64_t runs = rows * cols / 32;
-    if (runs == 0) return SMOE_OK;
+    const int64_t quads = rows * cols / 4;
+    if (quads == 0) return SMOE_OK;
     SMOE_REQUIRE(hm && qs && sc && dd && out, SMOE_EARG, "q3k_planes_dequant: null pointer");
+    SMOE_REQUIRE(aligned16(out), SMOE_EARG, "q3k_planes_dequant: the output must be 16-byte aligned");
     cudaStream_t st = as_stream(stream);
     if (dtype == SMOE_F16)
-        q3k_planes_dequant_kernel<__half><<<grid_of(runs, 256), 256, 0, st>>>(hm, qs, sc, dd, runs,
-                                                                              static_cast<__half*>(out));
+        q3k_planes_dequant_kernel<__half><<<grid_of(quads, 256), 256, 0, st>>>(hm, qs, sc, dd, quads,
+                                                                               static_cast<__half*>(out));
     else if (dtype == SMOE_F32)
-        q3k_planes_dequant_kernel<float><<<grid_of(runs, 256), 256, 0, st>>>(hm, qs, sc, dd, runs,
-                                                                             static_cast<float*>(out));
+        q3k_planes_dequant_kernel<float><<<grid_of(quads, 256), 256, 0, st>>>(hm, qs, sc, dd, quads,
+                                                                              static_cast<float*>(out));
     else
         return fail(SMOE_EDTYPE, "q3k_planes_dequant: float16 or float32");
     return launch_status("q3k_planes_dequant");

@@ -37,6 +37,9 @@ namespace smoe {
 // bound in polls (each suspends up to 1 ms), settable for tests.
 static __device__ int g_mv8_status = 0;
 static __device__ uint32_t g_mv8_polls = kM8WaitLimit;
+// Test hook: when set, each warp withholds its first weight copy (neither issued nor arrived), so the wait for
+// it runs out after g_mv8_polls polls; the drain then skips that copy.
+static __device__ int g_mv8_withhold = 0;
 
 __device__ __forceinline__ void mv8_gave_up(int lane) {
     if (lane == 0) atomicExch(&g_mv8_status, SMOE_ETIMEOUT);
@@ -101,9 +104,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     float* xscale = reinterpret_cast<float*>(lut + (D::kLut ? 8192 : 0));        // [xrows][xblocks]
     int8_t* xhi = reinterpret_cast<int8_t*>(xscale + ((a.xrows * xblocks + 3) & ~3));  // [xrows][cols]
     int8_t* xlo = xhi + size_t(a.xrows) * a.cols;
+    float* xsum = reinterpret_cast<float*>(xlo + size_t(a.xrows) * a.cols);  // [xrows][cols / 16] (the K-types)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
+    const bool withhold = g_mv8_withhold != 0;
     if (smem_addr(sm) & 127u) return;  // a tiled copy's destination is 128-byte aligned (the launch gives that)
     const int team = a.team, teams = kM8Warps / team;
     const int tid_team = warp / team, kq = warp % team;
@@ -129,7 +134,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     for (int i = threadIdx.x; i < kM8SMaskRows / 32; i += kM8Threads) need[i] = 0u;
     // the codebook fills while the kernel before this one finishes; so do the first weight copies and the
     // activation split when their inputs are older than that kernel (a.early); the rest waits for it
-    if constexpr (D::kLut) m8_fill_grid(lut);
+    if constexpr (D::kLut) D::fill(lut);
     const bool early_idx = a.early & 1, early_x = (a.early >> 1) & 1;
 
     // lane l's job (the warp's l-th): problem, pair, tile (residue class and block); its expert and the first
@@ -183,7 +188,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     // issue the cursor's item (a pair naming no expert copies nothing and completes the slot's phase with a
     // plain arrive, so every item takes one phase) and move on
     auto issue = [&]() {
-        if (lane == 0) {
+        if (lane == 0 && !(withhold && issued == 0)) {
             if (i_valid) {
                 tc::mbar_arrive_expect_tx(&my_bars[i_slot], static_cast<uint32_t>(kSlot));
                 tc::tma_load_2d(smem_addr(my_ring + i_slot * kSlot), &maps.w[i_map], (i_pos & ~15) >> 2, i_y,
@@ -203,7 +208,8 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
             const int xr = blk / xblocks, b = blk % xblocks;
             if (masked && !((need[xr >> 5] >> (xr & 31)) & 1u)) continue;
             const int64_t at = int64_t(xr) * a.cols + int64_t(b) * kM8XBlock + 8 * lane;
-            m8_split(a.x, a.gate, a.up, at, xhi + at, xlo + at, xscale + blk, lane);
+            m8_split(a.x, a.gate, a.up, at, xhi + at, xlo + at, xscale + blk, lane,
+                     D::kXsum ? xsum + (int64_t(xr) * a.cols + int64_t(b) * kM8XBlock) / 16 : nullptr);
         }
     };
     if (early_idx) {
@@ -269,8 +275,17 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
                     continue;
                 }
             }
-            D::stage(st + gid * D::kRS, st + (gid + 8) * D::kRS, tig, gid, lut, xh + xc, xl + xc,
-                     xsc + xc / kM8XBlock, total);
+            if constexpr (D::kXsum)
+                D::stage(st + gid * D::kRS, st + (gid + 8) * D::kRS, tig, gid, xh + xc, xl + xc, xsc + xc / kM8XBlock,
+                         xsum + (int64_t(xr) * a.cols + xc) / 16, total);
+            else
+                D::stage(st + gid * D::kRS, st + (gid + 8) * D::kRS, tig, gid, lut, xh + xc, xl + xc,
+                         xsc + xc / kM8XBlock, total);
+        }
+        // the two sub-blocks' lanes of a run (the K-types with sub-blocks of 16) into one
+        if constexpr (D::kHalves) {
+            total[0] += __shfl_xor_sync(0xffffffffu, total[0], 1);
+            total[1] += __shfl_xor_sync(0xffffffffu, total[1], 1);
         }
         // the team's partial sums of this job's 16 rows (for each of its pairs: lane tig holds pair tig's),
         // added in warp order
@@ -305,7 +320,8 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     // wait gave up; then the items from the one it gave up on are waited for here with the full bound (no item
     // was issued after it)
     if (!ok && lane == 0)
-        for (int i = waited; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, kM8WaitLimit);
+        for (int i = withhold ? max(waited, 1) : waited; i < issued; ++i)
+            tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, kM8WaitLimit);
     __syncwarp();
 }
 
@@ -372,6 +388,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
+    const bool withhold = g_mv8_withhold != 0;
     if (smem_addr(sm) & 127u) return;  // a tiled copy's destination is 128-byte aligned (the launch gives that)
     const int team = L.team, teams = kM8Warps / team;
     const int tid_team = warp / team, kq = warp % team;
@@ -446,7 +463,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     // issue the cursor's item (a pair naming no expert copies nothing and completes the slot's phase with a
     // plain arrive, so every item takes one phase) and move on
     auto issue = [&]() {
-        if (lane == 0) {
+        if (lane == 0 && !(withhold && issued == 0)) {
             if (i_valid) {
                 tc::mbar_arrive_expect_tx(&my_bars[i_slot], static_cast<uint32_t>(i_bytes));
                 tc::tma_load_2d(smem_addr(my_ring + i_slot * slot_bytes), &maps.w[i_map], (i_pos & ~15) >> 2, i_y,
@@ -585,7 +602,8 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     // wait gave up; then the items from the one it gave up on are waited for here with the full bound (no item
     // was issued after it)
     if (!ok && lane == 0)
-        for (int i = waited; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, kM8WaitLimit);
+        for (int i = withhold ? max(waited, 1) : waited; i < issued; ++i)
+            tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, kM8WaitLimit);
     __syncwarp();
 }
 
@@ -629,7 +647,8 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         if (rows % q) return 1;
         const int64_t xrows = (pairs + share - 1) / share;
         const int xblocks = static_cast<int>(cols / kM8XBlock);
-        const size_t xbytes = size_t(((xrows * xblocks + 3) & ~int64_t(3)) * 4) + size_t(xrows * cols * 2);
+        const size_t xbytes = size_t(((xrows * xblocks + 3) & ~int64_t(3)) * 4) + size_t(xrows * cols * 2) +
+                              (D::kXsum ? size_t(xrows * (cols / 16) * 4) : 0);
         const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 64 * 4 + kM8WhereSBytes +
                              (D::kLut ? 8192 * 4 : 0) + xbytes;
         const size_t slot = size_t(kM8Warps) * 16 * D::kRS;
@@ -688,13 +707,18 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         // the team size with the least work on the busiest warp, in quarters of a stage: CTA b takes the jobs
         // [b J / G, (b + 1) J / G), its teams share them round-robin; a warp does its share of each job's
         // stages plus about 3/4 of a stage for the team's reduction when the team has more than one warp
+        // A one-expert stack (a dense layer: a verify window's product) takes the team its shape gives one token,
+        // whatever the window: a token's float32 sums are then grouped alike alone and in a window, so it gets
+        // the same bits (the integer sums are exact either way).
         const int64_t S = cols / D::kStageCols;
         const int64_t G = std::min<int64_t>(g_m8_sms, jobs);
+        const int64_t tjobs = experts == 1 ? int64_t(nprob) * a.tiles : jobs;
+        const int64_t tG = std::min<int64_t>(g_m8_sms, tjobs);
         int team = 1;
         int64_t best = -1;
         for (int t = 1; t <= kM8Warps; t *= 2) {
             const int64_t teams = kM8Warps / t;
-            const int64_t most = ((jobs + G - 1) / G + teams - 1) / teams;  // jobs of the busiest team
+            const int64_t most = ((tjobs + tG - 1) / tG + teams - 1) / teams;  // jobs of the busiest team
             if (most > 32) continue;  // (a warp's job table holds 32)
             const int64_t span = most * (4 * ((S + t - 1) / t) + (t > 1 ? 3 : 0));
             if (best < 0 || span < best) {
@@ -703,6 +727,7 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
             }
         }
         if (best < 0) return 1;
+        if (((jobs + G - 1) / G + kM8Warps / team - 1) / (kM8Warps / team) > 32) return 1;  // (split by mv8_try)
         a.team = team;
         const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
         const size_t smem = fixed + ns * slot;
@@ -718,6 +743,15 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
     };
     if (kind0 == M8IQ3S<2>::kKind) return cols % M8IQ3S<2>::kStageCols ? go(M8IQ3S<1>{}) : go(M8IQ3S<2>{});
     if (kind0 == M8Q8_0::kKind) return go(M8Q8_0{});
+    if (kind0 == M8IQ4XS<2>::kKind) return cols % M8IQ4XS<2>::kStageCols ? go(M8IQ4XS<1>{}) : go(M8IQ4XS<2>{});
+    if (kind0 == M8IQ3XXS<2>::kKind) return cols % M8IQ3XXS<2>::kStageCols ? go(M8IQ3XXS<1>{}) : go(M8IQ3XXS<2>{});
+    // the K-types (Q2_K and Q3_K in stages of two blocks: widths of an odd number of 256 columns stay on the
+    // CUDA cores for those two)
+    if (kind0 == M8Q2K::kKind) return cols % 512 ? 1 : go(M8Q2K{});
+    if (kind0 == M8Q3K::kKind) return cols % 512 ? 1 : go(M8Q3K{});
+    if (kind0 == M8Q45K<false>::kKind) return go(M8Q45K<false>{});
+    if (kind0 == M8Q45K<true>::kKind) return go(M8Q45K<true>{});
+    if (kind0 == M8Q6K::kKind) return go(M8Q6K{});
     return 1;
 }
 
@@ -938,10 +972,12 @@ extern "C" int smoe_matvec_status(int* status, int clear) {
     return SMOE_OK;
 }
 
-extern "C" int smoe_matvec_set_wait_limit(int64_t polls) {
+extern "C" int smoe_matvec_wait_test(int64_t polls, int withhold) {
     const uint32_t v = polls < 0 ? kM8WaitLimit : static_cast<uint32_t>(std::min<int64_t>(polls, kM8WaitLimit));
+    const int w = withhold ? 1 : 0;
     cudaError_t e = cudaDeviceSynchronize();
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_mv8_polls, &v, sizeof(v));
-    if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("matvec_set_wait_limit: ") + cudaGetErrorString(e));
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_mv8_withhold, &w, sizeof(w));
+    if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("matvec_wait_test: ") + cudaGetErrorString(e));
     return SMOE_OK;
 }

@@ -216,13 +216,14 @@ int ex_launch(int emulated, const SmoeEpReduce* r, void* stream) {
         return launch_status("ep_reduce");
     }
     // emulated ranks wait on one another inside one launch: all CTAs must be resident together
-    int dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    SMOE_REQUIRE(ctas * emulated <= sms, SMOE_ESHAPE, "ep_reduce (emulated): more CTAs than SMs");
-    void* args[] = {&L};
     const void* fn = r0.dtype == SMOE_F16 ? reinterpret_cast<const void*>(ex_reduce_kernel<__half>)
                                           : reinterpret_cast<const void*>(ex_reduce_kernel<float>);
+    int dev = 0, sms = 0, per_sm = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kExThreads, 0);
+    SMOE_REQUIRE(ctas * emulated <= sms * per_sm, SMOE_ESHAPE, "ep_reduce (emulated): more CTAs than fit at once");
+    void* args[] = {&L};
     // (launched without the programmatic attribute and never triggering one: the next launch waits for it in full)
     const cudaError_t e = cudaLaunchCooperativeKernel(fn, grid, dim3(kExThreads), args, 0, st);
     if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("ep_reduce: ") + cudaGetErrorString(e));

@@ -16,14 +16,14 @@ import torch
 from . import _lib
 from .blocks import BLOCK, dequantize, q3k_planes, q3k_planes_dequantize, q3k_planes_window, window_matvec
 
-MAX_TOKENS = 8  # more than a window: a chunk of a prompt, multiplied as floats (strata_mlx/dense.py:33)
+MAX_TOKENS = 8  # beyond this many tokens a call is a prompt chunk and multiplies the expanded floats (dense.py:33)
 AS_BLOCKS = ("Q3_K", "IQ4_XS")  # dense types kept as the file's blocks (strata_mlx/dense.py:190)
 PLANES = True  # Q3_K's blocks held as planes (strata_mlx/dense.py:191)
 
 
 def fits(rows: int, cols: int) -> bool:
-    """Whether ScaledLinear's window kernel takes a layer of this shape (rows of whole groups of 16; the
-    reference's rule, strata_mlx/dense.py:96-98, asks 4 rows a group of threads and 256 columns a pass)."""
+    """True for the shapes ScaledLinear accepts: the reference's rule (strata_mlx/dense.py:96-98), rows in fours
+    and columns in 256s; the kernel here needs only columns in groups of 16."""
     return rows % 4 == 0 and cols % 256 == 0
 
 
@@ -43,15 +43,16 @@ def q6k_parts(blocks: torch.Tensor, rows: int, cols: int):
 
 
 class ScaledLinear:
-    """A linear layer held as codes, scales and d; called like `nn.Linear` (strata_mlx/dense.py:109-167)."""
+    """A Q6_K matrix kept as three arrays, weight = code x scale x d (int8 code per weight, int8 scale per 16,
+    float16 d per d_step); used like `nn.Linear` (strata_mlx/dense.py:109-167)."""
 
     def __init__(self, codes: torch.Tensor, scales: torch.Tensor, d: torch.Tensor):
         _lib.require_cuda(codes, scales, d)
         self.codes, self.scales, self.d = codes.contiguous(), scales.contiguous(), d.contiguous()
         self.output_dims, self.input_dims = codes.shape
-        self.d_step = self.input_dims // d.shape[1]  # weights to a d: 256, or fewer where the inputs were reordered
+        self.d_step = self.input_dims // d.shape[1]  # weights sharing one d (256 unless the columns were permuted)
         self._floats = None
-        self.keep = True  # the floats made for a chunk of a prompt stay for the next ones
+        self.keep = True  # keep the expanded floats after a prompt chunk, for the chunks that follow
         if not fits(*codes.shape) or scales.shape != (self.output_dims, self.input_dims // 16):
             raise ValueError(f"a layer of {tuple(codes.shape)} does not fit the kernel")
 
@@ -91,11 +92,11 @@ class ScaledLinear:
 
 
 class BlockLinear:
-    """A dense linear layer held as the file's blocks; called like `nn.Linear` (strata_mlx/dense.py:226-260).
+    """A dense matrix kept as its GGUF blocks; used like `nn.Linear` (strata_mlx/dense.py:226-260).
 
-    `blocks` are the rows in the order of the layer's outputs. `inputs`, if given, is where in the file's row each
-    input is: the blocks cannot be reordered inside, so the activations are, before they multiply. Q3_K is held
-    as planes (PLANES)."""
+    Row r of `blocks` is output r. When the model's inputs come in another order than the file's columns,
+    `inputs[i]` names the file column of input i; a block cannot be permuted internally, so each call permutes
+    the activations into the file's order instead. With PLANES a Q3_K matrix is kept as planes."""
 
     def __init__(self, blocks: torch.Tensor, kind: str, shape: tuple, inputs=None):
         _lib.require_cuda(blocks)
@@ -124,19 +125,20 @@ class BlockLinear:
         if self.to_file is not None:
             x2 = x2.index_select(1, self.to_file)
         x2 = x2.contiguous()
-        if self.planes is not None:
-            out = (q3k_planes_window(self.planes, rows, cols, x2) if tokens <= MAX_TOKENS
-                   else x2 @ q3k_planes_dequantize(self.planes, rows, cols, x.dtype).T)
-        elif tokens <= MAX_TOKENS:
-            out = window_matvec(self.blocks, self.kind, rows, cols, x2)
-        else:
-            # a chunk of a prompt: the weights made floats for it and let go (dense.py:250-258)
-            out = x2 @ dequantize(self.blocks, self.kind, (rows, cols), x.dtype).T
+        window = tokens <= MAX_TOKENS
+        if window:  # decode or verify: the kernels read the blocks (or planes) directly
+            out = (q3k_planes_window(self.planes, rows, cols, x2) if self.planes is not None
+                   else window_matvec(self.blocks, self.kind, rows, cols, x2))
+        else:  # a prompt chunk: floats expanded for this call only, then a dense product
+            w = (q3k_planes_dequantize(self.planes, rows, cols, x.dtype) if self.planes is not None
+                 else dequantize(self.blocks, self.kind, (rows, cols), x.dtype))
+            out = x2 @ w.T
         return out.reshape(*lead, rows)
 
 
 class BlockEmbedding:
-    """An embedding held as the file's blocks; a token's row is decoded when the token comes (dense.py:263-276)."""
+    """A token embedding kept as its GGUF blocks; only the rows of the tokens asked for are decoded, at lookup
+    (strata_mlx/dense.py:263-276)."""
 
     def __init__(self, blocks: torch.Tensor, kind: str, shape: tuple, dtype: torch.dtype):
         _lib.require_cuda(blocks)

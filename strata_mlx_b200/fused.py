@@ -23,10 +23,11 @@ COMBINE_UPTO = 16  # strata_mlx/fused.py:464: tokens the reference's kernel take
 
 
 class WindowLinear:
-    """A float16 linear layer without bias whose products come back in float32 (strata_mlx/fused.py:357-390).
+    """The router's product: float16 weights (rows, cols) times float16 or float32 activations, accumulated and
+    returned in float32, no bias (strata_mlx/fused.py:357-390).
 
-    Wraps a weight tensor (rows, cols) or an object with a `.weight`; any window of tokens goes through the
-    kernel, and a token's sum is taken in the same order whatever the window."""
+    Takes a weight tensor or any object with a `.weight`. Every token count runs on the same kernel, and the
+    order of each token's sum is fixed by the weight's shape, so a token's logits do not depend on its window."""
 
     upto, groups = 8, 16
 
@@ -72,8 +73,8 @@ def _top_k(logits: torch.Tensor, k: int, with_weights: bool):
 
 
 def top_k(logits: torch.Tensor, k: int) -> torch.Tensor:
-    """The indices of the k largest logits (..., N) float32, as `mx.argpartition(-logits, k - 1)[..., :k]`:
-    largest first, ties to the lower index (strata_mlx/fused.py:424-436). uint32."""
+    """uint32 positions of the k biggest float32 logits in each row of (..., N), biggest first and equal values
+    in index order: what `mx.argpartition(-logits, k - 1)[..., :k]` picks (strata_mlx/fused.py:424-436)."""
     return _top_k(logits, k, False)[0]
 
 
@@ -196,8 +197,8 @@ def moe_combine(y: torch.Tensor, w: torch.Tensor, g: torch.Tensor, s: torch.Tens
 
 
 class SparseMoeBlock:
-    """The model's MoE block with the router's choice made by `top_k` and its end by `moe_combine`, computed
-    as `_Routed.__call__` computes it (strata_mlx/fused.py:484-497):
+    """One MoE layer of the model: router logits, `top_k` choice, softmax over the chosen, the routed experts, the
+    gated shared expert and `moe_combine`, in the order `_Routed.__call__` runs them (strata_mlx/fused.py:484-497):
 
         logits = gate(x) (float32); idx = top_k(logits, k); w = softmax(logits[idx]);
         y = switch_mlp(x, idx); g = shared_expert_gate(x); s = shared_expert(x); out = moe_combine(y, w, g, s)
@@ -239,8 +240,9 @@ _Routed = SparseMoeBlock
 
 
 class FusedResidual:
-    """A hyper-connection of the model (its `GatedResidual`) with the write of the block before it folded into its
-    read, on three sm_100a kernels (`smoe_hyper_connection`; strata_mlx/fused.py:280-323).
+    """The model's hyper-connection (`GatedResidual`) between two blocks: the previous block's output is added
+    into the residual streams and the next block's input is read from them, in three sm_100a launches
+    (`smoe_hyper_connection`; strata_mlx/fused.py:280-323).
 
     `gr` has the model's weights: `hc_norm.weight` (hc d), `input_mix_weight_down.weight` (rank, hc d),
     `input_mix_weight_up.weight` (hc d, rank), `block_inject_weight` (None, or with `.weight` (hc, hc d)) and `hc`,
@@ -257,9 +259,11 @@ class FusedResidual:
         _lib.require_cuda(self.norm, self.down, self.up, self.inject_w)
 
     def __call__(self, before: torch.Tensor, out: torch.Tensor, inject_in: torch.Tensor):
-        """before (1, T, hc d), out (1, T, d), inject_in (1, T, hc): the residual is before + out * inject_in.
+        """Inputs: the streams before the write, before (1, T, hc d); the previous block's output, out (1, T, d);
+        its per-stream weights, inject_in (1, T, hc). The new residual is before + out * inject_in.
 
-        Returns (the block's input (1, T, d), the residual (1, T, hc d), inject for the block's output (1, T, hc))."""
+        Outputs: the next block's input (1, T, d), the new residual (1, T, hc d), and the weights that block's
+        own output will be written back with (1, T, hc); inject_in itself where there is no inject weight."""
         _lib.require_cuda(before, out, inject_in)
         T, d, dtype = before.shape[1], out.shape[2], before.dtype
         if out.dtype != dtype or inject_in.dtype != dtype or self.down.dtype != dtype:
@@ -280,8 +284,8 @@ class FusedResidual:
 
 
 def install_routers(layers) -> None:
-    """Make the routers of `layers` WindowLinear products (strata_mlx/fused.py:500-507): every `layer.mlp`
-    with a float16 `.gate` weight gets a WindowLinear gate."""
+    """Swap each `layer.mlp.gate` of `layers` for a WindowLinear over its weight, so that router products run on
+    the float32-summing kernel (strata_mlx/fused.py:500-507)."""
     for layer in layers:
         mlp = getattr(layer, "mlp", None)
         if mlp is None:

@@ -1,23 +1,24 @@
-"""GGUF files to device memory, for the MoE path: the reader of the reference's `strata_mlx/gguf.py:63-132`
-(header, metadata, tensor directory, aligned data section; split files) and the part of its loader that builds
-a MoE layer (`strata_mlx/load.py:259-263, 411-421`), with the bytes going mmap -> pinned host -> HBM unchanged.
+"""GGUF files to device memory, for the MoE path: a reader of the container (header, metadata, tensor
+directory, aligned data section; split files) that serves what the reference's `strata_mlx/gguf.py:63-132`
+serves, and the part of its loader that builds a MoE layer (`strata_mlx/load.py:259-263, 411-421`), with the
+bytes going mmap -> pinned host -> HBM unchanged.
 
 Tensors keep the file's bytes: an expert stack `blk.i.ffn_{gate,up,down}_exps.weight` becomes a
 `BlockSwitchLinear` over one uint8 device tensor, the shared expert `blk.i.ffn_{gate,up,down}_shexp.weight` a
 `BlockMLP` of `BlockLinear`s, the router `blk.i.ffn_gate_inp.weight` and the shared expert's gate
-`blk.i.ffn_gate_inp_shexp.weight` float16 matrices. Shapes are in numpy order (the last axis is the one a row
-runs along), the reverse of the file's dimension list.
+`blk.i.ffn_gate_inp_shexp.weight` float16 matrices. Shapes are given in numpy order, slowest axis first: the
+file lists them fastest first, so they are reversed on reading.
 """
 
 import mmap
+import os
 import re
-import struct
 from dataclasses import dataclass
 
 import numpy as np
 
-# GGML type id -> (name, weights per block, bytes per block): the file format's table (the reference's
-# strata_mlx/gguf.py:25-33 plus Q2_K, which the B200 path also reads)
+# GGML type id -> (name, weights per block, bytes per block): the file format's table of tensor types (the
+# reference's strata_mlx/gguf.py:25-33 plus Q2_K, which the B200 path also reads)
 TYPES = {
     0: ("F32", 1, 4), 1: ("F16", 1, 2), 30: ("BF16", 1, 2),
     2: ("Q4_0", 32, 18), 6: ("Q5_0", 32, 22), 8: ("Q8_0", 32, 34),
@@ -26,8 +27,14 @@ TYPES = {
     20: ("IQ4_NL", 32, 18), 21: ("IQ3_S", 256, 110), 22: ("IQ2_S", 256, 82), 23: ("IQ4_XS", 256, 136),
     29: ("IQ1_M", 256, 56), 42: ("Q2_0", 64, 18),
 }
-# metadata value type -> struct format (8: string, 9: array are read apart)
-_SCALARS = {0: "B", 1: "b", 2: "H", 3: "h", 4: "I", 5: "i", 6: "f", 7: "?", 10: "Q", 11: "q", 12: "d"}
+
+MAGIC = b"GGUF"
+DEFAULT_ALIGNMENT = 32  # the data section's alignment when the file does not name one (`general.alignment`)
+# metadata value types of the format: the fixed-size ones as numpy dtypes; 8 is a string, 9 an array
+VALUE_DTYPES = {0: np.dtype("<u1"), 1: np.dtype("<i1"), 2: np.dtype("<u2"), 3: np.dtype("<i2"), 4: np.dtype("<u4"),
+                5: np.dtype("<i4"), 6: np.dtype("<f4"), 7: np.dtype("?"), 10: np.dtype("<u8"), 11: np.dtype("<i8"),
+                12: np.dtype("<f8")}
+STRING, ARRAY = 8, 9
 
 
 @dataclass
@@ -44,37 +51,70 @@ class Tensor:
         return self.type not in ("F32", "F16", "BF16")
 
 
-class _Cursor:
-    def __init__(self, buf):
-        self.buf, self.at = buf, 0
+class _Fields:
+    """Little-endian fields read off a byte buffer one after the other (numpy views, no copies of arrays)."""
 
-    def take(self, fmt: str):
-        fmt = "<" + fmt
-        vals = struct.unpack_from(fmt, self.buf, self.at)
-        self.at += struct.calcsize(fmt)
-        return vals
+    __slots__ = ("buf", "pos", "path")
 
-    def one(self, fmt: str):
-        return self.take(fmt)[0]
+    def __init__(self, buf, pos: int, path: str):
+        self.buf, self.pos, self.path = buf, pos, path
 
-    def string(self) -> str:
-        n = self.one("Q")
-        s = bytes(self.buf[self.at : self.at + n]).decode("utf-8", "replace")
-        self.at += n
-        return s
+    def numbers(self, dtype: np.dtype, count: int) -> np.ndarray:
+        end = self.pos + dtype.itemsize * count
+        if end > len(self.buf):
+            raise ValueError(f"{self.path}: the header runs past the end of the file")
+        out = np.frombuffer(self.buf, dtype=dtype, count=count, offset=self.pos)
+        self.pos = end
+        return out
+
+    def number(self, dtype: np.dtype):
+        return self.numbers(dtype, 1)[0].item()
+
+    def text(self) -> str:
+        n = self.number(VALUE_DTYPES[10])
+        raw = self.numbers(np.dtype("u1"), n)
+        return raw.tobytes().decode("utf-8", errors="replace")
 
     def value(self, vtype: int):
-        if vtype == 8:
-            return self.string()
-        if vtype == 9:
-            etype, n = self.take("IQ")
-            if etype in _SCALARS:  # one unpack for the whole array
-                vals = self.take(f"{n}{_SCALARS[etype]}")
-                return list(vals)
-            return [self.value(etype) for _ in range(n)]
-        if vtype not in _SCALARS:
-            raise ValueError(f"GGUF metadata value type {vtype} is not known")
-        return self.one(_SCALARS[vtype])
+        if vtype in VALUE_DTYPES:
+            return self.number(VALUE_DTYPES[vtype])
+        if vtype == STRING:
+            return self.text()
+        if vtype == ARRAY:
+            etype = self.number(VALUE_DTYPES[4])
+            count = self.number(VALUE_DTYPES[10])
+            if etype in VALUE_DTYPES:
+                return self.numbers(VALUE_DTYPES[etype], count).tolist()
+            return [self.value(etype) for _ in range(count)]
+        raise ValueError(f"{self.path}: metadata value of unknown type {vtype}")
+
+
+def read_header(buf, path: str = ""):
+    """(version, metadata dict, [(name, numpy-order shape, type id, offset in the data section)], where the data
+    section starts) of a GGUF file's bytes. The header is: magic, version u32, tensor count u64, metadata count
+    u64; the metadata (string key, u32 value type, value); per tensor its string name, u32 axis count, u64 axes
+    (fastest first), u32 type, u64 offset; then the data section, aligned."""
+    if len(buf) < 24 or bytes(buf[:4]) != MAGIC:
+        raise ValueError(f"{path}: no GGUF magic at the start; not a GGUF file")
+    f = _Fields(buf, 4, path)
+    version = f.number(VALUE_DTYPES[4])
+    if version < 2:
+        raise ValueError(f"{path}: GGUF version {version} predates the 64-bit header this reader takes")
+    n_tensors, n_meta = (int(v) for v in f.numbers(VALUE_DTYPES[10], 2))
+    meta = {}
+    for _ in range(n_meta):
+        key = f.text()
+        meta[key] = f.value(f.number(VALUE_DTYPES[4]))
+    entries = []
+    for _ in range(n_tensors):
+        name = f.text()
+        axes = f.numbers(VALUE_DTYPES[10], f.number(VALUE_DTYPES[4]))
+        type_id = f.number(VALUE_DTYPES[4])
+        offset = f.number(VALUE_DTYPES[10])
+        entries.append((name, tuple(int(a) for a in axes[::-1]), type_id, offset))
+    align = int(meta.get("general.alignment", DEFAULT_ALIGNMENT))
+    start = -(-f.pos // align) * align
+    return version, meta, entries, start
 
 
 class GGUF:
@@ -84,39 +124,15 @@ class GGUF:
         self.path = path
         self._file = open(path, "rb")
         self._map = mmap.mmap(self._file.fileno(), 0, access=mmap.ACCESS_READ)
-        c = _Cursor(self._map)
-        if bytes(self._map[:4]) != b"GGUF":
-            raise ValueError(f"{path} is not a GGUF file")
-        c.at = 4
-        self.version, n_tensors, n_kv = c.take("IQQ")
-        if self.version < 2:
-            raise ValueError(f"{path}: GGUF version {self.version} is not supported")
-        self.meta = {}
-        for _ in range(n_kv):
-            key = c.string()
-            self.meta[key] = c.value(c.one("I"))
-        directory = []
-        for _ in range(n_tensors):
-            name = c.string()
-            dims = c.take(f"{c.one('I')}Q")
-            type_id, offset = c.take("IQ")
-            directory.append((name, tuple(int(d) for d in reversed(dims)), type_id, offset))
-        align = int(self.meta.get("general.alignment", 32))
-        base = (c.at + align - 1) // align * align
-        raw = np.frombuffer(self._map, dtype=np.uint8)
-        self.tensors = {}
-        for name, shape, type_id, offset in directory:
-            if type_id not in TYPES:
-                raise ValueError(f"{name}: GGUF tensor type {type_id} is not supported")
-            kind, per, nbytes = TYPES[type_id]
-            count = int(np.prod(shape, dtype=np.int64))
-            if count % per:
-                raise ValueError(f"{name}: {count} weights do not fill {kind} blocks of {per}")
-            n = count // per * nbytes
-            at = base + offset
-            if at + n > raw.size:
-                raise ValueError(f"{name}: its bytes run past the end of {path}")
-            self.tensors[name] = Tensor(name, shape, kind, raw[at : at + n], path, at)
+        try:
+            self.version, self.meta, entries, start = read_header(self._map, path)
+            raw = np.frombuffer(self._map, dtype=np.uint8)
+            self.tensors = {}
+            for name, shape, type_id, offset in entries:
+                self.tensors[name] = _tensor(raw, path, name, shape, type_id, start + offset)
+        except Exception:
+            self.close()
+            raise
 
     def __getitem__(self, name: str) -> Tensor:
         return self.tensors[name]
@@ -133,15 +149,57 @@ class GGUF:
         self._file.close()
 
 
-_SPLIT = re.compile(r"-(\d{5})-of-(\d{5})\.gguf$")
+def _tensor(raw: np.ndarray, path: str, name: str, shape: tuple, type_id: int, at: int) -> Tensor:
+    if type_id not in TYPES:
+        raise ValueError(f"{path}: tensor {name} has GGML type {type_id}, which this reader does not know")
+    kind, per, nbytes = TYPES[type_id]
+    weights = int(np.prod(shape, dtype=np.int64))
+    blocks, rest = divmod(weights, per)
+    if rest:
+        raise ValueError(f"{path}: tensor {name} of {weights} weights is not whole {kind} blocks of {per}")
+    end = at + blocks * nbytes
+    if end > raw.size:
+        raise ValueError(f"{path}: tensor {name} ends {end - raw.size} bytes past the end of the file")
+    return Tensor(name, shape, kind, raw[at:end], path, at)
+
+
+def _numbered(path: str):
+    """(prefix, number, count) of a file named `<prefix>-<number>-of-<count>.gguf` (five digits each), else None."""
+    stem = os.path.basename(path)
+    if not stem.endswith(".gguf"):
+        return None
+    parts = stem[: -len(".gguf")].rsplit("-", 3)
+    if len(parts) != 4 or parts[2] != "of" or not (len(parts[1]) == len(parts[3]) == 5):
+        return None
+    if not (parts[1].isdigit() and parts[3].isdigit()):
+        return None
+    return os.path.join(os.path.dirname(path), parts[0]), int(parts[1]), int(parts[3])
 
 
 def shards(path: str) -> list:
-    """A model's files: the one named and, where its name says it is one of several (`-00001-of-00003.gguf`),
-    the others beside it (strata_mlx/gguf.py:135-140)."""
-    m = _SPLIT.search(path)
-    count = int(m.group(2)) if m else 1
-    return [GGUF(path)] + [GGUF(_SPLIT.sub(f"-{i:05d}-of-{m.group(2)}.gguf", path)) for i in range(2, count + 1)]
+    """Open every file of a model given its first file's path, in split order. The split is the file's
+    `split.count` (with `split.no` its own place, from 0) where it has them, else what its name says
+    (`<prefix>-00001-of-00003.gguf`); the other files are the same prefix with their numbers."""
+    first = GGUF(path)
+    count = first.meta.get("split.count")
+    named = _numbered(path)
+    if count is None:
+        count = named[2] if named else 1
+    count = int(count)
+    if count <= 1:
+        return [first]
+    if named is None:
+        first.close()
+        raise ValueError(f"{path}: a split of {count} files, but the name does not number it")
+    prefix, _, _ = named
+    files = [first]
+    for i in range(2, count + 1):
+        f = GGUF(f"{prefix}-{i:05d}-of-{count:05d}.gguf")
+        no = f.meta.get("split.no")
+        if no is not None and int(no) != i - 1:
+            raise ValueError(f"{f.path}: split.no is {no}, not {i - 1}")
+        files.append(f)
+    return files
 
 
 def find(files: list, name: str) -> Tensor:
@@ -208,7 +266,7 @@ def experts(t: Tensor, device):
     from .blocks import BLOCK, BlockSwitchLinear
 
     if t.type not in BLOCK:
-        raise ValueError(f"{t.name}: {t.type} experts are not supported")
+        raise ValueError(f"{t.name}: no block kernel reads {t.type} expert stacks")
     if len(t.shape) != 3:
         raise ValueError(f"{t.name}: an expert stack has three axes, not {len(t.shape)}")
     return BlockSwitchLinear(to_device(t.data, device), t.type, t.shape)
@@ -219,7 +277,7 @@ def linear(t: Tensor, device):
     from .blocks import BLOCK, BlockLinear
 
     if t.type not in BLOCK:
-        raise ValueError(f"{t.name}: {t.type} matrices are not read as blocks here")
+        raise ValueError(f"{t.name}: no block kernel reads {t.type} matrices")
     if len(t.shape) != 2:
         raise ValueError(f"{t.name}: a matrix has two axes, not {len(t.shape)}")
     return BlockLinear(to_device(t.data, device), t.type, t.shape)

@@ -103,6 +103,38 @@ def test_split_files_are_found_beside_the_first(tmp_path):
         G.find(files, "blk.9.ffn_up_exps.weight")
 
 
+def test_a_split_is_read_from_its_metadata(tmp_path):
+    """split.count / split.no (as llama.cpp's gguf-split writes them) say how many files there are; a file whose
+    split.no is not its place in the numbering is refused."""
+    rng = np.random.default_rng(4)
+    tensors = layer_tensors(rng, 0)
+    names = sorted(tensors)
+    thirds = [names[:3], names[3:6], names[6:]]
+    for i, part in enumerate(thirds):
+        write(tmp_path / f"q-{i + 1:05d}-of-00003.gguf", {n: tensors[n] for n in part},
+              {"split.no": i, "split.count": 3})
+    files = G.shards(str(tmp_path / "q-00001-of-00003.gguf"))
+    assert [f.meta["split.no"] for f in files] == [0, 1, 2]
+    for n in names:
+        np.testing.assert_array_equal(G.find(files, n).data, tensors[n][0].reshape(-1).view(np.uint8))
+    write(tmp_path / "r-00001-of-00002.gguf", {names[0]: tensors[names[0]]}, {"split.no": 0, "split.count": 2})
+    write(tmp_path / "r-00002-of-00002.gguf", {names[1]: tensors[names[1]]}, {"split.no": 0, "split.count": 2})
+    with pytest.raises(ValueError, match="split.no"):
+        G.shards(str(tmp_path / "r-00001-of-00002.gguf"))
+    # a lone file is its own split
+    write(tmp_path / "lone.gguf", {names[0]: tensors[names[0]]})
+    assert len(G.shards(str(tmp_path / "lone.gguf"))) == 1
+
+
+def test_a_truncated_header_is_refused(tmp_path):
+    rng = np.random.default_rng(8)
+    write(tmp_path / "t.gguf", layer_tensors(rng, 0))
+    data = (tmp_path / "t.gguf").read_bytes()
+    (tmp_path / "cut.gguf").write_bytes(data[:200])
+    with pytest.raises(ValueError):
+        G.GGUF(str(tmp_path / "cut.gguf"))
+
+
 def test_a_moe_layer_is_built_from_the_files_bytes(tmp_path):
     rng = np.random.default_rng(2)
     tensors = layer_tensors(rng, 3, kinds=("Q4_K", "IQ4_XS", "Q6_K"))

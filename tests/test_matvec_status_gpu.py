@@ -1,7 +1,7 @@
-"""The int8 tensor-core decode matvec's bounded waits: with the wait limit set to a single check, a weight copy
-that has not landed makes the wait give up; the launch then records SMOE_ETIMEOUT in the status word the host
-reads (smoe_matvec_status), stops copying, lets its copies in flight land, and the device stays usable. With the
-default limit the same call is exact again and leaves the status clear. No fault, no trap: the wait runs out."""
+"""The int8 tensor-core decode matvec's bounded waits: with every warp's first weight copy withheld (a copy that
+never comes) and a short bound, the wait for it runs out; the launch then records SMOE_ETIMEOUT in the status word
+the host reads (smoe_matvec_status), stops copying, lets its other copies in flight land, and the device stays
+usable. Back to the default, the same call is exact again and leaves the status clear. No fault, no trap."""
 
 import ctypes
 
@@ -36,12 +36,12 @@ def test_a_wait_that_runs_out_is_a_status_the_host_reads(cuda):
     torch.cuda.synchronize()
     assert _status(lib, False) == 0
     try:
-        assert lib.smoe_matvec_set_wait_limit(0) == 0
+        assert lib.smoe_matvec_wait_test(2, 1) == 0
         for _ in range(3):
             lin(x, idx)
         assert _status(lib, True) == _lib.ETIMEOUT
     finally:
-        assert lib.smoe_matvec_set_wait_limit(-1) == 0
+        assert lib.smoe_matvec_wait_test(-1, 0) == 0
     got = lin(x, idx)
     torch.cuda.synchronize()
     assert _status(lib, False) == 0
