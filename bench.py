@@ -9,8 +9,8 @@ sigmoid gate; SwiGLU; weighted combine. A step is one token through one such lay
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
 value    token-layers/s with the token already in HBM (device-timed with CUDA events, max over ranks)
-e2e      the same through the public API `SparseMoeBlock.__call__` with the token copied from pinned host
-         memory and the result copied back inside every step
+e2e      the same through the public API (`GraphedBlock.__call__` in its host_io mode) with every step copying
+         its token from pinned host memory and its result back to pinned host memory
 roofline the dominant kernel (the step's batched gate/up: 16 IQ3_S matrices of 1536 x 4096 and the shared
          expert's two Q8_0 4096 x 4096 in one launch) against the measured HBM copy bandwidth: algorithmic
          bytes per launch / its CUDA-event time
@@ -856,22 +856,22 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     gu = g0.elapsed_time(g1) / (n_rep * reps * args.layers)
 
-    # end to end through the public API (GraphedBlock.__call__): pinned host token in, result back out
+    # end to end through the public API (GraphedBlock.__call__ with host_io): each step copies its token from
+    # pinned host memory to the device and its result back to pinned host memory, both inside the step's graph
+    del graphs
+    host_graphs = [GraphedBlock(blocks[i], 1, H, torch.float16, device, host_io=True) for i in range(args.layers)]
     host_in = [x.cpu().pin_memory() for x in xs]
-    host_out = torch.empty(1, H, dtype=torch.float16).pin_memory()
     for i in range(args.warmup):
-        d = host_in[i % args.layers].to(device, non_blocking=True)
-        host_out.copy_(graphs[i % args.layers](d), non_blocking=True)
+        host_graphs[i % args.layers](host_in[i % args.layers])
     align()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(args.steps):
-        d = host_in[i % args.layers].to(device, non_blocking=True)
-        host_out.copy_(graphs[i % args.layers](d), non_blocking=True)
+        host_graphs[i % args.layers](host_in[i % args.layers])
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1)
-    del graphs, gu_graph
+    del host_graphs, gu_graph
     if exchange is not None and exchange.failed():
         raise RuntimeError("a wait of the peer exchange gave up during the end-to-end steps")
 

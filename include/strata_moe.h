@@ -165,6 +165,13 @@ SMOE_API size_t smoe_route_counters(int64_t tokens);
 SMOE_API int smoe_route(const uint16_t* weight, const uint16_t* gate_weight, const void* x, int x_dtype,
                         int64_t tokens, int64_t experts, int64_t hidden, int64_t k, float* logits, uint32_t* idx,
                         float* weights, void* gate_out, uint32_t* counters, void* stream);
+/* smoe_route that also writes the expert-parallel rank's view of the choice in the same launch: lidx[t, j] =
+ * idx[t, j] - lo for the rank's experts [lo, lo + count), else `count` (what smoe_localize writes). No counterpart
+ * in the reference (one device): it fuses smoe_localize into the start of `_Routed.__call__`. */
+SMOE_API int smoe_route_local(const uint16_t* weight, const uint16_t* gate_weight, const void* x, int x_dtype,
+                              int64_t tokens, int64_t experts, int64_t hidden, int64_t k, float* logits, uint32_t* idx,
+                              float* weights, void* gate_out, uint32_t* counters, int64_t lo, int64_t count,
+                              uint32_t* lidx, void* stream);
 
 /* The end of the MoE block: out[t, d] = half(sum_k y[t,k,d] w[t,k]) + half(half(sigmoid(g[t])) s[t,d]),
  * the sum in float32 in MLX's col_reduce_small order (partials j = k mod 8, then in order), every product

@@ -74,6 +74,7 @@ SIGNATURES = {
     "smoe_combine": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
     "smoe_route_counters": (_sz, [_i64]),
     "smoe_route": (_i, [_p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p]),
+    "smoe_route_local": (_i, [_p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _i64, _p, _p]),
     "smoe_localize": (_i, [_p, _i64, _i64, _i64, _p, _p]),
     "smoe_partial_sums": (_i, [_p, _p, _p, _i64, _p, _i64, _i64, _i64, _p, _i, _p]),
     "smoe_combine_sums": (_i, [_p, _p, _i64, _i64, _p, _i, _p]),

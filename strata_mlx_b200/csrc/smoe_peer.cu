@@ -2,19 +2,21 @@
 // the MoE block.
 //
 // Every rank holds an exchange buffer (cudaMalloc'd here, shared with the other ranks of the node through CUDA
-// IPC handles). A launch of ex_reduce_kernel on rank r:
-//   1. works out, for its CTA's slice of the block's outputs, rank r's float32 partials: the weighted sum of
-//      its own experts' outputs (MLX's combine order among them) and its slice of the shared expert;
-//   2. stores them into every rank's inbox (plain stores to peer memory, no copy engine, no library kernel),
-//      fences them at system scope and raises its flag, a launch sequence number, on every rank;
-//   3. waits (bounded) until every rank's flag for this CTA has reached the sequence number;
+// IPC handles). A launch of ex_reduce_kernel on rank r, each thread for its own output elements:
+//   1. works out rank r's float32 partials of the element: the weighted sum of its own experts' outputs (MLX's
+//      combine order among them) and its slice of the shared expert;
+//   2. stores them into every other rank's inbox as two 8-byte words (value, launch sequence number): each word
+//      is written by one single-copy-atomic 64-bit store, so a reader that sees the sequence number sees the
+//      value with it -- no fence, no flag, no barrier between the threads;
+//   3. reads every other rank's two words of the element until their sequence numbers are this launch's
+//      (bounded polls of local memory);
 //   4. adds the ranks' partials in rank order (so every rank forms the same bits) and applies the combine's
 //      rounding: out = half(routed) + half(half(sigmoid(g)) half(shared)).
-// The inbox is double-buffered by the sequence number's parity: a rank can only run one launch ahead of any
-// other (it waits for all flags of the launch before), so the buffer it writes is never the one a slower rank
-// still reads. Each CTA keeps its own sequence counter in its rank's buffer, so CUDA graph replays need no
-// host work. A wait that gives up records SMOE_ETIMEOUT in the buffer's status word (smoe_ep_exchange_status)
-// and leaves the outputs unwritten.
+// The inbox is double-buffered by the sequence number's parity: a rank writes launch v + 1's words into the half
+// another rank read in launch v - 1 only after receiving that rank's launch v words, which it writes after its
+// launch v - 1 has completed. Each CTA keeps its own sequence counter in its rank's buffer, so CUDA graph replays
+// need no host work. A wait that gives up records SMOE_ETIMEOUT in the buffer's status word
+// (smoe_ep_exchange_status) and leaves that element's output unwritten.
 //
 // No TMA and no multicast: peer memory is only ever touched by plain loads and stores.
 #include <algorithm>
@@ -32,10 +34,11 @@ constexpr int kExMaxEmulated = 8;
 constexpr uint32_t kExDefaultPolls = 1u << 26;
 constexpr uint64_t kExWaitNs = 1000000000ull;  // a wait gives up after one second at most
 
-// A rank's exchange buffer: status word, the CTAs' launch counters, the flags its peers raise, the inbox.
+// A rank's exchange buffer: status word, the CTAs' launch counters, the inbox: [2 halves][rank][element] of two
+// 8-byte words (routed value, sequence number) and (shared value, sequence number).
 constexpr size_t kExSeqOff = 256;
-constexpr size_t kExFlagOff = kExSeqOff + 4 * kExMaxCtas;
-constexpr size_t kExInboxOff = (kExFlagOff + 4 * size_t(kExMaxRanks) * kExMaxCtas + 255) & ~size_t(255);
+constexpr size_t kExInboxOff = (kExSeqOff + 4 * kExMaxCtas + 255) & ~size_t(255);
+constexpr size_t kExSlot = 16;  // bytes per element per rank
 
 struct ExRank {
     const void* y;          // (tokens, k, d): this rank's experts' outputs (rows of other ranks' pairs unread)
@@ -55,18 +58,36 @@ struct ExLaunch {
     int release;  // trigger the next launch at the end (programmatic dependent launch)
 };
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_word(uint2* p, float v, uint32_t seq) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(seq) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint2 ld_word(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
     return v;
 }
 __device__ __forceinline__ uint64_t now_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+// the value of a word once its sequence number is `seq` (false: the wait gave up)
+__device__ __forceinline__ bool wait_word(const uint2* p, uint32_t seq, uint32_t polls, float& v) {
+    uint2 w = ld_word(p);
+    if (w.y == seq) {
+        v = __uint_as_float(w.x);
+        return true;
+    }
+    const uint64_t t0 = now_ns();
+    for (uint32_t i = 0; i < polls; ++i) {
+        w = ld_word(p);
+        if (w.y == seq) {
+            v = __uint_as_float(w.x);
+            return true;
+        }
+        if ((i & 255u) == 255u && now_ns() - t0 > kExWaitNs) break;
+    }
+    return false;
 }
 
 template <typename T>
@@ -78,23 +99,25 @@ __global__ void __launch_bounds__(kExThreads) ex_reduce_kernel(const __grid_cons
     const int64_t e0 = int64_t(c) * per, e1 = min(n, e0 + per);
     uint8_t* mine = R.peers[R.rank];
     __shared__ uint32_t s_seq;
-    __shared__ int s_ok;
     pdl_wait();
     if (threadIdx.x == 0) {
         uint32_t* seqp = reinterpret_cast<uint32_t*>(mine + kExSeqOff) + c;
         s_seq = *seqp + 1u;
         *seqp = s_seq;
-        s_ok = 1;
     }
     __syncthreads();
     const uint32_t seq = s_seq;
-    const int64_t buf = seq & 1u;
+    const int64_t half = seq & 1u;
     const T* y = static_cast<const T*>(R.y);
     const T* s = static_cast<const T*>(R.s);
+    const T* g = static_cast<const T*>(R.g);
+    T* out = static_cast<T*>(R.out);
     const int k = L.k;
-    // 1-2. this rank's partials, into every rank's inbox
+    const int64_t row = 2 * L.capacity;  // words of one rank's part of a half
+    bool ok = true;
     for (int64_t e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
         const int64_t t = e / L.d, i = e - t * L.d;
+        // 1. this rank's partials
         float acc = 0.0f;
         for (int j = 0; j < 8 && j < k; ++j) {
             float part = 0.0f;
@@ -103,52 +126,35 @@ __global__ void __launch_bounds__(kExThreads) ex_reduce_kernel(const __grid_cons
                     part = __fadd_rn(__fmul_rn(to_f32(y[(t * k + kk) * L.d + i]), R.w[t * k + kk]), part);
             acc = j == 0 ? part : __fadd_rn(part, acc);
         }
-        const float2 v = make_float2(acc, s ? to_f32(s[e]) : 0.0f);
+        const float sh = s ? to_f32(s[e]) : 0.0f;
+        // 2. to every other rank
         for (int p = 0; p < L.ranks; ++p) {
-            float2* box = reinterpret_cast<float2*>(R.peers[p] + kExInboxOff) + (buf * L.ranks + R.rank) * L.capacity;
-            box[e] = v;
+            if (p == R.rank) continue;
+            uint2* box = reinterpret_cast<uint2*>(R.peers[p] + kExInboxOff) + (half * L.ranks + R.rank) * row + 2 * e;
+            st_word(box, acc, seq);
+            st_word(box + 1, sh, seq);
         }
-    }
-    __threadfence_system();
-    __syncthreads();
-    if (threadIdx.x < L.ranks)
-        st_release_sys(reinterpret_cast<uint32_t*>(R.peers[threadIdx.x] + kExFlagOff) + R.rank * kExMaxCtas + c, seq);
-    // 3. every rank's partials of this slice
-    if (threadIdx.x < L.ranks) {
-        const uint32_t* f = reinterpret_cast<const uint32_t*>(mine + kExFlagOff) + threadIdx.x * kExMaxCtas + c;
-        bool ok = false;
-        const uint64_t t0 = now_ns();
-        for (uint32_t i = 0; i < L.polls; ++i) {
-            if (static_cast<int32_t>(ld_acquire_sys(f) - seq) >= 0) {
-                ok = true;
-                break;
+        // 3-4. every rank's, in rank order
+        const uint2* inbox = reinterpret_cast<const uint2*>(mine + kExInboxOff) + half * L.ranks * row + 2 * e;
+        float routed = 0.0f, shared = 0.0f;
+        bool have = true;
+        for (int p = 0; p < L.ranks; ++p) {
+            float vr = acc, vs = sh;
+            if (p != R.rank) {
+                have = have && wait_word(inbox + p * row, seq, L.polls, vr);
+                have = have && wait_word(inbox + p * row + 1, seq, L.polls, vs);
             }
-            if ((i & 255u) == 255u && now_ns() - t0 > kExWaitNs) break;
+            routed = p == 0 ? vr : __fadd_rn(routed, vr);
+            shared = p == 0 ? vs : __fadd_rn(shared, vs);
         }
-        if (!ok) {
-            s_ok = 0;
-            atomicExch(reinterpret_cast<int*>(mine), SMOE_ETIMEOUT);
+        if (!have) {
+            ok = false;
+            continue;
         }
+        const T gate = from_f32<T>(1.0f / (1.0f + expf(-to_f32(g[t]))));
+        out[e] = add_t<T>(from_f32<T>(routed), mul_t<T>(gate, from_f32<T>(shared)));
     }
-    __syncthreads();
-    if (s_ok) {
-        // 4. the ranks' partials in rank order, then the combine's rounding
-        const float2* inbox = reinterpret_cast<const float2*>(mine + kExInboxOff) + buf * L.ranks * L.capacity;
-        const T* g = static_cast<const T*>(R.g);
-        T* out = static_cast<T*>(R.out);
-        for (int64_t e = e0 + threadIdx.x; e < e1; e += blockDim.x) {
-            const int64_t t = e / L.d;
-            float2 v = __ldcg(inbox + e);
-            float routed = v.x, shared = v.y;
-            for (int p = 1; p < L.ranks; ++p) {
-                v = __ldcg(inbox + int64_t(p) * L.capacity + e);
-                routed = __fadd_rn(routed, v.x);
-                shared = __fadd_rn(shared, v.y);
-            }
-            const T gate = from_f32<T>(1.0f / (1.0f + expf(-to_f32(g[t]))));
-            out[e] = add_t<T>(from_f32<T>(routed), mul_t<T>(gate, from_f32<T>(shared)));
-        }
-    }
+    if (!ok) atomicExch(reinterpret_cast<int*>(mine), SMOE_ETIMEOUT);
     if (L.release) pdl_release();
 }
 
@@ -202,8 +208,18 @@ int ex_launch(int emulated, const SmoeEpReduce* r, void* stream) {
     L.polls = r0.wait_polls ? r0.wait_polls : kExDefaultPolls;
     L.release = emulated == 1;
     const int64_t n = r0.tokens * r0.d;
-    // every rank must cut the outputs into the same slices: the CTA count depends on the shape alone
-    const int ctas = static_cast<int>(std::min<int64_t>(kExMaxCtas, (n + kExThreads - 1) / kExThreads));
+    // every rank must cut the outputs into the same slices: the CTA count depends on the shape alone (an
+    // emulated launch, all ranks' CTAs resident together, takes fewer where they would not fit)
+    int ctas = static_cast<int>(std::min<int64_t>(kExMaxCtas, (n + kExThreads - 1) / kExThreads));
+    const void* fn = r0.dtype == SMOE_F16 ? reinterpret_cast<const void*>(ex_reduce_kernel<__half>)
+                                          : reinterpret_cast<const void*>(ex_reduce_kernel<float>);
+    int dev = 0, sms = 0, per_sm = 0;
+    if (emulated > 1) {
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kExThreads, 0);
+        ctas = std::max(1, std::min(ctas, sms * per_sm / emulated));
+    }
     cudaStream_t st = as_stream(stream);
     Writes wr;
     wr.add(r0.out, size_t(n) * (r0.dtype == SMOE_F16 ? 2 : 4));
@@ -216,12 +232,6 @@ int ex_launch(int emulated, const SmoeEpReduce* r, void* stream) {
         return launch_status("ep_reduce");
     }
     // emulated ranks wait on one another inside one launch: all CTAs must be resident together
-    const void* fn = r0.dtype == SMOE_F16 ? reinterpret_cast<const void*>(ex_reduce_kernel<__half>)
-                                          : reinterpret_cast<const void*>(ex_reduce_kernel<float>);
-    int dev = 0, sms = 0, per_sm = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kExThreads, 0);
     SMOE_REQUIRE(ctas * emulated <= sms * per_sm, SMOE_ESHAPE, "ep_reduce (emulated): more CTAs than fit at once");
     void* args[] = {&L};
     // (launched without the programmatic attribute and never triggering one: the next launch waits for it in full)
@@ -237,7 +247,7 @@ using namespace smoe;
 
 extern "C" size_t smoe_ep_exchange_bytes(int64_t ranks, int64_t max_tokens, int64_t d) {
     if (ranks < 1 || ranks > kExMaxRanks || max_tokens < 1 || d < 1) return 0;
-    return kExInboxOff + size_t(2) * ranks * max_tokens * d * sizeof(float2);
+    return kExInboxOff + size_t(2) * ranks * max_tokens * d * kExSlot;
 }
 
 extern "C" int smoe_ep_exchange_alloc(size_t bytes, void** buffer, void* ipc_handle) {

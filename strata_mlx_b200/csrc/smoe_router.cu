@@ -63,7 +63,8 @@ __global__ void __launch_bounds__(256) route_kernel(const __half* __restrict__ w
                                                     const XT* __restrict__ x, int64_t tokens, int64_t experts,
                                                     int64_t hidden, int k, float* __restrict__ logits,
                                                     uint32_t* __restrict__ idx, float* __restrict__ weights,
-                                                    XT* __restrict__ gate_out, uint32_t* __restrict__ counters) {
+                                                    XT* __restrict__ gate_out, uint32_t* __restrict__ counters,
+                                                    uint32_t lo, uint32_t count, uint32_t* __restrict__ lidx) {
     __shared__ float part[2][4][kRtTokens];
     __shared__ bool last;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -109,6 +110,13 @@ __global__ void __launch_bounds__(256) route_kernel(const __half* __restrict__ w
         const float* in = logits + (t0 + warp) * experts;
         topk_row<NV>([&](int j) { return __ldcg(in + j); }, static_cast<int>(experts), k, idx + (t0 + warp) * k,
                      weights + (t0 + warp) * k);
+        if (lidx != nullptr) {  // this rank's view of the choice: expert - lo for its own, `count` for the others'
+            __syncwarp();
+            for (int j = lane; j < k; j += 32) {
+                const uint32_t e = idx[(t0 + warp) * k + j] - lo;
+                lidx[(t0 + warp) * k + j] = e < count ? e : count;
+            }
+        }
     }
     if (threadIdx.x == 0) counters[blockIdx.y] = 0u;
 }
@@ -268,9 +276,10 @@ extern "C" size_t smoe_route_counters(int64_t tokens) {
     return static_cast<size_t>(tokens > 0 ? (tokens + kRtTokens - 1) / kRtTokens : 1) * sizeof(uint32_t);
 }
 
-extern "C" int smoe_route(const uint16_t* weight, const uint16_t* gate_weight, const void* x, int x_dtype,
-                          int64_t tokens, int64_t experts, int64_t hidden, int64_t k, float* logits, uint32_t* idx,
-                          float* weights, void* gate_out, uint32_t* counters, void* stream) {
+static int route_launch(const uint16_t* weight, const uint16_t* gate_weight, const void* x, int x_dtype,
+                        int64_t tokens, int64_t experts, int64_t hidden, int64_t k, float* logits, uint32_t* idx,
+                        float* weights, void* gate_out, uint32_t* counters, int64_t lo, int64_t count, uint32_t* lidx,
+                        void* stream) {
     if (tokens == 0) return SMOE_OK;
     SMOE_REQUIRE(weight && x && logits && idx && weights && counters && tokens > 0 && experts > 0, SMOE_EARG,
                  "null pointer or empty router");
@@ -296,19 +305,38 @@ extern "C" int smoe_route(const uint16_t* weight, const uint16_t* gate_weight, c
         Writes wr;
         wr.add(logits, size_t(tokens) * experts * 4).add(idx, size_t(tokens) * k * 4).add(weights, size_t(tokens) * k * 4);
         wr.add(gate_out, size_t(tokens) * sizeof(XT)).add(counters, smoe_route_counters(tokens));
+        wr.add(lidx, size_t(tokens) * k * 4);
+        const uint32_t l0 = static_cast<uint32_t>(lo), cn = static_cast<uint32_t>(count);
         if (experts <= 256)
-            launch_pdl(wr, route_kernel<XT, 8>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(wr, route_kernel<XT, 8>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters, l0, cn, lidx);
         else if (experts <= 512)
-            launch_pdl(wr, route_kernel<XT, 16>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(wr, route_kernel<XT, 16>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters, l0, cn, lidx);
         else if (experts <= 1024)
-            launch_pdl(wr, route_kernel<XT, 32>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(wr, route_kernel<XT, 32>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters, l0, cn, lidx);
         else
-            launch_pdl(wr, route_kernel<XT, 64>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters);
+            launch_pdl(wr, route_kernel<XT, 64>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters, l0, cn, lidx);
     };
     if (x_dtype == SMOE_F16) go(__half{});
     else if (x_dtype == SMOE_F32) go(float{});
     else return fail(SMOE_EDTYPE, "router activations must be float16 or float32");
     return launch_status("route");
+}
+
+extern "C" int smoe_route(const uint16_t* weight, const uint16_t* gate_weight, const void* x, int x_dtype,
+                          int64_t tokens, int64_t experts, int64_t hidden, int64_t k, float* logits, uint32_t* idx,
+                          float* weights, void* gate_out, uint32_t* counters, void* stream) {
+    return route_launch(weight, gate_weight, x, x_dtype, tokens, experts, hidden, k, logits, idx, weights, gate_out,
+                        counters, 0, 0, nullptr, stream);
+}
+
+extern "C" int smoe_route_local(const uint16_t* weight, const uint16_t* gate_weight, const void* x, int x_dtype,
+                                int64_t tokens, int64_t experts, int64_t hidden, int64_t k, float* logits,
+                                uint32_t* idx, float* weights, void* gate_out, uint32_t* counters, int64_t lo,
+                                int64_t count, uint32_t* lidx, void* stream) {
+    SMOE_REQUIRE(lidx && lo >= 0 && count > 0 && lo + count <= experts, SMOE_EARG,
+                 "route_local: this rank's experts [lo, lo + count) must lie within the router's");
+    return route_launch(weight, gate_weight, x, x_dtype, tokens, experts, hidden, k, logits, idx, weights, gate_out,
+                        counters, lo, count, lidx, stream);
 }
 
 extern "C" int smoe_combine(const void* y, const float* w, const void* g, const void* s, int64_t tokens, int64_t k,

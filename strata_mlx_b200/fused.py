@@ -148,10 +148,12 @@ def decode_layer_failed(x: torch.Tensor, block: "SparseMoeBlock") -> bool:
     return flag.value != 0
 
 
-def route(gate: "WindowLinear", shared_gate, x: torch.Tensor, k: int):
+def route(gate: "WindowLinear", shared_gate, x: torch.Tensor, k: int, local=None):
     """The start of the MoE block in one launch: (idx, w, g) = (top_k_softmax(gate(x), k),
     shared_gate(x).to(x.dtype)) with the same sums and choice as those calls (strata_mlx/fused.py:487-491).
-    shared_gate: a WindowLinear of one row, or None (g is then None). None where the kernel does not take x."""
+    shared_gate: a WindowLinear of one row, or None (g is then None). With `local` = (lo, count), an expert-
+    parallel rank's experts, a fourth result lidx: idx - lo for those experts, `count` for the others, from the
+    same launch. None where the kernel does not take x."""
     if not gate.takes(x) or gate.rows > 2048 or not 1 <= k <= min(gate.rows, 32):
         return None
     if shared_gate is not None and (not shared_gate.takes(x) or shared_gate.rows != 1 or shared_gate.cols != gate.cols):
@@ -169,14 +171,19 @@ def route(gate: "WindowLinear", shared_gate, x: torch.Tensor, k: int):
     counters = _COUNTERS.get(key)
     if counters is None:
         counters = _COUNTERS[key] = torch.zeros(nbytes // 4, dtype=torch.int32, device=dev)
+    lidx = torch.empty((tokens, k), dtype=torch.uint32, device=dev) if local is not None else None
     if tokens:
-        _lib.call("smoe_route", _lib.ptr(gate.weight.contiguous()),
+        common = (_lib.ptr(gate.weight.contiguous()),
                   _lib.ptr(shared_gate.weight.contiguous()) if shared_gate is not None else None, _lib.ptr(x2),
                   _lib.dtype_code(x.dtype), tokens, gate.rows, gate.cols, k, _lib.ptr(logits), _lib.ptr(idx),
-                  _lib.ptr(w), _lib.ptr(g) if g is not None else None, _lib.ptr(counters), _lib.stream())
+                  _lib.ptr(w), _lib.ptr(g) if g is not None else None, _lib.ptr(counters))
+        if local is None:
+            _lib.call("smoe_route", *common, _lib.stream())
+        else:
+            _lib.call("smoe_route_local", *common, local[0], local[1], _lib.ptr(lidx), _lib.stream())
     lead = x.shape[:-1]
-    return (idx.reshape(*lead, k), w.reshape(*lead, k),
-            g.reshape(*lead, 1) if g is not None else None)
+    out = (idx.reshape(*lead, k), w.reshape(*lead, k), g.reshape(*lead, 1) if g is not None else None)
+    return out if local is None else out + (lidx.reshape(*lead, k),)
 
 
 def moe_combine(y: torch.Tensor, w: torch.Tensor, g: torch.Tensor, s: torch.Tensor):
@@ -300,23 +307,44 @@ class GraphedBlock:
 
     Calling it copies x into the graph's static input, replays every launch of `block(x)` without host
     work in between, and returns the graph's static output (overwritten by the next call). Kernels, shapes
-    and numerics are those of `block(x)`."""
+    and numerics are those of `block(x)`.
 
-    def __init__(self, block, tokens: int, hidden: int, dtype=torch.float16, device=None):
+    With `host_io` the step's copies are in the graph too: the host-to-device copy of the token from a pinned
+    host buffer and the device-to-host copy of the result into another, so a step is one graph launch. Call it
+    with a host tensor; it returns the pinned host result, valid once the stream has reached the step
+    (`torch.cuda.current_stream().synchronize()`, or `ready.synchronize()`). A call first waits for this graph's
+    previous replay to have read its input buffer."""
+
+    def __init__(self, block, tokens: int, hidden: int, dtype=torch.float16, device=None, host_io: bool = False):
         device = device or torch.device("cuda", torch.cuda.current_device())
-        self.block = block
+        self.block, self.host_io = block, host_io
         self.x = torch.zeros(tokens, hidden, dtype=dtype, device=device)
         side = torch.cuda.Stream(device)
         side.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(side):
             for _ in range(2):  # load the library, size the allocator's pool
-                block(self.x)
+                out = block(self.x)
         torch.cuda.current_stream(device).wait_stream(side)
+        if host_io:
+            self.host_x = torch.zeros(tokens, hidden, dtype=dtype).pin_memory()
+            self.host_out = torch.empty(tuple(out.shape), dtype=out.dtype).pin_memory()
+            self.ready = torch.cuda.Event()
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
+            if host_io:
+                self.x.copy_(self.host_x, non_blocking=True)
             self.out = block(self.x)
+            if host_io:
+                self.host_out.copy_(self.out, non_blocking=True)
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        if self.host_io:
+            self.ready.synchronize()  # (the previous replay has read host_x and filled host_out)
+            if x.data_ptr() != self.host_x.data_ptr():
+                self.host_x.copy_(x.reshape(self.host_x.shape))
+            self.graph.replay()
+            self.ready.record()
+            return self.host_out
         self.x.copy_(x.reshape(self.x.shape), non_blocking=True)
         self.graph.replay()
         return self.out

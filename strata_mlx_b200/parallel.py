@@ -170,10 +170,10 @@ class ExpertParallelMoE:
     `layer` is this rank's part (`shard_layer`): the full router and shared-expert gate, the rank's experts,
     its slice of the shared expert. Returns the whole block's output on every rank.
 
-    With a `PeerExchange`, a decode step of float16 tokens is five launches overlapped by programmatic
-    dependent launch: `smoe_route` (router, top-k, softmax, shared gate), `smoe_localize`, the routed and shared
-    gate / up products in one launch, both down products in one launch, and `smoe_ep_reduce_combine` (the
-    exchange of the partial sums over peer memory with the combine). Without one (or for other activations),
+    With a `PeerExchange`, a decode step of float16 tokens is four launches overlapped by programmatic
+    dependent launch: `smoe_route_local` (router, top-k, softmax, shared gate and this rank's view of the
+    choice), the routed and shared gate / up products in one launch, both down products in one launch, and
+    `smoe_ep_reduce_combine` (the exchange of the partial sums over peer memory with the combine). Without one (or for other activations),
     the partial sums go through one all-reduce of the process group."""
 
     def __init__(self, layer: SparseMoeBlock, rank: int, world: int, experts: int, group=None,
@@ -198,11 +198,10 @@ class ExpertParallelMoE:
                 or x2.dtype not in (torch.float16, torch.float32)):
             return None
         k = layer.top_k
-        r = route(layer.gate, layer.shared_expert_gate, x2, k)
+        r = route(layer.gate, layer.shared_expert_gate, x2, k, local=(self.lo, self.count))
         if r is None:
             return None
-        idx, w, g = r
-        lidx = self.local_indices(idx)
+        idx, w, g, lidx = r
         sw, sh = layer.switch_mlp, layer.shared_expert
         ys = None
         if isinstance(sw, BlockSwitchGLU) and isinstance(sh, BlockMLP):

@@ -199,3 +199,42 @@ def test_a_prompt_chunk_at_baseline_shapes_is_the_oracles(cuda):
     assert counts.min() > 0 and counts.max() > 2 * counts.mean()  # skewed, every expert hit
     assert np.isfinite(got).all()
     assert rel_l2(got, want) <= 1e-3
+
+
+def test_a_graph_with_its_host_copies_gives_the_eager_bits(cuda):
+    """GraphedBlock(host_io=True): the token's copy in from pinned host memory and the result's copy out are in
+    the graph; a step returns the eager block's bits on the host, calls in a row included."""
+    rng = np.random.default_rng(12)
+    H, F_, E, Fs, k = 512, 256, 16, 512, 4
+    routed, shared, router, sgate = make_layer(rng, H, F_, E, Fs, ("IQ3_S",) * 3, "Q8_0")
+    block = build_block(routed, shared, router, sgate, k)
+    xs = [rng.standard_normal((1, H)).astype(np.float16) for _ in range(3)]
+    eager = [block(dev(x)).cpu().numpy() for x in xs]
+    gb = F.GraphedBlock(block, 1, H, torch.float16, cuda, host_io=True)
+    for _ in range(2):
+        for x, want in zip(xs, eager):
+            got = gb(torch.from_numpy(x))
+            gb.ready.synchronize()
+            assert not got.is_cuda and got.is_pinned()
+            np.testing.assert_array_equal(got.numpy().view(np.uint16), want.view(np.uint16))
+
+
+@pytest.mark.parametrize("lo, count", [(0, 64), (64, 64), (192, 64), (0, 256), (96, 32)])
+def test_route_with_the_ranks_view_is_route_then_localize(cuda, lo, count):
+    """smoe_route_local: the same logits, choice, weights and gate bits as smoe_route, and the local indices
+    smoe_localize gives for the experts [lo, lo + count)."""
+    from strata_mlx_b200 import _lib
+
+    rng = np.random.default_rng(lo + count)
+    E, H, k, T = 256, 4096, 8, 3
+    router = dev((0.02 * rng.standard_normal((E, H))).astype(np.float16))
+    sgate = dev((0.02 * rng.standard_normal((1, H))).astype(np.float16))
+    x = dev(rng.standard_normal((T, H)).astype(np.float16))
+    gate, sg = F.WindowLinear(router), F.WindowLinear(sgate)
+    idx, w, g = F.route(gate, sg, x, k)
+    idx2, w2, g2, lidx = F.route(gate, sg, x, k, local=(lo, count))
+    assert torch.equal(idx, idx2) and torch.equal(w, w2) and torch.equal(g, g2)
+    want = torch.empty_like(idx)
+    flat = idx.reshape(-1).contiguous()
+    _lib.call("smoe_localize", _lib.ptr(flat), flat.numel(), lo, count, _lib.ptr(want), _lib.stream())
+    assert torch.equal(lidx.reshape(-1), want.reshape(-1))
