@@ -777,7 +777,8 @@ def run_ours(args, rank, world, local_rank):
         blocks = layers
     stream = torch.cuda.current_stream()
     from strata_mlx_b200 import _lib
-    from strata_mlx_b200.fused import GraphedBlock, top_k_softmax
+    from strata_mlx_b200 import fused as Fz
+    from strata_mlx_b200.fused import GraphedBlock, route, top_k_softmax
 
     # one CUDA graph per layer: a decode engine's step, with the token already in its static input
     graphs = []
@@ -814,8 +815,9 @@ def run_ours(args, rank, world, local_rank):
         raise RuntimeError("a wait of the peer exchange gave up during the timed steps")
 
     # the dominant kernel alone: a graph of its launches over the rotating layers, with each layer's routing: the
-    # step's batched gate/up launch (the routed experts' of this rank and the shared expert's, in one int8
-    # tensor-core kernel)
+    # step's batched gate / up launch (the routed experts' of this rank and the shared expert's products in one
+    # int8 tensor-core kernel; with FUSED_ROUTE the route with this rank's view of it in the same launch)
+    fuse = Fz.FUSED_ROUTE
     routes, gu_bytes = [], 0
     for i in range(args.layers):
         blk = blocks[i]
@@ -827,24 +829,30 @@ def run_ours(args, rank, world, local_rank):
         sw, sh = layer.switch_mlp, layer.shared_expert
         valid = int((fi.view(torch.int32) < sw.gate_proj.num_experts).sum().item())
         gu_bytes += (2 * valid * F_ * B.row_bytes(KIND, H)
-                     + 2 * sh.gate_proj.output_dims * B.row_bytes(SHARED_KIND, H))
+                     + 2 * sh.gate_proj.output_dims * B.row_bytes(SHARED_KIND, H) + ((E + 1) * H * 2 if fuse else 0))
+        if fuse:
+            r = route(layer.gate, layer.shared_expert_gate, xs[i], K, defer=True,
+                      local=(blk.lo, blk.count) if world > 1 else None)
+            step_r, ri = r[-1], (r[3] if world > 1 else r[0]).reshape(-1)
+        else:
+            step_r, ri = None, fi
         outs = [torch.empty((K, F_), dtype=torch.float16, device=device) for _ in range(2)]
         souts = [torch.empty((1, sh.gate_proj.output_dims), dtype=torch.float16, device=device) for _ in range(2)]
         z = B._zeros_idx(1, device)
-        probs = [B._problem(sw.gate_proj, fi, K, K, outs[0], x=xs[i]), B._problem(sw.up_proj, fi, K, K, outs[1], x=xs[i]),
+        probs = [B._problem(sw.gate_proj, ri, K, K, outs[0], x=xs[i]), B._problem(sw.up_proj, ri, K, K, outs[1], x=xs[i]),
                  B._problem(sh.gate_proj.stack, z, 1, 1, souts[0], x=xs[i]),
                  B._problem(sh.up_proj.stack, z, 1, 1, souts[1], x=xs[i])]
-        routes.append((probs, outs + souts, fi))
+        routes.append((probs, outs + souts, step_r))
     gu_bytes /= args.layers  # per launch, averaged over the layers' routings
     reps = max(1, 64 // args.layers)
-    for probs, _, _ in routes:
-        B.matvec_batch(probs)
+    for probs, _, step_r in routes:
+        B.matvec_batch(probs, route=step_r)
     torch.cuda.synchronize()
     gu_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gu_graph):
         for _ in range(reps):
-            for probs, _, _ in routes:
-                B.matvec_batch(probs)
+            for probs, _, step_r in routes:
+                B.matvec_batch(probs, route=step_r)
     gu_graph.replay()
     torch.cuda.synchronize()
     g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -922,8 +930,11 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": launches * args.steps,
         "e2e": {"value": args.steps / (e2e_ms * 1e-3), "unit": "token-layers/s",
                 "h2d_bytes_per_step": H * 2, "d2h_bytes_per_step": H * 2},
-        "roofline": {"kernel": "mv8_kernel (batched gate+up: this rank's IQ3_S 1536 x 4096 pairs + the Q8_0 shared "
-                               "expert's gate and up rows)", "bound": "hbm",
+        "roofline": {"kernel": ("mv8_kernel (the route with the batched gate+up: the router's 257 x 4096 float16 rows, "
+                                "this rank's IQ3_S 1536 x 4096 pairs, the Q8_0 shared expert's gate and up rows)") if fuse
+                     else ("mv8_kernel (batched gate+up: this rank's IQ3_S 1536 x 4096 pairs + the Q8_0 shared "
+                           "expert's gate and up rows)"),
+                     "bound": "hbm",
                      "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind,
                      "algorithmic_bytes_per_launch": gu_bytes, "launch_ms": gu,

@@ -85,8 +85,10 @@ SMOE_API int smoe_matvec(int kind, const uint8_t* blocks, int64_t experts, int64
  * and leaves that launch's outputs not valid. smoe_matvec_status synchronizes the current device and reads the
  * word (0 or SMOE_ETIMEOUT); `clear` zeroes it. smoe_matvec_wait_test is for tests that make a wait run out:
  * it sets, on the current device, the bound in polls (each suspends the waiting thread up to 1 ms; < 0 restores
- * the default) and, with `withhold`, has every warp leave its first weight copy unissued, so that the wait for it
- * runs out; it synchronizes the device. No counterpart in the reference (its kernels have no device-side waits). */
+ * the default) and, with `withhold` 1, has every warp leave its first weight copy unissued, so that the wait for it
+ * runs out, or with `withhold` 2 has smoe_route_matvec_batch's fused launch never announce its route, so that
+ * the routed products' waits for it run out; it synchronizes the device. No counterpart in the reference (its
+ * kernels have no device-side waits). */
 SMOE_API int smoe_matvec_status(int* status, int clear);
 SMOE_API int smoe_matvec_wait_test(int64_t polls, int withhold);
 
@@ -172,6 +174,35 @@ SMOE_API int smoe_route_local(const uint16_t* weight, const uint16_t* gate_weigh
                               int64_t tokens, int64_t experts, int64_t hidden, int64_t k, float* logits, uint32_t* idx,
                               float* weights, void* gate_out, uint32_t* counters, int64_t lo, int64_t count,
                               uint32_t* lidx, void* stream);
+
+/* The route of a decode step and the products that read it, in one launch where the kernel takes them:
+ * smoe_route (lidx NULL) or smoe_route_local (lidx set), then smoe_matvec_batch(n, problems) -- the same
+ * logits, idx, weights, gate_out and lidx, and the same products within the batch's rounding (its teams may
+ * group a product's partial sums differently from another batch). A problem whose idx points into the route's
+ * idx or lidx reads the route's choice: the launch's CTAs each take two router rows, the last CTA in takes the
+ * top-k, and the copies of the routed experts' weights start once it has; the other problems' (the shared
+ * expert's) run meanwhile. Taken for float16 x, at most 8 tokens and 256 experts and the batch's one-launch
+ * problems; otherwise the two calls run one after the other. `counters`: smoe_route_step_counters(tokens)
+ * bytes, zero before the first call (calls sharing them must not overlap on the GPU): two words for the fused
+ * launch, then smoe_route's counters for the two calls' form. No single reference
+ * counterpart: it fuses the start of `_Routed.__call__` (strata_mlx/fused.py:487-491) with the first products
+ * of `switch_mlp` and `shared_expert` (strata_mlx/blocks.py:939-986, strata_mlx/load.py:419-421). */
+typedef struct SmoeRouteStep {
+    const uint16_t* weight;       /* router (experts, hidden), float16 */
+    const uint16_t* gate_weight;  /* the shared gate (1, hidden), float16, or NULL */
+    const void* x;                /* (tokens, hidden) of x_dtype */
+    int x_dtype;
+    int64_t tokens, experts, hidden, k;
+    float* logits;                /* (tokens, experts) */
+    uint32_t* idx;                /* (tokens, k) */
+    float* weights;               /* (tokens, k) */
+    void* gate_out;               /* (tokens) of x_dtype; NULL with gate_weight NULL */
+    uint32_t* counters;
+    int64_t lo, count;            /* with lidx: this rank's experts [lo, lo + count) */
+    uint32_t* lidx;               /* (tokens, k), or NULL */
+} SmoeRouteStep;
+SMOE_API size_t smoe_route_step_counters(int64_t tokens);
+SMOE_API int smoe_route_matvec_batch(const SmoeRouteStep* route, int n, const SmoeMatvec* problems, void* stream);
 
 /* The end of the MoE block: out[t, d] = half(sum_k y[t,k,d] w[t,k]) + half(half(sigmoid(g[t])) s[t,d]),
  * the sum in float32 in MLX's col_reduce_small order (partials j = k mod 8, then in order), every product

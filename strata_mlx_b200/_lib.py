@@ -27,6 +27,14 @@ class SmoeMatvec(ctypes.Structure):
                 ("pairs", _i64), ("share", _i64), ("x", _p), ("gate", _p), ("up", _p), ("out", _p), ("dtype", _i)]
 
 
+class SmoeRouteStep(ctypes.Structure):
+    """`SmoeRouteStep` of include/strata_moe.h: a decode step's route for smoe_route_matvec_batch."""
+
+    _fields_ = [("weight", _p), ("gate_weight", _p), ("x", _p), ("x_dtype", _i), ("tokens", _i64), ("experts", _i64),
+                ("hidden", _i64), ("k", _i64), ("logits", _p), ("idx", _p), ("weights", _p), ("gate_out", _p),
+                ("counters", _p), ("lo", _i64), ("count", _i64), ("lidx", _p)]
+
+
 class SmoeDecodeLayer(ctypes.Structure):
     """`SmoeDecodeLayer` of include/strata_moe.h: one MoE block for smoe_decode_layer."""
 
@@ -73,6 +81,8 @@ SIGNATURES = {
     "smoe_top_k": (_i, [_p, _i64, _i64, _i64, _p, _p, _p]),
     "smoe_combine": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
     "smoe_route_counters": (_sz, [_i64]),
+    "smoe_route_step_counters": (_sz, [_i64]),
+    "smoe_route_matvec_batch": (_i, [_c.POINTER(SmoeRouteStep), _i, _c.POINTER(SmoeMatvec), _p]),
     "smoe_route": (_i, [_p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p]),
     "smoe_route_local": (_i, [_p, _p, _p, _i, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p, _i64, _i64, _p, _p]),
     "smoe_localize": (_i, [_p, _i64, _i64, _i64, _p, _p]),

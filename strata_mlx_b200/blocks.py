@@ -15,6 +15,7 @@ reference (strata_mlx/blocks.py), so an engine written against it can import thi
 are torch CUDA tensors; there is no CPU path and no fallback to another library's kernels.
 """
 
+import ctypes
 import math
 
 import torch
@@ -382,13 +383,19 @@ def _problem(lin, idx, pairs, share, out, x=None, gate=None, up=None):
                            _lib.dtype_code(out.dtype if out is not None else torch.float16))
 
 
-def matvec_batch(problems) -> None:
-    """Run several products in one smoe_matvec_batch call (each an smoe_matvec or smoe_matvec_glu problem)."""
+def matvec_batch(problems, route=None) -> None:
+    """Run several products in one smoe_matvec_batch call (each an smoe_matvec or smoe_matvec_glu problem); with
+    `route` (a deferred route's SmoeRouteStep) the route too, in the same launch where the kernel takes both
+    (smoe_route_matvec_batch)."""
     arr = (_lib.SmoeMatvec * len(problems))(*problems)
-    _lib.call("smoe_matvec_batch", len(problems), arr, _lib.stream())
+    if route is None:
+        _lib.call("smoe_matvec_batch", len(problems), arr, _lib.stream())
+    else:
+        _lib.call("smoe_route_matvec_batch", ctypes.byref(route), len(problems), arr, _lib.stream())
 
 
-def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, w=None, g=None, batched_down=None):
+def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, w=None, g=None, batched_down=None,
+                    route_step=None):
     """(switch_mlp(x, indices), shared(x)) for a step that runs both on the decode matvec, with the routed and
     the shared expert's gate and up products in one launch (the same products, within the kernel's rounding,
     as the separate calls), then the two down products. With the combine's w (..., k) float32 and g (..., 1),
@@ -396,7 +403,10 @@ def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, 
     the result is (None, out). `batched_down` (default: the module's BATCHED_DOWN) puts both down products in
     one launch and returns (y, s). None where either would take another path (a prompt's tiles, unpacked
     floats, a SwiGLU the down product does not take, activations of another type). Indices at or past a stack's
-    expert count name pairs the products leave out (their rows are not written)."""
+    expert count name pairs the products leave out (their rows are not written).
+
+    `route_step`: the deferred route (`fused.route(..., defer=True)`) that writes `indices` (and w, g); it is
+    launched with the gate / up products. When the result is None nothing was launched, the route included."""
     lins = (switch_mlp.gate_proj, switch_mlp.up_proj, switch_mlp.down_proj)
     slins = (shared.gate_proj, shared.up_proj, shared.down_proj)
     if x.dtype != torch.float16 or indices.numel() >= TILES_FROM or not BLOCK_GLU:
@@ -421,7 +431,8 @@ def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, 
         # with the two down stacks' weights fetched into L2 meanwhile (the gate/up launch is compute-bound)
         ahead = [_problem(down, idx, pairs, 1, None), _problem(sd, zeros, tokens, 1, None)] if PREFETCH_DOWN else []
         matvec_batch([_problem(gate, idx, pairs, k, g_r, x=x2), _problem(up, idx, pairs, k, u_r, x=x2),
-                      _problem(sg, zeros, tokens, 1, gs, x=x2), _problem(su, zeros, tokens, 1, us, x=x2)] + ahead)
+                      _problem(sg, zeros, tokens, 1, gs, x=x2), _problem(su, zeros, tokens, 1, us, x=x2)] + ahead,
+                     route=route_step)
     if batched_down is None:
         batched_down = BATCHED_DOWN
     if batched_down and sd.kind in FUSED_GLU and down.kind in FUSED_GLU:

@@ -61,15 +61,20 @@ __device__ __forceinline__ void pdl_release() { asm volatile("griddepcontrol.lau
 
 // The device memory one launch writes.
 struct Writes {
-    static constexpr int kMax = 6;
+    static constexpr int kMax = 12;
     const void* p[kMax] = {};
     size_t n[kMax] = {};
     int count = 0;
+    bool all = false;  // more ranges than kMax: the launch counts as writing everything
     Writes& add(const void* ptr, size_t bytes) {
-        if (ptr != nullptr && bytes > 0 && count < kMax) {
-            p[count] = ptr;
-            n[count] = bytes;
-            ++count;
+        if (ptr != nullptr && bytes > 0) {
+            if (count < kMax) {
+                p[count] = ptr;
+                n[count] = bytes;
+                ++count;
+            } else {
+                all = true;
+            }
         }
         return *this;
     }

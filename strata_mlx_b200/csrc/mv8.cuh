@@ -29,9 +29,28 @@ struct M8Pref {
     uint32_t experts;
 };
 
-// n <= 4 problems in one launch (and up to two stacks' weights fetched into L2 for later launches): 0 launched,
-// 1 not taken (the caller runs them another way), else an error.
-int mv8_batch(int n, const M8Spec* specs, cudaStream_t st, int npf = 0, const M8Pref* pf = nullptr);
+// The route of the tokens whose products a launch takes (smoe_route / smoe_route_local in the same launch):
+// router rows w (experts, hidden) and the shared gate row gw (or null) against x (tokens, hidden) float16 ->
+// logits, idx, weights, gate_out, and with lidx set the pairs' local expert numbers (idx - lo where below
+// count, else count). counters[0] counts the CTAs whose router rows are in; counters[1] is the launch number
+// the CTA that takes the top-k moves on once idx is written. Problems whose idx is this idx or lidx read it
+// once that number has moved.
+struct M8Route {
+    const __half *w, *gw, *x;
+    float* logits;
+    uint32_t* idx;
+    float* weights;
+    __half* gate_out;
+    uint32_t* counters;
+    uint32_t* lidx;
+    uint32_t lo, count;
+    int tokens, experts, hidden, k;
+};
+
+// n <= 4 problems in one launch (and up to two stacks' weights fetched into L2 for later launches, and the
+// route of their tokens): 0 launched, 1 not taken (the caller runs them another way), else an error.
+int mv8_batch(int n, const M8Spec* specs, cudaStream_t st, int npf = 0, const M8Pref* pf = nullptr,
+              const M8Route* route = nullptr);
 
 // the gate / up problems (nprob 1 or 2) of one stack pair: 0 launched, 1 not taken, else an error
 int mv8_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t experts, int64_t rows, int64_t cols,

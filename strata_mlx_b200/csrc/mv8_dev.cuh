@@ -327,7 +327,7 @@ struct M8Q8_0 {
     __device__ static void fill(uint32_t*) {}
     __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t*,
                                  const uint8_t* xh, const uint8_t* xl, const float* xs, float (&total)[2]) {
-        const uint8_t* rb[2] = {r0, r1};
+        const uint32_t rb[2] = {smem_addr(r0), smem_addr(r1)};  // (32-bit shared addresses: plain LDS)
         const uint8_t* xsrc = gid == 0 ? xh : xl;
         const float k = xs[0] * (1.0f / 128.0f);  // (a stage lies within one 256-column scale block)
 #pragma unroll
@@ -336,13 +336,12 @@ struct M8Q8_0 {
             float d[2];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const uint8_t* p = rb[j] + 34 * r + 2 + 8 * tig;
-                const uint32_t* w = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
-                const uint32_t sh = 8u * static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 3u);
-                const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+                const uint32_t p = rb[j] + 34 * r + 2 + 8 * tig;
+                const uint32_t wa = p & ~3u, sh = 8u * (p & 3u);
+                const uint32_t w0 = ld_s32(wa), w1 = ld_s32(wa + 4), w2 = ld_s32(wa + 8);
                 a[j][0] = __funnelshift_r(w0, w1, sh);
                 a[j][1] = __funnelshift_r(w1, w2, sh);
-                d[j] = h2f(lds_u16(rb[j] + 34 * r));
+                d[j] = h2f(lds_u16_at(rb[j] + 34 * r));
             }
             uint2 b = make_uint2(0u, 0u);
             if (gid < 2) b = *reinterpret_cast<const uint2*>(xsrc + 32 * r + 8 * tig);
@@ -358,7 +357,7 @@ struct M8Q8_0 {
     __device__ static void stage_tokens(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint8_t* xh,
                                         const uint8_t* xl, int64_t xstride, const float* xs, int xsstride, int nt,
                                         float (&total)[2]) {
-        const uint8_t* rb[2] = {r0, r1};
+        const uint32_t rb[2] = {smem_addr(r0), smem_addr(r1)};
         const int t = gid >> 1;
         const uint8_t* xsrc = ((gid & 1) ? xl : xh) + int64_t(t) * xstride;
         const float k = tig < nt ? xs[tig * xsstride] * (1.0f / 128.0f) : 0.0f;
@@ -368,13 +367,12 @@ struct M8Q8_0 {
             float d[2];
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
-                const uint8_t* p = rb[j] + 34 * r + 2 + 8 * tig;
-                const uint32_t* w = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
-                const uint32_t sh = 8u * static_cast<uint32_t>(reinterpret_cast<uintptr_t>(p) & 3u);
-                const uint32_t w0 = w[0], w1 = w[1], w2 = w[2];
+                const uint32_t p = rb[j] + 34 * r + 2 + 8 * tig;
+                const uint32_t wa = p & ~3u, sh = 8u * (p & 3u);
+                const uint32_t w0 = ld_s32(wa), w1 = ld_s32(wa + 4), w2 = ld_s32(wa + 8);
                 a[j][0] = __funnelshift_r(w0, w1, sh);
                 a[j][1] = __funnelshift_r(w1, w2, sh);
-                d[j] = h2f(lds_u16(rb[j] + 34 * r));
+                d[j] = h2f(lds_u16_at(rb[j] + 34 * r));
             }
             uint2 b = make_uint2(0u, 0u);
             if (t < nt) b = *reinterpret_cast<const uint2*>(xsrc + 32 * r + 8 * tig);

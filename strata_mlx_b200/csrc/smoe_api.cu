@@ -46,6 +46,7 @@ bool pdl_early(cudaStream_t st, const void* p, size_t n) {
     if (it == g_pdl.end()) return true;
     const uintptr_t a0 = reinterpret_cast<uintptr_t>(p), a1 = a0 + n;
     const Writes& w = it->second.w;
+    if (w.all) return false;
     for (int i = 0; i < w.count; ++i) {
         const uintptr_t b0 = reinterpret_cast<uintptr_t>(w.p[i]), b1 = b0 + w.n[i];
         if (a0 < b1 && b0 < a1) return false;

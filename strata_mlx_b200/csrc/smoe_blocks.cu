@@ -530,16 +530,19 @@ extern "C" int smoe_matvec(int kind, const uint8_t* blocks, int64_t experts, int
     return fail(SMOE_EDTYPE, "activations must be float16 or float32");
 }
 
-extern "C" int smoe_matvec_batch(int n, const SmoeMatvec* pr, void* stream) {
+namespace {
+// smoe_matvec_batch's checks, and the problems one int8 tensor-core launch takes: `one` when all are float16
+// and at most four compute (spec[0 .. m)), with up to two L2 fetches for a later launch (pref[0 .. npf)).
+int batch_specs(int n, const SmoeMatvec* pr, M8Spec* spec, int& m, M8Pref* pref, int& npf, bool& one) {
     SMOE_REQUIRE(n >= 0 && n <= 64, SMOE_EARG, "a batch holds 0 to 64 problems");
+    m = npf = 0;
+    one = false;
     if (n == 0) return SMOE_OK;
     SMOE_REQUIRE(pr != nullptr, SMOE_EARG, "null problem list");
     // every problem checked as its own entry point checks it, before any launch
-    M8Spec spec[4];
-    M8Pref pref[2];
-    int m = 0, npf = 0, ncomp = 0;
+    int ncomp = 0;
     for (int i = 0; i < n; ++i) ncomp += pr[i].out != nullptr ? 1 : 0;
-    bool one_launch = ncomp <= 4;
+    one = ncomp <= 4;
     for (int i = 0; i < n; ++i) {
         const SmoeMatvec& p = pr[i];
         int per, bytes;
@@ -560,21 +563,17 @@ extern "C" int smoe_matvec_batch(int n, const SmoeMatvec* pr, void* stream) {
         if (p.pairs == 0) continue;
         SMOE_REQUIRE(p.blocks && p.idx && p.out, SMOE_EARG, "null pointer");
         SMOE_REQUIRE(p.x == nullptr || p.share >= 1, SMOE_EARG, "share must be >= 1");
-        if (p.dtype != SMOE_F16) one_launch = false;
-        if (one_launch)
+        if (p.dtype != SMOE_F16) one = false;
+        if (one)
             spec[m++] = M8Spec{p.kind, p.blocks, p.experts, p.rows, p.cols, p.cols / per * bytes, p.idx, p.pairs,
                                p.x ? p.share : 1, static_cast<const __half*>(p.x), static_cast<const __half*>(p.gate),
                                static_cast<const __half*>(p.up), static_cast<__half*>(p.out)};
     }
-    cudaStream_t st = as_stream(stream);
-    if (one_launch && m > 0) {
-        const M8Spec& a = spec[0];
-        const int r = m == 1 && npf == 0
-                          ? mv8_try(a.kind, a.kind, a.blocks, a.blocks, a.experts, a.rows, a.cols, a.row_bytes, a.idx,
-                                    a.pairs, a.share, a.x, a.gate, a.up, a.out, a.out, 1, st)
-                          : mv8_batch(m, spec, st, npf, pref);
-        if (r != 1) return r;
-    }
+    return SMOE_OK;
+}
+
+// the problems one by one through their own entry points
+int batch_each(int n, const SmoeMatvec* pr, void* stream) {
     for (int i = 0; i < n; ++i) {
         const SmoeMatvec& p = pr[i];
         if (p.pairs == 0 || p.out == nullptr) continue;
@@ -585,6 +584,75 @@ extern "C" int smoe_matvec_batch(int n, const SmoeMatvec* pr, void* stream) {
         if (r) return r;
     }
     return SMOE_OK;
+}
+}  // namespace
+
+extern "C" int smoe_matvec_batch(int n, const SmoeMatvec* pr, void* stream) {
+    M8Spec spec[4];
+    M8Pref pref[2];
+    int m = 0, npf = 0;
+    bool one_launch = false;
+    if (int s = batch_specs(n, pr, spec, m, pref, npf, one_launch)) return s;
+    cudaStream_t st = as_stream(stream);
+    if (one_launch && m > 0) {
+        const M8Spec& a = spec[0];
+        const int r = m == 1 && npf == 0
+                          ? mv8_try(a.kind, a.kind, a.blocks, a.blocks, a.experts, a.rows, a.cols, a.row_bytes, a.idx,
+                                    a.pairs, a.share, a.x, a.gate, a.up, a.out, a.out, 1, st)
+                          : mv8_batch(m, spec, st, npf, pref);
+        if (r != 1) return r;
+    }
+    return batch_each(n, pr, stream);
+}
+
+// [0] the fused launch's arrivals, [1] its launch number, then smoe_route's counters (the two calls' form)
+extern "C" size_t smoe_route_step_counters(int64_t tokens) {
+    return (8 + smoe_route_counters(tokens) + 15) & ~size_t(15);
+}
+
+extern "C" int smoe_route_matvec_batch(const SmoeRouteStep* r, int n, const SmoeMatvec* pr, void* stream) {
+    SMOE_REQUIRE(r != nullptr, SMOE_EARG, "null route");
+    SMOE_REQUIRE(r->tokens >= 0, SMOE_EARG, "negative token count");
+    if (r->tokens == 0) return SMOE_OK;  // (no tokens: no pairs)
+    SMOE_REQUIRE(r->lidx == nullptr || (r->lo >= 0 && r->count >= 0 && r->lo + r->count <= r->experts &&
+                                        r->count < (int64_t(1) << 31)),
+                 SMOE_EARG, "route: this rank's experts [lo, lo + count) lie within the router's");
+    M8Spec spec[4];
+    M8Pref pref[2];
+    int m = 0, npf = 0;
+    bool one_launch = false;
+    if (int s = batch_specs(n, pr, spec, m, pref, npf, one_launch)) return s;
+    cudaStream_t st = as_stream(stream);
+    if (one_launch && m > 0 && r->x_dtype == SMOE_F16 && r->weight && r->x && r->logits && r->idx && r->weights &&
+        r->counters && r->experts > 0 && r->k > 0) {
+        M8Route R{};
+        R.w = reinterpret_cast<const __half*>(r->weight);
+        R.gw = reinterpret_cast<const __half*>(r->gate_weight);
+        R.x = static_cast<const __half*>(r->x);
+        R.logits = r->logits;
+        R.idx = r->idx;
+        R.weights = r->weights;
+        R.gate_out = static_cast<__half*>(r->gate_out);
+        R.counters = r->counters;
+        R.lidx = r->lidx;
+        R.lo = static_cast<uint32_t>(r->lidx ? r->lo : 0);
+        R.count = static_cast<uint32_t>(r->lidx ? r->count : 0);
+        R.tokens = static_cast<int>(std::min<int64_t>(r->tokens, 1 << 20));
+        R.experts = static_cast<int>(std::min<int64_t>(r->experts, 1 << 20));
+        R.hidden = static_cast<int>(std::min<int64_t>(r->hidden, 1 << 30));
+        R.k = static_cast<int>(std::min<int64_t>(r->k, 1 << 20));
+        const int res = mv8_batch(m, spec, st, npf, pref, &R);
+        if (res != 1) return res;
+    }
+    // the route alone, then the products
+    uint32_t* rc = r->counters ? r->counters + 2 : nullptr;
+    const int s = r->lidx ? smoe_route_local(r->weight, r->gate_weight, r->x, r->x_dtype, r->tokens, r->experts,
+                                             r->hidden, r->k, r->logits, r->idx, r->weights, r->gate_out, rc, r->lo,
+                                             r->count, r->lidx, stream)
+                          : smoe_route(r->weight, r->gate_weight, r->x, r->x_dtype, r->tokens, r->experts, r->hidden,
+                                       r->k, r->logits, r->idx, r->weights, r->gate_out, rc, stream);
+    if (s) return s;
+    return smoe_matvec_batch(n, pr, stream);
 }
 
 extern "C" int smoe_matvec_glu_combine(int kind, const uint8_t* blocks, int64_t rows, int64_t cols,

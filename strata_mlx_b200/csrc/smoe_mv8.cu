@@ -30,6 +30,7 @@
 
 #include "mv8.cuh"
 #include "mv8_dev.cuh"
+#include "router_dev.cuh"
 
 namespace smoe {
 // A wait for a weight copy that gives up (it should not: each is bounded, about a second) records SMOE_ETIMEOUT
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
-    const bool withhold = g_mv8_withhold != 0;
+    const bool withhold = g_mv8_withhold == 1;
     if (smem_addr(sm) & 127u) return;  // a tiled copy's destination is 128-byte aligned (the launch gives that)
     const int team = a.team, teams = kM8Warps / team;
     const int tid_team = warp / team, kq = warp % team;
@@ -186,13 +187,14 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         i_valid = __shfl_sync(0xffffffffu, j_valid, job);
     };
     // issue the cursor's item (a pair naming no expert copies nothing and completes the slot's phase with a
-    // plain arrive, so every item takes one phase) and move on
+    // plain arrive, so every item takes one phase) and move on; the weights are read once: evict-first in L2
+    const uint64_t stream_policy = tc::policy_evict_first();
     auto issue = [&]() {
         if (lane == 0 && !(withhold && issued == 0)) {
             if (i_valid) {
                 tc::mbar_arrive_expect_tx(&my_bars[i_slot], static_cast<uint32_t>(kSlot));
-                tc::tma_load_2d(smem_addr(my_ring + i_slot * kSlot), &maps.w[i_map], (i_pos & ~15) >> 2, i_y,
-                                &my_bars[i_slot]);
+                tc::tma_load_2d_hint(smem_addr(my_ring + i_slot * kSlot), &maps.w[i_map], (i_pos & ~15) >> 2, i_y,
+                                     &my_bars[i_slot], stream_policy);
             } else {
                 tc::mbar_arrive(&my_bars[i_slot]);
             }
@@ -344,6 +346,7 @@ struct M8Prob {
     int job0, jobs;               // its jobs in the launch: [job0, job0 + jobs)
     int pairs, share, xs;         // pairs, pairs per activation row, activation source
     int early;                    // idx may be read before pdl_wait (the launch ahead does not write it)
+    int wait;                     // idx is written by this launch's route: read it once the route is in
 };
 // An activation source: rows of `cols` float16, or the SwiGLU of two such (down's input).
 struct M8X {
@@ -362,10 +365,24 @@ struct M8Launch {
     M8Prob p[kM8MaxProbs];
     M8X x[kM8MaxX];
     M8Pref pf[kM8MaxPref];  // later launches' weights fetched into L2 while this one streams its own
-    int npf;
+    M8Route r;              // the route of the tokens (has_route): CTAs [0, route_ctas) hold two router rows each
+    int npf, has_route, route_ctas;
     int nprob, nx, jobs, team, nslots, slot_bytes, lut, scales;
     int64_t xbytes;
 };
+constexpr int kM8RouteBytes = 2 * 4 * kRtTokens * 4 + 16;  // the route's partial sums and its last-CTA flag
+
+__device__ __forceinline__ uint32_t ld_relaxed_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+// warps 0..7 of a CTA (the route's rows) meet at named barrier 15 (team barriers use 1..8)
+__device__ __forceinline__ void route_sync() { asm volatile("bar.sync 15, 256;" ::: "memory"); }
 struct alignas(64) M8Maps {
     CUtensorMap w[kM8MaxProbs];
 };
@@ -388,7 +405,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
-    const bool withhold = g_mv8_withhold != 0;
+    const bool withhold = g_mv8_withhold == 1;
     if (smem_addr(sm) & 127u) return;  // a tiled copy's destination is 128-byte aligned (the launch gives that)
     const int team = L.team, teams = kM8Warps / team;
     const int tid_team = warp / team, kq = warp % team;
@@ -397,13 +414,29 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     const int my_jobs = q0 < L.jobs ? min((L.jobs - q0 + nteams - 1) / nteams, kM8MaxWarpJobs) : 0;
     uint8_t* my_ring = ring + size_t(warp) * ns * slot_bytes;
     uint64_t* my_bars = bars + warp * kM8MaxSlots;
+    // the route's scratch (has_route): partial sums [2 rows][4 quarters][tokens], the launch number as read at
+    // the start, whether this CTA arrived last
+    float* rpart = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xsplit) + L.xbytes);
+    uint32_t* rseq = reinterpret_cast<uint32_t*>(rpart + 2 * 4 * kRtTokens);
+    uint32_t* rlast = rseq + 1;
 
-    // barriers and the codebook are set up while the kernel before this one finishes
+    // barriers and the codebook are set up while the kernel before this one finishes; the route CTAs' warps
+    // 0..7 load their router rows' first chunks (weights: no kernel writes them)
     if (lane == 0) {
         for (int i = 0; i < ns; ++i) tc::mbar_init(&my_bars[i], 1);
         tc::fence_barrier_init();
     }
     for (int i = threadIdx.x; i < kM8MaxRows / 32; i += kM8Threads) need[i] = 0u;
+    const M8Route& R = L.r;
+    const int64_t rrows = L.has_route ? R.experts + (R.gw != nullptr ? 1 : 0) : 0;
+    const int64_t rrow = int64_t(blockIdx.x) * 2 + (warp >> 2);
+    const bool rt_warp = L.has_route && warp < 8;
+    const bool rt_live = rt_warp && rrow < rrows;
+    const __half* rrow_ptr = rrow < R.experts ? R.w + rrow * R.hidden : R.gw;
+    float rwv[4][8];
+    if (rt_live) router_first(rrow_ptr, true, R.hidden, rwv);
+    // (read before this CTA arrives below, so before the launch's last CTA moves it on)
+    if (L.has_route && threadIdx.x == 0) *rseq = ld_relaxed_u32(R.counters + 1);
     if (L.lut) m8_fill_grid(lut);
 
     // lane l's job: problem, pair, tile (residue class and block), activation row; then its expert and the
@@ -426,7 +459,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     auto place = [&](bool now) {  // the expert of lane l's job, for the jobs whose indices may be read now
         if (has && now) {
             const M8Prob& P = L.p[j_prob];
-            const uint32_t e = __ldg(P.idx + j_pair);
+            const uint32_t e = P.wait ? __ldcg(P.idx + j_pair) : __ldg(P.idx + j_pair);
             j_valid = e < P.experts ? 1 : 0;
             j_y = static_cast<int>((int64_t(j_valid ? e : 0) * P.rows) >> P.lq) + 16 * j_blk;
         }
@@ -461,13 +494,14 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
         }
     };
     // issue the cursor's item (a pair naming no expert copies nothing and completes the slot's phase with a
-    // plain arrive, so every item takes one phase) and move on
+    // plain arrive, so every item takes one phase) and move on; the weights are read once: evict-first in L2
+    const uint64_t stream_policy = tc::policy_evict_first();
     auto issue = [&]() {
         if (lane == 0 && !(withhold && issued == 0)) {
             if (i_valid) {
                 tc::mbar_arrive_expect_tx(&my_bars[i_slot], static_cast<uint32_t>(i_bytes));
-                tc::tma_load_2d(smem_addr(my_ring + i_slot * slot_bytes), &maps.w[i_map], (i_pos & ~15) >> 2, i_y,
-                                &my_bars[i_slot]);
+                tc::tma_load_2d_hint(smem_addr(my_ring + i_slot * slot_bytes), &maps.w[i_map], (i_pos & ~15) >> 2,
+                                     i_y, &my_bars[i_slot], stream_policy);
             } else {
                 tc::mbar_arrive(&my_bars[i_slot]);
             }
@@ -499,11 +533,65 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     };
     split(true);
     pdl_wait();
-    place(has && !L.p[j_prob].early);
-    if (i_job < my_jobs && !L.p[i_map].early) seek(i_job);  // (re-read the place: its expert is known now)
+    // the route: a route CTA's two router rows (four warps to a row, as smoe_route computes them) into the
+    // logits; then every CTA arrives (thread 0), and the last one in takes the top-k below
+    if (rt_warp) {
+        if (blockIdx.x < L.route_ctas) {
+            float acc[kRtTokens];
+            router_rows(rrow_ptr, rt_live, R.x, R.hidden, 0, R.tokens, acc, rwv);
+#pragma unroll
+            for (int t = 0; t < kRtTokens; ++t) acc[t] = warp_sum(acc[t]);
+            if (lane == 0) {
+#pragma unroll
+                for (int t = 0; t < kRtTokens; ++t) rpart[((warp >> 2) * 4 + (warp & 3)) * kRtTokens + t] = acc[t];
+            }
+            route_sync();
+            if (threadIdx.x < 2 * kRtTokens) {
+                const int r = threadIdx.x / kRtTokens, t = threadIdx.x % kRtTokens;
+                const int64_t er = int64_t(blockIdx.x) * 2 + r;
+                if (er < rrows && t < R.tokens) {
+                    float sum = rpart[(r * 4 + 0) * kRtTokens + t];
+                    sum += rpart[(r * 4 + 1) * kRtTokens + t];
+                    sum += rpart[(r * 4 + 2) * kRtTokens + t];
+                    sum += rpart[(r * 4 + 3) * kRtTokens + t];
+                    if (er < R.experts) R.logits[int64_t(t) * R.experts + er] = sum;
+                    else R.gate_out[t] = __float2half_rn(sum);
+                }
+            }
+        }
+        __threadfence();
+        route_sync();
+        if (threadIdx.x == 0) *rlast = atomicAdd(R.counters, 1u) == gridDim.x - 1 ? 1u : 0u;
+        route_sync();
+    }
+    place(has && !L.p[j_prob].early && !L.p[j_prob].wait);
+    if (i_job < my_jobs && !L.p[i_map].early && !L.p[i_map].wait) seek(i_job);  // (its expert is known now)
     split(false);
     __syncthreads();
-    while (i_job < my_jobs && issued < ns - 1) issue();
+    while (i_job < my_jobs && issued < ns - 1 && (!L.has_route || !L.p[i_map].wait)) issue();
+    // the last CTA in: one warp a token takes its top-k and softmax over the logits all CTAs wrote, then the
+    // launch number moves on (release: idx, weights, lidx and gate_out are written)
+    const uint32_t seq0 = L.has_route ? *rseq : 0u;
+    if (rt_warp && *rlast && warp < R.tokens) {
+        __threadfence();
+        const float* in = R.logits + int64_t(warp) * R.experts;
+        topk_row<8>([&](int j) { return __ldcg(in + j); }, R.experts, R.k, R.idx + int64_t(warp) * R.k,
+                    R.weights + int64_t(warp) * R.k);
+        if (R.lidx != nullptr) {
+            __syncwarp();
+            for (int j = lane; j < R.k; j += 32) {
+                const uint32_t e = R.idx[int64_t(warp) * R.k + j] - R.lo;
+                R.lidx[int64_t(warp) * R.k + j] = e < R.count ? e : R.count;
+            }
+        }
+        __threadfence();
+        asm volatile("bar.sync 14, %0;" ::"r"(32 * R.tokens) : "memory");
+        if (threadIdx.x == 0) {
+            R.counters[0] = 0u;
+            __threadfence();
+            if (g_mv8_withhold != 2) st_release_u32(R.counters + 1, seq0 + 1u);  // (2: a test withholds it)
+        }
+    }
 
     // a team of one warp needs no named barrier (there are 16, barrier 0 is __syncthreads')
     auto team_sync = [&]() {
@@ -517,13 +605,47 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
     float total[2] = {0.f, 0.f};
     int slot = 0, waited = 0;
     uint32_t phase = 0;
+    // the route's indices: the copy cursor stops at the first job of a problem that reads them until the
+    // launch number has moved on (lane 0 reads it a stage ahead of looking at it, and waits for it, bounded,
+    // only when the item the warp is to decode next has not been issued)
+    bool rdy = !L.has_route;
+    uint32_t fpoll = seq0;
+    int consumed = 0;
+    auto route_in = [&]() {  // the number has moved: the routed jobs' places, the cursor's (at a job's start)
+        fence_acq_rel_gpu();
+        place(has && L.p[j_prob].wait);
+        if (i_job < my_jobs) seek(i_job);
+        rdy = true;
+    };
+    auto route_wait = [&]() -> bool {
+        bool got = true;
+        if (lane == 0) {
+            uint32_t v = fpoll;
+            if (v == seq0) {
+                const uint64_t t0 = tc::globaltimer_ns();
+                for (uint32_t i = 0;; ++i) {
+                    v = ld_relaxed_u32(R.counters + 1);
+                    if (v != seq0) break;
+                    if (i >= polls || tc::globaltimer_ns() - t0 > tc::kWaitNs) {
+                        got = false;
+                        break;
+                    }
+                }
+            }
+            fpoll = v;
+        }
+        got = __shfl_sync(0xffffffffu, got ? 1 : 0, 0) != 0;
+        if (got) route_in();
+        else mv8_gave_up(lane);
+        return got;
+    };
     for (int job = 0; job < my_jobs; ++job) {
         const int pr = __shfl_sync(0xffffffffu, j_prob, job);
         const int pair = __shfl_sync(0xffffffffu, j_pair, job);
         const int cls = __shfl_sync(0xffffffffu, j_cls, job);
         const int blk = __shfl_sync(0xffffffffu, j_blk, job);
         const int xr = __shfl_sync(0xffffffffu, j_xr, job);
-        const int valid = __shfl_sync(0xffffffffu, j_valid, job);
+        int valid = __shfl_sync(0xffffffffu, j_valid, job);
         const M8Prob& P = L.p[pr];
         const M8X& X = L.x[P.xs];
         const int lx = xr - X.row0;
@@ -539,7 +661,17 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
         for (int k = 0; k < n; ++k, pos += step, xc += xstep) {
             // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
             __syncwarp();
-            if (ok && i_job < my_jobs) issue();  // (after a wait gave up, nothing more is copied)
+            if (!rdy && ok && i_job < my_jobs && L.p[i_map].wait) {
+                if (__shfl_sync(0xffffffffu, fpoll != seq0 ? 1 : 0, 0)) route_in();
+                else if (lane == 0) fpoll = ld_relaxed_u32(R.counters + 1);
+            }
+            if (ok && i_job < my_jobs && (rdy || !L.p[i_map].wait)) issue();  // (after a wait gave up, nothing)
+            if (ok && issued == consumed) {  // this item waits for the route
+                ok = route_wait();
+                if (ok) issue();
+            }
+            if (!rdy || k == 0) valid = __shfl_sync(0xffffffffu, j_valid, job);  // (placed once the route is in)
+            ++consumed;
             const int cur = slot;
             if (ok) {
                 ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cur], phase, polls));
@@ -587,7 +719,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
             const int64_t s0 = (int64_t(blockIdx.x) * eb / gridDim.x) & ~int64_t(15);
             const int64_t s1 = (int64_t(blockIdx.x + 1) * eb / gridDim.x) & ~int64_t(15);
             for (int i = lane; i < Pf.pairs; i += 32) {
-                const uint32_t e = __ldg(Pf.idx + i);
+                const uint32_t e = __ldcg(Pf.idx + i);  // (the launch's own route may have written it)
                 if (e >= Pf.experts) continue;
                 const uint8_t* base = Pf.blocks + int64_t(e) * eb;
                 for (int64_t o = s0; o < s1; o += 65536)
@@ -758,15 +890,38 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
 
 // Launch several matvec problems as one int8 tensor-core kernel: 0 launched, 1 not taken (the caller runs
 // them another way), else an error status. Problems with the same activation pointers share one source.
-int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st, int npf, const M8Pref* pf) {
+int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st, int npf, const M8Pref* pf, const M8Route* route) {
     if (n < 1 || n > kM8MaxProbs || npf < 0 || npf > kM8MaxPref) return 1;
-    // the problems in order of falling cost per job (bytes of a 16-row tile), so that the round-robin of jobs
-    // over teams hands the big jobs out first
+    // with the route in this launch, a problem whose indices lie in its idx or lidx reads them once the route
+    // is in: such problems go after the others (their jobs come last in every warp's list)
+    auto overlaps = [](const uint32_t* a, int64_t na, const uint32_t* b, int64_t nb) {
+        return b != nullptr && a < b + nb && b < a + na;
+    };
+    auto waits = [&](const M8Spec& sp) {
+        if (route == nullptr) return false;
+        const int64_t nk = int64_t(route->tokens) * route->k;
+        return overlaps(sp.idx, sp.pairs, route->idx, nk) || overlaps(sp.idx, sp.pairs, route->lidx, nk);
+    };
+    // then in order of falling cost per job (bytes of a 16-row tile), so that the round-robin of jobs over
+    // teams hands the big jobs out first
     M8Spec specs[kM8MaxProbs];
     for (int i = 0; i < n; ++i) specs[i] = specs_in[i];
     auto job_bytes = [](const M8Spec& sp) { return sp.row_bytes * 16; };
+    auto before = [&](const M8Spec& a, const M8Spec& b) {
+        return waits(a) != waits(b) ? !waits(a) : job_bytes(a) > job_bytes(b);
+    };
     for (int i = 1; i < n; ++i)
-        for (int j = i; j > 0 && job_bytes(specs[j]) > job_bytes(specs[j - 1]); --j) std::swap(specs[j], specs[j - 1]);
+        for (int j = i; j > 0 && before(specs[j], specs[j - 1]); --j) std::swap(specs[j], specs[j - 1]);
+    if (route != nullptr) {
+        const int64_t rows = int64_t(route->experts) + (route->gw != nullptr ? 1 : 0);
+        if (route->tokens < 1 || route->tokens > kRtTokens || route->experts < 1 || route->experts > 256 ||
+            route->k < 1 || route->k > std::min(route->experts, 32) || route->hidden < 8 || route->hidden % 8 ||
+            !route->w || !route->x || !route->logits || !route->idx || !route->weights || !route->counters ||
+            (reinterpret_cast<uintptr_t>(route->w) & 15) || (reinterpret_cast<uintptr_t>(route->gw) & 15) ||
+            (reinterpret_cast<uintptr_t>(route->x) & 15) || (route->gw != nullptr) != (route->gate_out != nullptr) ||
+            rows > 2 * 148)
+            return 1;
+    }
     M8EncodeFn encode = m8_encoder();
     if (!encode) return 1;
     M8Launch L{};
@@ -839,7 +994,8 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st, int npf, const M8P
         P.pairs = static_cast<int>(sp.pairs);
         P.share = static_cast<int>(sp.share);
         P.xs = xs;
-        P.early = pdl_early(st, sp.idx, size_t(sp.pairs) * 4) ? 1 : 0;
+        P.wait = waits(sp) ? 1 : 0;
+        P.early = !P.wait && pdl_early(st, sp.idx, size_t(sp.pairs) * 4) ? 1 : 0;
         P.job0 = jobs;
         const int64_t pj = int64_t(P.pairs) * P.tiles;
         if (pj + jobs > (int64_t(1) << 30)) return 1;
@@ -869,7 +1025,8 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st, int npf, const M8P
     L.lut = lut ? 1 : 0;
     L.slot_bytes = 16 * max_rs;
     const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 16 * 4 + kM8MaxRows / 8 +
-                         (lut ? 8192 * 4 : 0) + size_t((scales + 3) & ~3) * 4 + size_t(xbytes);
+                         (lut ? 8192 * 4 : 0) + size_t((scales + 3) & ~3) * 4 + size_t(xbytes) +
+                         (route ? kM8RouteBytes : 0);
     const size_t slot = size_t(kM8Warps) * L.slot_bytes;
     int ns = kM8MaxSlots;
     while (ns > 2 && fixed + ns * slot > size_t(227 * 1024)) --ns;
@@ -910,8 +1067,20 @@ int mv8_batch(int n, const M8Spec* specs_in, cudaStream_t st, int npf, const M8P
     const unsigned grid = static_cast<unsigned>(std::max<int64_t>(1, G));
     const size_t smem = fixed + ns * slot;
     if (int s = max_smem(mv8_kernel, static_cast<int>(smem))) return fail(s, "matvec: shared memory limit");
+    if (route != nullptr) {
+        // a CTA for every two router rows, all in the grid (one CTA an SM: all are running at once)
+        L.has_route = 1;
+        L.r = *route;
+        L.route_ctas = (route->experts + (route->gw != nullptr ? 1 : 0) + 1) / 2;
+        if (L.route_ctas > static_cast<int>(grid)) return 1;
+    }
     Writes wr;
     for (int i = 0; i < n; ++i) wr.add(L.p[i].out, size_t(L.p[i].pairs) * L.p[i].rows * sizeof(__half));
+    if (route != nullptr) {
+        const size_t tk = size_t(route->tokens) * route->k * 4;
+        wr.add(route->logits, size_t(route->tokens) * route->experts * 4).add(route->idx, tk).add(route->weights, tk);
+        wr.add(route->gate_out, size_t(route->tokens) * sizeof(__half)).add(route->counters, 8).add(route->lidx, tk);
+    }
     launch_pdl(wr, mv8_kernel, dim3(grid), dim3(kM8Threads), smem, st, L, maps);
     return launch_status("matvec (int8 tensor cores)");
 }
@@ -974,7 +1143,7 @@ extern "C" int smoe_matvec_status(int* status, int clear) {
 
 extern "C" int smoe_matvec_wait_test(int64_t polls, int withhold) {
     const uint32_t v = polls < 0 ? kM8WaitLimit : static_cast<uint32_t>(std::min<int64_t>(polls, kM8WaitLimit));
-    const int w = withhold ? 1 : 0;
+    const int w = withhold == 2 ? 2 : withhold ? 1 : 0;
     cudaError_t e = cudaDeviceSynchronize();
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_mv8_polls, &v, sizeof(v));
     if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_mv8_withhold, &w, sizeof(w));

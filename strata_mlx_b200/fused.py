@@ -86,6 +86,7 @@ def top_k_softmax(logits: torch.Tensor, k: int):
 
 _COUNTERS = {}
 
+FUSED_ROUTE = False  # decode: the route in the gate / up launch (smoe_route_matvec_batch; measured slower)
 LAYER_KERNEL = False  # one launch per one-token step (smoe_decode_layer) where the types and shapes allow it
 _LAYER_SCRATCH = {}
 
@@ -148,12 +149,16 @@ def decode_layer_failed(x: torch.Tensor, block: "SparseMoeBlock") -> bool:
     return flag.value != 0
 
 
-def route(gate: "WindowLinear", shared_gate, x: torch.Tensor, k: int, local=None):
+def route(gate: "WindowLinear", shared_gate, x: torch.Tensor, k: int, local=None, defer: bool = False):
     """The start of the MoE block in one launch: (idx, w, g) = (top_k_softmax(gate(x), k),
     shared_gate(x).to(x.dtype)) with the same sums and choice as those calls (strata_mlx/fused.py:487-491).
     shared_gate: a WindowLinear of one row, or None (g is then None). With `local` = (lo, count), an expert-
     parallel rank's experts, a fourth result lidx: idx - lo for those experts, `count` for the others, from the
-    same launch. None where the kernel does not take x."""
+    same launch. None where the kernel does not take x.
+
+    With `defer`, nothing is launched yet: the result gains a last item, the route's `SmoeRouteStep`, which
+    either the products that read its choice take into their own launch (`decode_products(route_step=...)`)
+    or `launch_route` launches alone; the outputs are written by that launch."""
     if not gate.takes(x) or gate.rows > 2048 or not 1 <= k <= min(gate.rows, 32):
         return None
     if shared_gate is not None and (not shared_gate.takes(x) or shared_gate.rows != 1 or shared_gate.cols != gate.cols):
@@ -166,12 +171,24 @@ def route(gate: "WindowLinear", shared_gate, x: torch.Tensor, k: int, local=None
     idx = torch.empty((tokens, k), dtype=torch.uint32, device=dev)
     w = torch.empty((tokens, k), dtype=torch.float32, device=dev)
     g = torch.empty((tokens,), dtype=x.dtype, device=dev) if shared_gate is not None else None
-    nbytes = int(_lib.lib().smoe_route_counters(tokens))
-    key = (str(dev), nbytes)
+    nbytes = int(_lib.lib().smoe_route_step_counters(tokens) if defer else _lib.lib().smoe_route_counters(tokens))
+    key = (str(dev), nbytes, defer)
     counters = _COUNTERS.get(key)
     if counters is None:
         counters = _COUNTERS[key] = torch.zeros(nbytes // 4, dtype=torch.int32, device=dev)
     lidx = torch.empty((tokens, k), dtype=torch.uint32, device=dev) if local is not None else None
+    lead = x.shape[:-1]
+    if defer:
+        wt = gate.weight.contiguous()
+        gw = shared_gate.weight.contiguous() if shared_gate is not None else None
+        step = _lib.SmoeRouteStep(_lib.ptr(wt), _lib.ptr(gw) if gw is not None else None, _lib.ptr(x2),
+                                  _lib.dtype_code(x.dtype), tokens, gate.rows, gate.cols, k, _lib.ptr(logits),
+                                  _lib.ptr(idx), _lib.ptr(w), _lib.ptr(g) if g is not None else None,
+                                  _lib.ptr(counters), local[0] if local is not None else 0,
+                                  local[1] if local is not None else 0, _lib.ptr(lidx) if lidx is not None else None)
+        step._keep = (wt, gw, x2, logits, idx, w, g, counters, lidx)  # (the tensors the pointers name)
+        out = (idx.reshape(*lead, k), w.reshape(*lead, k), g.reshape(*lead, 1) if g is not None else None)
+        return (out if local is None else out + (lidx.reshape(*lead, k),)) + (step,)
     if tokens:
         common = (_lib.ptr(gate.weight.contiguous()),
                   _lib.ptr(shared_gate.weight.contiguous()) if shared_gate is not None else None, _lib.ptr(x2),
@@ -181,9 +198,14 @@ def route(gate: "WindowLinear", shared_gate, x: torch.Tensor, k: int, local=None
             _lib.call("smoe_route", *common, _lib.stream())
         else:
             _lib.call("smoe_route_local", *common, local[0], local[1], _lib.ptr(lidx), _lib.stream())
-    lead = x.shape[:-1]
     out = (idx.reshape(*lead, k), w.reshape(*lead, k), g.reshape(*lead, 1) if g is not None else None)
     return out if local is None else out + (lidx.reshape(*lead, k),)
+
+
+def launch_route(step) -> None:
+    """Launch a deferred route (`route(..., defer=True)`) by itself."""
+    if step.tokens:
+        _lib.call("smoe_route_matvec_batch", ctypes.byref(step), 0, None, _lib.stream())
 
 
 def moe_combine(y: torch.Tensor, w: torch.Tensor, g: torch.Tensor, s: torch.Tensor):
@@ -224,8 +246,12 @@ class SparseMoeBlock:
         out = decode_layer(self, x)
         if out is not None:
             return out
-        r = route(self.gate, self.shared_expert_gate, x, self.top_k)
-        if r is not None:
+        # the route goes into the gate / up launch of the decode products where they take it (FUSED_ROUTE)
+        r = route(self.gate, self.shared_expert_gate, x, self.top_k, defer=FUSED_ROUTE)
+        step = None
+        if r is not None and FUSED_ROUTE:
+            idx, w, g, step = r
+        elif r is not None:
             idx, w, g = r
         else:
             logits = self.gate(x)
@@ -233,7 +259,9 @@ class SparseMoeBlock:
             g = self.shared_expert_gate(x).to(x.dtype)
         ys = None
         if isinstance(self.switch_mlp, BlockSwitchGLU) and isinstance(self.shared_expert, BlockMLP):
-            ys = decode_products(self.switch_mlp, self.shared_expert, x, idx, w, g)
+            ys = decode_products(self.switch_mlp, self.shared_expert, x, idx, w, g, route_step=step)
+        if ys is None and step is not None:
+            launch_route(step)
         if ys is not None and ys[0] is None:
             return ys[1]  # the shared expert's down product formed the combine
         y, s = ys if ys is not None else (self.switch_mlp(x, idx), self.shared_expert(x))

@@ -29,7 +29,8 @@ import torch.distributed as dist
 from . import _lib
 from .blocks import (BlockLinear, BlockMLP, BlockSwitchGLU, BlockSwitchLinear, decode_products, gate_up, matvec_glu,
                      row_bytes)
-from .fused import SparseMoeBlock, WindowLinear, route, top_k_softmax
+from . import fused as _fused
+from .fused import SparseMoeBlock, WindowLinear, launch_route, route, top_k_softmax
 
 
 def expert_range(rank: int, world: int, experts: int):
@@ -171,9 +172,10 @@ class ExpertParallelMoE:
     its slice of the shared expert. Returns the whole block's output on every rank.
 
     With a `PeerExchange`, a decode step of float16 tokens is four launches overlapped by programmatic
-    dependent launch: `smoe_route_local` (router, top-k, softmax, shared gate and this rank's view of the
-    choice), the routed and shared gate / up products in one launch, both down products in one launch, and
-    `smoe_ep_reduce_combine` (the exchange of the partial sums over peer memory with the combine). Without one (or for other activations),
+    dependent launch: the route (router, top-k, softmax, shared gate and this rank's view of the choice), the
+    routed and shared gate / up products in one launch (with `fused.FUSED_ROUTE`, the route goes into that
+    launch: `smoe_route_matvec_batch`), both down products in one launch, and `smoe_ep_reduce_combine` (the
+    exchange of the partial sums over peer memory with the combine). Without one (or for other activations),
     the partial sums go through one all-reduce of the process group."""
 
     def __init__(self, layer: SparseMoeBlock, rank: int, world: int, experts: int, group=None,
@@ -198,14 +200,20 @@ class ExpertParallelMoE:
                 or x2.dtype not in (torch.float16, torch.float32)):
             return None
         k = layer.top_k
-        r = route(layer.gate, layer.shared_expert_gate, x2, k, local=(self.lo, self.count))
+        r = route(layer.gate, layer.shared_expert_gate, x2, k, local=(self.lo, self.count), defer=True)
         if r is None:
             return None
-        idx, w, g, lidx = r
+        idx, w, g, lidx, step = r
+        if not _fused.FUSED_ROUTE:
+            launch_route(step)
+            step = None
         sw, sh = layer.switch_mlp, layer.shared_expert
         ys = None
         if isinstance(sw, BlockSwitchGLU) and isinstance(sh, BlockMLP):
-            ys = decode_products(sw, sh, x2, lidx, batched_down=True)
+            # the route in the gate / up launch
+            ys = decode_products(sw, sh, x2, lidx, batched_down=True, route_step=step)
+        if ys is None and step is not None:
+            launch_route(step)
         if ys is None or ys[0] is None:
             ys = (sw(x2, lidx), sh(x2))
         y, s = ys
