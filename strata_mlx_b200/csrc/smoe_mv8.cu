@@ -465,7 +465,8 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8_kernel(const __grid_constan
         }
     };
     place(has && L.p[j_prob].early);
-    if (has) atomicOr(&need[j_xr >> 5], 1u << (j_xr & 31));
+    // the activation rows this CTA's jobs read (not those of pairs already known to name no expert)
+    if (has && (!L.p[j_prob].early || j_valid)) atomicOr(&need[j_xr >> 5], 1u << (j_xr & 31));
     __syncthreads();
 
     // the copy cursor (warp-uniform): the next item's job, its stage index k of n, slot, byte position in the
