@@ -394,8 +394,10 @@ SMOE_API int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts, 
  * zero before the first call and then left to the library (the launches count their grid barriers in it);
  * calls sharing a scratch must not overlap on the GPU. One CTA per SM, all resident together (a cooperative
  * launch); every wait on another CTA gives up after a second, leaving a flag that
- * smoe_decode_layer_status() reads (1: some wait gave up, the outputs are not valid). No single reference
- * counterpart: it fuses the four calls above. */
+ * smoe_decode_layer_status() reads (1: some wait gave up, the outputs are not valid). After a wait gave up the
+ * scratch's barrier count is off: zero the scratch again before the next call. smoe_decode_layer_wait_test(1)
+ * (for tests; it synchronizes the device) has one CTA skip its first arrival, so that the waits run out;
+ * smoe_decode_layer_wait_test(0) restores it. No single reference counterpart: it fuses the four calls above. */
 typedef struct SmoeDecodeLayer {
     const uint16_t* router;      /* [experts][hidden] float16 */
     const uint16_t* shared_gate; /* [hidden] float16, the shared expert's gate row */
@@ -417,6 +419,7 @@ SMOE_API size_t smoe_decode_layer_scratch(int64_t hidden, int64_t k, int64_t ffn
 SMOE_API int smoe_decode_layer(const SmoeDecodeLayer* layer, const void* x, void* stream);
 SMOE_API int smoe_decode_layer_status(const void* scratch, int64_t hidden, int64_t k, int64_t ffn, int64_t sffn,
                                       int* failed);
+SMOE_API int smoe_decode_layer_wait_test(int withhold);
 
 #ifdef __cplusplus
 }

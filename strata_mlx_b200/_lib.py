@@ -76,6 +76,7 @@ SIGNATURES = {
     "smoe_decode_layer_scratch": (_sz, [_i64, _i64, _i64, _i64]),
     "smoe_decode_layer": (_i, [_c.POINTER(SmoeDecodeLayer), _p, _p]),
     "smoe_decode_layer_status": (_i, [_p, _i64, _i64, _i64, _i64, _c.POINTER(_i)]),
+    "smoe_decode_layer_wait_test": (_i, [_i]),
     "smoe_swiglu": (_i, [_p, _p, _i64, _p, _i, _p]),
     "smoe_router_logits": (_i, [_p, _p, _i, _i64, _i64, _i64, _p, _p]),
     "smoe_top_k": (_i, [_p, _i64, _i64, _i64, _p, _p, _p]),
@@ -119,7 +120,7 @@ _lib = None
 # kernels each entry point launches (for the benchmark's launch count); 1 where not named
 KERNELS_PER_CALL = {"smoe_tiles_of": 2, "smoe_tiles_of_noalloc": 2, "smoe_tile_matmul": 2, "smoe_ep_dispatch": 2,
                     "smoe_ep_exchange_alloc": 0, "smoe_ep_exchange_open": 0, "smoe_ep_exchange_close": 0,
-                    "smoe_ep_exchange_free": 0, "smoe_ep_exchange_status": 0, "smoe_decode_layer_status": 0,
+                    "smoe_ep_exchange_free": 0, "smoe_ep_exchange_status": 0, "smoe_decode_layer_status": 0, "smoe_decode_layer_wait_test": 0,
                     "smoe_matvec_status": 0, "smoe_matvec_wait_test": 0, "smoe_hyper_connection": 3}
 launches = 0
 

@@ -79,11 +79,16 @@ __device__ __forceinline__ unsigned long long ld_acquire(const unsigned long lon
 
 // Every CTA arrives, then waits (thread 0, bounded) until all G have: `target` arrivals in all. Returns false
 // when the wait gave up (the error flag is then set).
-__device__ __forceinline__ bool grid_sync(unsigned long long* bar, unsigned long long target, int* err, int* flag) {
+// A test hook (smoe_decode_layer_wait_test): CTA 0 does not arrive at the first barrier, so every wait there runs
+// out (bounded) and the launch reports it.
+static __device__ int g_ly_withhold = 0;
+
+__device__ __forceinline__ bool grid_sync(unsigned long long* bar, unsigned long long target, int* err, int* flag,
+                                          bool arrive = true) {
     __syncthreads();
     if (threadIdx.x == 0) {
         __threadfence();
-        atomicAdd(bar, 1ull);
+        if (arrive) atomicAdd(bar, 1ull);
         bool ok = true;
         if (ld_acquire(bar) < target) {
             const uint64_t t0 = tc::globaltimer_ns();
@@ -357,7 +362,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
         }
     }
     const unsigned long long base = base_s;
-    bool ok = grid_sync(A.bar, base + G, A.err, flag);
+    bool ok = grid_sync(A.bar, base + G, A.err, flag, !(g_ly_withhold && b == 0));
 
     // ---- C: the top-k of the logits, in every CTA
     if (warp == 0) {
@@ -373,14 +378,14 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
     if (lane < ja_e) ye = place(ER, me, sidx[(me >> 7) & 63], me);
     else if (lane < ja_e + jb_e) ye = place(ES, me, 0u, me);
     placed = true;
-    while (issued < ns - 1 && cursor_ready()) issue();
+    while (ok && issued < ns - 1 && cursor_ready()) issue();  // (nothing more after a wait gave up)
 
     // ---- D and E: this warp's units. A warp adds up each job's units it has (two jobs open at a time: one
     // of each kind); its partial sums then go to the job's slot, and the warp whose units complete the job adds
     // the 16 warps' slots in warp order (zero where a warp had none) and writes the 16 rows.
     float tot[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
     int open_job[2] = {-1, -1}, open_units[2] = {0, 0};
-    int slot = 0, consumed = 0;
+    int slot = 0, waited = 0;
     uint32_t phase = 0;
     auto flush = [&](int P, int kind) {
         const int job = open_job[kind];
@@ -430,10 +435,12 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
             ++open_units[u.kind];
             // keep ns - 1 copies ahead; the slot refilled is the one this warp finished last
             __syncwarp();
-            if (cursor_ready()) issue();
+            if (ok && cursor_ready()) issue();  // (after a wait gave up, nothing more is copied)
             const int cs = slot;
-            if (ok) ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cs], phase, kM8WaitLimit));
-            ++consumed;
+            if (ok) {
+                ok = __all_sync(0xffffffffu, tc::mbar_wait(&my_bars[cs], phase, kM8WaitLimit));
+                if (ok) ++waited;
+            }
             if (++slot == ns) {
                 slot = 0;
                 phase ^= 1;
@@ -495,10 +502,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) decode_layer_kernel(const __gri
             A.out[r] = combine_one(yv, 1, sw, K, g, sv);
         }
     }
-    // no copy may still be writing this CTA's shared memory when it exits (every item was waited for, unless
-    // a wait gave up)
+    // no copy may still be writing this CTA's shared memory when it exits: every item was waited for, unless a
+    // wait gave up; then the items issued after the last one waited for are waited for here (no item was issued
+    // after the wait gave up)
     if (!ok && lane == 0)
-        for (int i = consumed; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, 1u << 12);
+        for (int i = waited; i < issued; ++i) tc::mbar_wait(&my_bars[i % ns], (i / ns) & 1, kM8WaitLimit);
     __syncwarp();
 }
 
@@ -668,6 +676,14 @@ extern "C" int smoe_decode_layer(const SmoeDecodeLayer* L, const void* x, void* 
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, decode_layer_kernel, A, maps);
     return launch_status("decode_layer");
+}
+
+extern "C" int smoe_decode_layer_wait_test(int withhold) {
+    const int w = withhold ? 1 : 0;
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_ly_withhold, &w, sizeof(w));
+    if (e != cudaSuccess) return fail(-static_cast<int>(e), std::string("decode_layer_wait_test: ") + cudaGetErrorString(e));
+    return SMOE_OK;
 }
 
 extern "C" int smoe_decode_layer_status(const void* scratch, int64_t hidden, int64_t k, int64_t ffn, int64_t sffn,

@@ -117,3 +117,32 @@ def test_the_one_launch_step_at_baseline_shapes_is_the_oracles(cuda):
     logits = block.gate(dev(x)).cpu().numpy()
     want, idx, w, _ = M.moe_block(x, router, k, routed, shared, sgate, logits=logits)
     assert rel_l2(got, want) <= 1e-3
+
+
+def test_a_grid_barrier_that_never_fills_is_a_status_the_host_reads(cuda, monkeypatch):
+    """With one CTA's first arrival withheld (a test hook), every wait at the first grid barrier runs out after
+    about a second and the later barriers' waits too: the step's status reads 1, nothing more is copied, the
+    copies in flight land, and the device stays usable. With the scratch zeroed again (its barrier count is off
+    after a wait gave up) the next step is the four launches' again and its status is clear. No fault, no trap."""
+    from strata_mlx_b200 import _lib
+
+    rng = np.random.default_rng(44)
+    E, H, F_, Fs, k = 64, 1024, 512, 512, 8
+    routed, shared, router, sgate = make_layer(rng, H, F_, E, Fs, ("IQ3_S",) * 3, "Q8_0")
+    block = build_block(routed, shared, router, sgate, k)
+    x = dev(rng.standard_normal((1, H)).astype(np.float16))
+    block(x)
+    assert not F.decode_layer_failed(x, block)
+    lib = _lib.lib()
+    try:
+        assert lib.smoe_decode_layer_wait_test(1) == 0
+        block(x)
+        torch.cuda.synchronize()
+        assert F.decode_layer_failed(x, block)
+    finally:
+        assert lib.smoe_decode_layer_wait_test(0) == 0
+    F._LAYER_SCRATCH[(str(x.device), H, k, F_, Fs)].zero_()
+    got = block(x)
+    want, _, _, _ = four_launches(block, x, monkeypatch)
+    assert rel_l2(got.float().cpu().numpy(), want.float().cpu().numpy()) <= 1e-3
+    assert not F.decode_layer_failed(x, block)
