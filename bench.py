@@ -59,7 +59,7 @@ def _args():
     p.add_argument("--only-stack", action="store_true", help="only the config-5 stack measurement")
     p.add_argument("--stack-layers", type=int, default=26)
     p.add_argument("--only-verify", action="store_true", help="only the config-4 verify-pass measurement")
-    p.add_argument("--only-matvec", metavar="KIND", help="profiling: the CUDA-core matvec of config 4's down "
+    p.add_argument("--only-matvec", metavar="KIND", help="profiling: the decode matvec of config 4's down "
                    "product (40 pairs of 5 tokens, 64 experts of 4096 x 1536 KIND blocks), a few launches")
     return p.parse_args()
 
@@ -613,9 +613,9 @@ def run_stack(args, rank, world, local_rank, prompt=32768, chunk=2048, decode_st
 
 
 def run_matvec(kind, seed, steps=3, warmup=3, experts=64, tokens=5):
-    """One product of config 4's shape on the CUDA-core decode matvec (a type the tensor-core kernels do not
-    take): `tokens` x top-8 pairs through a stack of `experts` (4096 x 1536) of `kind`, 283 MB for Q5_K (more
-    than L2), small enough for a profiler's replays."""
+    """One product of config 4's shape on the decode matvec the type takes: `tokens` x top-8 pairs through a
+    stack of `experts` (4096 x 1536) of `kind`, 283 MB for Q5_K (more than L2), small enough for a profiler's
+    replays."""
     import torch
 
     from strata_mlx_b200 import blocks as B
