@@ -320,9 +320,11 @@ struct M8IQ3XXS {
 };
 
 // ---------------------------------------------------------------- Q8_0
-// (34 bytes: d 0, qs 2..33.) A stage is four runs; in run r lane tig takes codes 8 tig .. 8 tig + 7.
-struct M8Q8_0 {
-    static constexpr int kKind = 8, kStageCols = 128, kStageBytes = 136, kRS = 176;
+// (34 bytes: d 0, qs 2..33.) A stage is NB runs (blocks); in run r lane tig takes codes 8 tig .. 8 tig + 7. Eight
+// blocks a stage (256 columns: one activation scale block), so a warp's loop turns half as often as with four.
+template <int NB>
+struct M8Q8_0N {
+    static constexpr int kKind = 8, kStageCols = 32 * NB, kStageBytes = 34 * NB, kRS = NB == 8 ? 304 : 176;
     static constexpr bool kLut = false, kTokens = true, kXsum = false, kHalves = false;
     __device__ static void fill(uint32_t*) {}
     __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t*,
@@ -331,7 +333,7 @@ struct M8Q8_0 {
         const uint8_t* xsrc = gid == 0 ? xh : xl;
         const float k = xs[0] * (1.0f / 128.0f);  // (a stage lies within one 256-column scale block)
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
+        for (int r = 0; r < NB; ++r) {
             uint32_t a[2][2];
             float d[2];
 #pragma unroll
@@ -362,7 +364,7 @@ struct M8Q8_0 {
         const uint8_t* xsrc = ((gid & 1) ? xl : xh) + int64_t(t) * xstride;
         const float k = tig < nt ? xs[tig * xsstride] * (1.0f / 128.0f) : 0.0f;
 #pragma unroll
-        for (int r = 0; r < 4; ++r) {
+        for (int r = 0; r < NB; ++r) {
             uint32_t a[2][2];
             float d[2];
 #pragma unroll
@@ -383,6 +385,7 @@ struct M8Q8_0 {
         }
     }
 };
+using M8Q8_0 = M8Q8_0N<8>;
 
 // Eight values a lane of one 256-column block (a warp) split into int8 hi and lo and the block's scale:
 // v = s (hi + lo / 128), s = max|v| / 127. With sum16 set, sum16[c] receives the block's 16-column group c's
