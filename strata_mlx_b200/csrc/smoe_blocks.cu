@@ -572,11 +572,23 @@ int batch_specs(int n, const SmoeMatvec* pr, M8Spec* spec, int& m, M8Pref* pref,
     return SMOE_OK;
 }
 
-// the problems one by one through their own entry points
+// the problems through their own entry points: a problem and the next one of the same kind and shape on the
+// same pairs and activations (a gate / up pair) in one launch, the others one by one
 int batch_each(int n, const SmoeMatvec* pr, void* stream) {
     for (int i = 0; i < n; ++i) {
         const SmoeMatvec& p = pr[i];
         if (p.pairs == 0 || p.out == nullptr) continue;
+        if (p.x != nullptr && i + 1 < n) {
+            const SmoeMatvec& q = pr[i + 1];
+            if (q.out != nullptr && q.x == p.x && q.kind == p.kind && q.experts == p.experts && q.rows == p.rows &&
+                q.cols == p.cols && q.idx == p.idx && q.pairs == p.pairs && q.share == p.share && q.dtype == p.dtype) {
+                const int r = smoe_matvec_gate_up(p.kind, p.blocks, q.kind, q.blocks, p.experts, p.rows, p.cols, p.idx,
+                                                  p.pairs, p.share, p.x, p.out, q.out, p.dtype, stream);
+                if (r) return r;
+                ++i;
+                continue;
+            }
+        }
         const int r = p.x ? smoe_matvec(p.kind, p.blocks, p.experts, p.rows, p.cols, p.idx, p.pairs, p.share, p.x,
                                         p.out, p.dtype, stream)
                           : smoe_matvec_glu(p.kind, p.blocks, p.experts, p.rows, p.cols, p.idx, p.pairs, p.gate,
