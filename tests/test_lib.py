@@ -71,6 +71,15 @@ def test_invalid_arguments_are_rejected_on_the_host(lib):
     assert lib.smoe_route(v, v, v, 1, 1, 256, 512, 8, v, v, v, None, v, None) == 4  # gate weight, no output
     assert lib.smoe_route(v, None, v, 1, 1, 4096, 512, 8, v, v, v, None, v, None) == 2  # too many experts
     assert lib.smoe_route_counters(20) == 12
+    # the fused route step: its counters hold two words before smoe_route's, and it checks its arguments first
+    assert lib.smoe_route_step_counters(1) == 16 and lib.smoe_route_step_counters(20) == 32
+    assert lib.smoe_route_matvec_batch(None, 0, None, None) == 4  # null route
+    step = _lib.SmoeRouteStep(16, None, 16, 1, 1, 256, 512, 8, 16, 16, 16, None, 16, 200, 100, 16)
+    assert lib.smoe_route_matvec_batch(ctypes.byref(step), 0, None, None) == 4  # [lo, lo + count) past the experts
+    step.tokens = -1
+    assert lib.smoe_route_matvec_batch(ctypes.byref(step), 0, None, None) == 4  # negative token count
+    step.tokens = 0
+    assert lib.smoe_route_matvec_batch(ctypes.byref(step), 0, None, None) == 0  # nothing to do
     with pytest.raises(ValueError):
         _lib.call("smoe_dequant", 21, None, 4, 100, None, 1, None)
 
