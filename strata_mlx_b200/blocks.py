@@ -38,6 +38,9 @@ TILES_FROM = 1600  # a call with at least this many (token, expert) pairs takes 
 TOKENS_TILE, ROWS_TILE, COLS_TILE = 16, 64, 64  # strata_mlx/blocks.py:580
 BLOCK_GLU = True  # pairs unsorted, swiglu formed by the down kernel (strata_mlx/blocks.py:934)
 MATVEC_GLU_UPTO = 30  # pairs up to which down forms swiglu itself (strata_mlx/blocks.py:936)
+# pairs up to which a step of the block runs as the fused decode products (decode_products): the int8 down
+# kernel forms swiglu itself at any pair count, so this is not the reference's MATVEC_GLU_UPTO
+DECODE_UPTO = 256
 
 
 def _kind(kind: str) -> int:
@@ -415,7 +418,7 @@ def decode_products(switch_mlp, shared, x: torch.Tensor, indices: torch.Tensor, 
     idx = _flat_idx(indices)
     x2 = x.reshape(-1, x.shape[-1]).contiguous()
     tokens, pairs = x2.shape[0], idx.numel()
-    if (pairs != tokens * k or pairs > MATVEC_GLU_UPTO or pairs >= min(lin.unpack_from for lin in lins)
+    if (pairs != tokens * k or pairs > DECODE_UPTO or pairs >= min(lin.unpack_from for lin in lins)
             or any(lin.gemm(x2) for lin in slins)):
         return None
     _lib.require_cuda(x, indices, *(lin.blocks for lin in lins), *(lin.blocks for lin in slins))
