@@ -128,18 +128,20 @@ def test_float16_products_of_the_k_types_on_int8_dot_products(cuda, kind, rows, 
 
 
 @pytest.mark.parametrize("kind", ["IQ3_S", "Q8_0", "Q4_K", "Q6_K", "IQ4_XS", "IQ3_XXS"])
-def test_a_window_gives_each_token_its_bits_alone(cuda, kind):
+@pytest.mark.parametrize("window", [5, 8, 11])
+def test_a_window_gives_each_token_its_bits_alone(cuda, kind, window):
     """window_matvec (strata_mlx/blocks.py:349-396): a verify window's dense product within 1e-3 of the largest
     value of the float64 product; each token the same bits as alone, on the CUDA-core kernels and on the int8
-    tensor-core kernel (a one-expert stack's team of warps follows its shape, not the window)."""
-    rng = np.random.default_rng(len(kind))
+    tensor-core kernel (a one-expert stack's team of warps follows its shape, not the window; Q8_0 takes up to
+    four tokens a pass: 5 as four and one, 8 as two passes, 11 as four, four and three)."""
+    rng = np.random.default_rng(len(kind) + 16 * window)
     rows, cols = 256, 1024
     b, w = stack(kind, rng, 1, rows, cols, scale=(-0.05, 0.05))
-    x = rng.standard_normal((5, cols)).astype(np.float16)
+    x = rng.standard_normal((window, cols)).astype(np.float16)
     got = B.window_matvec(dev(b), kind, rows, cols, dev(x))
-    assert got.shape == (5, rows) and got.dtype == torch.float16
+    assert got.shape == (window, rows) and got.dtype == torch.float16
     want = x.astype(np.float64) @ w[0].astype(np.float64).T
-    for t in range(5):
+    for t in range(window):
         alone = B.window_matvec(dev(b), kind, rows, cols, dev(x[t : t + 1]))
         assert torch.equal(got[t : t + 1], alone)
     assert np.abs(got.float().cpu().numpy() - want).max() <= 1e-3 * np.abs(want).max()
