@@ -121,6 +121,125 @@ __global__ void __launch_bounds__(256) route_kernel(const __half* __restrict__ w
     if (threadIdx.x == 0) counters[blockIdx.y] = 0u;
 }
 
+// ---------------------------------------------------------------- the route of a prompt chunk
+//
+// The same sums as router_rows, bit for bit: for each (row, token) lane l of quarter q adds the products of
+// its chunks q 32 + l + 128 u in increasing u, a chunk's eight in order, from 0.0f by fused multiply-adds; the
+// quarter's lanes are added by warp_sum's shuffle tree and the four quarters in order. Only the mapping differs:
+// a warp takes one quarter of kPrRows rows x kPrTok tokens, so a lane's chunk of a weight row serves kPrTok
+// tokens and its chunk of a token kPrRows rows from registers; a CTA's 8 warps are the four quarters of two
+// token halves (kPrRows rows x 2 kPrTok tokens). Against route_kernel (2 rows x 8 tokens a CTA, every chunk of x
+// loaded once per row) a prompt chunk reads about a third of the bytes from L2 and issues a quarter of the
+// loads a multiply-add. The last CTA of a token group takes the group's top-k (counters: one word per 16
+// tokens, within smoe_route_counters' size); without counters the launch writes only the logits.
+
+constexpr int kPrRows = 4, kPrTok = 8;
+constexpr int64_t kPrFrom = 32;  // windows of more tokens than this take route_chunk_kernel
+
+template <typename XT, int NV>
+__global__ void __launch_bounds__(256) route_chunk_kernel(const __half* __restrict__ w, const __half* __restrict__ gw,
+                                                          const XT* __restrict__ x, int64_t tokens, int64_t experts,
+                                                          int64_t hidden, int k, float* __restrict__ logits,
+                                                          uint32_t* __restrict__ idx, float* __restrict__ weights,
+                                                          XT* __restrict__ gate_out, uint32_t* __restrict__ counters,
+                                                          uint32_t lo, uint32_t count, uint32_t* __restrict__ lidx) {
+    __shared__ float part[4][2 * kPrTok][kPrRows];
+    __shared__ bool last;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int64_t rows = experts + (gw != nullptr ? 1 : 0);
+    const int64_t r0 = int64_t(blockIdx.x) * kPrRows;
+    const int64_t tg0 = int64_t(blockIdx.y) * (2 * kPrTok);
+    const int64_t t0 = tg0 + half * kPrTok;
+    const int nt = static_cast<int>(max(int64_t(0), min(int64_t(kPrTok), tokens - t0)));
+    const __half* rp[kPrRows];
+    bool live[kPrRows];
+#pragma unroll
+    for (int r = 0; r < kPrRows; ++r) {
+        const int64_t e = r0 + r;
+        live[r] = e < rows;
+        rp[r] = e < experts ? w + e * hidden : gw;
+    }
+    float acc[kPrRows][kPrTok];
+#pragma unroll
+    for (int r = 0; r < kPrRows; ++r)
+#pragma unroll
+        for (int t = 0; t < kPrTok; ++t) acc[r][t] = 0.0f;
+    pdl_wait();
+    pdl_release();
+    const int64_t chunks = hidden >> 3;
+#pragma unroll 2
+    for (int64_t c = quarter * 32 + lane; c < chunks; c += 128) {
+        float wv[kPrRows][8];
+#pragma unroll
+        for (int r = 0; r < kPrRows; ++r) {
+            if (live[r]) {
+                load8<__half>(rp[r] + 8 * c, wv[r]);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) wv[r][j] = 0.0f;
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < kPrTok; ++t) {
+            if (t < nt) {
+                float xv[8];
+                load8<XT>(x + (t0 + t) * hidden + 8 * c, xv);
+#pragma unroll
+                for (int r = 0; r < kPrRows; ++r)
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[r][t] = fmaf(wv[r][j], xv[j], acc[r][t]);
+            }
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < kPrRows; ++r)
+#pragma unroll
+        for (int t = 0; t < kPrTok; ++t) acc[r][t] = warp_sum(acc[r][t]);
+    if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < kPrRows; ++r)
+#pragma unroll
+            for (int t = 0; t < kPrTok; ++t) part[quarter][half * kPrTok + t][r] = acc[r][t];
+    }
+    __syncthreads();
+    if (threadIdx.x < 2 * kPrTok * kPrRows) {
+        const int tt = threadIdx.x / kPrRows, r = threadIdx.x % kPrRows;
+        const int64_t e = r0 + r, t = tg0 + tt;
+        if (e < rows && t < tokens) {
+            float s = part[0][tt][r];
+            s += part[1][tt][r];
+            s += part[2][tt][r];
+            s += part[3][tt][r];
+            if (e < experts) logits[t * experts + e] = s;
+            else gate_out[t] = from_f32<XT>(s);
+        }
+    }
+    if (counters == nullptr) return;
+    // the last CTA of this token group to finish takes the group's top-k, a warp to two tokens
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(&counters[blockIdx.y], 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int tt = warp; tt < 2 * kPrTok; tt += 8) {
+        const int64_t t = tg0 + tt;
+        if (t >= tokens) break;
+        const float* in = logits + t * experts;
+        topk_row<NV>([&](int j) { return __ldcg(in + j); }, static_cast<int>(experts), k, idx + t * k, weights + t * k);
+        if (lidx != nullptr) {  // this rank's view of the choice: expert - lo for its own, `count` for the others'
+            __syncwarp();
+            for (int j = lane; j < k; j += 32) {
+                const uint32_t e = idx[t * k + j] - lo;
+                lidx[t * k + j] = e < count ? e : count;
+            }
+        }
+        __syncwarp();
+    }
+    if (threadIdx.x == 0) counters[blockIdx.y] = 0u;
+}
+
 // ---------------------------------------------------------------- combine
 
 template <typename T>
@@ -243,12 +362,27 @@ extern "C" int smoe_router_logits(const uint16_t* weight, const void* x, int x_d
     dim3 grid(static_cast<unsigned>((experts + 1) / 2), static_cast<unsigned>((tokens + kRtTokens - 1) / kRtTokens));
     cudaStream_t st = as_stream(stream);
     const __half* w = reinterpret_cast<const __half*>(weight);
-    if (x_dtype == SMOE_F16)
-        router_kernel<__half><<<grid, 256, 0, st>>>(w, static_cast<const __half*>(x), tokens, experts, hidden, logits);
-    else if (x_dtype == SMOE_F32)
-        router_kernel<float><<<grid, 256, 0, st>>>(w, static_cast<const float*>(x), tokens, experts, hidden, logits);
-    else
+    // a prompt chunk: the same sums with the chunks reused from registers (route_chunk_kernel, logits only)
+    const bool chunk = tokens > kPrFrom;
+    const dim3 cgrid(static_cast<unsigned>((experts + kPrRows - 1) / kPrRows),
+                     static_cast<unsigned>((tokens + 2 * kPrTok - 1) / (2 * kPrTok)));
+    if (x_dtype == SMOE_F16) {
+        const __half* xp = static_cast<const __half*>(x);
+        if (chunk)
+            route_chunk_kernel<__half, 8><<<cgrid, 256, 0, st>>>(w, nullptr, xp, tokens, experts, hidden, 1, logits,
+                                                                 nullptr, nullptr, nullptr, nullptr, 0u, 0u, nullptr);
+        else
+            router_kernel<__half><<<grid, 256, 0, st>>>(w, xp, tokens, experts, hidden, logits);
+    } else if (x_dtype == SMOE_F32) {
+        const float* xp = static_cast<const float*>(x);
+        if (chunk)
+            route_chunk_kernel<float, 8><<<cgrid, 256, 0, st>>>(w, nullptr, xp, tokens, experts, hidden, 1, logits,
+                                                                nullptr, nullptr, nullptr, nullptr, 0u, 0u, nullptr);
+        else
+            router_kernel<float><<<grid, 256, 0, st>>>(w, xp, tokens, experts, hidden, logits);
+    } else {
         return fail(SMOE_EDTYPE, "router activations must be float16 or float32");
+    }
     return launch_status("router_logits");
 }
 
@@ -307,6 +441,20 @@ static int route_launch(const uint16_t* weight, const uint16_t* gate_weight, con
         wr.add(gate_out, size_t(tokens) * sizeof(XT)).add(counters, smoe_route_counters(tokens));
         wr.add(lidx, size_t(tokens) * k * 4);
         const uint32_t l0 = static_cast<uint32_t>(lo), cn = static_cast<uint32_t>(count);
+        if (tokens > kPrFrom) {
+            // a prompt chunk: the same sums with the chunks reused from registers, one counter per 16 tokens
+            const dim3 cgrid(static_cast<unsigned>((rows + kPrRows - 1) / kPrRows),
+                             static_cast<unsigned>((tokens + 2 * kPrTok - 1) / (2 * kPrTok)));
+            if (experts <= 256)
+                launch_pdl(wr, route_chunk_kernel<XT, 8>, cgrid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters, l0, cn, lidx);
+            else if (experts <= 512)
+                launch_pdl(wr, route_chunk_kernel<XT, 16>, cgrid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters, l0, cn, lidx);
+            else if (experts <= 1024)
+                launch_pdl(wr, route_chunk_kernel<XT, 32>, cgrid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters, l0, cn, lidx);
+            else
+                launch_pdl(wr, route_chunk_kernel<XT, 64>, cgrid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters, l0, cn, lidx);
+            return;
+        }
         if (experts <= 256)
             launch_pdl(wr, route_kernel<XT, 8>, grid, dim3(256), 0, st, w, gw, xp, tokens, experts, hidden, kk, logits, idx, weights, go_, counters, l0, cn, lidx);
         else if (experts <= 512)
