@@ -143,6 +143,12 @@ SMOE_API int smoe_matvec_glu_combine(int kind, const uint8_t* blocks, int64_t ro
  * strata_mlx/blocks.py:222-237 (the unfused form `down(swiglu(g, u), indices)`, blocks.py:976). */
 SMOE_API int smoe_swiglu(const void* gate, const void* up, int64_t n, void* out, int dtype, void* stream);
 
+/* smoe_swiglu from float32 gate and up (a tile product's sums) to float16 out: the float32 SwiGLU rounded once,
+ * `swiglu(g, u).astype(x.dtype)` of the tiled path (strata_mlx/blocks.py:690-692); with out_dtype == dtype it is
+ * smoe_swiglu. */
+SMOE_API int smoe_swiglu_to(const void* gate, const void* up, int64_t n, int dtype, void* out, int out_dtype,
+                            void* stream);
+
 /* Router product: logits[t, e] = W[e, :] . x[t, :], W float16 (experts, hidden), x `x_dtype`
  * (tokens, hidden), float32 sums and result. A token's sum does not depend on `tokens`.
  * Replaces `WindowLinear.__call__` / `_MATVEC` of fused.py (strata_mlx/fused.py:334-390). */
@@ -382,6 +388,21 @@ SMOE_API size_t smoe_tile_matmul_workspace_size(int64_t p16);
 SMOE_API int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
                      const void* a, int a_dtype, int64_t p16, const uint32_t* tile_expert, float* out,
                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* smoe_tile_matmul with its result read back in the caller's order and type: the sums of slot s, rounded once
+ * to float16, go to row slot_row[s] of out (out_rows, rows) float16, or to row s without slot_row; rows at or past
+ * out_rows are not written. Float16 activations a (a_rows <= p16 rows: the slots past a_rows multiply zeros, so a
+ * dense layer's tokens need no padding to a whole tile), cols a multiple of 256 (the tensor-core kernel;
+ * SMOE_ESHAPE otherwise). No single reference counterpart: it is `tile_matmul` followed by the read-back of the
+ * tiled path, `out[where].astype(x.dtype)` (strata_mlx/blocks.py:684-694), in one launch. */
+SMOE_API int smoe_tile_matmul_rows(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
+                                   const void* a, int64_t a_rows, int64_t p16, const uint32_t* tile_expert,
+                                   const uint32_t* slot_row, int64_t out_rows, void* out, void* workspace,
+                                   size_t workspace_bytes, void* stream);
+
+/* slot_row[s] = p for the pair p with where[p] = s (smoe_tiles_of's `where` inverted), 0xffffffff for slots no
+ * pair fills: the map smoe_tile_matmul_rows takes to write a tiled product in pair order. slots entries. */
+SMOE_API int smoe_slot_rows(const uint32_t* where, int64_t pairs, int64_t slots, uint32_t* slot_row, void* stream);
 
 /* One MoE block's decode step for one float16 token in a single persistent launch: smoe_route (with the
  * shared gate), the four gate / up products of smoe_matvec_batch, the routed down product of smoe_matvec_glu

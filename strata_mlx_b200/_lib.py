@@ -78,6 +78,7 @@ SIGNATURES = {
     "smoe_decode_layer_status": (_i, [_p, _i64, _i64, _i64, _i64, _c.POINTER(_i)]),
     "smoe_decode_layer_wait_test": (_i, [_i]),
     "smoe_swiglu": (_i, [_p, _p, _i64, _p, _i, _p]),
+    "smoe_swiglu_to": (_i, [_p, _p, _i64, _i, _p, _i, _p]),
     "smoe_router_logits": (_i, [_p, _p, _i, _i64, _i64, _i64, _p, _p]),
     "smoe_top_k": (_i, [_p, _i64, _i64, _i64, _p, _p, _p]),
     "smoe_combine": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _p, _i, _p]),
@@ -113,12 +114,15 @@ SIGNATURES = {
     "smoe_tileable": (_i, [_i, _i64, _i64]),
     "smoe_tile_matmul_workspace_size": (_sz, [_i64]),
     "smoe_tile_matmul": (_i, [_i, _p, _i64, _i64, _i64, _p, _i, _i64, _p, _p, _p, _sz, _p]),
+    "smoe_tile_matmul_rows": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _p, _p, _sz, _p]),
+    "smoe_slot_rows": (_i, [_p, _i64, _i64, _p, _p]),
 }
 
 _lib = None
 
 # kernels each entry point launches (for the benchmark's launch count); 1 where not named
-KERNELS_PER_CALL = {"smoe_tiles_of": 2, "smoe_tiles_of_noalloc": 2, "smoe_tile_matmul": 2, "smoe_ep_dispatch": 2,
+KERNELS_PER_CALL = {"smoe_tiles_of": 2, "smoe_tiles_of_noalloc": 2, "smoe_tile_matmul": 2, "smoe_tile_matmul_rows": 2,
+                    "smoe_ep_dispatch": 2,
                     "smoe_ep_exchange_alloc": 0, "smoe_ep_exchange_open": 0, "smoe_ep_exchange_close": 0,
                     "smoe_ep_exchange_free": 0, "smoe_ep_exchange_status": 0, "smoe_decode_layer_status": 0, "smoe_decode_layer_wait_test": 0,
                     "smoe_matvec_status": 0, "smoe_matvec_wait_test": 0, "smoe_hyper_connection": 3}

@@ -241,6 +241,44 @@ def tile_matmul(blocks: torch.Tensor, kind: str, shape: tuple, a: torch.Tensor, 
     return out
 
 
+def tile_matmul_rows(blocks: torch.Tensor, kind: str, shape: tuple, a: torch.Tensor, tile_expert: torch.Tensor,
+                     slot_row, out_rows: int) -> torch.Tensor:
+    """tile_matmul with the result read back in the caller's order, rounded once to float16: row slot_row[s] of
+    the (out_rows, rows) float16 result is slot s's row (`tile_matmul(...)[where].astype(float16)` of the tiled
+    path, strata_mlx/blocks.py:693, in one launch); without slot_row (None), row s for s < out_rows. `a` float16
+    with at most TOKENS_TILE rows per tile (slots past its rows multiply zeros, so a dense layer's tokens need no
+    padding); cols a multiple of 256."""
+    _lib.require_cuda(blocks, a, tile_expert)
+    experts, rows, cols = shape
+    te = tile_expert.reshape(-1).contiguous()
+    if te.dtype not in (torch.int32, torch.uint32):
+        te = te.to(torch.int32)
+    p16 = te.numel() * TOKENS_TILE
+    if a.dtype != torch.float16 or not 0 < a.shape[0] <= p16:
+        raise ValueError("tile_matmul_rows takes float16 activations of 1 to TOKENS_TILE rows per tile")
+    a = a.contiguous()
+    out = torch.empty((out_rows, rows), dtype=torch.float16, device=a.device)
+    ws = torch.empty(int(_lib.lib().smoe_tile_matmul_workspace_size(p16)), dtype=torch.uint8, device=a.device)
+    _lib.call("smoe_tile_matmul_rows", _kind(kind), _lib.ptr(blocks), experts, rows, cols, _lib.ptr(a), a.shape[0],
+              p16, _lib.ptr(te), _lib.ptr(slot_row) if slot_row is not None else None, out_rows, _lib.ptr(out),
+              _lib.ptr(ws), ws.numel(), _lib.stream())
+    return out
+
+
+def slot_rows(where: torch.Tensor, slots: int) -> torch.Tensor:
+    """The inverse of tiles_of's `where`: slot s -> the pair in it, 0xffffffff for slots no pair fills."""
+    _lib.require_cuda(where)
+    where = where.contiguous()
+    out = torch.empty(slots, dtype=torch.uint32, device=where.device)
+    _lib.call("smoe_slot_rows", _lib.ptr(where), where.numel(), slots, _lib.ptr(out), _lib.stream())
+    return out
+
+
+def rows_take(kind: str, cols: int, dtype) -> bool:
+    """Whether tile_matmul_rows takes this stack with activations of `dtype`."""
+    return dtype == torch.float16 and cols % 256 == 0
+
+
 def tiles_of(indices: torch.Tensor, experts: int) -> tuple:
     """Group the (token, expert) pairs of `indices` (..., k) by expert into tiles of TOKENS_TILE slots
     (strata_mlx/blocks.py:657-681).
@@ -267,6 +305,18 @@ def tiles_of(indices: torch.Tensor, experts: int) -> tuple:
     return tile_expert, token, where
 
 
+def swiglu_to(gate: torch.Tensor, up: torch.Tensor, dtype) -> torch.Tensor:
+    """swiglu(gate, up).to(dtype) in one pass: float32 gate and up to float16, the float32 SwiGLU rounded once."""
+    if gate.dtype == dtype:
+        return swiglu(gate, up)
+    _lib.require_cuda(gate, up)
+    gate, up = gate.contiguous(), up.contiguous()
+    out = torch.empty(gate.shape, dtype=dtype, device=gate.device)
+    _lib.call("smoe_swiglu_to", _lib.ptr(gate), _lib.ptr(up), gate.numel(), _lib.dtype_code(gate.dtype), _lib.ptr(out),
+              _lib.dtype_code(dtype), _lib.stream())
+    return out
+
+
 def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """mlx-lm's swiglu = silu(gate) * up in the inputs' type (sigmoid in float32 rounded to the type, then two
     products in the type), as the reference relies on it (strata_mlx/blocks.py:222-237)."""
@@ -286,11 +336,18 @@ def _tiled_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.
     """A prompt chunk's SwiGLU experts on the tile path: tiles_of, gather of the token rows, gate and up tile
     GEMMs, SwiGLU, the down tile GEMM, and the results read back in pair order (strata_mlx/blocks.py:684-694)."""
     tiles, token, where = tiles_of(indices, gate.num_experts)
-    a = x.reshape(-1, x.shape[-1]).index_select(0, _as_int64(token))
+    a = x.reshape(-1, x.shape[-1]).index_select(0, token.view(torch.int32))
 
     def product(lin, a):
         return tile_matmul(lin.blocks, lin.kind, lin.shape, a, tiles)
 
+    if x.dtype == torch.float16 and rows_take(down.kind, down.input_dims, x.dtype):
+        # the same values in fewer passes: the SwiGLU of the float32 sums rounded once to float16, and the down
+        # product written in pair order as float16 by its own launch
+        h = swiglu_to(product(gate, a), product(up, a), x.dtype)
+        out = tile_matmul_rows(down.blocks, down.kind, down.shape, h, tiles, slot_rows(where, h.shape[0]),
+                               where.numel())
+        return out.reshape(*indices.shape, down.output_dims)
     h = swiglu(product(gate, a), product(up, a)).to(x.dtype)
     out = product(down, h).index_select(0, _as_int64(where)).to(x.dtype)
     return out.reshape(*indices.shape, down.output_dims)
@@ -487,14 +544,19 @@ def _zeros_idx(n: int, device) -> torch.Tensor:
 GEMM_FROM = 32  # tokens from which a one-expert layer goes through the tensor-core tile product
 
 
-def _dense_tiles(lin, x2: torch.Tensor) -> torch.Tensor:
-    """x2 (tokens, in) through a one-expert stack on the tile product: tokens padded to tiles of 16 of expert 0.
-    Returns (tokens, out) float32 (weights rounded to x's type, float32 sums, as `tile_matmul`)."""
+def _dense_tiles(lin, x2: torch.Tensor, dtype=None) -> torch.Tensor:
+    """x2 (tokens, in) through a one-expert stack on the tile product, tokens in tiles of 16 of expert 0.
+    Returns (tokens, out) float32 (weights rounded to x's type, float32 sums, as `tile_matmul`), or with
+    `dtype` those sums rounded to it: float16 activations take the rows variant (no padding rows, float16
+    written by the product's own launch)."""
     tokens = x2.shape[0]
     p16 = (tokens + TOKENS_TILE - 1) // TOKENS_TILE * TOKENS_TILE
+    te = _zeros_idx(p16 // TOKENS_TILE, x2.device)
+    if dtype == torch.float16 and rows_take(lin.kind, lin.input_dims, x2.dtype):
+        return tile_matmul_rows(lin.blocks, lin.kind, lin.shape, x2, te, None, tokens)
     a = x2 if p16 == tokens else torch.cat([x2, x2.new_zeros(p16 - tokens, x2.shape[1])])
-    te = torch.zeros(p16 // TOKENS_TILE, dtype=torch.int32, device=x2.device)
-    return tile_matmul(lin.blocks, lin.kind, lin.shape, a, te)[:tokens]
+    out = tile_matmul(lin.blocks, lin.kind, lin.shape, a, te)[:tokens]
+    return out if dtype is None else out.to(dtype)
 
 
 class BlockLinear:
@@ -519,7 +581,7 @@ class BlockLinear:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         x2 = x.reshape(-1, self.input_dims).contiguous()
         if self.gemm(x2):
-            out = _dense_tiles(self.stack, x2).to(x.dtype)
+            out = _dense_tiles(self.stack, x2, x.dtype)
         else:
             idx = _zeros_idx(x2.shape[0], x.device)
             out = _matvec(self.stack, x2, idx, 1, x.dtype)
@@ -537,9 +599,9 @@ class BlockMLP:
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
         if all(p.gemm(x2) for p in (self.gate_proj, self.up_proj, self.down_proj)):
             # a prompt's chunk: the three products on the tensor cores, rounded to x's type as QuantizedLinear does
-            g = _dense_tiles(self.gate_proj.stack, x2).to(x.dtype)
-            u = _dense_tiles(self.up_proj.stack, x2).to(x.dtype)
-            out = _dense_tiles(self.down_proj.stack, swiglu(g, u)).to(x.dtype)
+            g = _dense_tiles(self.gate_proj.stack, x2, x.dtype)
+            u = _dense_tiles(self.up_proj.stack, x2, x.dtype)
+            out = _dense_tiles(self.down_proj.stack, swiglu(g, u), x.dtype)
             return out.reshape(*x.shape[:-1], self.down_proj.output_dims)
         idx = _zeros_idx(x2.shape[0], x.device)
         g, u = gate_up(self.gate_proj.stack, self.up_proj.stack, x2, idx, 1)

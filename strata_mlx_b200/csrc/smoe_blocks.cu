@@ -401,6 +401,13 @@ __global__ void swiglu_kernel(const T* __restrict__ g, const T* __restrict__ u, 
         out[i] = swiglu_one(g[i], u[i]);
 }
 
+// float32 gate and up, float16 out: the float32 SwiGLU rounded once to float16
+__global__ void swiglu_to_half_kernel(const float* __restrict__ g, const float* __restrict__ u, int64_t n,
+                                      __half* __restrict__ out) {
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        out[i] = __float2half_rn(swiglu_one(g[i], u[i]));
+}
+
 // ---------------------------------------------------------------- host side
 
 // the float16 tensor-core decode matvec (smoe_mv.cu), for what the int8 one does not take
@@ -710,6 +717,19 @@ extern "C" int smoe_matvec_glu(int kind, const uint8_t* blocks, int64_t experts,
         return matvec_common<float>(kind, blocks, kind, nullptr, experts, rows, cols, idx, pairs, 1, nullptr, gate, up,
                                     out, nullptr, 1, as_stream(stream));
     return fail(SMOE_EDTYPE, "activations must be float16 or float32");
+}
+
+extern "C" int smoe_swiglu_to(const void* gate, const void* up, int64_t n, int dtype, void* out, int out_dtype,
+                              void* stream) {
+    if (dtype == out_dtype) return smoe_swiglu(gate, up, n, out, dtype, stream);
+    if (n == 0) return SMOE_OK;
+    SMOE_REQUIRE(gate && up && out && n > 0, SMOE_EARG, "null pointer or negative size");
+    SMOE_REQUIRE(dtype == SMOE_F32 && out_dtype == SMOE_F16, SMOE_EDTYPE,
+                 "swiglu_to takes float32 gate and up to float16, or one type throughout");
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 148 * 16));
+    swiglu_to_half_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const float*>(gate),
+                                                               static_cast<const float*>(up), n, static_cast<__half*>(out));
+    return launch_status("swiglu_to");
 }
 
 extern "C" int smoe_swiglu(const void* gate, const void* up, int64_t n, void* out, int dtype, void* stream) {

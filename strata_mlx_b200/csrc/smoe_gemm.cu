@@ -151,6 +151,11 @@ struct GemmArgs {
     const uint8_t* end;
     const __half* a;
     float* out;
+    // the rows variant: slot s's row goes to row slot_row[s] of out16 / out (float16 when out16 is set; rows at or
+    // past out_rows are not written); without slot_row, slot s to row s
+    __half* out16;
+    const uint32_t* slot_row;
+    int64_t out_rows;
     const GemmPlanHeader* hdr;
     const TileRun* runs;
     int* status;
@@ -464,17 +469,44 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
             }
             if (!ok) break;
             // epilogue: accumulators of rows m, tokens 8 qq + 32 i .. + 7
+            const int64_t s0 = int64_t(run.first_tile) * 16;
+            const int ncol = 16 * run.tiles;
+            // (the rows variant: lane l holds the output rows of slots s0 + l + 32 i, loaded before the wait)
+            uint32_t orow[4] = {~0u, ~0u, ~0u, ~0u};
+            if (g.slot_row != nullptr) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                    if (32 * i + lane < ncol) orow[i] = __ldg(g.slot_row + s0 + 32 * i + lane);
+            }
             ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.dfull, jobs & 1, kWaitLimit));
             if (!ok) break;
             tc::fence_after_sync();
-            float* obase = g.out + int64_t(run.first_tile) * 16 * g.rows + row0 + m;
-            for (int c0 = 8 * qq; c0 < 16 * run.tiles; c0 += 32) {
-                uint32_t v[8];
-                tc::tmem_ld8(tmem + (uint32_t(32 * (warp & 3)) << 16) + uint32_t(c0), v);
-                tc::tmem_wait_ld();
-                if (m < mrows) {
+            if (g.out != nullptr) {
+                float* obase = g.out + s0 * g.rows + row0 + m;
+                for (int c0 = 8 * qq; c0 < ncol; c0 += 32) {
+                    uint32_t v[8];
+                    tc::tmem_ld8(tmem + (uint32_t(32 * (warp & 3)) << 16) + uint32_t(c0), v);
+                    tc::tmem_wait_ld();
+                    if (m < mrows) {
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) obase[int64_t(c0 + j) * g.rows] = __uint_as_float(v[j]);
+                        for (int j = 0; j < 8; ++j) obase[int64_t(c0 + j) * g.rows] = __uint_as_float(v[j]);
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const int c0 = 8 * qq + 32 * i;
+                    if (c0 >= ncol) break;
+                    uint32_t v[8];
+                    tc::tmem_ld8(tmem + (uint32_t(32 * (warp & 3)) << 16) + uint32_t(c0), v);
+                    tc::tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t sr = __shfl_sync(0xffffffffu, orow[i], 8 * qq + j);
+                        const int64_t r = g.slot_row != nullptr ? int64_t(sr) : s0 + c0 + j;
+                        if (m < mrows && r < g.out_rows)
+                            g.out16[r * g.rows + row0 + m] = __float2half_rn(__uint_as_float(v[j]));
+                    }
                 }
             }
             tc::fence_before_sync();
@@ -585,7 +617,7 @@ static EncodeTiledFn encoder() {
 }
 
 static int encode_maps(GemmMaps* maps, const uint8_t* blocks, int64_t total_rows, int64_t row_bytes, int q, int rawb,
-                       const void* a, int64_t p16, int64_t cols) {
+                       const void* a, int64_t a_rows, int64_t cols) {
     EncodeTiledFn encode = encoder();
     if (!encode) return fail(SMOE_EARG, "tile_matmul: cuTensorMapEncodeTiled is not available");
     const cuuint32_t estr[2] = {1, 1};
@@ -601,7 +633,8 @@ static int encode_maps(GemmMaps* maps, const uint8_t* blocks, int64_t total_rows
             return fail(SMOE_EARG, "tile_matmul: block tensor map rejected (" + std::to_string(int(r)) + ")");
     }
     for (int b = 0; b < 4; ++b) {
-        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(p16)};
+        // (rows of the last tile past a_rows read as zeros: the copy's fill)
+        const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(a_rows)};
         const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 2};
         const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(16 << b)};
         const CUresult r = encode(&maps->a[b], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a), dims, strides,
@@ -613,14 +646,27 @@ static int encode_maps(GemmMaps* maps, const uint8_t* blocks, int64_t total_rows
     return SMOE_OK;
 }
 
-extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
-                                const void* a, int a_dtype, int64_t p16, const uint32_t* tile_expert, float* out,
-                                void* workspace, size_t workspace_bytes, void* stream) {
+// slot_row[where[p]] = p for every pair p; slots no pair names keep 0xffffffff
+__global__ void slot_rows_kernel(const uint32_t* __restrict__ where, int64_t pairs, int64_t slots,
+                                 uint32_t* __restrict__ slot_row) {
+    for (int64_t p = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; p < pairs; p += int64_t(gridDim.x) * blockDim.x) {
+        const uint32_t s = where[p];
+        if (s < slots) slot_row[s] = static_cast<uint32_t>(p);
+    }
+}
+
+// out (float32, slot order) or, the rows variant, out16 (float16) at the rows slot_row names
+static int tile_matmul_impl(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
+                            const void* a, int a_dtype, int64_t a_rows, int64_t p16, const uint32_t* tile_expert,
+                            float* out, __half* out16, const uint32_t* slot_row, int64_t out_rows, void* workspace,
+                            size_t workspace_bytes, void* stream) {
     if (p16 == 0) return SMOE_OK;
     int per, bytes;
     if (!block_info(kind, per, bytes)) return fail(SMOE_EKIND, "block type " + std::to_string(kind) + " has no decoder");
     SMOE_REQUIRE(smoe_tileable(kind, rows, cols), SMOE_ESHAPE, "stack not tileable: rows and cols must divide by 64 and cols by the block");
-    SMOE_REQUIRE(blocks && a && tile_expert && out && p16 > 0 && experts > 0, SMOE_EARG, "null pointer or empty stack");
+    SMOE_REQUIRE(blocks && a && tile_expert && (out || out16) && p16 > 0 && experts > 0, SMOE_EARG,
+                 "null pointer or empty stack");
+    SMOE_REQUIRE(a_rows > 0 && a_rows <= p16, SMOE_ESHAPE, "a's rows must be 1 to the tiles' slots");
     SMOE_REQUIRE(p16 % 16 == 0, SMOE_ESHAPE, "a's rows must be a multiple of 16");
     SMOE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0, SMOE_EARG, "a must be 16-byte aligned");
     SMOE_REQUIRE((reinterpret_cast<uintptr_t>(blocks) & 15) == 0, SMOE_EARG, "blocks must be 16-byte aligned");
@@ -636,6 +682,9 @@ extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts
         g.end = blocks + experts * rows * row_bytes;
         g.a = static_cast<const __half*>(a);
         g.out = out;
+        g.out16 = out16;
+        g.slot_row = slot_row;
+        g.out_rows = out_rows;
         g.hdr = static_cast<const GemmPlanHeader*>(workspace);
         g.runs = reinterpret_cast<const TileRun*>(static_cast<uint8_t*>(workspace) + sizeof(GemmPlanHeader));
         g.status = &static_cast<GemmPlanHeader*>(workspace)->status;
@@ -663,7 +712,7 @@ extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts
         g.q = 16 / gcd;
         g.region_bytes = (kGmM / g.q) * rawb;
         GemmMaps maps;
-        if (int e = encode_maps(&maps, blocks, experts * rows, row_bytes, g.q, rawb, a, p16, cols)) return e;
+        if (int e = encode_maps(&maps, blocks, experts * rows, row_bytes, g.q, rawb, a, a_rows, cols)) return e;
         gemm_plan_kernel<<<1, 1024, 0, st>>>(tile_expert, ntiles, experts, static_cast<GemmPlanHeader*>(workspace),
                                              const_cast<TileRun*>(g.runs));
         if (int s = launch_status("tile_matmul plan")) return s;
@@ -687,6 +736,8 @@ extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts
         if (status) return status;
         return launch_status("tile_matmul");
     }
+    SMOE_REQUIRE(out != nullptr && a_rows == p16, SMOE_EDTYPE,
+                 "tile_matmul_rows takes float16 activations and columns a multiple of 256");
     SMOE_REQUIRE(a_dtype == SMOE_F16 || a_dtype == SMOE_F32, SMOE_EDTYPE, "a must be float16 or float32");
     SMOE_REQUIRE(ntiles <= 65535, SMOE_ESHAPE, "too many tiles for one tile_matmul call");
     dim3 grid(static_cast<unsigned>((rows + 7) / 8), static_cast<unsigned>(ntiles));
@@ -701,4 +752,36 @@ extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts
     });
     if (status) return fail(status, "block type has no decoder");
     return launch_status("tile_matmul simt");
+}
+
+extern "C" int smoe_tile_matmul(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
+                                const void* a, int a_dtype, int64_t p16, const uint32_t* tile_expert, float* out,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+    return tile_matmul_impl(kind, blocks, experts, rows, cols, a, a_dtype, p16, p16, tile_expert, out, nullptr, nullptr,
+                            0, workspace, workspace_bytes, stream);
+}
+
+extern "C" int smoe_tile_matmul_rows(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
+                                     const void* a, int64_t a_rows, int64_t p16, const uint32_t* tile_expert,
+                                     const uint32_t* slot_row, int64_t out_rows, void* out, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    if (p16 == 0) return SMOE_OK;
+    SMOE_REQUIRE(out != nullptr && out_rows >= 0, SMOE_EARG, "null output");
+    SMOE_REQUIRE(cols % kGmKStage == 0, SMOE_ESHAPE, "tile_matmul_rows takes columns a multiple of 256");
+    SMOE_REQUIRE((reinterpret_cast<uintptr_t>(out) & 1) == 0, SMOE_EARG, "out must be 2-byte aligned");
+    return tile_matmul_impl(kind, blocks, experts, rows, cols, a, SMOE_F16, a_rows, p16, tile_expert, nullptr,
+                            static_cast<__half*>(out), slot_row, out_rows, workspace, workspace_bytes, stream);
+}
+
+extern "C" int smoe_slot_rows(const uint32_t* where, int64_t pairs, int64_t slots, uint32_t* slot_row, void* stream) {
+    if (slots == 0) return SMOE_OK;
+    SMOE_REQUIRE(where && slot_row && pairs >= 0 && slots > 0, SMOE_EARG, "null pointer or negative size");
+    cudaStream_t st = as_stream(stream);
+    if (cudaMemsetAsync(slot_row, 0xff, size_t(slots) * sizeof(uint32_t), st) != cudaSuccess)
+        return launch_status("slot_rows");
+    if (pairs > 0) {
+        const unsigned grid = static_cast<unsigned>(std::min<int64_t>((pairs + 255) / 256, 148 * 8));
+        slot_rows_kernel<<<grid, 256, 0, st>>>(where, pairs, slots, slot_row);
+    }
+    return launch_status("slot_rows");
 }

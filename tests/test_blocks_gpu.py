@@ -159,6 +159,45 @@ def test_half_precision_activations_come_back_as_half(cuda):
     assert (out.float() - want).abs().max().item() <= 2e-3 * want.abs().max().item()
 
 
+@pytest.mark.parametrize("kind", ["Q2_K", "IQ3_S", "Q8_0", "Q4_K", "IQ4_XS"])
+def test_the_rows_variant_is_the_tile_product_read_back(cuda, kind):
+    """smoe_tile_matmul_rows: the tiled path's `product(down, h)[where].astype(x.dtype)`
+    (strata_mlx/blocks.py:693) in one launch gives the same bits as the product then the read-back; a dense
+    layer's tokens without padding rows the same bits as padded; smoe_swiglu_to the bits of the float32
+    SwiGLU then the cast (blocks.py:692)."""
+    rng = np.random.default_rng(11)
+    E, rows, cols, T, k = 6, 256, 512, 45, 4
+    b, _ = stack(kind, rng, E, rows, cols)
+    blocks = dev(b)
+    idx = dev(rng.choice(E, (T, k), replace=True).astype(np.int32))
+    tiles, token, where = B.tiles_of(idx, E)
+    x = dev(rng.standard_normal((T, cols)).astype(np.float16))
+    a = x.index_select(0, token.view(torch.int32))
+    want = B.tile_matmul(blocks, kind, (E, rows, cols), a, tiles).index_select(0, where.view(torch.int32)).half()
+    got = B.tile_matmul_rows(blocks, kind, (E, rows, cols), a, tiles, B.slot_rows(where, a.shape[0]), T * k)
+    assert torch.equal(got, want)
+    # a dense layer: expert 0 for every tile, 45 tokens in 3 tiles without padding rows
+    te = torch.zeros(3, dtype=torch.int32, device="cuda")
+    padded = torch.cat([x, x.new_zeros(3 * 16 - T, cols)])
+    want = B.tile_matmul(blocks, kind, (E, rows, cols), padded, te)[:T].half()
+    got = B.tile_matmul_rows(blocks, kind, (E, rows, cols), x, te, None, T)
+    assert torch.equal(got, want)
+    g32, u32 = (dev(rng.standard_normal((T, rows)).astype(np.float32)) for _ in range(2))
+    assert torch.equal(B.swiglu_to(g32, u32, torch.float16), B.swiglu(g32, u32).half())
+
+
+def test_slot_rows_inverts_where(cuda):
+    """smoe_slot_rows: slot where[p] holds p, every other slot 0xffffffff."""
+    rng = np.random.default_rng(12)
+    idx = dev(rng.choice(9, (31, 3), replace=True).astype(np.int32))
+    tiles, token, where = B.tiles_of(idx, 9)
+    inv = B.slot_rows(where, token.numel()).view(torch.int32).cpu().numpy().astype(np.uint32)
+    w = where.view(torch.int32).cpu().numpy().astype(np.int64)
+    want = np.full(token.numel(), 0xFFFFFFFF, dtype=np.uint64)
+    want[w] = np.arange(w.size)
+    np.testing.assert_array_equal(inv.astype(np.uint64), want)
+
+
 @pytest.mark.parametrize("kind", KINDS)
 @pytest.mark.parametrize("dtype", [np.float16, np.float32])
 def test_the_tile_product_is_the_product_with_the_weights(cuda, kind, dtype):
