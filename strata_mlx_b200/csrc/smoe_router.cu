@@ -1,5 +1,7 @@
 // The router's product, its top-k choice with the softmax over the chosen, and the combine at the end of the
 // MoE block.
+#include <type_traits>
+
 #include "router_dev.cuh"
 
 namespace smoe {
@@ -128,12 +130,32 @@ __global__ void __launch_bounds__(256) route_kernel(const __half* __restrict__ w
 // quarter's lanes are added by warp_sum's shuffle tree and the four quarters in order. Only the mapping differs:
 // a warp takes one quarter of kPrRows rows x kPrTok tokens, so a lane's chunk of a weight row serves kPrTok
 // tokens and its chunk of a token kPrRows rows from registers; a CTA's 8 warps are the four quarters of two
-// token halves (kPrRows rows x 2 kPrTok tokens). Against route_kernel (2 rows x 8 tokens a CTA, every chunk of x
-// loaded once per row) a prompt chunk reads about a third of the bytes from L2 and issues a quarter of the
-// loads a multiply-add. The last CTA of a token group takes the group's top-k (counters: one word per 16
-// tokens, within smoe_route_counters' size); without counters the launch writes only the logits.
+// token halves (kPrRows rows x 2 kPrTok tokens), small enough in registers for five CTAs an SM: the kernel is
+// bound by the latency of its loads, not by L2 bandwidth. Float16 activations multiply as they are (no
+// conversions). The last CTA of a group of 8 tokens takes the group's top-k (counters: one word per 8 tokens,
+// smoe_route_counters' size); without counters the launch writes only the logits.
 
-constexpr int kPrRows = 4, kPrTok = 8;
+constexpr int kPrRows = 4, kPrTok = 4;
+// a counter word covers 8 tokens (smoe_route_counters' size): the CTAs of those tokens count on it
+constexpr int kPrGroup = kRtTokens, kPrCtasPerGroup = kPrGroup / (2 * kPrTok);
+static_assert(kPrGroup % (2 * kPrTok) == 0, "a counter's tokens are whole CTAs' tokens");
+
+// the eight float16 values of a 16-byte chunk, in order
+__device__ __forceinline__ void split8(const uint4 q, unsigned short (&h)[8]) {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        h[2 * i] = static_cast<unsigned short>(w[i] & 0xffffu);
+        h[2 * i + 1] = static_cast<unsigned short>(w[i] >> 16);
+    }
+}
+
+// acc + w x as one float32 fused multiply-add of two float16 values (mixed precision: fmaf of the values widened
+// to float32, which is exact)
+__device__ __forceinline__ float fma_h(unsigned short w, unsigned short x, float acc) {
+    asm("fma.rn.f32.f16 %0, %1, %2, %0;" : "+f"(acc) : "h"(w), "h"(x));
+    return acc;
+}
 constexpr int64_t kPrFrom = 32;  // windows of more tokens than this take route_chunk_kernel
 
 template <typename XT, int NV>
@@ -168,6 +190,30 @@ __global__ void __launch_bounds__(256) route_chunk_kernel(const __half* __restri
     pdl_wait();
     pdl_release();
     const int64_t chunks = hidden >> 3;
+    if constexpr (std::is_same<XT, __half>::value) {
+        // float16 activations: fma.rn.f32.f16 takes both float16 operands as they are (their float32 values are
+        // exact, so each step is fmaf(float(w), float(x), acc), router_rows' step) with no conversions
+#pragma unroll 2
+        for (int64_t c = quarter * 32 + lane; c < chunks; c += 128) {
+            unsigned short wh[kPrRows][8];
+#pragma unroll
+            for (int r = 0; r < kPrRows; ++r) {
+                const uint4 q = live[r] ? *reinterpret_cast<const uint4*>(rp[r] + 8 * c) : make_uint4(0u, 0u, 0u, 0u);
+                split8(q, wh[r]);
+            }
+#pragma unroll
+            for (int t = 0; t < kPrTok; ++t) {
+                if (t < nt) {
+                    unsigned short xh[8];
+                    split8(*reinterpret_cast<const uint4*>(x + (t0 + t) * hidden + 8 * c), xh);
+#pragma unroll
+                    for (int r = 0; r < kPrRows; ++r)
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) acc[r][t] = fma_h(wh[r][j], xh[j], acc[r][t]);
+                }
+            }
+        }
+    } else {
 #pragma unroll 2
     for (int64_t c = quarter * 32 + lane; c < chunks; c += 128) {
         float wv[kPrRows][8];
@@ -191,6 +237,7 @@ __global__ void __launch_bounds__(256) route_chunk_kernel(const __half* __restri
                     for (int j = 0; j < 8; ++j) acc[r][t] = fmaf(wv[r][j], xv[j], acc[r][t]);
             }
         }
+    }
     }
 #pragma unroll
     for (int r = 0; r < kPrRows; ++r)
@@ -216,15 +263,17 @@ __global__ void __launch_bounds__(256) route_chunk_kernel(const __half* __restri
         }
     }
     if (counters == nullptr) return;
-    // the last CTA of this token group to finish takes the group's top-k, a warp to two tokens
+    // the last CTA of this group of 8 tokens to finish takes the group's top-k, a warp to a token
+    const unsigned grp = blockIdx.y / kPrCtasPerGroup;
+    const unsigned ys = min(unsigned(kPrCtasPerGroup), gridDim.y - grp * kPrCtasPerGroup);  // the group's rows of CTAs
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) last = atomicAdd(&counters[blockIdx.y], 1u) == gridDim.x - 1;
+    if (threadIdx.x == 0) last = atomicAdd(&counters[grp], 1u) == gridDim.x * ys - 1;
     __syncthreads();
     if (!last) return;
     __threadfence();
-    for (int tt = warp; tt < 2 * kPrTok; tt += 8) {
-        const int64_t t = tg0 + tt;
+    for (int tt = warp; tt < kPrGroup; tt += 8) {
+        const int64_t t = int64_t(grp) * kPrGroup + tt;
         if (t >= tokens) break;
         const float* in = logits + t * experts;
         topk_row<NV>([&](int j) { return __ldcg(in + j); }, static_cast<int>(experts), k, idx + t * k, weights + t * k);
@@ -237,7 +286,7 @@ __global__ void __launch_bounds__(256) route_chunk_kernel(const __half* __restri
         }
         __syncwarp();
     }
-    if (threadIdx.x == 0) counters[blockIdx.y] = 0u;
+    if (threadIdx.x == 0) counters[grp] = 0u;
 }
 
 // ---------------------------------------------------------------- combine
