@@ -385,7 +385,32 @@ def run_config1(device, seed, steps=200, cpu_steps=3):
         lin(x, idxs[(37 * i) % experts])
     e1.record()
     torch.cuda.synchronize()
-    gpu_us = e0.elapsed_time(e1) / steps * 1e3
+    eager_us = e0.elapsed_time(e1) / steps * 1e3
+    # the same launches replayed from a CUDA graph: the product's own latency without the host's per-call
+    # Python work; 96 different experts a graph (260 MB, more than L2), so every replay reads them from HBM
+    per_graph = 96
+    seq = [idxs[(37 * i) % experts] for i in range(per_graph)]
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for idx in seq:
+            lin(x, idx)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        for idx in seq:
+            lin(x, idx)
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    reps = max(1, steps // per_graph)
+    e0.record()
+    for _ in range(reps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    gpu_us = e0.elapsed_time(e1) / (reps * per_graph) * 1e3
+    del graph
     mbytes = rows * B.row_bytes(KIND, cols)
     # the CPU: one expert's blocks decoded and multiplied, then the product alone
     blocks = b[: rows * cols // per].cpu().numpy().reshape(-1)
@@ -406,7 +431,10 @@ def run_config1(device, seed, steps=200, cpu_steps=3):
         prod_s = (time.perf_counter() - t0) / 50
     return {"workload": "config 1: one expert's matvec, W [1536 x 4096] IQ3_S blocks, x float16 [4096]",
             "gpu_us_per_matvec": gpu_us, "gpu_gbs": mbytes / (gpu_us * 1e-6) / 1e9,
-            "gpu_note": "one launch per matvec (its latency included), a different expert of a 692 MB stack each",
+            "gpu_note": "one launch per matvec (its latency included), a different expert of a 692 MB stack each, "
+                        "replayed from a CUDA graph of 96 such launches",
+            "gpu_us_per_matvec_eager": eager_us,
+            "eager_note": "the same calls one at a time from Python (BlockSwitchLinear.__call__), host work included",
             "cpu_ms_decode_and_product": cpu_s * 1e3, "cpu_ms_product_only": prod_s * 1e3,
             "cpu_threads": os.cpu_count(), "bytes_per_matvec": mbytes}
 
