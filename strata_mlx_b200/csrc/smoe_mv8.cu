@@ -61,6 +61,7 @@ struct M8Args {
     int jobs;       // nprob * pairs * tiles
     int team;       // warps per job: 1, 2, 4, 8 or 16
     int xrows;      // activation rows (pairs / share)
+    int xwin;       // activation rows a CTA holds: its jobs' rows from the first one's on (<= xrows)
     int nslots;     // ring slots per warp
     // when cy is set, the product is the shared expert's down and out[0] receives the block's combine instead:
     // out[t, r] = half(sum_j cy[t, j, r] cw[t, j]) + half(half(sigmoid(cg[t])) half(product[t, r])) (pair t is
@@ -102,10 +103,11 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     uint32_t* need = reinterpret_cast<uint32_t*>(spare + kM8WhereSBytes - kM8SMaskRows / 8);  // kM8SMaskRows bits
     uint32_t* lut = reinterpret_cast<uint32_t*>(spare + kM8WhereSBytes);        // 512 x 16 words
     const int xblocks = static_cast<int>(a.cols / kM8XBlock);
-    float* xscale = reinterpret_cast<float*>(lut + (D::kLut ? 8192 : 0));        // [xrows][xblocks]
-    int8_t* xhi = reinterpret_cast<int8_t*>(xscale + ((a.xrows * xblocks + 3) & ~3));  // [xrows][cols]
-    int8_t* xlo = xhi + size_t(a.xrows) * a.cols;
-    float* xsum = reinterpret_cast<float*>(xlo + size_t(a.xrows) * a.cols);  // [xrows][cols / 16] (the K-types)
+    // the activation rows xr_lo .. xr_lo + xwin - 1 (row xr at xr - xr_lo)
+    float* xscale = reinterpret_cast<float*>(lut + (D::kLut ? 8192 : 0));        // [xwin][xblocks]
+    int8_t* xhi = reinterpret_cast<int8_t*>(xscale + ((a.xwin * xblocks + 3) & ~3));  // [xwin][cols]
+    int8_t* xlo = xhi + size_t(a.xwin) * a.cols;
+    float* xsum = reinterpret_cast<float*>(xlo + size_t(a.xwin) * a.cols);  // [xwin][cols / 16] (the K-types)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int gid = lane >> 2, tig = lane & 3;
@@ -119,11 +121,24 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     // takes every teams-th of them from the i-th on (at most 32: one per lane of the warp's job table)
     const int cj0 = static_cast<int>(int64_t(blockIdx.x) * a.jobs / gridDim.x);
     const int cj1 = static_cast<int>(int64_t(blockIdx.x + 1) * a.jobs / gridDim.x);
-    const int q0 = cj0 + tid_team;
-    const int my_jobs = q0 < cj1 ? min((cj1 - q0 + teams - 1) / teams, 32) : 0;
     const int tok = a.tok;
     const int units = static_cast<int>((a.pairs + tok - 1) / tok);  // a job's pairs: [unit tok, unit tok + tok)
     const int per_prob = units * a.tiles;  // < 2^30 (the host checks)
+    // a window of the activation rows (xwin < xrows, one problem): the CTA's jobs are consecutive, so their rows
+    // run from its first job's to its last job's, which the host sized xwin for (checked here once: a CTA
+    // whose rows would not fit records SMOE_ESHAPE and takes no job)
+    int xr_lo = 0;
+    bool window_ok = true;
+    if (a.xwin < a.xrows && cj0 < cj1) {
+        const int u0 = cj0 / a.tiles, u1 = (cj1 - 1) / a.tiles;
+        const int share = static_cast<int>(a.share);
+        xr_lo = tok == 1 ? u0 / share : u0 * tok;
+        const int xr_hi = tok == 1 ? u1 / share : min(u1 * tok + tok - 1, a.xrows - 1);
+        window_ok = a.jobs == per_prob && xr_hi - xr_lo < a.xwin;
+        if (!window_ok && threadIdx.x == 0) atomicExch(&g_mv8_status, SMOE_ESHAPE);
+    }
+    const int q0 = cj0 + tid_team;
+    const int my_jobs = q0 < cj1 && window_ok ? min((cj1 - q0 + teams - 1) / teams, 32) : 0;
     uint8_t* my_ring = ring + size_t(warp) * ns * kSlot;
     uint64_t* my_bars = bars + warp * kM8MaxSlots;
 
@@ -206,12 +221,13 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
     };
     // the activations, split per 256-column block into int8 hi and lo: a warp per block, 8 values a lane
     auto split = [&]() {
-        for (int blk = warp; blk < a.xrows * xblocks; blk += kM8Warps) {
-            const int xr = blk / xblocks, b = blk % xblocks;
+        for (int blk = warp; blk < a.xwin * xblocks; blk += kM8Warps) {
+            const int xw = blk / xblocks, b = blk % xblocks, xr = xr_lo + xw;
+            if (xr >= a.xrows) break;
             if (masked && !((need[xr >> 5] >> (xr & 31)) & 1u)) continue;
-            const int64_t at = int64_t(xr) * a.cols + int64_t(b) * kM8XBlock + 8 * lane;
-            m8_split(a.x, a.gate, a.up, at, xhi + at, xlo + at, xscale + blk, lane,
-                     D::kXsum ? xsum + (int64_t(xr) * a.cols + int64_t(b) * kM8XBlock) / 16 : nullptr);
+            const int64_t at = int64_t(xw) * a.cols + int64_t(b) * kM8XBlock + 8 * lane;
+            m8_split(a.x, a.gate, a.up, at + int64_t(xr_lo) * a.cols, xhi + at, xlo + at, xscale + blk, lane,
+                     D::kXsum ? xsum + (int64_t(xw) * a.cols + int64_t(b) * kM8XBlock) / 16 : nullptr);
         }
     };
     if (early_idx) {
@@ -247,7 +263,7 @@ __global__ void __launch_bounds__(kM8Threads, 1) mv8s_kernel(const M8Args a, con
         const int cls = __shfl_sync(0xffffffffu, j_cls, job);
         const int blk = __shfl_sync(0xffffffffu, j_blk, job);
         const int valid = __shfl_sync(0xffffffffu, j_valid, job);
-        const int xr = tok == 1 ? pair / static_cast<int>(a.share) : pair * tok;
+        const int xr = (tok == 1 ? pair / static_cast<int>(a.share) : pair * tok) - xr_lo;  // (in the window)
         const int nt = tok == 1 ? 1 : min(tok, static_cast<int>(a.pairs) - pair * tok);
         const uint8_t* xh = reinterpret_cast<const uint8_t*>(xhi) + int64_t(xr) * a.cols;
         const uint8_t* xl = reinterpret_cast<const uint8_t*>(xlo) + int64_t(xr) * a.cols;
@@ -780,11 +796,42 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         if (rows % q) return 1;
         const int64_t xrows = (pairs + share - 1) / share;
         const int xblocks = static_cast<int>(cols / kM8XBlock);
-        const size_t xbytes = size_t(((xrows * xblocks + 3) & ~int64_t(3)) * 4) + size_t(xrows * cols * 2) +
-                              (D::kXsum ? size_t(xrows * (cols / 16) * 4) : 0);
-        const size_t fixed = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 64 * 4 + kM8WhereSBytes +
-                             (D::kLut ? 8192 * 4 : 0) + xbytes;
+        // tokens a job takes: a one-expert stack's tokens (an activation row each) up to four a pass
+        const int tok = D::kTokens && experts == 1 && share == 1 && pairs > 1 ? 4 : 1;
+        // the activation rows a CTA holds: all of them when they fit beside two ring slots (one launch);
+        // else, with one problem, only the CTA's own: CTA b's jobs [b J / G, (b + 1) J / G) are consecutive, so
+        // their rows are those from its first job's to its last job's (two problems hold all: the callers then
+        // split the pairs over launches). (Holding the window where all rows fit measured slower at decode.)
         const size_t slot = size_t(kM8Warps) * 16 * D::kRS;
+        const size_t base = size_t(kM8Warps) * kM8MaxSlots * 8 + kM8Warps * 64 * 4 + kM8WhereSBytes +
+                            (D::kLut ? 8192 * 4 : 0);
+        const auto xbytes_of = [&](int64_t r) {
+            return size_t(((r * xblocks + 3) & ~int64_t(3)) * 4) + size_t(r * cols * 2) +
+                   (D::kXsum ? size_t(r * (cols / 16) * 4) : 0);
+        };
+        if (g_m8_sms == 0) {
+            int dev = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&g_m8_sms, cudaDevAttrMultiProcessorCount, dev);
+            if (g_m8_sms <= 0) g_m8_sms = 148;
+        }
+        const int64_t ntiles = (rows + 16 * q - 1) / (16 * q) * q;
+        const int64_t njobs = int64_t(nprob) * ((pairs + tok - 1) / tok) * ntiles;
+        int64_t xwin = xrows;
+        if (nprob == 1 && njobs > 0 && base + xbytes_of(xrows) + 2 * slot > size_t(227 * 1024)) {
+            const int64_t G = std::min<int64_t>(g_m8_sms, njobs);
+            xwin = 0;
+            for (int64_t b = 0; b < G; ++b) {
+                const int64_t c0 = b * njobs / G, c1 = (b + 1) * njobs / G;
+                if (c0 >= c1) continue;
+                const int64_t u0 = c0 / ntiles, u1 = (c1 - 1) / ntiles;
+                const int64_t lo = tok == 1 ? u0 / share : u0 * tok;
+                const int64_t hi = tok == 1 ? u1 / share : std::min(u1 * tok + tok - 1, xrows - 1);
+                xwin = std::max(xwin, hi - lo + 1);
+            }
+            xwin = std::min(std::max<int64_t>(xwin, 1), xrows);
+        }
+        const size_t fixed = base + xbytes_of(xwin);
         int ns = kM8MaxSlots;
         while (ns > 2 && fixed + ns * slot > size_t(227 * 1024)) --ns;
         if (fixed + ns * slot > size_t(227 * 1024)) return 1;
@@ -819,13 +866,14 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
         a.q = q;
         a.lq = q == 1 ? 0 : q == 2 ? 1 : q == 4 ? 2 : q == 8 ? 3 : 4;
         a.tiles = static_cast<int>((rows + 16 * q - 1) / (16 * q)) * q;
-        a.tok = D::kTokens && experts == 1 && share == 1 && pairs > 1 ? 4 : 1;
+        a.tok = tok;
         const int64_t jobs = int64_t(nprob) * ((pairs + a.tok - 1) / a.tok) * a.tiles;
         if (jobs > (int64_t(1) << 30) || xrows > (int64_t(1) << 20) || experts * rows / q >= (int64_t(1) << 31) ||
             q * row_bytes >= (int64_t(1) << 27))
             return 1;
         a.jobs = static_cast<int>(jobs);
         a.xrows = static_cast<int>(xrows);
+        a.xwin = static_cast<int>(xwin);
         a.nslots = ns;
         a.cy = cy;
         a.cw = cw;
