@@ -5,6 +5,8 @@
 // activation row is staged once in shared memory as float32; each warp streams its rows' bytes into its own
 // shared-memory slots with 16-byte cp.async copies (coalesced, all issued up front so every warp has several
 // KB in flight), then its lanes decode runs of 32 weights in registers and reduce with warp shuffles.
+#include <type_traits>
+
 #include "blocks.cuh"
 #include "mv8.cuh"
 
@@ -408,6 +410,36 @@ __global__ void swiglu_to_half_kernel(const float* __restrict__ g, const float* 
         out[i] = __float2half_rn(swiglu_one(g[i], u[i]));
 }
 
+// the two above eight values a thread (n a multiple of 8, 16-byte aligned), in 16-byte loads and stores
+template <typename T, typename O>
+__global__ void swiglu8_kernel(const T* __restrict__ g, const T* __restrict__ u, int64_t n, O* __restrict__ out) {
+    constexpr int kVec = 16 / sizeof(T);  // values a 16-byte load holds
+    for (int64_t i = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) * 8; i < n;
+         i += int64_t(gridDim.x) * blockDim.x * 8) {
+        T gv[8], uv[8];
+#pragma unroll
+        for (int c = 0; c < 8 / kVec; ++c) {
+            *reinterpret_cast<uint4*>(gv + c * kVec) = *reinterpret_cast<const uint4*>(g + i + c * kVec);
+            *reinterpret_cast<uint4*>(uv + c * kVec) = *reinterpret_cast<const uint4*>(u + i + c * kVec);
+        }
+        O ov[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const T h = swiglu_one(gv[e], uv[e]);
+            if constexpr (std::is_same<O, T>::value) ov[e] = h;
+            else ov[e] = __float2half_rn(h);
+        }
+#pragma unroll
+        for (int c = 0; c < int(8 * sizeof(O)) / 16; ++c)
+            *reinterpret_cast<uint4*>(out + i + c * (16 / sizeof(O))) = *reinterpret_cast<const uint4*>(ov + c * (16 / sizeof(O)));
+    }
+}
+
+static bool aligned8(int64_t n, const void* a, const void* b, const void* c) {
+    return n % 8 == 0 && ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                           reinterpret_cast<uintptr_t>(c)) & 15) == 0;
+}
+
 // ---------------------------------------------------------------- host side
 
 // the float16 tensor-core decode matvec (smoe_mv.cu), for what the int8 one does not take
@@ -726,6 +758,12 @@ extern "C" int smoe_swiglu_to(const void* gate, const void* up, int64_t n, int d
     SMOE_REQUIRE(gate && up && out && n > 0, SMOE_EARG, "null pointer or negative size");
     SMOE_REQUIRE(dtype == SMOE_F32 && out_dtype == SMOE_F16, SMOE_EDTYPE,
                  "swiglu_to takes float32 gate and up to float16, or one type throughout");
+    if (aligned8(n, gate, up, out)) {
+        const unsigned grid8 = static_cast<unsigned>(std::min<int64_t>((n / 8 + 255) / 256, 148 * 16));
+        swiglu8_kernel<float, __half><<<grid8, 256, 0, as_stream(stream)>>>(
+            static_cast<const float*>(gate), static_cast<const float*>(up), n, static_cast<__half*>(out));
+        return launch_status("swiglu_to");
+    }
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 148 * 16));
     swiglu_to_half_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<const float*>(gate),
                                                                static_cast<const float*>(up), n, static_cast<__half*>(out));
@@ -736,8 +774,15 @@ extern "C" int smoe_swiglu(const void* gate, const void* up, int64_t n, void* ou
     if (n == 0) return SMOE_OK;
     SMOE_REQUIRE(gate && up && out && n > 0, SMOE_EARG, "null pointer or negative size");
     const unsigned grid = static_cast<unsigned>(std::min<int64_t>((n + 255) / 256, 148 * 16));
+    const unsigned grid8 = static_cast<unsigned>(std::min<int64_t>((n / 8 + 255) / 256, 148 * 16));
     cudaStream_t st = as_stream(stream);
-    if (dtype == SMOE_F16)
+    if (dtype == SMOE_F16 && aligned8(n, gate, up, out))
+        swiglu8_kernel<__half, __half><<<grid8, 256, 0, st>>>(static_cast<const __half*>(gate),
+                                                              static_cast<const __half*>(up), n, static_cast<__half*>(out));
+    else if (dtype == SMOE_F32 && aligned8(n, gate, up, out))
+        swiglu8_kernel<float, float><<<grid8, 256, 0, st>>>(static_cast<const float*>(gate),
+                                                            static_cast<const float*>(up), n, static_cast<float*>(out));
+    else if (dtype == SMOE_F16)
         swiglu_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(gate), static_cast<const __half*>(up), n,
                                                    static_cast<__half*>(out));
     else if (dtype == SMOE_F32)

@@ -186,6 +186,27 @@ def test_the_rows_variant_is_the_tile_product_read_back(cuda, kind):
     assert torch.equal(B.swiglu_to(g32, u32, torch.float16), B.swiglu(g32, u32).half())
 
 
+@pytest.mark.parametrize("dtype", [np.float16, np.float32])
+def test_swiglu_eight_a_thread_is_the_one_a_thread(cuda, dtype):
+    """smoe_swiglu / smoe_swiglu_to: the eight-wide kernels (aligned, a multiple of 8 values) give each value the
+    bits of the one-value kernels (an odd offset takes those); float16 within one float16 step of the oracle's
+    (strata_mlx/blocks.py:222-237; its float32 exp is numpy's)."""
+    rng = np.random.default_rng(21)
+    n = 4096 * 3 + 8
+    g = dev((2 * rng.standard_normal(n + 1)).astype(dtype))
+    u = dev((2 * rng.standard_normal(n + 1)).astype(dtype))
+    wide = B.swiglu(g[1:].clone(), u[1:].clone())
+    one = B.swiglu(g[1:], u[1:])
+    assert torch.equal(wide, one)
+    if dtype == np.float16:
+        want = M.swiglu(g[1:].cpu().numpy(), u[1:].cpu().numpy()).astype(np.float32)
+        got = wide.cpu().numpy().astype(np.float32)
+        assert np.all(np.abs(got - want) <= 2.0 ** -10 * np.maximum(np.abs(want), 2.0 ** -14))
+    else:
+        assert torch.equal(B.swiglu_to(g[1:].clone(), u[1:].clone(), torch.float16), one.half())
+        assert torch.equal(B.swiglu_to(g[1:], u[1:], torch.float16), one.half())
+
+
 def test_slot_rows_inverts_where(cuda):
     """smoe_slot_rows: slot where[p] holds p, every other slot 0xffffffff."""
     rng = np.random.default_rng(12)

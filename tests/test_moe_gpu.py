@@ -84,7 +84,7 @@ def test_the_routers_choice_is_argpartitions(cuda, tokens, ties, n, k):
 
 
 @pytest.mark.parametrize("tokens", [1, 3, 8, 16, 40])
-@pytest.mark.parametrize("k, d", [(10, 2560), (8, 4096)])
+@pytest.mark.parametrize("k, d", [(10, 2560), (8, 4096), (8, 1028)])
 def test_the_end_of_the_moe_block_is_the_restated_bits(cuda, tokens, k, d):
     """tests/test_fused.py:124-138: bit-equal to (y * w).sum(-2).astype(half) + sigmoid(g) * s in MLX's order."""
     rng = np.random.default_rng(tokens)
