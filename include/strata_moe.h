@@ -400,6 +400,21 @@ SMOE_API int smoe_tile_matmul_rows(int kind, const uint8_t* blocks, int64_t expe
                                    const uint32_t* slot_row, int64_t out_rows, void* out, void* workspace,
                                    size_t workspace_bytes, void* stream);
 
+/* Two stacks of the same type and shape (a layer's gate and up) through the same tiles and activations in one
+ * launch: out_a from blocks_a, out_b from blocks_b, each as smoe_tile_matmul gives it (float32, slot order) or,
+ * the _rows form, as smoe_tile_matmul_rows gives it (float16 at slot_row's rows). Float16 activations and cols a
+ * multiple of 256 (SMOE_EARG otherwise). Replaces the reference's two `product(gate, a)`, `product(up, a)` calls
+ * of the tiled path (strata_mlx/blocks.py:690-692); one launch has one tail where two had two. Workspace as
+ * smoe_tile_matmul's. */
+SMOE_API int smoe_tile_matmul_pair(int kind, const uint8_t* blocks_a, const uint8_t* blocks_b, int64_t experts,
+                                   int64_t rows, int64_t cols, const void* a, int64_t p16, const uint32_t* tile_expert,
+                                   float* out_a, float* out_b, void* workspace, size_t workspace_bytes, void* stream);
+SMOE_API int smoe_tile_matmul_pair_rows(int kind, const uint8_t* blocks_a, const uint8_t* blocks_b, int64_t experts,
+                                        int64_t rows, int64_t cols, const void* a, int64_t a_rows, int64_t p16,
+                                        const uint32_t* tile_expert, const uint32_t* slot_row, int64_t out_rows,
+                                        void* out_a, void* out_b, void* workspace, size_t workspace_bytes,
+                                        void* stream);
+
 /* slot_row[s] = p for the pair p with where[p] = s (smoe_tiles_of's `where` inverted), 0xffffffff for slots no
  * pair fills: the map smoe_tile_matmul_rows takes to write a tiled product in pair order. slots entries. */
 SMOE_API int smoe_slot_rows(const uint32_t* where, int64_t pairs, int64_t slots, uint32_t* slot_row, void* stream);

@@ -116,13 +116,16 @@ SIGNATURES = {
     "smoe_tile_matmul": (_i, [_i, _p, _i64, _i64, _i64, _p, _i, _i64, _p, _p, _p, _sz, _p]),
     "smoe_tile_matmul_rows": (_i, [_i, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _p, _p, _sz, _p]),
     "smoe_slot_rows": (_i, [_p, _i64, _i64, _p, _p]),
+    "smoe_tile_matmul_pair": (_i, [_i, _p, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _p, _p, _sz, _p]),
+    "smoe_tile_matmul_pair_rows": (_i, [_i, _p, _p, _i64, _i64, _i64, _p, _i64, _i64, _p, _p, _i64, _p, _p, _p, _sz,
+                                        _p]),
 }
 
 _lib = None
 
 # kernels each entry point launches (for the benchmark's launch count); 1 where not named
 KERNELS_PER_CALL = {"smoe_tiles_of": 2, "smoe_tiles_of_noalloc": 2, "smoe_tile_matmul": 2, "smoe_tile_matmul_rows": 2,
-                    "smoe_ep_dispatch": 2,
+                    "smoe_tile_matmul_pair": 2, "smoe_tile_matmul_pair_rows": 2, "smoe_ep_dispatch": 2,
                     "smoe_ep_exchange_alloc": 0, "smoe_ep_exchange_open": 0, "smoe_ep_exchange_close": 0,
                     "smoe_ep_exchange_free": 0, "smoe_ep_exchange_status": 0, "smoe_decode_layer_status": 0, "smoe_decode_layer_wait_test": 0,
                     "smoe_matvec_status": 0, "smoe_matvec_wait_test": 0, "smoe_hyper_connection": 3}

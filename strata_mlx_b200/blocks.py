@@ -265,6 +265,42 @@ def tile_matmul_rows(blocks: torch.Tensor, kind: str, shape: tuple, a: torch.Ten
     return out
 
 
+def tile_matmul_pair(lin_a, lin_b, a: torch.Tensor, tile_expert: torch.Tensor, slot_row=None, out_rows=None):
+    """Two stacks of one type and shape (a layer's gate and up) through the same tiles and activations in one
+    launch: `tile_matmul` of each (float32, slot order), or with `out_rows` the rows form of each
+    (`tile_matmul_rows`: float16, row slot_row[s] or s). `a` float16, cols a multiple of 256."""
+    _lib.require_cuda(lin_a.blocks, lin_b.blocks, a, tile_expert)
+    experts, rows, cols = lin_a.shape
+    te = tile_expert.reshape(-1).contiguous()
+    if te.dtype not in (torch.int32, torch.uint32):
+        te = te.to(torch.int32)
+    p16 = te.numel() * TOKENS_TILE
+    a = a.contiguous()
+    ws = torch.empty(int(_lib.lib().smoe_tile_matmul_workspace_size(p16)), dtype=torch.uint8, device=a.device)
+    if out_rows is None:
+        if a.shape[0] != p16:
+            raise ValueError("a's rows must be TOKENS_TILE per entry of tile_expert")
+        outs = [torch.empty((p16, rows), dtype=torch.float32, device=a.device) for _ in range(2)]
+        _lib.call("smoe_tile_matmul_pair", _kind(lin_a.kind), _lib.ptr(lin_a.blocks), _lib.ptr(lin_b.blocks), experts,
+                  rows, cols, _lib.ptr(a), p16, _lib.ptr(te), _lib.ptr(outs[0]), _lib.ptr(outs[1]), _lib.ptr(ws),
+                  ws.numel(), _lib.stream())
+    else:
+        if not 0 < a.shape[0] <= p16:
+            raise ValueError("a holds 1 to TOKENS_TILE rows per tile")
+        outs = [torch.empty((out_rows, rows), dtype=torch.float16, device=a.device) for _ in range(2)]
+        _lib.call("smoe_tile_matmul_pair_rows", _kind(lin_a.kind), _lib.ptr(lin_a.blocks), _lib.ptr(lin_b.blocks),
+                  experts, rows, cols, _lib.ptr(a), a.shape[0], p16, _lib.ptr(te),
+                  _lib.ptr(slot_row) if slot_row is not None else None, out_rows, _lib.ptr(outs[0]),
+                  _lib.ptr(outs[1]), _lib.ptr(ws), ws.numel(), _lib.stream())
+    return outs[0], outs[1]
+
+
+def pair_takes(lin_a, lin_b, dtype) -> bool:
+    """Whether tile_matmul_pair takes these two stacks with activations of `dtype`."""
+    return (lin_a.kind == lin_b.kind and tuple(lin_a.shape) == tuple(lin_b.shape)
+            and rows_take(lin_a.kind, lin_a.shape[2], dtype))
+
+
 def slot_rows(where: torch.Tensor, slots: int) -> torch.Tensor:
     """The inverse of tiles_of's `where`: slot s -> the pair in it, 0xffffffff for slots no pair fills."""
     _lib.require_cuda(where)
@@ -344,7 +380,11 @@ def _tiled_glu(x: torch.Tensor, indices: torch.Tensor, up, gate, down) -> torch.
     if x.dtype == torch.float16 and rows_take(down.kind, down.input_dims, x.dtype):
         # the same values in fewer passes: the SwiGLU of the float32 sums rounded once to float16, and the down
         # product written in pair order as float16 by its own launch
-        h = swiglu_to(product(gate, a), product(up, a), x.dtype)
+        if pair_takes(gate, up, x.dtype):
+            g32, u32 = tile_matmul_pair(gate, up, a, tiles)
+        else:
+            g32, u32 = product(gate, a), product(up, a)
+        h = swiglu_to(g32, u32, x.dtype)
         out = tile_matmul_rows(down.blocks, down.kind, down.shape, h, tiles, slot_rows(where, h.shape[0]),
                                where.numel())
         return out.reshape(*indices.shape, down.output_dims)
@@ -599,8 +639,15 @@ class BlockMLP:
         x2 = x.reshape(-1, x.shape[-1]).contiguous()
         if all(p.gemm(x2) for p in (self.gate_proj, self.up_proj, self.down_proj)):
             # a prompt's chunk: the three products on the tensor cores, rounded to x's type as QuantizedLinear does
-            g = _dense_tiles(self.gate_proj.stack, x2, x.dtype)
-            u = _dense_tiles(self.up_proj.stack, x2, x.dtype)
+            gs, us = self.gate_proj.stack, self.up_proj.stack
+            if x.dtype == torch.float16 and pair_takes(gs, us, x2.dtype):
+                # gate and up in one launch (one-expert stacks: tiles of expert 0, no padding rows)
+                tokens = x2.shape[0]
+                te = _zeros_idx((tokens + TOKENS_TILE - 1) // TOKENS_TILE, x2.device)
+                g, u = tile_matmul_pair(gs, us, x2, te, None, tokens)
+            else:
+                g = _dense_tiles(gs, x2, x.dtype)
+                u = _dense_tiles(us, x2, x.dtype)
             out = _dense_tiles(self.down_proj.stack, swiglu(g, u), x.dtype)
             return out.reshape(*x.shape[:-1], self.down_proj.output_dims)
         idx = _zeros_idx(x2.shape[0], x.device)

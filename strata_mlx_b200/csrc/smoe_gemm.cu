@@ -156,6 +156,11 @@ struct GemmArgs {
     __half* out16;
     const uint32_t* slot_row;
     int64_t out_rows;
+    // a pair (blocks2 set): the same tiles and activations through a second stack of the same type and shape,
+    // its jobs after the first stack's, its results in out2 / out16_2 as the first's go to out / out16
+    const uint8_t* blocks2;
+    float* out2;
+    __half* out16_2;
     const GemmPlanHeader* hdr;
     const TileRun* runs;
     int* status;
@@ -173,7 +178,21 @@ struct GemmArgs {
 struct alignas(64) GemmMaps {
     CUtensorMap w;
     CUtensorMap a[4];
+    CUtensorMap w2;  // a pair's second stack
 };
+
+// job -> its run of tiles, first weight row and stack: the first count x mblocks jobs take the first stack, a
+// pair's next count x mblocks the second
+struct GemmJob {
+    TileRun run;
+    int64_t row0;
+    int second;
+};
+__device__ __forceinline__ GemmJob gemm_job(const GemmArgs& g, int job, int half) {
+    const int second = job >= half ? 1 : 0;
+    const int j = job - (second ? half : 0);
+    return GemmJob{g.runs[j / g.mblocks], int64_t(j % g.mblocks) * kGmM, second};
+}
 
 template <class D>
 struct D_lut {
@@ -240,7 +259,8 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
     uint32_t* mc = reinterpret_cast<uint32_t*>(raw + size_t(nr) * raw_slot);                     // 16 x (m, c)
     GemmSmem& S = *reinterpret_cast<GemmSmem*>(reinterpret_cast<uint8_t*>(mc) + 128);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int njobs = g.hdr->count * g.mblocks;
+    const int half = g.hdr->count * g.mblocks;
+    const int njobs = g.blocks2 != nullptr ? 2 * half : half;
     const int nk = static_cast<int>(g.cols / kGmKStage);
 
     // the 128-byte swizzle of the TMA writes and of the B descriptors needs 1024-byte aligned slots
@@ -310,9 +330,11 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
         uint32_t gs = 0;
         bool ok = true;
         for (int job = blockIdx.x; job < njobs && ok; job += gridDim.x) {
-            const TileRun run = g.runs[job / g.mblocks];
-            const int64_t row0 = int64_t(job % g.mblocks) * kGmM;
+            const GemmJob jb = gemm_job(g, job, half);
+            const TileRun run = jb.run;
+            const int64_t row0 = jb.row0;
             const int64_t y0 = (int64_t(run.expert) * g.rows + row0) / g.q;
+            const CUtensorMap* wmap = jb.second ? &maps.w2 : &maps.w;
             for (int s = 0; s < nk; ++s, ++gs, rr.next(nr)) {
                 if (gs >= uint32_t(nr)) {
                     ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.rawfree[rr.slot], rr.phase ^ 1, kWaitLimit));
@@ -325,7 +347,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
                     const int64_t x = ((int64_t(lane) * g.row_bytes + int64_t(s) * g.stage_bytes) & ~int64_t(15)) >> 2;
                     const uint32_t dst = smem_addr(raw + size_t(rr.slot) * raw_slot + raw_region(lane, g.region_bytes));
                     if (dst & 127u) atomicExch(g.status, SMOE_EARG);  // a tiled copy's destination is 128-byte aligned
-                    else tc::tma_load_2d(dst, &maps.w, static_cast<int>(x), static_cast<int>(y0), &S.rawfull[rr.slot]);
+                    else tc::tma_load_2d(dst, wmap, static_cast<int>(x), static_cast<int>(y0), &S.rawfull[rr.slot]);
                 }
             }
         }
@@ -342,7 +364,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
         uint32_t gs = 0;
         bool ok = true;
         for (int job = blockIdx.x; job < njobs && ok; job += gridDim.x) {
-            const TileRun run = g.runs[job / g.mblocks];
+            const TileRun run = gemm_job(g, job, half).run;
             for (int s = 0; s < nk; ++s, ++gs, br.next(nb)) {
                 if (gs >= uint32_t(nb)) {
                     ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.bfree[br.slot], br.phase ^ 1, kWaitLimit));
@@ -376,7 +398,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
         uint32_t gs = 0, jobs = 0;
         bool ok = true;
         for (int job = blockIdx.x; job < njobs && ok; job += gridDim.x, ++jobs) {
-            const TileRun run = g.runs[job / g.mblocks];
+            const TileRun run = gemm_job(g, job, half).run;
             const uint32_t idesc = tc::idesc_f16_f32(kGmM, 16 * run.tiles);
             if (jobs > 0) ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.dfree, (jobs - 1) & 1, kWaitLimit));
             if (!ok) break;
@@ -416,10 +438,13 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
         uint32_t gs = 0, jobs = 0;
         bool ok = true;
         for (int job = blockIdx.x; job < njobs && ok; job += gridDim.x, ++jobs) {
-            const TileRun run = g.runs[job / g.mblocks];
-            const int64_t row0 = int64_t(job % g.mblocks) * kGmM;
+            const GemmJob jb = gemm_job(g, job, half);
+            const TileRun run = jb.run;
+            const int64_t row0 = jb.row0;
             const int mrows = static_cast<int>(min(int64_t(kGmM), g.rows - row0));
-            const uint8_t* wrow = g.blocks + ((int64_t(run.expert) * g.rows + row0) + m) * g.row_bytes;
+            const uint8_t* wrow = (jb.second ? g.blocks2 : g.blocks) + ((int64_t(run.expert) * g.rows + row0) + m) * g.row_bytes;
+            float* const out32 = jb.second ? g.out2 : g.out;
+            __half* const out16 = jb.second ? g.out16_2 : g.out16;
             for (int s = 0; s < nk; ++s, ++gs, rr.next(nr)) {
                 const uint32_t as = gs % kGmASlots;
                 ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.rawfull[rr.slot], rr.phase, kWaitLimit) &&
@@ -481,8 +506,8 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
             ok = __all_sync(0xffffffffu, tc::mbar_wait(&S.dfull, jobs & 1, kWaitLimit));
             if (!ok) break;
             tc::fence_after_sync();
-            if (g.out != nullptr) {
-                float* obase = g.out + s0 * g.rows + row0 + m;
+            if (out32 != nullptr) {
+                float* obase = out32 + s0 * g.rows + row0 + m;
                 for (int c0 = 8 * qq; c0 < ncol; c0 += 32) {
                     uint32_t v[8];
                     tc::tmem_ld8(tmem + (uint32_t(32 * (warp & 3)) << 16) + uint32_t(c0), v);
@@ -505,7 +530,7 @@ __global__ void __launch_bounds__(kGmThreads, 1) gemm_tc_kernel(const GemmArgs g
                         const uint32_t sr = __shfl_sync(0xffffffffu, orow[i], 8 * qq + j);
                         const int64_t r = g.slot_row != nullptr ? int64_t(sr) : s0 + c0 + j;
                         if (m < mrows && r < g.out_rows)
-                            g.out16[r * g.rows + row0 + m] = __float2half_rn(__uint_as_float(v[j]));
+                            out16[r * g.rows + row0 + m] = __float2half_rn(__uint_as_float(v[j]));
                     }
                 }
             }
@@ -659,7 +684,8 @@ __global__ void slot_rows_kernel(const uint32_t* __restrict__ where, int64_t pai
 static int tile_matmul_impl(int kind, const uint8_t* blocks, int64_t experts, int64_t rows, int64_t cols,
                             const void* a, int a_dtype, int64_t a_rows, int64_t p16, const uint32_t* tile_expert,
                             float* out, __half* out16, const uint32_t* slot_row, int64_t out_rows, void* workspace,
-                            size_t workspace_bytes, void* stream) {
+                            size_t workspace_bytes, void* stream, const uint8_t* blocks2 = nullptr,
+                            float* out2 = nullptr, __half* out16_2 = nullptr) {
     if (p16 == 0) return SMOE_OK;
     int per, bytes;
     if (!block_info(kind, per, bytes)) return fail(SMOE_EKIND, "block type " + std::to_string(kind) + " has no decoder");
@@ -669,7 +695,11 @@ static int tile_matmul_impl(int kind, const uint8_t* blocks, int64_t experts, in
     SMOE_REQUIRE(a_rows > 0 && a_rows <= p16, SMOE_ESHAPE, "a's rows must be 1 to the tiles' slots");
     SMOE_REQUIRE(p16 % 16 == 0, SMOE_ESHAPE, "a's rows must be a multiple of 16");
     SMOE_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0, SMOE_EARG, "a must be 16-byte aligned");
-    SMOE_REQUIRE((reinterpret_cast<uintptr_t>(blocks) & 15) == 0, SMOE_EARG, "blocks must be 16-byte aligned");
+    SMOE_REQUIRE((reinterpret_cast<uintptr_t>(blocks) & 15) == 0 && (reinterpret_cast<uintptr_t>(blocks2) & 15) == 0,
+                 SMOE_EARG, "blocks must be 16-byte aligned");
+    SMOE_REQUIRE(blocks2 == nullptr || (a_dtype == SMOE_F16 && cols % kGmKStage == 0 && (out2 || out16_2) &&
+                                        (out2 != nullptr) == (out != nullptr)),
+                 SMOE_EARG, "a pair of stacks takes float16 activations, columns a multiple of 256 and two outputs");
     cudaStream_t st = as_stream(stream);
     const int64_t ntiles = p16 / 16;
     const int64_t row_bytes = cols / per * bytes;
@@ -685,6 +715,9 @@ static int tile_matmul_impl(int kind, const uint8_t* blocks, int64_t experts, in
         g.out16 = out16;
         g.slot_row = slot_row;
         g.out_rows = out_rows;
+        g.blocks2 = blocks2;
+        g.out2 = out2;
+        g.out16_2 = out16_2;
         g.hdr = static_cast<const GemmPlanHeader*>(workspace);
         g.runs = reinterpret_cast<const TileRun*>(static_cast<uint8_t*>(workspace) + sizeof(GemmPlanHeader));
         g.status = &static_cast<GemmPlanHeader*>(workspace)->status;
@@ -713,6 +746,11 @@ static int tile_matmul_impl(int kind, const uint8_t* blocks, int64_t experts, in
         g.region_bytes = (kGmM / g.q) * rawb;
         GemmMaps maps;
         if (int e = encode_maps(&maps, blocks, experts * rows, row_bytes, g.q, rawb, a, a_rows, cols)) return e;
+        if (blocks2 != nullptr) {
+            GemmMaps m2;
+            if (int e = encode_maps(&m2, blocks2, experts * rows, row_bytes, g.q, rawb, a, a_rows, cols)) return e;
+            maps.w2 = m2.w;
+        }
         gemm_plan_kernel<<<1, 1024, 0, st>>>(tile_expert, ntiles, experts, static_cast<GemmPlanHeader*>(workspace),
                                              const_cast<TileRun*>(g.runs));
         if (int s = launch_status("tile_matmul plan")) return s;
@@ -722,7 +760,7 @@ static int tile_matmul_impl(int kind, const uint8_t* blocks, int64_t experts, in
             cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
             if (g_num_sms <= 0) g_num_sms = 148;
         }
-        const int64_t max_jobs = ntiles * g.mblocks;
+        const int64_t max_jobs = ntiles * g.mblocks * (blocks2 != nullptr ? 2 : 1);
         const unsigned grid = static_cast<unsigned>(std::min<int64_t>(max_jobs, g_num_sms));
         int status = SMOE_OK;
         auto launch = [&](auto kern) {
@@ -784,4 +822,29 @@ extern "C" int smoe_slot_rows(const uint32_t* where, int64_t pairs, int64_t slot
         slot_rows_kernel<<<grid, 256, 0, st>>>(where, pairs, slots, slot_row);
     }
     return launch_status("slot_rows");
+}
+
+extern "C" int smoe_tile_matmul_pair(int kind, const uint8_t* blocks_a, const uint8_t* blocks_b, int64_t experts,
+                                     int64_t rows, int64_t cols, const void* a, int64_t p16,
+                                     const uint32_t* tile_expert, float* out_a, float* out_b, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    if (p16 == 0) return SMOE_OK;
+    SMOE_REQUIRE(blocks_b != nullptr && out_a != nullptr && out_b != nullptr, SMOE_EARG, "null pointer");
+    return tile_matmul_impl(kind, blocks_a, experts, rows, cols, a, SMOE_F16, p16, p16, tile_expert, out_a, nullptr,
+                            nullptr, 0, workspace, workspace_bytes, stream, blocks_b, out_b, nullptr);
+}
+
+extern "C" int smoe_tile_matmul_pair_rows(int kind, const uint8_t* blocks_a, const uint8_t* blocks_b, int64_t experts,
+                                          int64_t rows, int64_t cols, const void* a, int64_t a_rows, int64_t p16,
+                                          const uint32_t* tile_expert, const uint32_t* slot_row, int64_t out_rows,
+                                          void* out_a, void* out_b, void* workspace, size_t workspace_bytes,
+                                          void* stream) {
+    if (p16 == 0) return SMOE_OK;
+    SMOE_REQUIRE(blocks_b != nullptr && out_a != nullptr && out_b != nullptr && out_rows >= 0, SMOE_EARG,
+                 "null pointer");
+    SMOE_REQUIRE(((reinterpret_cast<uintptr_t>(out_a) | reinterpret_cast<uintptr_t>(out_b)) & 1) == 0, SMOE_EARG,
+                 "outputs must be 2-byte aligned");
+    return tile_matmul_impl(kind, blocks_a, experts, rows, cols, a, SMOE_F16, a_rows, p16, tile_expert, nullptr,
+                            static_cast<__half*>(out_a), slot_row, out_rows, workspace, workspace_bytes, stream,
+                            blocks_b, nullptr, static_cast<__half*>(out_b));
 }

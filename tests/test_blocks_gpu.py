@@ -186,6 +186,32 @@ def test_the_rows_variant_is_the_tile_product_read_back(cuda, kind):
     assert torch.equal(B.swiglu_to(g32, u32, torch.float16), B.swiglu(g32, u32).half())
 
 
+@pytest.mark.parametrize("kind", ["Q2_K", "IQ3_S", "Q8_0", "Q5_K"])
+def test_a_pair_of_stacks_in_one_launch_is_the_two_products(cuda, kind):
+    """smoe_tile_matmul_pair(_rows): gate and up through the same tiles in one launch give each the bits of its own
+    tile product (strata_mlx/blocks.py:690-692), in slot order as float32 and in the rows form as float16."""
+    rng = np.random.default_rng(13)
+    E, rows, cols, T, k = 6, 256, 512, 45, 4
+    ga = B.BlockSwitchLinear(dev(stack(kind, rng, E, rows, cols)[0]), kind, (E, rows, cols))
+    ub = B.BlockSwitchLinear(dev(stack(kind, rng, E, rows, cols)[0]), kind, (E, rows, cols))
+    idx = dev(rng.choice(E, (T, k), replace=True).astype(np.int32))
+    tiles, token, where = B.tiles_of(idx, E)
+    x = dev(rng.standard_normal((T, cols)).astype(np.float16))
+    a = x.index_select(0, token.view(torch.int32))
+    g, u = B.tile_matmul_pair(ga, ub, a, tiles)
+    live = (tiles.view(torch.int32).long() < E).repeat_interleave(16)  # (rows of padding tiles are not written)
+    assert torch.equal(g[live], B.tile_matmul(ga.blocks, kind, ga.shape, a, tiles)[live])
+    assert torch.equal(u[live], B.tile_matmul(ub.blocks, kind, ub.shape, a, tiles)[live])
+    sr = B.slot_rows(where, a.shape[0])
+    g16, u16 = B.tile_matmul_pair(ga, ub, a, tiles, sr, T * k)
+    assert torch.equal(g16, B.tile_matmul_rows(ga.blocks, kind, ga.shape, a, tiles, sr, T * k))
+    assert torch.equal(u16, B.tile_matmul_rows(ub.blocks, kind, ub.shape, a, tiles, sr, T * k))
+    te = torch.zeros(3, dtype=torch.int32, device="cuda")  # a dense layer: expert 0, 45 tokens, no padding rows
+    g16, u16 = B.tile_matmul_pair(ga, ub, x, te, None, T)
+    assert torch.equal(g16, B.tile_matmul_rows(ga.blocks, kind, ga.shape, x, te, None, T))
+    assert torch.equal(u16, B.tile_matmul_rows(ub.blocks, kind, ub.shape, x, te, None, T))
+
+
 @pytest.mark.parametrize("dtype", [np.float16, np.float32])
 def test_swiglu_eight_a_thread_is_the_one_a_thread(cuda, dtype):
     """smoe_swiglu / smoe_swiglu_to: the eight-wide kernels (aligned, a multiple of 8 values) give each value the
