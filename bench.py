@@ -446,7 +446,7 @@ def run_config1(device, seed, steps=200, cpu_steps=3):
 VERIFY_TYPES = ("Q8_0", "Q4_K", "Q5_K", "Q6_K", "Q2_K", "Q3_K", "IQ3_S", "IQ3_XXS", "IQ4_XS")
 # the float16 scale fields of each type's block (byte offsets), overwritten with |N(0, SIGMA)|
 SCALE_AT = {"Q8_0": (0,), "Q4_K": (0, 2), "Q5_K": (0, 2), "Q6_K": (208,), "Q2_K": (80, 82), "Q3_K": (108,),
-            "IQ3_S": (0,), "IQ3_XXS": (0,), "IQ4_XS": (0,)}
+            "IQ3_S": (0,), "IQ3_XXS": (0,), "IQ4_XS": (0,), "Q2_0": (0,)}
 
 
 def run_verify(device, seed, steps=50, warmup=5, n_layers=8, tokens=5):

@@ -387,6 +387,58 @@ struct M8Q8_0N {
 };
 using M8Q8_0 = M8Q8_0N<8>;
 
+// ---------------------------------------------------------------- Q2_0
+// (18 bytes: d 0, codes 2..17; weight j of the block is d (q_j - 1) with q_j bits 2 (j % 4) .. + 1 of byte
+// 2 + j / 4.) A stage is four blocks: 256 columns, one activation scale. In run h (32 weights) of a block, lane
+// tig of a row's quad takes weights 8 tig .. 8 tig + 7 (two code bytes): K 4 tig .. 4 tig + 3 of the MMA are the
+// first four, K 16 + 4 tig .. the last four, the activations in the same order (as Q8_0's runs). The codes enter
+// the MMA as the exact int8 values q - 1 (-1 .. 2); a block's two runs add up in int32 before its d.
+struct M8Q2_0 {
+    static constexpr int kKind = 42, kStageCols = 256, kStageBytes = 72, kRS = 112;
+    static constexpr bool kLut = false, kTokens = false, kXsum = false, kHalves = false;
+    __device__ static void fill(uint32_t*) {}
+    // a byte's four codes as four int8 values q - 1: each 2-bit field moved to the bottom of its own byte (the
+    // copies at bit offsets 0, 6, 12 and 18 put field i at bit 8 i), then 1 taken from each byte without a
+    // borrow between bytes (every byte is first raised by 0x80)
+    __device__ static __forceinline__ uint32_t expand(uint32_t c) {
+        const uint32_t t = c | (c << 12);
+        const uint32_t x = (t | (t << 6)) & 0x03030303u;
+        return ((x | 0x80808080u) - 0x01010101u) ^ 0x80808080u;
+    }
+    __device__ static void stage(const uint8_t* r0, const uint8_t* r1, int tig, int gid, const uint32_t*,
+                                 const uint8_t* xh, const uint8_t* xl, const float* xs, float (&total)[2]) {
+        const uint32_t rb[2] = {smem_addr(r0), smem_addr(r1)};  // (even addresses: 16-bit loads)
+        const uint8_t* xsrc = gid == 0 ? xh : xl;
+        const float k = xs[0] * (1.0f / 128.0f);
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+            float d[2];
+            int t[2] = {0, 0};
+#pragma unroll
+            for (int j = 0; j < 2; ++j) d[j] = h2f(lds_u16_at(rb[j] + 18 * blk));
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t a[2][2];
+#pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                    const uint32_t c = lds_u16_at(rb[j] + 18 * blk + 2 + 8 * h + 2 * tig);
+                    a[j][0] = expand(c & 255u);
+                    a[j][1] = expand(c >> 8);
+                }
+                uint2 b = make_uint2(0u, 0u);
+                if (gid < 2) b = *reinterpret_cast<const uint2*>(xsrc + 64 * blk + 32 * h + 8 * tig);
+                int acc[4];
+                mma_s8(acc, a[0][0], a[1][0], a[0][1], a[1][1], b.x, b.y);
+                // (lanes with tig > 0 hold columns 2..7: zeros)
+                t[0] += acc[0] * 128 + acc[1];
+                t[1] += acc[2] * 128 + acc[3];
+            }
+            total[0] = fmaf(d[0] * k, static_cast<float>(t[0]), total[0]);
+            total[1] = fmaf(d[1] * k, static_cast<float>(t[1]), total[1]);
+        }
+    }
+};
+
 // Eight values a lane of one 256-column block (a warp) split into int8 hi and lo and the block's scale:
 // v = s (hi + lo / 128), s = max|v| / 127. With sum16 set, sum16[c] receives the block's 16-column group c's
 // sum of 128 hi + lo (exact in float32): its split values' sum in units of s / 128.

@@ -924,6 +924,7 @@ int mv8s_try(int kind0, int kind1, const uint8_t* b0, const uint8_t* b1, int64_t
     };
     if (kind0 == M8IQ3S<2>::kKind) return cols % M8IQ3S<2>::kStageCols ? go(M8IQ3S<1>{}) : go(M8IQ3S<2>{});
     if (kind0 == M8Q8_0::kKind) return go(M8Q8_0{});
+    if (kind0 == M8Q2_0::kKind) return go(M8Q2_0{});
     if (kind0 == M8IQ4XS<2>::kKind) return cols % M8IQ4XS<2>::kStageCols ? go(M8IQ4XS<1>{}) : go(M8IQ4XS<2>{});
     if (kind0 == M8IQ3XXS<2>::kKind) return cols % M8IQ3XXS<2>::kStageCols ? go(M8IQ3XXS<1>{}) : go(M8IQ3XXS<2>{});
     // the K-types (Q2_K and Q3_K in stages of two blocks: widths of an odd number of 256 columns stay on the

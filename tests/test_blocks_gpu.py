@@ -88,12 +88,13 @@ def test_a_prompt_gets_the_same_products_a_pair_at_a_time_and_from_unpacked_weig
     assert np.abs(got[:, 0] - want).max() <= 1e-5 * scale
 
 
-@pytest.mark.parametrize("kind", ["IQ3_S", "Q8_0", "IQ4_XS", "IQ3_XXS"])
+@pytest.mark.parametrize("kind", ["IQ3_S", "Q8_0", "IQ4_XS", "IQ3_XXS", "Q2_0"])
 @pytest.mark.parametrize("rows, cols", [(40, 512), (1536, 4096), (4096, 1536), (16, 256)])
 @pytest.mark.parametrize("share", [1, 4])
 def test_float16_products_on_the_tensor_core_path(cuda, kind, rows, cols, share):
-    """The decode matvec of the hot path's types (mma.sync on exact float16 integers, float32 scales) against
-    the float64 product: the float16 result within 1e-3 of the largest value (its own rounding is 2^-11)."""
+    """The decode matvec of the hot path's types and Q2_0 (int8 mma.sync on the exact codes, the activations
+    split into int8 hi / lo, float32 scales) against the float64 product: the float16 result within 1e-3 of the
+    largest value (its own rounding is 2^-11)."""
     rng = np.random.default_rng(rows + cols + share)
     E, pairs = 5, 8
     b, w = stack(kind, rng, E, rows, cols, scale=(-0.05, 0.05))
@@ -322,7 +323,7 @@ def test_gate_and_up_in_one_launch_are_two_launches(cuda):
     assert torch.equal(g, gate(x5, idx).reshape(6, -1)) and torch.equal(u, up(x5, idx).reshape(6, -1))
 
 
-@pytest.mark.parametrize("kind", ["IQ3_S", "IQ2_XS", "IQ4_NL", "Q2_K", "Q5_K", "Q8_0"])
+@pytest.mark.parametrize("kind", ["IQ3_S", "IQ2_XS", "IQ4_NL", "Q2_K", "Q5_K", "Q8_0", "Q2_0"])
 @pytest.mark.parametrize("tokens", [1, 20])
 def test_down_taking_swiglu_itself_and_unsorted_pairs_give_the_same_bits(cuda, monkeypatch, kind, tokens):
     """tests/test_blocks.py:257-280: the BLOCK_GLU path (swiglu formed in down) == down(swiglu(g, u))."""
